@@ -1,0 +1,143 @@
+// Internal declarations shared by the translation units of libauratensor_cuda.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+#include "../../include/auratensor.h"
+
+namespace at {
+
+// Error carrying an AT_ERR_* status; every C-ABI entry point converts it to
+// a return code and stores the message for at_last_error().
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+void set_last_error(const std::string& msg);
+
+[[noreturn]] inline void fail(int code, const std::string& msg) { throw Error(code, msg); }
+
+inline void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) {
+        int code = (e == cudaErrorMemoryAllocation) ? AT_ERR_OOM : AT_ERR_CUDA;
+        fail(code, std::string(what) + ": " + cudaGetErrorString(e));
+    }
+}
+#define AT_CUDA(x) ::at::cuda_check((x), #x)
+#define AT_REQUIRE(cond, code, msg) do { if (!(cond)) ::at::fail((code), (msg)); } while (0)
+
+// Runs `body` and converts exceptions into status codes.
+template <class F>
+int guard(F&& body) {
+    try {
+        body();
+        return AT_OK;
+    } catch (const Error& e) {
+        set_last_error(e.what());
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        set_last_error("host allocation failed");
+        return AT_ERR_OOM;
+    } catch (const std::exception& e) {
+        set_last_error(e.what());
+        return AT_ERR_CUDA;
+    }
+}
+
+struct NcclApi;  // dlopen'd NCCL entry points
+
+}  // namespace at
+
+struct at_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;      // stream every launch of this context uses
+    cudaStream_t own_stream = nullptr;  // stream created with the context
+    int num_sms = 148;
+    // tensor parallelism
+    int rank = 0;
+    int world = 1;
+    void* nccl_comm = nullptr;  // ncclComm_t
+};
+
+// Planar device layout of one quantized matrix.
+//  Orientation N: rows-major; block (r, b) at qs[(r*nb + b)*QB], d[r*nb + b].
+//  Orientation T: block-column-major; block (r, c) at qs[(c*rows + r)*QB], d[c*rows + r].
+// QB = 16 (Q4_0) or 32 (Q8_0) quant bytes per block. F32 matrices keep
+// row-major floats in `f32`.
+struct at_qmat {
+    at_ctx* ctx = nullptr;
+    int type = AT_GGML_Q4_0;
+    int orient = AT_ORIENT_N;
+    int64_t rows = 0, cols = 0;
+    uint8_t* qs = nullptr;
+    uint16_t* d = nullptr;
+    float* f32 = nullptr;
+    bool owns = true;
+};
+
+namespace at {
+
+constexpr int QK = 32;
+inline int quant_bytes(int type) { return type == AT_GGML_Q4_0 ? 16 : 32; }
+inline int block_bytes(int type) { return type == AT_GGML_Q4_0 ? 18 : 34; }
+
+// Allocates the planes of `m` (type/orient/rows/cols already set).
+void qmat_alloc(at_qmat* m);
+void qmat_free(at_qmat* m);
+// Repack raw GGUF blocks (row-major stream, device memory) into the planes of
+// `m`, taking rows [r0, r0+m->rows) and block-columns [c0/32, ...) of a source
+// matrix with `src_cols` columns.
+void qmat_fill_from_blocks(at_qmat* m, const uint8_t* src_dev, int64_t src_cols, int64_t r0, int64_t c0,
+                           cudaStream_t s);
+// Copies rows [src_r0, +n_rows) x cols [src_c0, +n_cols) of a raw row-major
+// block matrix with src_cols columns into `m` at (dst_r0, dst_c0).
+void qmat_fill_region(at_qmat* m, const uint8_t* src_dev, int64_t src_cols, int64_t src_r0, int64_t src_c0,
+                      int64_t n_rows, int64_t n_cols, int64_t dst_r0, int64_t dst_c0, cudaStream_t s);
+// F32 / F16 source into an f32 matrix.
+void qmat_fill_from_float(at_qmat* m, const void* src_dev, int src_type, int64_t src_cols, int64_t r0,
+                          int64_t c0, cudaStream_t s);
+
+// Prologue/epilogue variants of the fused GEMV kernels.
+enum class Pro { Plain, AddNorm };         // x from global, or x = norm(xin + yin) (F7 residual)
+enum class Epi { Plain, SiluMul, QkvRope }; // y; silu(g)*u; RoPE + KV append
+
+struct GemvArgs {
+    const float* x = nullptr;     // Pro::Plain input [B][in]
+    const float* xin = nullptr;   // Pro::AddNorm: residual stream (normed, F7)
+    const float* yin = nullptr;   // Pro::AddNorm: projection output to add (may be null)
+    const float* gamma = nullptr; // Pro::AddNorm: norm weight
+    float* xout = nullptr;        // Pro::AddNorm: normed x written by CTA 0
+    float eps = 1e-5f;
+    float* y = nullptr;           // output [B][out]
+    int x_stride = 0;             // floats between batch rows of x / xin / yin / xout
+    int y_stride = 0;             // floats between batch rows of y
+    // Epi::SiluMul
+    const at_qmat* m2 = nullptr;
+    // Epi::QkvRope
+    const float* rope_cos = nullptr;   // [ctx][hd]
+    const float* rope_sin = nullptr;
+    const int64_t* pos = nullptr;      // [B] device
+    float* kcache = nullptr;           // [B][L][Hkv][ctx][hd] base of this layer slice
+    float* vcache = nullptr;
+    int64_t kv_slot_stride = 0;        // floats between sequence slots
+    int head_dim = 0, n_q_cols = 0, n_kv_cols = 0, ctx_len = 0;
+    // T split-K scratch (partials + tile counters)
+    float* scratch = nullptr;
+    unsigned* counters = nullptr;
+};
+
+void launch_gemv_n(const at_qmat* m, int batch, Pro pro, Epi epi, const GemvArgs& a, int num_sms,
+                   cudaStream_t s);
+void launch_gemv_t(const at_qmat* m, int batch, Pro pro, Epi epi, const GemvArgs& a, int num_sms,
+                   cudaStream_t s);
+// Scratch floats / counters a T launch needs for (m, batch).
+void gemv_t_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* floats, size_t* counters);
+void launch_sgemv_f32(const float* A, const float* x, float* y, int M, int K, int batch, int a_ld,
+                      cudaStream_t s);
+
+}  // namespace at

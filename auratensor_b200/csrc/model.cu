@@ -1,0 +1,960 @@
+// Device-resident Llama decode (LlamaModel.forwardStep, inference/LlamaModel.java:141-308)
+// with Megatron tensor parallelism over NCCL.
+//
+// Per step and per layer the work is five kernels plus, under tensor
+// parallelism, two all-reduces:
+//   1. QKV GEMV (orientation T) with the attention RMSNorm in its prologue
+//      (x = norm(x + y), F7 residual semantics) and RoPE + KV append in its
+//      epilogue;
+//   2. split-KV attention over the fp32 KV cache;  3. log-sum-exp combine;
+//   4. wo GEMV (T) -> y  [all-reduce y];
+//   5. gate/up GEMV (N) with the FFN RMSNorm prologue and SiLU*up epilogue;
+//   6. down GEMV (N) -> y  [all-reduce y].
+// The embedding row dequant starts the step, the lm_head GEMV with the output
+// norm prologue and an argmax end it. The whole sequence is captured once per
+// batch size into a CUDA graph and replayed; token ids and positions are read
+// from device memory so the graph does not change between steps.
+#include <dlfcn.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "at_internal.h"
+#include "dev_common.cuh"
+#include "nccl_dl.h"
+
+namespace at {
+
+// ---------------------------------------------------------------------------
+// NCCL loader
+// ---------------------------------------------------------------------------
+const NcclApi& nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    static std::string err;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {
+            err = std::string("cannot load libnccl.so.2: ") + dlerror();
+            return;
+        }
+#define AT_SYM(field, name) api.field = reinterpret_cast<decltype(api.field)>(dlsym(h, name))
+        AT_SYM(GetUniqueId, "ncclGetUniqueId");
+        AT_SYM(CommInitRank, "ncclCommInitRank");
+        AT_SYM(CommDestroy, "ncclCommDestroy");
+        AT_SYM(CommAbort, "ncclCommAbort");
+        AT_SYM(CommGetAsyncError, "ncclCommGetAsyncError");
+        AT_SYM(AllReduce, "ncclAllReduce");
+        AT_SYM(AllGather, "ncclAllGather");
+        AT_SYM(GetErrorString, "ncclGetErrorString");
+#undef AT_SYM
+        if (!api.GetUniqueId || !api.CommInitRank || !api.AllReduce || !api.AllGather || !api.CommDestroy)
+            err = "libnccl.so.2 lacks required symbols";
+    });
+    if (!err.empty()) fail(AT_ERR_NCCL, err);
+    return api;
+}
+
+void nccl_check(ncclResult_t r, const char* what) {
+    if (r != ncclSuccess) {
+        const char* s = nccl().GetErrorString ? nccl().GetErrorString(r) : "?";
+        fail(AT_ERR_NCCL, std::string(what) + ": " + s);
+    }
+}
+
+namespace {
+
+constexpr int CH = 64;  // KV positions per attention CTA
+
+// ---------------------------------------------------------------------------
+// Step kernels
+// ---------------------------------------------------------------------------
+// writeTokenEmbedding (inference/LlamaModel.java:181-186): one dequantized row
+// of token_embd into xa; y <- 0 so the first layer's prologue reads x + 0.
+template <int QT>
+__global__ void embed_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc,
+                             const int* __restrict__ tokens, int d, float* __restrict__ xa, float* __restrict__ y) {
+    constexpr int QB = (QT == AT_GGML_Q4_0) ? 16 : 32;
+    const int b = blockIdx.x;
+    const int64_t tok = tokens[b];
+    const int nb = d / 32;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const int64_t blk = tok * nb + (i >> 5);
+        const int w = i & 31;
+        int q;
+        if constexpr (QT == AT_GGML_Q4_0) {
+            const uint32_t pack = qs[blk * QB + (w >> 1)];
+            q = ((w & 1) ? (int)(pack >> 4) : (int)(pack & 0xF)) - 8;
+        } else {
+            q = (int)(int8_t)qs[blk * QB + w];
+        }
+        xa[(size_t)b * d + i] = __fmul_rn((float)q, fp16_ftz(dsc[blk]));
+        y[(size_t)b * d + i] = 0.f;
+    }
+}
+
+__device__ __forceinline__ float exp_ref(float v) { return (float)exp((double)v); }
+
+// LlamaModel.attention (inference/LlamaModel.java:255-297) split over KV
+// chunks: for the G query heads sharing KV head `kvh`, scores over positions
+// [p0, p1) = (K q) * scale, chunk max m, l = sum exp(s - m), o = sum exp(s - m) V.
+template <int HD>
+__global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                                                         const float* __restrict__ vc,
+                                                         const int64_t* __restrict__ pos, float* __restrict__ part,
+                                                         int Hl, int Hkvl, int ctx, int64_t slot_stride,
+                                                         int nchunk_max, float scale) {
+    constexpr int G_MAX = 8;
+    __shared__ __align__(16) float qs[G_MAX][HD];
+    __shared__ float sc[G_MAX][CH];
+    __shared__ float s_m[G_MAX], s_l[G_MAX];
+    const int kvh = blockIdx.x, chunk = blockIdx.y, b = blockIdx.z;
+    const int G = Hl / Hkvl;
+    const int64_t P = pos[b] + 1;
+    const int64_t p0 = (int64_t)chunk * CH;
+    if (p0 >= P) return;
+    const int n = (int)((P - p0) < CH ? (P - p0) : CH);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const float* kbase = kc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD;
+    const float* vbase = vc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD;
+    for (int i = tid; i < G * HD; i += 256) {
+        const int g = i / HD, dd = i - g * HD;
+        qs[g][dd] = q[(size_t)b * Hl * HD + (size_t)(kvh * G + g) * HD + dd];
+    }
+    __syncthreads();
+    constexpr int PER = HD / 32;
+    for (int i = warp; i < n; i += 8) {
+        float kr[PER];
+#pragma unroll
+        for (int t = 0; t < PER; ++t) kr[t] = kbase[(size_t)i * HD + lane * PER + t];
+        for (int g = 0; g < G; ++g) {
+            float acc = 0.f;
+#pragma unroll
+            for (int t = 0; t < PER; ++t) acc = fmaf(kr[t], qs[g][lane * PER + t], acc);
+            acc = warp_sum(acc);
+            if (lane == 0) sc[g][i] = __fmul_rn(acc, scale);
+        }
+    }
+    __syncthreads();
+    if (warp < G) {
+        const int g = warp;
+        float m = -INFINITY;
+        for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[g][i]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int i = lane; i < n; i += 32) {
+            const float e = exp_ref(__fsub_rn(sc[g][i], m));
+            sc[g][i] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) { s_m[g] = m; s_l[g] = l; }
+    }
+    __syncthreads();
+    for (int o = tid; o < G * HD; o += 256) {
+        const int g = o / HD, dd = o - g * HD;
+        float acc = 0.f;
+        for (int i = 0; i < n; ++i) acc = fmaf(sc[g][i], vbase[(size_t)i * HD + dd], acc);
+        const int h = kvh * G + g;
+        float* dst = part + (((size_t)b * Hl + h) * nchunk_max + chunk) * (HD + 2);
+        dst[dd] = acc;
+        if (dd == 0) { dst[HD] = s_m[g]; dst[HD + 1] = s_l[g]; }
+    }
+}
+
+// Merges the chunk partials of one (sequence, head): out = sum_c o_c e^(m_c-M) / sum_c l_c e^(m_c-M).
+template <int HD>
+__global__ void attn_combine_kernel(const float* __restrict__ part, const int64_t* __restrict__ pos,
+                                    float* __restrict__ att, int Hl, int nchunk_max) {
+    const int h = blockIdx.x, b = blockIdx.y, dd = threadIdx.x;
+    const int64_t P = pos[b] + 1;
+    const int nch = (int)((P + CH - 1) / CH);
+    const float* base = part + ((size_t)b * Hl + h) * nchunk_max * (HD + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, base[(size_t)c * (HD + 2) + HD]);
+    float L = 0.f, o = 0.f;
+    for (int c = 0; c < nch; ++c) {
+        const float* pc = base + (size_t)c * (HD + 2);
+        const float w = exp_ref(__fsub_rn(pc[HD], M));
+        L = fmaf(pc[HD + 1], w, L);
+        o = fmaf(pc[dd], w, o);
+    }
+    att[(size_t)b * Hl * HD + (size_t)h * HD + dd] = __fdiv_rn(o, L);
+}
+
+// Greedy fast path of Sampler.sample (inference/Sampler.java:56-67): first
+// index of the maximum; a NaN never wins unless it is element 0.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V, int stride,
+                                                      int* __restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const float* row = logits + (size_t)blockIdx.x * stride;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        float v = row[i];
+        if (v != v) v = -INFINITY;
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+        if (bv == -INFINITY && bi == 0x7fffffff) bi = 0;
+        if (row[0] != row[0]) bi = 0;
+        out[blockIdx.x] = bi;
+    }
+}
+
+// All-gathered [rank][b][Vl] logits -> [b][V].
+__global__ void gather_logits_kernel(const float* __restrict__ g, float* __restrict__ out, int world, int B, int Vl,
+                                     int V) {
+    const int64_t total = (int64_t)B * V;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int b = (int)(t / V), v = (int)(t - (t / V) * V);
+        const int r = v / Vl, j = v - r * Vl;
+        out[t] = g[((size_t)r * B + b) * Vl + j];
+    }
+}
+
+inline int grid_for(int64_t n, int tpb = 256) {
+    int64_t g = (n + tpb - 1) / tpb;
+    if (g > 65535 * 16) g = 65535 * 16;
+    return (int)(g < 1 ? 1 : g);
+}
+
+struct Layer {
+    at_qmat qkv, wo, w1, w3, w2;
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+};
+
+}  // namespace
+}  // namespace at
+
+using namespace at;
+
+struct at_model {
+    at_ctx* ctx = nullptr;
+    at_model_config cfg{};
+    int d = 0, hd = 0, H = 0, Hkv = 0, F = 0, V = 0, L = 0, ctx_len = 0, B = 1;
+    int Hl = 0, Hkvl = 0, Fl = 0, Vl = 0;  // per-rank shares
+    int wtype = -1;                        // type of the first quantized matrix seen
+    std::vector<Layer> layers;
+    at_qmat tok, out;
+    float* out_norm = nullptr;
+    // activations
+    float *xa = nullptr, *xb = nullptr, *y = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
+    float *logits = nullptr, *logits_local = nullptr, *gather = nullptr, *att_part = nullptr;
+    float *kcache = nullptr, *vcache = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    float* scratch = nullptr;
+    unsigned* counters = nullptr;
+    int* d_tokens = nullptr;
+    int64_t* d_pos = nullptr;
+    int* d_argmax = nullptr;
+    int* h_tokens = nullptr;      // pinned
+    int64_t* h_pos = nullptr;     // pinned
+    int nchunk_max = 0;
+    int64_t slot_stride = 0;      // floats per KV slot (all layers)
+    std::vector<int64_t> kv_size;
+    std::map<std::string, bool> seen;
+    cudaGraphExec_t graph[9] = {};
+    bool finalized = false;
+};
+
+namespace {
+
+void alloc_zero(void** p, size_t bytes) {
+    AT_CUDA(cudaMalloc(p, bytes ? bytes : 16));
+    AT_CUDA(cudaMemset(*p, 0, bytes ? bytes : 16));
+}
+
+void make_qmat(at_qmat& m, int type, int orient, int64_t rows, int64_t cols) {
+    if (m.qs || m.f32) return;
+    m.type = type;
+    m.orient = orient;
+    m.rows = rows;
+    m.cols = cols;
+    qmat_alloc(&m);
+    const size_t nblk = (size_t)(rows * (cols / QK));
+    AT_CUDA(cudaMemset(m.qs, 0, nblk * quant_bytes(type)));
+    AT_CUDA(cudaMemset(m.d, 0, nblk * 2 + 16));
+}
+
+bool parse_layer(const std::string& name, int* layer, std::string* leaf) {
+    if (name.rfind("blk.", 0) != 0) return false;
+    const size_t dot = name.find('.', 4);
+    if (dot == std::string::npos) return false;
+    *layer = std::stoi(name.substr(4, dot - 4));
+    *leaf = name.substr(dot + 1);
+    return true;
+}
+
+void enqueue_step(at_model* m, int B) {
+    at_ctx* c = m->ctx;
+    cudaStream_t s = c->stream;
+    const int d = m->d, hd = m->hd;
+    if (m->tok.type == AT_GGML_Q4_0)
+        embed_kernel<AT_GGML_Q4_0><<<B, 256, 0, s>>>(m->tok.qs, m->tok.d, m->d_tokens, d, m->xa, m->y);
+    else
+        embed_kernel<AT_GGML_Q8_0><<<B, 256, 0, s>>>(m->tok.qs, m->tok.d, m->d_tokens, d, m->xa, m->y);
+    AT_CUDA(cudaGetLastError());
+    const float scale = (float)(1.0 / std::sqrt((double)hd));
+    const size_t layer_kv = (size_t)m->Hkvl * m->ctx_len * hd;
+    for (int L = 0; L < m->L; ++L) {
+        Layer& ly = m->layers[L];
+        GemvArgs a;
+        a.xin = m->xa; a.yin = m->y; a.gamma = ly.attn_norm; a.xout = m->xb; a.eps = m->cfg.rms_norm_eps;
+        a.x_stride = d;
+        a.y = m->q; a.y_stride = m->Hl * hd;
+        a.rope_cos = m->rope_cos; a.rope_sin = m->rope_sin; a.pos = m->d_pos;
+        a.kcache = m->kcache + L * layer_kv; a.vcache = m->vcache + L * layer_kv;
+        a.kv_slot_stride = m->slot_stride;
+        a.head_dim = hd; a.n_q_cols = m->Hl * hd; a.n_kv_cols = m->Hkvl * hd; a.ctx_len = m->ctx_len;
+        a.scratch = m->scratch; a.counters = m->counters;
+        launch_gemv_t(&ly.qkv, B, Pro::AddNorm, Epi::QkvRope, a, c->num_sms, s);
+
+        dim3 g1(m->Hkvl, m->nchunk_max, B);
+        if (hd == 128)
+            attn_split_kernel<128><<<g1, 256, 0, s>>>(m->q, a.kcache, a.vcache, m->d_pos, m->att_part, m->Hl, m->Hkvl,
+                                                      m->ctx_len, m->slot_stride, m->nchunk_max, scale);
+        else
+            attn_split_kernel<64><<<g1, 256, 0, s>>>(m->q, a.kcache, a.vcache, m->d_pos, m->att_part, m->Hl, m->Hkvl,
+                                                     m->ctx_len, m->slot_stride, m->nchunk_max, scale);
+        AT_CUDA(cudaGetLastError());
+        dim3 g2(m->Hl, B);
+        if (hd == 128)
+            attn_combine_kernel<128><<<g2, 128, 0, s>>>(m->att_part, m->d_pos, m->att, m->Hl, m->nchunk_max);
+        else
+            attn_combine_kernel<64><<<g2, 64, 0, s>>>(m->att_part, m->d_pos, m->att, m->Hl, m->nchunk_max);
+        AT_CUDA(cudaGetLastError());
+
+        GemvArgs o;
+        o.x = m->att; o.x_stride = m->Hl * hd; o.y = m->y; o.y_stride = d;
+        o.scratch = m->scratch; o.counters = m->counters;
+        launch_gemv_t(&ly.wo, B, Pro::Plain, Epi::Plain, o, c->num_sms, s);
+        if (c->world > 1)
+            nccl_check(nccl().AllReduce(m->y, m->y, (size_t)B * d, ncclFloat32, ncclSum, (ncclComm_t)c->nccl_comm, s),
+                       "ncclAllReduce(attention)");
+
+        GemvArgs f;
+        f.xin = m->xb; f.yin = m->y; f.gamma = ly.ffn_norm; f.xout = m->xa; f.eps = m->cfg.rms_norm_eps;
+        f.x_stride = d; f.y = m->h; f.y_stride = m->Fl; f.m2 = &ly.w3;
+        launch_gemv_n(&ly.w1, B, Pro::AddNorm, Epi::SiluMul, f, c->num_sms, s);
+
+        GemvArgs dn;
+        dn.x = m->h; dn.x_stride = m->Fl; dn.y = m->y; dn.y_stride = d;
+        launch_gemv_n(&ly.w2, B, Pro::Plain, Epi::Plain, dn, c->num_sms, s);
+        if (c->world > 1)
+            nccl_check(nccl().AllReduce(m->y, m->y, (size_t)B * d, ncclFloat32, ncclSum, (ncclComm_t)c->nccl_comm, s),
+                       "ncclAllReduce(mlp)");
+    }
+    GemvArgs hd_args;
+    hd_args.xin = m->xa; hd_args.yin = m->y; hd_args.gamma = m->out_norm; hd_args.xout = m->xb;
+    hd_args.eps = m->cfg.rms_norm_eps; hd_args.x_stride = d;
+    hd_args.y = (c->world > 1) ? m->logits_local : m->logits; hd_args.y_stride = m->Vl;
+    launch_gemv_n(&m->out, B, Pro::AddNorm, Epi::Plain, hd_args, c->num_sms, s);
+    if (c->world > 1) {
+        nccl_check(nccl().AllGather(m->logits_local, m->gather, (size_t)B * m->Vl, ncclFloat32,
+                                    (ncclComm_t)c->nccl_comm, s),
+                   "ncclAllGather(logits)");
+        gather_logits_kernel<<<grid_for((int64_t)B * m->V), 256, 0, s>>>(m->gather, m->logits, c->world, B, m->Vl, m->V);
+        AT_CUDA(cudaGetLastError());
+    }
+    argmax_kernel<<<B, 1024, 0, s>>>(m->logits, m->V, m->V, m->d_argmax);
+    AT_CUDA(cudaGetLastError());
+}
+
+void run_step(at_model* m, const int* tokens, const int64_t* positions, int B, float* logits_host) {
+    AT_REQUIRE(m && m->finalized, AT_ERR_STATE, "model is not finalized");
+    AT_REQUIRE(B >= 1 && B <= m->B, AT_ERR_INVALID_ARG, "batch exceeds the model's max_batch");
+    AT_REQUIRE(tokens && positions, AT_ERR_INVALID_ARG, "null tokens/positions");
+    for (int b = 0; b < B; ++b) {
+        AT_REQUIRE(tokens[b] >= 0 && tokens[b] < m->V, AT_ERR_INVALID_ARG,
+                   "token id " + std::to_string(tokens[b]) + " out of range");
+        AT_REQUIRE(positions[b] >= 0, AT_ERR_INVALID_ARG, "negative position");
+        // KVCache.append (inference/KVCache.java:83-85)
+        AT_REQUIRE(positions[b] < m->ctx_len, AT_ERR_STATE,
+                   "position " + std::to_string(positions[b]) + " exceeds maxContext " + std::to_string(m->ctx_len));
+    }
+    at_ctx* c = m->ctx;
+    AT_CUDA(cudaSetDevice(c->device));
+    // previous step's copies out of the pinned buffers are complete (stream order + sync below)
+    for (int b = 0; b < B; ++b) { m->h_tokens[b] = tokens[b]; m->h_pos[b] = positions[b]; }
+    AT_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tokens, sizeof(int) * B, cudaMemcpyHostToDevice, c->stream));
+    AT_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pos, sizeof(int64_t) * B, cudaMemcpyHostToDevice, c->stream));
+    if (!m->graph[B]) {
+        cudaGraph_t g;
+        AT_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        try {
+            enqueue_step(m, B);
+        } catch (...) {
+            cudaStreamEndCapture(c->stream, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        AT_CUDA(cudaStreamEndCapture(c->stream, &g));
+        AT_CUDA(cudaGraphInstantiate(&m->graph[B], g, 0));
+        AT_CUDA(cudaGraphDestroy(g));
+    }
+    AT_CUDA(cudaGraphLaunch(m->graph[B], c->stream));
+    if (logits_host)
+        AT_CUDA(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * (size_t)B * m->V, cudaMemcpyDeviceToHost,
+                                c->stream));
+    AT_CUDA(cudaStreamSynchronize(c->stream));
+    for (int b = 0; b < B; ++b) m->kv_size[b] = std::max<int64_t>(m->kv_size[b], positions[b] + 1);
+}
+
+void destroy_model(at_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    for (auto& g : m->graph)
+        if (g) cudaGraphExecDestroy(g);
+    for (auto& ly : m->layers) {
+        qmat_free(&ly.qkv); qmat_free(&ly.wo); qmat_free(&ly.w1); qmat_free(&ly.w3); qmat_free(&ly.w2);
+        cudaFree(ly.attn_norm); cudaFree(ly.ffn_norm);
+    }
+    qmat_free(&m->tok);
+    qmat_free(&m->out);
+    void* bufs[] = {m->out_norm, m->xa, m->xb, m->y, m->q, m->att, m->h, m->logits, m->logits_local, m->gather,
+                    m->att_part, m->kcache, m->vcache, m->rope_cos, m->rope_sin, m->scratch, m->counters,
+                    m->d_tokens, m->d_pos, m->d_argmax};
+    for (void* p : bufs)
+        if (p) cudaFree(p);
+    if (m->h_tokens) cudaFreeHost(m->h_tokens);
+    if (m->h_pos) cudaFreeHost(m->h_pos);
+    delete m;
+}
+
+// --- GGUF ------------------------------------------------------------------
+struct GgufView {
+    const uint8_t* base = nullptr;
+    size_t len = 0;
+    size_t pos = 0;
+    void need(size_t n) {
+        if (pos + n > len) fail(AT_ERR_IO, "truncated GGUF file");
+    }
+    template <class T>
+    T rd() {
+        need(sizeof(T));
+        T v;
+        memcpy(&v, base + pos, sizeof(T));
+        pos += sizeof(T);
+        return v;
+    }
+    std::string str() {
+        const int64_t n = rd<int64_t>();
+        if (n < 0 || n > 0x7fffffff) fail(AT_ERR_IO, "implausible string length");
+        need((size_t)n);
+        std::string s(reinterpret_cast<const char*>(base + pos), (size_t)n);
+        pos += (size_t)n;
+        return s;
+    }
+};
+
+struct MetaVal {
+    int type = -1;
+    double num = 0;
+    bool is_num = false;
+    std::string s;
+};
+
+// GgufFile.readValue (format/GgufFile.java:259-294); arrays are skipped.
+MetaVal read_value(GgufView& v, int vt) {
+    MetaVal r;
+    r.type = vt;
+    switch (vt) {
+        case 0: r.num = v.rd<uint8_t>(); r.is_num = true; break;
+        case 1: r.num = v.rd<int8_t>(); r.is_num = true; break;
+        case 2: r.num = v.rd<uint16_t>(); r.is_num = true; break;
+        case 3: r.num = v.rd<int16_t>(); r.is_num = true; break;
+        case 4: r.num = v.rd<uint32_t>(); r.is_num = true; break;
+        case 5: r.num = v.rd<int32_t>(); r.is_num = true; break;
+        case 6: r.num = v.rd<float>(); r.is_num = true; break;
+        case 7: r.num = v.rd<uint8_t>() != 0; break;
+        case 8: r.s = v.str(); break;
+        case 9: {
+            const int et = v.rd<int32_t>();
+            const int64_t n = v.rd<int64_t>();
+            if (n < 0 || n > (1 << 26)) fail(AT_ERR_IO, "implausible array length");
+            for (int64_t i = 0; i < n; ++i) read_value(v, et);
+            break;
+        }
+        case 10: r.num = (double)v.rd<uint64_t>(); r.is_num = true; break;
+        case 11: r.num = (double)v.rd<int64_t>(); r.is_num = true; break;
+        case 12: r.num = v.rd<double>(); r.is_num = true; break;
+        default: fail(AT_ERR_IO, "Unknown GGUF metadata value type: " + std::to_string(vt));
+    }
+    return r;
+}
+
+}  // namespace
+
+extern "C" {
+
+int at_tp_unique_id(uint8_t out_id[128]) {
+    return guard([&] {
+        AT_REQUIRE(out_id, AT_ERR_INVALID_ARG, "null output");
+        ncclUniqueId id;
+        nccl_check(nccl().GetUniqueId(&id), "ncclGetUniqueId");
+        static_assert(sizeof(id) == 128, "ncclUniqueId is 128 bytes");
+        memcpy(out_id, &id, 128);
+    });
+}
+
+int at_ctx_create_tp(int device, int rank, int world, const uint8_t id[128], at_ctx** out) {
+    at_ctx* c = nullptr;
+    const int rc = guard([&] {
+        AT_REQUIRE(out && id, AT_ERR_INVALID_ARG, "null argument");
+        AT_REQUIRE(world >= 1 && rank >= 0 && rank < world, AT_ERR_INVALID_ARG, "bad rank/world");
+        const int r0 = at_ctx_create(device, &c);
+        if (r0 != AT_OK) fail(r0, "context creation failed");
+        c->rank = rank;
+        c->world = world;
+        if (world > 1) {
+            ncclUniqueId uid;
+            memcpy(&uid, id, 128);
+            ncclComm_t comm;
+            AT_CUDA(cudaSetDevice(device));
+            nccl_check(nccl().CommInitRank(&comm, world, uid, rank), "ncclCommInitRank");
+            c->nccl_comm = comm;
+        }
+        *out = c;
+    });
+    if (rc != AT_OK && c) at_ctx_destroy(c);
+    return rc;
+}
+
+int at_ctx_destroy(at_ctx* ctx) {
+    return guard([&] {
+        if (!ctx) return;
+        cudaSetDevice(ctx->device);
+        if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+        if (ctx->nccl_comm) nccl().CommDestroy((ncclComm_t)ctx->nccl_comm);
+        if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+        delete ctx;
+    });
+}
+
+int at_model_create(at_ctx* ctx, const at_model_config* cfg, at_model** out) {
+    at_model* m = nullptr;
+    const int rc = guard([&] {
+        AT_REQUIRE(ctx && cfg && out, AT_ERR_INVALID_ARG, "null argument");
+        AT_REQUIRE(cfg->head_count > 0, AT_ERR_STATE, "headCount == 0");
+        AT_REQUIRE(cfg->context_length > 0 && cfg->embedding_length > 0 && cfg->block_count > 0 &&
+                       cfg->head_count_kv > 0 && cfg->feed_forward_length > 0 && cfg->vocab_size > 0,
+                   AT_ERR_INVALID_ARG, "model dims must be positive");
+        AT_CUDA(cudaSetDevice(ctx->device));
+        m = new at_model();
+        m->ctx = ctx;
+        m->cfg = *cfg;
+        m->B = cfg->max_batch < 1 ? 1 : cfg->max_batch;
+        AT_REQUIRE(m->B <= 8, AT_ERR_INVALID_ARG, "max_batch must be in [1, 8]");
+        m->d = (int)cfg->embedding_length;
+        m->H = (int)cfg->head_count;
+        m->Hkv = (int)cfg->head_count_kv;
+        m->hd = m->d / m->H;  // LlamaConfig.headDim (inference/LlamaConfig.java:293-296)
+        m->F = (int)cfg->feed_forward_length;
+        m->V = (int)cfg->vocab_size;
+        m->L = (int)cfg->block_count;
+        m->ctx_len = (int)cfg->context_length;
+        const int W = ctx->world, r = ctx->rank;
+        AT_REQUIRE(m->hd == 64 || m->hd == 128, AT_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+        AT_REQUIRE(m->d % 32 == 0, AT_ERR_INVALID_ARG, "embedding_length must be a multiple of 32");
+        AT_REQUIRE(m->H % m->Hkv == 0 && m->H / m->Hkv <= 8, AT_ERR_UNSUPPORTED, "query heads per KV head must be 1..8");
+        AT_REQUIRE(m->Hkv % W == 0, AT_ERR_INVALID_ARG, "KV heads must divide evenly across tensor-parallel ranks");
+        AT_REQUIRE(m->F % (32 * W) == 0, AT_ERR_INVALID_ARG, "FFN width must split into 32-aligned shards");
+        m->Hl = m->H / W;
+        m->Hkvl = m->Hkv / W;
+        m->Fl = m->F / W;
+        m->Vl = (m->V + W - 1) / W;
+        (void)r;
+        m->layers.resize(m->L);
+        m->kv_size.assign(m->B, 0);
+        *out = m;
+    });
+    if (rc != AT_OK && m) destroy_model(m);
+    return rc;
+}
+
+int at_model_set_tensor(at_model* m, const char* cname, int type, const void* data, size_t bytes, int on_device) {
+    void* staging = nullptr;
+    const int rc = guard([&] {
+        AT_REQUIRE(m && cname && data, AT_ERR_INVALID_ARG, "null argument");
+        AT_REQUIRE(!m->finalized, AT_ERR_STATE, "model already finalized");
+        at_ctx* c = m->ctx;
+        AT_CUDA(cudaSetDevice(c->device));
+        const std::string name(cname);
+        const int W = c->world, r = c->rank;
+        const int d = m->d, hd = m->hd;
+        int layer = -1;
+        std::string leaf;
+        const bool is_layer = parse_layer(name, &layer, &leaf);
+        if (is_layer) AT_REQUIRE(layer >= 0 && layer < m->L, AT_ERR_INVALID_ARG, "layer index out of range: " + name);
+        const bool is_norm = (name == "output_norm.weight") || (is_layer && (leaf == "attn_norm.weight" ||
+                                                                              leaf == "ffn_norm.weight"));
+        // element count of the logical tensor (inference/Weights.java:84-112)
+        int64_t rows = 0, cols = 0;
+        if (is_norm) { rows = 1; cols = d; }
+        else if (name == "token_embd.weight" || name == "output.weight") { rows = m->V; cols = d; }
+        else if (is_layer && leaf == "attn_q.weight") { rows = d; cols = (int64_t)m->H * hd; }
+        else if (is_layer && (leaf == "attn_k.weight" || leaf == "attn_v.weight")) { rows = d; cols = (int64_t)m->Hkv * hd; }
+        else if (is_layer && leaf == "attn_output.weight") { rows = (int64_t)m->H * hd; cols = d; }
+        else if (is_layer && (leaf == "ffn_gate.weight" || leaf == "ffn_up.weight")) { rows = m->F; cols = d; }
+        else if (is_layer && leaf == "ffn_down.weight") { rows = d; cols = m->F; }
+        else return;  // tensors the decode path does not read are ignored, as in Weights.load
+        const int64_t numel = rows * cols;
+        size_t expect;
+        if (type == AT_GGML_F32) expect = (size_t)numel * 4;
+        else if (type == AT_GGML_F16) expect = (size_t)numel * 2;
+        else if (type == AT_GGML_Q4_0 || type == AT_GGML_Q8_0) expect = (size_t)(numel / 32) * block_bytes(type);
+        else fail(AT_ERR_UNSUPPORTED, "tensor '" + name + "' has unsupported type " + std::to_string(type));
+        AT_REQUIRE(bytes == expect, AT_ERR_INVALID_ARG,
+                   "tensor '" + name + "' has " + std::to_string(bytes) + " bytes, expected " + std::to_string(expect));
+        const void* src = data;
+        if (!on_device) {
+            AT_CUDA(cudaMalloc(&staging, bytes));
+            AT_CUDA(cudaMemcpyAsync(staging, data, bytes, cudaMemcpyHostToDevice, c->stream));
+            src = staging;
+        }
+        const uint8_t* s8 = static_cast<const uint8_t*>(src);
+        if (is_norm) {
+            float** dst = (name == "output_norm.weight") ? &m->out_norm
+                          : (leaf == "attn_norm.weight" ? &m->layers[layer].attn_norm : &m->layers[layer].ffn_norm);
+            if (!*dst) alloc_zero((void**)dst, (size_t)d * 4);
+            at_qmat tmp;
+            tmp.type = AT_GGML_F32; tmp.rows = 1; tmp.cols = d; tmp.f32 = *dst; tmp.owns = false;
+            qmat_fill_from_float(&tmp, src, type, d, 0, 0, c->stream);
+        } else {
+            AT_REQUIRE(type == AT_GGML_Q4_0 || type == AT_GGML_Q8_0, AT_ERR_UNSUPPORTED,
+                       "tensor '" + name + "': the device path keeps weight matrices in Q4_0 or Q8_0");
+            if (m->wtype < 0) m->wtype = type;
+            auto place = [&](at_qmat& q, int orient, int64_t qr, int64_t qc, int64_t sr0, int64_t sc0, int64_t nr,
+                             int64_t nc, int64_t dr0, int64_t dc0) {
+                make_qmat(q, type, orient, qr, qc);
+                AT_REQUIRE(q.type == type, AT_ERR_UNSUPPORTED,
+                           "tensor '" + name + "' differs in type from the tensors fused with it");
+                qmat_fill_region(&q, s8, cols, sr0, sc0, nr, nc, dr0, dc0, c->stream);
+            };
+            const int64_t qcols = (int64_t)(m->Hl + 2 * m->Hkvl) * hd;
+            if (name == "token_embd.weight") {
+                place(m->tok, AT_ORIENT_N, m->V, d, 0, 0, m->V, d, 0, 0);
+            } else if (name == "output.weight") {
+                const int64_t v0 = (int64_t)r * m->Vl;
+                const int64_t nv = std::max<int64_t>(0, std::min<int64_t>(m->Vl, m->V - v0));
+                place(m->out, AT_ORIENT_N, m->Vl, d, v0, 0, nv, d, 0, 0);
+            } else {
+                Layer& ly = m->layers[layer];
+                if (leaf == "attn_q.weight")
+                    place(ly.qkv, AT_ORIENT_T, d, qcols, 0, (int64_t)r * m->Hl * hd, d, (int64_t)m->Hl * hd, 0, 0);
+                else if (leaf == "attn_k.weight")
+                    place(ly.qkv, AT_ORIENT_T, d, qcols, 0, (int64_t)r * m->Hkvl * hd, d, (int64_t)m->Hkvl * hd, 0,
+                          (int64_t)m->Hl * hd);
+                else if (leaf == "attn_v.weight")
+                    place(ly.qkv, AT_ORIENT_T, d, qcols, 0, (int64_t)r * m->Hkvl * hd, d, (int64_t)m->Hkvl * hd, 0,
+                          (int64_t)(m->Hl + m->Hkvl) * hd);
+                else if (leaf == "attn_output.weight")
+                    place(ly.wo, AT_ORIENT_T, (int64_t)m->Hl * hd, d, (int64_t)r * m->Hl * hd, 0, (int64_t)m->Hl * hd, d,
+                          0, 0);
+                else if (leaf == "ffn_gate.weight")
+                    place(ly.w1, AT_ORIENT_N, m->Fl, d, (int64_t)r * m->Fl, 0, m->Fl, d, 0, 0);
+                else if (leaf == "ffn_up.weight")
+                    place(ly.w3, AT_ORIENT_N, m->Fl, d, (int64_t)r * m->Fl, 0, m->Fl, d, 0, 0);
+                else if (leaf == "ffn_down.weight")
+                    place(ly.w2, AT_ORIENT_N, d, m->Fl, 0, (int64_t)r * m->Fl, d, m->Fl, 0, 0);
+            }
+        }
+        AT_CUDA(cudaStreamSynchronize(c->stream));
+        m->seen[name] = true;
+    });
+    if (staging) cudaFree(staging);
+    return rc;
+}
+
+int at_model_finalize(at_model* m) {
+    return guard([&] {
+        AT_REQUIRE(m, AT_ERR_INVALID_ARG, "null model");
+        if (m->finalized) return;
+        at_ctx* c = m->ctx;
+        AT_CUDA(cudaSetDevice(c->device));
+        const int d = m->d, hd = m->hd, B = m->B;
+        const int wt = m->wtype < 0 ? AT_GGML_Q8_0 : m->wtype;
+        const int64_t qcols = (int64_t)(m->Hl + 2 * m->Hkvl) * hd;
+        // Missing tensors become zeros (inference/Weights.java:131-135).
+        make_qmat(m->tok, wt, AT_ORIENT_N, m->V, d);
+        make_qmat(m->out, wt, AT_ORIENT_N, m->Vl, d);
+        if (!m->out_norm) alloc_zero((void**)&m->out_norm, (size_t)d * 4);
+        for (auto& ly : m->layers) {
+            make_qmat(ly.qkv, wt, AT_ORIENT_T, d, qcols);
+            make_qmat(ly.wo, wt, AT_ORIENT_T, (int64_t)m->Hl * hd, d);
+            make_qmat(ly.w1, wt, AT_ORIENT_N, m->Fl, d);
+            make_qmat(ly.w3, ly.w1.type, AT_ORIENT_N, m->Fl, d);
+            make_qmat(ly.w2, wt, AT_ORIENT_N, d, m->Fl);
+            if (!ly.attn_norm) alloc_zero((void**)&ly.attn_norm, (size_t)d * 4);
+            if (!ly.ffn_norm) alloc_zero((void**)&ly.ffn_norm, (size_t)d * 4);
+            AT_REQUIRE(ly.w1.type == ly.w3.type, AT_ERR_UNSUPPORTED, "ffn_gate and ffn_up must share a type");
+        }
+        // activations
+        alloc_zero((void**)&m->xa, (size_t)B * d * 4);
+        alloc_zero((void**)&m->xb, (size_t)B * d * 4);
+        alloc_zero((void**)&m->y, (size_t)B * d * 4);
+        alloc_zero((void**)&m->q, (size_t)B * m->Hl * hd * 4);
+        alloc_zero((void**)&m->att, (size_t)B * m->Hl * hd * 4);
+        alloc_zero((void**)&m->h, (size_t)B * m->Fl * 4);
+        alloc_zero((void**)&m->logits, (size_t)B * m->V * 4);
+        if (c->world > 1) {
+            alloc_zero((void**)&m->logits_local, (size_t)B * m->Vl * 4);
+            alloc_zero((void**)&m->gather, (size_t)c->world * B * m->Vl * 4);
+        }
+        m->nchunk_max = (m->ctx_len + CH - 1) / CH;
+        alloc_zero((void**)&m->att_part, (size_t)B * m->Hl * m->nchunk_max * (hd + 2) * 4);
+        // KV cache (inference/KVCache.java:43-63): [slot][layer][kvHead][ctx][headDim] fp32
+        m->slot_stride = (int64_t)m->L * m->Hkvl * m->ctx_len * hd;
+        alloc_zero((void**)&m->kcache, (size_t)B * m->slot_stride * 4);
+        alloc_zero((void**)&m->vcache, (size_t)B * m->slot_stride * 4);
+        // RoPE tables (inference/RopeCache.java:154-177): freq = (float) pow(base, -2i/hd)
+        // in double, angle = pos * freq in float, cos/sin in double then float.
+        {
+            std::vector<float> cs((size_t)m->ctx_len * hd), sn((size_t)m->ctx_len * hd);
+            const double base = (double)m->cfg.rope_freq_base;
+            for (int64_t p = 0; p < m->ctx_len; ++p)
+                for (int i = 0; i < hd / 2; ++i) {
+                    const float freq = (float)std::pow(base, -2.0 * i / (double)hd);
+                    const float ang = (float)p * freq;
+                    const float cv = (float)std::cos((double)ang), sv = (float)std::sin((double)ang);
+                    cs[p * hd + 2 * i] = cv; cs[p * hd + 2 * i + 1] = cv;
+                    sn[p * hd + 2 * i] = sv; sn[p * hd + 2 * i + 1] = sv;
+                }
+            AT_CUDA(cudaMalloc(&m->rope_cos, cs.size() * 4));
+            AT_CUDA(cudaMalloc(&m->rope_sin, sn.size() * 4));
+            AT_CUDA(cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+            AT_CUDA(cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+        }
+        // split scratch for the T GEMVs at every batch size
+        size_t nf = 16, nc = 16;
+        for (int b = 1; b <= B; ++b) {
+            size_t f1, c1;
+            gemv_t_scratch_need(&m->layers[0].qkv, b, c->num_sms, &f1, &c1);
+            nf = std::max(nf, f1); nc = std::max(nc, c1);
+            gemv_t_scratch_need(&m->layers[0].wo, b, c->num_sms, &f1, &c1);
+            nf = std::max(nf, f1); nc = std::max(nc, c1);
+        }
+        alloc_zero((void**)&m->scratch, nf * 4);
+        alloc_zero((void**)&m->counters, nc * 4);
+        alloc_zero((void**)&m->d_tokens, 8 * sizeof(int));
+        alloc_zero((void**)&m->d_pos, 8 * sizeof(int64_t));
+        alloc_zero((void**)&m->d_argmax, 8 * sizeof(int));
+        AT_CUDA(cudaMallocHost(&m->h_tokens, 8 * sizeof(int)));
+        AT_CUDA(cudaMallocHost(&m->h_pos, 8 * sizeof(int64_t)));
+        AT_CUDA(cudaDeviceSynchronize());
+        m->finalized = true;
+    });
+}
+
+int at_model_load_gguf(at_ctx* ctx, const char* path, int max_batch, at_model** out) {
+    int fd = -1;
+    void* map = MAP_FAILED;
+    size_t len = 0;
+    at_model* m = nullptr;
+    const int rc = guard([&] {
+        AT_REQUIRE(ctx && path && out, AT_ERR_INVALID_ARG, "null argument");
+        fd = open(path, O_RDONLY);
+        AT_REQUIRE(fd >= 0, AT_ERR_IO, std::string("cannot open ") + path);
+        struct stat st;
+        AT_REQUIRE(fstat(fd, &st) == 0, AT_ERR_IO, "fstat failed");
+        len = (size_t)st.st_size;
+        AT_REQUIRE(len >= 24, AT_ERR_IO, "Not a GGUF file: too short");
+        map = mmap(nullptr, len, PROT_READ, MAP_PRIVATE, fd, 0);
+        AT_REQUIRE(map != MAP_FAILED, AT_ERR_IO, "mmap failed");
+        GgufView v{static_cast<const uint8_t*>(map), len, 0};
+        const uint32_t magic = v.rd<uint32_t>();
+        if (magic != 0x46554747u) {
+            char buf[64];
+            snprintf(buf, sizeof buf, "Not a GGUF file: magic=0x%x", magic);
+            fail(AT_ERR_IO, buf);
+        }
+        const uint32_t version = v.rd<uint32_t>();
+        AT_REQUIRE(version == 3, AT_ERR_IO,
+                   "Unsupported GGUF version: " + std::to_string(version) + " (AuraTensor supports v3)");
+        const int64_t n_tensors = v.rd<int64_t>();
+        const int64_t n_kv = v.rd<int64_t>();
+        AT_REQUIRE(n_tensors >= 0 && n_kv >= 0, AT_ERR_IO, "negative counts in GGUF header");
+        std::map<std::string, MetaVal> meta;
+        for (int64_t i = 0; i < n_kv; ++i) {
+            std::string k = v.str();
+            const int vt = v.rd<int32_t>();
+            meta[k] = read_value(v, vt);
+        }
+        struct TI { std::string name; int type; int64_t numel; uint64_t off; };
+        std::vector<TI> tis;
+        for (int64_t i = 0; i < n_tensors; ++i) {
+            TI t;
+            t.name = v.str();
+            const int nd = v.rd<int32_t>();
+            AT_REQUIRE(nd >= 1 && nd <= 4, AT_ERR_IO, "Unsupported rank: " + std::to_string(nd) + " (" + t.name + ")");
+            t.numel = 1;
+            for (int k = 0; k < nd; ++k) t.numel *= v.rd<int64_t>();
+            t.type = v.rd<int32_t>();
+            t.off = v.rd<uint64_t>();
+            tis.push_back(t);
+        }
+        // LlamaConfig.fromGguf (inference/LlamaConfig.java:30-53)
+        auto s_or = [&](const std::string& k, const std::string& dflt) {
+            auto it = meta.find(k);
+            return (it == meta.end() || it->second.type != 8) ? dflt : it->second.s;
+        };
+        auto n_or = [&](const std::string& k, double dflt) {
+            auto it = meta.find(k);
+            if (it == meta.end()) return dflt;
+            AT_REQUIRE(it->second.is_num, AT_ERR_STATE, "Metadata '" + k + "' is not a number");
+            return it->second.num;
+        };
+        const std::string arch = s_or("general.architecture", "llama");
+        at_model_config cfg{};
+        cfg.context_length = (int64_t)n_or(arch + ".context_length", 4096);
+        cfg.embedding_length = (int64_t)n_or(arch + ".embedding_length", 4096);
+        cfg.block_count = (int64_t)n_or(arch + ".block_count", 32);
+        cfg.head_count = (int64_t)n_or(arch + ".attention.head_count", 32);
+        cfg.head_count_kv = (int64_t)n_or(arch + ".attention.head_count_kv", (double)cfg.head_count);
+        cfg.feed_forward_length = (int64_t)n_or(arch + ".feed_forward_length", 11008);
+        const bool llama_big = arch.find("llama") != std::string::npos && cfg.embedding_length >= 4096;
+        cfg.rope_freq_base = (float)n_or(arch + ".rope.freq_base", llama_big ? 500000.0 : 10000.0);
+        cfg.rms_norm_eps = (float)n_or(arch + ".attention.layer_norm_rms_epsilon", 1e-5);
+        cfg.vocab_size = (int64_t)n_or(arch + ".vocab_size", n_or("tokenizer.ggml.vocab_size", 32000));
+        cfg.max_batch = max_batch < 1 ? 1 : max_batch;
+        const int64_t align = (int64_t)n_or("general.alignment", 32);
+        AT_REQUIRE(align > 0, AT_ERR_IO, "bad general.alignment");
+        const uint64_t data_off = ((v.pos + align - 1) / align) * align;
+        int rc2 = at_model_create(ctx, &cfg, &m);
+        if (rc2 != AT_OK) fail(rc2, "model creation failed");
+        for (const TI& t : tis) {
+            int64_t bytes;
+            if (t.type == AT_GGML_F32) bytes = t.numel * 4;
+            else if (t.type == AT_GGML_F16) bytes = t.numel * 2;
+            else if (t.type == AT_GGML_Q4_0) bytes = (t.numel + 31) / 32 * 18;
+            else if (t.type == AT_GGML_Q8_0) bytes = (t.numel + 31) / 32 * 34;
+            else continue;  // types the decode path cannot use stay zero stand-ins (inference/Weights.java:143-149)
+            AT_REQUIRE(data_off + t.off + (uint64_t)bytes <= len, AT_ERR_IO, "tensor '" + t.name + "' past end of file");
+            rc2 = at_model_set_tensor(m, t.name.c_str(), t.type, static_cast<const uint8_t*>(map) + data_off + t.off,
+                                      (size_t)bytes, 0);
+            if (rc2 != AT_OK) {
+                char msg[512];
+                at_last_error(msg, sizeof msg);
+                fail(rc2, msg);
+            }
+        }
+        rc2 = at_model_finalize(m);
+        if (rc2 != AT_OK) {
+            char msg[512];
+            at_last_error(msg, sizeof msg);
+            fail(rc2, msg);
+        }
+        *out = m;
+    });
+    if (map != MAP_FAILED) munmap(map, len);
+    if (fd >= 0) close(fd);
+    if (rc != AT_OK && m) destroy_model(m);
+    return rc;
+}
+
+int at_model_get_config(const at_model* m, at_model_config* out) {
+    return guard([&] {
+        AT_REQUIRE(m && out, AT_ERR_INVALID_ARG, "null argument");
+        *out = m->cfg;
+    });
+}
+
+int at_model_destroy(at_model* m) {
+    return guard([&] { destroy_model(m); });
+}
+
+int at_model_forward_step(at_model* m, int token, int64_t position, float* logits_host) {
+    return guard([&] { run_step(m, &token, &position, 1, logits_host); });
+}
+
+int at_model_forward_prompt(at_model* m, const int* tokens, int n) {
+    return guard([&] {
+        AT_REQUIRE(m && (n == 0 || tokens), AT_ERR_INVALID_ARG, "null argument");
+        // LlamaModel.forwardPrompt (inference/LlamaModel.java:167-170)
+        AT_REQUIRE(n >= 0 && n < m->ctx_len, AT_ERR_INVALID_ARG,
+                   "Prompt length " + std::to_string(n) + " exceeds contextLength " + std::to_string(m->ctx_len));
+        for (int i = 0; i < n; ++i) {
+            const int64_t p = i;
+            run_step(m, tokens + i, &p, 1, nullptr);
+        }
+    });
+}
+
+int at_model_forward_batch(at_model* m, const int* tokens, const int64_t* positions, int batch, float* logits_host) {
+    return guard([&] { run_step(m, tokens, positions, batch, logits_host); });
+}
+
+int at_model_logits_device(at_model* m, float** logits_dev) {
+    return guard([&] {
+        AT_REQUIRE(m && logits_dev && m->finalized, AT_ERR_INVALID_ARG, "bad argument");
+        *logits_dev = m->logits;
+    });
+}
+
+int at_model_argmax(at_model* m, int batch, int* tokens_host) {
+    return guard([&] {
+        AT_REQUIRE(m && tokens_host && m->finalized, AT_ERR_INVALID_ARG, "bad argument");
+        AT_REQUIRE(batch >= 1 && batch <= m->B, AT_ERR_INVALID_ARG, "batch out of range");
+        AT_CUDA(cudaMemcpyAsync(tokens_host, m->d_argmax, sizeof(int) * batch, cudaMemcpyDeviceToHost, m->ctx->stream));
+        AT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    });
+}
+
+int at_model_kv_size(const at_model* m, int slot, int64_t* size) {
+    return guard([&] {
+        AT_REQUIRE(m && size, AT_ERR_INVALID_ARG, "null argument");
+        AT_REQUIRE(slot >= 0 && slot < m->B, AT_ERR_INVALID_ARG, "slot out of range");
+        *size = m->kv_size[slot];
+    });
+}
+
+int at_model_kv_read(at_model* m, int slot, int layer, int kv_head, int64_t position, float* k_host, float* v_host) {
+    return guard([&] {
+        AT_REQUIRE(m && m->finalized && k_host && v_host, AT_ERR_INVALID_ARG, "bad argument");
+        // KVCache.offsetOf bounds (inference/KVCache.java:70-76); kv_head is rank-local under TP
+        AT_REQUIRE(slot >= 0 && slot < m->B, AT_ERR_INVALID_ARG, "slot oob");
+        AT_REQUIRE(layer >= 0 && layer < m->L, AT_ERR_INVALID_ARG, "layer oob");
+        AT_REQUIRE(kv_head >= 0 && kv_head < m->Hkvl, AT_ERR_INVALID_ARG, "kvHead oob");
+        AT_REQUIRE(position >= 0 && position < m->ctx_len, AT_ERR_INVALID_ARG, "position oob");
+        const size_t off = (size_t)slot * m->slot_stride +
+                           (((size_t)layer * m->Hkvl + kv_head) * m->ctx_len + (size_t)position) * m->hd;
+        AT_CUDA(cudaMemcpyAsync(k_host, m->kcache + off, m->hd * 4, cudaMemcpyDeviceToHost, m->ctx->stream));
+        AT_CUDA(cudaMemcpyAsync(v_host, m->vcache + off, m->hd * 4, cudaMemcpyDeviceToHost, m->ctx->stream));
+        AT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    });
+}
+
+int at_model_kv_reset(at_model* m, int slot) {
+    return guard([&] {
+        AT_REQUIRE(m && m->finalized, AT_ERR_INVALID_ARG, "bad argument");
+        AT_REQUIRE(slot >= 0 && slot < m->B, AT_ERR_INVALID_ARG, "slot out of range");
+        AT_CUDA(cudaMemsetAsync(m->kcache + (size_t)slot * m->slot_stride, 0, (size_t)m->slot_stride * 4, m->ctx->stream));
+        AT_CUDA(cudaMemsetAsync(m->vcache + (size_t)slot * m->slot_stride, 0, (size_t)m->slot_stride * 4, m->ctx->stream));
+        AT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+        m->kv_size[slot] = 0;
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,100 @@
+// Sampler.sample (inference/Sampler.java:37-121) on the host, with the same
+// float arithmetic and the java.util.Random generator it seeds per call.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdint>
+#include <numeric>
+#include <vector>
+
+#include "at_internal.h"
+
+namespace {
+
+// java.util.Random: the 48-bit LCG specified in the Java SE API documentation.
+struct JavaRandom {
+    uint64_t seed;
+    explicit JavaRandom(int64_t s) : seed(((uint64_t)s ^ 0x5DEECE66DULL) & ((1ULL << 48) - 1)) {}
+    int32_t next(int bits) {
+        seed = (seed * 0x5DEECE66DULL + 0xBULL) & ((1ULL << 48) - 1);
+        return (int32_t)(int64_t)(seed >> (48 - bits));
+    }
+    float next_float() { return (float)next(24) / (float)(1 << 24); }
+};
+
+// Double.compare(x, y) < 0: NaN is above +inf and -0.0 is below 0.0.
+bool java_double_less(double x, double y) {
+    if (std::isnan(x)) return false;
+    if (std::isnan(y)) return true;
+    if (x != y) return x < y;
+    return std::signbit(x) && !std::signbit(y);
+}
+
+}  // namespace
+
+extern "C" int at_sample(float* logits, int vocab, const int* history, int n_history, float temperature, int top_k,
+                         float top_p, float rep_penalty, int64_t seed, int* out_token) {
+    return at::guard([&] {
+        AT_REQUIRE(logits && out_token && vocab > 0, AT_ERR_INVALID_ARG, "bad sampler argument");
+        // 1) repetition penalty, in place (Sampler.java:44-53)
+        if (rep_penalty != 1.0f && history && n_history > 0) {
+            for (int i = 0; i < n_history; ++i) {
+                const int t = history[i];
+                if (t >= 0 && t < vocab) {
+                    if (logits[t] > 0) logits[t] = logits[t] / rep_penalty;
+                    else logits[t] = logits[t] * rep_penalty;
+                }
+            }
+        }
+        // 2) greedy fast path (Sampler.java:56-67)
+        if (temperature == 0.0f || (top_k == 1 && top_p >= 1.0f)) {
+            int best = 0;
+            float bs = logits[0];
+            for (int i = 1; i < vocab; ++i)
+                if (logits[i] > bs) { bs = logits[i]; best = i; }
+            *out_token = best;
+            return;
+        }
+        // 3) temperature, stable descending sort, top-k, top-p (Sampler.java:71-110)
+        const float inv_t = 1.0f / temperature;
+        std::vector<float> adj(vocab);
+        for (int i = 0; i < vocab; ++i) adj[i] = logits[i] * inv_t;
+        std::vector<int> idx(vocab);
+        std::iota(idx.begin(), idx.end(), 0);
+        // Comparator.comparingDouble(..).reversed(): b before a when
+        // Double.compare(adj[a], adj[b]) < 0; List.sort is stable.
+        std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return java_double_less(adj[b], adj[a]); });
+        const int k = std::min(top_k, vocab);
+        AT_REQUIRE(k >= 1, AT_ERR_INVALID_ARG, "topK must be positive");
+        const float max_logit = adj[idx[0]];
+        std::vector<float> probs(k);
+        float sum_exp = 0.0f;
+        for (int i = 0; i < k; ++i) {
+            const float p = (float)std::exp((double)(adj[idx[i]] - max_logit));
+            probs[i] = p;
+            sum_exp += p;
+        }
+        int cutoff = k;
+        if (top_p < 1.0f) {
+            float running = 0.0f;
+            const float total = sum_exp;
+            for (int i = 0; i < k; ++i) {
+                running += probs[i];
+                if (running / total >= top_p) { cutoff = i + 1; break; }
+            }
+        }
+        float new_sum = 0.0f;
+        for (int i = 0; i < cutoff; ++i) new_sum += probs[i];
+        for (int i = 0; i < cutoff; ++i) probs[i] /= new_sum;
+        // 4) r from a fresh java.util.Random(seed); seed 0 means an unseeded generator
+        int64_t s = seed;
+        if (s == 0) s = (int64_t)std::chrono::steady_clock::now().time_since_epoch().count();
+        const float r = JavaRandom(s).next_float();
+        float cum = 0.0f;
+        for (int i = 0; i < cutoff; ++i) {
+            cum += probs[i];
+            if (r <= cum) { *out_token = idx[i]; return; }
+        }
+        *out_token = idx[cutoff - 1];
+    });
+}

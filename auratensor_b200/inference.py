@@ -1,0 +1,267 @@
+"""Device mirror of the reference's inference package: LlamaConfig, Weights
+loading, LlamaModel, KVCache and Sampler (inference/*.java).
+
+``LlamaModel`` owns an ``at_model`` of libauratensor_cuda.so: the raw Q4_0 /
+Q8_0 blocks are uploaded once and every forward step runs as one CUDA graph.
+``forwardStep`` returns the logits as a float32 numpy array, as the reference
+returns ``float[]``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import ModelConfig, call
+from .core import context
+from .gguf import GgufFile
+
+
+@dataclass
+class LlamaConfig:
+    """inference/LlamaConfig.java:12-53."""
+    architecture: str = "llama"
+    contextLength: int = 4096
+    embeddingLength: int = 4096
+    blockCount: int = 32
+    headCount: int = 32
+    headCountKv: int = 32
+    feedForwardLength: int = 11008
+    ropeFrequencyBase: float = 10000.0
+    rmsNormEpsilon: float = 1e-5
+    vocabSize: int = 32000
+
+    def headDim(self) -> int:
+        if self.headCount == 0:
+            raise _lib.IllegalStateException(_lib.AT_ERR_STATE, "headCount == 0")
+        return self.embeddingLength // self.headCount
+
+    @classmethod
+    def fromGguf(cls, m) -> "LlamaConfig":
+        arch = m.string_or_default("general.architecture", "llama")
+        n_emb = m.long_or_default(arch + ".embedding_length", 4096)
+        n_heads = m.long_or_default(arch + ".attention.head_count", 32)
+        rope_default = 500000.0 if ("llama" in arch and n_emb >= 4096) else 10000.0
+        return cls(
+            architecture=arch,
+            contextLength=m.long_or_default(arch + ".context_length", 4096),
+            embeddingLength=n_emb,
+            blockCount=m.long_or_default(arch + ".block_count", 32),
+            headCount=n_heads,
+            headCountKv=m.long_or_default(arch + ".attention.head_count_kv", n_heads),
+            feedForwardLength=m.long_or_default(arch + ".feed_forward_length", 11008),
+            ropeFrequencyBase=float(np.float32(m.float_or_default(arch + ".rope.freq_base", rope_default))),
+            rmsNormEpsilon=float(np.float32(m.float_or_default(arch + ".attention.layer_norm_rms_epsilon", 1e-5))),
+            vocabSize=m.long_or_default(arch + ".vocab_size", m.long_or_default("tokenizer.ggml.vocab_size", 32000)),
+        )
+
+    @classmethod
+    def fromShape(cls, s) -> "LlamaConfig":
+        return cls("llama", s.ctx, s.dim, s.n_layers, s.n_heads, s.n_kv_heads, s.ffn, float(s.rope_theta),
+                   float(s.eps), s.vocab)
+
+    def to_c(self, max_batch: int = 1) -> ModelConfig:
+        return ModelConfig(self.contextLength, self.embeddingLength, self.blockCount, self.headCount,
+                           self.headCountKv, self.feedForwardLength, self.vocabSize, self.ropeFrequencyBase,
+                           self.rmsNormEpsilon, max_batch, 0)
+
+
+class KVCache:
+    """View of the device KV cache of one sequence slot (inference/KVCache.java:29-111)."""
+
+    def __init__(self, model: "LlamaModel", slot: int = 0):
+        self._m, self._slot = model, slot
+        c = model.config
+        self._dims = (c.blockCount, c.headCountKv // model.world, c.headDim(), c.contextLength)
+
+    def size(self) -> int:
+        v = C.c_int64()
+        call("at_model_kv_size", self._m._h, self._slot, C.byref(v))
+        return v.value
+
+    def maxContext(self) -> int:
+        return self._dims[3]
+
+    def blockCount(self) -> int:
+        return self._dims[0]
+
+    def headCountKv(self) -> int:
+        return self._dims[1]
+
+    def headDim(self) -> int:
+        return self._dims[2]
+
+    def rowBytes(self) -> int:
+        return self._dims[3] * self._dims[2] * 4
+
+    def offsetOf(self, layer, kv_head, position, dim) -> int:
+        L, H, hd, ctx = self._dims
+        if not 0 <= layer < L:
+            raise _lib.IllegalArgumentException(_lib.AT_ERR_INVALID_ARG, "layer oob")
+        if not 0 <= kv_head < H:
+            raise _lib.IllegalArgumentException(_lib.AT_ERR_INVALID_ARG, "kvHead oob")
+        if not 0 <= position < ctx:
+            raise _lib.IllegalArgumentException(_lib.AT_ERR_INVALID_ARG, "position oob")
+        if dim >= hd:
+            raise _lib.IllegalArgumentException(_lib.AT_ERR_INVALID_ARG, "dim oob")
+        return ((layer * H) + kv_head) * self.rowBytes() + position * hd * 4 + dim * 4
+
+    def read(self, layer: int, kv_head: int, position: int):
+        hd = self._dims[2]
+        k = np.empty(hd, dtype=np.float32)
+        v = np.empty(hd, dtype=np.float32)
+        call("at_model_kv_read", self._m._h, self._slot, layer, kv_head, position,
+             k.ctypes.data_as(C.c_void_p), v.ctypes.data_as(C.c_void_p))
+        return k, v
+
+    def reset(self) -> None:
+        call("at_model_kv_reset", self._m._h, self._slot)
+
+
+class LlamaModel:
+    """inference/LlamaModel.java:41-381 on the device.
+
+    Build from a GGUF path (``LlamaModel.fromGguf``), or from a config plus a
+    {name: raw bytes} tensor table (``LlamaModel(config, tensors)``); tensors
+    may be numpy arrays / bytes (uploaded once) or uint8 CUDA tensors.
+    Under tensor parallelism pass ``ctx`` from ``tp.init_tp_context``.
+    """
+
+    def __init__(self, config: LlamaConfig, tensors: dict | None = None, max_batch: int = 1, ctx=None,
+                 world: int = 1):
+        self.config = config
+        self.max_batch = max_batch
+        self.world = world
+        self._ctx = ctx if ctx is not None else context()
+        self._h = C.c_void_p()
+        cfg = config.to_c(max_batch)
+        call("at_model_create", self._ctx, C.byref(cfg), C.byref(self._h))
+        self._logits = np.empty((max_batch, config.vocabSize), dtype=np.float32)
+        if tensors is not None:
+            for name, t in tensors.items():
+                self.setTensor(name, t["type"], t["data"])
+            self.finalize()
+
+    @classmethod
+    def fromGguf(cls, path: str, max_batch: int = 1) -> "LlamaModel":
+        with GgufFile.open(path) as g:
+            cfg = LlamaConfig.fromGguf(g.metadata)
+        self = cls.__new__(cls)
+        self.config = cfg
+        self.max_batch = max_batch
+        self.world = 1
+        self._ctx = context()
+        self._h = C.c_void_p()
+        call("at_model_load_gguf", self._ctx, path.encode(), max_batch, C.byref(self._h))
+        self._logits = np.empty((max_batch, cfg.vocabSize), dtype=np.float32)
+        return self
+
+    def setTensor(self, name: str, ggml_type: int, data) -> None:
+        if isinstance(data, torch.Tensor) and data.is_cuda:
+            d = data.contiguous()
+            call("at_model_set_tensor", self._h, name.encode(), ggml_type, C.c_void_p(d.data_ptr()),
+                 d.numel() * d.element_size(), 1)
+        else:
+            arr = np.ascontiguousarray(np.frombuffer(memoryview(data), dtype=np.uint8))
+            call("at_model_set_tensor", self._h, name.encode(), ggml_type, arr.ctypes.data_as(C.c_void_p),
+                 arr.nbytes, 0)
+
+    def finalize(self) -> None:
+        call("at_model_finalize", self._h)
+
+    def kvCache(self, slot: int = 0) -> KVCache:
+        return KVCache(self, slot)
+
+    def forwardStep(self, tokenId: int, position: int) -> np.ndarray:
+        """LlamaModel.forwardStep: logits over the vocabulary (host array)."""
+        out = self._logits[0]
+        call("at_model_forward_step", self._h, int(tokenId), int(position), out.ctypes.data_as(C.c_void_p))
+        return out
+
+    def forwardStepDevice(self, tokenId: int, position: int) -> None:
+        """forwardStep without copying the logits to the host."""
+        call("at_model_forward_step", self._h, int(tokenId), int(position), None)
+
+    def forwardPrompt(self, promptTokenIds) -> None:
+        arr = np.ascontiguousarray(np.asarray(promptTokenIds, dtype=np.int32))
+        call("at_model_forward_prompt", self._h, arr.ctypes.data_as(C.c_void_p), int(arr.size))
+        return None
+
+    def forwardBatch(self, tokens, positions, copy_logits: bool = True) -> np.ndarray | None:
+        """One decode step of len(tokens) independent sequences (slot b <- tokens[b])."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        p = np.ascontiguousarray(np.asarray(positions, dtype=np.int64))
+        b = int(t.size)
+        out = self._logits[:b] if copy_logits else None
+        call("at_model_forward_batch", self._h, t.ctypes.data_as(C.c_void_p), p.ctypes.data_as(C.c_void_p), b,
+             out.ctypes.data_as(C.c_void_p) if out is not None else None)
+        return out
+
+    def logitsDevice(self) -> torch.Tensor:
+        """The last step's logits [max_batch][vocab] as a CUDA tensor view."""
+        p = C.c_void_p()
+        call("at_model_logits_device", self._h, C.byref(p))
+        n = self.max_batch * self.config.vocabSize
+        return _device_view(p.value, n, torch.cuda.current_device()).view(self.max_batch, self.config.vocabSize)
+
+    def argmax(self, batch: int = 1) -> np.ndarray:
+        out = np.empty(batch, dtype=np.int32)
+        call("at_model_argmax", self._h, batch, out.ctypes.data_as(C.c_void_p))
+        return out
+
+    def close(self) -> None:
+        if self._h:
+            call("at_model_destroy", self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _device_view(addr: int, n: int, device: int) -> torch.Tensor:
+    """A float32 CUDA tensor aliasing n floats at a device address owned by the library."""
+
+    class _Holder:
+        __cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (addr, False), "version": 3}
+
+    return torch.as_tensor(_Holder(), device=f"cuda:{device}")
+
+
+@dataclass
+class SamplerConfig:
+    """Sampler.Config (inference/Sampler.java:20-30)."""
+    temperature: float = 1.0
+    topK: int = 1
+    topP: float = 1.0
+    repetitionPenalty: float = 1.0
+    seed: int = 0
+
+    @staticmethod
+    def greedy() -> "SamplerConfig":
+        return SamplerConfig(1.0, 1, 1.0, 1.0, 0)
+
+
+class Sampler:
+    """Sampler.sample (inference/Sampler.java:37-121), native host code."""
+    Config = SamplerConfig
+
+    @staticmethod
+    def sample(logits, history, config: SamplerConfig) -> int:
+        arr = np.asarray(logits, dtype=np.float32)
+        if not arr.flags.writeable or not arr.flags.c_contiguous:
+            arr = np.ascontiguousarray(arr).copy()
+        h = None if history is None else np.ascontiguousarray(np.asarray(history, dtype=np.int32))
+        out = C.c_int()
+        call("at_sample", arr.ctypes.data_as(C.c_void_p), int(arr.size),
+             h.ctypes.data_as(C.c_void_p) if h is not None else None, 0 if h is None else int(h.size),
+             float(config.temperature), int(config.topK), float(config.topP), float(config.repetitionPenalty),
+             int(config.seed), C.byref(out))
+        if isinstance(logits, np.ndarray) and arr is not logits and logits.flags.writeable:
+            logits[...] = arr  # the reference mutates logits in place (repetition penalty)
+        return out.value

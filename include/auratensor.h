@@ -1,0 +1,190 @@
+/*
+ * auratensor.h — C ABI of libauratensor_cuda.so, the B200 (sm_100a) engine for
+ * AuraTensor's quantized-matvec decode path.
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes, and
+ * returns an int status (AT_OK = 0, negative = error class). The message of
+ * the last failure on the calling thread is returned by at_last_error().
+ * Device pointers are CUDA device addresses on the context's device.
+ *
+ * The comment above each declaration names the reference interface it
+ * replaces (paths relative to src/main/java/io/auratensor/ in AuraTensor).
+ * The Java side binds these through java.lang.foreign downcall handles.
+ */
+#ifndef AURATENSOR_H
+#define AURATENSOR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. The Java shim maps them to the exception classes the
+ * reference throws for the same condition. */
+#define AT_OK                 0
+#define AT_ERR_INVALID_ARG   -1  /* IllegalArgumentException  (core/Kernels.java:55-57,101-113,332-340) */
+#define AT_ERR_STATE         -2  /* IllegalStateException     (inference/KVCache.java:83-85)           */
+#define AT_ERR_UNSUPPORTED   -3  /* UnsupportedOperationException (format/GgufFile.java:157-163)       */
+#define AT_ERR_IO            -4  /* IOException               (format/GgufFile.java:105-117)           */
+#define AT_ERR_CUDA          -5  /* CUDA runtime failure                                                */
+#define AT_ERR_NCCL          -6  /* NCCL failure                                                        */
+#define AT_ERR_OOM           -7  /* device allocation failed                                            */
+#define AT_ERR_TIMEOUT       -8  /* a bounded wait ran out                                              */
+
+/* GGUF tensor type codes (format/GgufTensorType.java:15-27). */
+#define AT_GGML_F32   0
+#define AT_GGML_F16   1
+#define AT_GGML_Q4_0  2
+#define AT_GGML_Q8_0  8
+
+/* GEMV orientations of a row-major block matrix W[rows][cols] whose
+ * quantization blocks run along cols (inference/LlamaModel.java:326-369).
+ *   AT_ORIENT_N: y[b][r] = sum_c W[r][c] * x[b][c]   (ffn, lm_head: [out][in])
+ *   AT_ORIENT_T: y[b][c] = sum_r W[r][c] * x[b][r]   (wq/wk/wv/wo: [in][out]) */
+#define AT_ORIENT_N 0
+#define AT_ORIENT_T 1
+
+typedef struct at_ctx   at_ctx;    /* one device, one stream, optional NCCL communicator */
+typedef struct at_qmat  at_qmat;   /* device-resident quantized matrix (planar re-layout) */
+typedef struct at_model at_model;  /* device-resident Llama model + KV cache              */
+
+/* ---- runtime ------------------------------------------------------------ */
+const char* at_version(void);
+/* Copies the calling thread's last error message into buf; returns its length. */
+int at_last_error(char* buf, size_t len);
+int at_device_count(int* n);
+/* New: device context (the reference runs on the calling Java thread). */
+int at_ctx_create(int device, at_ctx** out);
+int at_ctx_destroy(at_ctx* ctx);
+int at_ctx_synchronize(at_ctx* ctx);
+/* Returns the cudaStream_t the context launches on. */
+int at_ctx_stream(at_ctx* ctx, void** stream);
+/* Makes the context launch on `stream` (a cudaStream_t of the same device, for
+ * example the host framework's current stream); NULL restores its own stream. */
+int at_ctx_set_stream(at_ctx* ctx, void* stream);
+
+/* ---- memory: Tensor.allocate / wrap / close (core/Tensor.java:88-120,234-239) */
+int at_alloc(at_ctx* ctx, size_t bytes, void** dptr);
+int at_free(at_ctx* ctx, void* dptr);
+int at_memcpy_h2d(at_ctx* ctx, void* dst_dev, const void* src_host, size_t bytes);
+int at_memcpy_d2h(at_ctx* ctx, void* dst_host, const void* src_dev, size_t bytes);
+int at_memset_zero(at_ctx* ctx, void* dst_dev, size_t bytes);
+
+/* ---- fp16: Fp16.toFloat (core/Fp16.java:19-37), subnormals flush to zero -- */
+int at_fp16_to_f32(at_ctx* ctx, const uint16_t* src_dev, float* dst_dev, int64_t n);
+
+/* ---- block codecs ----------------------------------------------------------
+ * src_dev holds raw GGUF blocks (fp16 d first, then qs). n % 32 == 0.       */
+/* Q4_0.dequantToFloat (quant/Q4_0.java:32-45), interleaved nibble order. */
+int at_q4_0_dequant(at_ctx* ctx, const void* src_dev, float* dst_dev, int64_t n);
+/* Q8_0.dequantToFloat (quant/Q8_0.java:32-44). */
+int at_q8_0_dequant(at_ctx* ctx, const void* src_dev, float* dst_dev, int64_t n);
+/* Q4_0.dot (quant/Q4_0.java:51-90) with dequantToFloat semantics over all 32
+ * elements of every block; result written to *out_dev. */
+int at_q4_0_dot(at_ctx* ctx, const void* q4_dev, const float* x_dev, int64_t n, float* out_dev);
+/* Q8_0.dot (quant/Q8_0.java:54-93), same convention. */
+int at_q8_0_dot(at_ctx* ctx, const void* q8_dev, const float* x_dev, int64_t n, float* out_dev);
+
+/* ---- quantized matrices ------------------------------------------------------
+ * Uploads rows*cols elements of raw GGUF blocks (Q4_0, Q8_0, or F32/F16 which
+ * are kept as f32) and re-lays them out losslessly for the given orientation:
+ * scales and quant bytes in separate 16-byte-aligned planes; orientation T is
+ * stored block-column-major. The raw bytes are never re-quantized.
+ * Replaces the load-time dequant of Weights.wrapByName (inference/Weights.java:185-203)
+ * and the transposes of LlamaModel (inference/LlamaModel.java:326-369).  */
+int at_qmat_create(at_ctx* ctx, int ggml_type, int orient, int64_t rows, int64_t cols,
+                   const void* blocks, int blocks_on_device, at_qmat** out);
+int at_qmat_destroy(at_qmat* m);
+/* Writes the matrix back as raw GGUF blocks (row-major) to dst_dev. */
+int at_qmat_export(at_ctx* ctx, const at_qmat* m, void* dst_dev);
+/* Fused dequant GEMV on the stored orientation; x_dev [batch][in], y_dev
+ * [batch][out], 1 <= batch <= 8. Replaces Kernels.sgemv over the dequantized
+ * FP32 weights (core/Kernels.java:331-371) on the model path. */
+int at_gemv(at_ctx* ctx, const at_qmat* m, const float* x_dev, float* y_dev, int batch);
+
+/* ---- Kernels (core/Kernels.java), FP32 device buffers ----------------------- */
+/* Kernels.sgemv(MemorySegment a,x,y,int M,int K)  (core/Kernels.java:350-371) */
+int at_sgemv(at_ctx* ctx, const float* a_dev, const float* x_dev, float* y_dev, int M, int K);
+/* Kernels.sgemm(a,b,c,int M,int K,int N)          (core/Kernels.java:395-452) */
+int at_sgemm(at_ctx* ctx, const float* a_dev, const float* b_dev, float* c_dev, int M, int K, int N);
+/* Kernels.rmsNormInPlace(x, weight, eps) over `rows` rows of length d (core/Kernels.java:100-154) */
+int at_rmsnorm(at_ctx* ctx, float* x_dev, const float* w_dev, float eps, int rows, int d);
+/* Kernels.softmaxInPlace / softmaxInPlaceSegment, per row of length n (core/Kernels.java:161-232) */
+int at_softmax(at_ctx* ctx, float* x_dev, int rows, int n);
+/* Kernels.ropeInPlaceSegment(qk, cos, sin, headDim, n) (core/Kernels.java:274-321) */
+int at_rope(at_ctx* ctx, float* qk_dev, const float* cos_dev, const float* sin_dev, int head_dim, int n);
+/* Kernels.siluInPlaceSegment(seg, n) (core/Kernels.java:61-90) */
+int at_silu(at_ctx* ctx, float* x_dev, int64_t n);
+
+/* ---- model: LlamaConfig / Weights / LlamaModel / KVCache ------------------- */
+typedef struct at_model_config {
+    int64_t context_length;       /* inference/LlamaConfig.java:30 */
+    int64_t embedding_length;
+    int64_t block_count;
+    int64_t head_count;
+    int64_t head_count_kv;
+    int64_t feed_forward_length;
+    int64_t vocab_size;
+    float   rope_freq_base;
+    float   rms_norm_eps;
+    int32_t max_batch;            /* independent sequences (KV slots), 1..8 */
+    int32_t reserved;
+} at_model_config;
+
+/* new LlamaModel(cfg, weights, tok) (inference/LlamaModel.java:79-129) without
+ * weights yet; then at_model_set_tensor per GGUF tensor; then at_model_finalize. */
+int at_model_create(at_ctx* ctx, const at_model_config* cfg, at_model** out);
+/* Weights.wrapByName for one tensor (inference/Weights.java:117-203): name is
+ * the GGUF tensor name ("blk.3.attn_q.weight", ...); data is that tensor's raw
+ * bytes (host, or device when data_on_device != 0), uploaded once. Under
+ * tensor parallelism the rank's shard is cut out on the device. */
+int at_model_set_tensor(at_model* m, const char* name, int ggml_type, const void* data,
+                        size_t bytes, int data_on_device);
+/* Missing tensors become zeros (inference/Weights.java:131-135); builds the
+ * RoPE table (inference/RopeCache.java:154-177), the KV cache and the step graph. */
+int at_model_finalize(at_model* m);
+/* GgufFile.open + LlamaConfig.fromGguf + Weights.load (format/GgufFile.java:97-143,
+ * inference/LlamaConfig.java:30-53, inference/Weights.java:83-115): mmap, parse,
+ * upload raw blocks once. */
+int at_model_load_gguf(at_ctx* ctx, const char* path, int max_batch, at_model** out);
+int at_model_get_config(const at_model* m, at_model_config* out);
+int at_model_destroy(at_model* m);
+/* LlamaModel.forwardStep(tokenId, position) (inference/LlamaModel.java:141-158):
+ * logits_host receives vocab floats (may be NULL to keep them on device). */
+int at_model_forward_step(at_model* m, int token, int64_t position, float* logits_host);
+/* LlamaModel.forwardPrompt (inference/LlamaModel.java:166-175). */
+int at_model_forward_prompt(at_model* m, const int* tokens, int n);
+/* Batched decode of `batch` independent sequences: sequence b uses KV slot b,
+ * token tokens[b] at positions[b]. logits_host: [batch][vocab] or NULL. */
+int at_model_forward_batch(at_model* m, const int* tokens, const int64_t* positions, int batch,
+                           float* logits_host);
+/* Device address of the last step's logits [max_batch][vocab] (full vocab on every rank). */
+int at_model_logits_device(at_model* m, float** logits_dev);
+/* Greedy token of each of the last step's `batch` rows (Sampler greedy path,
+ * inference/Sampler.java:56-67: first index of the maximum). */
+int at_model_argmax(at_model* m, int batch, int* tokens_host);
+/* KVCache.size / offsetOf / keys() / values() (inference/KVCache.java:70-104):
+ * copies head_dim floats of K and V for (slot, layer, kv_head, position). */
+int at_model_kv_size(const at_model* m, int slot, int64_t* size);
+int at_model_kv_read(at_model* m, int slot, int layer, int kv_head, int64_t position,
+                     float* k_host, float* v_host);
+/* Rewinds a sequence slot to empty (the reference builds a new KVCache). */
+int at_model_kv_reset(at_model* m, int slot);
+
+/* ---- sampler: Sampler.sample (inference/Sampler.java:37-121), host -------- */
+int at_sample(float* logits, int vocab, const int* history, int n_history, float temperature,
+              int top_k, float top_p, float repetition_penalty, int64_t seed, int* out_token);
+
+/* ---- tensor parallelism over NCCL (new: the reference is single-process) --- */
+/* 128-byte ncclUniqueId for rank 0 to broadcast to the other ranks. */
+int at_tp_unique_id(uint8_t out_id[128]);
+/* Context whose models shard weights Megatron-style over `world` ranks and
+ * all-reduce after each attention block and each MLP block. */
+int at_ctx_create_tp(int device, int rank, int world, const uint8_t id[128], at_ctx** out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AURATENSOR_H */

@@ -1,0 +1,139 @@
+"""LlamaModel.forwardStep on the GPU vs the oracle restatement of the reference.
+
+Parity rule (FP32 GEMV path): at every teacher-forced step,
+max |logit_gpu - logit_ref| <= 1e-3 x (max - min of the reference logits);
+greedy tokens are identical except where the reference's top-2 gap is below
+that tolerance.
+"""
+import numpy as np
+import pytest
+
+from auratensor_b200 import _lib, synth
+from auratensor_b200.inference import LlamaConfig, LlamaModel
+from oracle import ref
+
+pytestmark = pytest.mark.gpu
+REL_TOL = 1e-3
+
+
+def oracle_cfg(s):
+    return ref.LlamaConfig(s.ctx, s.dim, s.n_layers, s.n_heads, s.n_kv_heads, s.ffn, s.rope_theta, s.eps, s.vocab)
+
+
+def teacher_forced(shape, tensors, prompt, n_decode, max_batch=1):
+    gpu = LlamaModel(LlamaConfig.fromShape(shape), tensors, max_batch=max_batch)
+    orc = ref.LlamaModelRef(oracle_cfg(shape), tensors)
+    toks = list(prompt)
+    worst = 0.0
+    agree = 0
+    pos = 0
+    for step in range(len(prompt) + n_decode):
+        tok = toks[step]
+        lr = orc.forward_step(tok, pos)
+        lg = gpu.forwardStep(tok, pos).copy()
+        rng_ = float(lr.max() - lr.min())
+        err = float(np.max(np.abs(lg - lr)))
+        worst = max(worst, err / rng_)
+        assert err <= REL_TOL * rng_, (step, err, rng_)
+        if step >= len(prompt) - 1:
+            ref_tok = int(np.argmax(lr))
+            srt = np.sort(lr)
+            gap = float(srt[-1] - srt[-2])
+            if int(np.argmax(lg)) == ref_tok:
+                agree += 1
+            else:
+                assert gap < REL_TOL * rng_, (step, gap)
+            if len(toks) < len(prompt) + n_decode:
+                toks.append(ref_tok)
+        pos += 1
+    return gpu, orc, worst
+
+
+@pytest.mark.parametrize("shape", [synth.TINY, synth.TINY_Q8], ids=["q4_0", "q8_0"])
+def test_tiny_teacher_forced(shape, cuda):
+    t = synth.generate_numpy(shape, seed=21)
+    prompt = synth.prompt_ids(shape, 21, 8).tolist()
+    gpu, orc, worst = teacher_forced(shape, t, prompt, 24)
+    # the device KV cache equals the oracle's
+    kv = gpu.kvCache()
+    assert kv.size() == orc.kv.size == 32
+    for layer in range(shape.n_layers):
+        for h in range(shape.n_kv_heads):
+            for p in (0, 5, 31):
+                k, v = kv.read(layer, h, p)
+                np.testing.assert_allclose(k, orc.kv.k[layer, h, p], rtol=1e-4, atol=1e-5)
+                np.testing.assert_allclose(v, orc.kv.v[layer, h, p], rtol=1e-4, atol=1e-5)
+    assert gpu.argmax(1)[0] == int(np.argmax(gpu._logits[0]))
+
+
+def test_batched_decode_matches_independent_sequences(cuda):
+    """Batch of 4 independent sequences (KV slots), one restarted mid-way so
+    the slots sit at different positions; each equals its own oracle run."""
+    shape = synth.TINY
+    t = synth.generate_numpy(shape, seed=5)
+    B = 4
+    gpu = LlamaModel(LlamaConfig.fromShape(shape), t, max_batch=B)
+    orcs = [ref.LlamaModelRef(oracle_cfg(shape), t) for _ in range(B)]
+    rng = np.random.default_rng(9)
+    pos = [0] * B
+    for step in range(14):
+        if step == 6:  # restart slot 2 from position 0
+            gpu.kvCache(2).reset()
+            orcs[2] = ref.LlamaModelRef(oracle_cfg(shape), t)
+            pos[2] = 0
+        toks = [int(v) for v in rng.integers(0, shape.vocab, size=B)]
+        lg = gpu.forwardBatch(toks, pos).copy()
+        for b in range(B):
+            lr = orcs[b].forward_step(toks[b], pos[b])
+            assert np.max(np.abs(lg[b] - lr)) <= REL_TOL * float(lr.max() - lr.min()), (step, b)
+        pos = [p + 1 for p in pos]
+    assert gpu.kvCache(2).size() == 8 and gpu.kvCache(0).size() == 14
+
+
+def test_gguf_load_matches_tensor_upload(tmp_path, cuda):
+    shape = synth.TINY
+    t = synth.generate_numpy(shape, seed=8)
+    p = str(tmp_path / "tiny.gguf")
+    synth.write_gguf(shape, t, p)
+    a = LlamaModel(LlamaConfig.fromShape(shape), t)
+    b = LlamaModel.fromGguf(p)
+    assert b.config.vocabSize == shape.vocab
+    for pos, tok in enumerate([3, 17, 999, 0]):
+        la = a.forwardStep(tok, pos).copy()
+        lb = b.forwardStep(tok, pos).copy()
+        assert np.array_equal(la, lb)
+
+
+def test_missing_output_weight_gives_zero_logits(cuda):
+    shape = synth.TINY
+    t = synth.generate_numpy(shape, seed=4)
+    del t["output.weight"]
+    gpu = LlamaModel(LlamaConfig.fromShape(shape), t)
+    assert np.all(gpu.forwardStep(1, 0) == 0)
+
+
+def test_errors_match_reference(cuda):
+    shape = synth.TINY
+    gpu = LlamaModel(LlamaConfig.fromShape(shape), synth.generate_numpy(shape, seed=4))
+    with pytest.raises(_lib.IllegalStateException, match="maxContext"):
+        gpu.forwardStep(1, shape.ctx)
+    with pytest.raises(_lib.IllegalArgumentException):
+        gpu.forwardStep(shape.vocab, 0)
+    with pytest.raises(_lib.IllegalArgumentException, match="contextLength"):
+        gpu.forwardPrompt([1] * shape.ctx)
+    assert gpu.forwardPrompt([1, 2, 3]) is None
+    assert gpu.kvCache().size() == 3
+    with pytest.raises(_lib.IllegalStateException, match="finalized"):
+        gpu.setTensor("blk.0.attn_q.weight", 2, b"\0" * 10)
+    fresh = LlamaModel(LlamaConfig.fromShape(shape), None)
+    with pytest.raises(_lib.IllegalArgumentException, match="bytes"):
+        fresh.setTensor("blk.0.attn_q.weight", 2, b"\0" * 10)
+
+
+def test_llama32_1b_shape_parity(cuda):
+    """Llama-3.2-1B-shaped Q4_0 model, 8 seeded prompt tokens + greedy decode, ctx 128."""
+    shape = synth.LLAMA32_1B
+    t = synth.generate_numpy(shape, seed=1)
+    prompt = synth.prompt_ids(shape, 1, 8).tolist()
+    _, _, worst = teacher_forced(shape, t, prompt, 8)
+    assert worst <= REL_TOL
