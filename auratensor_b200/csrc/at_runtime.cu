@@ -296,7 +296,9 @@ int at_ctx_create(int device, at_ctx** out) {
         AT_CUDA(cudaSetDevice(device));
         auto* c = new at_ctx();
         c->device = device;
-        AT_CUDA(cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking));
+        // A blocking stream: it orders itself after work on the legacy default
+        // stream (where host frameworks enqueue by default) and vice versa.
+        AT_CUDA(cudaStreamCreateWithFlags(&c->own_stream, cudaStreamDefault));
         c->stream = c->own_stream;
         AT_CUDA(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device));
         *out = c;

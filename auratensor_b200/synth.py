@@ -93,8 +93,8 @@ LLAMA3_8B = ModelShape("llama-3-8b", 32, 4096, 14336, 32, 8, 128256, 500000.0, 2
 MISTRAL_7B = ModelShape("mistral-7b", 32, 4096, 14336, 32, 8, 32000, 1e6, 4096, Q8_0)
 LLAMA3_70B = ModelShape("llama-3-70b", 80, 8192, 28672, 64, 8, 128256, 500000.0, 8192, Q4_0)
 # Small shapes for parity tests.
-TINY = ModelShape("tiny", 2, 256, 512, 8, 2, 1000, 10000.0, 64, Q4_0)
-TINY_Q8 = ModelShape("tiny-q8", 2, 256, 512, 8, 2, 1000, 1e6, 64, Q8_0)
+TINY = ModelShape("tiny", 2, 256, 512, 4, 2, 1000, 10000.0, 64, Q4_0)
+TINY_Q8 = ModelShape("tiny-q8", 2, 256, 512, 4, 2, 1000, 1e6, 64, Q8_0)
 
 
 # --------------------------------------------------------------------------

@@ -37,7 +37,7 @@ def test_roundtrip_tiny_model(tmp_path):
     with gguf.GgufFile.open(p) as g:
         assert g.data_offset % 32 == 0
         cfg = LlamaConfig.fromGguf(g.metadata)
-        assert (cfg.embeddingLength, cfg.blockCount, cfg.headCount, cfg.headCountKv) == (256, 2, 8, 2)
+        assert (cfg.embeddingLength, cfg.blockCount, cfg.headCount, cfg.headCountKv) == (256, 2, 4, 2)
         assert cfg.vocabSize == shape.vocab and cfg.contextLength == shape.ctx
         assert cfg.ropeFrequencyBase == shape.rope_theta
         for name, tt in t.items():

@@ -137,3 +137,21 @@ def test_missing_output_weight_gives_zero_logits():
     cfg = ref.LlamaConfig(shape.ctx, shape.dim, shape.n_layers, shape.n_heads, shape.n_kv_heads, shape.ffn,
                           shape.rope_theta, shape.eps, shape.vocab)
     assert np.all(ref.LlamaModelRef(cfg, t).forward_step(1, 0) == 0)
+
+
+def test_c_restatement_matches_numpy_oracle():
+    """The C restatement (CPU baseline) and the numpy oracle agree on a tiny model."""
+    from auratensor_b200 import synth
+    from oracle.cref import RefDecoder
+    shape = synth.TINY
+    t = synth.generate_numpy(shape, seed=31)
+    cfg = ref.LlamaConfig(shape.ctx, shape.dim, shape.n_layers, shape.n_heads, shape.n_kv_heads, shape.ffn,
+                          shape.rope_theta, shape.eps, shape.vocab)
+    a = ref.LlamaModelRef(cfg, t)
+    b = RefDecoder(shape, threads=2)
+    for name, tt in t.items():
+        b.set_tensor(name, tt["type"], tt["data"], int(np.prod(tt["dims"])))
+    for pos, tok in enumerate([3, 99, 500, 7, 7]):
+        la = a.forward_step(tok, pos)
+        lb = b.forward_step(tok, pos)
+        assert np.max(np.abs(la - lb)) <= 1e-5 * float(la.max() - la.min())
