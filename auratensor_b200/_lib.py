@@ -25,6 +25,7 @@ AT_ERR_TIMEOUT = -8
 
 GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0 = 0, 1, 2, 8
 ORIENT_N, ORIENT_T = 0, 1
+PROF_CLASSES = ["embed", "qkv", "attn", "wo", "ffn_up", "ffn_down", "lm_head", "argmax", "comm"]
 
 
 class AtError(RuntimeError):
@@ -105,6 +106,8 @@ SIGNATURES = {
     "at_model_forward_batch": [_vp, _vp, _vp, _i, _vp],
     "at_model_logits_device": [_vp, _PP],
     "at_model_argmax": [_vp, _i, _vp],
+    "at_model_generate": [_vp, _i, _i64, _i, _vp],
+    "at_model_profile_step": [_vp, _i, _i64, _vp, _vp],
     "at_model_kv_size": [_vp, _i, C.POINTER(C.c_int64)],
     "at_model_kv_read": [_vp, _i, _i, _i, _i64, _vp, _vp],
     "at_model_kv_reset": [_vp, _i],

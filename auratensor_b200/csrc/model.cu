@@ -239,6 +239,16 @@ inline int grid_for(int64_t n, int tpb = 256) {
     return (int)(g < 1 ? 1 : g);
 }
 
+// Greedy loop step: the argmax becomes the next token, the position advances.
+__global__ void advance_kernel(const int* __restrict__ argmax, int* __restrict__ tokens, int64_t* __restrict__ pos,
+                               int* __restrict__ out, int* __restrict__ counter) {
+    const int t = argmax[0];
+    out[*counter] = t;
+    *counter += 1;
+    tokens[0] = t;
+    pos[0] += 1;
+}
+
 struct Layer {
     at_qmat qkv, wo, w1, w3, w2;
     float* attn_norm = nullptr;
@@ -275,6 +285,14 @@ struct at_model {
     std::vector<int64_t> kv_size;
     std::map<std::string, bool> seen;
     cudaGraphExec_t graph[9] = {};
+    cudaGraphExec_t graph_gen = nullptr;  // step + greedy advance (slot 0)
+    int* d_gen_out = nullptr;             // [ctx] generated tokens
+    int* d_gen_count = nullptr;
+    // eager profiling: event pairs around each launch
+    bool profiling = false;
+    std::vector<cudaEvent_t> prof_ev;
+    std::vector<int> prof_cls;
+    size_t prof_used = 0;
     bool finalized = false;
 };
 
@@ -306,78 +324,152 @@ bool parse_layer(const std::string& name, int* layer, std::string* leaf) {
     return true;
 }
 
+// Brackets the launches of one kernel class with events when profiling.
+struct ProfScope {
+    at_model* m;
+    int cls;
+    size_t idx = 0;
+    ProfScope(at_model* mm, int c) : m(mm), cls(c) {
+        if (!m->profiling) return;
+        if (m->prof_used + 2 > m->prof_ev.size()) {
+            for (int k = 0; k < 64; ++k) {
+                cudaEvent_t e;
+                AT_CUDA(cudaEventCreate(&e));
+                m->prof_ev.push_back(e);
+            }
+        }
+        idx = m->prof_used;
+        m->prof_used += 2;
+        m->prof_cls.push_back(cls);
+        AT_CUDA(cudaEventRecord(m->prof_ev[idx], m->ctx->stream));
+    }
+    ~ProfScope() {
+        if (m->profiling) cudaEventRecord(m->prof_ev[idx + 1], m->ctx->stream);
+    }
+};
+
 void enqueue_step(at_model* m, int B) {
     at_ctx* c = m->ctx;
     cudaStream_t s = c->stream;
     const int d = m->d, hd = m->hd;
-    if (m->tok.type == AT_GGML_Q4_0)
-        embed_kernel<AT_GGML_Q4_0><<<B, 256, 0, s>>>(m->tok.qs, m->tok.d, m->d_tokens, d, m->xa, m->y);
-    else
-        embed_kernel<AT_GGML_Q8_0><<<B, 256, 0, s>>>(m->tok.qs, m->tok.d, m->d_tokens, d, m->xa, m->y);
-    AT_CUDA(cudaGetLastError());
+    auto allreduce_y = [&](const char* what) {
+        if (c->world <= 1) return;
+        ProfScope p(m, AT_PROF_COMM);
+        nccl_check(nccl().AllReduce(m->y, m->y, (size_t)B * d, ncclFloat32, ncclSum, (ncclComm_t)c->nccl_comm, s),
+                   what);
+    };
+    {
+        ProfScope p(m, AT_PROF_EMBED);
+        if (m->tok.type == AT_GGML_Q4_0)
+            embed_kernel<AT_GGML_Q4_0><<<B, 256, 0, s>>>(m->tok.qs, m->tok.d, m->d_tokens, d, m->xa, m->y);
+        else
+            embed_kernel<AT_GGML_Q8_0><<<B, 256, 0, s>>>(m->tok.qs, m->tok.d, m->d_tokens, d, m->xa, m->y);
+        AT_CUDA(cudaGetLastError());
+    }
     const float scale = (float)(1.0 / std::sqrt((double)hd));
     const size_t layer_kv = (size_t)m->Hkvl * m->ctx_len * hd;
     for (int L = 0; L < m->L; ++L) {
         Layer& ly = m->layers[L];
-        GemvArgs a;
-        a.xin = m->xa; a.yin = m->y; a.gamma = ly.attn_norm; a.xout = m->xb; a.eps = m->cfg.rms_norm_eps;
-        a.x_stride = d;
-        a.y = m->q; a.y_stride = m->Hl * hd;
-        a.rope_cos = m->rope_cos; a.rope_sin = m->rope_sin; a.pos = m->d_pos;
-        a.kcache = m->kcache + L * layer_kv; a.vcache = m->vcache + L * layer_kv;
-        a.kv_slot_stride = m->slot_stride;
-        a.head_dim = hd; a.n_q_cols = m->Hl * hd; a.n_kv_cols = m->Hkvl * hd; a.ctx_len = m->ctx_len;
-        a.scratch = m->scratch; a.counters = m->counters;
-        launch_gemv_t(&ly.qkv, B, Pro::AddNorm, Epi::QkvRope, a, c->num_sms, s);
-
-        dim3 g1(m->Hkvl, m->nchunk_max, B);
-        if (hd == 128)
-            attn_split_kernel<128><<<g1, 256, 0, s>>>(m->q, a.kcache, a.vcache, m->d_pos, m->att_part, m->Hl, m->Hkvl,
-                                                      m->ctx_len, m->slot_stride, m->nchunk_max, scale);
-        else
-            attn_split_kernel<64><<<g1, 256, 0, s>>>(m->q, a.kcache, a.vcache, m->d_pos, m->att_part, m->Hl, m->Hkvl,
-                                                     m->ctx_len, m->slot_stride, m->nchunk_max, scale);
-        AT_CUDA(cudaGetLastError());
-        dim3 g2(m->Hl, B);
-        if (hd == 128)
-            attn_combine_kernel<128><<<g2, 128, 0, s>>>(m->att_part, m->d_pos, m->att, m->Hl, m->nchunk_max);
-        else
-            attn_combine_kernel<64><<<g2, 64, 0, s>>>(m->att_part, m->d_pos, m->att, m->Hl, m->nchunk_max);
-        AT_CUDA(cudaGetLastError());
-
-        GemvArgs o;
-        o.x = m->att; o.x_stride = m->Hl * hd; o.y = m->y; o.y_stride = d;
-        o.scratch = m->scratch; o.counters = m->counters;
-        launch_gemv_t(&ly.wo, B, Pro::Plain, Epi::Plain, o, c->num_sms, s);
-        if (c->world > 1)
-            nccl_check(nccl().AllReduce(m->y, m->y, (size_t)B * d, ncclFloat32, ncclSum, (ncclComm_t)c->nccl_comm, s),
-                       "ncclAllReduce(attention)");
-
-        GemvArgs f;
-        f.xin = m->xb; f.yin = m->y; f.gamma = ly.ffn_norm; f.xout = m->xa; f.eps = m->cfg.rms_norm_eps;
-        f.x_stride = d; f.y = m->h; f.y_stride = m->Fl; f.m2 = &ly.w3;
-        launch_gemv_n(&ly.w1, B, Pro::AddNorm, Epi::SiluMul, f, c->num_sms, s);
-
-        GemvArgs dn;
-        dn.x = m->h; dn.x_stride = m->Fl; dn.y = m->y; dn.y_stride = d;
-        launch_gemv_n(&ly.w2, B, Pro::Plain, Epi::Plain, dn, c->num_sms, s);
-        if (c->world > 1)
-            nccl_check(nccl().AllReduce(m->y, m->y, (size_t)B * d, ncclFloat32, ncclSum, (ncclComm_t)c->nccl_comm, s),
-                       "ncclAllReduce(mlp)");
+        float* kc = m->kcache + L * layer_kv;
+        float* vc = m->vcache + L * layer_kv;
+        {
+            ProfScope p(m, AT_PROF_QKV);
+            GemvArgs a;
+            a.xin = m->xa; a.yin = m->y; a.gamma = ly.attn_norm; a.xout = m->xb; a.eps = m->cfg.rms_norm_eps;
+            a.x_stride = d;
+            a.y = m->q; a.y_stride = m->Hl * hd;
+            a.rope_cos = m->rope_cos; a.rope_sin = m->rope_sin; a.pos = m->d_pos;
+            a.kcache = kc; a.vcache = vc;
+            a.kv_slot_stride = m->slot_stride;
+            a.head_dim = hd; a.n_q_cols = m->Hl * hd; a.n_kv_cols = m->Hkvl * hd; a.ctx_len = m->ctx_len;
+            a.scratch = m->scratch; a.counters = m->counters;
+            launch_gemv_t(&ly.qkv, B, Pro::AddNorm, Epi::QkvRope, a, c->num_sms, s);
+        }
+        {
+            ProfScope p(m, AT_PROF_ATTN);
+            dim3 g1(m->Hkvl, m->nchunk_max, B);
+            if (hd == 128)
+                attn_split_kernel<128><<<g1, 256, 0, s>>>(m->q, kc, vc, m->d_pos, m->att_part, m->Hl, m->Hkvl,
+                                                          m->ctx_len, m->slot_stride, m->nchunk_max, scale);
+            else
+                attn_split_kernel<64><<<g1, 256, 0, s>>>(m->q, kc, vc, m->d_pos, m->att_part, m->Hl, m->Hkvl,
+                                                         m->ctx_len, m->slot_stride, m->nchunk_max, scale);
+            AT_CUDA(cudaGetLastError());
+            dim3 g2(m->Hl, B);
+            if (hd == 128)
+                attn_combine_kernel<128><<<g2, 128, 0, s>>>(m->att_part, m->d_pos, m->att, m->Hl, m->nchunk_max);
+            else
+                attn_combine_kernel<64><<<g2, 64, 0, s>>>(m->att_part, m->d_pos, m->att, m->Hl, m->nchunk_max);
+            AT_CUDA(cudaGetLastError());
+        }
+        {
+            ProfScope p(m, AT_PROF_WO);
+            GemvArgs o;
+            o.x = m->att; o.x_stride = m->Hl * hd; o.y = m->y; o.y_stride = d;
+            o.scratch = m->scratch; o.counters = m->counters;
+            launch_gemv_t(&ly.wo, B, Pro::Plain, Epi::Plain, o, c->num_sms, s);
+        }
+        allreduce_y("ncclAllReduce(attention)");
+        {
+            ProfScope p(m, AT_PROF_FFN_UP);
+            GemvArgs f;
+            f.xin = m->xb; f.yin = m->y; f.gamma = ly.ffn_norm; f.xout = m->xa; f.eps = m->cfg.rms_norm_eps;
+            f.x_stride = d; f.y = m->h; f.y_stride = m->Fl; f.m2 = &ly.w3;
+            launch_gemv_n(&ly.w1, B, Pro::AddNorm, Epi::SiluMul, f, c->num_sms, s);
+        }
+        {
+            ProfScope p(m, AT_PROF_FFN_DOWN);
+            GemvArgs dn;
+            dn.x = m->h; dn.x_stride = m->Fl; dn.y = m->y; dn.y_stride = d;
+            launch_gemv_n(&ly.w2, B, Pro::Plain, Epi::Plain, dn, c->num_sms, s);
+        }
+        allreduce_y("ncclAllReduce(mlp)");
     }
-    GemvArgs hd_args;
-    hd_args.xin = m->xa; hd_args.yin = m->y; hd_args.gamma = m->out_norm; hd_args.xout = m->xb;
-    hd_args.eps = m->cfg.rms_norm_eps; hd_args.x_stride = d;
-    hd_args.y = (c->world > 1) ? m->logits_local : m->logits; hd_args.y_stride = m->Vl;
-    launch_gemv_n(&m->out, B, Pro::AddNorm, Epi::Plain, hd_args, c->num_sms, s);
+    {
+        ProfScope p(m, AT_PROF_LM_HEAD);
+        GemvArgs ha;
+        ha.xin = m->xa; ha.yin = m->y; ha.gamma = m->out_norm; ha.xout = m->xb;
+        ha.eps = m->cfg.rms_norm_eps; ha.x_stride = d;
+        ha.y = (c->world > 1) ? m->logits_local : m->logits; ha.y_stride = m->Vl;
+        launch_gemv_n(&m->out, B, Pro::AddNorm, Epi::Plain, ha, c->num_sms, s);
+    }
     if (c->world > 1) {
+        ProfScope p(m, AT_PROF_COMM);
         nccl_check(nccl().AllGather(m->logits_local, m->gather, (size_t)B * m->Vl, ncclFloat32,
                                     (ncclComm_t)c->nccl_comm, s),
                    "ncclAllGather(logits)");
         gather_logits_kernel<<<grid_for((int64_t)B * m->V), 256, 0, s>>>(m->gather, m->logits, c->world, B, m->Vl, m->V);
         AT_CUDA(cudaGetLastError());
     }
-    argmax_kernel<<<B, 1024, 0, s>>>(m->logits, m->V, m->V, m->d_argmax);
+    {
+        ProfScope p(m, AT_PROF_ARGMAX);
+        argmax_kernel<<<B, 1024, 0, s>>>(m->logits, m->V, m->V, m->d_argmax);
+        AT_CUDA(cudaGetLastError());
+    }
+}
+
+cudaGraphExec_t capture(at_model* m, void (*body)(at_model*, int), int B) {
+    at_ctx* c = m->ctx;
+    cudaGraph_t g = nullptr;
+    AT_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    try {
+        body(m, B);
+    } catch (...) {
+        cudaStreamEndCapture(c->stream, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+    }
+    AT_CUDA(cudaStreamEndCapture(c->stream, &g));
+    cudaGraphExec_t e = nullptr;
+    const cudaError_t err = cudaGraphInstantiate(&e, g, 0);
+    cudaGraphDestroy(g);
+    AT_CUDA(err);
+    return e;
+}
+
+void enqueue_generate_step(at_model* m, int) {
+    enqueue_step(m, 1);
+    advance_kernel<<<1, 1, 0, m->ctx->stream>>>(m->d_argmax, m->d_tokens, m->d_pos, m->d_gen_out, m->d_gen_count);
     AT_CUDA(cudaGetLastError());
 }
 
@@ -399,20 +491,7 @@ void run_step(at_model* m, const int* tokens, const int64_t* positions, int B, f
     for (int b = 0; b < B; ++b) { m->h_tokens[b] = tokens[b]; m->h_pos[b] = positions[b]; }
     AT_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tokens, sizeof(int) * B, cudaMemcpyHostToDevice, c->stream));
     AT_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pos, sizeof(int64_t) * B, cudaMemcpyHostToDevice, c->stream));
-    if (!m->graph[B]) {
-        cudaGraph_t g;
-        AT_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-        try {
-            enqueue_step(m, B);
-        } catch (...) {
-            cudaStreamEndCapture(c->stream, &g);
-            if (g) cudaGraphDestroy(g);
-            throw;
-        }
-        AT_CUDA(cudaStreamEndCapture(c->stream, &g));
-        AT_CUDA(cudaGraphInstantiate(&m->graph[B], g, 0));
-        AT_CUDA(cudaGraphDestroy(g));
-    }
+    if (!m->graph[B]) m->graph[B] = capture(m, enqueue_step, B);
     AT_CUDA(cudaGraphLaunch(m->graph[B], c->stream));
     if (logits_host)
         AT_CUDA(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * (size_t)B * m->V, cudaMemcpyDeviceToHost,
@@ -427,6 +506,8 @@ void destroy_model(at_model* m) {
     cudaStreamSynchronize(m->ctx->stream);
     for (auto& g : m->graph)
         if (g) cudaGraphExecDestroy(g);
+    if (m->graph_gen) cudaGraphExecDestroy(m->graph_gen);
+    for (cudaEvent_t e : m->prof_ev) cudaEventDestroy(e);
     for (auto& ly : m->layers) {
         qmat_free(&ly.qkv); qmat_free(&ly.wo); qmat_free(&ly.w1); qmat_free(&ly.w3); qmat_free(&ly.w2);
         cudaFree(ly.attn_norm); cudaFree(ly.ffn_norm);
@@ -435,7 +516,7 @@ void destroy_model(at_model* m) {
     qmat_free(&m->out);
     void* bufs[] = {m->out_norm, m->xa, m->xb, m->y, m->q, m->att, m->h, m->logits, m->logits_local, m->gather,
                     m->att_part, m->kcache, m->vcache, m->rope_cos, m->rope_sin, m->scratch, m->counters,
-                    m->d_tokens, m->d_pos, m->d_argmax};
+                    m->d_tokens, m->d_pos, m->d_argmax, m->d_gen_out, m->d_gen_count};
     for (void* p : bufs)
         if (p) cudaFree(p);
     if (m->h_tokens) cudaFreeHost(m->h_tokens);
@@ -575,7 +656,7 @@ int at_model_create(at_ctx* ctx, const at_model_config* cfg, at_model** out) {
         m->V = (int)cfg->vocab_size;
         m->L = (int)cfg->block_count;
         m->ctx_len = (int)cfg->context_length;
-        const int W = ctx->world, r = ctx->rank;
+        const int W = ctx->world;
         AT_REQUIRE(m->hd == 64 || m->hd == 128, AT_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
         AT_REQUIRE(m->d % 32 == 0, AT_ERR_INVALID_ARG, "embedding_length must be a multiple of 32");
         AT_REQUIRE(m->H % m->Hkv == 0 && m->H / m->Hkv <= 8, AT_ERR_UNSUPPORTED, "query heads per KV head must be 1..8");
@@ -585,7 +666,6 @@ int at_model_create(at_ctx* ctx, const at_model_config* cfg, at_model** out) {
         m->Hkvl = m->Hkv / W;
         m->Fl = m->F / W;
         m->Vl = (m->V + W - 1) / W;
-        (void)r;
         m->layers.resize(m->L);
         m->kv_size.assign(m->B, 0);
         *out = m;
@@ -761,6 +841,8 @@ int at_model_finalize(at_model* m) {
         alloc_zero((void**)&m->d_tokens, 8 * sizeof(int));
         alloc_zero((void**)&m->d_pos, 8 * sizeof(int64_t));
         alloc_zero((void**)&m->d_argmax, 8 * sizeof(int));
+        alloc_zero((void**)&m->d_gen_out, (size_t)m->ctx_len * sizeof(int));
+        alloc_zero((void**)&m->d_gen_count, sizeof(int));
         AT_CUDA(cudaMallocHost(&m->h_tokens, 8 * sizeof(int)));
         AT_CUDA(cudaMallocHost(&m->h_pos, 8 * sizeof(int64_t)));
         AT_CUDA(cudaDeviceSynchronize());
@@ -904,6 +986,67 @@ int at_model_forward_prompt(at_model* m, const int* tokens, int n) {
 
 int at_model_forward_batch(at_model* m, const int* tokens, const int64_t* positions, int batch, float* logits_host) {
     return guard([&] { run_step(m, tokens, positions, batch, logits_host); });
+}
+
+int at_model_generate(at_model* m, int first_token, int64_t start_pos, int n_steps, int* tokens_out_host) {
+    return guard([&] {
+        AT_REQUIRE(m && m->finalized, AT_ERR_STATE, "model is not finalized");
+        AT_REQUIRE(n_steps >= 0, AT_ERR_INVALID_ARG, "negative step count");
+        AT_REQUIRE(first_token >= 0 && first_token < m->V, AT_ERR_INVALID_ARG, "token id out of range");
+        AT_REQUIRE(start_pos >= 0, AT_ERR_INVALID_ARG, "negative position");
+        AT_REQUIRE(start_pos + n_steps <= m->ctx_len, AT_ERR_STATE,
+                   "position " + std::to_string(start_pos + n_steps - 1) + " exceeds maxContext " +
+                       std::to_string(m->ctx_len));
+        if (n_steps == 0) return;
+        at_ctx* c = m->ctx;
+        AT_CUDA(cudaSetDevice(c->device));
+        m->h_tokens[0] = first_token;
+        m->h_pos[0] = start_pos;
+        AT_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tokens, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+        AT_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pos, sizeof(int64_t), cudaMemcpyHostToDevice, c->stream));
+        AT_CUDA(cudaMemsetAsync(m->d_gen_count, 0, sizeof(int), c->stream));
+        if (!m->graph_gen) m->graph_gen = capture(m, enqueue_generate_step, 1);
+        for (int i = 0; i < n_steps; ++i) AT_CUDA(cudaGraphLaunch(m->graph_gen, c->stream));
+        m->kv_size[0] = std::max<int64_t>(m->kv_size[0], start_pos + n_steps);
+        if (tokens_out_host) {
+            AT_CUDA(cudaMemcpyAsync(tokens_out_host, m->d_gen_out, sizeof(int) * n_steps, cudaMemcpyDeviceToHost,
+                                    c->stream));
+            AT_CUDA(cudaStreamSynchronize(c->stream));
+        }
+    });
+}
+
+int at_model_profile_step(at_model* m, int token, int64_t position, float* class_ms, int* class_launches) {
+    return guard([&] {
+        AT_REQUIRE(m && m->finalized && class_ms && class_launches, AT_ERR_INVALID_ARG, "bad argument");
+        AT_REQUIRE(token >= 0 && token < m->V, AT_ERR_INVALID_ARG, "token id out of range");
+        AT_REQUIRE(position >= 0 && position < m->ctx_len, AT_ERR_STATE, "position exceeds maxContext");
+        at_ctx* c = m->ctx;
+        AT_CUDA(cudaSetDevice(c->device));
+        m->h_tokens[0] = token;
+        m->h_pos[0] = position;
+        AT_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tokens, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+        AT_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pos, sizeof(int64_t), cudaMemcpyHostToDevice, c->stream));
+        m->profiling = true;
+        m->prof_used = 0;
+        m->prof_cls.clear();
+        try {
+            enqueue_step(m, 1);
+        } catch (...) {
+            m->profiling = false;
+            throw;
+        }
+        m->profiling = false;
+        AT_CUDA(cudaStreamSynchronize(c->stream));
+        for (int k = 0; k < AT_PROF_CLASSES; ++k) { class_ms[k] = 0.f; class_launches[k] = 0; }
+        for (size_t i = 0; i < m->prof_cls.size(); ++i) {
+            float ms = 0.f;
+            AT_CUDA(cudaEventElapsedTime(&ms, m->prof_ev[2 * i], m->prof_ev[2 * i + 1]));
+            class_ms[m->prof_cls[i]] += ms;
+            class_launches[m->prof_cls[i]] += 1;
+        }
+        m->kv_size[0] = std::max<int64_t>(m->kv_size[0], position + 1);
+    });
 }
 
 int at_model_logits_device(at_model* m, float** logits_dev) {

@@ -139,7 +139,7 @@ class LlamaModel:
         self._h = C.c_void_p()
         cfg = config.to_c(max_batch)
         call("at_model_create", self._ctx, C.byref(cfg), C.byref(self._h))
-        self._logits = np.empty((max_batch, config.vocabSize), dtype=np.float32)
+        self._logits = _host_logits(max_batch, config.vocabSize)
         if tensors is not None:
             for name, t in tensors.items():
                 self.setTensor(name, t["type"], t["data"])
@@ -156,7 +156,7 @@ class LlamaModel:
         self._ctx = context()
         self._h = C.c_void_p()
         call("at_model_load_gguf", self._ctx, path.encode(), max_batch, C.byref(self._h))
-        self._logits = np.empty((max_batch, cfg.vocabSize), dtype=np.float32)
+        self._logits = _host_logits(max_batch, cfg.vocabSize)
         return self
 
     def setTensor(self, name: str, ggml_type: int, data) -> None:
@@ -207,6 +207,29 @@ class LlamaModel:
         n = self.max_batch * self.config.vocabSize
         return _device_view(p.value, n, torch.cuda.current_device()).view(self.max_batch, self.config.vocabSize)
 
+    def generate(self, firstToken: int, startPos: int, nSteps: int, wait: bool = True) -> np.ndarray | None:
+        """Greedy decode of slot 0 on the device: nSteps tokens, no host round trip per step."""
+        if not wait:
+            call("at_model_generate", self._h, int(firstToken), int(startPos), int(nSteps), None)
+            return None
+        out = np.empty(max(1, nSteps), dtype=np.int32)
+        call("at_model_generate", self._h, int(firstToken), int(startPos), int(nSteps),
+             out.ctypes.data_as(C.c_void_p))
+        return out[:nSteps]
+
+    def profileStep(self, tokenId: int, position: int) -> dict:
+        """Per-kernel-class device time (ms) and launch counts of one eager step."""
+        ms = np.zeros(len(_lib.PROF_CLASSES), dtype=np.float32)
+        n = np.zeros(len(_lib.PROF_CLASSES), dtype=np.int32)
+        call("at_model_profile_step", self._h, int(tokenId), int(position), ms.ctypes.data_as(C.c_void_p),
+             n.ctypes.data_as(C.c_void_p))
+        return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(_lib.PROF_CLASSES)}
+
+    def stream(self) -> int:
+        p = C.c_void_p()
+        call("at_ctx_stream", self._ctx, C.byref(p))
+        return p.value or 0
+
     def argmax(self, batch: int = 1) -> np.ndarray:
         out = np.empty(batch, dtype=np.int32)
         call("at_model_argmax", self._h, batch, out.ctypes.data_as(C.c_void_p))
@@ -222,6 +245,13 @@ class LlamaModel:
             self.close()
         except Exception:
             pass
+
+
+def _host_logits(rows: int, vocab: int) -> np.ndarray:
+    """Page-locked host buffer for the logits copies (plain memory without a GPU)."""
+    if torch.cuda.is_available():
+        return torch.empty((rows, vocab), dtype=torch.float32, pin_memory=True).numpy()
+    return np.empty((rows, vocab), dtype=np.float32)
 
 
 def _device_view(addr: int, n: int, device: int) -> torch.Tensor:

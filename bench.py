@@ -1,0 +1,420 @@
+"""Benchmark: Llama-3-8B-shaped Q4_0 batch-1 greedy decode (tokens/s) on B200.
+
+Workload: random-init Llama-3-8B shape (32 layers, dim 4096, FFN 14336, 32/8
+heads, head_dim 128, vocab 128256, RoPE theta 500000, context 2048), weights
+N(0, 0.02) quantized to Q4_0 on the device, a seeded 512-token prompt run
+through forwardPrompt (untimed), then timed decode steps from position 512.
+One step = one decode token. Weights (4.6 GB) exceed the 126 MB L2, so no
+flush is needed between steps.
+
+  value  device-resident greedy loop (at_model_generate), CUDA events on the
+         engine's stream, max over ranks.
+  e2e    the reference-facing call: at_model_forward_step with the token in
+         and the full logits out in host memory each step, then the greedy
+         Sampler on the host (the reference's decode loop).
+
+N > 1: one process per GPU (torchrun), Megatron tensor parallelism with NCCL
+all-reduces inside the captured step graph; scaling "strong".
+
+--impl reference: the reference's CPU algorithm (load-time dequant to FP32,
+FP32 sgemv; the C restatement under oracle/) on all host cores, each step a
+sampled decode token (2 of 32 layers plus the lm_head, extrapolated).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Llama-3-8B Q4_0 decode tok/s"
+UNIT = "tok/s"
+PROMPT = 512
+SAMPLE_LAYERS = 2
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=256)
+    p.add_argument("--warmup", type=int, default=16)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--profile-steps", type=int, default=8)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    # smaller cases for profiler captures only (the bench line uses the defaults)
+    p.add_argument("--prompt", type=int, default=PROMPT)
+    p.add_argument("--layers", type=int, default=None)
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+CLOCK_Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+           "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+           "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+class ClockSampler:
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={CLOCK_Q}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", ",".join(str(g) for g in self.gpus)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# algorithmic bytes per launch (weights + input vector + output vector)
+# ---------------------------------------------------------------------------
+def q_bytes(rows, cols, bpb=18):
+    return rows * (cols // 32) * bpb
+
+
+def class_bytes(shape, world, pos):
+    d, hd = shape.dim, shape.head_dim
+    hl, hkvl, fl = shape.n_heads // world, shape.n_kv_heads // world, shape.ffn // world
+    vl = -(-shape.vocab // world)
+    qkv_cols = (hl + 2 * hkvl) * hd
+    return {
+        "qkv": q_bytes(d, qkv_cols) + d * 4 + qkv_cols * 4,
+        "wo": q_bytes(hl * hd, d) + hl * hd * 4 + d * 4,
+        "ffn_up": 2 * q_bytes(fl, d) + d * 4 + fl * 4,
+        "ffn_down": q_bytes(d, fl) + fl * 4 + d * 4,
+        "lm_head": q_bytes(vl, d) + d * 4 + vl * 4,
+        "attn": 2 * hkvl * (pos + 1) * hd * 4 + 2 * hl * hd * 4,
+    }
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def committed_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if any."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference algorithm (C restatement) on a sampled token
+# ---------------------------------------------------------------------------
+def cpu_decode_sample(shape, host_tensors, threads, steps, start_pos):
+    """Time `steps` decode tokens of the reference algorithm with SAMPLE_LAYERS
+    layers, extrapolated to all layers. Returns (tok/s list per step, detail)."""
+    from oracle.cref import RefDecoder
+    dec = RefDecoder(shape, n_layers=SAMPLE_LAYERS, threads=threads)
+    for name, (tt, data, numel) in host_tensors.items():
+        dec.set_tensor(name, tt, data, numel)
+    rates = []
+    tok = 1
+    for i in range(steps):
+        dec.forward_step(tok, start_pos + i)
+        te, tl, th = dec.times()
+        t_tok = te + tl * (shape.n_layers / SAMPLE_LAYERS) + th
+        rates.append(1.0 / t_tok)
+    dec.close()
+    return rates
+
+
+def sample_host_tensors_cpu(shape, seed):
+    """Synthetic Q4_0 tensors of the sampled layers, generated on the CPU."""
+    import torch
+    from auratensor_b200 import synth
+    g = torch.Generator().manual_seed(seed)
+    out = {}
+    for name, dims, t in shape.tensor_dims():
+        if name.startswith("blk.") and int(name.split(".")[1]) >= SAMPLE_LAYERS:
+            continue
+        n = int(np.prod(dims))
+        if t == 0:
+            data = np.ones(n, dtype=np.float32).view(np.uint8)
+        else:
+            parts = []
+            step = 1 << 25
+            for s0 in range(0, n, step):
+                c = min(step, n - s0)
+                x = torch.randn(c, generator=g, dtype=torch.float32) * 0.02
+                parts.append(synth.quantize_torch(x, t).numpy())
+            data = np.concatenate(parts)
+        out[name] = (t, data, n)
+    return out
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from auratensor_b200 import synth
+    shape = synth.LLAMA3_8B
+    threads = os.cpu_count() or 1
+    t0 = time.time()
+    tensors = sample_host_tensors_cpu(shape, args.seed)
+    gen_s = time.time() - t0
+    rates = cpu_decode_sample(shape, tensors, threads, args.warmup + args.steps, PROMPT)
+    timed = rates[args.warmup:]
+    value = len(timed) / sum(1.0 / r for r in timed)
+    sample = (f"{SAMPLE_LAYERS} of {shape.n_layers} layers + lm_head per step, decode positions "
+              f"{PROMPT}..{PROMPT + args.warmup + args.steps - 1}, extrapolated to {shape.n_layers} layers")
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1000.0 / value, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": "llama-3-8b-q4_0-decode", "batch": 1, "prompt_tokens": PROMPT, "context": 2048,
+                   "weights": "Q4_0 dequantized to FP32 at load (reference algorithm)"},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample, "setup_s": round(gen_s, 1)},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our engine
+# ---------------------------------------------------------------------------
+def build_model(shape, seed, ctx, world, keep_host: bool):
+    import torch
+    from auratensor_b200 import synth
+    from auratensor_b200.inference import LlamaConfig, LlamaModel
+    model = LlamaModel(LlamaConfig.fromShape(shape), None, max_batch=1, ctx=ctx, world=world)
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    host = {}
+    for name, dims, t in shape.tensor_dims():
+        data = synth.generate_torch_tensor(dims, t, g, "cuda")
+        model.setTensor(name, t, data)
+        if keep_host and (not name.startswith("blk.") or int(name.split(".")[1]) < SAMPLE_LAYERS):
+            host[name] = (t, data.cpu().numpy(), int(np.prod(dims)))
+        del data
+    model.finalize()
+    torch.cuda.synchronize()
+    return model, host
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from auratensor_b200 import _lib, build as libbuild, synth, tp
+    from auratensor_b200.inference import Sampler, SamplerConfig
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+    libbuild.build()
+    torch.cuda.set_device(local)
+    import ctypes as C
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        ctx, _, _ = tp.init_tp_context(local)
+    else:
+        p = C.c_void_p()
+        _lib.call("at_ctx_create", local, C.byref(p))
+        ctx = p.value
+    shape = synth.LLAMA3_8B
+    if args.layers is not None:
+        import dataclasses
+        shape = dataclasses.replace(shape, n_layers=args.layers)
+    keep_host = (rank == 0 and world == 1 and not args.no_cpu_baseline and args.layers is None)
+    t0 = time.time()
+    model, host = build_model(shape, args.seed, ctx, world, keep_host)
+    load_s = time.time() - t0
+    stream = torch.cuda.ExternalStream(model.stream())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    prompt = synth.prompt_ids(shape, args.seed, args.prompt).tolist()
+    t0 = time.time()
+    model.forwardPrompt(prompt)
+    prefill_s = time.time() - t0
+    ctx_len = shape.ctx
+
+    def positions(start, n):
+        """Segments of consecutive positions in [start, ctx); wraps back to PROMPT."""
+        segs, p, left = [], start, n
+        while left:
+            if p >= ctx_len:
+                p = PROMPT
+            k = min(left, ctx_len - p)
+            segs.append((p, k))
+            p += k
+            left -= k
+        return segs, p
+
+    tok = int(prompt[-1])
+    segs, pos = positions(args.prompt, args.warmup)
+    for p0, k in segs:
+        model.generate(tok, p0, k)
+    gpus = list(range(torch.cuda.device_count()))[: max(1, world)] if world > 1 else [local]
+
+    with ClockSampler(gpus) as clk:
+        # value: device-resident greedy loop
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        segs, pos = positions(pos, args.steps)
+        e0.record(stream)
+        for p0, k in segs:
+            model.generate(tok, p0, k, wait=False)
+        e1.record(stream)
+        e1.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1))
+        # e2e: forwardStep with host logits + host greedy sampler, every step
+        barrier()
+        greedy = SamplerConfig.greedy()
+        segs2, pos2 = positions(pos, args.steps)
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        t = tok
+        for p0, k in segs2:
+            for i in range(k):
+                logits = model.forwardStep(t, p0 + i)
+                t = Sampler.sample(logits, None, greedy)
+        f1.record(stream)
+        f1.synchronize()
+        ms_e2e = max_over_ranks(f0.elapsed_time(f1))
+    clocks = clk.summary()
+    pos = pos2
+
+    # roofline: eager per-class kernel times over a few steps
+    tot = {}
+    for i in range(args.profile_steps):
+        p = pos if pos < ctx_len else PROMPT
+        r = model.profileStep(tok, p)
+        pos = p + 1
+        for k, (msk, n) in r.items():
+            a = tot.setdefault(k, [0.0, 0])
+            a[0] += msk
+            a[1] += n
+    value = args.steps / (ms / 1000.0)
+    e2e = args.steps / (ms_e2e / 1000.0)
+    if rank != 0:
+        finish(model, ctx, world)
+        return
+    bytes_per = class_bytes(shape, world, pos)
+    gemv = {k: v for k, v in tot.items() if k in bytes_per}
+    dom = max(gemv, key=lambda k: gemv[k][0])
+    avg_ms = gemv[dom][0] / max(1, gemv[dom][1])
+    peak, peak_kind = load_peaks()
+    achieved = bytes_per[dom] / (avg_ms / 1000.0) / 1e9
+    traffic = committed_traffic().get(dom)
+    step_ms_eager = sum(v[0] for v in tot.values()) / args.profile_steps
+    launches_per_step = 1 + 6 * shape.n_layers + 3 + (1 if world > 1 else 0)
+
+    cpu = None
+    if keep_host:
+        threads = os.cpu_count() or 1
+        rates = cpu_decode_sample(shape, host, threads, 4, PROMPT + 64)
+        rates1 = cpu_decode_sample(shape, host, 1, 2, PROMPT + 64)
+        cpu = {"value": round(len(rates) / sum(1 / r for r in rates), 4), "unit": UNIT, "cores": threads,
+               "kind": "port",
+               "sample": f"{SAMPLE_LAYERS} of {shape.n_layers} layers + lm_head, 4 decode tokens at positions "
+                         f"{PROMPT + 64}.., extrapolated to {shape.n_layers} layers; same Q4_0 weights",
+               "single_thread_value": round(len(rates1) / sum(1 / r for r in rates1), 4)}
+
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "llama-3-8b-q4_0-decode", "batch": 1, "prompt_tokens": PROMPT, "context": ctx_len,
+                   "weights": "Q4_0 (4.6 GB, > L2; no flush needed)", "parallelism": f"tp{world}",
+                   "seed": args.seed},
+        "e2e": {"value": round(e2e, 3), "unit": UNIT, "h2d_bytes_per_step": 12,
+                "d2h_bytes_per_step": shape.vocab * 4},
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": traffic, "bytes_per_launch": bytes_per[dom],
+                     "avg_launch_us": round(avg_ms * 1000.0, 2)},
+        "kernel_ms_per_step": {k: round(v[0] / args.profile_steps, 4) for k, v in tot.items() if v[1]},
+        "eager_step_ms": round(step_ms_eager, 4),
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+        "setup": {"load_s": round(load_s, 1), "prefill_s": round(prefill_s, 2)},
+    }
+    print(json.dumps(line), flush=True)
+    finish(model, ctx, world)
+
+
+def finish(model, ctx, world):
+    """Releases the step graphs (which hold NCCL calls) and the communicator
+    before the process group goes away; every rank takes the same steps."""
+    import torch.distributed as dist
+    from auratensor_b200 import _lib
+    model.close()
+    _lib.call("at_ctx_destroy", ctx)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -165,6 +165,29 @@ int at_model_logits_device(at_model* m, float** logits_dev);
 /* Greedy token of each of the last step's `batch` rows (Sampler greedy path,
  * inference/Sampler.java:56-67: first index of the maximum). */
 int at_model_argmax(at_model* m, int batch, int* tokens_host);
+/* Greedy decode loop resident on the device (the decode loop of the
+ * reference's TokenThroughputBenchmark.decodeLoop, benchmarks/TokenThroughputBenchmark.java:147-158:
+ * forwardStep then greedy Sampler.sample, repeated): n_steps steps of slot 0,
+ * step i at position start_pos + i, whose token is first_token for i = 0 and
+ * the previous step's argmax after that. No host round trip between steps.
+ * tokens_out_host receives the n_steps generated tokens; when it is NULL the
+ * steps are only enqueued on the context's stream (the call does not wait). */
+int at_model_generate(at_model* m, int first_token, int64_t start_pos, int n_steps, int* tokens_out_host);
+/* Per-kernel-class device time of one eager (non-graph) forward step of slot 0,
+ * each launch bracketed by CUDA events: class_ms[AT_PROF_CLASSES] milliseconds
+ * and class_launches[AT_PROF_CLASSES] launch counts. New (the reference has
+ * only wall-clock prints). */
+#define AT_PROF_EMBED    0
+#define AT_PROF_QKV      1  /* QKV GEMV + RMSNorm + RoPE + KV append   */
+#define AT_PROF_ATTN     2  /* split-KV attention + combine            */
+#define AT_PROF_WO       3  /* attention output GEMV                   */
+#define AT_PROF_FFN_UP   4  /* gate/up GEMV + RMSNorm + SiLU*up        */
+#define AT_PROF_FFN_DOWN 5  /* down GEMV                               */
+#define AT_PROF_LM_HEAD  6  /* output norm + lm_head GEMV              */
+#define AT_PROF_ARGMAX   7
+#define AT_PROF_COMM     8  /* NCCL all-reduce / all-gather            */
+#define AT_PROF_CLASSES  9
+int at_model_profile_step(at_model* m, int token, int64_t position, float* class_ms, int* class_launches);
 /* KVCache.size / offsetOf / keys() / values() (inference/KVCache.java:70-104):
  * copies head_dim floats of K and V for (slot, layer, kv_head, position). */
 int at_model_kv_size(const at_model* m, int slot, int64_t* size);

@@ -137,3 +137,38 @@ def test_llama32_1b_shape_parity(cuda):
     prompt = synth.prompt_ids(shape, 1, 8).tolist()
     _, _, worst = teacher_forced(shape, t, prompt, 8)
     assert worst <= REL_TOL
+
+
+def test_device_greedy_loop_matches_step_loop(cuda):
+    """at_model_generate (argmax fed back on the device) equals forwardStep + greedy Sampler."""
+    from auratensor_b200.inference import Sampler, SamplerConfig
+    shape = synth.TINY
+    t = synth.generate_numpy(shape, seed=13)
+    a = LlamaModel(LlamaConfig.fromShape(shape), t)
+    b = LlamaModel(LlamaConfig.fromShape(shape), t)
+    prompt = [5, 6, 7, 8]
+    a.forwardPrompt(prompt)
+    b.forwardPrompt(prompt)
+    gen = a.generate(prompt[-1], len(prompt), 20)
+    tok, seq = prompt[-1], []
+    for i in range(20):
+        tok = Sampler.sample(b.forwardStep(tok, len(prompt) + i).copy(), None, SamplerConfig.greedy())
+        seq.append(tok)
+    assert gen.tolist() == seq
+    assert a.kvCache().size() == len(prompt) + 20
+    with pytest.raises(_lib.IllegalStateException):
+        a.generate(1, shape.ctx - 2, 5)
+
+
+def test_profile_step_counts(cuda):
+    shape = synth.TINY
+    m = LlamaModel(LlamaConfig.fromShape(shape), synth.generate_numpy(shape, seed=14))
+    r = m.profileStep(3, 0)
+    L = shape.n_layers
+    assert r["qkv"][1] == L and r["attn"][1] == L and r["wo"][1] == L
+    assert r["ffn_up"][1] == L and r["ffn_down"][1] == L and r["lm_head"][1] == 1
+    assert r["comm"][1] == 0 and all(v[0] >= 0 for v in r.values())
+    # the profiled eager step computes the same logits as the graph step
+    m2 = LlamaModel(LlamaConfig.fromShape(shape), synth.generate_numpy(shape, seed=14))
+    lg = m2.forwardStep(3, 0).copy()
+    assert np.array_equal(m.logitsDevice()[0].cpu().numpy(), lg)
