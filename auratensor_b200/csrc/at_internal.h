@@ -64,18 +64,27 @@ struct at_ctx {
     void* nccl_comm = nullptr;  // ncclComm_t
 };
 
-// Planar device layout of one quantized matrix.
-//  Orientation N: rows-major; block (r, b) at qs[(r*nb + b)*QB], d[r*nb + b].
-//  Orientation T: block-column-major; block (r, c) at qs[(c*rows + r)*QB], d[c*rows + r].
-// QB = 16 (Q4_0) or 32 (Q8_0) quant bytes per block. F32 matrices keep
-// row-major floats in `f32`.
+// Tiled device layout of one quantized matrix: a lossless re-layout of whole
+// GGUF blocks (the fp16 scale and the quant bytes of every block are moved,
+// never re-quantized) so that the bytes one warp step consumes are contiguous.
+//  Orientation N (blocks along the rows): tiles of 4 rows x 32 blocks;
+//    tile (g, s) = rows 4g..4g+3, blocks 32s..32s+31, at (g * nsteps + s) * tile_bytes;
+//    inside: scales [4][32] u16, then quant bytes [4][32][QB].
+//  Orientation T (blocks along the columns): tiles of 32 rows x 1 block column;
+//    tile (c, g) = block column c, rows 32g..32g+31, at (c * ngroups + g) * tile_bytes;
+//    inside: scales [32] u16, then quant bytes [32][QB].
+// QB = 16 (Q4_0) or 32 (Q8_0). Padding rows/blocks are zero (scale 0 -> weight 0).
+// F32 matrices keep row-major floats in `f32`.
 struct at_qmat {
     at_ctx* ctx = nullptr;
     int type = AT_GGML_Q4_0;
     int orient = AT_ORIENT_N;
     int64_t rows = 0, cols = 0;
-    uint8_t* qs = nullptr;
-    uint16_t* d = nullptr;
+    uint8_t* tiles = nullptr;
+    int64_t tile_bytes = 0;
+    int64_t nsteps = 0;    // N: 32-block steps per row group
+    int64_t ngroups = 0;   // N: 4-row groups; T: 32-row groups
+    size_t bytes = 0;
     float* f32 = nullptr;
     bool owns = true;
 };
@@ -86,10 +95,33 @@ constexpr int QK = 32;
 inline int quant_bytes(int type) { return type == AT_GGML_Q4_0 ? 16 : 32; }
 inline int block_bytes(int type) { return type == AT_GGML_Q4_0 ? 18 : 34; }
 
-// Allocates the planes of `m` (type/orient/rows/cols already set).
+// Byte offsets of the scale and of the quant bytes of block (row, b) (b in
+// units of 32-element blocks) inside the tiles of a matrix.
+struct QTileMap {
+    int orient, qb;
+    int64_t tile_bytes, nsteps, ngroups;
+    __host__ __device__ __forceinline__ void offsets(int64_t row, int64_t b, int64_t* d_off, int64_t* q_off) const {
+        if (orient == AT_ORIENT_N) {
+            const int64_t g = row >> 2, r = row & 3, s = b >> 5, l = b & 31;
+            const int64_t t = (g * nsteps + s) * tile_bytes;
+            *d_off = t + (r * 32 + l) * 2;
+            *q_off = t + 256 + (r * 32 + l) * qb;
+        } else {
+            const int64_t g = row >> 5, l = row & 31;
+            const int64_t t = (b * ngroups + g) * tile_bytes;
+            *d_off = t + l * 2;
+            *q_off = t + 64 + l * qb;
+        }
+    }
+};
+inline QTileMap tile_map(const at_qmat* m) {
+    return QTileMap{m->orient, quant_bytes(m->type), m->tile_bytes, m->nsteps, m->ngroups};
+}
+
+// Allocates (zeroed) the tiles of `m` (type/orient/rows/cols already set).
 void qmat_alloc(at_qmat* m);
 void qmat_free(at_qmat* m);
-// Repack raw GGUF blocks (row-major stream, device memory) into the planes of
+// Repack raw GGUF blocks (row-major stream, device memory) into the tiles of
 // `m`, taking rows [r0, r0+m->rows) and block-columns [c0/32, ...) of a source
 // matrix with `src_cols` columns.
 void qmat_fill_from_blocks(at_qmat* m, const uint8_t* src_dev, int64_t src_cols, int64_t r0, int64_t c0,
@@ -131,10 +163,12 @@ struct GemvArgs {
     unsigned* counters = nullptr;
 };
 
+// pdl: launch with programmatic stream serialization (the kernel prefetches
+// its weights before waiting on the previous kernel in the stream).
 void launch_gemv_n(const at_qmat* m, int batch, Pro pro, Epi epi, const GemvArgs& a, int num_sms,
-                   cudaStream_t s);
+                   cudaStream_t s, bool pdl = false);
 void launch_gemv_t(const at_qmat* m, int batch, Pro pro, Epi epi, const GemvArgs& a, int num_sms,
-                   cudaStream_t s);
+                   cudaStream_t s, bool pdl = false);
 // Scratch floats / counters a T launch needs for (m, batch).
 void gemv_t_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* floats, size_t* counters);
 void launch_sgemv_f32(const float* A, const float* x, float* y, int M, int K, int batch, int a_ld,

@@ -82,31 +82,31 @@ __global__ void __launch_bounds__(1024) qdot_kernel(const uint8_t* __restrict__ 
 // ---------------------------------------------------------------------------
 __global__ void repack_kernel(const uint8_t* __restrict__ src, int bb /*18|34*/, int qb /*16|32*/,
                               int64_t src_nb, int64_t r0, int64_t cb0, int64_t n_rows, int64_t n_cb,
-                              int64_t dst_rows, int64_t dst_nb, int64_t dr0, int64_t dcb0, int orient,
-                              uint8_t* __restrict__ qs, uint16_t* __restrict__ d) {
+                              int64_t dr0, int64_t dcb0, QTileMap map, uint8_t* __restrict__ tiles) {
     const int64_t total = n_rows * n_cb;
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = t / n_cb, b = t - (t / n_cb) * n_cb;
         const uint8_t* s = src + ((r0 + r) * src_nb + cb0 + b) * bb;
-        const int64_t rr = dr0 + r, cc = dcb0 + b;
-        const int64_t dst = (orient == AT_ORIENT_N) ? (rr * dst_nb + cc) : (cc * dst_rows + rr);
-        d[dst] = (uint16_t)(s[0] | (s[1] << 8));
-        uint8_t* q = qs + dst * qb;
+        int64_t d_off, q_off;
+        map.offsets(dr0 + r, dcb0 + b, &d_off, &q_off);
+        tiles[d_off] = s[0];
+        tiles[d_off + 1] = s[1];
+        uint8_t* q = tiles + q_off;
         for (int k = 0; k < qb; ++k) q[k] = s[2 + k];
     }
 }
 
-__global__ void unpack_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ d, int bb, int qb,
-                              int64_t rows, int64_t nb, int orient, uint8_t* __restrict__ out) {
+__global__ void unpack_kernel(const uint8_t* __restrict__ tiles, QTileMap map, int bb, int qb, int64_t rows,
+                              int64_t nb, uint8_t* __restrict__ out) {
     const int64_t total = rows * nb;
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = t / nb, b = t - (t / nb) * nb;
-        const int64_t src = (orient == AT_ORIENT_N) ? (r * nb + b) : (b * rows + r);
+        int64_t d_off, q_off;
+        map.offsets(r, b, &d_off, &q_off);
         uint8_t* o = out + (r * nb + b) * bb;
-        o[0] = (uint8_t)(d[src] & 0xFF);
-        o[1] = (uint8_t)(d[src] >> 8);
-        const uint8_t* q = qs + src * qb;
-        for (int k = 0; k < qb; ++k) o[2 + k] = q[k];
+        o[0] = tiles[d_off];
+        o[1] = tiles[d_off + 1];
+        for (int k = 0; k < qb; ++k) o[2 + k] = tiles[q_off + k];
     }
 }
 
@@ -130,17 +130,28 @@ void qmat_alloc(at_qmat* m) {
     AT_REQUIRE(m->type == AT_GGML_Q4_0 || m->type == AT_GGML_Q8_0, AT_ERR_UNSUPPORTED,
                "unsupported tensor type " + std::to_string(m->type));
     AT_REQUIRE(m->cols % QK == 0, AT_ERR_INVALID_ARG, "quantized matrix cols must be a multiple of 32");
-    const size_t nblk = (size_t)(m->rows * (m->cols / QK));
-    AT_CUDA(cudaMalloc(&m->qs, nblk * quant_bytes(m->type)));
-    AT_CUDA(cudaMalloc(&m->d, nblk * 2 + 16));
+    const int64_t nb = m->cols / QK;
+    const int64_t qb = quant_bytes(m->type);
+    if (m->orient == AT_ORIENT_N) {
+        m->tile_bytes = 4 * 32 * (2 + qb);
+        m->nsteps = (nb + 31) / 32;
+        m->ngroups = (m->rows + 3) / 4;
+        m->bytes = (size_t)(m->ngroups * m->nsteps * m->tile_bytes);
+    } else {
+        m->tile_bytes = 32 * (2 + qb);
+        m->nsteps = 0;
+        m->ngroups = (m->rows + 31) / 32;
+        m->bytes = (size_t)(nb * m->ngroups * m->tile_bytes);
+    }
+    AT_CUDA(cudaMalloc(&m->tiles, m->bytes));
+    AT_CUDA(cudaMemset(m->tiles, 0, m->bytes));
 }
 
 void qmat_free(at_qmat* m) {
     if (!m->owns) return;
-    if (m->qs) cudaFree(m->qs);
-    if (m->d) cudaFree(m->d);
+    if (m->tiles) cudaFree(m->tiles);
     if (m->f32) cudaFree(m->f32);
-    m->qs = nullptr; m->d = nullptr; m->f32 = nullptr;
+    m->tiles = nullptr; m->f32 = nullptr;
 }
 
 void qmat_fill_region(at_qmat* m, const uint8_t* src_dev, int64_t src_cols, int64_t src_r0, int64_t src_c0,
@@ -152,8 +163,8 @@ void qmat_fill_region(at_qmat* m, const uint8_t* src_dev, int64_t src_cols, int6
     if (n_rows <= 0 || n_cols <= 0) return;
     const int64_t n_cb = n_cols / QK;
     repack_kernel<<<grid_for(n_rows * n_cb), TPB, 0, s>>>(src_dev, block_bytes(m->type), quant_bytes(m->type),
-                                                          src_cols / QK, src_r0, src_c0 / QK, n_rows, n_cb, m->rows,
-                                                          m->cols / QK, dst_r0, dst_c0 / QK, m->orient, m->qs, m->d);
+                                                          src_cols / QK, src_r0, src_c0 / QK, n_rows, n_cb, dst_r0,
+                                                          dst_c0 / QK, tile_map(m), m->tiles);
     AT_CUDA(cudaGetLastError());
 }
 
@@ -197,10 +208,21 @@ __global__ void sgemv_t_f32_kernel(const float* __restrict__ W, const float* __r
 
 __global__ void __launch_bounds__(256) rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ w, float eps,
                                                       int d) {
-    __shared__ float s_red[8], s_inv[1];
+    __shared__ float s_red[8];
+    __shared__ float s_inv;
     float* row = x + (size_t)blockIdx.x * d;
-    block_rms_inv<1>(row, nullptr, d, d, eps, s_red, s_inv);
-    for (int i = threadIdx.x; i < d; i += 256) row[i] = norm_apply(row[i], s_inv[0], w[i]);
+    float acc = 0.f;
+    for (int i = threadIdx.x; i < d; i += 256) acc = fmaf(row[i], row[i], acc);
+    acc = warp_sum(acc);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int k = 0; k < 8; ++k) t += s_red[k];
+        s_inv = rms_inv(t, d, eps);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < d; i += 256) row[i] = norm_apply(row[i], s_inv, w[i]);
 }
 
 // Kernels.softmaxInPlaceSegment (core/Kernels.java:181-232): max, exp(x - max),
@@ -474,7 +496,7 @@ int at_qmat_export(at_ctx* ctx, const at_qmat* m, void* dst) {
         }
         const int64_t nb = m->cols / QK;
         unpack_kernel<<<grid_for(m->rows * nb), TPB, 0, ctx->stream>>>(
-            m->qs, m->d, block_bytes(m->type), quant_bytes(m->type), m->rows, nb, m->orient, (uint8_t*)dst);
+            m->tiles, tile_map(m), block_bytes(m->type), quant_bytes(m->type), m->rows, nb, (uint8_t*)dst);
         AT_CUDA(cudaGetLastError());
     });
 }
@@ -491,6 +513,7 @@ int at_gemv(at_ctx* ctx, const at_qmat* m, const float* x, float* y, int batch) 
     return guard([&] {
         AT_REQUIRE(ctx && m && x && y, AT_ERR_INVALID_ARG, "null argument");
         AT_REQUIRE(batch >= 1 && batch <= 8, AT_ERR_INVALID_ARG, "batch must be in [1, 8]");
+        AT_REQUIRE(((uintptr_t)x & 15) == 0, AT_ERR_INVALID_ARG, "x must be 16-byte aligned");
         const int64_t in = (m->orient == AT_ORIENT_N) ? m->cols : m->rows;
         const int64_t outn = (m->orient == AT_ORIENT_N) ? m->rows : m->cols;
         if (m->type == AT_GGML_F32) {

@@ -16,6 +16,15 @@ __device__ __forceinline__ float fp16_ftz(uint32_t h) {
     return __uint_as_float(bits);
 }
 
+// Fp16.toFloat with the same results as fp16_ftz, using the hardware f16->f32
+// conversion: subnormal inputs are scaled by zero (keeping the sign), so they
+// flush to signed zero; NaN stays NaN.
+__device__ __forceinline__ float fp16_ftz_fast(uint32_t h) {
+    float f;
+    asm("{\n\t.reg .f16 t;\n\tmov.b16 t, %1;\n\tcvt.f32.f16 %0, t;\n\t}" : "=f"(f) : "h"((unsigned short)h));
+    return (h & 0x7C00u) ? f : __fmul_rn(f, 0.0f);
+}
+
 // Float with value 2^23 + byte k of w: byte k becomes the low mantissa byte
 // of 0x4B000000 (one PRMT). Subtracting 2^23 + offset is then exact.
 __device__ __forceinline__ float magic_byte(uint32_t w, int k) {
@@ -57,22 +66,38 @@ __device__ __forceinline__ float rms_inv(float sum_sq, int d, float eps) {
 }
 
 // Block-wide sum of squares of (xin + yin) for each of B rows of length d,
-// returning the RMSNorm scale per row in s_inv[B]. Requires blockDim.x == 256.
-template <int B>
+// returning the RMSNorm scale per row in s_inv[B]. Requires blockDim.x == NT,
+// d % 4 == 0 and 16-byte aligned rows. Loads are issued 8 float4 at a time
+// before any of them is used.
+template <int B, int NT = 256>
 __device__ __forceinline__ void block_rms_inv(const float* __restrict__ xin, const float* __restrict__ yin,
-                                              int stride, int d, float eps, float* s_red /*[8*B]*/,
+                                              int stride, int d, float eps, float* s_red /*[NT/32*B]*/,
                                               float* s_inv /*[B]*/) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n4 = d >> 2;
     float ss[B];
 #pragma unroll
     for (int b = 0; b < B; ++b) {
+        const float4* xr = reinterpret_cast<const float4*>(xin + (size_t)b * stride);
+        const float4* yr = yin ? reinterpret_cast<const float4*>(yin + (size_t)b * stride) : nullptr;
         float acc = 0.f;
-        const float* xr = xin + (size_t)b * stride;
-        const float* yr = yin ? yin + (size_t)b * stride : nullptr;
-        for (int i = tid; i < d; i += 256) {
-            float v = xr[i];
-            if (yr) v = __fadd_rn(v, yr[i]);
-            acc = fmaf(v, v, acc);
+        for (int base = 0; base < n4; base += NT * 8) {
+            float4 xv[8], yv[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int i = base + k * NT + tid;
+                xv[k] = (i < n4) ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                yv[k] = (yr && i < n4) ? yr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float a0 = __fadd_rn(xv[k].x, yv[k].x), a1 = __fadd_rn(xv[k].y, yv[k].y);
+                const float a2 = __fadd_rn(xv[k].z, yv[k].z), a3 = __fadd_rn(xv[k].w, yv[k].w);
+                acc = fmaf(a0, a0, acc);
+                acc = fmaf(a1, a1, acc);
+                acc = fmaf(a2, a2, acc);
+                acc = fmaf(a3, a3, acc);
+            }
         }
         ss[b] = warp_sum(acc);
     }
@@ -84,7 +109,7 @@ __device__ __forceinline__ void block_rms_inv(const float* __restrict__ xin, con
     if (tid < B) {
         float t = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) t += s_red[w * B + tid];
+        for (int w = 0; w < NT / 32; ++w) t += s_red[w * B + tid];
         s_inv[tid] = rms_inv(t, d, eps);
     }
     __syncthreads();

@@ -5,24 +5,32 @@
 // GGUF blocks stay resident in HBM and are dequantized in registers.
 //
 // Dequant: Q4_0 w = (q - 8) * d with the interleaved nibble order of
-// quant/Q4_0.java:39-42 (element 2k = low nibble of byte k); Q8_0 w = q * d
-// (quant/Q8_0.java:130-132); d decoded by Fp16.toFloat with flush-to-zero.
-// A nibble/byte becomes the exact float (q - 8) through one byte permute into
-// the mantissa of 2^23 plus one packed f32x2 subtraction; products and sums are
-// FP32 (packed f32x2 FMA), so (q - 8) * x is formed exactly as the reference's
-// dequantized weight times x, only the summation order differs.
+// quant/Q4_0.java:39-42 (element 2k = low nibble of byte k, 2k+1 = high
+// nibble); Q8_0 w = q * d (quant/Q8_0.java:130-132); d decoded by
+// Fp16.toFloat with flush-to-zero. A nibble/byte becomes the exact float
+// q - 8 (or q) through one byte permute into the mantissa of 2^23 and one
+// packed f32x2 subtraction; products and sums are FP32 (packed f32x2 FMA), so
+// each (q - 8) * x term equals the reference's dequantized weight times x and
+// only the summation order differs.
 //
-// Orientation N (rows = outputs, blocks along the row): each warp streams R
-// rows with 128-bit loads, lanes stride over blocks, x staged in shared
-// memory (per block: even elements then odd elements, padded to 36 floats so
-// a quarter-warp of 128-bit reads hits 32 distinct banks).
-// Orientation T (rows = inputs, blocks along the outputs, stored
-// block-column-major): each lane owns input rows of one block column and
-// accumulates the 32 (or 8) outputs of that block; lanes are combined by a
-// butterfly reduce-scatter, warps through shared memory, and CTAs that split
-// the rows through a deterministic ordered reduction by the last CTA to arrive.
+// Weights use the tiled layout of at_qmat (a lossless re-layout of whole
+// blocks): the bytes one warp step consumes are one contiguous tile.
+// Orientation N (rows = outputs, blocks along the row): a warp streams the
+// tiles (4 rows x 32 blocks) of its row group through a cp.async ring in
+// shared memory, one block per lane per step; x is staged once per CTA in
+// shared memory (natural order, 36 floats per 32-element block so a
+// quarter-warp of 128-bit reads touches 32 distinct banks).
+// Orientation T (rows = inputs, blocks along the outputs): a lane owns rows
+// of one block column (tiles of 32 rows) and accumulates its 32 (or 8)
+// outputs; lanes combine by a butterfly reduce-scatter, warps through shared
+// memory, and CTAs that split the rows through an ordered reduction by the
+// last CTA to arrive (counter per block column, reset by that CTA).
+// All kernels support programmatic dependent launch: weights (never written
+// by an earlier kernel) are prefetched before griddepcontrol.wait; every
+// activation read comes after it.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <map>
 #include <mutex>
 
@@ -34,46 +42,11 @@ namespace at {
 namespace {
 
 constexpr int THREADS = 256;
-constexpr int XPAD = 36;  // floats per staged 32-element block
+constexpr int XPAD = 36;                 // floats per staged 32-element block
+constexpr int kMaxXSmemChunk = 96 * 1024;
 
-// ---------------------------------------------------------------------------
-// Per-block dot products on staged x.
-// ---------------------------------------------------------------------------
-// Q4_0: xr[0..3] hold the 16 even elements, xr[4..7] the 16 odd elements.
-__device__ __forceinline__ float dot_q4(const uint4 q, const float4* xr) {
-    const float2 moff = f2(-8388616.f, -8388616.f);  // -(2^23 + 8)
-    float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t lo = w[i] & 0x0F0F0F0Fu, hi = (w[i] >> 4) & 0x0F0F0F0Fu;
-        const float2 e01 = __fadd2_rn(f2(magic_byte(lo, 0), magic_byte(lo, 1)), moff);
-        const float2 e23 = __fadd2_rn(f2(magic_byte(lo, 2), magic_byte(lo, 3)), moff);
-        const float2 o01 = __fadd2_rn(f2(magic_byte(hi, 0), magic_byte(hi, 1)), moff);
-        const float2 o23 = __fadd2_rn(f2(magic_byte(hi, 2), magic_byte(hi, 3)), moff);
-        a0 = __ffma2_rn(e01, f2(xr[i].x, xr[i].y), a0);
-        a1 = __ffma2_rn(e23, f2(xr[i].z, xr[i].w), a1);
-        a0 = __ffma2_rn(o01, f2(xr[4 + i].x, xr[4 + i].y), a0);
-        a1 = __ffma2_rn(o23, f2(xr[4 + i].z, xr[4 + i].w), a1);
-    }
-    return (a0.x + a0.y) + (a1.x + a1.y);
-}
-
-// Q8_0: xr[0..7] hold the 32 elements in order.
-__device__ __forceinline__ float dot_q8(const uint4 q0, const uint4 q1, const float4* xr) {
-    const float2 moff = f2(-8388736.f, -8388736.f);  // -(2^23 + 128)
-    float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
-    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const uint32_t u = w[i] ^ 0x80808080u;  // int8 q -> unsigned q + 128
-        const float2 v01 = __fadd2_rn(f2(magic_byte(u, 0), magic_byte(u, 1)), moff);
-        const float2 v23 = __fadd2_rn(f2(magic_byte(u, 2), magic_byte(u, 3)), moff);
-        a0 = __ffma2_rn(v01, f2(xr[i].x, xr[i].y), a0);
-        a1 = __ffma2_rn(v23, f2(xr[i].z, xr[i].w), a1);
-    }
-    return (a0.x + a0.y) + (a1.x + a1.y);
-}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 template <int QT>
 struct QTraits;
@@ -82,19 +55,358 @@ struct QTraits<AT_GGML_Q4_0> { static constexpr int QB = 16; static constexpr in
 template <>
 struct QTraits<AT_GGML_Q8_0> { static constexpr int QB = 32; static constexpr int NV = 2; };
 
-// Slot of element w (0..31) of a block in the staged x layout.
+// Decodes the 32 weights of one block (unscaled: q - 8 for Q4_0, q for Q8_0)
+// into 16 float pairs of consecutive elements (2k, 2k+1).
 template <int QT>
-__device__ __forceinline__ int x_slot(int w) {
-    if constexpr (QT == AT_GGML_Q4_0) return (w & 1) ? 16 + (w >> 1) : (w >> 1);
-    else return w;
+__device__ __forceinline__ void decode32(const uint4* q, float2* w) {
+    if constexpr (QT == AT_GGML_Q4_0) {
+        const float2 moff = f2(-8388616.f, -8388616.f);  // -(2^23 + 8)
+        const uint32_t ws[4] = {q[0].x, q[0].y, q[0].z, q[0].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t lo = ws[i] & 0x0F0F0F0Fu, hi = (ws[i] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                w[4 * i + k] = __fadd2_rn(f2(magic_byte(lo, k), magic_byte(hi, k)), moff);  // elements 8i+2k, +1
+        }
+    } else {
+        const float2 moff = f2(-8388736.f, -8388736.f);  // -(2^23 + 128)
+        const uint32_t ws[8] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t u = ws[i] ^ 0x80808080u;  // int8 q -> unsigned q + 128
+            w[2 * i + 0] = __fadd2_rn(f2(magic_byte(u, 0), magic_byte(u, 1)), moff);  // elements 4i, 4i+1
+            w[2 * i + 1] = __fadd2_rn(f2(magic_byte(u, 2), magic_byte(u, 3)), moff);  // elements 4i+2, 4i+3
+        }
+    }
+}
+
+// Two fp16 values (1024 + v) packed in h, minus c, as exact FP32 pair: one
+// mixed-precision add per element (f16 operand, f32 result), on the FMA pipe.
+__device__ __forceinline__ float2 h2_minus(uint32_t h, float c) {
+    float a, b;
+    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+        "add.rn.f32.f16 %0, lo, %3;\n\tadd.rn.f32.f16 %1, hi, %3;\n\t}"
+        : "=f"(a), "=f"(b) : "r"(h), "f"(c));
+    return f2(a, b);
+}
+
+// Unscaled dot of one block with x staged by stage_x (see there for the
+// element order). A pair of fp16 (1024 + nibble) or (1024 + byte) values is
+// built with one LOP3 from the packed quant word; an exact f16->f32 add
+// removes the offset.
+//  Q4_0, word i (elements 8i..8i+7, byte k = e[2k] | e[2k+1] << 4):
+//    (w & 0x000F000F)  -> 1024 + (e0, e4)       minus 1032   -> e - 8
+//    (w & 0x00F000F0)  -> 1024 + 16 (e1, e5)    minus 1152   -> 16 (e - 8)
+//    same on w >> 8    -> (e2, e6), 16 (e3, e7)
+//    x staged per word as (x0, x4, x1/16, x5/16), (x2, x6, x3/16, x7/16).
+//  Q8_0, word i (elements 4i..4i+3, int8): ((w & 0x00FF00FF) ^ 0x64806480)
+//    -> 1024 + 128 + (e0, e2), minus 1152 -> e; same on w >> 8 -> (e1, e3);
+//    x staged per word as (x0, x2, x1, x3).
+template <int QT>
+__device__ __forceinline__ float dot32(const uint4* q, const float4* xr) {
+    float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
+    if constexpr (QT == AT_GGML_Q4_0) {
+        const uint32_t ws[4] = {q[0].x, q[0].y, q[0].z, q[0].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t w = ws[i], w8 = ws[i] >> 8;
+            const float2 p0 = h2_minus((w & 0x000F000Fu) | 0x64006400u, -1032.f);
+            const float2 p1 = h2_minus((w & 0x00F000F0u) | 0x64006400u, -1152.f);
+            const float2 p2 = h2_minus((w8 & 0x000F000Fu) | 0x64006400u, -1032.f);
+            const float2 p3 = h2_minus((w8 & 0x00F000F0u) | 0x64006400u, -1152.f);
+            a0 = __ffma2_rn(p0, f2(xr[2 * i].x, xr[2 * i].y), a0);
+            a1 = __ffma2_rn(p1, f2(xr[2 * i].z, xr[2 * i].w), a1);
+            a0 = __ffma2_rn(p2, f2(xr[2 * i + 1].x, xr[2 * i + 1].y), a0);
+            a1 = __ffma2_rn(p3, f2(xr[2 * i + 1].z, xr[2 * i + 1].w), a1);
+        }
+    } else {
+        const uint32_t ws[8] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t w = ws[i], w8 = ws[i] >> 8;
+            const float2 p0 = h2_minus((w & 0x00FF00FFu) ^ 0x64806480u, -1152.f);
+            const float2 p1 = h2_minus((w8 & 0x00FF00FFu) ^ 0x64806480u, -1152.f);
+            a0 = __ffma2_rn(p0, f2(xr[i].x, xr[i].y), a0);
+            a1 = __ffma2_rn(p1, f2(xr[i].z, xr[i].w), a1);
+        }
+    }
+    return (a0.x + a0.y) + (a1.x + a1.y);
+}
+
+// Position of natural element e (0..31) of a block in the staged x row, and
+// the exact power-of-two scale applied to it (matches dot32).
+template <int QT>
+__device__ __forceinline__ int x_slot(int e) {
+    if constexpr (QT == AT_GGML_Q4_0) {
+        const int w = e >> 3, r = e & 7;  // word, element in word
+        // r -> slot: 0->0, 4->1, 1->2, 5->3, 2->4, 6->5, 3->6, 7->7
+        const int hi = r & 1, idx = r >> 1;  // r = 2 * byte + nibble
+        return 8 * w + 4 * (idx & 1) + 2 * hi + (idx >> 1);
+    } else {
+        const int w = e >> 2, r = e & 3;  // (x0, x2, x1, x3)
+        return 4 * w + 2 * (r & 1) + (r >> 1);
+    }
+}
+template <int QT>
+__device__ __forceinline__ float x_scale(int e) {
+    if constexpr (QT == AT_GGML_Q4_0) return (e & 1) ? 0.0625f : 1.0f;
+    else return 1.0f;
+}
+
+// Stages x (or the normed x + y) for blocks [b0, b0 + nbc) of B rows into
+// shared memory in the order dot32<QT> reads it, XPAD floats per block.
+// float4 global loads, eight in flight per thread before any is stored.
+template <int QT, int B, Pro PRO, int NT = THREADS>
+__device__ __forceinline__ void stage_x(float* xs, const GemvArgs& a, int b0, int nbc, int chunk_blocks,
+                                        const float* s_inv) {
+    const int nf4 = nbc * 8;
+    const int total = B * nf4;
+    for (int base = 0; base < total; base += NT * 8) {
+        float4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int idx = base + k * NT + threadIdx.x;
+            if (idx < total) {
+                const int bb = idx / nf4, r = idx - bb * nf4;
+                const size_t off = (size_t)bb * a.x_stride + (size_t)(b0 + (r >> 3)) * 32 + (r & 7) * 4;
+                if constexpr (PRO == Pro::Plain) {
+                    v[k] = *reinterpret_cast<const float4*>(a.x + off);
+                } else {
+                    float4 t = *reinterpret_cast<const float4*>(a.xin + off);
+                    if (a.yin) {
+                        const float4 u = *reinterpret_cast<const float4*>(a.yin + off);
+                        t.x = __fadd_rn(t.x, u.x); t.y = __fadd_rn(t.y, u.y);
+                        t.z = __fadd_rn(t.z, u.z); t.w = __fadd_rn(t.w, u.w);
+                    }
+                    v[k] = t;
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int idx = base + k * NT + threadIdx.x;
+            if (idx < total) {
+                const int bb = idx / nf4, r = idx - bb * nf4;
+                const int blk = r >> 3, q4 = r & 7;
+                float o[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+                if constexpr (PRO == Pro::AddNorm) {
+                    const float4 g = *reinterpret_cast<const float4*>(a.gamma + (size_t)(b0 + blk) * 32 + q4 * 4);
+                    const float inv = s_inv[bb];
+                    o[0] = norm_apply(o[0], inv, g.x); o[1] = norm_apply(o[1], inv, g.y);
+                    o[2] = norm_apply(o[2], inv, g.z); o[3] = norm_apply(o[3], inv, g.w);
+                }
+                float* dst = xs + ((size_t)bb * chunk_blocks + blk) * XPAD;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const int e = q4 * 4 + t;
+                    dst[x_slot<QT>(e)] = __fmul_rn(o[t], x_scale<QT>(e));
+                }
+            }
+        }
+    }
+}
+
+// Writes the normed x (x + y scaled, F7 residual stream) for all B rows: CTA 0 only.
+template <int B, int NT = THREADS>
+__device__ __forceinline__ void write_xout(const GemvArgs& a, int d, const float* s_inv) {
+    for (int idx = threadIdx.x; idx < B * d / 4; idx += NT) {
+        const int bb = idx / (d / 4), i4 = idx - bb * (d / 4);
+        const size_t off = (size_t)bb * a.x_stride + (size_t)i4 * 4;
+        float4 t = *reinterpret_cast<const float4*>(a.xin + off);
+        if (a.yin) {
+            const float4 u = *reinterpret_cast<const float4*>(a.yin + off);
+            t.x = __fadd_rn(t.x, u.x); t.y = __fadd_rn(t.y, u.y); t.z = __fadd_rn(t.z, u.z); t.w = __fadd_rn(t.w, u.w);
+        }
+        const float4 g = *reinterpret_cast<const float4*>(a.gamma + (size_t)i4 * 4);
+        const float inv = s_inv[bb];
+        *reinterpret_cast<float4*>(a.xout + off) = make_float4(
+            norm_apply(t.x, inv, g.x), norm_apply(t.y, inv, g.y), norm_apply(t.z, inv, g.z), norm_apply(t.w, inv, g.w));
+    }
+}
+
+template <Epi EPI>
+__device__ __forceinline__ float n_epilogue(float g, float u) {
+    if constexpr (EPI == Epi::SiluMul) {
+        // Kernels.siluInPlace then elementwiseMul (core/Kernels.java:86-87,
+        // inference/LlamaModel.java:372-380): g / (1 + exp(-g)) * u
+        return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    } else {
+        return g;
+    }
 }
 
 // ---------------------------------------------------------------------------
-// Orientation N
+// Orientation N, tile streams through per-warp cp.async rings
 // ---------------------------------------------------------------------------
-struct NParams {
-    const uint8_t* qs[2];
-    const uint16_t* d[2];
+// A warp owns a 4-row group and a contiguous range of its 32-block steps; one
+// step is one tile (4 rows x 32 blocks, scales then quant bytes), copied
+// 16 bytes per lane into the warp's ring slot with cp.async. Lanes then read
+// their own block of each row. Warps that split one group's steps (KS > 1)
+// combine through shared memory in a fixed order. A CTA stages x once and
+// walks `per` rounds of groups.
+constexpr int N4_THREADS = 512;
+constexpr int N4_WARPS = N4_THREADS / 32;
+
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int QT>
+struct NTile {
+    static constexpr int QB = QTraits<QT>::QB;
+    static constexpr int BYTES = 4 * 32 * (2 + QB);  // 2304 (Q4_0) or 4352 (Q8_0)
+    static constexpr int CHUNKS = BYTES / 16;
+};
+
+struct N4Params {
+    const uint8_t* tiles[2];
+    int rows, nb, ngroups, nsteps;
+    int KS;         // warps splitting the steps of one group
+    int gpc;        // groups per CTA round = N4_WARPS / KS
+    int per;        // rounds per CTA
+    int steps_ks;   // steps per step range = ceil(nsteps / KS)
+    int ring_off;
+    GemvArgs a;
+};
+
+template <int QT, int NM>
+__device__ __forceinline__ void n4_issue(uint32_t slot, const N4Params& p, int g, int s, int lane) {
+    using TL = NTile<QT>;
+    if (g < p.ngroups && s < p.nsteps) {
+#pragma unroll
+        for (int m = 0; m < NM; ++m) {
+            const uint8_t* src = p.tiles[m] + ((size_t)g * p.nsteps + s) * TL::BYTES;
+            for (int k = lane; k < TL::CHUNKS; k += 32)
+                cp_async16(slot + (uint32_t)(m * TL::BYTES + 16 * k), src + 16 * k);
+        }
+    }
+    cp_commit();
+}
+
+template <int QT, int B, Pro PRO, Epi EPI, int NST>
+__global__ void __launch_bounds__(N4_THREADS, 1) gemv_n4_kernel(const N4Params p) {
+    constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
+    using TL = NTile<QT>;
+    constexpr int SLOT = NM * TL::BYTES;
+    constexpr int NV = QTraits<QT>::NV;
+    extern __shared__ __align__(16) float xs[];
+    __shared__ float s_red[N4_WARPS * B];
+    __shared__ float s_inv[B];
+    __shared__ float red[N4_WARPS][NM * 4 * B];
+
+    pdl_trigger();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int kpart = warp % p.KS, gslot = warp / p.KS;
+    const int s0 = kpart * p.steps_ks;
+    const int nsk = max(0, min(p.nsteps, s0 + p.steps_ks) - s0);  // steps of this warp per round
+    const int T = p.per * nsk;
+    const uint8_t* ring_ptr = reinterpret_cast<const uint8_t*>(xs) + p.ring_off + warp * NST * SLOT;
+    const uint32_t ring = (uint32_t)__cvta_generic_to_shared(ring_ptr);
+    auto group_of = [&](int round) { return (blockIdx.x * p.per + round) * p.gpc + gslot; };
+
+    // Weights are never written by earlier kernels: start their copies
+    // before waiting on those kernels.
+#pragma unroll
+    for (int k = 0; k < NST; ++k) {
+        if (k < T) n4_issue<QT, NM>(ring + k * SLOT, p, group_of(k / nsk), s0 + k % nsk, lane);
+        else cp_commit();
+    }
+    pdl_wait();
+
+    const int d_model = p.nb * 32;
+    if constexpr (PRO == Pro::AddNorm) {
+        block_rms_inv<B, N4_THREADS>(p.a.xin, p.a.yin, p.a.x_stride, d_model, p.a.eps, s_red, s_inv);
+        if (blockIdx.x == 0) write_xout<B, N4_THREADS>(p.a, d_model, s_inv);
+    }
+    stage_x<QT, B, PRO, N4_THREADS>(xs, p.a, 0, p.nb, p.nb, s_inv);
+    __syncthreads();
+
+    float acc[NM * 4][B];
+#pragma unroll
+    for (int i = 0; i < NM * 4; ++i)
+#pragma unroll
+        for (int b = 0; b < B; ++b) acc[i][b] = 0.f;
+
+    int t = 0;
+    for (int round = 0; round < p.per; ++round) {
+        const int g = group_of(round);
+        for (int ks = 0; ks < nsk; ++ks, ++t) {
+            cp_wait<NST - 1>();
+            __syncwarp();  // every lane's 16-byte pieces of this slot have landed
+            const int slot = t % NST;
+            const uint8_t* sp = ring_ptr + slot * SLOT;
+            const int j = (s0 + ks) * 32 + lane;  // this lane's block
+            if (g < p.ngroups && j < p.nb) {
+                uint4 q[NM * 4][NV];
+                float dsc[NM * 4];
+#pragma unroll
+                for (int m = 0; m < NM; ++m)
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const uint8_t* tb = sp + m * TL::BYTES;
+#pragma unroll
+                        for (int v = 0; v < NV; ++v)
+                            q[m * 4 + r][v] = *reinterpret_cast<const uint4*>(tb + 256 + (r * 32 + lane) * TL::QB + 16 * v);
+                        dsc[m * 4 + r] = fp16_ftz_fast(*reinterpret_cast<const uint16_t*>(tb + (r * 32 + lane) * 2));
+                    }
+#pragma unroll
+                for (int b = 0; b < B; ++b) {
+                    const float4* xv = reinterpret_cast<const float4*>(xs + ((size_t)b * p.nb + j) * XPAD);
+                    float4 xr[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) xr[k] = xv[k];
+#pragma unroll
+                    for (int i = 0; i < NM * 4; ++i) acc[i][b] = fmaf(dsc[i], dot32<QT>(q[i], xr), acc[i][b]);
+                }
+            }
+            __syncwarp();  // every lane is done with this slot before it is refilled
+            const int tn = t + NST;
+            if (tn < T) n4_issue<QT, NM>(ring + slot * SLOT, p, group_of(tn / nsk), s0 + tn % nsk, lane);
+            else cp_commit();
+        }
+        // round complete: reduce over lanes, then over the KS warps of each group
+#pragma unroll
+        for (int i = 0; i < NM * 4; ++i)
+#pragma unroll
+            for (int b = 0; b < B; ++b) acc[i][b] = warp_sum(acc[i][b]);
+        if (lane == 0) {
+#pragma unroll
+            for (int i = 0; i < NM * 4; ++i)
+#pragma unroll
+                for (int b = 0; b < B; ++b) red[warp][i * B + b] = acc[i][b];
+        }
+#pragma unroll
+        for (int i = 0; i < NM * 4; ++i)
+#pragma unroll
+            for (int b = 0; b < B; ++b) acc[i][b] = 0.f;
+        __syncthreads();
+        if (kpart == 0 && lane < 4 * B) {
+            const int r = lane / B, b = lane - (lane / B) * B;
+            const int row = g * 4 + r;
+            if (g < p.ngroups && row < p.rows) {
+                float v0 = 0.f, v1 = 0.f;
+                for (int k = 0; k < p.KS; ++k) {
+                    v0 += red[warp + k][(0 * 4 + r) * B + b];
+                    if constexpr (NM == 2) v1 += red[warp + k][(1 * 4 + r) * B + b];
+                }
+                p.a.y[(size_t)b * p.a.y_stride + row] = n_epilogue<EPI>(v0, v1);
+            }
+        }
+        __syncthreads();
+    }
+    cp_wait<0>();
+}
+
+// ---------------------------------------------------------------------------
+// Orientation N, K staged in chunks (x larger than the shared-memory budget)
+// ---------------------------------------------------------------------------
+struct NCParams {
+    const uint8_t* tiles[2];
+    QTileMap map;
     int rows, nb;
     int chunk_blocks, nchunks;
     int wk;        // warps splitting the blocks of a row (1, 2, 4, 8)
@@ -102,31 +414,10 @@ struct NParams {
     GemvArgs a;
 };
 
-template <int QT, int B, Pro PRO>
-__device__ __forceinline__ void fill_x_n(float* xs, const NParams& p, int b0, int nbc, const float* s_inv) {
-    const int n = nbc * 32;
-    const int cols = p.nb * 32;
-    for (int idx = threadIdx.x; idx < B * n; idx += THREADS) {
-        const int bb = idx / n, e = idx - bb * n;
-        const int col = b0 * 32 + e;
-        float v;
-        if constexpr (PRO == Pro::Plain) {
-            v = p.a.x[(size_t)bb * p.a.x_stride + col];
-        } else {
-            float t = p.a.xin[(size_t)bb * p.a.x_stride + col];
-            if (p.a.yin) t = __fadd_rn(t, p.a.yin[(size_t)bb * p.a.x_stride + col]);
-            v = norm_apply(t, s_inv[bb], p.a.gamma[col]);
-        }
-        (void)cols;
-        xs[(bb * p.chunk_blocks + (e >> 5)) * XPAD + x_slot<QT>(e & 31)] = v;
-    }
-}
-
 template <int QT, int B, Pro PRO, Epi EPI>
-__global__ void __launch_bounds__(THREADS) gemv_n_kernel(const NParams p) {
+__global__ void __launch_bounds__(THREADS) gemv_nc_kernel(const NCParams p) {
     constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
     constexpr int R = (NM == 2) ? 2 : 4;
-    constexpr int QB = QTraits<QT>::QB;
     constexpr int NV = QTraits<QT>::NV;
     constexpr int NVAL = NM * R * B;
 
@@ -135,6 +426,8 @@ __global__ void __launch_bounds__(THREADS) gemv_n_kernel(const NParams p) {
     __shared__ float s_red[8 * B];
     __shared__ float s_inv[B];
 
+    pdl_trigger();
+    pdl_wait();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int wk = p.wk, wrn = 8 / wk;
     const int wr = warp / wk, wki = warp - wr * wk;
@@ -142,16 +435,8 @@ __global__ void __launch_bounds__(THREADS) gemv_n_kernel(const NParams p) {
 
     if constexpr (PRO == Pro::AddNorm) {
         block_rms_inv<B>(p.a.xin, p.a.yin, p.a.x_stride, d_model, p.a.eps, s_red, s_inv);
-        if (blockIdx.x == 0) {
-            for (int idx = tid; idx < B * d_model; idx += THREADS) {
-                const int bb = idx / d_model, i = idx - bb * d_model;
-                float t = p.a.xin[(size_t)bb * p.a.x_stride + i];
-                if (p.a.yin) t = __fadd_rn(t, p.a.yin[(size_t)bb * p.a.x_stride + i]);
-                p.a.xout[(size_t)bb * p.a.x_stride + i] = norm_apply(t, s_inv[bb], p.a.gamma[i]);
-            }
-        }
+        if (blockIdx.x == 0) write_xout<B>(p.a, d_model, s_inv);
     }
-
     for (int tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
         const int row0 = (tile * wrn + wr) * R;
         float acc[NM][R][B];
@@ -161,13 +446,12 @@ __global__ void __launch_bounds__(THREADS) gemv_n_kernel(const NParams p) {
             for (int r = 0; r < R; ++r)
 #pragma unroll
                 for (int b = 0; b < B; ++b) acc[m][r][b] = 0.f;
-
         for (int ch = 0; ch < p.nchunks; ++ch) {
             const int b0 = ch * p.chunk_blocks;
             const int nbc = min(p.chunk_blocks, p.nb - b0);
             if (p.nchunks > 1 || tile == (int)blockIdx.x) {
                 __syncthreads();
-                fill_x_n<QT, B, PRO>(xs, p, b0, nbc, s_inv);
+                stage_x<QT, B, PRO>(xs, p.a, b0, nbc, p.chunk_blocks, s_inv);
                 __syncthreads();
             }
             for (int j = lane + 32 * wki; j < nbc; j += 32 * wk) {
@@ -179,11 +463,11 @@ __global__ void __launch_bounds__(THREADS) gemv_n_kernel(const NParams p) {
                     for (int r = 0; r < R; ++r) {
                         const int row = row0 + r;
                         if (row < p.rows) {
-                            const size_t blk = (size_t)row * p.nb + b0 + j;
-                            const uint8_t* src = p.qs[m] + blk * QB;
+                            int64_t d_off, q_off;
+                            p.map.offsets(row, b0 + j, &d_off, &q_off);
 #pragma unroll
-                            for (int v = 0; v < NV; ++v) q[m][r][v] = ld_stream_u4(src + 16 * v);
-                            dsc[m][r] = fp16_ftz(ld_stream_u16(p.d[m] + blk));
+                            for (int v = 0; v < NV; ++v) q[m][r][v] = ld_stream_u4(p.tiles[m] + q_off + 16 * v);
+                            dsc[m][r] = fp16_ftz(ld_stream_u16(reinterpret_cast<const uint16_t*>(p.tiles[m] + d_off)));
                         } else {
 #pragma unroll
                             for (int v = 0; v < NV; ++v) q[m][r][v] = make_uint4(0, 0, 0, 0);
@@ -192,23 +476,17 @@ __global__ void __launch_bounds__(THREADS) gemv_n_kernel(const NParams p) {
                     }
 #pragma unroll
                 for (int b = 0; b < B; ++b) {
-                    const float4* xv = reinterpret_cast<const float4*>(xs + (b * p.chunk_blocks + j) * XPAD);
+                    const float4* xv = reinterpret_cast<const float4*>(xs + ((size_t)b * p.chunk_blocks + j) * XPAD);
                     float4 xr[8];
 #pragma unroll
                     for (int t = 0; t < 8; ++t) xr[t] = xv[t];
 #pragma unroll
                     for (int m = 0; m < NM; ++m)
 #pragma unroll
-                        for (int r = 0; r < R; ++r) {
-                            float dv;
-                            if constexpr (QT == AT_GGML_Q4_0) dv = dot_q4(q[m][r][0], xr);
-                            else dv = dot_q8(q[m][r][0], q[m][r][NV - 1], xr);
-                            acc[m][r][b] = fmaf(dsc[m][r], dv, acc[m][r][b]);
-                        }
+                        for (int r = 0; r < R; ++r) acc[m][r][b] = fmaf(dsc[m][r], dot32<QT>(q[m][r], xr), acc[m][r][b]);
                 }
             }
         }
-        // warp reduction, then ordered reduction across the wk warps of a row tile
 #pragma unroll
         for (int m = 0; m < NM; ++m)
 #pragma unroll
@@ -234,29 +512,23 @@ __global__ void __launch_bounds__(THREADS) gemv_n_kernel(const NParams p) {
                     v0 += red[wr * wk + k][(0 * R + r) * B + b];
                     if constexpr (NM == 2) v1 += red[wr * wk + k][(1 * R + r) * B + b];
                 }
-                float out = v0;
-                if constexpr (EPI == Epi::SiluMul) {
-                    // Kernels.siluInPlace then elementwiseMul (core/Kernels.java:86-87,
-                    // inference/LlamaModel.java:372-380): g / (1 + exp(-g)) * u
-                    const float sg = __fdiv_rn(v0, __fadd_rn(1.0f, expf(-v0)));
-                    out = __fmul_rn(sg, v1);
-                }
-                p.a.y[(size_t)b * p.a.y_stride + row] = out;
+                p.a.y[(size_t)b * p.a.y_stride + row] = n_epilogue<EPI>(v0, v1);
             }
         }
     }
 }
 
 // ---------------------------------------------------------------------------
-// Orientation T (block-column-major planes)
+// Orientation T (tiles of 32 rows x 1 block column)
 // ---------------------------------------------------------------------------
 struct TParams {
-    const uint8_t* qs;
-    const uint16_t* d;
+    const uint8_t* tiles;
+    int64_t tile_bytes;
     int E;             // input rows
+    int ngroups;       // 32-row groups
     int n_bc;          // block columns (outputs / 32)
     int S;             // CTAs splitting the rows of a block column
-    int e_per_split;   // rows per CTA
+    int e_per_split;   // rows per CTA (multiple of the CTA row step)
     GemvArgs a;
 };
 
@@ -267,66 +539,55 @@ struct TCfg {
     static constexpr int LPB = 32 / CPL;           // lanes per block
     static constexpr int ROWS_PER_WARP = 32 / LPB; // rows a warp covers per step
     static constexpr int STEP = 8 * ROWS_PER_WARP; // rows a CTA covers per step
+    static constexpr int U = 4;                    // steps in flight
 };
 
-// Decodes the CPL weights this lane owns into float pairs (q - 8 or q), in the
-// column order given by col_of_pair().
 template <int QT, int CPL>
-__device__ __forceinline__ void decode_t(const uint4* q, int quarter, float2* wv) {
-    if constexpr (QT == AT_GGML_Q4_0) {
-        const float2 moff = f2(-8388616.f, -8388616.f);
-        uint32_t w[CPL / 8];
-        if constexpr (CPL == 32) { w[0] = q[0].x; w[1] = q[0].y; w[2] = q[0].z; w[3] = q[0].w; }
-        else {
-            const uint32_t a[4] = {q[0].x, q[0].y, q[0].z, q[0].w};
-            w[0] = a[quarter];
-        }
-#pragma unroll
-        for (int i = 0; i < CPL / 8; ++i) {
-            const uint32_t lo = w[i] & 0x0F0F0F0Fu, hi = (w[i] >> 4) & 0x0F0F0F0Fu;
-            wv[4 * i + 0] = __fadd2_rn(f2(magic_byte(lo, 0), magic_byte(lo, 1)), moff);  // cols 8i+0, 8i+2
-            wv[4 * i + 1] = __fadd2_rn(f2(magic_byte(lo, 2), magic_byte(lo, 3)), moff);  // cols 8i+4, 8i+6
-            wv[4 * i + 2] = __fadd2_rn(f2(magic_byte(hi, 0), magic_byte(hi, 1)), moff);  // cols 8i+1, 8i+3
-            wv[4 * i + 3] = __fadd2_rn(f2(magic_byte(hi, 2), magic_byte(hi, 3)), moff);  // cols 8i+5, 8i+7
-        }
+__device__ __forceinline__ void t_load(uint4* q, float& dsc, const uint8_t* col, int64_t tb, int e, int quarter) {
+    constexpr int QB = QTraits<QT>::QB;
+    const uint8_t* tile = col + (int64_t)(e >> 5) * tb;
+    const int l = e & 31;
+    const uint8_t* qp = tile + 64 + l * QB;
+    if constexpr (CPL == 32) {
+        q[0] = ld_stream_u4(qp);
+        if constexpr (QT == AT_GGML_Q8_0) q[1] = ld_stream_u4(qp + 16);
     } else {
-        const float2 moff = f2(-8388736.f, -8388736.f);
-        uint32_t w[CPL / 4];
-        if constexpr (CPL == 32) {
-            w[0] = q[0].x; w[1] = q[0].y; w[2] = q[0].z; w[3] = q[0].w;
-            w[4] = q[1].x; w[5] = q[1].y; w[6] = q[1].z; w[7] = q[1].w;
-        } else {
-            const uint32_t a[8] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w};
-            w[0] = a[2 * quarter];
-            w[1] = a[2 * quarter + 1];
-        }
-#pragma unroll
-        for (int i = 0; i < CPL / 4; ++i) {
-            const uint32_t u = w[i] ^ 0x80808080u;
-            wv[2 * i + 0] = __fadd2_rn(f2(magic_byte(u, 0), magic_byte(u, 1)), moff);  // cols 4i, 4i+1
-            wv[2 * i + 1] = __fadd2_rn(f2(magic_byte(u, 2), magic_byte(u, 3)), moff);  // cols 4i+2, 4i+3
-        }
+        // the 16-byte vector holding this lane's quarter (4 or 8 bytes)
+        q[0] = ld_stream_u4(qp + (QT == AT_GGML_Q8_0 ? 16 * (quarter >> 1) : 0));
     }
+    dsc = fp16_ftz(ld_stream_u16(reinterpret_cast<const uint16_t*>(tile + l * 2)));
 }
 
-// Column (within the lane's CPL columns) of element h (0/1) of pair k.
-template <int QT>
-__device__ __forceinline__ int col_of_pair(int k, int h) {
-    if constexpr (QT == AT_GGML_Q4_0) {
-        const int i = k >> 2, s = k & 3;
-        return 8 * i + ((s & 1) ? 4 : 0) + ((s & 2) ? 1 : 0) + 2 * h;
+// Decodes this lane's CPL weights into CPL/2 pairs of consecutive columns.
+template <int QT, int CPL>
+__device__ __forceinline__ void t_decode(const uint4* q, int quarter, float2* wv) {
+    if constexpr (CPL == 32) {
+        decode32<QT>(q, wv);
+    } else if constexpr (QT == AT_GGML_Q4_0) {
+        const uint32_t a4[4] = {q[0].x, q[0].y, q[0].z, q[0].w};
+        const uint32_t w = a4[quarter];  // bytes 4*quarter..: columns 8*quarter + 0..7
+        const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+        const float2 moff = f2(-8388616.f, -8388616.f);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) wv[k] = __fadd2_rn(f2(magic_byte(lo, k), magic_byte(hi, k)), moff);
     } else {
-        return 2 * k + h;
+        const uint32_t a4[4] = {q[0].x, q[0].y, q[0].z, q[0].w};
+        const int h = quarter & 1;  // which 8 bytes of the loaded 16
+        const float2 moff = f2(-8388736.f, -8388736.f);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const uint32_t u = a4[2 * h + i] ^ 0x80808080u;
+            wv[2 * i + 0] = __fadd2_rn(f2(magic_byte(u, 0), magic_byte(u, 1)), moff);
+            wv[2 * i + 1] = __fadd2_rn(f2(magic_byte(u, 2), magic_byte(u, 3)), moff);
+        }
     }
 }
 
 template <int QT, int B, Pro PRO, Epi EPI>
-__global__ void __launch_bounds__(THREADS) gemv_t_kernel(const TParams p) {
+__global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
     using C = TCfg<B>;
-    constexpr int CPL = C::CPL, LPB = C::LPB;
-    constexpr int QB = QTraits<QT>::QB;
+    constexpr int CPL = C::CPL, LPB = C::LPB, U = C::U;
     constexpr int NPAIR = CPL / 2;
-    constexpr int NLOAD = (QT == AT_GGML_Q8_0 && CPL == 32) ? 2 : 1;
 
     extern __shared__ __align__(16) float xs[];  // [B][e_per_split]
     __shared__ float red[8][B][32];
@@ -334,85 +595,111 @@ __global__ void __launch_bounds__(THREADS) gemv_t_kernel(const TParams p) {
     __shared__ float s_inv[B];
     __shared__ int s_last;
 
+    pdl_trigger();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = blockIdx.x / p.S, s = blockIdx.x - (blockIdx.x / p.S) * p.S;
     const int e_lo = s * p.e_per_split;
     const int e_hi = min(p.E, e_lo + p.e_per_split);
     const int ne = e_hi - e_lo;
+    const int quarter = (LPB == 1) ? 0 : (lane & (LPB - 1));
+    const int row_in_warp = lane / LPB;
+    const uint8_t* col = p.tiles + (size_t)c * p.ngroups * p.tile_bytes;
+
+    // first U steps of weights before waiting on earlier kernels
+    uint4 q[U][2];
+    float dsc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const int i = u * C::STEP + warp * C::ROWS_PER_WARP + row_in_warp;
+        if (i < ne) t_load<QT, CPL>(q[u], dsc[u], col, p.tile_bytes, e_lo + i, quarter);
+    }
+    pdl_wait();
 
     if constexpr (PRO == Pro::AddNorm) {
         block_rms_inv<B>(p.a.xin, p.a.yin, p.a.x_stride, p.E, p.a.eps, s_red, s_inv);
-        if (blockIdx.x == 0) {
-            for (int idx = tid; idx < B * p.E; idx += THREADS) {
-                const int bb = idx / p.E, i = idx - bb * p.E;
-                float t = p.a.xin[(size_t)bb * p.a.x_stride + i];
-                if (p.a.yin) t = __fadd_rn(t, p.a.yin[(size_t)bb * p.a.x_stride + i]);
-                p.a.xout[(size_t)bb * p.a.x_stride + i] = norm_apply(t, s_inv[bb], p.a.gamma[i]);
+        if (blockIdx.x == 0) write_xout<B>(p.a, p.E, s_inv);
+    }
+    if ((p.a.x_stride & 3) != 0 || (ne & 3) != 0) {
+        // rows not 16-byte aligned: scalar staging
+        for (int idx = tid; idx < B * ne; idx += THREADS) {
+            const int bb = idx / ne, i = idx - bb * ne;
+            const size_t off = (size_t)bb * p.a.x_stride + e_lo + i;
+            float v;
+            if constexpr (PRO == Pro::Plain) {
+                v = p.a.x[off];
+            } else {
+                float t = p.a.xin[off];
+                if (p.a.yin) t = __fadd_rn(t, p.a.yin[off]);
+                v = norm_apply(t, s_inv[bb], p.a.gamma[e_lo + i]);
+            }
+            xs[bb * p.e_per_split + i] = v;
+        }
+    } else {
+        // x slice [e_lo, e_hi) of each of the B rows, float4 (e_lo is a multiple of 64)
+        const int n4 = ne >> 2;
+        for (int base = 0; base < B * n4; base += THREADS * 4) {
+            float4 v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int idx = base + k * THREADS + tid;
+                if (idx < B * n4) {
+                    const int bb = idx / n4, i4 = idx - bb * n4;
+                    const size_t off = (size_t)bb * p.a.x_stride + e_lo + 4 * i4;
+                    if constexpr (PRO == Pro::Plain) {
+                        v[k] = *reinterpret_cast<const float4*>(p.a.x + off);
+                    } else {
+                        float4 t = *reinterpret_cast<const float4*>(p.a.xin + off);
+                        if (p.a.yin) {
+                            const float4 u = *reinterpret_cast<const float4*>(p.a.yin + off);
+                            t.x = __fadd_rn(t.x, u.x); t.y = __fadd_rn(t.y, u.y);
+                            t.z = __fadd_rn(t.z, u.z); t.w = __fadd_rn(t.w, u.w);
+                        }
+                        v[k] = t;
+                    }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int idx = base + k * THREADS + tid;
+                if (idx < B * n4) {
+                    const int bb = idx / n4, i4 = idx - bb * n4;
+                    float4 o = v[k];
+                    if constexpr (PRO == Pro::AddNorm) {
+                        const float4 g = *reinterpret_cast<const float4*>(p.a.gamma + e_lo + 4 * i4);
+                        const float inv = s_inv[bb];
+                        o = make_float4(norm_apply(o.x, inv, g.x), norm_apply(o.y, inv, g.y),
+                                        norm_apply(o.z, inv, g.z), norm_apply(o.w, inv, g.w));
+                    }
+                    *reinterpret_cast<float4*>(xs + bb * p.e_per_split + 4 * i4) = o;
+                }
             }
         }
     }
-    for (int idx = tid; idx < B * ne; idx += THREADS) {
-        const int bb = idx / ne, i = idx - bb * ne;
-        const int e = e_lo + i;
-        float v;
-        if constexpr (PRO == Pro::Plain) {
-            v = p.a.x[(size_t)bb * p.a.x_stride + e];
-        } else {
-            float t = p.a.xin[(size_t)bb * p.a.x_stride + e];
-            if (p.a.yin) t = __fadd_rn(t, p.a.yin[(size_t)bb * p.a.x_stride + e]);
-            v = norm_apply(t, s_inv[bb], p.a.gamma[e]);
-        }
-        xs[bb * p.e_per_split + i] = v;
-    }
     __syncthreads();
 
-    const int quarter = (LPB == 1) ? 0 : (lane & (LPB - 1));
-    const int row_in_warp = lane / LPB;
     float2 acc[B][NPAIR];
 #pragma unroll
     for (int b = 0; b < B; ++b)
 #pragma unroll
         for (int k = 0; k < NPAIR; ++k) acc[b][k] = f2(0.f, 0.f);
 
-    const uint8_t* colq = p.qs + (size_t)c * p.E * QB;
-    const uint16_t* cold = p.d + (size_t)c * p.E;
-    constexpr int U = 4;  // rows in flight per lane
     for (int base = 0; base < ne; base += C::STEP * U) {
-        uint4 q[U][2];
-        float dsc[U];
-        int iu[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int i = base + u * C::STEP + warp * C::ROWS_PER_WARP + row_in_warp;
-            iu[u] = i;
             if (i < ne) {
-                const int e = e_lo + i;
-                if constexpr (CPL == 32) {
-#pragma unroll
-                    for (int v = 0; v < NLOAD; ++v) q[u][v] = ld_stream_u4(colq + (size_t)e * QB + 16 * v);
-                } else {
-                    // a quarter block: 4 (Q4_0) or 8 (Q8_0) bytes, taken from the
-                    // 16-byte vector that holds them (selected in decode_t)
-                    q[u][0] = ld_stream_u4(colq + (size_t)e * QB + (QT == AT_GGML_Q8_0 ? 16 * (quarter >> 1) : 0));
-                    q[u][1] = q[u][0];
-                }
-                dsc[u] = fp16_ftz(ld_stream_u16(cold + e));
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            if (iu[u] < ne) {
                 float2 wv[NPAIR];
-                if constexpr (QT == AT_GGML_Q8_0 && CPL == 8) decode_t<QT, CPL>(q[u], quarter & 1, wv);
-                else decode_t<QT, CPL>(q[u], quarter, wv);
+                t_decode<QT, CPL>(q[u], quarter, wv);
 #pragma unroll
                 for (int b = 0; b < B; ++b) {
-                    const float sv = __fmul_rn(dsc[u], xs[b * p.e_per_split + iu[u]]);
+                    const float sv = __fmul_rn(dsc[u], xs[b * p.e_per_split + i]);
                     const float2 s2 = f2(sv, sv);
 #pragma unroll
                     for (int k = 0; k < NPAIR; ++k) acc[b][k] = __ffma2_rn(wv[k], s2, acc[b][k]);
                 }
             }
+            const int in = i + C::STEP * U;
+            if (in < ne) t_load<QT, CPL>(q[u], dsc[u], col, p.tile_bytes, e_lo + in, quarter);
         }
     }
 
@@ -422,8 +709,8 @@ __global__ void __launch_bounds__(THREADS) gemv_t_kernel(const TParams p) {
         float v[CPL];
 #pragma unroll
         for (int k = 0; k < NPAIR; ++k) {
-            v[col_of_pair<QT>(k, 0)] = acc[b][k].x;
-            v[col_of_pair<QT>(k, 1)] = acc[b][k].y;
+            v[2 * k] = acc[b][k].x;
+            v[2 * k + 1] = acc[b][k].y;
         }
         int n = CPL;
 #pragma unroll
@@ -439,21 +726,21 @@ __global__ void __launch_bounds__(THREADS) gemv_t_kernel(const TParams p) {
                 }
             }
         }
-        // v[0] is column: CPL==32 -> lane; CPL==8 -> 8*quarter + (lane >> 2)
-        const int col = (CPL == 32) ? lane : (8 * quarter + (lane >> 2));
-        red[warp][b][col] = v[0];
+        // v[0] is column: CPL == 32 -> lane; CPL == 8 -> 8 * quarter + (lane >> 2)
+        const int colx = (CPL == 32) ? lane : (8 * quarter + (lane >> 2));
+        red[warp][b][colx] = v[0];
     }
     __syncthreads();
 
     // CTA partial for (block column c, rows [e_lo, e_hi)): thread (b = warp, col = lane)
     float val = 0.f;
-    const int b_me = warp, col = lane;
+    const int b_me = warp, cl = lane;
     if (b_me < B) {
 #pragma unroll
-        for (int w = 0; w < 8; ++w) val += red[w][b_me][col];
+        for (int w = 0; w < 8; ++w) val += red[w][b_me][cl];
     }
     if (p.S > 1) {
-        if (b_me < B) p.a.scratch[(((size_t)c * p.S + s) * B + b_me) * 32 + col] = val;
+        if (b_me < B) p.a.scratch[(((size_t)c * p.S + s) * B + b_me) * 32 + cl] = val;
         __threadfence();
         __syncthreads();
         if (tid == 0) {
@@ -466,13 +753,13 @@ __global__ void __launch_bounds__(THREADS) gemv_t_kernel(const TParams p) {
         if (b_me < B) {
             val = 0.f;
             for (int k = 0; k < p.S; ++k)
-                val += __ldcg(&p.a.scratch[(((size_t)c * p.S + k) * B + b_me) * 32 + col]);
+                val += __ldcg(&p.a.scratch[(((size_t)c * p.S + k) * B + b_me) * 32 + cl]);
         }
         if (tid == 0) p.a.counters[c] = 0u;
     }
     if (b_me >= B) return;
 
-    const int j = c * 32 + col;  // output column
+    const int j = c * 32 + cl;  // output column
     if constexpr (EPI == Epi::Plain) {
         p.a.y[(size_t)b_me * p.a.y_stride + j] = val;
     } else {
@@ -508,6 +795,7 @@ __global__ void __launch_bounds__(THREADS) gemv_t_kernel(const TParams p) {
 // ---------------------------------------------------------------------------
 std::mutex g_attr_mu;
 std::map<const void*, int> g_smem_set;  // kernel -> dynamic smem attribute already set
+std::map<std::pair<const void*, int>, int> g_occ;
 
 void ensure_smem(const void* fn, int smem) {
     std::lock_guard<std::mutex> lk(g_attr_mu);
@@ -518,28 +806,101 @@ void ensure_smem(const void* fn, int smem) {
 }
 
 int occupancy(const void* fn, int smem) {
+    {
+        std::lock_guard<std::mutex> lk(g_attr_mu);
+        auto it = g_occ.find({fn, smem});
+        if (it != g_occ.end()) return it->second;
+    }
     int n = 0;
     AT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, THREADS, smem));
-    return n < 1 ? 1 : n;
+    n = n < 1 ? 1 : n;
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    g_occ[{fn, smem}] = n;
+    return n;
 }
 
-constexpr int kMaxXSmem = 96 * 1024;
+template <class P>
+void launch(const void* fn, int grid, int smem, cudaStream_t s, bool pdl, const P& params, int threads = THREADS) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    void* args[] = {const_cast<P*>(&params)};
+    AT_CUDA(cudaLaunchKernelExC(&cfg, fn, args));
+}
 
-template <int QT, int B, Pro PRO, Epi EPI>
-void run_n(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s) {
+// Chooses how many warps split the steps of a 4-row group (KS), and how many
+// rounds of groups each CTA (one per SM) walks, minimising the steps per warp.
+void n4_config(int ngroups, int nsteps, int num_sms, int* KS, int* gpc, int* per, int* grid, int* steps_ks) {
+    int best = -1;
+    for (int ks = 1; ks <= N4_WARPS; ks *= 2) {
+        if (ks > 1 && ks > nsteps) break;
+        const int g = N4_WARPS / ks;
+        const int ctas = (ngroups + g - 1) / g;
+        const int pr = (ctas + num_sms - 1) / num_sms;
+        const int sk = (nsteps + ks - 1) / ks;
+        const int cost = pr * sk;
+        if (best < 0 || cost < best) {
+            best = cost;
+            *KS = ks;
+            *gpc = g;
+            *per = pr;
+            *grid = (ngroups + g * pr - 1) / (g * pr);
+            *steps_ks = sk;
+        }
+    }
+}
+
+template <int QT, int B, Pro PRO, Epi EPI, int NST>
+void run_n4(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, bool pdl, int xbytes) {
     constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
-    constexpr int R = (NM == 2) ? 2 : 4;
-    NParams p{};
-    p.qs[0] = m->qs; p.d[0] = m->d;
-    if constexpr (NM == 2) { p.qs[1] = a.m2->qs; p.d[1] = a.m2->d; }
-    else { p.qs[1] = m->qs; p.d[1] = m->d; }
+    N4Params p{};
+    p.tiles[0] = m->tiles;
+    p.tiles[1] = (NM == 2) ? a.m2->tiles : m->tiles;
     p.rows = (int)m->rows;
     p.nb = (int)(m->cols / QK);
-    p.chunk_blocks = std::min(p.nb, std::max(32, kMaxXSmem / (B * XPAD * 4)));
+    p.ngroups = (int)m->ngroups;
+    p.nsteps = (int)m->nsteps;
+    p.ring_off = xbytes;
+    p.a = a;
+    int grid = 1;
+    n4_config(p.ngroups, p.nsteps, num_sms, &p.KS, &p.gpc, &p.per, &grid, &p.steps_ks);
+    const int smem = xbytes + N4_WARPS * NST * NM * NTile<QT>::BYTES;
+    const void* fn = reinterpret_cast<const void*>(&gemv_n4_kernel<QT, B, PRO, EPI, NST>);
+    ensure_smem(fn, smem);
+    launch(fn, grid, smem, s, pdl, p, N4_THREADS);
+}
+
+template <int QT, int B, Pro PRO, Epi EPI>
+void run_n(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, bool pdl) {
+    constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
+    const int nb = (int)(m->cols / QK);
+    const int xbytes = B * nb * XPAD * 4;
+    const int slot = NM * NTile<QT>::BYTES;
+    constexpr int kBudget = 200 * 1024;
+    if constexpr (B <= 2) {
+        // deepest ring (4 or 2 steps per warp) that fits next to the staged x
+        if (xbytes + N4_WARPS * 4 * slot <= kBudget) { run_n4<QT, B, PRO, EPI, 4>(m, a, num_sms, s, pdl, xbytes); return; }
+        if (xbytes + N4_WARPS * 2 * slot <= kBudget) { run_n4<QT, B, PRO, EPI, 2>(m, a, num_sms, s, pdl, xbytes); return; }
+    }
+    constexpr int R = (NM == 2) ? 2 : 4;
+    NCParams p{};
+    p.tiles[0] = m->tiles;
+    p.tiles[1] = (NM == 2) ? a.m2->tiles : m->tiles;
+    p.map = tile_map(m);
+    p.rows = (int)m->rows;
+    p.nb = nb;
+    p.chunk_blocks = std::min(p.nb, std::max(32, kMaxXSmemChunk / (B * XPAD * 4)));
     p.nchunks = (p.nb + p.chunk_blocks - 1) / p.chunk_blocks;
     p.a = a;
     const int smem = B * p.chunk_blocks * XPAD * 4;
-    const void* fn = reinterpret_cast<const void*>(&gemv_n_kernel<QT, B, PRO, EPI>);
+    const void* fn = reinterpret_cast<const void*>(&gemv_nc_kernel<QT, B, PRO, EPI>);
     ensure_smem(fn, smem);
     const int occ = occupancy(fn, smem);
     int wk = 1;
@@ -548,30 +909,32 @@ void run_n(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s) {
     p.wk = wk;
     p.n_tiles = tiles(wk);
     const int grid = std::max(1, std::min(p.n_tiles, num_sms * occ));
-    gemv_n_kernel<QT, B, PRO, EPI><<<grid, THREADS, smem, s>>>(p);
-    AT_CUDA(cudaGetLastError());
+    launch(fn, grid, smem, s, pdl, p);
 }
 
 void t_config(const at_qmat* m, int batch, int num_sms, int* S, int* eps_rows) {
     const int step = (batch <= 2) ? 256 : 64;
     const int E = (int)m->rows;
     const int n_bc = (int)(m->cols / QK);
-    int s = std::max(1, (2 * num_sms + n_bc - 1) / n_bc);
-    s = std::min(s, std::max(1, E / (2 * step)));
+    // enough CTAs for every SM, each with at least 4 steps of rows per warp
+    int s = std::max(1, (5 * num_sms / 4 + n_bc - 1) / n_bc);
+    s = std::min(s, std::max(1, E / (4 * step)));
     int per = (E + s - 1) / s;
     per = ((per + step - 1) / step) * step;
     // the staged x slice must fit the shared-memory budget
-    const int cap = std::max(step, (kMaxXSmem / (4 * batch)) / step * step);
+    const int cap = std::max(step, (kMaxXSmemChunk / (4 * batch)) / step * step);
     per = std::min(per, cap);
     *eps_rows = per;
     *S = (E + per - 1) / per;
 }
 
 template <int QT, int B, Pro PRO, Epi EPI>
-void run_t(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s) {
+void run_t(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, bool pdl) {
     TParams p{};
-    p.qs = m->qs; p.d = m->d;
+    p.tiles = m->tiles;
+    p.tile_bytes = m->tile_bytes;
     p.E = (int)m->rows;
+    p.ngroups = (int)m->ngroups;
     p.n_bc = (int)(m->cols / QK);
     t_config(m, B, num_sms, &p.S, &p.e_per_split);
     p.a = a;
@@ -579,16 +942,15 @@ void run_t(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s) {
     const int smem = B * p.e_per_split * 4;
     const void* fn = reinterpret_cast<const void*>(&gemv_t_kernel<QT, B, PRO, EPI>);
     ensure_smem(fn, smem);
-    gemv_t_kernel<QT, B, PRO, EPI><<<p.n_bc * p.S, THREADS, smem, s>>>(p);
-    AT_CUDA(cudaGetLastError());
+    launch(fn, p.n_bc * p.S, smem, s, pdl, p);
 }
 
 template <int QT, Pro PRO, Epi EPI, bool IS_T>
-void dispatch_b(const at_qmat* m, int batch, const GemvArgs& a, int num_sms, cudaStream_t s) {
-#define AT_CASE(BB)                                                      \
-    case BB:                                                             \
-        if constexpr (IS_T) run_t<QT, BB, PRO, EPI>(m, a, num_sms, s);   \
-        else run_n<QT, BB, PRO, EPI>(m, a, num_sms, s);                  \
+void dispatch_b(const at_qmat* m, int batch, const GemvArgs& a, int num_sms, cudaStream_t s, bool pdl) {
+#define AT_CASE(BB)                                                           \
+    case BB:                                                                  \
+        if constexpr (IS_T) run_t<QT, BB, PRO, EPI>(m, a, num_sms, s, pdl);   \
+        else run_n<QT, BB, PRO, EPI>(m, a, num_sms, s, pdl);                  \
         break;
     switch (batch) {
         AT_CASE(1) AT_CASE(2) AT_CASE(3) AT_CASE(4) AT_CASE(5) AT_CASE(6) AT_CASE(7) AT_CASE(8)
@@ -598,9 +960,9 @@ void dispatch_b(const at_qmat* m, int batch, const GemvArgs& a, int num_sms, cud
 }
 
 template <Pro PRO, Epi EPI, bool IS_T>
-void dispatch_q(const at_qmat* m, int batch, const GemvArgs& a, int num_sms, cudaStream_t s) {
-    if (m->type == AT_GGML_Q4_0) dispatch_b<AT_GGML_Q4_0, PRO, EPI, IS_T>(m, batch, a, num_sms, s);
-    else if (m->type == AT_GGML_Q8_0) dispatch_b<AT_GGML_Q8_0, PRO, EPI, IS_T>(m, batch, a, num_sms, s);
+void dispatch_q(const at_qmat* m, int batch, const GemvArgs& a, int num_sms, cudaStream_t s, bool pdl) {
+    if (m->type == AT_GGML_Q4_0) dispatch_b<AT_GGML_Q4_0, PRO, EPI, IS_T>(m, batch, a, num_sms, s, pdl);
+    else if (m->type == AT_GGML_Q8_0) dispatch_b<AT_GGML_Q8_0, PRO, EPI, IS_T>(m, batch, a, num_sms, s, pdl);
     else fail(AT_ERR_UNSUPPORTED, "fused GEMV supports Q4_0 and Q8_0");
 }
 
@@ -615,22 +977,24 @@ void gemv_t_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* float
 }
 
 void launch_gemv_n(const at_qmat* m, int batch, Pro pro, Epi epi, const GemvArgs& a, int num_sms,
-                   cudaStream_t s) {
+                   cudaStream_t s, bool pdl) {
     AT_REQUIRE(m->cols % QK == 0, AT_ERR_INVALID_ARG, "cols must be a multiple of 32");
-    if (pro == Pro::Plain && epi == Epi::Plain) dispatch_q<Pro::Plain, Epi::Plain, false>(m, batch, a, num_sms, s);
-    else if (pro == Pro::AddNorm && epi == Epi::Plain) dispatch_q<Pro::AddNorm, Epi::Plain, false>(m, batch, a, num_sms, s);
+    AT_REQUIRE(m->orient == AT_ORIENT_N, AT_ERR_INVALID_ARG, "matrix is not stored for orientation N");
+    if (pro == Pro::Plain && epi == Epi::Plain) dispatch_q<Pro::Plain, Epi::Plain, false>(m, batch, a, num_sms, s, pdl);
+    else if (pro == Pro::AddNorm && epi == Epi::Plain) dispatch_q<Pro::AddNorm, Epi::Plain, false>(m, batch, a, num_sms, s, pdl);
     else if (pro == Pro::AddNorm && epi == Epi::SiluMul) {
         AT_REQUIRE(a.m2 && a.m2->type == m->type && a.m2->rows == m->rows && a.m2->cols == m->cols,
                    AT_ERR_INVALID_ARG, "gate/up matrices must match");
-        dispatch_q<Pro::AddNorm, Epi::SiluMul, false>(m, batch, a, num_sms, s);
+        dispatch_q<Pro::AddNorm, Epi::SiluMul, false>(m, batch, a, num_sms, s, pdl);
     } else fail(AT_ERR_UNSUPPORTED, "unsupported N prologue/epilogue combination");
 }
 
 void launch_gemv_t(const at_qmat* m, int batch, Pro pro, Epi epi, const GemvArgs& a, int num_sms,
-                   cudaStream_t s) {
+                   cudaStream_t s, bool pdl) {
     AT_REQUIRE(m->cols % QK == 0, AT_ERR_INVALID_ARG, "cols must be a multiple of 32");
-    if (pro == Pro::Plain && epi == Epi::Plain) dispatch_q<Pro::Plain, Epi::Plain, true>(m, batch, a, num_sms, s);
-    else if (pro == Pro::AddNorm && epi == Epi::QkvRope) dispatch_q<Pro::AddNorm, Epi::QkvRope, true>(m, batch, a, num_sms, s);
+    AT_REQUIRE(m->orient == AT_ORIENT_T, AT_ERR_INVALID_ARG, "matrix is not stored for orientation T");
+    if (pro == Pro::Plain && epi == Epi::Plain) dispatch_q<Pro::Plain, Epi::Plain, true>(m, batch, a, num_sms, s, pdl);
+    else if (pro == Pro::AddNorm && epi == Epi::QkvRope) dispatch_q<Pro::AddNorm, Epi::QkvRope, true>(m, batch, a, num_sms, s, pdl);
     else fail(AT_ERR_UNSUPPORTED, "unsupported T prologue/epilogue combination");
 }
 

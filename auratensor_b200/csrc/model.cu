@@ -74,7 +74,7 @@ void nccl_check(ncclResult_t r, const char* what) {
 
 namespace {
 
-constexpr int CH = 64;  // KV positions per attention CTA
+constexpr int CH = 32;  // KV positions per attention CTA
 
 // ---------------------------------------------------------------------------
 // Step kernels
@@ -82,23 +82,24 @@ constexpr int CH = 64;  // KV positions per attention CTA
 // writeTokenEmbedding (inference/LlamaModel.java:181-186): one dequantized row
 // of token_embd into xa; y <- 0 so the first layer's prologue reads x + 0.
 template <int QT>
-__global__ void embed_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ dsc,
-                             const int* __restrict__ tokens, int d, float* __restrict__ xa, float* __restrict__ y) {
-    constexpr int QB = (QT == AT_GGML_Q4_0) ? 16 : 32;
+__global__ void embed_kernel(const uint8_t* __restrict__ tiles, QTileMap map, const int* __restrict__ tokens, int d,
+                             float* __restrict__ xa, float* __restrict__ y, unsigned long long* __restrict__ argkeys) {
     const int b = blockIdx.x;
+    if (threadIdx.x == 0) argkeys[b] = 0ull;
     const int64_t tok = tokens[b];
-    const int nb = d / 32;
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        const int64_t blk = tok * nb + (i >> 5);
+        int64_t d_off, q_off;
+        map.offsets(tok, i >> 5, &d_off, &q_off);
         const int w = i & 31;
         int q;
         if constexpr (QT == AT_GGML_Q4_0) {
-            const uint32_t pack = qs[blk * QB + (w >> 1)];
+            const uint32_t pack = tiles[q_off + (w >> 1)];
             q = ((w & 1) ? (int)(pack >> 4) : (int)(pack & 0xF)) - 8;
         } else {
-            q = (int)(int8_t)qs[blk * QB + w];
+            q = (int)(int8_t)tiles[q_off + w];
         }
-        xa[(size_t)b * d + i] = __fmul_rn((float)q, fp16_ftz(dsc[blk]));
+        const uint32_t h = (uint32_t)tiles[d_off] | ((uint32_t)tiles[d_off + 1] << 8);
+        xa[(size_t)b * d + i] = __fmul_rn((float)q, fp16_ftz(h));
         y[(size_t)b * d + i] = 0.f;
     }
 }
@@ -106,8 +107,10 @@ __global__ void embed_kernel(const uint8_t* __restrict__ qs, const uint16_t* __r
 __device__ __forceinline__ float exp_ref(float v) { return (float)exp((double)v); }
 
 // LlamaModel.attention (inference/LlamaModel.java:255-297) split over KV
-// chunks: for the G query heads sharing KV head `kvh`, scores over positions
-// [p0, p1) = (K q) * scale, chunk max m, l = sum exp(s - m), o = sum exp(s - m) V.
+// chunks of CH positions: for the G query heads sharing KV head `kvh`, scores
+// over positions [p0, p0 + n) = (K q) * scale, chunk max m, l = sum exp(s - m),
+// o = sum exp(s - m) V. K and V of the chunk are staged in shared memory with
+// all of the CTA's 128-bit loads in flight at once.
 template <int HD>
 __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict__ q, const float* __restrict__ kc,
                                                          const float* __restrict__ vc,
@@ -115,7 +118,10 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
                                                          int Hl, int Hkvl, int ctx, int64_t slot_stride,
                                                          int nchunk_max, float scale) {
     constexpr int G_MAX = 8;
-    __shared__ __align__(16) float qs[G_MAX][HD];
+    constexpr int F4 = HD / 4;  // float4 per row
+    __shared__ __align__(16) float4 ks[CH][F4];
+    __shared__ __align__(16) float4 vs[CH][F4];
+    __shared__ __align__(16) float4 qs[G_MAX][F4];
     __shared__ float sc[G_MAX][CH];
     __shared__ float s_m[G_MAX], s_l[G_MAX];
     const int kvh = blockIdx.x, chunk = blockIdx.y, b = blockIdx.z;
@@ -125,22 +131,34 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
     if (p0 >= P) return;
     const int n = (int)((P - p0) < CH ? (P - p0) : CH);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const float* kbase = kc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD;
-    const float* vbase = vc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD;
-    for (int i = tid; i < G * HD; i += 256) {
-        const int g = i / HD, dd = i - g * HD;
-        qs[g][dd] = q[(size_t)b * Hl * HD + (size_t)(kvh * G + g) * HD + dd];
+    const float4* kbase = reinterpret_cast<const float4*>(kc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD);
+    const float4* vbase = reinterpret_cast<const float4*>(vc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD);
+    const float4* qbase = reinterpret_cast<const float4*>(q + (size_t)b * Hl * HD + (size_t)kvh * G * HD);
+    constexpr int PER = (CH * F4 + 255) / 256;
+    float4 kr[PER], vr[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int i = k * 256 + tid;
+        if (i < n * F4) { kr[k] = kbase[i]; vr[k] = vbase[i]; }
+    }
+    for (int i = tid; i < G * F4; i += 256) qs[i / F4][i % F4] = qbase[i];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int i = k * 256 + tid;
+        if (i < n * F4) { ks[i / F4][i % F4] = kr[k]; vs[i / F4][i % F4] = vr[k]; }
     }
     __syncthreads();
-    constexpr int PER = HD / 32;
+    // scores: warp w takes positions w, w + 8, ...; lanes split head_dim
     for (int i = warp; i < n; i += 8) {
-        float kr[PER];
-#pragma unroll
-        for (int t = 0; t < PER; ++t) kr[t] = kbase[(size_t)i * HD + lane * PER + t];
         for (int g = 0; g < G; ++g) {
             float acc = 0.f;
-#pragma unroll
-            for (int t = 0; t < PER; ++t) acc = fmaf(kr[t], qs[g][lane * PER + t], acc);
+            for (int f = lane; f < F4; f += 32) {
+                const float4 kv = ks[i][f], qv = qs[g][f];
+                acc = fmaf(kv.x, qv.x, acc);
+                acc = fmaf(kv.y, qv.y, acc);
+                acc = fmaf(kv.z, qv.z, acc);
+                acc = fmaf(kv.w, qv.w, acc);
+            }
             acc = warp_sum(acc);
             if (lane == 0) sc[g][i] = __fmul_rn(acc, scale);
         }
@@ -161,10 +179,11 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
         if (lane == 0) { s_m[g] = m; s_l[g] = l; }
     }
     __syncthreads();
+    const float* vsf = reinterpret_cast<const float*>(vs);
     for (int o = tid; o < G * HD; o += 256) {
         const int g = o / HD, dd = o - g * HD;
         float acc = 0.f;
-        for (int i = 0; i < n; ++i) acc = fmaf(sc[g][i], vbase[(size_t)i * HD + dd], acc);
+        for (int i = 0; i < n; ++i) acc = fmaf(sc[g][i], vsf[i * HD + dd], acc);
         const int h = kvh * G + g;
         float* dst = part + (((size_t)b * Hl + h) * nchunk_max + chunk) * (HD + 2);
         dst[dd] = acc;
@@ -173,53 +192,106 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
 }
 
 // Merges the chunk partials of one (sequence, head): out = sum_c o_c e^(m_c-M) / sum_c l_c e^(m_c-M).
+// All chunk statistics are loaded at once (one round of loads, not one per chunk).
 template <int HD>
-__global__ void attn_combine_kernel(const float* __restrict__ part, const int64_t* __restrict__ pos,
-                                    float* __restrict__ att, int Hl, int nchunk_max) {
-    const int h = blockIdx.x, b = blockIdx.y, dd = threadIdx.x;
+__global__ void __launch_bounds__(HD) attn_combine_kernel(const float* __restrict__ part,
+                                                          const int64_t* __restrict__ pos, float* __restrict__ att,
+                                                          int Hl, int nchunk_max) {
+    constexpr int MAXC = 1024;  // chunks per head handled (context <= 32768 positions)
+    __shared__ float sw[MAXC];
+    __shared__ float sred[HD / 32];
+    __shared__ float s_M, s_L;
+    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t P = pos[b] + 1;
     const int nch = (int)((P + CH - 1) / CH);
     const float* base = part + ((size_t)b * Hl + h) * nchunk_max * (HD + 2);
-    float M = -INFINITY;
-    for (int c = 0; c < nch; ++c) M = fmaxf(M, base[(size_t)c * (HD + 2) + HD]);
-    float L = 0.f, o = 0.f;
-    for (int c = 0; c < nch; ++c) {
-        const float* pc = base + (size_t)c * (HD + 2);
-        const float w = exp_ref(__fsub_rn(pc[HD], M));
-        L = fmaf(pc[HD + 1], w, L);
-        o = fmaf(pc[dd], w, o);
+    float m = -INFINITY;
+    for (int c = tid; c < nch; c += HD) {
+        const float mc = base[(size_t)c * (HD + 2) + HD];
+        sw[c] = mc;
+        m = fmaxf(m, mc);
     }
-    att[(size_t)b * Hl * HD + (size_t)h * HD + dd] = __fdiv_rn(o, L);
+    m = warp_max(m);
+    if (lane == 0) sred[warp] = m;
+    __syncthreads();
+    if (tid == 0) {
+        float t = sred[0];
+        for (int w = 1; w < HD / 32; ++w) t = fmaxf(t, sred[w]);
+        s_M = t;
+    }
+    __syncthreads();
+    const float M = s_M;
+    float l = 0.f;
+    for (int c = tid; c < nch; c += HD) {
+        const float w = exp_ref(__fsub_rn(sw[c], M));
+        sw[c] = w;
+        l = fmaf(base[(size_t)c * (HD + 2) + HD + 1], w, l);
+    }
+    l = warp_sum(l);
+    __syncthreads();
+    if (lane == 0) sred[warp] = l;
+    __syncthreads();
+    if (tid == 0) {
+        float t = 0.f;
+        for (int w = 0; w < HD / 32; ++w) t += sred[w];
+        s_L = t;
+    }
+    __syncthreads();
+    float o = 0.f;
+    int c = 0;
+    for (; c + 8 <= nch; c += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = base[(size_t)(c + k) * (HD + 2) + tid];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) o = fmaf(v[k], sw[c + k], o);
+    }
+    for (; c < nch; ++c) o = fmaf(base[(size_t)c * (HD + 2) + tid], sw[c], o);
+    att[(size_t)b * Hl * HD + (size_t)h * HD + tid] = __fdiv_rn(o, s_L);
 }
 
-// Greedy fast path of Sampler.sample (inference/Sampler.java:56-67): first
-// index of the maximum; a NaN never wins unless it is element 0.
-__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V, int stride,
-                                                      int* __restrict__ out) {
-    __shared__ float sv[32];
-    __shared__ int si[32];
-    const float* row = logits + (size_t)blockIdx.x * stride;
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        float v = row[i];
-        if (v != v) v = -INFINITY;
-        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+// Greedy fast path of Sampler.sample (inference/Sampler.java:56-67): the
+// first index of the maximum; a NaN never wins unless it is element 0 (then
+// the reference returns 0). Every CTA reduces a slice and folds
+// (order-preserving bits of the value, ~index) into a 64-bit key with
+// atomicMax, so the result does not depend on CTA order. Keys are zeroed by
+// the embedding kernel at the start of the step.
+__device__ __forceinline__ uint32_t ordered_bits(float v) {
+    if (v != v) v = -INFINITY;
+    const uint32_t u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ logits, int V, int stride,
+                                                     unsigned long long* __restrict__ keys) {
+    __shared__ unsigned long long sk[8];
+    const int b = blockIdx.y;
+    const float* row = logits + (size_t)b * stride;
+    unsigned long long best = 0ull;
+    for (int i = blockIdx.x * 256 + threadIdx.x; i < V; i += gridDim.x * 256) {
+        const unsigned long long k = ((unsigned long long)ordered_bits(row[i]) << 32) | (0xFFFFFFFFu - (uint32_t)i);
+        best = k > best ? k : best;
     }
+    if (blockIdx.x == 0 && threadIdx.x == 0 && row[0] != row[0]) best = ~0ull;  // NaN at index 0 wins
     for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
     }
-    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+    if ((threadIdx.x & 31) == 0) sk[threadIdx.x >> 5] = best;
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
-            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
-        if (bv == -INFINITY && bi == 0x7fffffff) bi = 0;
-        if (row[0] != row[0]) bi = 0;
-        out[blockIdx.x] = bi;
+        for (int w = 1; w < 8; ++w) best = sk[w] > best ? sk[w] : best;
+        atomicMax(&keys[b], best);
     }
+}
+
+__device__ __forceinline__ int key_index(unsigned long long k) {
+    return (k == ~0ull) ? 0 : (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+}
+
+// Writes the argmax index of each of the B keys.
+__global__ void argmax_index_kernel(const unsigned long long* __restrict__ keys, int B, int* __restrict__ out) {
+    if (threadIdx.x < B) out[threadIdx.x] = key_index(keys[threadIdx.x]);
 }
 
 // All-gathered [rank][b][Vl] logits -> [b][V].
@@ -278,6 +350,7 @@ struct at_model {
     int* d_tokens = nullptr;
     int64_t* d_pos = nullptr;
     int* d_argmax = nullptr;
+    unsigned long long* d_argkey = nullptr;  // packed (value, index) max per row
     int* h_tokens = nullptr;      // pinned
     int64_t* h_pos = nullptr;     // pinned
     int nchunk_max = 0;
@@ -286,10 +359,12 @@ struct at_model {
     std::map<std::string, bool> seen;
     cudaGraphExec_t graph[9] = {};
     cudaGraphExec_t graph_gen = nullptr;  // step + greedy advance (slot 0)
+    cudaGraphExec_t graph_prof = nullptr; // step with an event pair around every launch
     int* d_gen_out = nullptr;             // [ctx] generated tokens
     int* d_gen_count = nullptr;
     // eager profiling: event pairs around each launch
     bool profiling = false;
+    bool pdl = true;                      // programmatic dependent launch between step kernels
     std::vector<cudaEvent_t> prof_ev;
     std::vector<int> prof_cls;
     size_t prof_used = 0;
@@ -304,15 +379,12 @@ void alloc_zero(void** p, size_t bytes) {
 }
 
 void make_qmat(at_qmat& m, int type, int orient, int64_t rows, int64_t cols) {
-    if (m.qs || m.f32) return;
+    if (m.tiles || m.f32) return;
     m.type = type;
     m.orient = orient;
     m.rows = rows;
     m.cols = cols;
-    qmat_alloc(&m);
-    const size_t nblk = (size_t)(rows * (cols / QK));
-    AT_CUDA(cudaMemset(m.qs, 0, nblk * quant_bytes(type)));
-    AT_CUDA(cudaMemset(m.d, 0, nblk * 2 + 16));
+    qmat_alloc(&m);  // zeroed: blocks never written stay zero (scale 0)
 }
 
 bool parse_layer(const std::string& name, int* layer, std::string* leaf) {
@@ -341,10 +413,10 @@ struct ProfScope {
         idx = m->prof_used;
         m->prof_used += 2;
         m->prof_cls.push_back(cls);
-        AT_CUDA(cudaEventRecord(m->prof_ev[idx], m->ctx->stream));
+        AT_CUDA(cudaEventRecordWithFlags(m->prof_ev[idx], m->ctx->stream, cudaEventRecordExternal));
     }
     ~ProfScope() {
-        if (m->profiling) cudaEventRecord(m->prof_ev[idx + 1], m->ctx->stream);
+        if (m->profiling) cudaEventRecordWithFlags(m->prof_ev[idx + 1], m->ctx->stream, cudaEventRecordExternal);
     }
 };
 
@@ -361,9 +433,11 @@ void enqueue_step(at_model* m, int B) {
     {
         ProfScope p(m, AT_PROF_EMBED);
         if (m->tok.type == AT_GGML_Q4_0)
-            embed_kernel<AT_GGML_Q4_0><<<B, 256, 0, s>>>(m->tok.qs, m->tok.d, m->d_tokens, d, m->xa, m->y);
+            embed_kernel<AT_GGML_Q4_0><<<B, 256, 0, s>>>(m->tok.tiles, tile_map(&m->tok), m->d_tokens, d, m->xa,
+                                                          m->y, m->d_argkey);
         else
-            embed_kernel<AT_GGML_Q8_0><<<B, 256, 0, s>>>(m->tok.qs, m->tok.d, m->d_tokens, d, m->xa, m->y);
+            embed_kernel<AT_GGML_Q8_0><<<B, 256, 0, s>>>(m->tok.tiles, tile_map(&m->tok), m->d_tokens, d, m->xa,
+                                                          m->y, m->d_argkey);
         AT_CUDA(cudaGetLastError());
     }
     const float scale = (float)(1.0 / std::sqrt((double)hd));
@@ -383,7 +457,7 @@ void enqueue_step(at_model* m, int B) {
             a.kv_slot_stride = m->slot_stride;
             a.head_dim = hd; a.n_q_cols = m->Hl * hd; a.n_kv_cols = m->Hkvl * hd; a.ctx_len = m->ctx_len;
             a.scratch = m->scratch; a.counters = m->counters;
-            launch_gemv_t(&ly.qkv, B, Pro::AddNorm, Epi::QkvRope, a, c->num_sms, s);
+            launch_gemv_t(&ly.qkv, B, Pro::AddNorm, Epi::QkvRope, a, c->num_sms, s, m->pdl);
         }
         {
             ProfScope p(m, AT_PROF_ATTN);
@@ -407,7 +481,7 @@ void enqueue_step(at_model* m, int B) {
             GemvArgs o;
             o.x = m->att; o.x_stride = m->Hl * hd; o.y = m->y; o.y_stride = d;
             o.scratch = m->scratch; o.counters = m->counters;
-            launch_gemv_t(&ly.wo, B, Pro::Plain, Epi::Plain, o, c->num_sms, s);
+            launch_gemv_t(&ly.wo, B, Pro::Plain, Epi::Plain, o, c->num_sms, s, m->pdl);
         }
         allreduce_y("ncclAllReduce(attention)");
         {
@@ -415,13 +489,13 @@ void enqueue_step(at_model* m, int B) {
             GemvArgs f;
             f.xin = m->xb; f.yin = m->y; f.gamma = ly.ffn_norm; f.xout = m->xa; f.eps = m->cfg.rms_norm_eps;
             f.x_stride = d; f.y = m->h; f.y_stride = m->Fl; f.m2 = &ly.w3;
-            launch_gemv_n(&ly.w1, B, Pro::AddNorm, Epi::SiluMul, f, c->num_sms, s);
+            launch_gemv_n(&ly.w1, B, Pro::AddNorm, Epi::SiluMul, f, c->num_sms, s, m->pdl);
         }
         {
             ProfScope p(m, AT_PROF_FFN_DOWN);
             GemvArgs dn;
             dn.x = m->h; dn.x_stride = m->Fl; dn.y = m->y; dn.y_stride = d;
-            launch_gemv_n(&ly.w2, B, Pro::Plain, Epi::Plain, dn, c->num_sms, s);
+            launch_gemv_n(&ly.w2, B, Pro::Plain, Epi::Plain, dn, c->num_sms, s, m->pdl);
         }
         allreduce_y("ncclAllReduce(mlp)");
     }
@@ -431,7 +505,7 @@ void enqueue_step(at_model* m, int B) {
         ha.xin = m->xa; ha.yin = m->y; ha.gamma = m->out_norm; ha.xout = m->xb;
         ha.eps = m->cfg.rms_norm_eps; ha.x_stride = d;
         ha.y = (c->world > 1) ? m->logits_local : m->logits; ha.y_stride = m->Vl;
-        launch_gemv_n(&m->out, B, Pro::AddNorm, Epi::Plain, ha, c->num_sms, s);
+        launch_gemv_n(&m->out, B, Pro::AddNorm, Epi::Plain, ha, c->num_sms, s, m->pdl);
     }
     if (c->world > 1) {
         ProfScope p(m, AT_PROF_COMM);
@@ -443,7 +517,9 @@ void enqueue_step(at_model* m, int B) {
     }
     {
         ProfScope p(m, AT_PROF_ARGMAX);
-        argmax_kernel<<<B, 1024, 0, s>>>(m->logits, m->V, m->V, m->d_argmax);
+        argmax_kernel<<<dim3(c->num_sms, B), 256, 0, s>>>(m->logits, m->V, m->V, m->d_argkey);
+        AT_CUDA(cudaGetLastError());
+        argmax_index_kernel<<<1, 32, 0, s>>>(m->d_argkey, B, m->d_argmax);
         AT_CUDA(cudaGetLastError());
     }
 }
@@ -507,6 +583,7 @@ void destroy_model(at_model* m) {
     for (auto& g : m->graph)
         if (g) cudaGraphExecDestroy(g);
     if (m->graph_gen) cudaGraphExecDestroy(m->graph_gen);
+    if (m->graph_prof) cudaGraphExecDestroy(m->graph_prof);
     for (cudaEvent_t e : m->prof_ev) cudaEventDestroy(e);
     for (auto& ly : m->layers) {
         qmat_free(&ly.qkv); qmat_free(&ly.wo); qmat_free(&ly.w1); qmat_free(&ly.w3); qmat_free(&ly.w2);
@@ -516,7 +593,7 @@ void destroy_model(at_model* m) {
     qmat_free(&m->out);
     void* bufs[] = {m->out_norm, m->xa, m->xb, m->y, m->q, m->att, m->h, m->logits, m->logits_local, m->gather,
                     m->att_part, m->kcache, m->vcache, m->rope_cos, m->rope_sin, m->scratch, m->counters,
-                    m->d_tokens, m->d_pos, m->d_argmax, m->d_gen_out, m->d_gen_count};
+                    m->d_tokens, m->d_pos, m->d_argmax, m->d_gen_out, m->d_gen_count, m->d_argkey};
     for (void* p : bufs)
         if (p) cudaFree(p);
     if (m->h_tokens) cudaFreeHost(m->h_tokens);
@@ -658,6 +735,7 @@ int at_model_create(at_ctx* ctx, const at_model_config* cfg, at_model** out) {
         m->ctx_len = (int)cfg->context_length;
         const int W = ctx->world;
         AT_REQUIRE(m->hd == 64 || m->hd == 128, AT_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+        AT_REQUIRE(cfg->context_length <= 32768, AT_ERR_UNSUPPORTED, "context_length above 32768");
         AT_REQUIRE(m->d % 32 == 0, AT_ERR_INVALID_ARG, "embedding_length must be a multiple of 32");
         AT_REQUIRE(m->H % m->Hkv == 0 && m->H / m->Hkv <= 8, AT_ERR_UNSUPPORTED, "query heads per KV head must be 1..8");
         AT_REQUIRE(m->Hkv % W == 0, AT_ERR_INVALID_ARG, "KV heads must divide evenly across tensor-parallel ranks");
@@ -841,6 +919,7 @@ int at_model_finalize(at_model* m) {
         alloc_zero((void**)&m->d_tokens, 8 * sizeof(int));
         alloc_zero((void**)&m->d_pos, 8 * sizeof(int64_t));
         alloc_zero((void**)&m->d_argmax, 8 * sizeof(int));
+        alloc_zero((void**)&m->d_argkey, 8 * sizeof(unsigned long long));
         alloc_zero((void**)&m->d_gen_out, (size_t)m->ctx_len * sizeof(int));
         alloc_zero((void**)&m->d_gen_count, sizeof(int));
         AT_CUDA(cudaMallocHost(&m->h_tokens, 8 * sizeof(int)));
@@ -1027,16 +1106,25 @@ int at_model_profile_step(at_model* m, int token, int64_t position, float* class
         m->h_pos[0] = position;
         AT_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tokens, sizeof(int), cudaMemcpyHostToDevice, c->stream));
         AT_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pos, sizeof(int64_t), cudaMemcpyHostToDevice, c->stream));
-        m->profiling = true;
-        m->prof_used = 0;
-        m->prof_cls.clear();
-        try {
-            enqueue_step(m, 1);
-        } catch (...) {
+        // The step is captured once into a graph with an event pair around
+        // every launch and no programmatic overlap, so each pair times one
+        // kernel on the device without host submission gaps.
+        if (!m->graph_prof) {
+            m->profiling = true;
+            m->pdl = false;
+            m->prof_used = 0;
+            m->prof_cls.clear();
+            try {
+                m->graph_prof = capture(m, enqueue_step, 1);
+            } catch (...) {
+                m->profiling = false;
+                m->pdl = true;
+                throw;
+            }
             m->profiling = false;
-            throw;
+            m->pdl = true;
         }
-        m->profiling = false;
+        AT_CUDA(cudaGraphLaunch(m->graph_prof, c->stream));
         AT_CUDA(cudaStreamSynchronize(c->stream));
         for (int k = 0; k < AT_PROF_CLASSES; ++k) { class_ms[k] = 0.f; class_launches[k] = 0; }
         for (size_t i = 0; i < m->prof_cls.size(); ++i) {

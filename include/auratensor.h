@@ -173,10 +173,10 @@ int at_model_argmax(at_model* m, int batch, int* tokens_host);
  * tokens_out_host receives the n_steps generated tokens; when it is NULL the
  * steps are only enqueued on the context's stream (the call does not wait). */
 int at_model_generate(at_model* m, int first_token, int64_t start_pos, int n_steps, int* tokens_out_host);
-/* Per-kernel-class device time of one eager (non-graph) forward step of slot 0,
- * each launch bracketed by CUDA events: class_ms[AT_PROF_CLASSES] milliseconds
- * and class_launches[AT_PROF_CLASSES] launch counts. New (the reference has
- * only wall-clock prints). */
+/* Per-kernel-class device time of one forward step of slot 0, run as a graph
+ * with a CUDA event pair around every launch (and no programmatic overlap):
+ * class_ms[AT_PROF_CLASSES] milliseconds and class_launches[AT_PROF_CLASSES]
+ * launch counts. New (the reference has only wall-clock prints). */
 #define AT_PROF_EMBED    0
 #define AT_PROF_QKV      1  /* QKV GEMV + RMSNorm + RoPE + KV append   */
 #define AT_PROF_ATTN     2  /* split-KV attention + combine            */
