@@ -33,6 +33,7 @@
 #include <algorithm>
 #include <map>
 #include <mutex>
+#include <string>
 
 #include "at_internal.h"
 #include "dev_common.cuh"
@@ -1022,4 +1023,70 @@ void launch_sgemv_f32(const float* A, const float* x, float* y, int M, int K, in
     AT_CUDA(cudaGetLastError());
 }
 
+// ---------------------------------------------------------------------------
+// Orientation T with its split scratch in a static device array
+// ---------------------------------------------------------------------------
+// For callers that cannot allocate device memory: the split-K partials and
+// the per-column arrival counters of the orientation-T GEMV live in one
+// file-scope array instead of cudaMalloc'd scratch. Every GPU that loads the
+// library holds this array (256 KiB) until the process exits.
+namespace {
+constexpr size_t kStaticSplitFloats = 61440;   // partials (240 KiB)
+constexpr size_t kStaticSplitCounters = 4096;  // arrival counters (16 KiB)
+constexpr int kMaxDevices = 64;
+static __device__ __align__(256) uint32_t g_static_split_scratch[kStaticSplitFloats + kStaticSplitCounters];
+
+std::mutex g_static_mu;
+void* g_static_addr[kMaxDevices] = {};
+
+// Device address of g_static_split_scratch on `device`, looked up once per
+// device with that device current (the host-side name is not a device address).
+void* static_split_scratch(int device) {
+    AT_REQUIRE(device >= 0 && device < kMaxDevices, AT_ERR_INVALID_ARG, "device index out of range");
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_addr[device]) {
+        int cur = -1;
+        AT_CUDA(cudaGetDevice(&cur));
+        if (cur != device) AT_CUDA(cudaSetDevice(device));
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_split_scratch);
+        if (cur != device) cudaSetDevice(cur);
+        AT_CUDA(e);
+        g_static_addr[device] = p;
+    }
+    return g_static_addr[device];
+}
+}  // namespace
 }  // namespace at
+
+extern "C" int at_gemv_t_static_scratch(at_ctx* ctx, const at_qmat* m, const float* x, float* y, int batch) {
+    using namespace at;
+    return guard([&] {
+        AT_REQUIRE(ctx && m && x && y, AT_ERR_INVALID_ARG, "null argument");
+        AT_REQUIRE(m->orient == AT_ORIENT_T, AT_ERR_INVALID_ARG,
+                   "at_gemv_t_static_scratch takes an orientation-T matrix (use at_gemv for orientation N)");
+        AT_REQUIRE(m->type == AT_GGML_Q4_0 || m->type == AT_GGML_Q8_0, AT_ERR_UNSUPPORTED,
+                   "at_gemv_t_static_scratch supports Q4_0 and Q8_0");
+        AT_REQUIRE(batch >= 1 && batch <= 8, AT_ERR_INVALID_ARG, "batch must be in [1, 8]");
+        AT_REQUIRE(((uintptr_t)x & 15) == 0, AT_ERR_INVALID_ARG, "x must be 16-byte aligned");
+        size_t nf = 0, nc = 0;
+        gemv_t_scratch_need(m, batch, ctx->num_sms, &nf, &nc);
+        AT_REQUIRE(nf <= kStaticSplitFloats && nc <= kStaticSplitCounters, AT_ERR_INVALID_ARG,
+                   "split scratch of " + std::to_string(nf) + " partials and " + std::to_string(nc) +
+                       " counters exceeds the static maximum of " + std::to_string(kStaticSplitFloats) + " and " +
+                       std::to_string(kStaticSplitCounters));
+        uint32_t* base = static_cast<uint32_t*>(static_split_scratch(ctx->device));
+        float* partials = reinterpret_cast<float*>(base);
+        unsigned* counters = base + kStaticSplitFloats;
+        // the array keeps the previous call's contents: the counters must start at zero
+        if (nc) AT_CUDA(cudaMemsetAsync(counters, 0, nc * sizeof(unsigned), ctx->stream));
+        GemvArgs a;
+        a.x = x;
+        a.y = y;
+        a.x_stride = (int)m->rows;
+        a.y_stride = (int)m->cols;
+        a.scratch = partials;
+        a.counters = counters;
+        launch_gemv_t(m, batch, Pro::Plain, Epi::Plain, a, ctx->num_sms, ctx->stream);
+    });
+}

@@ -103,6 +103,22 @@ int at_qmat_export(at_ctx* ctx, const at_qmat* m, void* dst_dev);
  * [batch][out], 1 <= batch <= 8. Replaces Kernels.sgemv over the dequantized
  * FP32 weights (core/Kernels.java:331-371) on the model path. */
 int at_gemv(at_ctx* ctx, const at_qmat* m, const float* x_dev, float* y_dev, int batch);
+/* Same orientation-T GEMV as at_gemv (same kernel, same results), for callers
+ * that cannot allocate device memory: callers whose device memory belongs to
+ * another allocator (a framework's caching allocator, or an arena sized up
+ * front) and callers that cannot take cudaMalloc's device-wide
+ * synchronisation in the middle of a decode loop. at_gemv grows its split-K
+ * scratch with cudaMalloc the first time a larger shape needs it; this entry
+ * point allocates nothing: the split partials and arrival counters live in
+ * one static device array of 256 KiB (61440 partial floats + 4096 counters),
+ * held by every GPU that loads the library until exit. Shapes whose split
+ * needs more are rejected with AT_ERR_INVALID_ARG. The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress, with that device
+ * current); make that first call before any stream capture. Every call shares
+ * the array and zeroes the counters first: calls that overlap on the GPU
+ * (other streams or contexts of the same device) race. No counterpart in the
+ * reference. m must be stored for AT_ORIENT_T. */
+int at_gemv_t_static_scratch(at_ctx* ctx, const at_qmat* m, const float* x_dev, float* y_dev, int batch);
 
 /* ---- Kernels (core/Kernels.java), FP32 device buffers ----------------------- */
 /* Kernels.sgemv(MemorySegment a,x,y,int M,int K)  (core/Kernels.java:350-371) */
