@@ -82,81 +82,46 @@ __device__ __forceinline__ void decode32(const uint4* q, float2* w) {
     }
 }
 
-// Two fp16 values (1024 + v) packed in h, minus c, as exact FP32 pair: one
-// mixed-precision add per element (f16 operand, f32 result), on the FMA pipe.
-__device__ __forceinline__ float2 h2_minus(uint32_t h, float c) {
-    float a, b;
-    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
-        "add.rn.f32.f16 %0, lo, %3;\n\tadd.rn.f32.f16 %1, hi, %3;\n\t}"
-        : "=f"(a), "=f"(b) : "r"(h), "f"(c));
-    return f2(a, b);
-}
-
-// Unscaled dot of one block with x staged by stage_x (see there for the
-// element order). A pair of fp16 (1024 + nibble) or (1024 + byte) values is
-// built with one LOP3 from the packed quant word; an exact f16->f32 add
-// removes the offset.
-//  Q4_0, word i (elements 8i..8i+7, byte k = e[2k] | e[2k+1] << 4):
-//    (w & 0x000F000F)  -> 1024 + (e0, e4)       minus 1032   -> e - 8
-//    (w & 0x00F000F0)  -> 1024 + 16 (e1, e5)    minus 1152   -> 16 (e - 8)
-//    same on w >> 8    -> (e2, e6), 16 (e3, e7)
-//    x staged per word as (x0, x4, x1/16, x5/16), (x2, x6, x3/16, x7/16).
-//  Q8_0, word i (elements 4i..4i+3, int8): ((w & 0x00FF00FF) ^ 0x64806480)
-//    -> 1024 + 128 + (e0, e2), minus 1152 -> e; same on w >> 8 -> (e1, e3);
-//    x staged per word as (x0, x2, x1, x3).
+// Unscaled dot of one block with x (natural order, xr[t] = x[4t..4t+3]).
+// Each nibble (byte) is placed in the low mantissa byte of 2^23 by one byte
+// permute, and one packed f32x2 subtraction of 2^23 + 8 (or 2^23 + 128 after
+// flipping the sign bit of an int8) leaves the exact integer weight.
 template <int QT>
 __device__ __forceinline__ float dot32(const uint4* q, const float4* xr) {
     float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
     if constexpr (QT == AT_GGML_Q4_0) {
+        const float2 moff = f2(-8388616.f, -8388616.f);  // -(2^23 + 8)
         const uint32_t ws[4] = {q[0].x, q[0].y, q[0].z, q[0].w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const uint32_t w = ws[i], w8 = ws[i] >> 8;
-            const float2 p0 = h2_minus((w & 0x000F000Fu) | 0x64006400u, -1032.f);
-            const float2 p1 = h2_minus((w & 0x00F000F0u) | 0x64006400u, -1152.f);
-            const float2 p2 = h2_minus((w8 & 0x000F000Fu) | 0x64006400u, -1032.f);
-            const float2 p3 = h2_minus((w8 & 0x00F000F0u) | 0x64006400u, -1152.f);
+            const uint32_t lo = ws[i] & 0x0F0F0F0Fu, hi = (ws[i] >> 4) & 0x0F0F0F0Fu;
+            // pair k = elements (8i + 2k, 8i + 2k + 1) = (low, high) nibble of byte k
+            const float2 p0 = __fadd2_rn(f2(magic_byte(lo, 0), magic_byte(hi, 0)), moff);
+            const float2 p1 = __fadd2_rn(f2(magic_byte(lo, 1), magic_byte(hi, 1)), moff);
+            const float2 p2 = __fadd2_rn(f2(magic_byte(lo, 2), magic_byte(hi, 2)), moff);
+            const float2 p3 = __fadd2_rn(f2(magic_byte(lo, 3), magic_byte(hi, 3)), moff);
             a0 = __ffma2_rn(p0, f2(xr[2 * i].x, xr[2 * i].y), a0);
             a1 = __ffma2_rn(p1, f2(xr[2 * i].z, xr[2 * i].w), a1);
             a0 = __ffma2_rn(p2, f2(xr[2 * i + 1].x, xr[2 * i + 1].y), a0);
             a1 = __ffma2_rn(p3, f2(xr[2 * i + 1].z, xr[2 * i + 1].w), a1);
         }
     } else {
+        const float2 moff = f2(-8388736.f, -8388736.f);  // -(2^23 + 128)
         const uint32_t ws[8] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const uint32_t w = ws[i], w8 = ws[i] >> 8;
-            const float2 p0 = h2_minus((w & 0x00FF00FFu) ^ 0x64806480u, -1152.f);
-            const float2 p1 = h2_minus((w8 & 0x00FF00FFu) ^ 0x64806480u, -1152.f);
-            a0 = __ffma2_rn(p0, f2(xr[i].x, xr[i].y), a0);
-            a1 = __ffma2_rn(p1, f2(xr[i].z, xr[i].w), a1);
+            const uint32_t u = ws[i] ^ 0x80808080u;  // int8 q -> unsigned q + 128
+            const float2 v01 = __fadd2_rn(f2(magic_byte(u, 0), magic_byte(u, 1)), moff);
+            const float2 v23 = __fadd2_rn(f2(magic_byte(u, 2), magic_byte(u, 3)), moff);
+            a0 = __ffma2_rn(v01, f2(xr[i].x, xr[i].y), a0);
+            a1 = __ffma2_rn(v23, f2(xr[i].z, xr[i].w), a1);
         }
     }
     return (a0.x + a0.y) + (a1.x + a1.y);
 }
 
-// Position of natural element e (0..31) of a block in the staged x row, and
-// the exact power-of-two scale applied to it (matches dot32).
-template <int QT>
-__device__ __forceinline__ int x_slot(int e) {
-    if constexpr (QT == AT_GGML_Q4_0) {
-        const int w = e >> 3, r = e & 7;  // word, element in word
-        // r -> slot: 0->0, 4->1, 1->2, 5->3, 2->4, 6->5, 3->6, 7->7
-        const int hi = r & 1, idx = r >> 1;  // r = 2 * byte + nibble
-        return 8 * w + 4 * (idx & 1) + 2 * hi + (idx >> 1);
-    } else {
-        const int w = e >> 2, r = e & 3;  // (x0, x2, x1, x3)
-        return 4 * w + 2 * (r & 1) + (r >> 1);
-    }
-}
-template <int QT>
-__device__ __forceinline__ float x_scale(int e) {
-    if constexpr (QT == AT_GGML_Q4_0) return (e & 1) ? 0.0625f : 1.0f;
-    else return 1.0f;
-}
-
 // Stages x (or the normed x + y) for blocks [b0, b0 + nbc) of B rows into
-// shared memory in the order dot32<QT> reads it, XPAD floats per block.
+// shared memory, natural order, XPAD floats per block.
 // float4 global loads, eight in flight per thread before any is stored.
 template <int QT, int B, Pro PRO, int NT = THREADS>
 __device__ __forceinline__ void stage_x(float* xs, const GemvArgs& a, int b0, int nbc, int chunk_blocks,
@@ -190,19 +155,14 @@ __device__ __forceinline__ void stage_x(float* xs, const GemvArgs& a, int b0, in
             if (idx < total) {
                 const int bb = idx / nf4, r = idx - bb * nf4;
                 const int blk = r >> 3, q4 = r & 7;
-                float o[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+                float4 o = v[k];
                 if constexpr (PRO == Pro::AddNorm) {
                     const float4 g = *reinterpret_cast<const float4*>(a.gamma + (size_t)(b0 + blk) * 32 + q4 * 4);
                     const float inv = s_inv[bb];
-                    o[0] = norm_apply(o[0], inv, g.x); o[1] = norm_apply(o[1], inv, g.y);
-                    o[2] = norm_apply(o[2], inv, g.z); o[3] = norm_apply(o[3], inv, g.w);
+                    o = make_float4(norm_apply(o.x, inv, g.x), norm_apply(o.y, inv, g.y), norm_apply(o.z, inv, g.z),
+                                    norm_apply(o.w, inv, g.w));
                 }
-                float* dst = xs + ((size_t)bb * chunk_blocks + blk) * XPAD;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    const int e = q4 * 4 + t;
-                    dst[x_slot<QT>(e)] = __fmul_rn(o[t], x_scale<QT>(e));
-                }
+                *reinterpret_cast<float4*>(xs + ((size_t)bb * chunk_blocks + blk) * XPAD + q4 * 4) = o;
             }
         }
     }
@@ -277,12 +237,15 @@ struct N4Params {
 template <int QT, int NM>
 __device__ __forceinline__ void n4_issue(uint32_t slot, const N4Params& p, int g, int s, int lane) {
     using TL = NTile<QT>;
-    if (g < p.ngroups && s < p.nsteps) {
+    if (g < p.ngroups) {
 #pragma unroll
         for (int m = 0; m < NM; ++m) {
             const uint8_t* src = p.tiles[m] + ((size_t)g * p.nsteps + s) * TL::BYTES;
-            for (int k = lane; k < TL::CHUNKS; k += 32)
-                cp_async16(slot + (uint32_t)(m * TL::BYTES + 16 * k), src + 16 * k);
+#pragma unroll
+            for (int u = 0; u < (TL::CHUNKS + 31) / 32; ++u) {
+                const int k = lane + 32 * u;
+                if (k < TL::CHUNKS) cp_async16(slot + (uint32_t)(m * TL::BYTES + 16 * k), src + 16 * k);
+            }
         }
     }
     cp_commit();
@@ -290,6 +253,7 @@ __device__ __forceinline__ void n4_issue(uint32_t slot, const N4Params& p, int g
 
 template <int QT, int B, Pro PRO, Epi EPI, int NST>
 __global__ void __launch_bounds__(N4_THREADS, 1) gemv_n4_kernel(const N4Params p) {
+    static_assert((NST & (NST - 1)) == 0, "ring depth is a power of two");
     constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
     using TL = NTile<QT>;
     constexpr int SLOT = NM * TL::BYTES;
@@ -307,15 +271,23 @@ __global__ void __launch_bounds__(N4_THREADS, 1) gemv_n4_kernel(const N4Params p
     const int T = p.per * nsk;
     const uint8_t* ring_ptr = reinterpret_cast<const uint8_t*>(xs) + p.ring_off + warp * NST * SLOT;
     const uint32_t ring = (uint32_t)__cvta_generic_to_shared(ring_ptr);
-    auto group_of = [&](int round) { return (blockIdx.x * p.per + round) * p.gpc + gslot; };
+    const int g_base = blockIdx.x * p.per * p.gpc + gslot;  // group of round r: g_base + r * gpc
 
-    // Weights are never written by earlier kernels: start their copies
-    // before waiting on those kernels.
+    // Issue iterator: (round, step) of the next step to copy. Weights are
+    // never written by earlier kernels, so the first NST copies start before
+    // waiting on those kernels.
+    int i_round = 0, i_step = 0, issued = 0;
+    auto issue_next = [&](uint32_t slot) {
+        if (issued < T) {
+            n4_issue<QT, NM>(slot, p, g_base + i_round * p.gpc, s0 + i_step, lane);
+            if (++i_step == nsk) { i_step = 0; ++i_round; }
+        } else {
+            cp_commit();
+        }
+        ++issued;
+    };
 #pragma unroll
-    for (int k = 0; k < NST; ++k) {
-        if (k < T) n4_issue<QT, NM>(ring + k * SLOT, p, group_of(k / nsk), s0 + k % nsk, lane);
-        else cp_commit();
-    }
+    for (int k = 0; k < NST; ++k) issue_next(ring + k * SLOT);
     pdl_wait();
 
     const int d_model = p.nb * 32;
@@ -334,14 +306,16 @@ __global__ void __launch_bounds__(N4_THREADS, 1) gemv_n4_kernel(const N4Params p
 
     int t = 0;
     for (int round = 0; round < p.per; ++round) {
-        const int g = group_of(round);
+        const int g = g_base + round * p.gpc;
+        const bool g_ok = g < p.ngroups;
+        const float* xrow = xs + ((size_t)s0 * 32 + lane) * XPAD;  // x of this lane's first block
         for (int ks = 0; ks < nsk; ++ks, ++t) {
             cp_wait<NST - 1>();
             __syncwarp();  // every lane's 16-byte pieces of this slot have landed
-            const int slot = t % NST;
+            const int slot = t & (NST - 1);
             const uint8_t* sp = ring_ptr + slot * SLOT;
             const int j = (s0 + ks) * 32 + lane;  // this lane's block
-            if (g < p.ngroups && j < p.nb) {
+            if (g_ok && j < p.nb) {
                 uint4 q[NM * 4][NV];
                 float dsc[NM * 4];
 #pragma unroll
@@ -356,7 +330,7 @@ __global__ void __launch_bounds__(N4_THREADS, 1) gemv_n4_kernel(const N4Params p
                     }
 #pragma unroll
                 for (int b = 0; b < B; ++b) {
-                    const float4* xv = reinterpret_cast<const float4*>(xs + ((size_t)b * p.nb + j) * XPAD);
+                    const float4* xv = reinterpret_cast<const float4*>(xrow + (size_t)b * p.nb * XPAD + (size_t)ks * 32 * XPAD);
                     float4 xr[8];
 #pragma unroll
                     for (int k = 0; k < 8; ++k) xr[k] = xv[k];
@@ -365,9 +339,7 @@ __global__ void __launch_bounds__(N4_THREADS, 1) gemv_n4_kernel(const N4Params p
                 }
             }
             __syncwarp();  // every lane is done with this slot before it is refilled
-            const int tn = t + NST;
-            if (tn < T) n4_issue<QT, NM>(ring + slot * SLOT, p, group_of(tn / nsk), s0 + tn % nsk, lane);
-            else cp_commit();
+            issue_next(ring + slot * SLOT);
         }
         // round complete: reduce over lanes, then over the KS warps of each group
 #pragma unroll
@@ -388,7 +360,7 @@ __global__ void __launch_bounds__(N4_THREADS, 1) gemv_n4_kernel(const N4Params p
         if (kpart == 0 && lane < 4 * B) {
             const int r = lane / B, b = lane - (lane / B) * B;
             const int row = g * 4 + r;
-            if (g < p.ngroups && row < p.rows) {
+            if (g_ok && row < p.rows) {
                 float v0 = 0.f, v1 = 0.f;
                 for (int k = 0; k < p.KS; ++k) {
                     v0 += red[warp + k][(0 * 4 + r) * B + b];
