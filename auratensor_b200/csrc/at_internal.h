@@ -169,8 +169,10 @@ void launch_gemv_n(const at_qmat* m, int batch, Pro pro, Epi epi, const GemvArgs
                    cudaStream_t s, bool pdl = false);
 void launch_gemv_t(const at_qmat* m, int batch, Pro pro, Epi epi, const GemvArgs& a, int num_sms,
                    cudaStream_t s, bool pdl = false);
-// Scratch floats / counters a T launch needs for (m, batch).
+// Scratch floats / counters a T or N launch needs for (m, batch); the N
+// figure covers every epilogue.
 void gemv_t_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* floats, size_t* counters);
+void gemv_n_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* floats, size_t* counters);
 void launch_sgemv_f32(const float* A, const float* x, float* y, int M, int K, int batch, int a_ld,
                       cudaStream_t s);
 

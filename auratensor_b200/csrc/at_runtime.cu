@@ -501,7 +501,7 @@ int at_qmat_export(at_ctx* ctx, const at_qmat* m, void* dst) {
     });
 }
 
-// Scratch buffer for split T launches made through at_gemv.
+// Scratch buffer for split launches made through at_gemv.
 struct GemvScratch {
     float* buf = nullptr;
     unsigned* counters = nullptr;
@@ -531,32 +531,30 @@ int at_gemv(at_ctx* ctx, const at_qmat* m, const float* x, float* y, int batch) 
         a.y = y;
         a.x_stride = (int)in;
         a.y_stride = (int)outn;
-        if (m->orient == AT_ORIENT_N) {
-            launch_gemv_n(m, batch, Pro::Plain, Epi::Plain, a, ctx->num_sms, ctx->stream);
-        } else {
-            static GemvScratch sc;  // shared by at_gemv calls; calls are serialized by the stream
-            size_t nf = 0, nc = 0;
-            gemv_t_scratch_need(m, batch, ctx->num_sms, &nf, &nc);
-            {
-                std::lock_guard<std::mutex> lk(g_scratch_mu);
-                if (nf > sc.floats) {
-                    AT_CUDA(cudaStreamSynchronize(ctx->stream));
-                    if (sc.buf) cudaFree(sc.buf);
-                    AT_CUDA(cudaMalloc(&sc.buf, nf * 4));
-                    sc.floats = nf;
-                }
-                if (nc > sc.ncounters) {
-                    AT_CUDA(cudaStreamSynchronize(ctx->stream));
-                    if (sc.counters) cudaFree(sc.counters);
-                    AT_CUDA(cudaMalloc(&sc.counters, nc * 4));
-                    AT_CUDA(cudaMemset(sc.counters, 0, nc * 4));
-                    sc.ncounters = nc;
-                }
+        static GemvScratch sc;  // shared by at_gemv calls; calls are serialized by the stream
+        size_t nf = 0, nc = 0;
+        if (m->orient == AT_ORIENT_N) gemv_n_scratch_need(m, batch, ctx->num_sms, &nf, &nc);
+        else gemv_t_scratch_need(m, batch, ctx->num_sms, &nf, &nc);
+        {
+            std::lock_guard<std::mutex> lk(g_scratch_mu);
+            if (nf > sc.floats) {
+                AT_CUDA(cudaStreamSynchronize(ctx->stream));
+                if (sc.buf) cudaFree(sc.buf);
+                AT_CUDA(cudaMalloc(&sc.buf, nf * 4));
+                sc.floats = nf;
             }
-            a.scratch = sc.buf;
-            a.counters = sc.counters;
-            launch_gemv_t(m, batch, Pro::Plain, Epi::Plain, a, ctx->num_sms, ctx->stream);
+            if (nc > sc.ncounters) {
+                AT_CUDA(cudaStreamSynchronize(ctx->stream));
+                if (sc.counters) cudaFree(sc.counters);
+                AT_CUDA(cudaMalloc(&sc.counters, nc * 4));
+                AT_CUDA(cudaMemset(sc.counters, 0, nc * 4));
+                sc.ncounters = nc;
+            }
         }
+        a.scratch = sc.buf;
+        a.counters = sc.counters;
+        if (m->orient == AT_ORIENT_N) launch_gemv_n(m, batch, Pro::Plain, Epi::Plain, a, ctx->num_sms, ctx->stream);
+        else launch_gemv_t(m, batch, Pro::Plain, Epi::Plain, a, ctx->num_sms, ctx->stream);
     });
 }
 

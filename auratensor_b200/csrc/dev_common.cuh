@@ -6,6 +6,14 @@
 
 namespace at {
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start before the previous kernel in the stream ends.
+// pdl_wait() blocks until that kernel has completed and its writes are
+// visible; everything before it may only touch memory no earlier kernel of
+// the step writes. pdl_trigger() lets the next kernel start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Fp16.toFloat (core/Fp16.java:19-37): subnormals flush to signed zero,
 // e == 31 gives +-inf or the canonical NaN 0x7FC00000, otherwise rebias.
 __device__ __forceinline__ float fp16_ftz(uint32_t h) {

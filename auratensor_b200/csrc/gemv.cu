@@ -15,11 +15,15 @@
 //
 // Weights use the tiled layout of at_qmat (a lossless re-layout of whole
 // blocks): the bytes one warp step consumes are one contiguous tile.
-// Orientation N (rows = outputs, blocks along the row): a warp streams the
-// tiles (4 rows x 32 blocks) of its row group through a cp.async ring in
-// shared memory, one block per lane per step; x is staged once per CTA in
-// shared memory (natural order, 36 floats per 32-element block so a
-// quarter-warp of 128-bit reads touches 32 distinct banks).
+// Orientation N (rows = outputs, blocks along the row), batch <= 2: the
+// tiles (4 rows x 32 blocks) form one stream split evenly over one CTA per
+// SM and its 16 warps; a warp copies its tiles through a cp.async ring in
+// shared memory, one block per lane per step, and x is staged once per CTA
+// in shared memory (natural order, 36 floats per 32-element block so a
+// quarter-warp of 128-bit reads touches 32 distinct banks). The RMSNorm of
+// an AddNorm prologue is folded into the result (the GEMV runs on
+// (x + y) * gamma and 1/rms multiplies the finished dot products), so the
+// prologue is one pass over x. Larger batches stage x in chunks.
 // Orientation T (rows = inputs, blocks along the outputs): a lane owns rows
 // of one block column (tiles of 32 rows) and accumulates its 32 (or 8)
 // outputs; lanes combine by a butterfly reduce-scatter, warps through shared
@@ -46,8 +50,6 @@ constexpr int THREADS = 256;
 constexpr int XPAD = 36;                 // floats per staged 32-element block
 constexpr int kMaxXSmemChunk = 96 * 1024;
 
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 template <int QT>
 struct QTraits;
@@ -186,6 +188,26 @@ __device__ __forceinline__ void write_xout(const GemvArgs& a, int d, const float
     }
 }
 
+// The same for the slice [c*n4/C, (c+1)*n4/C) of float4s of each row: CTA c of C.
+template <int B, int NT>
+__device__ __forceinline__ void write_xout_slice(const GemvArgs& a, int d, const float* s_inv, int c, int C) {
+    const int n4 = d / 4;
+    const int i0 = (int)((int64_t)c * n4 / C), i1 = (int)((int64_t)(c + 1) * n4 / C);
+    for (int idx = threadIdx.x; idx < B * (i1 - i0); idx += NT) {
+        const int bb = idx / (i1 - i0), i4 = i0 + idx - bb * (i1 - i0);
+        const size_t off = (size_t)bb * a.x_stride + (size_t)i4 * 4;
+        float4 t = *reinterpret_cast<const float4*>(a.xin + off);
+        if (a.yin) {
+            const float4 u = *reinterpret_cast<const float4*>(a.yin + off);
+            t.x = __fadd_rn(t.x, u.x); t.y = __fadd_rn(t.y, u.y); t.z = __fadd_rn(t.z, u.z); t.w = __fadd_rn(t.w, u.w);
+        }
+        const float4 g = *reinterpret_cast<const float4*>(a.gamma + (size_t)i4 * 4);
+        const float inv = s_inv[bb];
+        *reinterpret_cast<float4*>(a.xout + off) = make_float4(
+            norm_apply(t.x, inv, g.x), norm_apply(t.y, inv, g.y), norm_apply(t.z, inv, g.z), norm_apply(t.w, inv, g.w));
+    }
+}
+
 template <Epi EPI>
 __device__ __forceinline__ float n_epilogue(float g, float u) {
     if constexpr (EPI == Epi::SiluMul) {
@@ -198,16 +220,34 @@ __device__ __forceinline__ float n_epilogue(float g, float u) {
 }
 
 // ---------------------------------------------------------------------------
-// Orientation N, tile streams through per-warp cp.async rings
+// Balanced unit streams (orientation N and T, batch <= 2)
 // ---------------------------------------------------------------------------
-// A warp owns a 4-row group and a contiguous range of its 32-block steps; one
-// step is one tile (4 rows x 32 blocks, scales then quant bytes), copied
-// 16 bytes per lane into the warp's ring slot with cp.async. Lanes then read
-// their own block of each row. Warps that split one group's steps (KS > 1)
-// combine through shared memory in a fixed order. A CTA stages x once and
-// walks `per` rounds of groups.
-constexpr int N4_THREADS = 512;
-constexpr int N4_WARPS = N4_THREADS / 32;
+// The tiles of a matrix form one stream of units in storage order:
+//   N: unit (g, s) = tile of rows 4g..4g+3 x blocks 32s..32s+31 (the steps of
+//      a row group are consecutive); segment = row group g;
+//   T: unit (c, g) = tile of rows 32g..32g+31 of block column c (the tiles
+//      of a column are consecutive); segment = block column c.
+// CTA c (one per SM) streams units [start[c], start[c+1]) of a host-computed
+// map (whole segments when that costs little balance, else an even split)
+// and its 16 warps split that range evenly, so every SM streams the same
+// bytes within a unit or a segment. A warp copies its units into a per-warp
+// ring of NST slots with cp.async (16 bytes per lane-copy; a __syncwarp after
+// each wait publishes the slot), accumulates in registers while consecutive
+// units belong to one segment, and stores the segment's partial sums to its
+// shared-memory slot when the segment changes. After one barrier each
+// segment inside the CTA is summed over its warps in warp order. A segment
+// shared with neighbouring CTAs goes through global scratch: every CTA
+// stores its partial (slot 2c for its first segment, 2c + 1 for its last),
+// and the last CTA to arrive (counter per segment, reset by that CTA) sums
+// them in CTA order and applies the epilogue. Results do not depend on
+// timing.
+//
+// Activation loads are issued before the bulk of the weight copies: the
+// copies of one SM drain at its share of HBM bandwidth, and a load queued
+// behind them would wait for all of them.
+constexpr int S_THREADS = 512;
+constexpr int S_WARPS = S_THREADS / 32;
+constexpr int kMaxStreamCtas = 160;
 
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
@@ -216,6 +256,12 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// Unit ranges of the CTAs: CTA c streams units [start[c], start[c + 1]).
+struct StreamMap {
+    int len;                           // units per segment
+    int start[kMaxStreamCtas + 1];
+};
+
 template <int QT>
 struct NTile {
     static constexpr int QB = QTraits<QT>::QB;
@@ -223,79 +269,230 @@ struct NTile {
     static constexpr int CHUNKS = BYTES / 16;
 };
 
-struct N4Params {
-    const uint8_t* tiles[2];
-    int rows, nb, ngroups, nsteps;
-    int KS;         // warps splitting the steps of one group
-    int gpc;        // groups per CTA round = N4_WARPS / KS
-    int per;        // rounds per CTA
-    int steps_ks;   // steps per step range = ceil(nsteps / KS)
-    int ring_off;
-    GemvArgs a;
-};
+// Copies one unit (CHUNKS x 16 bytes) from src into a ring slot.
+template <int CHUNKS>
+__device__ __forceinline__ void copy_unit(uint32_t slot, const uint8_t* src, int lane) {
+#pragma unroll
+    for (int u = 0; u < (CHUNKS + 31) / 32; ++u) {
+        const int k = lane + 32 * u;
+        if (k < CHUNKS) cp_async16(slot + (uint32_t)(16 * k), src + 16 * k);
+    }
+}
 
-template <int QT, int NM>
-__device__ __forceinline__ void n4_issue(uint32_t slot, const N4Params& p, int g, int s, int lane) {
-    using TL = NTile<QT>;
-    if (g < p.ngroups) {
+// Warp w of a CTA with n units streams units [floor(w n / 16), floor((w+1) n / 16))
+// of the CTA's range; warp_of(x) is the warp holding unit x of the range.
+__device__ __forceinline__ int warp_of(int x, int n) {
+    const int w = (16 * x + 15) / n;
+    return w < S_WARPS - 1 ? w : S_WARPS - 1;
+}
+
+// This CTA's sum of the warp partials of segment `seg` (units [s0, s1) of the
+// CTA range, relative), value v, in warp order. Warp w stored its partial of
+// its k-th segment at red[(w * slots + k) * vals + v].
+__device__ __forceinline__ float sum_warp_partials(const float* red, int slots, int vals, int seg, int s0, int s1,
+                                                   int n, int u_lo, int len, int v) {
+    const int wa = warp_of(s0, n), wb = warp_of(s1 - 1, n);
+    float acc = 0.f;
+    for (int w = wa; w <= wb; ++w) {
+        const int first_unit = u_lo + ((w * n) >> 4);
+        const int k = seg - first_unit / len;
+        if (k >= 0 && k < slots) acc += red[((size_t)w * slots + k) * vals + v];
+    }
+    return acc;
+}
+
+// CTAs [first, last] whose ranges overlap segment `seg` (one of them is `cta`).
+__device__ __forceinline__ void seg_ctas(const StreamMap& mp, int C, int cta, int seg, int* first, int* last) {
+    const int s0 = seg * mp.len, s1 = s0 + mp.len;
+    int f = cta, l = cta;
+    while (f > 0 && mp.start[f] > s0) --f;
+    while (l + 1 < C && mp.start[l + 1] < s1) ++l;
+    *first = f;
+    *last = l;
+}
+
+// Scratch slot of CTA cc's partial of segment seg: 2cc if seg is cc's first segment, else 2cc + 1.
+__device__ __forceinline__ int seg_slot(const StreamMap& mp, int cc, int seg) {
+    return 2 * cc + (mp.start[cc] >= seg * mp.len ? 0 : 1);
+}
+
+// Finishes the (at most two) segments this CTA shares with other CTAs: the
+// partials are already in scratch; the last CTA to arrive at a segment calls
+// finish(seg, first, last) with every partial visible. One thread publishes
+// the CTA's stores (barrier, then a device-scope fence, which is cumulative
+// over the stores the barrier ordered before it) and takes the arrival ticket.
+template <class Finish>
+__device__ __forceinline__ void finish_shared_segments(const GemvArgs& a, const StreamMap& mp, int cta, int seg_lo,
+                                                       int seg_hi, bool lo_shared, bool hi_shared, int* s_last,
+                                                       Finish finish) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_last[0] = s_last[1] = 0;
+        int f, l;
+        if (lo_shared) {
+            seg_ctas(mp, gridDim.x, cta, seg_lo, &f, &l);
+            s_last[0] = atomicAdd(&a.counters[seg_lo], 1u) == (unsigned)(l - f);
+        }
+        if (hi_shared && !(lo_shared && seg_hi == seg_lo)) {
+            seg_ctas(mp, gridDim.x, cta, seg_hi, &f, &l);
+            s_last[1] = atomicAdd(&a.counters[seg_hi], 1u) == (unsigned)(l - f);
+        }
+        if (s_last[0] | s_last[1]) __threadfence();
+    }
+    __syncthreads();
 #pragma unroll
-        for (int m = 0; m < NM; ++m) {
-            const uint8_t* src = p.tiles[m] + ((size_t)g * p.nsteps + s) * TL::BYTES;
+    for (int k = 0; k < 2; ++k) {
+        if (s_last[k]) {
+            const int seg = k ? seg_hi : seg_lo;
+            int f, l;
+            seg_ctas(mp, gridDim.x, cta, seg, &f, &l);
+            finish(seg, f, l);
+            if (threadIdx.x == 0) a.counters[seg] = 0u;
+        }
+    }
+}
+
+// Stages x (Pro::Plain) or (xin + yin) * gamma (Pro::AddNorm) for all nb
+// blocks of B rows into shared memory (natural order, XPAD floats per block),
+// eight float4 loads in flight per thread. For AddNorm it also returns this
+// thread's sums of (xin + yin)^2 per row: the RMSNorm scale 1/rms multiplies
+// the finished dot products instead of every staged element, so the staging
+// needs no prior reduction pass.
+template <int B, Pro PRO, int NT>
+__device__ __forceinline__ void stage_x_fold(float* xs, const GemvArgs& a, int nb, float* ss) {
+    const int nf4 = nb * 8;
+    const int total = B * nf4;
 #pragma unroll
-            for (int u = 0; u < (TL::CHUNKS + 31) / 32; ++u) {
-                const int k = lane + 32 * u;
-                if (k < TL::CHUNKS) cp_async16(slot + (uint32_t)(m * TL::BYTES + 16 * k), src + 16 * k);
+    for (int b = 0; b < B; ++b) ss[b] = 0.f;
+    for (int base = 0; base < total; base += NT * 8) {
+        float4 v[8], g[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int idx = base + k * NT + threadIdx.x;
+            if (idx < total) {
+                const int bb = idx / nf4, r = idx - bb * nf4;
+                const size_t off = (size_t)bb * a.x_stride + 4 * (size_t)r;
+                if constexpr (PRO == Pro::Plain) {
+                    v[k] = *reinterpret_cast<const float4*>(a.x + off);
+                } else {
+                    float4 t = *reinterpret_cast<const float4*>(a.xin + off);
+                    if (a.yin) {
+                        const float4 u = *reinterpret_cast<const float4*>(a.yin + off);
+                        t.x = __fadd_rn(t.x, u.x); t.y = __fadd_rn(t.y, u.y);
+                        t.z = __fadd_rn(t.z, u.z); t.w = __fadd_rn(t.w, u.w);
+                    }
+                    v[k] = t;
+                    g[k] = *reinterpret_cast<const float4*>(a.gamma + 4 * (size_t)r);
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int idx = base + k * NT + threadIdx.x;
+            if (idx < total) {
+                const int bb = idx / nf4, r = idx - bb * nf4;
+                float4 o = v[k];
+                if constexpr (PRO == Pro::AddNorm) {
+                    float q = fmaf(o.x, o.x, fmaf(o.y, o.y, fmaf(o.z, o.z, __fmul_rn(o.w, o.w))));
+#pragma unroll
+                    for (int b = 0; b < B; ++b)
+                        if (b == bb) ss[b] += q;
+                    o = make_float4(__fmul_rn(o.x, g[k].x), __fmul_rn(o.y, g[k].y), __fmul_rn(o.z, g[k].z),
+                                    __fmul_rn(o.w, g[k].w));
+                }
+                *reinterpret_cast<float4*>(xs + ((size_t)bb * nb + (r >> 3)) * XPAD + (r & 7) * 4) = o;
             }
         }
     }
-    cp_commit();
 }
 
+// RMSNorm scales of the B rows from the per-warp sums of squares s_ss[warp][b]
+// (fixed summation order: every CTA computes the same values).
+template <int B, int NW>
+__device__ __forceinline__ void rms_scales(const float* s_ss, int d, float eps, float* inv) {
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) t += s_ss[w * B + b];
+        inv[b] = rms_inv(t, d, eps);
+    }
+}
+
+struct NSParams {
+    const uint8_t* tiles[2];
+    int rows, nb, nsteps;
+    int slots;     // partial slots per warp (row groups one warp can touch)
+    int red_off;   // byte offsets in dynamic shared memory: partial slots, weight rings
+    int ring_off;
+    int pre;       // ring slots copied before waiting on the previous kernel
+    StreamMap map;
+    GemvArgs a;
+};
+
 template <int QT, int B, Pro PRO, Epi EPI, int NST>
-__global__ void __launch_bounds__(N4_THREADS, 1) gemv_n4_kernel(const N4Params p) {
+__global__ void __launch_bounds__(S_THREADS, 1) gemv_ns_kernel(const NSParams p) {
     static_assert((NST & (NST - 1)) == 0, "ring depth is a power of two");
     constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
     using TL = NTile<QT>;
     constexpr int SLOT = NM * TL::BYTES;
     constexpr int NV = QTraits<QT>::NV;
+    constexpr int VPG = NM * 4 * B;  // partial values per row group
     extern __shared__ __align__(16) float xs[];
-    __shared__ float s_red[N4_WARPS * B];
+    __shared__ float s_ss[S_WARPS * B];  // AddNorm: per-warp sums of squares
     __shared__ float s_inv[B];
-    __shared__ float red[N4_WARPS][NM * 4 * B];
+    __shared__ int s_last[2];
 
     pdl_trigger();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int kpart = warp % p.KS, gslot = warp / p.KS;
-    const int s0 = kpart * p.steps_ks;
-    const int nsk = max(0, min(p.nsteps, s0 + p.steps_ks) - s0);  // steps of this warp per round
-    const int T = p.per * nsk;
+    const int cta = blockIdx.x;
+    const int L = p.nsteps;
+    const int u_lo = p.map.start[cta], u_hi = p.map.start[cta + 1], n = u_hi - u_lo;
+    const int w_lo = u_lo + ((warp * n) >> 4);
+    const int T = u_lo + (((warp + 1) * n) >> 4) - w_lo;
+    int g = w_lo / L, s = w_lo - g * L;
+    const int g_first = g;
+    // row groups of this CTA; the first / last may be shared with neighbours
+    const int g_lo = u_lo / L, g_hi = (u_hi - 1) / L;
+    const bool lo_shared = g_lo * L < u_lo, hi_shared = (g_hi + 1) * L > u_hi;
+    float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + p.red_off);
     const uint8_t* ring_ptr = reinterpret_cast<const uint8_t*>(xs) + p.ring_off + warp * NST * SLOT;
     const uint32_t ring = (uint32_t)__cvta_generic_to_shared(ring_ptr);
-    const int g_base = blockIdx.x * p.per * p.gpc + gslot;  // group of round r: g_base + r * gpc
 
-    // Issue iterator: (round, step) of the next step to copy. Weights are
-    // never written by earlier kernels, so the first NST copies start before
-    // waiting on those kernels.
-    int i_round = 0, i_step = 0, issued = 0;
-    auto issue_next = [&](uint32_t slot) {
+    const uint8_t* src = p.tiles[0] + (size_t)w_lo * TL::BYTES;
+    const uint8_t* src2 = p.tiles[1] + (size_t)w_lo * TL::BYTES;
+    int issued = 0;
+    auto issue_next = [&]() {
+        const uint32_t slot = ring + (issued & (NST - 1)) * SLOT;
         if (issued < T) {
-            n4_issue<QT, NM>(slot, p, g_base + i_round * p.gpc, s0 + i_step, lane);
-            if (++i_step == nsk) { i_step = 0; ++i_round; }
-        } else {
-            cp_commit();
+            copy_unit<TL::CHUNKS>(slot, src, lane);
+            if constexpr (NM == 2) copy_unit<TL::CHUNKS>(slot + TL::BYTES, src2, lane);
+            src += TL::BYTES;
+            src2 += TL::BYTES;
         }
+        cp_commit();
         ++issued;
     };
-#pragma unroll
-    for (int k = 0; k < NST; ++k) issue_next(ring + k * SLOT);
+    // Weights are never written by earlier kernels: `pre` slots are copied
+    // before waiting on them; the ring fills up inside the main loop, after
+    // the activation loads.
+    for (int k = 0; k < p.pre; ++k) issue_next();
+    for (int i = tid; i < S_WARPS * p.slots * VPG; i += S_THREADS) red[i] = 0.f;
     pdl_wait();
 
     const int d_model = p.nb * 32;
-    if constexpr (PRO == Pro::AddNorm) {
-        block_rms_inv<B, N4_THREADS>(p.a.xin, p.a.yin, p.a.x_stride, d_model, p.a.eps, s_red, s_inv);
-        if (blockIdx.x == 0) write_xout<B, N4_THREADS>(p.a, d_model, s_inv);
+    {
+        float ss[B];
+        stage_x_fold<B, PRO, S_THREADS>(xs, p.a, p.nb, ss);
+        if constexpr (PRO == Pro::AddNorm) {
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                const float t = warp_sum(ss[b]);
+                if (lane == 0) s_ss[warp * B + b] = t;
+            }
+        }
     }
-    stage_x<QT, B, PRO, N4_THREADS>(xs, p.a, 0, p.nb, p.nb, s_inv);
     __syncthreads();
 
     float acc[NM * 4][B];
@@ -304,74 +501,110 @@ __global__ void __launch_bounds__(N4_THREADS, 1) gemv_n4_kernel(const N4Params p
 #pragma unroll
         for (int b = 0; b < B; ++b) acc[i][b] = 0.f;
 
-    int t = 0;
-    for (int round = 0; round < p.per; ++round) {
-        const int g = g_base + round * p.gpc;
-        const bool g_ok = g < p.ngroups;
-        const float* xrow = xs + ((size_t)s0 * 32 + lane) * XPAD;  // x of this lane's first block
-        for (int ks = 0; ks < nsk; ++ks, ++t) {
-            cp_wait<NST - 1>();
-            __syncwarp();  // every lane's 16-byte pieces of this slot have landed
-            const int slot = t & (NST - 1);
-            const uint8_t* sp = ring_ptr + slot * SLOT;
-            const int j = (s0 + ks) * 32 + lane;  // this lane's block
-            if (g_ok && j < p.nb) {
-                uint4 q[NM * 4][NV];
-                float dsc[NM * 4];
+    for (int t = 0; t < T; ++t) {
+        while (issued < t + NST) issue_next();  // NST groups after this one are committed
+        cp_wait<NST - 1>();
+        __syncwarp();  // every lane's 16-byte pieces of this slot have landed
+        const uint8_t* sp = ring_ptr + (t & (NST - 1)) * SLOT;
+        const int j = s * 32 + lane;  // this lane's block
+        if (j < p.nb) {
+            uint4 q[NM * 4][NV];
+            float dsc[NM * 4];
 #pragma unroll
-                for (int m = 0; m < NM; ++m)
+            for (int m = 0; m < NM; ++m)
 #pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        const uint8_t* tb = sp + m * TL::BYTES;
+                for (int r = 0; r < 4; ++r) {
+                    const uint8_t* tb = sp + m * TL::BYTES;
 #pragma unroll
-                        for (int v = 0; v < NV; ++v)
-                            q[m * 4 + r][v] = *reinterpret_cast<const uint4*>(tb + 256 + (r * 32 + lane) * TL::QB + 16 * v);
-                        dsc[m * 4 + r] = fp16_ftz_fast(*reinterpret_cast<const uint16_t*>(tb + (r * 32 + lane) * 2));
-                    }
-#pragma unroll
-                for (int b = 0; b < B; ++b) {
-                    const float4* xv = reinterpret_cast<const float4*>(xrow + (size_t)b * p.nb * XPAD + (size_t)ks * 32 * XPAD);
-                    float4 xr[8];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) xr[k] = xv[k];
-#pragma unroll
-                    for (int i = 0; i < NM * 4; ++i) acc[i][b] = fmaf(dsc[i], dot32<QT>(q[i], xr), acc[i][b]);
+                    for (int v = 0; v < NV; ++v)
+                        q[m * 4 + r][v] = *reinterpret_cast<const uint4*>(tb + 256 + (r * 32 + lane) * TL::QB + 16 * v);
+                    dsc[m * 4 + r] = fp16_ftz_fast(*reinterpret_cast<const uint16_t*>(tb + (r * 32 + lane) * 2));
                 }
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                const float4* xv = reinterpret_cast<const float4*>(xs + ((size_t)b * p.nb + j) * XPAD);
+                float4 xr[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) xr[k] = xv[k];
+#pragma unroll
+                for (int i = 0; i < NM * 4; ++i) acc[i][b] = fmaf(dsc[i], dot32<QT>(q[i], xr), acc[i][b]);
             }
-            __syncwarp();  // every lane is done with this slot before it is refilled
-            issue_next(ring + slot * SLOT);
         }
-        // round complete: reduce over lanes, then over the KS warps of each group
-#pragma unroll
-        for (int i = 0; i < NM * 4; ++i)
-#pragma unroll
-            for (int b = 0; b < B; ++b) acc[i][b] = warp_sum(acc[i][b]);
-        if (lane == 0) {
+        __syncwarp();  // every lane is done with this slot before it is refilled
+        int s_next = s + 1, g_next = g;
+        if (s_next == L) { s_next = 0; ++g_next; }
+        if (t == T - 1 || g_next != g) {
+            // row group done (or range end): lane sums into this warp's slot
+            float* dst = red + ((size_t)warp * p.slots + (g - g_first)) * VPG;
 #pragma unroll
             for (int i = 0; i < NM * 4; ++i)
 #pragma unroll
-                for (int b = 0; b < B; ++b) red[warp][i * B + b] = acc[i][b];
-        }
-#pragma unroll
-        for (int i = 0; i < NM * 4; ++i)
-#pragma unroll
-            for (int b = 0; b < B; ++b) acc[i][b] = 0.f;
-        __syncthreads();
-        if (kpart == 0 && lane < 4 * B) {
-            const int r = lane / B, b = lane - (lane / B) * B;
-            const int row = g * 4 + r;
-            if (g_ok && row < p.rows) {
-                float v0 = 0.f, v1 = 0.f;
-                for (int k = 0; k < p.KS; ++k) {
-                    v0 += red[warp + k][(0 * 4 + r) * B + b];
-                    if constexpr (NM == 2) v1 += red[warp + k][(1 * 4 + r) * B + b];
+                for (int b = 0; b < B; ++b) {
+                    const float v = warp_sum(acc[i][b]);
+                    if (lane == 0) dst[i * B + b] = v;
+                    acc[i][b] = 0.f;
                 }
-                p.a.y[(size_t)b * p.a.y_stride + row] = n_epilogue<EPI>(v0, v1);
-            }
         }
-        __syncthreads();
+        g = g_next;
+        s = s_next;
     }
     cp_wait<0>();
+    if (tid < B) {
+        if constexpr (PRO == Pro::AddNorm) {
+            float inv[B];
+            rms_scales<B, S_WARPS>(s_ss, d_model, p.a.eps, inv);
+            s_inv[tid] = inv[tid];
+        } else {
+            s_inv[tid] = 1.f;
+        }
+    }
+    __syncthreads();
+    if constexpr (PRO == Pro::AddNorm) {
+        write_xout_slice<B, S_THREADS>(p.a, d_model, s_inv, cta, gridDim.x);
+    }
+
+    // Row groups of this CTA: sum over warps in warp order, times the RMSNorm scale.
+    const int ngc = g_hi - g_lo + 1;
+    for (int it = tid; it < ngc * 4 * B; it += S_THREADS) {
+        const int gi = it / (4 * B), rb = it - gi * (4 * B);
+        const int r = rb / B, b = rb - (rb / B) * B;
+        const int gg = g_lo + gi;
+        const int s0 = max(gg * L, u_lo) - u_lo, s1 = min((gg + 1) * L, u_hi) - u_lo;
+        float v[NM];
+#pragma unroll
+        for (int m = 0; m < NM; ++m)
+            v[m] = sum_warp_partials(red, p.slots, VPG, gg, s0, s1, n, u_lo, L, (m * 4 + r) * B + b);
+        if (!((gi == 0 && lo_shared) || (gi == ngc - 1 && hi_shared))) {
+            const int row = gg * 4 + r;
+            const float inv = s_inv[b];
+            if (row < p.rows)
+                p.a.y[(size_t)b * p.a.y_stride + row] = n_epilogue<EPI>(__fmul_rn(v[0], inv), __fmul_rn(v[NM - 1], inv));
+        } else {
+            float* dst = p.a.scratch + (2 * (size_t)cta + (gi == 0 ? 0 : 1)) * VPG;
+#pragma unroll
+            for (int m = 0; m < NM; ++m) dst[(m * 4 + r) * B + b] = v[m];
+        }
+    }
+    if (lo_shared || hi_shared) {
+        finish_shared_segments(p.a, p.map, cta, g_lo, g_hi, lo_shared, hi_shared, s_last, [&](int seg, int f, int l) {
+            for (int it = tid; it < 4 * B; it += S_THREADS) {
+                const int r = it / B, b = it - (it / B) * B;
+                float v[NM];
+#pragma unroll
+                for (int m = 0; m < NM; ++m) v[m] = 0.f;
+                for (int cc = f; cc <= l; ++cc) {
+                    const float* part = p.a.scratch + (size_t)seg_slot(p.map, cc, seg) * VPG;
+#pragma unroll
+                    for (int m = 0; m < NM; ++m) v[m] += __ldcg(part + (m * 4 + r) * B + b);
+                }
+                const int row = seg * 4 + r;
+                const float inv = s_inv[b];
+                if (row < p.rows)
+                    p.a.y[(size_t)b * p.a.y_stride + row] =
+                        n_epilogue<EPI>(__fmul_rn(v[0], inv), __fmul_rn(v[NM - 1], inv));
+            }
+        });
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -556,6 +789,50 @@ __device__ __forceinline__ void t_decode(const uint4* q, int quarter, float2* wv
     }
 }
 
+// Stores output column j of batch row b. Every lane of the warp calls it (the
+// RoPE pair partner of column j is column j ^ 1, held by the neighbouring lane).
+// RoPE coefficients (cos, sin) of output column j of batch row b (QKV epilogue;
+// columns past q and k get (1, 0)). Positions and tables are not written by
+// the step's kernels, so this may run before pdl_wait().
+__device__ __forceinline__ float2 rope_coef(const GemvArgs& a, int j, int b) {
+    const int hd = a.head_dim, nq = a.n_q_cols, nkv = a.n_kv_cols;
+    if (j >= nq + nkv) return f2(1.f, 0.f);
+    const int64_t pos = a.pos[b];
+    const int dd = (j < nq ? j : j - nq) % hd;
+    return f2(a.rope_cos[pos * hd + dd], a.rope_sin[pos * hd + dd]);
+}
+
+template <Epi EPI>
+__device__ __forceinline__ void t_store(const GemvArgs& a, float val, int j, int b, float2 cs_sn) {
+    if constexpr (EPI == Epi::Plain) {
+        a.y[(size_t)b * a.y_stride + j] = val;
+    } else {
+        // QKV epilogue: RoPE on q and k (core/Kernels.java:296-309 vector path:
+        // a' = fma(a, c, b * -s), b' = fma(b, c, a * s)), then the KV-cache
+        // append of k and v (inference/KVCache.java:79-95).
+        const int hd = a.head_dim;
+        const int nq = a.n_q_cols, nkv = a.n_kv_cols;
+        const int64_t pos = a.pos[b];
+        const float partner = __shfl_xor_sync(0xffffffffu, val, 1);
+        float out = val;
+        if (j < nq + nkv) {
+            const int dd = (j < nq ? j : j - nq) % hd;
+            const float cs = cs_sn.x, sn = cs_sn.y;
+            if ((dd & 1) == 0) out = fmaf(val, cs, __fmul_rn(partner, -sn));
+            else out = fmaf(val, cs, __fmul_rn(partner, sn));
+        }
+        if (j < nq) {
+            a.y[(size_t)b * a.y_stride + j] = out;
+        } else {
+            const bool is_k = j < nq + nkv;
+            const int jj = is_k ? j - nq : j - nq - nkv;
+            const int kvh = jj / hd, dd = jj - kvh * hd;
+            float* cache = is_k ? a.kcache : a.vcache;
+            cache[(size_t)b * a.kv_slot_stride + ((size_t)kvh * a.ctx_len + pos) * hd + dd] = out;
+        }
+    }
+}
+
 template <int QT, int B, Pro PRO, Epi EPI>
 __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
     using C = TCfg<B>;
@@ -732,35 +1009,8 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
     }
     if (b_me >= B) return;
 
-    const int j = c * 32 + cl;  // output column
-    if constexpr (EPI == Epi::Plain) {
-        p.a.y[(size_t)b_me * p.a.y_stride + j] = val;
-    } else {
-        // QKV epilogue: RoPE on q and k (core/Kernels.java:296-309 vector path:
-        // a' = fma(a, c, b * -s), b' = fma(b, c, a * s)), then the KV-cache
-        // append of k and v (inference/KVCache.java:79-95).
-        const int hd = p.a.head_dim;
-        const int nq = p.a.n_q_cols, nkv = p.a.n_kv_cols;
-        const int64_t pos = p.a.pos[b_me];
-        const float partner = __shfl_xor_sync(0xffffffffu, val, 1);
-        float out = val;
-        if (j < nq + nkv) {
-            const int dd = (j < nq ? j : j - nq) % hd;
-            const float cs = p.a.rope_cos[pos * hd + dd];
-            const float sn = p.a.rope_sin[pos * hd + dd];
-            if ((dd & 1) == 0) out = fmaf(val, cs, __fmul_rn(partner, -sn));
-            else out = fmaf(val, cs, __fmul_rn(partner, sn));
-        }
-        if (j < nq) {
-            p.a.y[(size_t)b_me * p.a.y_stride + j] = out;
-        } else {
-            const bool is_k = j < nq + nkv;
-            const int jj = is_k ? j - nq : j - nq - nkv;
-            const int kvh = jj / hd, dd = jj - kvh * hd;
-            float* cache = is_k ? p.a.kcache : p.a.vcache;
-            cache[(size_t)b_me * p.a.kv_slot_stride + ((size_t)kvh * p.a.ctx_len + pos) * hd + dd] = out;
-        }
-    }
+    const int j = c * 32 + cl;
+    t_store<EPI>(p.a, val, j, b_me, EPI == Epi::QkvRope ? rope_coef(p.a, j, b_me) : f2(1.f, 0.f));
 }
 
 // ---------------------------------------------------------------------------
@@ -808,59 +1058,91 @@ void launch(const void* fn, int grid, int smem, cudaStream_t s, bool pdl, const 
     AT_CUDA(cudaLaunchKernelExC(&cfg, fn, args));
 }
 
-// Chooses how many warps split the steps of a 4-row group (KS), and how many
-// rounds of groups each CTA (one per SM) walks, minimising the steps per warp.
-void n4_config(int ngroups, int nsteps, int num_sms, int* KS, int* gpc, int* per, int* grid, int* steps_ks) {
-    int best = -1;
-    for (int ks = 1; ks <= N4_WARPS; ks *= 2) {
-        if (ks > 1 && ks > nsteps) break;
-        const int g = N4_WARPS / ks;
-        const int ctas = (ngroups + g - 1) / g;
-        const int pr = (ctas + num_sms - 1) / num_sms;
-        const int sk = (nsteps + ks - 1) / ks;
-        const int cost = pr * sk;
-        if (best < 0 || cost < best) {
-            best = cost;
-            *KS = ks;
-            *gpc = g;
-            *per = pr;
-            *grid = (ngroups + g * pr - 1) / (g * pr);
-            *steps_ks = sk;
+// Stream plan: one CTA per SM (never more CTAs than units), the CTA unit
+// map, and the number of shared-memory partial slots per warp (segments one
+// warp's units can touch).
+struct StreamPlan {
+    int grid = 1, slots = 1, nst = 0;  // nst = ring depth, 0 = the stream kernel does not fit
+    bool aligned = false;              // CTA ranges are whole segments (nothing shared between CTAs)
+    int xbytes = 0, red_bytes = 0, smem = 0;
+    StreamMap map{};
+};
+constexpr int kStreamSmem = 220 * 1024;  // dynamic shared memory budget of the stream kernels
+// Segment-aligned CTA ranges are taken when the busiest CTA streams at most
+// kAlignSlack x the mean: they need no cross-CTA combine at the end.
+constexpr double kAlignSlack = 1.08;
+// Ring depth (units per warp in flight). Two 2304-byte units per warp keep
+// 74 KB per SM in flight; deeper rings measured slower in the decode step.
+constexpr int kMaxNst = 2;
+
+StreamPlan stream_plan(int64_t U, int64_t seg_len, int num_sms, int xbytes, int vals_per_seg, int slot_bytes,
+                       int max_nst, double slack) {
+    StreamPlan sp;
+    AT_REQUIRE(U < (int64_t(1) << 27), AT_ERR_INVALID_ARG, "matrix too large for the stream GEMV");
+    const int sms = std::min(num_sms, kMaxStreamCtas);
+    const int64_t nseg = U / seg_len;
+    // whole segments per CTA when the busiest CTA streams at most kAlignSlack x the mean
+    const int64_t ga = std::min<int64_t>(sms, nseg);
+    const double mean = (double)U / (double)std::max<int64_t>(1, std::min<int64_t>(sms, U));
+    sp.aligned = ga >= 1 && (double)((nseg + ga - 1) / ga * seg_len) <= slack * mean;
+    sp.grid = sp.aligned ? (int)ga : (int)std::max<int64_t>(1, std::min<int64_t>(sms, U));
+    sp.map.len = (int)seg_len;
+    for (int c = 0; c <= sp.grid; ++c)
+        sp.map.start[c] = sp.aligned ? (int)((int64_t)c * nseg / sp.grid * seg_len) : (int)((int64_t)c * U / sp.grid);
+    int64_t per_cta = 0;
+    for (int c = 0; c < sp.grid; ++c) per_cta = std::max<int64_t>(per_cta, sp.map.start[c + 1] - sp.map.start[c]);
+    const int64_t per_warp = (per_cta + S_WARPS - 1) / S_WARPS;
+    sp.slots = (int)((per_warp + seg_len - 1) / seg_len + 1);
+    sp.xbytes = (xbytes + 15) / 16 * 16;
+    sp.red_bytes = (S_WARPS * sp.slots * vals_per_seg * 4 + 15) / 16 * 16;
+    for (int nst = max_nst; nst >= 2; nst /= 2) {
+        const int smem = sp.xbytes + sp.red_bytes + S_WARPS * nst * slot_bytes;
+        if (smem <= kStreamSmem) {
+            sp.nst = nst;
+            sp.smem = smem;
+            break;
         }
     }
+    return sp;
+}
+
+template <int QT, int B, Epi EPI>
+StreamPlan n_stream_plan(const at_qmat* m, int num_sms) {
+    constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
+    const int nb = (int)(m->cols / QK);
+    return stream_plan(m->ngroups * m->nsteps, m->nsteps, num_sms, B * nb * XPAD * 4, NM * 4 * B,
+                       NM * NTile<QT>::BYTES, kMaxNst, kAlignSlack);
 }
 
 template <int QT, int B, Pro PRO, Epi EPI, int NST>
-void run_n4(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, bool pdl, int xbytes) {
+void run_ns(const at_qmat* m, const GemvArgs& a, const StreamPlan& sp, cudaStream_t s, bool pdl) {
     constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
-    N4Params p{};
+    NSParams p{};
     p.tiles[0] = m->tiles;
     p.tiles[1] = (NM == 2) ? a.m2->tiles : m->tiles;
     p.rows = (int)m->rows;
     p.nb = (int)(m->cols / QK);
-    p.ngroups = (int)m->ngroups;
     p.nsteps = (int)m->nsteps;
-    p.ring_off = xbytes;
+    p.slots = sp.slots;
+    p.red_off = sp.xbytes;
+    p.ring_off = sp.xbytes + sp.red_bytes;
+    p.pre = pdl ? 2 : 1;
+    p.map = sp.map;
     p.a = a;
-    int grid = 1;
-    n4_config(p.ngroups, p.nsteps, num_sms, &p.KS, &p.gpc, &p.per, &grid, &p.steps_ks);
-    const int smem = xbytes + N4_WARPS * NST * NM * NTile<QT>::BYTES;
-    const void* fn = reinterpret_cast<const void*>(&gemv_n4_kernel<QT, B, PRO, EPI, NST>);
-    ensure_smem(fn, smem);
-    launch(fn, grid, smem, s, pdl, p, N4_THREADS);
+    if (!sp.aligned && sp.grid > 1) AT_REQUIRE(a.scratch && a.counters, AT_ERR_STATE, "N GEMV needs split scratch");
+    const void* fn = reinterpret_cast<const void*>(&gemv_ns_kernel<QT, B, PRO, EPI, NST>);
+    ensure_smem(fn, sp.smem);
+    launch(fn, sp.grid, sp.smem, s, pdl, p, S_THREADS);
 }
 
 template <int QT, int B, Pro PRO, Epi EPI>
 void run_n(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, bool pdl) {
     constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
     const int nb = (int)(m->cols / QK);
-    const int xbytes = B * nb * XPAD * 4;
-    const int slot = NM * NTile<QT>::BYTES;
-    constexpr int kBudget = 200 * 1024;
     if constexpr (B <= 2) {
-        // deepest ring (4 or 2 steps per warp) that fits next to the staged x
-        if (xbytes + N4_WARPS * 4 * slot <= kBudget) { run_n4<QT, B, PRO, EPI, 4>(m, a, num_sms, s, pdl, xbytes); return; }
-        if (xbytes + N4_WARPS * 2 * slot <= kBudget) { run_n4<QT, B, PRO, EPI, 2>(m, a, num_sms, s, pdl, xbytes); return; }
+        const StreamPlan sp = n_stream_plan<QT, B, EPI>(m, num_sms);
+        if (sp.nst == 4) { run_ns<QT, B, PRO, EPI, 4>(m, a, sp, s, pdl); return; }
+        if (sp.nst == 2) { run_ns<QT, B, PRO, EPI, 2>(m, a, sp, s, pdl); return; }
     }
     constexpr int R = (NM == 2) ? 2 : 4;
     NCParams p{};
@@ -947,6 +1229,14 @@ void gemv_t_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* float
     const size_t n_bc = (size_t)(m->cols / QK);
     *floats = (S > 1) ? n_bc * S * batch * 32 : 0;
     *counters = (S > 1) ? n_bc : 0;
+}
+
+void gemv_n_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* floats, size_t* counters) {
+    // upper bound over the epilogues (gate/up pairs carry two partials per row)
+    const int64_t U = m->ngroups * m->nsteps;
+    const size_t grid = (size_t)std::max<int64_t>(1, std::min<int64_t>(num_sms, U));
+    *floats = (batch <= 2 && grid > 1) ? 2 * grid * 2 * 4 * batch : 0;
+    *counters = (batch <= 2 && grid > 1) ? (size_t)m->ngroups : 0;
 }
 
 void launch_gemv_n(const at_qmat* m, int batch, Pro pro, Epi epi, const GemvArgs& a, int num_sms,

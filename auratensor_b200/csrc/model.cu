@@ -126,10 +126,15 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
     __shared__ float s_m[G_MAX], s_l[G_MAX];
     const int kvh = blockIdx.x, chunk = blockIdx.y, b = blockIdx.z;
     const int G = Hl / Hkvl;
+    pdl_trigger();
+    // The position was advanced by an earlier step; the rows of positions
+    // before it were appended by earlier steps, so they are loaded before
+    // waiting on the QKV kernel, which appends row P - 1 and writes q.
     const int64_t P = pos[b] + 1;
     const int64_t p0 = (int64_t)chunk * CH;
     if (p0 >= P) return;
     const int n = (int)((P - p0) < CH ? (P - p0) : CH);
+    const int n_past = (p0 + n == P) ? n - 1 : n;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const float4* kbase = reinterpret_cast<const float4*>(kc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD);
     const float4* vbase = reinterpret_cast<const float4*>(vc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD);
@@ -139,7 +144,13 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
 #pragma unroll
     for (int k = 0; k < PER; ++k) {
         const int i = k * 256 + tid;
-        if (i < n * F4) { kr[k] = kbase[i]; vr[k] = vbase[i]; }
+        if (i < n_past * F4) { kr[k] = kbase[i]; vr[k] = vbase[i]; }
+    }
+    pdl_wait();
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int i = k * 256 + tid;
+        if (i >= n_past * F4 && i < n * F4) { kr[k] = kbase[i]; vr[k] = vbase[i]; }
     }
     for (int i = tid; i < G * F4; i += 256) qs[i / F4][i % F4] = qbase[i];
 #pragma unroll
@@ -202,8 +213,10 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(const float* __restric
     __shared__ float sred[HD / 32];
     __shared__ float s_M, s_L;
     const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_trigger();
     const int64_t P = pos[b] + 1;
     const int nch = (int)((P + CH - 1) / CH);
+    pdl_wait();
     const float* base = part + ((size_t)b * Hl + h) * nchunk_max * (HD + 2);
     float m = -INFINITY;
     for (int c = tid; c < nch; c += HD) {
@@ -420,6 +433,24 @@ struct ProfScope {
     }
 };
 
+// Launches kern<<<grid, block, 0, s>>>(args...), with programmatic stream
+// serialization when pdl is set (the kernel calls pdl_wait before reading
+// what the previous kernel writes).
+template <class... KArgs, class... Args>
+void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    AT_CUDA(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...));
+}
+
 void enqueue_step(at_model* m, int B) {
     at_ctx* c = m->ctx;
     cudaStream_t s = c->stream;
@@ -462,19 +493,20 @@ void enqueue_step(at_model* m, int B) {
         {
             ProfScope p(m, AT_PROF_ATTN);
             dim3 g1(m->Hkvl, m->nchunk_max, B);
+            const float* qp = m->q;
+            const int64_t* dp = m->d_pos;
             if (hd == 128)
-                attn_split_kernel<128><<<g1, 256, 0, s>>>(m->q, kc, vc, m->d_pos, m->att_part, m->Hl, m->Hkvl,
-                                                          m->ctx_len, m->slot_stride, m->nchunk_max, scale);
+                launch_k(attn_split_kernel<128>, g1, 256, s, m->pdl, qp, (const float*)kc, (const float*)vc, dp,
+                         m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max, scale);
             else
-                attn_split_kernel<64><<<g1, 256, 0, s>>>(m->q, kc, vc, m->d_pos, m->att_part, m->Hl, m->Hkvl,
-                                                         m->ctx_len, m->slot_stride, m->nchunk_max, scale);
-            AT_CUDA(cudaGetLastError());
+                launch_k(attn_split_kernel<64>, g1, 256, s, m->pdl, qp, (const float*)kc, (const float*)vc, dp,
+                         m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max, scale);
             dim3 g2(m->Hl, B);
+            const float* pp = m->att_part;
             if (hd == 128)
-                attn_combine_kernel<128><<<g2, 128, 0, s>>>(m->att_part, m->d_pos, m->att, m->Hl, m->nchunk_max);
+                launch_k(attn_combine_kernel<128>, g2, 128, s, m->pdl, pp, dp, m->att, m->Hl, m->nchunk_max);
             else
-                attn_combine_kernel<64><<<g2, 64, 0, s>>>(m->att_part, m->d_pos, m->att, m->Hl, m->nchunk_max);
-            AT_CUDA(cudaGetLastError());
+                launch_k(attn_combine_kernel<64>, g2, 64, s, m->pdl, pp, dp, m->att, m->Hl, m->nchunk_max);
         }
         {
             ProfScope p(m, AT_PROF_WO);
@@ -489,12 +521,14 @@ void enqueue_step(at_model* m, int B) {
             GemvArgs f;
             f.xin = m->xb; f.yin = m->y; f.gamma = ly.ffn_norm; f.xout = m->xa; f.eps = m->cfg.rms_norm_eps;
             f.x_stride = d; f.y = m->h; f.y_stride = m->Fl; f.m2 = &ly.w3;
+            f.scratch = m->scratch; f.counters = m->counters;
             launch_gemv_n(&ly.w1, B, Pro::AddNorm, Epi::SiluMul, f, c->num_sms, s, m->pdl);
         }
         {
             ProfScope p(m, AT_PROF_FFN_DOWN);
             GemvArgs dn;
             dn.x = m->h; dn.x_stride = m->Fl; dn.y = m->y; dn.y_stride = d;
+            dn.scratch = m->scratch; dn.counters = m->counters;
             launch_gemv_n(&ly.w2, B, Pro::Plain, Epi::Plain, dn, c->num_sms, s, m->pdl);
         }
         allreduce_y("ncclAllReduce(mlp)");
@@ -505,6 +539,7 @@ void enqueue_step(at_model* m, int B) {
         ha.xin = m->xa; ha.yin = m->y; ha.gamma = m->out_norm; ha.xout = m->xb;
         ha.eps = m->cfg.rms_norm_eps; ha.x_stride = d;
         ha.y = (c->world > 1) ? m->logits_local : m->logits; ha.y_stride = m->Vl;
+        ha.scratch = m->scratch; ha.counters = m->counters;
         launch_gemv_n(&m->out, B, Pro::AddNorm, Epi::Plain, ha, c->num_sms, s, m->pdl);
     }
     if (c->world > 1) {
@@ -905,7 +940,7 @@ int at_model_finalize(at_model* m) {
             AT_CUDA(cudaMemcpy(m->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
             AT_CUDA(cudaMemcpy(m->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
         }
-        // split scratch for the T GEMVs at every batch size
+        // split scratch for the GEMVs at every batch size (launches are serialized on the stream)
         size_t nf = 16, nc = 16;
         for (int b = 1; b <= B; ++b) {
             size_t f1, c1;
@@ -913,6 +948,10 @@ int at_model_finalize(at_model* m) {
             nf = std::max(nf, f1); nc = std::max(nc, c1);
             gemv_t_scratch_need(&m->layers[0].wo, b, c->num_sms, &f1, &c1);
             nf = std::max(nf, f1); nc = std::max(nc, c1);
+            for (const at_qmat* q : {&m->layers[0].w1, &m->layers[0].w2, &m->out}) {
+                gemv_n_scratch_need(q, b, c->num_sms, &f1, &c1);
+                nf = std::max(nf, f1); nc = std::max(nc, c1);
+            }
         }
         alloc_zero((void**)&m->scratch, nf * 4);
         alloc_zero((void**)&m->counters, nc * 4);

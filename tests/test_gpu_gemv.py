@@ -55,6 +55,19 @@ def test_kernel_sweep_shapes(qt, shape, batch, cuda):
 
 
 @pytest.mark.parametrize("qt", [ref.GGML_Q4_0, ref.GGML_Q8_0])
+@pytest.mark.parametrize("orient,rows,cols", [(ORIENT_N, 16, 14336), (ORIENT_N, 40, 8192), (ORIENT_N, 128, 4096),
+                                              (ORIENT_T, 14336, 64), (ORIENT_T, 16, 14336), (ORIENT_T, 4096, 6144)])
+@pytest.mark.parametrize("batch", [1, 2])
+def test_segments_shared_by_many_ctas(qt, orient, rows, cols, batch, cuda):
+    """Row groups (N) or block columns (T) whose tiles are spread over many
+    CTAs: their partials meet in global scratch and the last CTA to arrive
+    finishes them. Two calls in a row also check that the arrival counters
+    are reset."""
+    for seed in (11, 12):
+        check(qt, orient, rows, cols, batch, cuda, seed=seed)
+
+
+@pytest.mark.parametrize("qt", [ref.GGML_Q4_0, ref.GGML_Q8_0])
 @pytest.mark.parametrize("orient", [ORIENT_N, ORIENT_T])
 def test_planar_relayout_is_lossless(qt, orient, cuda):
     blocks, _ = make(qt, 300, 640, 3)
