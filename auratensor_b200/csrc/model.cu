@@ -81,11 +81,15 @@ constexpr int CH = 32;  // KV positions per attention CTA
 // ---------------------------------------------------------------------------
 // writeTokenEmbedding (inference/LlamaModel.java:181-186): one dequantized row
 // of token_embd into xa; y <- 0 so the first layer's prologue reads x + 0.
+// Also advances the step sequence number the tensor-parallel all-reduces
+// match on (every rank runs the same steps, so the numbers agree).
 template <int QT>
 __global__ void embed_kernel(const uint8_t* __restrict__ tiles, QTileMap map, const int* __restrict__ tokens, int d,
-                             float* __restrict__ xa, float* __restrict__ y, unsigned long long* __restrict__ argkeys) {
+                             float* __restrict__ xa, float* __restrict__ y, unsigned long long* __restrict__ argkeys,
+                             unsigned* __restrict__ step) {
     const int b = blockIdx.x;
     if (threadIdx.x == 0) argkeys[b] = 0ull;
+    if (b == 0 && threadIdx.x == 0) *step += 1u;
     const int64_t tok = tokens[b];
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
         int64_t d_off, q_off;
@@ -263,6 +267,174 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(const float* __restric
     att[(size_t)b * Hl * HD + (size_t)h * HD + tid] = __fdiv_rn(o, s_L);
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-parallel exchanges through NVLink peer memory (no NCCL inside a
+// step). Every rank owns receive areas, mapped by every other rank (CUDA IPC):
+// per exchange site one slot per rank, plus flags. A sender pushes its data
+// into slot `rank` of a peer's area with plain peer stores and, after a
+// system-scope fence, sets its flag there to the step number (release store);
+// a receiver polls only its own memory. All waits are bounded (iterations
+// and 1 s of device time); a peer that never arrives sets *err, later waits
+// are skipped, and the host fails the call.
+//   Sites 0 .. 2L-1: all-reduce of the wo / w2 outputs (B x d floats). The
+//     rank's GEMV writes its partial straight into its own slot; the sums are
+//     taken in rank order, so every rank gets bit-identical results.
+//   Site 2L: the logits shards (B x Vl floats), concatenated on every rank.
+//   Site 2L + 1: flags only, the teardown barrier.
+// A slot is written once per site and step, and a rank cannot reach the same
+// site of the next step before every rank has read it (that needs the
+// peers' data of all later sites of this step).
+// ---------------------------------------------------------------------------
+constexpr int kMaxRanks = 8;
+constexpr int kPushCtas = 8;                            // CTAs that may push to one peer (flag slots per sender)
+constexpr int kArSpinLimit = 1 << 24;                   // polls of a flag before giving up ...
+constexpr unsigned long long kArWaitNs = 1000000000ull;  // ... or 1 s of device time, whichever comes first
+
+struct ArPeers {
+    float* base[kMaxRanks];  // rank r's receive areas, mapped into this process
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Flag of (site, sender, part) inside an area base (as u32).
+__device__ __forceinline__ unsigned* flag_at(float* base, int64_t flag_off, int site, int world, int sender, int part) {
+    return reinterpret_cast<unsigned*>(base + flag_off) + ((int64_t)site * world + sender) * kPushCtas + part;
+}
+
+// After this CTA's stores to a peer: publish flag (site, rank, part) there.
+__device__ __forceinline__ void publish(float* peer_base, int64_t flag_off, int site, int world, int rank, int part,
+                                       unsigned seq) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        st_release_sys(flag_at(peer_base, flag_off, site, world, rank, part), seq);
+    }
+}
+
+// Waits (thread 0, bounded) until every peer's flags (site, r, 0..parts-1) in
+// this rank's own area reach seq; returns the CTA-wide verdict.
+__device__ __forceinline__ bool arrived(unsigned flag, unsigned seq, bool exact) {
+    return exact ? flag == seq : (int)(flag - seq) >= 0;
+}
+
+__device__ __forceinline__ bool wait_peers(float* mine, int64_t flag_off, int site, int world, int rank, int parts,
+                                           unsigned seq, int* err, int* s_ok, bool exact = false) {
+    if (threadIdx.x == 0) {
+        int ok = *reinterpret_cast<volatile int*>(err) == 0;
+        const unsigned long long t0 = global_ns();
+        for (int r = 0; r < world && ok; ++r) {
+            if (r == rank) continue;
+            for (int part = 0; part < parts && ok; ++part) {
+                const unsigned* f = flag_at(mine, flag_off, site, world, r, part);
+                int it = 0;
+                while (!arrived(ld_acquire_sys(f), seq, exact)) {
+                    if (++it > kArSpinLimit || global_ns() - t0 > kArWaitNs) {
+                        ok = 0;
+                        atomicExch(err, 1);
+                        break;
+                    }
+                    if (it > 64) __nanosleep(64);
+                }
+            }
+        }
+        *s_ok = ok;
+    }
+    __syncthreads();
+    return *s_ok != 0;
+}
+
+// All-reduce site: grid = world - 1 CTAs, CTA k pushes to peer rank + 1 + k;
+// then every CTA sums its share of the n4 float4s in rank order into out.
+__global__ void __launch_bounds__(512) allreduce_push_kernel(ArPeers peers, int world, int rank, int64_t area_off,
+                                                             int64_t slot_floats, int64_t flag_off, int site, int n4,
+                                                             const unsigned* __restrict__ step,
+                                                             float* __restrict__ out, int* __restrict__ err) {
+    pdl_trigger();
+    pdl_wait();  // this rank's partial (written by the previous kernel) is complete
+    __shared__ int s_ok;
+    const unsigned seq = *step;
+    float* mine = peers.base[rank];
+    const float4* own = reinterpret_cast<const float4*>(mine + area_off + rank * slot_floats);
+    const int k = blockIdx.x;
+    if (k < world - 1) {
+        const int peer = (rank + 1 + k) % world;
+        float4* dst = reinterpret_cast<float4*>(peers.base[peer] + area_off + rank * slot_floats);
+        for (int i = threadIdx.x; i < n4; i += blockDim.x) dst[i] = own[i];
+        publish(peers.base[peer], flag_off, site, world, rank, 0, seq);
+    }
+    if (!wait_peers(mine, flag_off, site, world, rank, 1, seq, err, &s_ok)) return;
+    const int per = (n4 + gridDim.x - 1) / gridDim.x;
+    const int i0 = k * per, i1 = min(n4, i0 + per);
+    const float4* slot0 = reinterpret_cast<const float4*>(mine + area_off);
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        float4 acc = __ldcv(slot0 + i);
+        for (int r = 1; r < world; ++r) {
+            const float4 v = __ldcv(slot0 + r * (slot_floats / 4) + i);
+            acc.x = __fadd_rn(acc.x, v.x); acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z); acc.w = __fadd_rn(acc.w, v.w);
+        }
+        reinterpret_cast<float4*>(out)[i] = acc;
+    }
+}
+
+// Logits site: grid = (world - 1) * kPushCtas CTAs; CTA k pushes part
+// k % kPushCtas of this rank's B x Vl shard to peer rank + 1 + k / kPushCtas,
+// then the CTAs assemble out[b][r * Vl + j] (j < Vl, r * Vl + j < V) from
+// the local shard and the received slots.
+__global__ void __launch_bounds__(512) gather_push_kernel(ArPeers peers, int world, int rank, int64_t area_off,
+                                                          int64_t slot_floats, int64_t flag_off, int site,
+                                                          const float* __restrict__ shard, int B, int Vl, int V,
+                                                          const unsigned* __restrict__ step, float* __restrict__ out,
+                                                          int* __restrict__ err) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ int s_ok;
+    const unsigned seq = *step;
+    float* mine = peers.base[rank];
+    const int n = B * Vl;
+    const int k = blockIdx.x;
+    {
+        const int peer = (rank + 1 + k / kPushCtas) % world, part = k % kPushCtas;
+        const int j0 = (int)((int64_t)part * n / kPushCtas), j1 = (int)((int64_t)(part + 1) * n / kPushCtas);
+        float* dst = peers.base[peer] + area_off + rank * slot_floats;
+        for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) dst[j] = shard[j];
+        publish(peers.base[peer], flag_off, site, world, rank, part, seq);
+    }
+    if (!wait_peers(mine, flag_off, site, world, rank, kPushCtas, seq, err, &s_ok)) return;
+    const int64_t total = (int64_t)B * V;
+    for (int64_t t = (int64_t)k * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int b = (int)(t / V), v = (int)(t - (t / V) * V);
+        const int r = v / Vl, j = v - r * Vl;
+        out[t] = (r == rank) ? shard[(int64_t)b * Vl + j] : __ldcv(mine + area_off + r * slot_floats + (int64_t)b * Vl + j);
+    }
+}
+
+// Teardown barrier: flags only (site 2L + 1), one CTA per peer. The flag
+// value is a fixed sentinel that only the peer's own teardown push writes, so
+// passing the barrier means the peer has made its last store into this
+// rank's areas, whatever steps either rank ran.
+constexpr unsigned kTeardownFlag = 0xC0FFEE01u;
+
+__global__ void peer_barrier_kernel(ArPeers peers, int world, int rank, int64_t flag_off, int site,
+                                    int* __restrict__ err) {
+    __shared__ int s_ok;
+    const int peer = (rank + 1 + blockIdx.x) % world;
+    publish(peers.base[peer], flag_off, site, world, rank, 0, kTeardownFlag);
+    wait_peers(peers.base[rank], flag_off, site, world, rank, 1, kTeardownFlag, err, &s_ok, true);
+}
+
 // Greedy fast path of Sampler.sample (inference/Sampler.java:56-67): the
 // first index of the maximum; a NaN never wins unless it is element 0 (then
 // the reference returns 0). Every CTA reduces a slice and folds
@@ -307,17 +479,6 @@ __global__ void argmax_index_kernel(const unsigned long long* __restrict__ keys,
     if (threadIdx.x < B) out[threadIdx.x] = key_index(keys[threadIdx.x]);
 }
 
-// All-gathered [rank][b][Vl] logits -> [b][V].
-__global__ void gather_logits_kernel(const float* __restrict__ g, float* __restrict__ out, int world, int B, int Vl,
-                                     int V) {
-    const int64_t total = (int64_t)B * V;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-        const int b = (int)(t / V), v = (int)(t - (t / V) * V);
-        const int r = v / Vl, j = v - r * Vl;
-        out[t] = g[((size_t)r * B + b) * Vl + j];
-    }
-}
-
 inline int grid_for(int64_t n, int tpb = 256) {
     int64_t g = (n + tpb - 1) / tpb;
     if (g > 65535 * 16) g = 65535 * 16;
@@ -356,12 +517,19 @@ struct at_model {
     float* out_norm = nullptr;
     // activations
     float *xa = nullptr, *xb = nullptr, *y = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
-    float *logits = nullptr, *logits_local = nullptr, *gather = nullptr, *att_part = nullptr;
+    float *logits = nullptr, *logits_local = nullptr, *att_part = nullptr;
     float *kcache = nullptr, *vcache = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
     float* scratch = nullptr;
     unsigned* counters = nullptr;
     int* d_tokens = nullptr;
     int64_t* d_pos = nullptr;
+    unsigned* d_step = nullptr;           // step sequence number (advanced by the embedding kernel)
+    // tensor parallelism: one-shot all-reduce through peer memory
+    float* ar_base = nullptr;             // this rank's receive areas [sites][world][site_floats] + flags (IPC-exported)
+    float* ar_peer[8] = {};               // every rank's ar_base, mapped into this process (own rank: ar_base)
+    int64_t ar_site_floats = 0, ar_logit_floats = 0, ar_flag_off = 0;
+    int* d_ar_err = nullptr;
+    int* h_ar_err = nullptr;              // pinned copy, read after each step
     int* d_argmax = nullptr;
     unsigned long long* d_argkey = nullptr;  // packed (value, index) max per row
     int* h_tokens = nullptr;      // pinned
@@ -455,20 +623,30 @@ void enqueue_step(at_model* m, int B) {
     at_ctx* c = m->ctx;
     cudaStream_t s = c->stream;
     const int d = m->d, hd = m->hd;
-    auto allreduce_y = [&](const char* what) {
+    // Under tensor parallelism the wo and w2 GEMVs write their partial sums
+    // into the peer-visible slot of their all-reduce site; the all-reduce
+    // kernel leaves the sum in y.
+    ArPeers peers{};
+    for (int r = 0; r < c->world && r < kMaxRanks; ++r) peers.base[r] = m->ar_peer[r];
+    auto area_off = [&](int site) -> int64_t { return (int64_t)site * c->world * m->ar_site_floats; };
+    auto proj_out = [&](int site) -> float* {
+        return (c->world > 1) ? m->ar_base + area_off(site) + (int64_t)c->rank * m->ar_site_floats : m->y;
+    };
+    auto allreduce_y = [&](int site) {
         if (c->world <= 1) return;
         ProfScope p(m, AT_PROF_COMM);
-        nccl_check(nccl().AllReduce(m->y, m->y, (size_t)B * d, ncclFloat32, ncclSum, (ncclComm_t)c->nccl_comm, s),
-                   what);
+        launch_k(allreduce_push_kernel, dim3(c->world - 1), dim3(512), s, m->pdl, peers, c->world, c->rank,
+                 area_off(site), m->ar_site_floats, m->ar_flag_off, site, B * d / 4, (const unsigned*)m->d_step,
+                 m->y, m->d_ar_err);
     };
     {
         ProfScope p(m, AT_PROF_EMBED);
         if (m->tok.type == AT_GGML_Q4_0)
             embed_kernel<AT_GGML_Q4_0><<<B, 256, 0, s>>>(m->tok.tiles, tile_map(&m->tok), m->d_tokens, d, m->xa,
-                                                          m->y, m->d_argkey);
+                                                          m->y, m->d_argkey, m->d_step);
         else
             embed_kernel<AT_GGML_Q8_0><<<B, 256, 0, s>>>(m->tok.tiles, tile_map(&m->tok), m->d_tokens, d, m->xa,
-                                                          m->y, m->d_argkey);
+                                                          m->y, m->d_argkey, m->d_step);
         AT_CUDA(cudaGetLastError());
     }
     const float scale = (float)(1.0 / std::sqrt((double)hd));
@@ -511,11 +689,11 @@ void enqueue_step(at_model* m, int B) {
         {
             ProfScope p(m, AT_PROF_WO);
             GemvArgs o;
-            o.x = m->att; o.x_stride = m->Hl * hd; o.y = m->y; o.y_stride = d;
+            o.x = m->att; o.x_stride = m->Hl * hd; o.y = proj_out(2 * L); o.y_stride = d;
             o.scratch = m->scratch; o.counters = m->counters;
             launch_gemv_t(&ly.wo, B, Pro::Plain, Epi::Plain, o, c->num_sms, s, m->pdl);
         }
-        allreduce_y("ncclAllReduce(attention)");
+        allreduce_y(2 * L);
         {
             ProfScope p(m, AT_PROF_FFN_UP);
             GemvArgs f;
@@ -527,11 +705,11 @@ void enqueue_step(at_model* m, int B) {
         {
             ProfScope p(m, AT_PROF_FFN_DOWN);
             GemvArgs dn;
-            dn.x = m->h; dn.x_stride = m->Fl; dn.y = m->y; dn.y_stride = d;
+            dn.x = m->h; dn.x_stride = m->Fl; dn.y = proj_out(2 * L + 1); dn.y_stride = d;
             dn.scratch = m->scratch; dn.counters = m->counters;
             launch_gemv_n(&ly.w2, B, Pro::Plain, Epi::Plain, dn, c->num_sms, s, m->pdl);
         }
-        allreduce_y("ncclAllReduce(mlp)");
+        allreduce_y(2 * L + 1);
     }
     {
         ProfScope p(m, AT_PROF_LM_HEAD);
@@ -544,11 +722,10 @@ void enqueue_step(at_model* m, int B) {
     }
     if (c->world > 1) {
         ProfScope p(m, AT_PROF_COMM);
-        nccl_check(nccl().AllGather(m->logits_local, m->gather, (size_t)B * m->Vl, ncclFloat32,
-                                    (ncclComm_t)c->nccl_comm, s),
-                   "ncclAllGather(logits)");
-        gather_logits_kernel<<<grid_for((int64_t)B * m->V), 256, 0, s>>>(m->gather, m->logits, c->world, B, m->Vl, m->V);
-        AT_CUDA(cudaGetLastError());
+        const int site = 2 * m->L;
+        launch_k(gather_push_kernel, dim3((c->world - 1) * kPushCtas), dim3(512), s, m->pdl, peers, c->world,
+                 c->rank, area_off(site), m->ar_logit_floats, m->ar_flag_off, site, (const float*)m->logits_local, B,
+                 m->Vl, m->V, (const unsigned*)m->d_step, m->logits, m->d_ar_err);
     }
     {
         ProfScope p(m, AT_PROF_ARGMAX);
@@ -584,6 +761,13 @@ void enqueue_generate_step(at_model* m, int) {
     AT_CUDA(cudaGetLastError());
 }
 
+// Fails the call when a tensor-parallel all-reduce gave up waiting for a peer
+// (the peer died or never reached the step); the model is unusable after it.
+void check_peer_allreduce(at_model* m) {
+    if (m->ctx->world > 1 && m->h_ar_err && *m->h_ar_err)
+        fail(AT_ERR_NCCL, "tensor-parallel all-reduce: a peer rank did not arrive within the wait limit");
+}
+
 void run_step(at_model* m, const int* tokens, const int64_t* positions, int B, float* logits_host) {
     AT_REQUIRE(m && m->finalized, AT_ERR_STATE, "model is not finalized");
     AT_REQUIRE(B >= 1 && B <= m->B, AT_ERR_INVALID_ARG, "batch exceeds the model's max_batch");
@@ -607,14 +791,36 @@ void run_step(at_model* m, const int* tokens, const int64_t* positions, int B, f
     if (logits_host)
         AT_CUDA(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * (size_t)B * m->V, cudaMemcpyDeviceToHost,
                                 c->stream));
+    if (c->world > 1)
+        AT_CUDA(cudaMemcpyAsync(m->h_ar_err, m->d_ar_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
     AT_CUDA(cudaStreamSynchronize(c->stream));
+    check_peer_allreduce(m);
     for (int b = 0; b < B; ++b) m->kv_size[b] = std::max<int64_t>(m->kv_size[b], positions[b] + 1);
 }
 
 void destroy_model(at_model* m) {
     if (!m) return;
-    cudaSetDevice(m->ctx->device);
-    cudaStreamSynchronize(m->ctx->stream);
+    at_ctx* c = m->ctx;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    if (c->world > 1 && m->ar_base) {
+        // No peer may still write into this rank's areas when they are freed:
+        // the teardown barrier completes only after every peer's last push.
+        // A peer that never arrives ends the wait at its bound instead (and
+        // the areas are then left allocated, below).
+        ArPeers peers{};
+        for (int r = 0; r < c->world; ++r) peers.base[r] = m->ar_peer[r];
+        peer_barrier_kernel<<<c->world - 1, 32, 0, c->stream>>>(peers, c->world, c->rank, m->ar_flag_off,
+                                                                2 * m->L + 1, m->d_ar_err);
+        cudaStreamSynchronize(c->stream);
+        for (int r = 0; r < c->world; ++r)
+            if (r != c->rank && m->ar_peer[r]) cudaIpcCloseMemHandle(m->ar_peer[r]);
+        int err = 0;
+        if (m->d_ar_err) cudaMemcpy(&err, m->d_ar_err, sizeof(int), cudaMemcpyDeviceToHost);
+        // After a failed wait a live peer may still push into the receive
+        // areas, so they are left allocated rather than freed under it.
+        if (err) m->ar_base = nullptr;
+    }
     for (auto& g : m->graph)
         if (g) cudaGraphExecDestroy(g);
     if (m->graph_gen) cudaGraphExecDestroy(m->graph_gen);
@@ -626,13 +832,15 @@ void destroy_model(at_model* m) {
     }
     qmat_free(&m->tok);
     qmat_free(&m->out);
-    void* bufs[] = {m->out_norm, m->xa, m->xb, m->y, m->q, m->att, m->h, m->logits, m->logits_local, m->gather,
+    void* bufs[] = {m->out_norm, m->xa, m->xb, m->y, m->q, m->att, m->h, m->logits, m->logits_local,
                     m->att_part, m->kcache, m->vcache, m->rope_cos, m->rope_sin, m->scratch, m->counters,
-                    m->d_tokens, m->d_pos, m->d_argmax, m->d_gen_out, m->d_gen_count, m->d_argkey};
+                    m->d_tokens, m->d_pos, m->d_argmax, m->d_gen_out, m->d_gen_count, m->d_argkey,
+                    m->d_step, m->ar_base, m->d_ar_err};
     for (void* p : bufs)
         if (p) cudaFree(p);
     if (m->h_tokens) cudaFreeHost(m->h_tokens);
     if (m->h_pos) cudaFreeHost(m->h_pos);
+    if (m->h_ar_err) cudaFreeHost(m->h_ar_err);
     delete m;
 }
 
@@ -881,6 +1089,46 @@ int at_model_set_tensor(at_model* m, const char* cname, int type, const void* da
     return rc;
 }
 
+// Allocates this rank's receive areas (2 all-reduce sites per layer with one
+// max-batch x dim slot per rank, the logits site with one shard slot per
+// rank, then the flags of every site plus the teardown site), exports them
+// with CUDA IPC, and maps
+// every peer's slots: the 64-byte handles travel through one ncclAllGather.
+void setup_peer_allreduce(at_model* m) {
+    at_ctx* c = m->ctx;
+    AT_REQUIRE(c->world <= kMaxRanks, AT_ERR_UNSUPPORTED, "tensor parallelism supports at most 8 ranks");
+    // sites 0..2L-1: all-reduce slots; site 2L: logits shards; site 2L+1: teardown flags
+    const int sites = 2 * m->L;
+    m->ar_site_floats = ((int64_t)m->B * m->d + 63) / 64 * 64;
+    m->ar_logit_floats = ((int64_t)m->B * m->Vl + 63) / 64 * 64;
+    m->ar_flag_off = ((int64_t)sites * m->ar_site_floats + m->ar_logit_floats) * c->world;
+    AT_REQUIRE(m->ar_logit_floats >= m->ar_site_floats, AT_ERR_UNSUPPORTED, "vocabulary shard smaller than dim");
+    const int64_t nflags = (int64_t)(sites + 2) * c->world * kPushCtas;
+    const size_t bytes = (size_t)(m->ar_flag_off + (nflags + 63) / 64 * 64) * 4;
+    alloc_zero((void**)&m->ar_base, bytes);
+    cudaIpcMemHandle_t mine;
+    AT_CUDA(cudaIpcGetMemHandle(&mine, m->ar_base));
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    uint8_t* d_h = nullptr;
+    AT_CUDA(cudaMalloc(&d_h, 64 * (size_t)(c->world + 1)));
+    AT_CUDA(cudaMemcpyAsync(d_h + 64 * c->world, &mine, 64, cudaMemcpyHostToDevice, c->stream));
+    nccl_check(nccl().AllGather(d_h + 64 * c->world, d_h, 64, ncclUint8, (ncclComm_t)c->nccl_comm, c->stream),
+               "ncclAllGather(IPC handles)");
+    std::vector<cudaIpcMemHandle_t> all(c->world);
+    AT_CUDA(cudaMemcpyAsync(all.data(), d_h, 64 * (size_t)c->world, cudaMemcpyDeviceToHost, c->stream));
+    AT_CUDA(cudaStreamSynchronize(c->stream));
+    cudaFree(d_h);
+    for (int r = 0; r < c->world; ++r) {
+        if (r == c->rank) {
+            m->ar_peer[r] = m->ar_base;
+        } else {
+            void* p = nullptr;
+            AT_CUDA(cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess));
+            m->ar_peer[r] = static_cast<float*>(p);
+        }
+    }
+}
+
 int at_model_finalize(at_model* m) {
     return guard([&] {
         AT_REQUIRE(m, AT_ERR_INVALID_ARG, "null model");
@@ -914,7 +1162,6 @@ int at_model_finalize(at_model* m) {
         alloc_zero((void**)&m->logits, (size_t)B * m->V * 4);
         if (c->world > 1) {
             alloc_zero((void**)&m->logits_local, (size_t)B * m->Vl * 4);
-            alloc_zero((void**)&m->gather, (size_t)c->world * B * m->Vl * 4);
         }
         m->nchunk_max = (m->ctx_len + CH - 1) / CH;
         alloc_zero((void**)&m->att_part, (size_t)B * m->Hl * m->nchunk_max * (hd + 2) * 4);
@@ -957,6 +1204,11 @@ int at_model_finalize(at_model* m) {
         alloc_zero((void**)&m->counters, nc * 4);
         alloc_zero((void**)&m->d_tokens, 8 * sizeof(int));
         alloc_zero((void**)&m->d_pos, 8 * sizeof(int64_t));
+        alloc_zero((void**)&m->d_step, sizeof(unsigned));
+        alloc_zero((void**)&m->d_ar_err, sizeof(int));
+        AT_CUDA(cudaMallocHost(&m->h_ar_err, sizeof(int)));
+        *m->h_ar_err = 0;
+        if (c->world > 1) setup_peer_allreduce(m);
         alloc_zero((void**)&m->d_argmax, 8 * sizeof(int));
         alloc_zero((void**)&m->d_argkey, 8 * sizeof(unsigned long long));
         alloc_zero((void**)&m->d_gen_out, (size_t)m->ctx_len * sizeof(int));
@@ -1126,10 +1378,13 @@ int at_model_generate(at_model* m, int first_token, int64_t start_pos, int n_ste
         if (!m->graph_gen) m->graph_gen = capture(m, enqueue_generate_step, 1);
         for (int i = 0; i < n_steps; ++i) AT_CUDA(cudaGraphLaunch(m->graph_gen, c->stream));
         m->kv_size[0] = std::max<int64_t>(m->kv_size[0], start_pos + n_steps);
+        if (c->world > 1)
+            AT_CUDA(cudaMemcpyAsync(m->h_ar_err, m->d_ar_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
         if (tokens_out_host) {
             AT_CUDA(cudaMemcpyAsync(tokens_out_host, m->d_gen_out, sizeof(int) * n_steps, cudaMemcpyDeviceToHost,
                                     c->stream));
             AT_CUDA(cudaStreamSynchronize(c->stream));
+            check_peer_allreduce(m);
         }
     });
 }
@@ -1164,7 +1419,10 @@ int at_model_profile_step(at_model* m, int token, int64_t position, float* class
             m->pdl = true;
         }
         AT_CUDA(cudaGraphLaunch(m->graph_prof, c->stream));
+        if (c->world > 1)
+            AT_CUDA(cudaMemcpyAsync(m->h_ar_err, m->d_ar_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
         AT_CUDA(cudaStreamSynchronize(c->stream));
+        check_peer_allreduce(m);
         for (int k = 0; k < AT_PROF_CLASSES; ++k) { class_ms[k] = 0.f; class_launches[k] = 0; }
         for (size_t i = 0; i < m->prof_cls.size(); ++i) {
             float ms = 0.f;
