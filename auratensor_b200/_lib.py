@@ -90,6 +90,7 @@ SIGNATURES = {
     "at_qmat_export": [_vp, _vp, _vp],
     "at_gemv": [_vp, _vp, _vp, _vp, _i],
     "at_gemv_t_static_scratch": [_vp, _vp, _vp, _vp, _i],
+    "at_gemm_tc": [_vp, _vp, _vp, _vp, _i],
     "at_sgemv": [_vp, _vp, _vp, _vp, _i, _i],
     "at_sgemm": [_vp, _vp, _vp, _vp, _i, _i, _i],
     "at_rmsnorm": [_vp, _vp, _vp, _f, _i, _i],

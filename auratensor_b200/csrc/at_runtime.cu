@@ -558,6 +558,29 @@ int at_gemv(at_ctx* ctx, const at_qmat* m, const float* x, float* y, int batch) 
     });
 }
 
+int at_gemm_tc(at_ctx* ctx, const at_qmat* m, const float* x, float* y, int tokens) {
+    return guard([&] {
+        AT_REQUIRE(ctx && m && x && y, AT_ERR_INVALID_ARG, "null argument");
+        AT_REQUIRE(tokens >= 1, AT_ERR_INVALID_ARG, "tokens must be positive");
+        AT_REQUIRE(m->type == AT_GGML_Q4_0 || m->type == AT_GGML_Q8_0, AT_ERR_UNSUPPORTED,
+                   "tensor-core GEMM supports Q4_0 and Q8_0");
+        const int64_t in = (m->orient == AT_ORIENT_N) ? m->cols : m->rows;
+        const int64_t outn = (m->orient == AT_ORIENT_N) ? m->rows : m->cols;
+        AT_CUDA(cudaSetDevice(ctx->device));
+        static int* d_err[64] = {};
+        AT_REQUIRE(ctx->device < 64, AT_ERR_INVALID_ARG, "device index");
+        if (!d_err[ctx->device]) {
+            AT_CUDA(cudaMalloc(&d_err[ctx->device], sizeof(int)));
+            AT_CUDA(cudaMemset(d_err[ctx->device], 0, sizeof(int)));
+        }
+        launch_gemm_tc(m, x, (int)in, y, (int)outn, tokens, d_err[ctx->device], ctx->stream);
+        int err = 0;
+        AT_CUDA(cudaMemcpyAsync(&err, d_err[ctx->device], sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+        AT_CUDA(cudaStreamSynchronize(ctx->stream));
+        AT_REQUIRE(err == 0, AT_ERR_CUDA, "tensor-core GEMM: an mbarrier wait ran out");
+    });
+}
+
 int at_sgemv(at_ctx* ctx, const float* A, const float* x, float* y, int M, int K) {
     return guard([&] {
         AT_REQUIRE(ctx && A && x && y, AT_ERR_INVALID_ARG, "sgemv: null argument");

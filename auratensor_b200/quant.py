@@ -117,6 +117,16 @@ class QMatrix:
         call("at_gemv", context(self.device), self._h, ptr(x2), ptr(y), b)
         return y
 
+    def gemm(self, x: torch.Tensor, y: torch.Tensor | None = None) -> torch.Tensor:
+        """Prompt-chunk GEMM on the tensor cores: x [tokens][in] float32 CUDA
+        tensor -> y [tokens][out], bf16 operands with FP32 sums."""
+        x2 = x.reshape(-1, self.in_features).contiguous()
+        t = x2.shape[0]
+        if y is None:
+            y = torch.empty((t, self.out_features), dtype=torch.float32, device=x.device)
+        call("at_gemm_tc", context(self.device), self._h, ptr(x2), ptr(y), t)
+        return y
+
     def export_blocks(self) -> torch.Tensor:
         bpb = QuantBlock.bytesPerBlock(self.type)
         out = torch.empty(self.rows * (self.cols // 32) * bpb, dtype=torch.uint8, device=f"cuda:{self.device}")

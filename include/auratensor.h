@@ -120,6 +120,13 @@ int at_gemv(at_ctx* ctx, const at_qmat* m, const float* x_dev, float* y_dev, int
  * reference. m must be stored for AT_ORIENT_T. */
 int at_gemv_t_static_scratch(at_ctx* ctx, const at_qmat* m, const float* x_dev, float* y_dev, int batch);
 
+/* Prompt-chunk GEMM on the tensor cores: y[t][:] = W x[t][:] for t < tokens,
+ * with the weights dequantized to bf16 and x rounded to bf16, FP32 sums
+ * (the forwardPrompt path, inference/LlamaModel.java:166-175, whose
+ * tolerance is 2e-2 of the logit range). x: [tokens][in], y: [tokens][out],
+ * device FP32; in must be a multiple of 64; any orientation, Q4_0 or Q8_0. */
+int at_gemm_tc(at_ctx* ctx, const at_qmat* m, const float* x_dev, float* y_dev, int tokens);
+
 /* ---- Kernels (core/Kernels.java), FP32 device buffers ----------------------- */
 /* Kernels.sgemv(MemorySegment a,x,y,int M,int K)  (core/Kernels.java:350-371) */
 int at_sgemv(at_ctx* ctx, const float* a_dev, const float* x_dev, float* y_dev, int M, int K);

@@ -1,0 +1,48 @@
+"""Tensor-core (tcgen05) prompt GEMM vs the oracle's dequantized FP32 product.
+
+The GEMM rounds the dequantized weights and the activations to bf16 and sums
+in FP32, so each output may differ from the FP32 oracle by about two bf16
+roundings per product: the bound is 8e-3 x sum_k |w_k x_k| (2^-8 is the
+relative error of a product of two bf16-rounded factors, plus margin); the
+model-level prompt tolerance is 2e-2 of the logit range.
+"""
+import numpy as np
+import pytest
+import torch
+
+from auratensor_b200 import synth
+from auratensor_b200.quant import ORIENT_N, ORIENT_T, QMatrix
+from oracle import ref
+
+pytestmark = pytest.mark.gpu
+TOL = 8e-3
+
+
+def check(qt, orient, rows, cols, tokens, cuda, seed=0):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal(rows * cols) * 0.02).astype(np.float32)
+    blocks = synth.quantize(w, qt)
+    W = ref.dequant(qt, blocks, rows * cols).reshape(rows, cols).astype(np.float64)
+    m = QMatrix(qt, orient, rows, cols, torch.from_numpy(blocks).to(cuda))
+    n_in = cols if orient == ORIENT_N else rows
+    x = rng.standard_normal((tokens, n_in)).astype(np.float32)
+    y = m.gemm(torch.from_numpy(x).to(cuda)).cpu().numpy()
+    Wo = W if orient == ORIENT_N else W.T  # [out][in]
+    want = x.astype(np.float64) @ Wo.T
+    bound = TOL * (np.abs(x).astype(np.float64) @ np.abs(Wo.T)) + 1e-30
+    err = np.abs(y - want)
+    assert np.all(err <= bound), (float(err.max()), float((err / bound).max()))
+
+
+@pytest.mark.parametrize("qt", [ref.GGML_Q4_0, ref.GGML_Q8_0])
+@pytest.mark.parametrize("orient", [ORIENT_N, ORIENT_T])
+@pytest.mark.parametrize("tokens", [1, 37, 128, 200])
+def test_gemm_tc_small(qt, orient, tokens, cuda):
+    check(qt, orient, 256, 128, tokens, cuda, seed=tokens)
+
+
+@pytest.mark.parametrize("qt", [ref.GGML_Q4_0, ref.GGML_Q8_0])
+@pytest.mark.parametrize("orient,rows,cols", [(ORIENT_N, 300, 640), (ORIENT_N, 1000, 256), (ORIENT_T, 640, 416),
+                                              (ORIENT_T, 4096, 1024)])
+def test_gemm_tc_ragged(qt, orient, rows, cols, cuda):
+    check(qt, orient, rows, cols, 130, cuda, seed=rows + cols)
