@@ -123,6 +123,12 @@ __device__ __forceinline__ void block_rms_inv(const float* __restrict__ xin, con
     __syncthreads();
 }
 
+// Kernels.siluInPlace then elementwiseMul (core/Kernels.java:86-87,
+// inference/LlamaModel.java:372-380): g / (1 + exp(-g)) * u.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
 // (x * invRms) * gamma, in that rounding order (core/Kernels.java:145).
 __device__ __forceinline__ float norm_apply(float x, float inv, float g) {
     return __fmul_rn(__fmul_rn(x, inv), g);

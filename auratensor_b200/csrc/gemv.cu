@@ -211,9 +211,7 @@ __device__ __forceinline__ void write_xout_slice(const GemvArgs& a, int d, const
 template <Epi EPI>
 __device__ __forceinline__ float n_epilogue(float g, float u) {
     if constexpr (EPI == Epi::SiluMul) {
-        // Kernels.siluInPlace then elementwiseMul (core/Kernels.java:86-87,
-        // inference/LlamaModel.java:372-380): g / (1 + exp(-g)) * u
-        return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+        return silu_mul(g, u);
     } else {
         return g;
     }

@@ -88,8 +88,8 @@ __global__ void embed_kernel(const uint8_t* __restrict__ tiles, QTileMap map, co
                              float* __restrict__ xa, float* __restrict__ y, unsigned long long* __restrict__ argkeys,
                              unsigned* __restrict__ step) {
     const int b = blockIdx.x;
-    if (threadIdx.x == 0) argkeys[b] = 0ull;
-    if (b == 0 && threadIdx.x == 0) *step += 1u;
+    if (threadIdx.x == 0 && argkeys) argkeys[b] = 0ull;
+    if (b == 0 && threadIdx.x == 0 && step) *step += 1u;
     const int64_t tok = tokens[b];
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
         int64_t d_off, q_off;
@@ -479,6 +479,70 @@ __global__ void argmax_index_kernel(const unsigned long long* __restrict__ keys,
     if (threadIdx.x < B) out[threadIdx.x] = key_index(keys[threadIdx.x]);
 }
 
+// ---------------------------------------------------------------------------
+// Batched prompt kernels (one row per prompt token)
+// ---------------------------------------------------------------------------
+// Row-wise x_out = rmsNorm(x_in + y_in) * gamma with the reference's rounding
+// (the F7 residual stream): one CTA per row.
+__global__ void __launch_bounds__(256) rows_addnorm_kernel(const float* __restrict__ xin, const float* __restrict__ yin,
+                                                           const float* __restrict__ gamma, float* __restrict__ xout,
+                                                           int d, float eps) {
+    __shared__ float s_red[8];
+    const size_t row = blockIdx.x;
+    const float* a = xin + row * d;
+    const float* b = yin + row * d;
+    float acc = 0.f;
+    for (int i = threadIdx.x; i < d; i += 256) {
+        const float t = __fadd_rn(a[i], b[i]);
+        acc = fmaf(t, t, acc);
+    }
+    acc = warp_sum(acc);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) tot += s_red[w];
+    const float inv = rms_inv(tot, d, eps);
+    for (int i = threadIdx.x; i < d; i += 256) xout[row * d + i] = norm_apply(__fadd_rn(a[i], b[i]), inv, gamma[i]);
+}
+
+// RoPE of q and k (core/Kernels.java:296-309: a' = fma(a, c, b * -s),
+// b' = fma(b, c, a * s)) and the KV-cache append (inference/KVCache.java:79-95)
+// of prompt row t at position p0 + t; q goes to q_out [T][nq].
+__global__ void __launch_bounds__(256) rope_append_kernel(const float* __restrict__ qkv, int qcols,
+                                                          float* __restrict__ q_out, float* __restrict__ kc,
+                                                          float* __restrict__ vc, const float* __restrict__ rcos,
+                                                          const float* __restrict__ rsin, int hd, int nq, int nkv,
+                                                          int ctx, int64_t p0) {
+    const int t = blockIdx.x;
+    const int64_t pos = p0 + t;
+    const float* row = qkv + (size_t)t * qcols;
+    for (int j = threadIdx.x; j < qcols; j += 256) {
+        const float val = row[j];
+        if (j < nq + nkv) {
+            const int dd = (j < nq ? j : j - nq) % hd;
+            const float partner = row[j ^ 1];
+            const float cs = rcos[pos * hd + dd], sn = rsin[pos * hd + dd];
+            const float out = ((dd & 1) == 0) ? fmaf(val, cs, __fmul_rn(partner, -sn)) : fmaf(val, cs, __fmul_rn(partner, sn));
+            if (j < nq) {
+                q_out[(size_t)t * nq + j] = out;
+            } else {
+                const int jj = j - nq, kvh = jj / hd;
+                kc[((size_t)kvh * ctx + pos) * hd + dd] = out;
+            }
+        } else {
+            const int jj = j - nq - nkv, kvh = jj / hd, dd = jj - kvh * hd;
+            vc[((size_t)kvh * ctx + pos) * hd + dd] = val;
+        }
+    }
+}
+
+// h = silu(g) * u elementwise (in place in g).
+__global__ void silu_mul_kernel(float* __restrict__ g, const float* __restrict__ u, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        g[i] = silu_mul(g[i], u[i]);
+}
+
 inline int grid_for(int64_t n, int tpb = 256) {
     int64_t g = (n + tpb - 1) / tpb;
     if (g > 65535 * 16) g = 65535 * 16;
@@ -530,6 +594,14 @@ struct at_model {
     int64_t ar_site_floats = 0, ar_logit_floats = 0, ar_flag_off = 0;
     int* d_ar_err = nullptr;
     int* h_ar_err = nullptr;              // pinned copy, read after each step
+    // batched prompt chunks (allocated on the first forwardPrompt that uses them)
+    float *pf_xa = nullptr, *pf_xb = nullptr, *pf_y = nullptr, *pf_qkv = nullptr, *pf_q = nullptr;
+    float *pf_att = nullptr, *pf_g = nullptr, *pf_u = nullptr, *pf_part = nullptr;
+    int* pf_tok = nullptr;
+    int64_t* pf_pos = nullptr;
+    int* pf_err = nullptr;
+    int* h_pf_tok = nullptr;              // pinned
+    int64_t* h_pf_pos = nullptr;          // pinned
     int* d_argmax = nullptr;
     unsigned long long* d_argkey = nullptr;  // packed (value, index) max per row
     int* h_tokens = nullptr;      // pinned
@@ -835,12 +907,15 @@ void destroy_model(at_model* m) {
     void* bufs[] = {m->out_norm, m->xa, m->xb, m->y, m->q, m->att, m->h, m->logits, m->logits_local,
                     m->att_part, m->kcache, m->vcache, m->rope_cos, m->rope_sin, m->scratch, m->counters,
                     m->d_tokens, m->d_pos, m->d_argmax, m->d_gen_out, m->d_gen_count, m->d_argkey,
-                    m->d_step, m->ar_base, m->d_ar_err};
+                    m->d_step, m->ar_base, m->d_ar_err, m->pf_xa, m->pf_xb, m->pf_y, m->pf_qkv, m->pf_q,
+                    m->pf_att, m->pf_g, m->pf_u, m->pf_part, m->pf_tok, m->pf_pos, m->pf_err};
     for (void* p : bufs)
         if (p) cudaFree(p);
     if (m->h_tokens) cudaFreeHost(m->h_tokens);
     if (m->h_pos) cudaFreeHost(m->h_pos);
     if (m->h_ar_err) cudaFreeHost(m->h_ar_err);
+    if (m->h_pf_tok) cudaFreeHost(m->h_pf_tok);
+    if (m->h_pf_pos) cudaFreeHost(m->h_pf_pos);
     delete m;
 }
 
@@ -1341,12 +1416,124 @@ int at_model_forward_step(at_model* m, int token, int64_t position, float* logit
     return guard([&] { run_step(m, &token, &position, 1, logits_host); });
 }
 
+// Prompt chunks of up to PF_T tokens go through every layer together: the
+// projections are tensor-core GEMMs (bf16 operands, FP32 sums; the prompt
+// path's tolerance is 2e-2 of the logit range), attention runs one row per
+// token against the growing KV cache of slot 0. Only the KV cache carries
+// over to the decode steps, so the last layer's feed-forward and the lm_head
+// are not needed; they are skipped.
+constexpr int PF_T = 128;
+
+bool prompt_batched_ok(const at_model* m) {
+    if (m->ctx->world != 1) return false;
+    if (m->hd != 64 && m->hd != 128) return false;
+    if (m->d % 64 || (m->Hl * m->hd) % 64 || m->Fl % 64) return false;
+    for (const auto& ly : m->layers)
+        for (const at_qmat* q : {&ly.qkv, &ly.wo, &ly.w1, &ly.w3, &ly.w2})
+            if (q->type != AT_GGML_Q4_0 && q->type != AT_GGML_Q8_0) return false;
+    return m->tok.type == AT_GGML_Q4_0 || m->tok.type == AT_GGML_Q8_0;
+}
+
+void ensure_prompt_buffers(at_model* m) {
+    if (m->pf_xa) return;
+    const int64_t d = m->d, qcols = (int64_t)(m->Hl + 2 * m->Hkvl) * m->hd, nq = (int64_t)m->Hl * m->hd;
+    alloc_zero((void**)&m->pf_xa, PF_T * d * 4);
+    alloc_zero((void**)&m->pf_xb, PF_T * d * 4);
+    alloc_zero((void**)&m->pf_y, PF_T * d * 4);
+    alloc_zero((void**)&m->pf_qkv, PF_T * qcols * 4);
+    alloc_zero((void**)&m->pf_q, PF_T * nq * 4);
+    alloc_zero((void**)&m->pf_att, PF_T * nq * 4);
+    alloc_zero((void**)&m->pf_g, PF_T * (int64_t)m->Fl * 4);
+    alloc_zero((void**)&m->pf_u, PF_T * (int64_t)m->Fl * 4);
+    alloc_zero((void**)&m->pf_part, PF_T * (int64_t)m->Hl * m->nchunk_max * (m->hd + 2) * 4);
+    alloc_zero((void**)&m->pf_tok, PF_T * sizeof(int));
+    alloc_zero((void**)&m->pf_pos, PF_T * sizeof(int64_t));
+    alloc_zero((void**)&m->pf_err, sizeof(int));
+    AT_CUDA(cudaMallocHost(&m->h_pf_tok, PF_T * sizeof(int)));
+    AT_CUDA(cudaMallocHost(&m->h_pf_pos, PF_T * sizeof(int64_t)));
+}
+
+void run_prompt_batched(at_model* m, const int* tokens, int n) {
+    at_ctx* c = m->ctx;
+    cudaStream_t s = c->stream;
+    AT_CUDA(cudaSetDevice(c->device));
+    ensure_prompt_buffers(m);
+    const int d = m->d, hd = m->hd;
+    const int nq = m->Hl * hd, nkv = m->Hkvl * hd, qcols = nq + 2 * nkv;
+    const float eps = m->cfg.rms_norm_eps;
+    const float scale = (float)(1.0 / std::sqrt((double)hd));
+    const size_t layer_kv = (size_t)m->Hkvl * m->ctx_len * hd;
+    for (int p0 = 0; p0 < n; p0 += PF_T) {
+        const int T = std::min(PF_T, n - p0);
+        AT_CUDA(cudaStreamSynchronize(s));  // the pinned staging buffers are free again
+        for (int t = 0; t < T; ++t) {
+            m->h_pf_tok[t] = tokens[p0 + t];
+            m->h_pf_pos[t] = p0 + t;
+        }
+        AT_CUDA(cudaMemcpyAsync(m->pf_tok, m->h_pf_tok, sizeof(int) * T, cudaMemcpyHostToDevice, s));
+        AT_CUDA(cudaMemcpyAsync(m->pf_pos, m->h_pf_pos, sizeof(int64_t) * T, cudaMemcpyHostToDevice, s));
+        if (m->tok.type == AT_GGML_Q4_0)
+            embed_kernel<AT_GGML_Q4_0><<<T, 256, 0, s>>>(m->tok.tiles, tile_map(&m->tok), m->pf_tok, d, m->pf_xa,
+                                                          m->pf_y, nullptr, nullptr);
+        else
+            embed_kernel<AT_GGML_Q8_0><<<T, 256, 0, s>>>(m->tok.tiles, tile_map(&m->tok), m->pf_tok, d, m->pf_xa,
+                                                          m->pf_y, nullptr, nullptr);
+        AT_CUDA(cudaGetLastError());
+        for (int L = 0; L < m->L; ++L) {
+            Layer& ly = m->layers[L];
+            float* kc = m->kcache + L * layer_kv;  // slot 0
+            float* vc = m->vcache + L * layer_kv;
+            // attention block: xb = norm(xa + y); q, k, v; RoPE + append; attention; y = wo att
+            rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xa, m->pf_y, ly.attn_norm, m->pf_xb, d, eps);
+            AT_CUDA(cudaGetLastError());
+            launch_gemm_tc(&ly.qkv, m->pf_xb, d, m->pf_qkv, qcols, T, m->pf_err, s);
+            rope_append_kernel<<<T, 256, 0, s>>>(m->pf_qkv, qcols, m->pf_q, kc, vc, m->rope_cos, m->rope_sin, hd, nq,
+                                                 nkv, m->ctx_len, p0);
+            AT_CUDA(cudaGetLastError());
+            dim3 g1(m->Hkvl, m->nchunk_max, T), g2(m->Hl, T);
+            if (hd == 128) {
+                attn_split_kernel<128><<<g1, 256, 0, s>>>(m->pf_q, kc, vc, m->pf_pos, m->pf_part, m->Hl, m->Hkvl,
+                                                          m->ctx_len, 0, m->nchunk_max, scale);
+                attn_combine_kernel<128><<<g2, 128, 0, s>>>(m->pf_part, m->pf_pos, m->pf_att, m->Hl, m->nchunk_max);
+            } else {
+                attn_split_kernel<64><<<g1, 256, 0, s>>>(m->pf_q, kc, vc, m->pf_pos, m->pf_part, m->Hl, m->Hkvl,
+                                                         m->ctx_len, 0, m->nchunk_max, scale);
+                attn_combine_kernel<64><<<g2, 64, 0, s>>>(m->pf_part, m->pf_pos, m->pf_att, m->Hl, m->nchunk_max);
+            }
+            AT_CUDA(cudaGetLastError());
+            if (L == m->L - 1) break;  // later layers' inputs only; the KV cache is complete
+            launch_gemm_tc(&ly.wo, m->pf_att, nq, m->pf_y, d, T, m->pf_err, s);
+            // feed-forward block: xa = norm(xb + y); h = silu(w1 xa) * (w3 xa); y = w2 h
+            rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xb, m->pf_y, ly.ffn_norm, m->pf_xa, d, eps);
+            AT_CUDA(cudaGetLastError());
+            launch_gemm_tc(&ly.w1, m->pf_xa, d, m->pf_g, m->Fl, T, m->pf_err, s);
+            launch_gemm_tc(&ly.w3, m->pf_xa, d, m->pf_u, m->Fl, T, m->pf_err, s);
+            silu_mul_kernel<<<grid_for((int64_t)T * m->Fl), 256, 0, s>>>(m->pf_g, m->pf_u, (int64_t)T * m->Fl);
+            AT_CUDA(cudaGetLastError());
+            launch_gemm_tc(&ly.w2, m->pf_g, m->Fl, m->pf_y, d, T, m->pf_err, s);
+        }
+    }
+    int err = 0;
+    AT_CUDA(cudaMemcpyAsync(&err, m->pf_err, sizeof(int), cudaMemcpyDeviceToHost, s));
+    AT_CUDA(cudaStreamSynchronize(s));
+    AT_REQUIRE(err == 0, AT_ERR_CUDA, "prompt GEMM: an mbarrier wait ran out");
+    m->kv_size[0] = std::max<int64_t>(m->kv_size[0], n);
+}
+
 int at_model_forward_prompt(at_model* m, const int* tokens, int n) {
     return guard([&] {
         AT_REQUIRE(m && (n == 0 || tokens), AT_ERR_INVALID_ARG, "null argument");
         // LlamaModel.forwardPrompt (inference/LlamaModel.java:167-170)
         AT_REQUIRE(n >= 0 && n < m->ctx_len, AT_ERR_INVALID_ARG,
                    "Prompt length " + std::to_string(n) + " exceeds contextLength " + std::to_string(m->ctx_len));
+        AT_REQUIRE(m->finalized, AT_ERR_STATE, "model is not finalized");
+        for (int i = 0; i < n; ++i)
+            AT_REQUIRE(tokens[i] >= 0 && tokens[i] < m->V, AT_ERR_INVALID_ARG,
+                       "token id " + std::to_string(tokens[i]) + " out of range");
+        if (n > 1 && prompt_batched_ok(m)) {
+            run_prompt_batched(m, tokens, n);
+            return;
+        }
         for (int i = 0; i < n; ++i) {
             const int64_t p = i;
             run_step(m, tokens + i, &p, 1, nullptr);
