@@ -567,13 +567,28 @@ int at_gemm_tc(at_ctx* ctx, const at_qmat* m, const float* x, float* y, int toke
         const int64_t in = (m->orient == AT_ORIENT_N) ? m->cols : m->rows;
         const int64_t outn = (m->orient == AT_ORIENT_N) ? m->rows : m->cols;
         AT_CUDA(cudaSetDevice(ctx->device));
+        // per-device error word and bf16 staging buffer, grown on demand (calls are stream-serialized)
+        static std::mutex mu;
         static int* d_err[64] = {};
+        static void* xbf[64] = {};
+        static size_t xbf_bytes[64] = {};
         AT_REQUIRE(ctx->device < 64, AT_ERR_INVALID_ARG, "device index");
-        if (!d_err[ctx->device]) {
-            AT_CUDA(cudaMalloc(&d_err[ctx->device], sizeof(int)));
-            AT_CUDA(cudaMemset(d_err[ctx->device], 0, sizeof(int)));
+        const size_t need = (size_t)tokens * in * 2;
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            if (!d_err[ctx->device]) {
+                AT_CUDA(cudaMalloc(&d_err[ctx->device], sizeof(int)));
+                AT_CUDA(cudaMemset(d_err[ctx->device], 0, sizeof(int)));
+            }
+            if (xbf_bytes[ctx->device] < need) {
+                AT_CUDA(cudaStreamSynchronize(ctx->stream));
+                if (xbf[ctx->device]) cudaFree(xbf[ctx->device]);
+                AT_CUDA(cudaMalloc(&xbf[ctx->device], need));
+                xbf_bytes[ctx->device] = need;
+            }
         }
-        launch_gemm_tc(m, x, (int)in, y, (int)outn, tokens, d_err[ctx->device], ctx->stream);
+        launch_gemm_tc(m, x, (int)in, y, (int)outn, tokens, xbf[ctx->device], xbf_bytes[ctx->device],
+                       d_err[ctx->device], ctx->stream);
         int err = 0;
         AT_CUDA(cudaMemcpyAsync(&err, d_err[ctx->device], sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
         AT_CUDA(cudaStreamSynchronize(ctx->stream));

@@ -13,18 +13,27 @@
 // CTA tile: 128 outputs (MMA M) x 128 tokens (MMA N), K in steps of 64.
 // Both operands are K-major in the canonical 128-byte-swizzled layout: row r
 // of a tile is 128 bytes (64 bf16) at (r / 8) * 1024 + (r % 8) * 128, and
-// its 16-byte chunk c is stored at chunk position c ^ (r % 8). One elected
-// thread issues four tcgen05.mma (K = 16 each) per step and commits them to
-// the stage's mbarrier; two stages let the warps dequantize step s + 1 while
-// the tensor core works on step s. The 128 x 128 FP32 accumulator lives in
-// 128 TMEM columns; the epilogue reads it with tcgen05.ld (warp w reads TMEM
-// lanes 32 (w % 4) ..) and stores FP32 rows of Y.
+// its 16-byte chunk c is stored at chunk position c ^ (r % 8). The token
+// tile (bf16 activations) arrives by TMA (cp.async.bulk.tensor with the
+// 128-byte swizzle, rows past the last token zero-filled), one step ahead,
+// completing on the stage's "full" mbarrier; the weight tile is dequantized
+// by all 8 warps from raw block bytes loaded into registers three steps ahead.
+// One thread issues four tcgen05.mma (K = 16 each) per step and commits them
+// to the stage's "empty" mbarrier; three stages keep the TMA, the dequant and
+// the tensor core working on different steps. The 128 x 128 FP32 accumulator
+// lives in 128 TMEM columns; the epilogue reads it with tcgen05.ld (warp w
+// reads TMEM lanes 32 (w % 4) ..) and stores FP32 rows of Y.
 //
 // Every wait on an mbarrier is bounded; a wait that runs out records an error
 // code, stops issuing, and the CTA still frees its TMEM before returning.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cstdint>
+#include <mutex>
+#include <string>
 
 #include "at_internal.h"
 #include "dev_common.cuh"
@@ -38,7 +47,7 @@ constexpr int TC_N = 128;        // tokens per CTA (MMA N)
 constexpr int TC_K = 64;         // K per pipeline step (one 128-byte swizzle row)
 constexpr int TC_THREADS = 256;  // 8 warps
 constexpr int TC_TILE_BYTES = TC_M * TC_K * 2;  // 16 KB per operand tile (TC_N == TC_M)
-constexpr int TC_STAGES = 2;
+constexpr int TC_STAGES = 3;
 constexpr int TC_SMEM = TC_STAGES * 2 * TC_TILE_BYTES + 1024;  // + alignment slack
 constexpr uint32_t TC_TMEM_COLS = 128;
 constexpr int kTcSpinLimit = 1 << 26;
@@ -130,126 +139,107 @@ struct TcParams {
     int M;        // outputs
     int K;        // inputs (multiple of 64)
     int T;        // tokens
-    const float* x;  // [T][x_stride]
-    int x_stride;
-    float* y;        // [T][y_stride]
+    float* y;     // [T][y_stride]
     int y_stride;
     int* err;
 };
 
-// Dequantizes W[m0 .. m0+127][k0 .. k0+63] into a swizzled bf16 tile.
-__device__ __forceinline__ void fill_a(uint8_t* tile, const TcParams& p, int m0, int k0) {
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// TMA: box {64 k, 128 tokens} at (k0, t0) of the bf16 activations -> swizzled smem tile.
+__device__ __forceinline__ void tma_load_x(uint32_t dst, const CUtensorMap* map, int k0, int t0, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(k0), "r"(t0), "r"(bar)
+        : "memory");
+}
+
+// Raw bytes of the one block a thread dequantizes per step (scale + 16 or 32 quant bytes).
+struct RawBlock {
+    uint4 q0, q1;
+    uint32_t d;
+};
+
+// Step k0: N orientation, thread (row r = tid / 2, half j = tid % 2) owns block
+// (m0 + r, k0/32 + j); T orientation, thread (k = tid % 64, cb = tid / 64) owns
+// block (input row k0 + k, output block m0/32 + cb).
+__device__ __forceinline__ void load_block(RawBlock& rb, const TcParams& p, int m0, int k0) {
     const int tid = threadIdx.x;
+    int64_t row, blk;
+    bool valid;
     if (p.orient == AT_ORIENT_N) {
-        // thread = (row r, half j): 32 weights of block (m0 + r, k0/32 + j), 4 chunks of 8
-        const int r = tid >> 1, j = tid & 1;
-        const int m = m0 + r;
-        uint32_t w[16];
-        if (m < p.M) {
-            int64_t d_off, q_off;
-            p.map.offsets(m, (k0 >> 5) + j, &d_off, &q_off);
-            const float d = fp16_ftz((uint32_t)p.tiles[d_off] | ((uint32_t)p.tiles[d_off + 1] << 8));
-            if (p.qtype == AT_GGML_Q4_0) {
-                const uint4 q = *reinterpret_cast<const uint4*>(p.tiles + q_off);
-                const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+        row = m0 + (tid >> 1);
+        blk = (k0 >> 5) + (tid & 1);
+        valid = row < p.M;
+    } else {
+        row = k0 + (tid & 63);
+        blk = (m0 >> 5) + (tid >> 6);
+        valid = blk * 32 < p.M;
+    }
+    if (!valid) {
+        rb.d = 0u;
+        rb.q0 = rb.q1 = make_uint4(0, 0, 0, 0);
+        return;
+    }
+    int64_t d_off, q_off;
+    p.map.offsets(row, blk, &d_off, &q_off);
+    rb.d = (uint32_t)p.tiles[d_off] | ((uint32_t)p.tiles[d_off + 1] << 8);
+    rb.q0 = *reinterpret_cast<const uint4*>(p.tiles + q_off);
+    if (p.qtype == AT_GGML_Q8_0) rb.q1 = *reinterpret_cast<const uint4*>(p.tiles + q_off + 16);
+}
+
+// The 32 weights of a raw block, (q - 8) * d or q * d in FP32, in element order.
+__device__ __forceinline__ void decode_block(const RawBlock& rb, int qtype, float* v) {
+    const float d = fp16_ftz(rb.d);
+    if (qtype == AT_GGML_Q4_0) {
+        const uint32_t qw[4] = {rb.q0.x, rb.q0.y, rb.q0.z, rb.q0.w};
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {  // byte i: elements 2i (low nibble), 2i + 1 (high nibble)
-                    const uint32_t byte = (qw[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-                    w[i] = pack_bf16(__fmul_rn((float)((int)(byte & 15u) - 8), d), __fmul_rn((float)((int)(byte >> 4) - 8), d));
-                }
-            } else {
-                const uint4 q0 = *reinterpret_cast<const uint4*>(p.tiles + q_off);
-                const uint4 q1 = *reinterpret_cast<const uint4*>(p.tiles + q_off + 16);
-                const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {  // elements 2i, 2i + 1
-                    const uint32_t word = qw[i >> 1];
-                    const int sh = 16 * (i & 1);
-                    const float a = (float)(int8_t)((word >> sh) & 0xFFu), b = (float)(int8_t)((word >> (sh + 8)) & 0xFFu);
-                    w[i] = pack_bf16(__fmul_rn(a, d), __fmul_rn(b, d));
-                }
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) w[i] = 0u;
+        for (int i = 0; i < 16; ++i) {  // byte i: elements 2i (low nibble), 2i + 1 (high nibble)
+            const uint32_t byte = (qw[i >> 2] >> (8 * (i & 3))) & 0xFFu;
+            v[2 * i] = __fmul_rn((float)((int)(byte & 15u) - 8), d);
+            v[2 * i + 1] = __fmul_rn((float)((int)(byte >> 4) - 8), d);
         }
+    } else {
+        const uint32_t qw[8] = {rb.q0.x, rb.q0.y, rb.q0.z, rb.q0.w, rb.q1.x, rb.q1.y, rb.q1.z, rb.q1.w};
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn((float)(int8_t)((qw[i >> 2] >> (8 * (i & 3))) & 0xFFu), d);
+    }
+}
+
+// Writes this thread's 32 dequantized weights into the swizzled bf16 weight tile.
+__device__ __forceinline__ void store_block(uint8_t* tile, const float* v, int orient) {
+    const int tid = threadIdx.x;
+    if (orient == AT_ORIENT_N) {
+        const int r = tid >> 1, j = tid & 1;  // 32 consecutive k of row r: chunks 4j .. 4j + 3
 #pragma unroll
         for (int c = 0; c < 4; ++c)
             *reinterpret_cast<uint4*>(tile + sw128_off(r, 4 * j + c)) =
-                make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+                make_uint4(pack_bf16(v[8 * c], v[8 * c + 1]), pack_bf16(v[8 * c + 2], v[8 * c + 3]),
+                           pack_bf16(v[8 * c + 4], v[8 * c + 5]), pack_bf16(v[8 * c + 6], v[8 * c + 7]));
     } else {
-        // orientation T: stored rows are inputs k, blocks run along the outputs.
-        // thread = (k, output block cb): 32 outputs m0 + 32 cb .. at input k0 + k
-        const int k = tid & 63, cb = tid >> 6;
-        const int kk = k0 + k;
-        const int mb = (m0 >> 5) + cb;
-        float v[32];
-        if (mb * 32 < p.M && kk < p.K) {
-            int64_t d_off, q_off;
-            p.map.offsets(kk, mb, &d_off, &q_off);
-            const float d = fp16_ftz((uint32_t)p.tiles[d_off] | ((uint32_t)p.tiles[d_off + 1] << 8));
-            if (p.qtype == AT_GGML_Q4_0) {
-                const uint4 q = *reinterpret_cast<const uint4*>(p.tiles + q_off);
-                const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const uint32_t byte = (qw[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-                    v[2 * i] = __fmul_rn((float)((int)(byte & 15u) - 8), d);
-                    v[2 * i + 1] = __fmul_rn((float)((int)(byte >> 4) - 8), d);
-                }
-            } else {
-                const uint4 q0 = *reinterpret_cast<const uint4*>(p.tiles + q_off);
-                const uint4 q1 = *reinterpret_cast<const uint4*>(p.tiles + q_off + 16);
-                const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = __fmul_rn((float)(int8_t)((qw[i >> 2] >> (8 * (i & 3))) & 0xFFu), d);
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.f;
-        }
+        const int k = tid & 63, cb = tid >> 6;  // 32 outputs (rows 32 cb ..) at column k
         const int c = k >> 3, e = k & 7;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const int r = 32 * cb + i;
-            *reinterpret_cast<__nv_bfloat16*>(tile + sw128_off(r, c) + 2 * e) = __float2bfloat16_rn(v[i]);
-        }
+        for (int i = 0; i < 32; ++i)
+            *reinterpret_cast<__nv_bfloat16*>(tile + sw128_off(32 * cb + i, c) + 2 * e) = __float2bfloat16_rn(v[i]);
     }
 }
 
-// Rounds X[t0 .. t0+127][k0 .. k0+63] to bf16 into a swizzled tile (zero rows past T).
-__device__ __forceinline__ void fill_b(uint8_t* tile, const TcParams& p, int t0, int k0) {
-    const int tid = threadIdx.x;
-    const int r = tid >> 1, j = tid & 1;  // token row, 32-element half
-    const int t = t0 + r;
-    uint32_t w[16];
-    if (t < p.T) {
-        const float4* xs = reinterpret_cast<const float4*>(p.x + (size_t)t * p.x_stride + k0 + 32 * j);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 f = xs[i];
-            w[2 * i] = pack_bf16(f.x, f.y);
-            w[2 * i + 1] = pack_bf16(f.z, f.w);
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) w[i] = 0u;
-    }
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-        *reinterpret_cast<uint4*>(tile + sw128_off(r, 4 * j + c)) =
-            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-}
+constexpr int TC_PF = 3;  // steps of weight bytes in flight per thread (registers)
 
-__global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcParams p) {
+__global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t s_bar[TC_STAGES];
+    __shared__ __align__(8) uint64_t s_full[TC_STAGES], s_empty[TC_STAGES];
     __shared__ uint32_t s_tmem;
-    __shared__ int s_fail;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int m0 = blockIdx.x * TC_M, t0 = blockIdx.y * TC_N;
-    // 1024-byte aligned stage buffers: [stage][A tile | B tile]
+    // 1024-byte aligned stage buffers: [stage][weight tile | token tile]
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    auto a_tile = [&](int st) { return base + st * 2 * TC_TILE_BYTES; };
+    auto b_tile = [&](int st) { return base + st * 2 * TC_TILE_BYTES + TC_TILE_BYTES; };
+    const int nk = p.K / TC_K;
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
@@ -258,9 +248,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcParams p
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        for (int s = 0; s < TC_STAGES; ++s) mbar_init(smem_u32(&s_bar[s]), 1);
+        for (int st = 0; st < TC_STAGES; ++st) {
+            mbar_init(smem_u32(&s_full[st]), 1);
+            mbar_init(smem_u32(&s_empty[st]), 1);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        s_fail = 0;
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
     }
     tc_fence_before();
     __syncthreads();
@@ -268,39 +261,62 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcParams p
     const uint32_t tmem = s_tmem;
     constexpr uint32_t idesc = make_idesc_bf16(TC_M, TC_N);
 
-    const int nk = p.K / TC_K;
+    // token tile of step 0 by TMA; weight bytes of step 0 into registers
+    if (tid == 0 && nk > 0) {
+        mbar_expect_tx(smem_u32(&s_full[0]), TC_TILE_BYTES);
+        tma_load_x(smem_u32(b_tile(0)), &xmap, 0, t0, smem_u32(&s_full[0]));
+    }
+    // ring of raw weight blocks: rb[i] holds step ks + i (loaded TC_PF steps ahead)
+    RawBlock rb[TC_PF];
+#pragma unroll
+    for (int i = 0; i < TC_PF; ++i)
+        if (i < nk) load_block(rb[i], p, m0, i * TC_K);
+
     bool ok = true;
     for (int ks = 0; ks < nk; ++ks) {
-        const int st = ks & 1;
-        uint8_t* a_tile = base + st * 2 * TC_TILE_BYTES;
-        uint8_t* b_tile = a_tile + TC_TILE_BYTES;
-        if (ks >= TC_STAGES) {
-            // the MMAs that read this stage two steps ago are complete
-            if (!mbar_wait(smem_u32(&s_bar[st]), ((ks - TC_STAGES) / TC_STAGES) & 1)) {
+        const int st = ks % TC_STAGES;
+        // issue the token tile of step ks + 1 once its stage's MMAs (step ks + 1 - STAGES) are done
+        if (tid == 0 && ks + 1 < nk) {
+            const int sn = (ks + 1) % TC_STAGES;
+            if (ks + 1 >= TC_STAGES && !mbar_wait(smem_u32(&s_empty[sn]), ((ks + 1 - TC_STAGES) / TC_STAGES) & 1)) {
                 ok = false;
-                if (tid == 0) atomicExch(p.err, 2);
+                atomicExch(p.err, 2);
+            }
+            if (ok) {
+                mbar_expect_tx(smem_u32(&s_full[sn]), TC_TILE_BYTES);
+                tma_load_x(smem_u32(b_tile(sn)), &xmap, (ks + 1) * TC_K, t0, smem_u32(&s_full[sn]));
             }
         }
-        if (__syncthreads_or(!ok)) { ok = false; break; }
-        fill_a(a_tile, p, m0, ks * TC_K);
-        fill_b(b_tile, p, t0, ks * TC_K);
-        // generic-proxy stores -> visible to the tensor core's async proxy
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t a_addr = smem_u32(a_tile), b_addr = smem_u32(b_tile);
+        // weight tile of step ks from the registers loaded one step ago (stage st was
+        // last read by the MMAs of step ks - STAGES, complete before the barrier
+        // that ended step ks - 1: thread 0 waited on them above)
+        float v[32];
+        decode_block(rb[0], p.qtype, v);
 #pragma unroll
-            for (int kk = 0; kk < TC_K / 16; ++kk)  // 16 bf16 = 32 bytes per MMA along K
-                tc_mma(tmem, make_sdesc_sw128(a_addr + 32 * kk), make_sdesc_sw128(b_addr + 32 * kk), idesc,
-                       (ks > 0 || kk > 0) ? 1u : 0u);
-            tc_commit(smem_u32(&s_bar[st]));
+        for (int i = 0; i + 1 < TC_PF; ++i) rb[i] = rb[i + 1];
+        if (ks + TC_PF < nk) load_block(rb[TC_PF - 1], p, m0, (ks + TC_PF) * TC_K);
+        store_block(a_tile(st), v, p.orient);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> async proxy
+        if (__syncthreads_or(!ok)) { ok = false; break; }
+        if (tid == 0) {
+            if (!mbar_wait(smem_u32(&s_full[st]), (ks / TC_STAGES) & 1)) {  // token tile landed
+                ok = false;
+                atomicExch(p.err, 2);
+            } else {
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(a_tile(st)), b_addr = smem_u32(b_tile(st));
+#pragma unroll
+                for (int kk = 0; kk < TC_K / 16; ++kk)  // 16 bf16 = 32 bytes per MMA along K
+                    tc_mma(tmem, make_sdesc_sw128(a_addr + 32 * kk), make_sdesc_sw128(b_addr + 32 * kk), idesc,
+                           (ks > 0 || kk > 0) ? 1u : 0u);
+                tc_commit(smem_u32(&s_empty[st]));
+            }
         }
     }
-    // all MMAs complete (the last commit covers every earlier one)
+    // the last commit covers every earlier MMA
     if (ok && nk > 0) {
         const int last = nk - 1;
-        if (!mbar_wait(smem_u32(&s_bar[last & 1]), (last / TC_STAGES) & 1)) {
+        if (!mbar_wait(smem_u32(&s_empty[last % TC_STAGES]), (last / TC_STAGES) & 1)) {
             ok = false;
             if (tid == 0) atomicExch(p.err, 2);
         }
@@ -332,10 +348,40 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_tc_kernel(const TcParams p
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
 }
 
+// FP32 activations -> bf16 (the GEMM's token operand), row-major [T][K].
+__global__ void to_bf16_kernel(const float* __restrict__ x, int x_stride, __nv_bfloat16* __restrict__ out, int K,
+                               int T) {
+    const int64_t n4 = (int64_t)T * K / 4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t e = 4 * i;
+        const int t = (int)(e / K), k = (int)(e - (int64_t)t * K);
+        const float4 f = *reinterpret_cast<const float4*>(x + (size_t)t * x_stride + k);
+        uint2 o;
+        o.x = pack_bf16(f.x, f.y);
+        o.y = pack_bf16(f.z, f.w);
+        *reinterpret_cast<uint2*>(out + e) = o;
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    AT_REQUIRE(fn, AT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    return fn;
+}
+
 }  // namespace
 
-void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, int y_stride, int T, int* err,
-                    cudaStream_t s) {
+void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, int y_stride, int T, void* xbf,
+                    size_t xbf_bytes, int* err, cudaStream_t s) {
     AT_REQUIRE(m->type == AT_GGML_Q4_0 || m->type == AT_GGML_Q8_0, AT_ERR_UNSUPPORTED,
                "tensor-core GEMM supports Q4_0 and Q8_0");
     const int64_t M = (m->orient == AT_ORIENT_N) ? m->rows : m->cols;
@@ -343,6 +389,24 @@ void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, in
     AT_REQUIRE(K % TC_K == 0, AT_ERR_INVALID_ARG, "tensor-core GEMM needs K a multiple of 64");
     AT_REQUIRE(T >= 1 && x_stride % 4 == 0 && ((uintptr_t)x & 15) == 0, AT_ERR_INVALID_ARG,
                "tensor-core GEMM: bad activation layout");
+    AT_REQUIRE(xbf && ((uintptr_t)xbf & 127) == 0 && xbf_bytes >= (size_t)T * K * 2, AT_ERR_INVALID_ARG,
+               "tensor-core GEMM: bf16 staging buffer too small or misaligned");
+    // activations -> bf16 [T][K], described to the TMA unit (128-byte swizzle, zero fill past T)
+    {
+        const int64_t n4 = (int64_t)T * K / 4;
+        const int grid = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 8);
+        to_bf16_kernel<<<grid, 256, 0, s>>>(x, x_stride, static_cast<__nv_bfloat16*>(xbf), (int)K, T);
+        AT_CUDA(cudaGetLastError());
+    }
+    CUtensorMap xmap;
+    const cuuint64_t gdim[2] = {(cuuint64_t)K, (cuuint64_t)T};
+    const cuuint64_t gstride[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)TC_K, (cuuint32_t)TC_N};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUresult r = encode_fn()(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xbf, gdim, gstride, box, estride,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    AT_REQUIRE(r == CUDA_SUCCESS, AT_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
     TcParams p{};
     p.tiles = m->tiles;
     p.map = tile_map(m);
@@ -351,8 +415,6 @@ void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, in
     p.M = (int)M;
     p.K = (int)K;
     p.T = T;
-    p.x = x;
-    p.x_stride = x_stride;
     p.y = y;
     p.y_stride = y_stride;
     p.err = err;
@@ -362,7 +424,7 @@ void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, in
         attr_set = true;
     }
     dim3 grid((unsigned)((M + TC_M - 1) / TC_M), (unsigned)((T + TC_N - 1) / TC_N));
-    gemm_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(p);
+    gemm_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(xmap, p);
     AT_CUDA(cudaGetLastError());
 }
 

@@ -8,6 +8,7 @@ time per call (µs) and the algorithmic bytes (weights + x + y) per second.
     python -m auratensor_b200.sweep                         # Q4_0/Q8_0, batch 1 and 8
     python -m auratensor_b200.sweep --types q4_0 --batch 1
     python -m auratensor_b200.sweep --one 14336 4096 N q4_0 --calls 8   # a few eager calls (for ncu)
+    python -m auratensor_b200.sweep --gemm --types q4_0             # tensor-core prompt GEMM, TFLOP/s
 
 Shapes are (rows, cols) of the stored matrix: orientation N computes
 y[rows] = W x[cols] (ffn, lm_head), orientation T computes y[cols] = W^T x[rows]
@@ -73,6 +74,33 @@ def time_case(qt: int, rows: int, cols: int, orient: int, batch: int, dev: torch
             "GBps": round(algo / us / 1e3, 1), "weight_bytes": nbytes}
 
 
+# Llama-3-8B prompt projections (rows, cols, orientation) for the tensor-core GEMM
+GEMM_SHAPES = [(4096, 6144, ORIENT_T), (4096, 4096, ORIENT_T), (14336, 4096, ORIENT_N), (4096, 14336, ORIENT_N)]
+
+
+def time_gemm(qt: int, rows: int, cols: int, orient: int, tokens: int, dev: torch.device, reps: int = 10) -> dict:
+    """Device time of one at_gemm_tc call (bf16 conversion of x + the tcgen05 GEMM)."""
+    g = torch.Generator(device=dev).manual_seed(rows + cols)
+    m = QMatrix(qt, orient, rows, cols, synth.generate_torch_tensor((rows, cols), qt, g, dev))
+    n_in, n_out = (cols, rows) if orient == ORIENT_N else (rows, cols)
+    x = torch.randn((tokens, n_in), device=dev)
+    y = torch.empty((tokens, n_out), device=dev)
+    m.gemm(x, y)
+    times = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        m.gemm(x, y)
+        e1.record()
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1) * 1000.0)
+    us = sorted(times)[len(times) // 2]
+    flops = 2.0 * n_in * n_out * tokens
+    return {"type": "q4_0" if qt == Q4_0 else "q8_0", "rows": rows, "cols": cols,
+            "orient": "N" if orient == ORIENT_N else "T", "tokens": tokens, "us_per_call": round(us, 2),
+            "TFLOPs": round(flops / us / 1e6, 1)}
+
+
 def run_one(rows: int, cols: int, orient: int, qt: int, calls: int, dev: torch.device) -> None:
     """A few eager calls on 4 copies of one matrix (a small case for ncu)."""
     g = torch.Generator(device=dev).manual_seed(0)
@@ -91,9 +119,17 @@ def main(argv=None) -> None:
     ap.add_argument("--batch", default="1,8")
     ap.add_argument("--one", nargs=4, metavar=("ROWS", "COLS", "N|T", "TYPE"))
     ap.add_argument("--calls", type=int, default=8)
+    ap.add_argument("--gemm", action="store_true", help="time the tensor-core prompt GEMM instead")
+    ap.add_argument("--tokens", default="128,512")
     args = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
+    if args.gemm:
+        for t in args.types.split(","):
+            for rows, cols, orient in GEMM_SHAPES:
+                for n in (int(v) for v in args.tokens.split(",")):
+                    print(json.dumps(time_gemm(TYPES[t.lower()], rows, cols, orient, n, dev)), flush=True)
+        return
     if args.one:
         rows, cols, o, t = args.one
         run_one(int(rows), int(cols), ORIENT_N if o.upper() == "N" else ORIENT_T, TYPES[t.lower()], args.calls, dev)
