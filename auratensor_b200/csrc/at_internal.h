@@ -175,10 +175,12 @@ void gemv_t_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* float
 void gemv_n_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* floats, size_t* counters);
 // Tensor-core prompt GEMM (gemm_tc.cu): y[t][:] = W x[t][:], bf16 operands,
 // FP32 sums; xbf is a 128-byte aligned device buffer of at least T x in bf16
-// (the activations are converted into it); *err records a bounded wait that
-// ran out (2).
+// (the activations are converted into it); ws (FP32, may be null) holds the
+// partials when K is split across CTAs (gemm_tc_splits(m, T) x T x out
+// floats); *err records a bounded wait that ran out (2).
+int gemm_tc_splits(const at_qmat* m, int T, int num_sms);
 void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, int y_stride, int T, void* xbf,
-                    size_t xbf_bytes, int* err, cudaStream_t s);
+                    size_t xbf_bytes, float* ws, size_t ws_bytes, int num_sms, int* err, cudaStream_t s);
 void launch_sgemv_f32(const float* A, const float* x, float* y, int M, int K, int batch, int a_ld,
                       cudaStream_t s);
 

@@ -572,6 +572,8 @@ int at_gemm_tc(at_ctx* ctx, const at_qmat* m, const float* x, float* y, int toke
         static int* d_err[64] = {};
         static void* xbf[64] = {};
         static size_t xbf_bytes[64] = {};
+        static float* ws[64] = {};
+        static size_t ws_bytes[64] = {};
         AT_REQUIRE(ctx->device < 64, AT_ERR_INVALID_ARG, "device index");
         const size_t need = (size_t)tokens * in * 2;
         {
@@ -586,9 +588,16 @@ int at_gemm_tc(at_ctx* ctx, const at_qmat* m, const float* x, float* y, int toke
                 AT_CUDA(cudaMalloc(&xbf[ctx->device], need));
                 xbf_bytes[ctx->device] = need;
             }
+            const size_t wneed = (size_t)gemm_tc_splits(m, tokens, ctx->num_sms) * tokens * outn * 4;
+            if (ws_bytes[ctx->device] < wneed) {
+                AT_CUDA(cudaStreamSynchronize(ctx->stream));
+                if (ws[ctx->device]) cudaFree(ws[ctx->device]);
+                AT_CUDA(cudaMalloc(&ws[ctx->device], wneed));
+                ws_bytes[ctx->device] = wneed;
+            }
         }
         launch_gemm_tc(m, x, (int)in, y, (int)outn, tokens, xbf[ctx->device], xbf_bytes[ctx->device],
-                       d_err[ctx->device], ctx->stream);
+                       ws[ctx->device], ws_bytes[ctx->device], ctx->num_sms, d_err[ctx->device], ctx->stream);
         int err = 0;
         AT_CUDA(cudaMemcpyAsync(&err, d_err[ctx->device], sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
         AT_CUDA(cudaStreamSynchronize(ctx->stream));

@@ -45,12 +45,14 @@ namespace {
 constexpr int TC_M = 128;        // outputs per CTA (MMA M)
 constexpr int TC_N = 128;        // tokens per CTA (MMA N)
 constexpr int TC_K = 64;         // K per pipeline step (one 128-byte swizzle row)
-constexpr int TC_THREADS = 256;  // 8 warps
+constexpr int TC_DQ_WARPS = 8;   // warps that dequantize the weight tile (256 threads, one block each)
+constexpr int TC_THREADS_WS = 64 + 32 * TC_DQ_WARPS;  // + a TMA warp and an MMA warp
 constexpr int TC_TILE_BYTES = TC_M * TC_K * 2;  // 16 KB per operand tile (TC_N == TC_M)
-constexpr int TC_STAGES = 3;
+constexpr int TC_STAGES = 4;
 constexpr int TC_SMEM = TC_STAGES * 2 * TC_TILE_BYTES + 1024;  // + alignment slack
 constexpr uint32_t TC_TMEM_COLS = 128;
 constexpr int kTcSpinLimit = 1 << 26;
+constexpr int kTcMaxSplits = 4;
 
 // Instruction descriptor of tcgen05.mma kind::f16: D f32 (bits 4-5 = 1),
 // A and B bf16 (bits 7-9 = 1, 10-12 = 1), both K-major (bits 15, 16 = 0),
@@ -139,8 +141,9 @@ struct TcParams {
     int M;        // outputs
     int K;        // inputs (multiple of 64)
     int T;        // tokens
-    float* y;     // [T][y_stride]
+    float* y;     // [T][y_stride], or with split K the partials [split][T][y_stride]
     int y_stride;
+    int splits;   // CTAs along K (blockIdx.z); split z covers steps [z nk / splits, (z+1) nk / splits)
     int* err;
 };
 
@@ -164,8 +167,7 @@ struct RawBlock {
 // Step k0: N orientation, thread (row r = tid / 2, half j = tid % 2) owns block
 // (m0 + r, k0/32 + j); T orientation, thread (k = tid % 64, cb = tid / 64) owns
 // block (input row k0 + k, output block m0/32 + cb).
-__device__ __forceinline__ void load_block(RawBlock& rb, const TcParams& p, int m0, int k0) {
-    const int tid = threadIdx.x;
+__device__ __forceinline__ void load_block(RawBlock& rb, const TcParams& p, int m0, int k0, int tid) {
     int64_t row, blk;
     bool valid;
     if (p.orient == AT_ORIENT_N) {
@@ -189,27 +191,41 @@ __device__ __forceinline__ void load_block(RawBlock& rb, const TcParams& p, int 
     if (p.qtype == AT_GGML_Q8_0) rb.q1 = *reinterpret_cast<const uint4*>(p.tiles + q_off + 16);
 }
 
-// The 32 weights of a raw block, (q - 8) * d or q * d in FP32, in element order.
+// The 32 weights of a raw block, (q - 8) * d or q * d in FP32, in element
+// order. A nibble (byte) becomes the exact float q - 8 (q) by one byte permute
+// into the mantissa of 2^23 and a packed f32x2 subtraction; then one rounding
+// in the multiply by d.
 __device__ __forceinline__ void decode_block(const RawBlock& rb, int qtype, float* v) {
     const float d = fp16_ftz(rb.d);
+    const float2 dd = f2(d, d);
     if (qtype == AT_GGML_Q4_0) {
+        const float2 moff = f2(-8388616.f, -8388616.f);  // -(2^23 + 8)
         const uint32_t qw[4] = {rb.q0.x, rb.q0.y, rb.q0.z, rb.q0.w};
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {  // byte i: elements 2i (low nibble), 2i + 1 (high nibble)
-            const uint32_t byte = (qw[i >> 2] >> (8 * (i & 3))) & 0xFFu;
-            v[2 * i] = __fmul_rn((float)((int)(byte & 15u) - 8), d);
-            v[2 * i + 1] = __fmul_rn((float)((int)(byte >> 4) - 8), d);
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t lo = qw[i] & 0x0F0F0F0Fu, hi = (qw[i] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {  // byte k of word i: elements 8i + 2k (low), 8i + 2k + 1 (high)
+                const float2 w = __fmul2_rn(__fadd2_rn(f2(magic_byte(lo, k), magic_byte(hi, k)), moff), dd);
+                v[8 * i + 2 * k] = w.x;
+                v[8 * i + 2 * k + 1] = w.y;
+            }
         }
     } else {
+        const float2 moff = f2(-8388736.f, -8388736.f);  // -(2^23 + 128)
         const uint32_t qw[8] = {rb.q0.x, rb.q0.y, rb.q0.z, rb.q0.w, rb.q1.x, rb.q1.y, rb.q1.z, rb.q1.w};
 #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __fmul_rn((float)(int8_t)((qw[i >> 2] >> (8 * (i & 3))) & 0xFFu), d);
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t u = qw[i] ^ 0x80808080u;  // int8 q -> unsigned q + 128
+            const float2 w01 = __fmul2_rn(__fadd2_rn(f2(magic_byte(u, 0), magic_byte(u, 1)), moff), dd);
+            const float2 w23 = __fmul2_rn(__fadd2_rn(f2(magic_byte(u, 2), magic_byte(u, 3)), moff), dd);
+            v[4 * i] = w01.x; v[4 * i + 1] = w01.y; v[4 * i + 2] = w23.x; v[4 * i + 3] = w23.y;
+        }
     }
 }
 
 // Writes this thread's 32 dequantized weights into the swizzled bf16 weight tile.
-__device__ __forceinline__ void store_block(uint8_t* tile, const float* v, int orient) {
-    const int tid = threadIdx.x;
+__device__ __forceinline__ void store_block(uint8_t* tile, const float* v, int orient, int tid) {
     if (orient == AT_ORIENT_N) {
         const int r = tid >> 1, j = tid & 1;  // 32 consecutive k of row r: chunks 4j .. 4j + 3
 #pragma unroll
@@ -226,22 +242,31 @@ __device__ __forceinline__ void store_block(uint8_t* tile, const float* v, int o
     }
 }
 
-constexpr int TC_PF = 3;  // steps of weight bytes in flight per thread (registers)
+constexpr int TC_PF = 3;  // steps of weight bytes in flight per dequant thread (registers)
 
-__global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap,
-                                                                const TcParams p) {
+// Warp roles: warp 0 issues the token tiles' TMA, warp 1 owns TMEM and issues
+// the MMAs, warps 2-9 dequantize the weight tiles (256 threads, one block of
+// 32 weights each per step). Per stage: full_b (TMA bytes), full_a (8 warp
+// arrivals after each warp's stores and proxy fence) and empty (the MMAs'
+// commit); no CTA-wide barrier inside the K loop.
+__global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                   const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t s_full[TC_STAGES], s_empty[TC_STAGES];
+    __shared__ __align__(8) uint64_t s_fa[TC_STAGES], s_fb[TC_STAGES], s_empty[TC_STAGES], s_done;
     __shared__ uint32_t s_tmem;
+    __shared__ int s_bad;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int m0 = blockIdx.x * TC_M, t0 = blockIdx.y * TC_N;
-    // 1024-byte aligned stage buffers: [stage][weight tile | token tile]
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     auto a_tile = [&](int st) { return base + st * 2 * TC_TILE_BYTES; };
     auto b_tile = [&](int st) { return base + st * 2 * TC_TILE_BYTES + TC_TILE_BYTES; };
-    const int nk = p.K / TC_K;
+    const int nk_all = p.K / TC_K;
+    const int ks0 = (int)((int64_t)blockIdx.z * nk_all / p.splits);
+    const int nk = (int)((int64_t)(blockIdx.z + 1) * nk_all / p.splits) - ks0;  // steps of this split
+    const int kbase = ks0 * TC_K;
+    float* yout = p.y + (size_t)blockIdx.z * p.T * p.y_stride;
 
-    if (warp == 0) {
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
                      "r"(TC_TMEM_COLS)
                      : "memory");
@@ -249,60 +274,45 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_con
     }
     if (tid == 0) {
         for (int st = 0; st < TC_STAGES; ++st) {
-            mbar_init(smem_u32(&s_full[st]), 1);
+            mbar_init(smem_u32(&s_fa[st]), TC_DQ_WARPS);
+            mbar_init(smem_u32(&s_fb[st]), 1);
             mbar_init(smem_u32(&s_empty[st]), 1);
         }
+        mbar_init(smem_u32(&s_done), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+        s_bad = 0;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
-    constexpr uint32_t idesc = make_idesc_bf16(TC_M, TC_N);
+    auto fail = [&]() { atomicExch(p.err, 2); s_bad = 1; };
 
-    // token tile of step 0 by TMA; weight bytes of step 0 into registers
-    if (tid == 0 && nk > 0) {
-        mbar_expect_tx(smem_u32(&s_full[0]), TC_TILE_BYTES);
-        tma_load_x(smem_u32(b_tile(0)), &xmap, 0, t0, smem_u32(&s_full[0]));
-    }
-    // ring of raw weight blocks: rb[i] holds step ks + i (loaded TC_PF steps ahead)
-    RawBlock rb[TC_PF];
-#pragma unroll
-    for (int i = 0; i < TC_PF; ++i)
-        if (i < nk) load_block(rb[i], p, m0, i * TC_K);
-
-    bool ok = true;
-    for (int ks = 0; ks < nk; ++ks) {
-        const int st = ks % TC_STAGES;
-        // issue the token tile of step ks + 1 once its stage's MMAs (step ks + 1 - STAGES) are done
-        if (tid == 0 && ks + 1 < nk) {
-            const int sn = (ks + 1) % TC_STAGES;
-            if (ks + 1 >= TC_STAGES && !mbar_wait(smem_u32(&s_empty[sn]), ((ks + 1 - TC_STAGES) / TC_STAGES) & 1)) {
-                ok = false;
-                atomicExch(p.err, 2);
-            }
-            if (ok) {
-                mbar_expect_tx(smem_u32(&s_full[sn]), TC_TILE_BYTES);
-                tma_load_x(smem_u32(b_tile(sn)), &xmap, (ks + 1) * TC_K, t0, smem_u32(&s_full[sn]));
+    if (warp == 0) {
+        // ---- token tiles by TMA ----
+        if (lane == 0) {
+            for (int ks = 0; ks < nk; ++ks) {
+                const int st = ks % TC_STAGES;
+                if (ks >= TC_STAGES && !mbar_wait(smem_u32(&s_empty[st]), ((ks - TC_STAGES) / TC_STAGES) & 1)) {
+                    fail();
+                    break;
+                }
+                mbar_expect_tx(smem_u32(&s_fb[st]), TC_TILE_BYTES);
+                tma_load_x(smem_u32(b_tile(st)), &xmap, kbase + ks * TC_K, t0, smem_u32(&s_fb[st]));
             }
         }
-        // weight tile of step ks from the registers loaded one step ago (stage st was
-        // last read by the MMAs of step ks - STAGES, complete before the barrier
-        // that ended step ks - 1: thread 0 waited on them above)
-        float v[32];
-        decode_block(rb[0], p.qtype, v);
-#pragma unroll
-        for (int i = 0; i + 1 < TC_PF; ++i) rb[i] = rb[i + 1];
-        if (ks + TC_PF < nk) load_block(rb[TC_PF - 1], p, m0, (ks + TC_PF) * TC_K);
-        store_block(a_tile(st), v, p.orient);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> async proxy
-        if (__syncthreads_or(!ok)) { ok = false; break; }
-        if (tid == 0) {
-            if (!mbar_wait(smem_u32(&s_full[st]), (ks / TC_STAGES) & 1)) {  // token tile landed
-                ok = false;
-                atomicExch(p.err, 2);
-            } else {
+    } else if (warp == 1) {
+        // ---- MMA issue ----
+        if (lane == 0) {
+            constexpr uint32_t idesc = make_idesc_bf16(TC_M, TC_N);
+            for (int ks = 0; ks < nk; ++ks) {
+                const int st = ks % TC_STAGES;
+                const uint32_t par = (ks / TC_STAGES) & 1;
+                if (!mbar_wait(smem_u32(&s_fb[st]), par) || !mbar_wait(smem_u32(&s_fa[st]), par)) {
+                    fail();
+                    break;
+                }
                 tc_fence_after();
                 const uint32_t a_addr = smem_u32(a_tile(st)), b_addr = smem_u32(b_tile(st));
 #pragma unroll
@@ -311,22 +321,41 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_con
                            (ks > 0 || kk > 0) ? 1u : 0u);
                 tc_commit(smem_u32(&s_empty[st]));
             }
+            tc_commit(smem_u32(&s_done));  // arrives when every MMA above is complete
+        }
+    } else {
+        // ---- weight tiles: dequantize into swizzled bf16 ----
+        const int dt = tid - 64;
+        RawBlock rb[TC_PF];
+#pragma unroll
+        for (int i = 0; i < TC_PF; ++i)
+            if (i < nk) load_block(rb[i], p, m0, kbase + i * TC_K, dt);
+        for (int ks = 0; ks < nk; ++ks) {
+            const int st = ks % TC_STAGES;
+            float v[32];
+            decode_block(rb[0], p.qtype, v);
+#pragma unroll
+            for (int i = 0; i + 1 < TC_PF; ++i) rb[i] = rb[i + 1];
+            if (ks + TC_PF < nk) load_block(rb[TC_PF - 1], p, m0, kbase + (ks + TC_PF) * TC_K, dt);
+            if (ks >= TC_STAGES && !mbar_wait(smem_u32(&s_empty[st]), ((ks - TC_STAGES) / TC_STAGES) & 1)) {
+                if (lane == 0) fail();
+                break;
+            }
+            store_block(a_tile(st), v, p.orient, dt);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> async proxy
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&s_fa[st])) : "memory");
         }
     }
-    // the last commit covers every earlier MMA
-    if (ok && nk > 0) {
-        const int last = nk - 1;
-        if (!mbar_wait(smem_u32(&s_empty[last % TC_STAGES]), (last / TC_STAGES) & 1)) {
-            ok = false;
-            if (tid == 0) atomicExch(p.err, 2);
-        }
-    }
-    if (__syncthreads_or(!ok)) ok = false;
-    tc_fence_after();
 
-    if (ok) {
-        // warp w reads TMEM lanes 32 (w % 4) .. + 31 (outputs), columns 64 (w / 4) .. + 63 (tokens)
-        const int quarter = warp & 3, half = warp >> 2;
+    // ---- epilogue: the accumulator (dequant warps 2-9: lanes 32 (w % 4) .., columns 64 ((w - 2) / 4) ..) ----
+    bool ok = mbar_wait(smem_u32(&s_done), 0);
+    if (!ok && tid == 0) atomicExch(p.err, 2);
+    __syncthreads();
+    ok = ok && (s_bad == 0);
+    tc_fence_after();
+    if (ok && warp >= 2) {
+        const int quarter = warp & 3, half = (warp - 2) >> 2;
         const int m = m0 + 32 * quarter + lane;
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
@@ -337,15 +366,27 @@ __global__ void __launch_bounds__(TC_THREADS, 2) gemm_tc_kernel(const __grid_con
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int t = t0 + col + i;
-                    if (t < p.T) p.y[(size_t)t * p.y_stride + m] = v[i];
+                    if (t < p.T) yout[(size_t)t * p.y_stride + m] = v[i];
                 }
             }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0)
+    if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
+}
+
+// y[t][m] = sum over splits z (in order) of ws[z][t][m].
+__global__ void splitk_sum_kernel(const float* __restrict__ ws, int splits, int T, int M, float* __restrict__ y,
+                                  int y_stride) {
+    const int64_t n = (int64_t)T * M;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / M), m = (int)(i - (int64_t)t * M);
+        float acc = ws[i];
+        for (int z = 1; z < splits; ++z) acc += ws[(size_t)z * n + i];
+        y[(size_t)t * y_stride + m] = acc;
+    }
 }
 
 // FP32 activations -> bf16 (the GEMM's token operand), row-major [T][K].
@@ -380,8 +421,18 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace
 
+int gemm_tc_splits(const at_qmat* m, int T, int num_sms) {
+    const int64_t M = (m->orient == AT_ORIENT_N) ? m->rows : m->cols;
+    const int64_t K = (m->orient == AT_ORIENT_N) ? m->cols : m->rows;
+    const int64_t tiles = ((M + TC_M - 1) / TC_M) * ((T + TC_N - 1) / TC_N);
+    // enough CTAs for most SMs, each split keeping at least 8 K-steps
+    int64_t sp = std::max<int64_t>(1, (num_sms + tiles / 2) / tiles);
+    sp = std::min<int64_t>(sp, std::max<int64_t>(1, (K / TC_K) / 8));
+    return (int)std::min<int64_t>(sp, kTcMaxSplits);
+}
+
 void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, int y_stride, int T, void* xbf,
-                    size_t xbf_bytes, int* err, cudaStream_t s) {
+                    size_t xbf_bytes, float* ws, size_t ws_bytes, int num_sms, int* err, cudaStream_t s) {
     AT_REQUIRE(m->type == AT_GGML_Q4_0 || m->type == AT_GGML_Q8_0, AT_ERR_UNSUPPORTED,
                "tensor-core GEMM supports Q4_0 and Q8_0");
     const int64_t M = (m->orient == AT_ORIENT_N) ? m->rows : m->cols;
@@ -415,17 +466,26 @@ void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, in
     p.M = (int)M;
     p.K = (int)K;
     p.T = T;
-    p.y = y;
-    p.y_stride = y_stride;
+    const int splits = gemm_tc_splits(m, T, num_sms);
+    const bool split = splits > 1 && ws && ws_bytes >= (size_t)splits * T * M * 4;
+    p.splits = split ? splits : 1;
+    p.y = split ? ws : y;
+    p.y_stride = split ? (int)M : y_stride;
     p.err = err;
     static bool attr_set = false;
     if (!attr_set) {
         AT_CUDA(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
         attr_set = true;
     }
-    dim3 grid((unsigned)((M + TC_M - 1) / TC_M), (unsigned)((T + TC_N - 1) / TC_N));
-    gemm_tc_kernel<<<grid, TC_THREADS, TC_SMEM, s>>>(xmap, p);
+    dim3 grid((unsigned)((M + TC_M - 1) / TC_M), (unsigned)((T + TC_N - 1) / TC_N), (unsigned)p.splits);
+    gemm_tc_kernel<<<grid, TC_THREADS_WS, TC_SMEM, s>>>(xmap, p);
     AT_CUDA(cudaGetLastError());
+    if (p.splits > 1) {
+        const int64_t n = (int64_t)T * M;
+        splitk_sum_kernel<<<(int)std::min<int64_t>((n + 255) / 256, 148 * 8), 256, 0, s>>>(ws, p.splits, T, (int)M, y,
+                                                                                             y_stride);
+        AT_CUDA(cudaGetLastError());
+    }
 }
 
 }  // namespace at

@@ -599,6 +599,8 @@ struct at_model {
     float *pf_att = nullptr, *pf_g = nullptr, *pf_u = nullptr, *pf_part = nullptr;
     void* pf_xbf = nullptr;               // bf16 activations of the prompt GEMMs
     size_t pf_xbf_bytes = 0;
+    float* pf_ws = nullptr;               // split-K partials of the prompt GEMMs
+    size_t pf_ws_bytes = 0;
     int* pf_tok = nullptr;
     int64_t* pf_pos = nullptr;
     int* pf_err = nullptr;
@@ -910,7 +912,7 @@ void destroy_model(at_model* m) {
                     m->att_part, m->kcache, m->vcache, m->rope_cos, m->rope_sin, m->scratch, m->counters,
                     m->d_tokens, m->d_pos, m->d_argmax, m->d_gen_out, m->d_gen_count, m->d_argkey,
                     m->d_step, m->ar_base, m->d_ar_err, m->pf_xa, m->pf_xb, m->pf_y, m->pf_qkv, m->pf_q,
-                    m->pf_att, m->pf_g, m->pf_u, m->pf_part, m->pf_tok, m->pf_pos, m->pf_err, m->pf_xbf};
+                    m->pf_att, m->pf_g, m->pf_u, m->pf_part, m->pf_tok, m->pf_pos, m->pf_err, m->pf_xbf, m->pf_ws};
     for (void* p : bufs)
         if (p) cudaFree(p);
     if (m->h_tokens) cudaFreeHost(m->h_tokens);
@@ -1453,6 +1455,16 @@ void ensure_prompt_buffers(at_model* m) {
     alloc_zero((void**)&m->pf_err, sizeof(int));
     m->pf_xbf_bytes = (size_t)PF_T * std::max<int64_t>(std::max<int64_t>(d, nq), m->Fl) * 2;
     alloc_zero(&m->pf_xbf, m->pf_xbf_bytes);
+    {
+        size_t ws = 16;
+        const Layer& ly = m->layers[0];
+        for (const at_qmat* q : {&ly.qkv, &ly.wo, &ly.w1, &ly.w3, &ly.w2}) {
+            const int64_t outn = (q->orient == AT_ORIENT_N) ? q->rows : q->cols;
+            ws = std::max(ws, (size_t)gemm_tc_splits(q, PF_T, m->ctx->num_sms) * PF_T * outn * 4);
+        }
+        m->pf_ws_bytes = ws;
+        alloc_zero((void**)&m->pf_ws, ws);
+    }
     AT_CUDA(cudaMallocHost(&m->h_pf_tok, PF_T * sizeof(int)));
     AT_CUDA(cudaMallocHost(&m->h_pf_pos, PF_T * sizeof(int64_t)));
 }
@@ -1490,7 +1502,8 @@ void run_prompt_batched(at_model* m, const int* tokens, int n) {
             // attention block: xb = norm(xa + y); q, k, v; RoPE + append; attention; y = wo att
             rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xa, m->pf_y, ly.attn_norm, m->pf_xb, d, eps);
             AT_CUDA(cudaGetLastError());
-            launch_gemm_tc(&ly.qkv, m->pf_xb, d, m->pf_qkv, qcols, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_err, s);
+            launch_gemm_tc(&ly.qkv, m->pf_xb, d, m->pf_qkv, qcols, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
+                           c->num_sms, m->pf_err, s);
             rope_append_kernel<<<T, 256, 0, s>>>(m->pf_qkv, qcols, m->pf_q, kc, vc, m->rope_cos, m->rope_sin, hd, nq,
                                                  nkv, m->ctx_len, p0);
             AT_CUDA(cudaGetLastError());
@@ -1506,15 +1519,19 @@ void run_prompt_batched(at_model* m, const int* tokens, int n) {
             }
             AT_CUDA(cudaGetLastError());
             if (L == m->L - 1) break;  // later layers' inputs only; the KV cache is complete
-            launch_gemm_tc(&ly.wo, m->pf_att, nq, m->pf_y, d, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_err, s);
+            launch_gemm_tc(&ly.wo, m->pf_att, nq, m->pf_y, d, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
+                           c->num_sms, m->pf_err, s);
             // feed-forward block: xa = norm(xb + y); h = silu(w1 xa) * (w3 xa); y = w2 h
             rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xb, m->pf_y, ly.ffn_norm, m->pf_xa, d, eps);
             AT_CUDA(cudaGetLastError());
-            launch_gemm_tc(&ly.w1, m->pf_xa, d, m->pf_g, m->Fl, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_err, s);
-            launch_gemm_tc(&ly.w3, m->pf_xa, d, m->pf_u, m->Fl, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_err, s);
+            launch_gemm_tc(&ly.w1, m->pf_xa, d, m->pf_g, m->Fl, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
+                           c->num_sms, m->pf_err, s);
+            launch_gemm_tc(&ly.w3, m->pf_xa, d, m->pf_u, m->Fl, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
+                           c->num_sms, m->pf_err, s);
             silu_mul_kernel<<<grid_for((int64_t)T * m->Fl), 256, 0, s>>>(m->pf_g, m->pf_u, (int64_t)T * m->Fl);
             AT_CUDA(cudaGetLastError());
-            launch_gemm_tc(&ly.w2, m->pf_g, m->Fl, m->pf_y, d, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_err, s);
+            launch_gemm_tc(&ly.w2, m->pf_g, m->Fl, m->pf_y, d, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
+                           c->num_sms, m->pf_err, s);
         }
     }
     int err = 0;
