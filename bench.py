@@ -399,6 +399,9 @@ def main():
         "clocks": clocks,
         "cpu_baseline": cpu,
         "setup": {"load_s": round(load_s, 1), "prefill_s": round(prefill_s, 2)},
+        # the untimed prompt (forwardPrompt: tcgen05 GEMMs over 128-token chunks on one GPU), host wall clock
+        "prompt": {"tokens": args.prompt, "seconds": round(prefill_s, 4),
+                   "tok_s": round(args.prompt / prefill_s, 1) if prefill_s > 0 else None},
     }
     print(json.dumps(line), flush=True)
     finish(model, ctx, world)
