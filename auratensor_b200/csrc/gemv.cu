@@ -606,6 +606,203 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_ns_kernel(const NSParams p)
 }
 
 // ---------------------------------------------------------------------------
+// Orientation N, batch 3..8: split K into 32-block steps
+// ---------------------------------------------------------------------------
+// CTA (p, q) stages the 1024 x values of step q for all batch rows (36 KB at
+// batch 8) and streams the tiles (g, q) of the row groups g of part p
+// through per-warp cp.async rings, a warp owning whole groups; a group's
+// 4 x NM x B sums are combined over the lanes by a butterfly reduce-scatter
+// (lane l ends with value l; matrices one at a time) and stored as the
+// step's partial. A second
+// kernel sums the steps' partials in step order (deterministic) and applies
+// the epilogue. Folded RMSNorm as in the stream kernel: each CTA also stores
+// its step's sums of (xin + yin)^2.
+constexpr int Q_THREADS = 256;
+constexpr int Q_WARPS = Q_THREADS / 32;
+constexpr int Q_NST = 2;
+
+struct NQParams {
+    const uint8_t* tiles[2];
+    int rows, nb, ngroups, nsteps;
+    int P;          // row parts (gridDim.x); the steps are gridDim.y
+    float* part;    // [nsteps][ngroups][VPAD] partial sums
+    float* ssq;     // [P][nsteps][B] sums of squares (AddNorm)
+    GemvArgs a;
+};
+
+// Sum over the 32 lanes of 32 values per lane: after the butterfly, lane l
+// holds the total of value l.
+__device__ __forceinline__ float lane_transpose_sum(float* v, int lane) {
+    int nn = 32;
+#pragma unroll
+    for (int bit = 16; bit >= 1; bit >>= 1) {
+        const bool upper = (lane & bit) != 0;
+        nn >>= 1;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (k < nn) {
+                const float send = upper ? v[k] : v[k + nn];
+                const float keep = upper ? v[k + nn] : v[k];
+                v[k] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+            }
+        }
+    }
+    return v[0];
+}
+
+template <int QT, int B, Pro PRO, Epi EPI>
+__global__ void __launch_bounds__(Q_THREADS, 1) gemv_nq_kernel(const NQParams p) {
+    constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
+    using TL = NTile<QT>;
+    constexpr int SLOT = NM * TL::BYTES;
+    constexpr int NV = QTraits<QT>::NV;
+    static_assert(4 * B <= 32, "one 32-value partial per matrix and group");
+    extern __shared__ __align__(16) float xs[];  // [B][32 blocks][XPAD], then the rings
+    pdl_trigger();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int pp = blockIdx.x, q = blockIdx.y;
+    const int g0 = (int)((int64_t)pp * p.ngroups / p.P), g1 = (int)((int64_t)(pp + 1) * p.ngroups / p.P);
+    const int nmine = (g1 - g0 - warp + Q_WARPS - 1) / Q_WARPS;  // groups g0 + warp + Q_WARPS * i
+    const uint8_t* ring_ptr = reinterpret_cast<const uint8_t*>(xs) + B * 32 * XPAD * 4 + warp * Q_NST * SLOT;
+    const uint32_t ring = (uint32_t)__cvta_generic_to_shared(ring_ptr);
+    int issued = 0;
+    auto issue_next = [&]() {
+        const uint32_t slot = ring + (issued & (Q_NST - 1)) * SLOT;
+        if (issued < nmine) {
+            const int g = g0 + warp + Q_WARPS * issued;
+            const size_t off = ((size_t)g * p.nsteps + q) * TL::BYTES;
+            copy_unit<TL::CHUNKS>(slot, p.tiles[0] + off, lane);
+            if constexpr (NM == 2) copy_unit<TL::CHUNKS>(slot + TL::BYTES, p.tiles[1] + off, lane);
+        }
+        cp_commit();
+        ++issued;
+    };
+    issue_next();  // weights are never written by earlier kernels
+    pdl_wait();
+
+    // stage x (or (xin + yin) * gamma) for blocks 32q .. 32q + 31 of the B rows
+    const int jb = q * 32, nbl = min(32, p.nb - jb);
+    float ss[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) ss[b] = 0.f;
+    for (int idx = tid; idx < B * 32 * 8; idx += Q_THREADS) {
+        const int b = idx / 256, r = idx - b * 256, jl = r >> 3, q4 = r & 7;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (jl < nbl) {
+            const size_t off = (size_t)b * p.a.x_stride + (size_t)(jb + jl) * 32 + q4 * 4;
+            if constexpr (PRO == Pro::Plain) {
+                o = *reinterpret_cast<const float4*>(p.a.x + off);
+            } else {
+                float4 t = *reinterpret_cast<const float4*>(p.a.xin + off);
+                if (p.a.yin) {
+                    const float4 u = *reinterpret_cast<const float4*>(p.a.yin + off);
+                    t.x = __fadd_rn(t.x, u.x); t.y = __fadd_rn(t.y, u.y); t.z = __fadd_rn(t.z, u.z); t.w = __fadd_rn(t.w, u.w);
+                }
+                const float qsum = fmaf(t.x, t.x, fmaf(t.y, t.y, fmaf(t.z, t.z, __fmul_rn(t.w, t.w))));
+#pragma unroll
+                for (int bb = 0; bb < B; ++bb)
+                    if (bb == b) ss[bb] += qsum;
+                const float4 g = *reinterpret_cast<const float4*>(p.a.gamma + (size_t)(jb + jl) * 32 + q4 * 4);
+                o = make_float4(__fmul_rn(t.x, g.x), __fmul_rn(t.y, g.y), __fmul_rn(t.z, g.z), __fmul_rn(t.w, g.w));
+            }
+        }
+        *reinterpret_cast<float4*>(xs + ((size_t)b * 32 + jl) * XPAD + q4 * 4) = o;
+    }
+    if constexpr (PRO == Pro::AddNorm) {
+        __shared__ float s_ss[Q_WARPS][B];
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            const float t = warp_sum(ss[b]);
+            if (lane == 0) s_ss[warp][b] = t;
+        }
+        __syncthreads();
+        if (tid < B) {
+            float t = 0.f;
+#pragma unroll
+            for (int w = 0; w < Q_WARPS; ++w) t += s_ss[w][tid];
+            p.ssq[((size_t)pp * p.nsteps + q) * B + tid] = t;
+        }
+    }
+    __syncthreads();
+
+    for (int t = 0; t < nmine; ++t) {
+        while (issued < t + Q_NST) issue_next();
+        cp_wait<Q_NST - 1>();
+        __syncwarp();
+        const uint8_t* sp = ring_ptr + (t & (Q_NST - 1)) * SLOT;
+        const int g = g0 + warp + Q_WARPS * t;
+        float* dst = p.part + ((size_t)q * p.ngroups + g) * (32 * NM);
+#pragma unroll
+        for (int m = 0; m < NM; ++m) {  // one matrix at a time keeps 32 partial values live
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0.f;
+            if (lane < nbl) {
+                uint4 qv[4][NV];
+                float dsc[4];
+                const uint8_t* tb = sp + m * TL::BYTES;
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+#pragma unroll
+                    for (int vv = 0; vv < NV; ++vv)
+                        qv[r][vv] = *reinterpret_cast<const uint4*>(tb + 256 + (r * 32 + lane) * TL::QB + 16 * vv);
+                    dsc[r] = fp16_ftz_fast(*reinterpret_cast<const uint16_t*>(tb + (r * 32 + lane) * 2));
+                }
+#pragma unroll
+                for (int b = 0; b < B; ++b) {
+                    const float4* xv = reinterpret_cast<const float4*>(xs + ((size_t)b * 32 + lane) * XPAD);
+                    float4 xr[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) xr[k] = xv[k];
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) v[r * B + b] = __fmul_rn(dsc[r], dot32<QT>(qv[r], xr));
+                }
+            }
+            dst[32 * m + lane] = lane_transpose_sum(v, lane);
+        }
+        __syncwarp();  // every lane is done with this slot before it is refilled
+    }
+    cp_wait<0>();
+}
+
+// y from the steps' partials (step order), with the folded RMSNorm scale and
+// the epilogue; CTA c also writes its slice of the normed residual stream.
+template <int B, Pro PRO, Epi EPI>
+__global__ void __launch_bounds__(256) gemv_nq_reduce_kernel(const NQParams p) {
+    constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
+    __shared__ float s_inv[B];
+    pdl_trigger();
+    pdl_wait();
+    const int d_model = p.nb * 32;
+    if (threadIdx.x < B) {
+        float inv = 1.f;
+        if constexpr (PRO == Pro::AddNorm) {
+            float t = 0.f;
+            for (int q = 0; q < p.nsteps; ++q) t += p.ssq[(size_t)q * B + threadIdx.x];  // part 0's sums
+            inv = rms_inv(t, d_model, p.a.eps);
+        }
+        s_inv[threadIdx.x] = inv;
+    }
+    __syncthreads();
+    if constexpr (PRO == Pro::AddNorm) write_xout_slice<B, 256>(p.a, d_model, s_inv, blockIdx.x, gridDim.x);
+    const int64_t total = (int64_t)p.rows * B;
+    for (int64_t it = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; it < total; it += (int64_t)gridDim.x * blockDim.x) {
+        const int row = (int)(it / B), b = (int)(it - (it / B) * B);
+        const int g = row >> 2, r = row & 3;
+        float v[NM];
+#pragma unroll
+        for (int m = 0; m < NM; ++m) v[m] = 0.f;
+        for (int q = 0; q < p.nsteps; ++q) {
+            const float* src = p.part + ((size_t)q * p.ngroups + g) * (32 * NM);
+#pragma unroll
+            for (int m = 0; m < NM; ++m) v[m] += src[32 * m + r * B + b];
+        }
+        const float inv = s_inv[b];
+        p.a.y[(size_t)b * p.a.y_stride + row] = n_epilogue<EPI>(__fmul_rn(v[0], inv), __fmul_rn(v[NM - 1], inv));
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Orientation N, K staged in chunks (x larger than the shared-memory budget)
 // ---------------------------------------------------------------------------
 struct NCParams {
@@ -1133,6 +1330,54 @@ void run_ns(const at_qmat* m, const GemvArgs& a, const StreamPlan& sp, cudaStrea
     launch(fn, sp.grid, sp.smem, s, pdl, p, S_THREADS);
 }
 
+// Layout of the batch 3..8 split-K scratch: partials then sums of squares.
+struct NQLayout {
+    int P = 1;
+    size_t part_floats = 0, ssq_floats = 0;
+};
+NQLayout nq_layout(const at_qmat* m, int batch, int num_sms, int nm) {
+    NQLayout l;
+    const int64_t steps = m->nsteps;
+    l.P = (int)std::max<int64_t>(1, std::min<int64_t>(m->ngroups, (num_sms + steps - 1) / steps));
+    l.part_floats = (size_t)steps * m->ngroups * 32 * nm;  // one 32-value partial per matrix and group
+    l.ssq_floats = (size_t)l.P * steps * batch;
+    return l;
+}
+
+template <int QT, int B, Pro PRO, Epi EPI>
+void run_nq(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, bool pdl) {
+    constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
+    const NQLayout l = nq_layout(m, B, num_sms, NM);
+    NQParams p{};
+    p.tiles[0] = m->tiles;
+    p.tiles[1] = (NM == 2) ? a.m2->tiles : m->tiles;
+    p.rows = (int)m->rows;
+    p.nb = (int)(m->cols / QK);
+    p.ngroups = (int)m->ngroups;
+    p.nsteps = (int)m->nsteps;
+    p.P = l.P;
+    p.part = a.scratch;
+    p.ssq = a.scratch + l.part_floats;
+    p.a = a;
+    const int smem = B * 32 * XPAD * 4 + Q_WARPS * Q_NST * NM * NTile<QT>::BYTES;
+    const void* fn = reinterpret_cast<const void*>(&gemv_nq_kernel<QT, B, PRO, EPI>);
+    ensure_smem(fn, smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.P, p.nsteps);
+    cfg.blockDim = dim3(Q_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    void* args[] = {&p};
+    AT_CUDA(cudaLaunchKernelExC(&cfg, fn, args));
+    const int rgrid = (int)std::min<int64_t>(((int64_t)p.rows * B + 255) / 256, (int64_t)num_sms * 4);
+    launch(reinterpret_cast<const void*>(&gemv_nq_reduce_kernel<B, PRO, EPI>), std::max(1, rgrid), 0, s, pdl, p, 256);
+}
+
 template <int QT, int B, Pro PRO, Epi EPI>
 void run_n(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, bool pdl) {
     constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
@@ -1141,6 +1386,8 @@ void run_n(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, boo
         const StreamPlan sp = n_stream_plan<QT, B, EPI>(m, num_sms);
         if (sp.nst == 4) { run_ns<QT, B, PRO, EPI, 4>(m, a, sp, s, pdl); return; }
         if (sp.nst == 2) { run_ns<QT, B, PRO, EPI, 2>(m, a, sp, s, pdl); return; }
+    } else {
+        if (a.scratch) { run_nq<QT, B, PRO, EPI>(m, a, num_sms, s, pdl); return; }
     }
     constexpr int R = (NM == 2) ? 2 : 4;
     NCParams p{};
@@ -1231,10 +1478,16 @@ void gemv_t_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* float
 
 void gemv_n_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* floats, size_t* counters) {
     // upper bound over the epilogues (gate/up pairs carry two partials per row)
+    if (batch > 2) {
+        const NQLayout l = nq_layout(m, batch, num_sms, 2);
+        *floats = l.part_floats + l.ssq_floats;
+        *counters = 0;
+        return;
+    }
     const int64_t U = m->ngroups * m->nsteps;
     const size_t grid = (size_t)std::max<int64_t>(1, std::min<int64_t>(num_sms, U));
-    *floats = (batch <= 2 && grid > 1) ? 2 * grid * 2 * 4 * batch : 0;
-    *counters = (batch <= 2 && grid > 1) ? (size_t)m->ngroups : 0;
+    *floats = (grid > 1) ? 2 * grid * 2 * 4 * batch : 0;
+    *counters = (grid > 1) ? (size_t)m->ngroups : 0;
 }
 
 void launch_gemv_n(const at_qmat* m, int batch, Pro pro, Epi epi, const GemvArgs& a, int num_sms,
