@@ -922,9 +922,12 @@ __global__ void __launch_bounds__(THREADS) gemv_nc_kernel(const NCParams p) {
 // ---------------------------------------------------------------------------
 // Orientation T (tiles of 32 rows x 1 block column)
 // ---------------------------------------------------------------------------
+constexpr int TR = 8;  // per-thread cp.async ring depth of the batch <= 2 T kernel (steps)
+
 struct TParams {
     const uint8_t* tiles;
     int64_t tile_bytes;
+    int ring_off;      // byte offset of the weight ring in dynamic shared memory
     int E;             // input rows
     int ngroups;       // 32-row groups
     int n_bc;          // block columns (outputs / 32)
@@ -1050,13 +1053,45 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
     const int row_in_warp = lane / LPB;
     const uint8_t* col = p.tiles + (size_t)c * p.ngroups * p.tile_bytes;
 
-    // first U steps of weights before waiting on earlier kernels
+    // Batch <= 2 (a lane owns whole rows): every thread copies its own rows'
+    // quant bytes and scale word into a per-thread cp.async ring, TR steps
+    // deep; larger batches keep U steps in registers. Weights are never
+    // written by earlier kernels, so the first steps start before the wait.
+    constexpr int NVQ = QTraits<QT>::NV;
+    uint4* ringq = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(xs) + p.ring_off);  // [TR][NVQ][THREADS]
+    uint32_t* rings = reinterpret_cast<uint32_t*>(ringq + TR * NVQ * THREADS);              // [TR][THREADS]
+    int t_issued = 0;
+    auto t_issue = [&]() {
+        if constexpr (CPL == 32) {
+            const int i = t_issued * C::STEP + warp * C::ROWS_PER_WARP + row_in_warp;
+            if (i < ne) {
+                const int e = e_lo + i;
+                const uint8_t* tile = col + (int64_t)(e >> 5) * p.tile_bytes;
+                const int l = e & 31, k = t_issued & (TR - 1);
+#pragma unroll
+                for (int v = 0; v < NVQ; ++v)
+                    cp_async16((uint32_t)__cvta_generic_to_shared(ringq + (k * NVQ + v) * THREADS + tid),
+                               tile + 64 + l * QTraits<QT>::QB + 16 * v);
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                                 (uint32_t)__cvta_generic_to_shared(rings + k * THREADS + tid)),
+                             "l"(tile + 4 * (l >> 1))
+                             : "memory");
+            }
+            cp_commit();
+            ++t_issued;
+        }
+    };
     uint4 q[U][2];
     float dsc[U];
+    if constexpr (CPL == 32) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-        const int i = u * C::STEP + warp * C::ROWS_PER_WARP + row_in_warp;
-        if (i < ne) t_load<QT, CPL>(q[u], dsc[u], col, p.tile_bytes, e_lo + i, quarter);
+        for (int k = 0; k < TR; ++k) t_issue();
+    } else {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = u * C::STEP + warp * C::ROWS_PER_WARP + row_in_warp;
+            if (i < ne) t_load<QT, CPL>(q[u], dsc[u], col, p.tile_bytes, e_lo + i, quarter);
+        }
     }
     pdl_wait();
 
@@ -1128,23 +1163,50 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
 #pragma unroll
         for (int k = 0; k < NPAIR; ++k) acc[b][k] = f2(0.f, 0.f);
 
-    for (int base = 0; base < ne; base += C::STEP * U) {
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int i = base + u * C::STEP + warp * C::ROWS_PER_WARP + row_in_warp;
+    if constexpr (CPL == 32) {
+        const int n_u = (ne + C::STEP - 1) / C::STEP;
+        for (int u = 0; u < n_u; ++u) {
+            cp_wait<TR - 1>();  // this thread's copies of step u have landed (it reads only its own)
+            const int i = u * C::STEP + warp * C::ROWS_PER_WARP + row_in_warp;
             if (i < ne) {
+                const int k = u & (TR - 1);
+                uint4 qq[2];
+#pragma unroll
+                for (int v = 0; v < NVQ; ++v) qq[v] = ringq[(k * NVQ + v) * THREADS + tid];
+                const uint32_t sw = rings[k * THREADS + tid];
+                const float d = fp16_ftz_fast(((e_lo + i) & 1) ? (sw >> 16) : (sw & 0xFFFFu));
                 float2 wv[NPAIR];
-                t_decode<QT, CPL>(q[u], quarter, wv);
+                t_decode<QT, CPL>(qq, quarter, wv);
 #pragma unroll
                 for (int b = 0; b < B; ++b) {
-                    const float sv = __fmul_rn(dsc[u], xs[b * p.e_per_split + i]);
+                    const float sv = __fmul_rn(d, xs[b * p.e_per_split + i]);
                     const float2 s2 = f2(sv, sv);
 #pragma unroll
-                    for (int k = 0; k < NPAIR; ++k) acc[b][k] = __ffma2_rn(wv[k], s2, acc[b][k]);
+                    for (int kk = 0; kk < NPAIR; ++kk) acc[b][kk] = __ffma2_rn(wv[kk], s2, acc[b][kk]);
                 }
             }
-            const int in = i + C::STEP * U;
-            if (in < ne) t_load<QT, CPL>(q[u], dsc[u], col, p.tile_bytes, e_lo + in, quarter);
+            t_issue();  // refills slot u % TR with step u + TR
+        }
+        cp_wait<0>();
+    } else {
+        for (int base = 0; base < ne; base += C::STEP * U) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = base + u * C::STEP + warp * C::ROWS_PER_WARP + row_in_warp;
+                if (i < ne) {
+                    float2 wv[NPAIR];
+                    t_decode<QT, CPL>(q[u], quarter, wv);
+#pragma unroll
+                    for (int b = 0; b < B; ++b) {
+                        const float sv = __fmul_rn(dsc[u], xs[b * p.e_per_split + i]);
+                        const float2 s2 = f2(sv, sv);
+#pragma unroll
+                        for (int k = 0; k < NPAIR; ++k) acc[b][k] = __ffma2_rn(wv[k], s2, acc[b][k]);
+                    }
+                }
+                const int in = i + C::STEP * U;
+                if (in < ne) t_load<QT, CPL>(q[u], dsc[u], col, p.tile_bytes, e_lo + in, quarter);
+            }
         }
     }
 
@@ -1439,7 +1501,9 @@ void run_t(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, boo
     t_config(m, B, num_sms, &p.S, &p.e_per_split);
     p.a = a;
     if (p.S > 1) AT_REQUIRE(a.scratch && a.counters, AT_ERR_STATE, "T GEMV needs split scratch");
-    const int smem = B * p.e_per_split * 4;
+    p.ring_off = (B * p.e_per_split * 4 + 15) / 16 * 16;
+    const int ring_bytes = (TCfg<B>::CPL == 32) ? TR * THREADS * (16 * QTraits<QT>::NV + 4) : 0;
+    const int smem = p.ring_off + ring_bytes;
     const void* fn = reinterpret_cast<const void*>(&gemv_t_kernel<QT, B, PRO, EPI>);
     ensure_smem(fn, smem);
     launch(fn, p.n_bc * p.S, smem, s, pdl, p);
