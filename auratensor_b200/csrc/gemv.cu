@@ -122,6 +122,71 @@ __device__ __forceinline__ float dot32(const uint4* q, const float4* xr) {
     return (a0.x + a0.y) + (a1.x + a1.y);
 }
 
+// Subnormal-scaled form of dot32 (the batch <= 2 stream kernel).
+// A quant field masked in place and read as a float is exactly
+// field * 2^-149: the bit patterns 0 .. 2^24 - 1 (subnormals and the first
+// normal binade) encode the integers N as N * 2^-149. So one LOP3 per weight
+// gives q * 2^(s_k) * 2^-149, s_k the field's bit offset: Q4_0 nibble j of a
+// 32-bit word at offset 4j (j < 6; nibbles 6 and 7 after one shift by 24, at
+// offsets 0 and 4), Q8_0 byte j (sign bit flipped: q + 128) at 8j (j < 3;
+// byte 3 after the shift, at 0). The staged x of element k carries the
+// matching power of two 2^(kXExp - s_k) (x_scale_dn), so every product is
+// exactly q_k * x_k * 2^(kXExp - 149), one FFMA2 per two weights, no
+// subtraction. The offset (8 or 128) times the block's sum of x, staged with
+// the block as sx = (sum x_k) * 2^(kXExp - 149), is taken off once per
+// block, and kDnUnscale = 2^(149 - kXExp) goes into the block scale.
+// Products are exact; only the FP32 summation differs from dot32 (the
+// offset is subtracted from the block sum instead of from each weight).
+// Requires |x| < 2^(128 - kXExp) = 2^48 for the staged values.
+constexpr int kXExp = 80;
+constexpr float kDnUnscale = 590295810358705651712.f;  // 2^69 = 2^(149 - kXExp)
+static_assert(149 - kXExp == 69, "kDnUnscale is 2^69");
+
+// Power of two that element k (k % 8 for Q4_0, k % 4 for Q8_0) of a block is
+// staged with.
+template <int QT>
+__host__ __device__ constexpr int x_shift_dn(int k) {
+    if constexpr (QT == AT_GGML_Q4_0) {
+        const int j = k & 7;
+        return j < 6 ? 4 * j : 4 * (j - 6);
+    } else {
+        const int j = k & 3;
+        return j < 3 ? 8 * j : 0;
+    }
+}
+
+__device__ __forceinline__ float bits_f(uint32_t u) { return __uint_as_float(u); }
+// 2^n for -126 <= n <= 127.
+__device__ __forceinline__ float exp2_i(int n) { return __uint_as_float((uint32_t)(n + 127) << 23); }
+
+template <int QT>
+__device__ __forceinline__ float dot32_dn(const uint4* q, const float4* xr, float sx) {
+    float2 a0 = f2(0.f, 0.f), a1 = f2(0.f, 0.f);
+    if constexpr (QT == AT_GGML_Q4_0) {
+        const uint32_t ws[4] = {q[0].x, q[0].y, q[0].z, q[0].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t w = ws[i], t = w >> 24;  // word i: elements 8i .. 8i + 7
+            a0 = __ffma2_rn(f2(bits_f(w & 0xFu), bits_f(w & 0xF0u)), f2(xr[2 * i].x, xr[2 * i].y), a0);
+            a1 = __ffma2_rn(f2(bits_f(w & 0xF00u), bits_f(w & 0xF000u)), f2(xr[2 * i].z, xr[2 * i].w), a1);
+            a0 = __ffma2_rn(f2(bits_f(w & 0xF0000u), bits_f(w & 0xF00000u)), f2(xr[2 * i + 1].x, xr[2 * i + 1].y), a0);
+            a1 = __ffma2_rn(f2(bits_f(t & 0xFu), bits_f(t & 0xF0u)), f2(xr[2 * i + 1].z, xr[2 * i + 1].w), a1);
+        }
+        return fmaf(-8.f, sx, (a0.x + a0.y) + (a1.x + a1.y));
+    } else {
+        const uint32_t ws[8] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t w = ws[i];  // word i: elements 4i .. 4i + 3
+            a0 = __ffma2_rn(f2(bits_f((w ^ 0x80u) & 0xFFu), bits_f((w ^ 0x8000u) & 0xFF00u)), f2(xr[i].x, xr[i].y),
+                            a0);
+            a1 = __ffma2_rn(f2(bits_f((w ^ 0x800000u) & 0xFF0000u), bits_f((w >> 24) ^ 0x80u)), f2(xr[i].z, xr[i].w),
+                            a1);
+        }
+        return fmaf(-128.f, sx, (a0.x + a0.y) + (a1.x + a1.y));
+    }
+}
+
 // Stages x (or the normed x + y) for blocks [b0, b0 + nbc) of B rows into
 // shared memory, natural order, XPAD floats per block.
 // float4 global loads, eight in flight per thread before any is stored.
@@ -357,7 +422,7 @@ __device__ __forceinline__ void finish_shared_segments(const GemvArgs& a, const 
 // thread's sums of (xin + yin)^2 per row: the RMSNorm scale 1/rms multiplies
 // the finished dot products instead of every staged element, so the staging
 // needs no prior reduction pass.
-template <int B, Pro PRO, int NT>
+template <int QT, int B, Pro PRO, int NT>
 __device__ __forceinline__ void stage_x_fold(float* xs, const GemvArgs& a, int nb, float* ss) {
     const int nf4 = nb * 8;
     const int total = B * nf4;
@@ -399,7 +464,31 @@ __device__ __forceinline__ void stage_x_fold(float* xs, const GemvArgs& a, int n
                     o = make_float4(__fmul_rn(o.x, g[k].x), __fmul_rn(o.y, g[k].y), __fmul_rn(o.z, g[k].z),
                                     __fmul_rn(o.w, g[k].w));
                 }
-                *reinterpret_cast<float4*>(xs + ((size_t)bb * nb + (r >> 3)) * XPAD + (r & 7) * 4) = o;
+                v[k] = o;
+            }
+        }
+        // Block sums (the 8 float4 of a block sit in 8 consecutive lanes: the
+        // row length and the index bases are multiples of 8), then the
+        // subnormal-form scaling of dot32_dn.
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int idx = base + k * NT + threadIdx.x;
+            const bool in = idx < total;
+            float bs = in ? (v[k].x + v[k].y) + (v[k].z + v[k].w) : 0.f;
+            bs += __shfl_xor_sync(0xffffffffu, bs, 1);
+            bs += __shfl_xor_sync(0xffffffffu, bs, 2);
+            bs += __shfl_xor_sync(0xffffffffu, bs, 4);
+            if (in) {
+                const int bb = idx / nf4, r = idx - bb * nf4;
+                const int e0 = (r & 7) * 4;  // element of the block
+                float* dst = xs + ((size_t)bb * nb + (r >> 3)) * XPAD;
+                const float4 o = v[k];
+                *reinterpret_cast<float4*>(dst + e0) =
+                    make_float4(__fmul_rn(o.x, exp2_i(kXExp - x_shift_dn<QT>(e0))),
+                                __fmul_rn(o.y, exp2_i(kXExp - x_shift_dn<QT>(e0 + 1))),
+                                __fmul_rn(o.z, exp2_i(kXExp - x_shift_dn<QT>(e0 + 2))),
+                                __fmul_rn(o.w, exp2_i(kXExp - x_shift_dn<QT>(e0 + 3))));
+                if ((r & 7) == 0) dst[32] = __fmul_rn(bs, exp2_i(kXExp - 149));
             }
         }
     }
@@ -482,7 +571,7 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_ns_kernel(const NSParams p)
     const int d_model = p.nb * 32;
     {
         float ss[B];
-        stage_x_fold<B, PRO, S_THREADS>(xs, p.a, p.nb, ss);
+        stage_x_fold<QT, B, PRO, S_THREADS>(xs, p.a, p.nb, ss);
         if constexpr (PRO == Pro::AddNorm) {
 #pragma unroll
             for (int b = 0; b < B; ++b) {
@@ -516,7 +605,8 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_ns_kernel(const NSParams p)
 #pragma unroll
                     for (int v = 0; v < NV; ++v)
                         q[m * 4 + r][v] = *reinterpret_cast<const uint4*>(tb + 256 + (r * 32 + lane) * TL::QB + 16 * v);
-                    dsc[m * 4 + r] = fp16_ftz_fast(*reinterpret_cast<const uint16_t*>(tb + (r * 32 + lane) * 2));
+                    dsc[m * 4 + r] = __fmul_rn(
+                        fp16_ftz_fast(*reinterpret_cast<const uint16_t*>(tb + (r * 32 + lane) * 2)), kDnUnscale);
                 }
 #pragma unroll
             for (int b = 0; b < B; ++b) {
@@ -524,8 +614,9 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_ns_kernel(const NSParams p)
                 float4 xr[8];
 #pragma unroll
                 for (int k = 0; k < 8; ++k) xr[k] = xv[k];
+                const float sx = xs[((size_t)b * p.nb + j) * XPAD + 32];
 #pragma unroll
-                for (int i = 0; i < NM * 4; ++i) acc[i][b] = fmaf(dsc[i], dot32<QT>(q[i], xr), acc[i][b]);
+                for (int i = 0; i < NM * 4; ++i) acc[i][b] = fmaf(dsc[i], dot32_dn<QT>(q[i], xr, sx), acc[i][b]);
             }
         }
         __syncwarp();  // every lane is done with this slot before it is refilled
@@ -987,6 +1078,34 @@ __device__ __forceinline__ void t_decode(const uint4* q, int quarter, float2* wv
     }
 }
 
+// Subnormal-scaled decode of a lane's 32 weights (see dot32_dn): pair k holds
+// the fields of columns 2k, 2k+1 masked in place, q * 2^(x_shift_dn(col) - 149)
+// (Q8_0: q + 128). The T kernel multiplies them by d * x * 2^kXExp and, per
+// column, scales the sums back by 2^(149 - kXExp - x_shift_dn(col)) and takes
+// off the offset (8 or 128) times the lane's sum of d * x.
+template <int QT>
+__device__ __forceinline__ void t_decode_dn(const uint4* q, float2* wv) {
+    if constexpr (QT == AT_GGML_Q4_0) {
+        const uint32_t ws[4] = {q[0].x, q[0].y, q[0].z, q[0].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t w = ws[i], t = w >> 24;
+            wv[4 * i + 0] = f2(bits_f(w & 0xFu), bits_f(w & 0xF0u));
+            wv[4 * i + 1] = f2(bits_f(w & 0xF00u), bits_f(w & 0xF000u));
+            wv[4 * i + 2] = f2(bits_f(w & 0xF0000u), bits_f(w & 0xF00000u));
+            wv[4 * i + 3] = f2(bits_f(t & 0xFu), bits_f(t & 0xF0u));
+        }
+    } else {
+        const uint32_t ws[8] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t w = ws[i];
+            wv[2 * i + 0] = f2(bits_f((w ^ 0x80u) & 0xFFu), bits_f((w ^ 0x8000u) & 0xFF00u));
+            wv[2 * i + 1] = f2(bits_f((w ^ 0x800000u) & 0xFF0000u), bits_f((w >> 24) ^ 0x80u));
+        }
+    }
+}
+
 // Stores output column j of batch row b. Every lane of the warp calls it (the
 // RoPE pair partner of column j is column j ^ 1, held by the neighbouring lane).
 // RoPE coefficients (cos, sin) of output column j of batch row b (QKV epilogue;
@@ -1158,10 +1277,13 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
     __syncthreads();
 
     float2 acc[B][NPAIR];
+    float dsum[B];  // CPL == 32: this lane's sum of d * x (offset correction)
 #pragma unroll
-    for (int b = 0; b < B; ++b)
+    for (int b = 0; b < B; ++b) {
+        dsum[b] = 0.f;
 #pragma unroll
         for (int k = 0; k < NPAIR; ++k) acc[b][k] = f2(0.f, 0.f);
+    }
 
     if constexpr (CPL == 32) {
         const int n_u = (ne + C::STEP - 1) / C::STEP;
@@ -1176,11 +1298,13 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
                 const uint32_t sw = rings[k * THREADS + tid];
                 const float d = fp16_ftz_fast(((e_lo + i) & 1) ? (sw >> 16) : (sw & 0xFFFFu));
                 float2 wv[NPAIR];
-                t_decode<QT, CPL>(qq, quarter, wv);
+                t_decode_dn<QT>(qq, wv);
 #pragma unroll
                 for (int b = 0; b < B; ++b) {
                     const float sv = __fmul_rn(d, xs[b * p.e_per_split + i]);
-                    const float2 s2 = f2(sv, sv);
+                    dsum[b] += sv;
+                    const float svs = __fmul_rn(sv, exp2_i(kXExp));
+                    const float2 s2 = f2(svs, svs);
 #pragma unroll
                     for (int kk = 0; kk < NPAIR; ++kk) acc[b][kk] = __ffma2_rn(wv[kk], s2, acc[b][kk]);
                 }
@@ -1214,10 +1338,20 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
 #pragma unroll
     for (int b = 0; b < B; ++b) {
         float v[CPL];
+        if constexpr (CPL == 32) {
+            // back from the subnormal-scaled sums of t_decode_dn
+            const float corr = __fmul_rn(QT == AT_GGML_Q4_0 ? -8.f : -128.f, dsum[b]);
 #pragma unroll
-        for (int k = 0; k < NPAIR; ++k) {
-            v[2 * k] = acc[b][k].x;
-            v[2 * k + 1] = acc[b][k].y;
+            for (int k = 0; k < NPAIR; ++k) {
+                v[2 * k] = fmaf(acc[b][k].x, exp2_i(149 - kXExp - x_shift_dn<QT>(2 * k)), corr);
+                v[2 * k + 1] = fmaf(acc[b][k].y, exp2_i(149 - kXExp - x_shift_dn<QT>(2 * k + 1)), corr);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < NPAIR; ++k) {
+                v[2 * k] = acc[b][k].x;
+                v[2 * k + 1] = acc[b][k].y;
+            }
         }
         int n = CPL;
 #pragma unroll

@@ -115,12 +115,19 @@ __device__ __forceinline__ float exp_ref(float v) { return (float)exp((double)v)
 // over positions [p0, p0 + n) = (K q) * scale, chunk max m, l = sum exp(s - m),
 // o = sum exp(s - m) V. K and V of the chunk are staged in shared memory with
 // all of the CTA's 128-bit loads in flight at once.
-template <int HD>
+// FUSED (decode step): the last CTA of a (sequence, KV head) to finish its
+// chunk (ticket per pair in `cnt`, reset by that CTA) merges the chunk
+// partials of the G heads into `att` (the log-sum-exp combine of
+// attn_combine_kernel, without a second launch). Needs G * chunks <= CH * HD
+// (the merge weights reuse the K staging buffer).
+template <int HD, bool FUSED = false>
 __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict__ q, const float* __restrict__ kc,
                                                          const float* __restrict__ vc,
                                                          const int64_t* __restrict__ pos, float* __restrict__ part,
                                                          int Hl, int Hkvl, int ctx, int64_t slot_stride,
-                                                         int nchunk_max, float scale) {
+                                                         int nchunk_max, float scale,
+                                                         unsigned* __restrict__ cnt = nullptr,
+                                                         float* __restrict__ att = nullptr) {
     constexpr int G_MAX = 8;
     constexpr int F4 = HD / 4;  // float4 per row
     __shared__ __align__(16) float4 ks[CH][F4];
@@ -128,6 +135,7 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
     __shared__ __align__(16) float4 qs[G_MAX][F4];
     __shared__ float sc[G_MAX][CH];
     __shared__ float s_m[G_MAX], s_l[G_MAX];
+    __shared__ int s_last;
     const int kvh = blockIdx.x, chunk = blockIdx.y, b = blockIdx.z;
     const int G = Hl / Hkvl;
     pdl_trigger();
@@ -203,6 +211,60 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
         float* dst = part + (((size_t)b * Hl + h) * nchunk_max + chunk) * (HD + 2);
         dst[dd] = acc;
         if (dd == 0) { dst[HD] = s_m[g]; dst[HD + 1] = s_l[g]; }
+    }
+    if constexpr (FUSED) {
+        const int nch = (int)((P + CH - 1) / CH);
+        // Publish this CTA's partial (barrier, then a device-scope fence that
+        // is cumulative over the stores ordered before it) and take a ticket.
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            const unsigned t = atomicAdd(&cnt[b * Hkvl + kvh], 1u);
+            s_last = (t == (unsigned)(nch - 1));
+            if (s_last) {
+                cnt[b * Hkvl + kvh] = 0u;
+                __threadfence();
+            }
+        }
+        __syncthreads();
+        if (!s_last) return;
+        float* sw = reinterpret_cast<float*>(ks);  // [G][nch] merge weights
+        if (warp < G) {
+            const int g = warp;
+            const float* base = part + ((size_t)b * Hl + kvh * G + g) * nchunk_max * (HD + 2);
+            float mx = -INFINITY;
+            for (int c = lane; c < nch; c += 32) {
+                const float mc = __ldcg(base + (size_t)c * (HD + 2) + HD);
+                sw[g * nch + c] = mc;
+                mx = fmaxf(mx, mc);
+            }
+            mx = warp_max(mx);
+            float l = 0.f;
+            for (int c = lane; c < nch; c += 32) {
+                const float w = exp_ref(__fsub_rn(sw[g * nch + c], mx));
+                sw[g * nch + c] = w;
+                l = fmaf(__ldcg(base + (size_t)c * (HD + 2) + HD + 1), w, l);
+            }
+            l = warp_sum(l);
+            if (lane == 0) s_l[g] = l;
+        }
+        __syncthreads();
+        for (int o = tid; o < G * HD; o += 256) {
+            const int g = o / HD, dd = o - g * HD;
+            const float* base = part + ((size_t)b * Hl + kvh * G + g) * nchunk_max * (HD + 2) + dd;
+            const float* wg = sw + g * nch;
+            float acc = 0.f;
+            int c = 0;
+            for (; c + 8 <= nch; c += 8) {
+                float v[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = __ldcg(base + (size_t)(c + k) * (HD + 2));
+#pragma unroll
+                for (int k = 0; k < 8; ++k) acc = fmaf(v[k], wg[c + k], acc);
+            }
+            for (; c < nch; ++c) acc = fmaf(__ldcg(base + (size_t)c * (HD + 2)), wg[c], acc);
+            att[(size_t)b * Hl * HD + (size_t)(kvh * G + g) * HD + dd] = __fdiv_rn(acc, s_l[g]);
+        }
     }
 }
 
@@ -582,6 +644,7 @@ struct at_model {
     // activations
     float *xa = nullptr, *xb = nullptr, *y = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
     float *logits = nullptr, *logits_local = nullptr, *att_part = nullptr;
+    unsigned* attn_cnt = nullptr;  // [max_batch][Hkvl] tickets of the fused decode attention
     float *kcache = nullptr, *vcache = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
     float* scratch = nullptr;
     unsigned* counters = nullptr;
@@ -749,18 +812,36 @@ void enqueue_step(at_model* m, int B) {
             dim3 g1(m->Hkvl, m->nchunk_max, B);
             const float* qp = m->q;
             const int64_t* dp = m->d_pos;
-            if (hd == 128)
-                launch_k(attn_split_kernel<128>, g1, 256, s, m->pdl, qp, (const float*)kc, (const float*)vc, dp,
-                         m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max, scale);
-            else
-                launch_k(attn_split_kernel<64>, g1, 256, s, m->pdl, qp, (const float*)kc, (const float*)vc, dp,
-                         m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max, scale);
-            dim3 g2(m->Hl, B);
-            const float* pp = m->att_part;
-            if (hd == 128)
-                launch_k(attn_combine_kernel<128>, g2, 128, s, m->pdl, pp, dp, m->att, m->Hl, m->nchunk_max);
-            else
-                launch_k(attn_combine_kernel<64>, g2, 64, s, m->pdl, pp, dp, m->att, m->Hl, m->nchunk_max);
+            // one launch (split + merge by the last CTA) when the merge
+            // weights of a KV head's query heads fit the K staging buffer
+            const bool fused = (m->Hl / m->Hkvl) * m->nchunk_max <= CH * hd;
+            if (fused) {
+                if (hd == 128)
+                    launch_k(attn_split_kernel<128, true>, g1, 256, s, m->pdl, qp, (const float*)kc,
+                             (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
+                             m->nchunk_max, scale, m->attn_cnt, m->att);
+                else
+                    launch_k(attn_split_kernel<64, true>, g1, 256, s, m->pdl, qp, (const float*)kc,
+                             (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
+                             m->nchunk_max, scale, m->attn_cnt, m->att);
+            } else {
+                unsigned* no_cnt = nullptr;
+                float* no_att = nullptr;
+                if (hd == 128)
+                    launch_k(attn_split_kernel<128>, g1, 256, s, m->pdl, qp, (const float*)kc, (const float*)vc,
+                             dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max, scale,
+                             no_cnt, no_att);
+                else
+                    launch_k(attn_split_kernel<64>, g1, 256, s, m->pdl, qp, (const float*)kc, (const float*)vc,
+                             dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max, scale,
+                             no_cnt, no_att);
+                dim3 g2(m->Hl, B);
+                const float* pp = m->att_part;
+                if (hd == 128)
+                    launch_k(attn_combine_kernel<128>, g2, 128, s, m->pdl, pp, dp, m->att, m->Hl, m->nchunk_max);
+                else
+                    launch_k(attn_combine_kernel<64>, g2, 64, s, m->pdl, pp, dp, m->att, m->Hl, m->nchunk_max);
+            }
         }
         {
             ProfScope p(m, AT_PROF_WO);
@@ -909,7 +990,7 @@ void destroy_model(at_model* m) {
     qmat_free(&m->tok);
     qmat_free(&m->out);
     void* bufs[] = {m->out_norm, m->xa, m->xb, m->y, m->q, m->att, m->h, m->logits, m->logits_local,
-                    m->att_part, m->kcache, m->vcache, m->rope_cos, m->rope_sin, m->scratch, m->counters,
+                    m->att_part, m->attn_cnt, m->kcache, m->vcache, m->rope_cos, m->rope_sin, m->scratch, m->counters,
                     m->d_tokens, m->d_pos, m->d_argmax, m->d_gen_out, m->d_gen_count, m->d_argkey,
                     m->d_step, m->ar_base, m->d_ar_err, m->pf_xa, m->pf_xb, m->pf_y, m->pf_qkv, m->pf_q,
                     m->pf_att, m->pf_g, m->pf_u, m->pf_part, m->pf_tok, m->pf_pos, m->pf_err, m->pf_xbf, m->pf_ws};
@@ -1244,6 +1325,7 @@ int at_model_finalize(at_model* m) {
         }
         m->nchunk_max = (m->ctx_len + CH - 1) / CH;
         alloc_zero((void**)&m->att_part, (size_t)B * m->Hl * m->nchunk_max * (hd + 2) * 4);
+        alloc_zero((void**)&m->attn_cnt, (size_t)B * m->Hkvl * sizeof(unsigned));
         // KV cache (inference/KVCache.java:43-63): [slot][layer][kvHead][ctx][headDim] fp32
         m->slot_stride = (int64_t)m->L * m->Hkvl * m->ctx_len * hd;
         alloc_zero((void**)&m->kcache, (size_t)B * m->slot_stride * 4);
