@@ -422,8 +422,52 @@ __device__ __forceinline__ void finish_shared_segments(const GemvArgs& a, const 
 // thread's sums of (xin + yin)^2 per row: the RMSNorm scale 1/rms multiplies
 // the finished dot products instead of every staged element, so the staging
 // needs no prior reduction pass.
+// The CTA's slice of the normed residual stream (AddNorm), float4 [i0, i0 + len)
+// of every row (the split of write_xout_slice). When B * len <= kXoutStash
+// the staging pass parks t = xin + yin and gamma of the slice in shared memory
+// and the kernel writes (t * inv) * gamma once 1/rms is known, with no second
+// load at its end; longer slices are written by write_xout_slice.
+constexpr int kXoutStash = 16;
+struct XoutStash {
+    float4 t[kXoutStash];
+    float4 g[kXoutStash];
+};
+__device__ __forceinline__ void xout_slice(int d, int c, int C, int* i0, int* len) {
+    const int n4 = d / 4;
+    *i0 = (int)((int64_t)c * n4 / C);
+    *len = (int)((int64_t)(c + 1) * n4 / C) - *i0;
+}
+template <int B, int NT>
+__device__ __forceinline__ void stash_put(XoutStash* st, int i0, int len, int bb, int r, float4 t, float4 g) {
+    if (B * len <= kXoutStash && r >= i0 && r < i0 + len) {
+        st->t[bb * len + r - i0] = t;
+        st->g[bb * len + r - i0] = g;
+    }
+}
+// Writes the stashed slice (barrier between stash_put and this call), or the
+// slice from global memory when it was too long to stash.
+template <int B, int NT>
+__device__ __forceinline__ void write_xout_stashed(const GemvArgs& a, int d, const float* s_inv, int c, int C,
+                                                   const XoutStash* st) {
+    int i0, len;
+    xout_slice(d, c, C, &i0, &len);
+    if (B * len > kXoutStash) {
+        write_xout_slice<B, NT>(a, d, s_inv, c, C);
+        return;
+    }
+    const int tid = threadIdx.x;
+    if (tid < B * len) {
+        const int bb = tid / len, i4 = i0 + tid - bb * len;
+        const float4 t = st->t[tid], g = st->g[tid];
+        const float inv = s_inv[bb];
+        *reinterpret_cast<float4*>(a.xout + (size_t)bb * a.x_stride + (size_t)i4 * 4) = make_float4(
+            norm_apply(t.x, inv, g.x), norm_apply(t.y, inv, g.y), norm_apply(t.z, inv, g.z), norm_apply(t.w, inv, g.w));
+    }
+}
+
 template <int QT, int B, Pro PRO, int NT>
-__device__ __forceinline__ void stage_x_fold(float* xs, const GemvArgs& a, int nb, float* ss) {
+__device__ __forceinline__ void stage_x_fold(float* xs, const GemvArgs& a, int nb, float* ss, XoutStash* st,
+                                             int st_i0, int st_len) {
     const int nf4 = nb * 8;
     const int total = B * nf4;
 #pragma unroll
@@ -461,6 +505,7 @@ __device__ __forceinline__ void stage_x_fold(float* xs, const GemvArgs& a, int n
 #pragma unroll
                     for (int b = 0; b < B; ++b)
                         if (b == bb) ss[b] += q;
+                    stash_put<B, NT>(st, st_i0, st_len, bb, r, o, g[k]);
                     o = make_float4(__fmul_rn(o.x, g[k].x), __fmul_rn(o.y, g[k].y), __fmul_rn(o.z, g[k].z),
                                     __fmul_rn(o.w, g[k].w));
                 }
@@ -530,6 +575,7 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_ns_kernel(const NSParams p)
     __shared__ float s_ss[S_WARPS * B];  // AddNorm: per-warp sums of squares
     __shared__ float s_inv[B];
     __shared__ int s_last[2];
+    __shared__ XoutStash s_xo;  // AddNorm: this CTA's slice of the normed x
 
     pdl_trigger();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -569,9 +615,11 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_ns_kernel(const NSParams p)
     pdl_wait();
 
     const int d_model = p.nb * 32;
+    int st_i0 = 0, st_len = 0;
+    xout_slice(d_model, cta, gridDim.x, &st_i0, &st_len);
     {
         float ss[B];
-        stage_x_fold<QT, B, PRO, S_THREADS>(xs, p.a, p.nb, ss);
+        stage_x_fold<QT, B, PRO, S_THREADS>(xs, p.a, p.nb, ss, &s_xo, st_i0, st_len);
         if constexpr (PRO == Pro::AddNorm) {
 #pragma unroll
             for (int b = 0; b < B; ++b) {
@@ -649,7 +697,7 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_ns_kernel(const NSParams p)
     }
     __syncthreads();
     if constexpr (PRO == Pro::AddNorm) {
-        write_xout_slice<B, S_THREADS>(p.a, d_model, s_inv, cta, gridDim.x);
+        write_xout_stashed<B, S_THREADS>(p.a, d_model, s_inv, cta, gridDim.x, &s_xo);
     }
 
     // Row groups of this CTA: sum over warps in warp order, times the RMSNorm scale.
@@ -1161,6 +1209,7 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
     __shared__ float s_red[8 * B];
     __shared__ float s_inv[B];
     __shared__ int s_last;
+    __shared__ XoutStash s_xo;  // AddNorm fold: this CTA's slice of the normed x
 
     pdl_trigger();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1214,11 +1263,71 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
     }
     pdl_wait();
 
-    if constexpr (PRO == Pro::AddNorm) {
+    // AddNorm with 16-byte rows folds the RMSNorm: one pass over the full
+    // rows sums the squares of t = xin + yin and stages t * gamma for this
+    // CTA's rows; 1/rms multiplies the finished column sums (every CTA sums
+    // in the same order, so all get the same scale), and each CTA writes its
+    // slice of the normed residual stream at the end.
+    const bool aligned = (p.a.x_stride & 3) == 0 && (ne & 3) == 0 && (p.E & 3) == 0;
+    const bool fold = PRO == Pro::AddNorm && aligned;
+    int st_i0 = 0, st_len = 0;
+    xout_slice(p.E, blockIdx.x, gridDim.x, &st_i0, &st_len);
+    if (fold) {
+        const int n4 = p.E >> 2;
+        float ss[B];
+#pragma unroll
+        for (int b = 0; b < B; ++b) ss[b] = 0.f;
+        for (int base = 0; base < B * n4; base += THREADS * 4) {
+            float4 v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int idx = base + k * THREADS + tid;
+                if (idx < B * n4) {
+                    const int bb = idx / n4, i4 = idx - bb * n4;
+                    const size_t off = (size_t)bb * p.a.x_stride + 4 * (size_t)i4;
+                    float4 t = *reinterpret_cast<const float4*>(p.a.xin + off);
+                    if (p.a.yin) {
+                        const float4 u = *reinterpret_cast<const float4*>(p.a.yin + off);
+                        t.x = __fadd_rn(t.x, u.x); t.y = __fadd_rn(t.y, u.y);
+                        t.z = __fadd_rn(t.z, u.z); t.w = __fadd_rn(t.w, u.w);
+                    }
+                    v[k] = t;
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int idx = base + k * THREADS + tid;
+                if (idx < B * n4) {
+                    const int bb = idx / n4, e = 4 * (idx - bb * n4);
+                    const float4 o = v[k];
+                    const float q = fmaf(o.x, o.x, fmaf(o.y, o.y, fmaf(o.z, o.z, __fmul_rn(o.w, o.w))));
+#pragma unroll
+                    for (int b = 0; b < B; ++b)
+                        if (b == bb) ss[b] += q;
+                    if (B * st_len <= kXoutStash && (e >> 2) >= st_i0 && (e >> 2) < st_i0 + st_len)
+                        stash_put<B, THREADS>(&s_xo, st_i0, st_len, bb, e >> 2, o,
+                                              *reinterpret_cast<const float4*>(p.a.gamma + e));
+                    if (e >= e_lo && e < e_hi) {
+                        const float4 g = *reinterpret_cast<const float4*>(p.a.gamma + e);
+                        *reinterpret_cast<float4*>(xs + bb * p.e_per_split + (e - e_lo)) =
+                            make_float4(__fmul_rn(o.x, g.x), __fmul_rn(o.y, g.y), __fmul_rn(o.z, g.z),
+                                        __fmul_rn(o.w, g.w));
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            const float t = warp_sum(ss[b]);
+            if (lane == 0) s_red[warp * B + b] = t;
+        }
+    } else if constexpr (PRO == Pro::AddNorm) {
         block_rms_inv<B>(p.a.xin, p.a.yin, p.a.x_stride, p.E, p.a.eps, s_red, s_inv);
         if (blockIdx.x == 0) write_xout<B>(p.a, p.E, s_inv);
     }
-    if ((p.a.x_stride & 3) != 0 || (ne & 3) != 0) {
+    if (fold) {
+        // staged above
+    } else if (!aligned) {
         // rows not 16-byte aligned: scalar staging
         for (int idx = tid; idx < B * ne; idx += THREADS) {
             const int bb = idx / ne, i = idx - bb * ne;
@@ -1371,7 +1480,14 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
         const int colx = (CPL == 32) ? lane : (8 * quarter + (lane >> 2));
         red[warp][b][colx] = v[0];
     }
+    if (fold && tid < B) {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) t += s_red[w * B + tid];
+        s_inv[tid] = rms_inv(t, p.E, p.a.eps);
+    }
     __syncthreads();
+    if (fold) write_xout_stashed<B, THREADS>(p.a, p.E, s_inv, blockIdx.x, gridDim.x, &s_xo);
 
     // CTA partial for (block column c, rows [e_lo, e_hi)): thread (b = warp, col = lane)
     float val = 0.f;
@@ -1399,6 +1515,7 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
         if (tid == 0) p.a.counters[c] = 0u;
     }
     if (b_me >= B) return;
+    if (fold) val = __fmul_rn(val, s_inv[b_me]);
 
     const int j = c * 32 + cl;
     t_store<EPI>(p.a, val, j, b_me, EPI == Epi::QkvRope ? rope_coef(p.a, j, b_me) : f2(1.f, 0.f));

@@ -130,7 +130,10 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
                                                          float* __restrict__ att = nullptr) {
     constexpr int G_MAX = 8;
     constexpr int F4 = HD / 4;  // float4 per row
-    __shared__ __align__(16) float4 ks[CH][F4];
+    // K rows padded by two float4: the 8 lanes of a quarter-warp (4 rows x 2
+    // interleaved halves) read 8 distinct 16-byte bank groups.
+    constexpr int KP = F4 + 2;
+    __shared__ __align__(16) float4 ks[CH][KP];
     __shared__ __align__(16) float4 vs[CH][F4];
     __shared__ __align__(16) float4 qs[G_MAX][F4];
     __shared__ float sc[G_MAX][CH];
@@ -171,20 +174,24 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
         if (i < n * F4) { ks[i / F4][i % F4] = kr[k]; vs[i / F4][i % F4] = vr[k]; }
     }
     __syncthreads();
-    // scores: warp w takes positions w, w + 8, ...; lanes split head_dim
-    for (int i = warp; i < n; i += 8) {
-        for (int g = 0; g < G; ++g) {
-            float acc = 0.f;
-            for (int f = lane; f < F4; f += 32) {
-                const float4 kv = ks[i][f], qv = qs[g][f];
+    // scores: lanes 2p and 2p + 1 take (position p % CH, head p / CH), each
+    // half of head_dim (interleaved float4), summed with one shuffle
+    static_assert(CH == 32, "a warp's 16 pairs share one head");
+    for (int pr = tid >> 1; pr < CH * G; pr += 128) {
+        const int i = pr & (CH - 1), g = pr / CH, h = tid & 1;
+        float acc = 0.f;
+        if (i < n) {
+#pragma unroll
+            for (int j = 0; j < F4 / 2; ++j) {
+                const float4 kv = ks[i][2 * j + h], qv = qs[g][2 * j + h];
                 acc = fmaf(kv.x, qv.x, acc);
                 acc = fmaf(kv.y, qv.y, acc);
                 acc = fmaf(kv.z, qv.z, acc);
                 acc = fmaf(kv.w, qv.w, acc);
             }
-            acc = warp_sum(acc);
-            if (lane == 0) sc[g][i] = __fmul_rn(acc, scale);
         }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        if (h == 0 && i < n) sc[g][i] = __fmul_rn(acc, scale);
     }
     __syncthreads();
     if (warp < G) {

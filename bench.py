@@ -367,7 +367,9 @@ def main():
     achieved = bytes_per[dom] / (avg_ms / 1000.0) / 1e9
     traffic = committed_traffic().get(dom)
     step_ms_eager = sum(v[0] for v in tot.values()) / args.profile_steps
-    launches_per_step = 1 + 6 * shape.n_layers + 3 + (1 if world > 1 else 0)
+    # embed; per layer QKV, attention (split + merge in one launch), wo, gate/up, down (+ two
+    # all-reduces under TP); lm_head, argmax (2), greedy advance (+ logits gather under TP)
+    launches_per_step = 1 + (5 + (2 if world > 1 else 0)) * shape.n_layers + 4 + (1 if world > 1 else 0)
 
     cpu = None
     if keep_host:
