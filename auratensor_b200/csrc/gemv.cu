@@ -32,6 +32,7 @@
 // All kernels support programmatic dependent launch: weights (never written
 // by an earlier kernel) are prefetched before griddepcontrol.wait; every
 // activation read comes after it.
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -1072,6 +1073,7 @@ struct TParams {
     int n_bc;          // block columns (outputs / 32)
     int S;             // CTAs splitting the rows of a block column
     int e_per_split;   // rows per CTA (multiple of the CTA row step)
+    int cluster;       // S > 1 launched as clusters of S CTAs: partials combined through DSMEM
     GemvArgs a;
 };
 
@@ -1278,7 +1280,9 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
 #pragma unroll
         for (int b = 0; b < B; ++b) ss[b] = 0.f;
         for (int base = 0; base < B * n4; base += THREADS * 4) {
-            float4 v[4];
+            // x, y and gamma in one round of loads (gamma of rows this CTA
+            // stages or writes back)
+            float4 v[4], gv[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const int idx = base + k * THREADS + tid;
@@ -1292,6 +1296,9 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
                         t.z = __fadd_rn(t.z, u.z); t.w = __fadd_rn(t.w, u.w);
                     }
                     v[k] = t;
+                    const int e = 4 * i4;
+                    const bool need = (e >= e_lo && e < e_hi) || (i4 >= st_i0 && i4 < st_i0 + st_len);
+                    if (need) gv[k] = *reinterpret_cast<const float4*>(p.a.gamma + e);
                 }
             }
 #pragma unroll
@@ -1305,10 +1312,9 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
                     for (int b = 0; b < B; ++b)
                         if (b == bb) ss[b] += q;
                     if (B * st_len <= kXoutStash && (e >> 2) >= st_i0 && (e >> 2) < st_i0 + st_len)
-                        stash_put<B, THREADS>(&s_xo, st_i0, st_len, bb, e >> 2, o,
-                                              *reinterpret_cast<const float4*>(p.a.gamma + e));
+                        stash_put<B, THREADS>(&s_xo, st_i0, st_len, bb, e >> 2, o, gv[k]);
                     if (e >= e_lo && e < e_hi) {
-                        const float4 g = *reinterpret_cast<const float4*>(p.a.gamma + e);
+                        const float4 g = gv[k];
                         *reinterpret_cast<float4*>(xs + bb * p.e_per_split + (e - e_lo)) =
                             make_float4(__fmul_rn(o.x, g.x), __fmul_rn(o.y, g.y), __fmul_rn(o.z, g.z),
                                         __fmul_rn(o.w, g.w));
@@ -1496,7 +1502,20 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
 #pragma unroll
         for (int w = 0; w < 8; ++w) val += red[w][b_me][cl];
     }
-    if (p.S > 1) {
+    if (p.S > 1 && p.cluster) {
+        // The S CTAs of block column c form one cluster (rank = s): rank 0
+        // sums the partials in split order from its peers' shared memory.
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        if (b_me < B) red[0][b_me][cl] = val;  // each (b_me, cl) slot is read above only by this thread
+        cluster.sync();
+        if (s == 0 && b_me < B) {
+            val = 0.f;
+            for (int k = 0; k < p.S; ++k) val += cluster.map_shared_rank(&red[0][0][0], k)[b_me * 32 + cl];
+        }
+        cluster.sync();  // peers keep their shared memory until rank 0 has read it
+        if (s != 0) return;
+    } else if (p.S > 1) {
         if (b_me < B) p.a.scratch[(((size_t)c * p.S + s) * B + b_me) * 32 + cl] = val;
         __threadfence();
         __syncthreads();
@@ -1551,17 +1570,29 @@ int occupancy(const void* fn, int smem) {
 }
 
 template <class P>
-void launch(const void* fn, int grid, int smem, cudaStream_t s, bool pdl, const P& params, int threads = THREADS) {
+void launch(const void* fn, int grid, int smem, cudaStream_t s, bool pdl, const P& params, int threads = THREADS,
+            int cluster = 1) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (cluster > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = (unsigned)cluster;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = na;
     void* args[] = {const_cast<P*>(&params)};
     AT_CUDA(cudaLaunchKernelExC(&cfg, fn, args));
 }
@@ -1751,13 +1782,16 @@ void run_t(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, boo
     p.n_bc = (int)(m->cols / QK);
     t_config(m, B, num_sms, &p.S, &p.e_per_split);
     p.a = a;
-    if (p.S > 1) AT_REQUIRE(a.scratch && a.counters, AT_ERR_STATE, "T GEMV needs split scratch");
+    // splits of up to 8 CTAs combine through cluster shared memory; larger
+    // ones through the scratch partials and per-column counters
+    p.cluster = (p.S > 1 && p.S <= 8) ? 1 : 0;
+    if (p.S > 1 && !p.cluster) AT_REQUIRE(a.scratch && a.counters, AT_ERR_STATE, "T GEMV needs split scratch");
     p.ring_off = (B * p.e_per_split * 4 + 15) / 16 * 16;
     const int ring_bytes = (TCfg<B>::CPL == 32) ? TR * THREADS * (16 * QTraits<QT>::NV + 4) : 0;
     const int smem = p.ring_off + ring_bytes;
     const void* fn = reinterpret_cast<const void*>(&gemv_t_kernel<QT, B, PRO, EPI>);
     ensure_smem(fn, smem);
-    launch(fn, p.n_bc * p.S, smem, s, pdl, p);
+    launch(fn, p.n_bc * p.S, smem, s, pdl, p, THREADS, p.cluster ? p.S : 1);
 }
 
 template <int QT, Pro PRO, Epi EPI, bool IS_T>
@@ -1787,8 +1821,9 @@ void gemv_t_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* float
     int S = 1, per = 0;
     t_config(m, batch, num_sms, &S, &per);
     const size_t n_bc = (size_t)(m->cols / QK);
-    *floats = (S > 1) ? n_bc * S * batch * 32 : 0;
-    *counters = (S > 1) ? n_bc : 0;
+    const bool global_split = S > 8;  // splits of up to 8 CTAs combine in cluster shared memory
+    *floats = global_split ? n_bc * S * batch * 32 : 0;
+    *counters = global_split ? n_bc : 0;
 }
 
 void gemv_n_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* floats, size_t* counters) {
@@ -1855,7 +1890,8 @@ void launch_sgemv_f32(const float* A, const float* x, float* y, int M, int K, in
 // Orientation T with its split scratch in a static device array
 // ---------------------------------------------------------------------------
 // For callers that cannot allocate device memory: the split-K partials and
-// the per-column arrival counters of the orientation-T GEMV live in one
+// the per-column arrival counters of the orientation-T GEMV (splits of more
+// than 8 CTAs; smaller ones combine in cluster shared memory) live in one
 // file-scope array instead of cudaMalloc'd scratch. Every GPU that loads the
 // library holds this array (256 KiB) until the process exits.
 namespace {

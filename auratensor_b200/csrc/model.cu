@@ -209,15 +209,34 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
         if (lane == 0) { s_m[g] = m; s_l[g] = l; }
     }
     __syncthreads();
+    // o = sum_i p_i V_i: a thread takes outputs o0 and o0 + 256, each summed
+    // as even and odd positions (four independent FMA chains)
     const float* vsf = reinterpret_cast<const float*>(vs);
-    for (int o = tid; o < G * HD; o += 256) {
-        const int g = o / HD, dd = o - g * HD;
-        float acc = 0.f;
-        for (int i = 0; i < n; ++i) acc = fmaf(sc[g][i], vsf[i * HD + dd], acc);
-        const int h = kvh * G + g;
-        float* dst = part + (((size_t)b * Hl + h) * nchunk_max + chunk) * (HD + 2);
-        dst[dd] = acc;
-        if (dd == 0) { dst[HD] = s_m[g]; dst[HD + 1] = s_l[g]; }
+    for (int o0 = tid; o0 < G * HD; o0 += 512) {
+        const int o1 = o0 + 256;
+        const bool has1 = o1 < G * HD;
+        const int g0 = o0 / HD, d0 = o0 - g0 * HD;
+        const int g1 = has1 ? o1 / HD : g0, d1 = has1 ? o1 - g1 * HD : d0;
+        float a0 = 0.f, a1 = 0.f, c0 = 0.f, c1 = 0.f;
+        int i = 0;
+        for (; i + 2 <= n; i += 2) {
+            a0 = fmaf(sc[g0][i], vsf[i * HD + d0], a0);
+            a1 = fmaf(sc[g1][i], vsf[i * HD + d1], a1);
+            c0 = fmaf(sc[g0][i + 1], vsf[(i + 1) * HD + d0], c0);
+            c1 = fmaf(sc[g1][i + 1], vsf[(i + 1) * HD + d1], c1);
+        }
+        if (i < n) {
+            a0 = fmaf(sc[g0][i], vsf[i * HD + d0], a0);
+            a1 = fmaf(sc[g1][i], vsf[i * HD + d1], a1);
+        }
+        float* dst0 = part + (((size_t)b * Hl + kvh * G + g0) * nchunk_max + chunk) * (HD + 2);
+        dst0[d0] = a0 + c0;
+        if (d0 == 0) { dst0[HD] = s_m[g0]; dst0[HD + 1] = s_l[g0]; }
+        if (has1) {
+            float* dst1 = part + (((size_t)b * Hl + kvh * G + g1) * nchunk_max + chunk) * (HD + 2);
+            dst1[d1] = a1 + c1;
+            if (d1 == 0) { dst1[HD] = s_m[g1]; dst1[HD + 1] = s_l[g1]; }
+        }
     }
     if constexpr (FUSED) {
         const int nch = (int)((P + CH - 1) / CH);
@@ -235,13 +254,16 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
         }
         __syncthreads();
         if (!s_last) return;
-        float* sw = reinterpret_cast<float*>(ks);  // [G][nch] merge weights
+        float* sw = reinterpret_cast<float*>(ks);  // [G][nch] chunk maxima, then merge weights
+        float* sl = reinterpret_cast<float*>(vs);  // [G][nch] chunk sums
         if (warp < G) {
+            // both statistics of every chunk in one round of loads
             const int g = warp;
             const float* base = part + ((size_t)b * Hl + kvh * G + g) * nchunk_max * (HD + 2);
             float mx = -INFINITY;
             for (int c = lane; c < nch; c += 32) {
                 const float mc = __ldcg(base + (size_t)c * (HD + 2) + HD);
+                sl[g * nch + c] = __ldcg(base + (size_t)c * (HD + 2) + HD + 1);
                 sw[g * nch + c] = mc;
                 mx = fmaxf(mx, mc);
             }
@@ -250,27 +272,41 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
             for (int c = lane; c < nch; c += 32) {
                 const float w = exp_ref(__fsub_rn(sw[g * nch + c], mx));
                 sw[g * nch + c] = w;
-                l = fmaf(__ldcg(base + (size_t)c * (HD + 2) + HD + 1), w, l);
+                l = fmaf(sl[g * nch + c], w, l);
             }
             l = warp_sum(l);
             if (lane == 0) s_l[g] = l;
         }
         __syncthreads();
-        for (int o = tid; o < G * HD; o += 256) {
-            const int g = o / HD, dd = o - g * HD;
-            const float* base = part + ((size_t)b * Hl + kvh * G + g) * nchunk_max * (HD + 2) + dd;
-            const float* wg = sw + g * nch;
-            float acc = 0.f;
-            int c = 0;
-            for (; c + 8 <= nch; c += 8) {
-                float v[8];
+        // outputs o0 and o0 + 256 per thread, 16 chunks of both in flight
+        for (int o0 = tid; o0 < G * HD; o0 += 512) {
+            const int o1 = o0 + 256;
+            const bool has1 = o1 < G * HD;
+            const int g0 = o0 / HD, d0 = o0 - g0 * HD;
+            const int g1 = has1 ? o1 / HD : g0, d1 = has1 ? o1 - g1 * HD : d0;
+            const float* base0 = part + ((size_t)b * Hl + kvh * G + g0) * nchunk_max * (HD + 2) + d0;
+            const float* base1 = part + ((size_t)b * Hl + kvh * G + g1) * nchunk_max * (HD + 2) + d1;
+            const float* w0 = sw + g0 * nch;
+            const float* w1 = sw + g1 * nch;
+            float acc0 = 0.f, acc1 = 0.f;
+            for (int c = 0; c < nch; c += 16) {
+                float v0[16], v1[16];
 #pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] = __ldcg(base + (size_t)(c + k) * (HD + 2));
+                for (int k = 0; k < 16; ++k) {
+                    const bool in = c + k < nch;
+                    v0[k] = in ? __ldcg(base0 + (size_t)(c + k) * (HD + 2)) : 0.f;
+                    v1[k] = (in && has1) ? __ldcg(base1 + (size_t)(c + k) * (HD + 2)) : 0.f;
+                }
 #pragma unroll
-                for (int k = 0; k < 8; ++k) acc = fmaf(v[k], wg[c + k], acc);
+                for (int k = 0; k < 16; ++k) {
+                    if (c + k < nch) {
+                        acc0 = fmaf(v0[k], w0[c + k], acc0);
+                        acc1 = fmaf(v1[k], w1[c + k], acc1);
+                    }
+                }
             }
-            for (; c < nch; ++c) acc = fmaf(__ldcg(base + (size_t)c * (HD + 2)), wg[c], acc);
-            att[(size_t)b * Hl * HD + (size_t)(kvh * G + g) * HD + dd] = __fdiv_rn(acc, s_l[g]);
+            att[(size_t)b * Hl * HD + (size_t)(kvh * G + g0) * HD + d0] = __fdiv_rn(acc0, s_l[g0]);
+            if (has1) att[(size_t)b * Hl * HD + (size_t)(kvh * G + g1) * HD + d1] = __fdiv_rn(acc1, s_l[g1]);
         }
     }
 }

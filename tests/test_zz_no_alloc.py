@@ -23,7 +23,11 @@ def static_gemv(m, x, y):
 
 
 @pytest.mark.parametrize("qt", [ref.GGML_Q4_0, ref.GGML_Q8_0])
-@pytest.mark.parametrize("rows,cols,batch", [(4096, 4096, 1), (2048, 1024, 2), (300, 640, 1), (1024, 512, 8)])
+# (8192, 64, 8) and (16384, 64, 1) split each block column over more than 8
+# CTAs (32 and 16), so their partials go through the static array; the
+# others combine in cluster shared memory or do not split.
+@pytest.mark.parametrize("rows,cols,batch", [(4096, 4096, 1), (2048, 1024, 2), (300, 640, 1), (1024, 512, 8),
+                                             (8192, 64, 8), (16384, 64, 1)])
 def test_static_scratch_matches_at_gemv(qt, rows, cols, batch, cuda):
     g = torch.Generator(device=cuda).manual_seed(rows + cols + batch)
     blocks = synth.generate_torch_tensor((rows, cols), qt, g, cuda)
@@ -41,12 +45,12 @@ def test_static_scratch_matches_at_gemv(qt, rows, cols, batch, cuda):
 
 
 def test_static_scratch_rejects_oversized_split(cuda):
-    # batch 8 over 150 block columns splits each column over 2 CTAs:
-    # 150 * 2 * 8 * 32 partials exceed the static 61440
+    # batch 8 over 16 block columns of 65536 rows splits each column over 22
+    # CTAs (more than one cluster): 16 * 22 * 8 * 32 partials exceed the static 61440
     g = torch.Generator(device=cuda).manual_seed(1)
-    m = QMatrix(ref.GGML_Q4_0, ORIENT_T, 4096, 4800, synth.generate_torch_tensor((4096, 4800), ref.GGML_Q4_0, g, cuda))
-    x = torch.randn((8, 4096), device=cuda)
-    y = torch.empty((8, 4800), device=cuda)
+    m = QMatrix(ref.GGML_Q4_0, ORIENT_T, 65536, 512, synth.generate_torch_tensor((65536, 512), ref.GGML_Q4_0, g, cuda))
+    x = torch.randn((8, 65536), device=cuda)
+    y = torch.empty((8, 512), device=cuda)
     with pytest.raises(_lib.IllegalArgumentException, match="static maximum"):
         static_gemv(m, x, y)
 
