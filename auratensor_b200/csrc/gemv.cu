@@ -1782,9 +1782,11 @@ void run_t(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, boo
     p.n_bc = (int)(m->cols / QK);
     t_config(m, B, num_sms, &p.S, &p.e_per_split);
     p.a = a;
-    // splits of up to 8 CTAs combine through cluster shared memory; larger
-    // ones through the scratch partials and per-column counters
-    p.cluster = (p.S > 1 && p.S <= 8) ? 1 : 0;
+    // batch <= 2 splits of up to 8 CTAs combine through cluster shared memory;
+    // others through the scratch partials and per-column counters (at batch 8
+    // a split's short CTA would hold its SM at the cluster barrier while the
+    // grid needs several waves: 4096 x 6144 took 80 instead of 57 us)
+    p.cluster = (B <= 2 && p.S > 1 && p.S <= 8) ? 1 : 0;
     if (p.S > 1 && !p.cluster) AT_REQUIRE(a.scratch && a.counters, AT_ERR_STATE, "T GEMV needs split scratch");
     p.ring_off = (B * p.e_per_split * 4 + 15) / 16 * 16;
     const int ring_bytes = (TCfg<B>::CPL == 32) ? TR * THREADS * (16 * QTraits<QT>::NV + 4) : 0;
@@ -1821,7 +1823,7 @@ void gemv_t_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* float
     int S = 1, per = 0;
     t_config(m, batch, num_sms, &S, &per);
     const size_t n_bc = (size_t)(m->cols / QK);
-    const bool global_split = S > 8;  // splits of up to 8 CTAs combine in cluster shared memory
+    const bool global_split = S > 8 || batch > 2;  // see run_t: the other splits combine in cluster shared memory
     *floats = global_split ? n_bc * S * batch * 32 : 0;
     *counters = global_split ? n_bc : 0;
 }
@@ -1890,8 +1892,8 @@ void launch_sgemv_f32(const float* A, const float* x, float* y, int M, int K, in
 // Orientation T with its split scratch in a static device array
 // ---------------------------------------------------------------------------
 // For callers that cannot allocate device memory: the split-K partials and
-// the per-column arrival counters of the orientation-T GEMV (splits of more
-// than 8 CTAs; smaller ones combine in cluster shared memory) live in one
+// the per-column arrival counters of the orientation-T GEMV (batch above 2 or
+// splits of more than 8 CTAs; the others combine in cluster shared memory) live in one
 // file-scope array instead of cudaMalloc'd scratch. Every GPU that loads the
 // library holds this array (256 KiB) until the process exits.
 namespace {

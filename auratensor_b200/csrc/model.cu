@@ -20,6 +20,8 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <cooperative_groups.h>
+
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -115,12 +117,20 @@ __device__ __forceinline__ float exp_ref(float v) { return (float)exp((double)v)
 // over positions [p0, p0 + n) = (K q) * scale, chunk max m, l = sum exp(s - m),
 // o = sum exp(s - m) V. K and V of the chunk are staged in shared memory with
 // all of the CTA's 128-bit loads in flight at once.
-// FUSED (decode step): the last CTA of a (sequence, KV head) to finish its
+// MODE 0 (prompt path): the chunk partials go to `part` for attn_combine_kernel.
+// MODE 1 (decode step): the last CTA of a (sequence, KV head) to finish its
 // chunk (ticket per pair in `cnt`, reset by that CTA) merges the chunk
 // partials of the G heads into `att` (the log-sum-exp combine of
 // attn_combine_kernel, without a second launch). Needs G * chunks <= CH * HD
 // (the merge weights reuse the K staging buffer).
-template <int HD, bool FUSED = false>
+// MODE 2 (decode step, launched with clusters of CS CTAs along the chunks):
+// the CTAs of a cluster keep their partials in shared memory; after a cluster
+// barrier rank 0 merges them through distributed shared memory. When one
+// cluster covers the sequence it writes `att` directly; otherwise the cluster
+// partials (one per CS * CH positions) are merged as in MODE 1. A cluster
+// whose first chunk lies past the sequence exits as a whole; idle CTAs of a
+// partly used cluster take part in its barriers with an empty partial.
+template <int HD, int MODE = 0>
 __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict__ q, const float* __restrict__ kc,
                                                          const float* __restrict__ vc,
                                                          const int64_t* __restrict__ pos, float* __restrict__ part,
@@ -138,6 +148,8 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
     __shared__ __align__(16) float4 qs[G_MAX][F4];
     __shared__ float sc[G_MAX][CH];
     __shared__ float s_m[G_MAX], s_l[G_MAX];
+    __shared__ __align__(16) float s_o[MODE == 2 ? G_MAX : 1][HD];  // MODE 2: this CTA's partial
+    __shared__ float s_cm[G_MAX], s_cl[G_MAX];                       // MODE 2: cluster statistics
     __shared__ int s_last;
     const int kvh = blockIdx.x, chunk = blockIdx.y, b = blockIdx.z;
     const int G = Hl / Hkvl;
@@ -147,10 +159,19 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
     // waiting on the QKV kernel, which appends row P - 1 and writes q.
     const int64_t P = pos[b] + 1;
     const int64_t p0 = (int64_t)chunk * CH;
-    if (p0 >= P) return;
+    int cs = 1, crank = 0;
+    if constexpr (MODE == 2) {
+        cs = (int)cooperative_groups::this_cluster().num_blocks();  // cluster dims (1, cs, 1)
+        crank = chunk % cs;
+        if ((int64_t)(chunk - crank) * CH >= P) return;  // the whole cluster is past the sequence
+    } else {
+        if (p0 >= P) return;
+    }
+    const bool active = p0 < P;  // MODE 2 only can be false here (CTA-uniform)
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (active) {
     const int n = (int)((P - p0) < CH ? (P - p0) : CH);
     const int n_past = (p0 + n == P) ? n - 1 : n;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const float4* kbase = reinterpret_cast<const float4*>(kc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD);
     const float4* vbase = reinterpret_cast<const float4*>(vc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD);
     const float4* qbase = reinterpret_cast<const float4*>(q + (size_t)b * Hl * HD + (size_t)kvh * G * HD);
@@ -229,17 +250,83 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
             a0 = fmaf(sc[g0][i], vsf[i * HD + d0], a0);
             a1 = fmaf(sc[g1][i], vsf[i * HD + d1], a1);
         }
-        float* dst0 = part + (((size_t)b * Hl + kvh * G + g0) * nchunk_max + chunk) * (HD + 2);
-        dst0[d0] = a0 + c0;
-        if (d0 == 0) { dst0[HD] = s_m[g0]; dst0[HD + 1] = s_l[g0]; }
-        if (has1) {
-            float* dst1 = part + (((size_t)b * Hl + kvh * G + g1) * nchunk_max + chunk) * (HD + 2);
-            dst1[d1] = a1 + c1;
-            if (d1 == 0) { dst1[HD] = s_m[g1]; dst1[HD + 1] = s_l[g1]; }
+        if constexpr (MODE == 2) {
+            s_o[g0][d0] = a0 + c0;
+            if (has1) s_o[g1][d1] = a1 + c1;
+        } else {
+            float* dst0 = part + (((size_t)b * Hl + kvh * G + g0) * nchunk_max + chunk) * (HD + 2);
+            dst0[d0] = a0 + c0;
+            if (d0 == 0) { dst0[HD] = s_m[g0]; dst0[HD + 1] = s_l[g0]; }
+            if (has1) {
+                float* dst1 = part + (((size_t)b * Hl + kvh * G + g1) * nchunk_max + chunk) * (HD + 2);
+                dst1[d1] = a1 + c1;
+                if (d1 == 0) { dst1[HD] = s_m[g1]; dst1[HD + 1] = s_l[g1]; }
+            }
         }
     }
-    if constexpr (FUSED) {
-        const int nch = (int)((P + CH - 1) / CH);
+    }  // active
+    int nparts = (int)((P + CH - 1) / CH);  // partials the global merge combines (MODE 1: chunks)
+    if constexpr (MODE == 2) {
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        if (!active) {
+            for (int i = tid; i < G * HD; i += 256) s_o[i / HD][i % HD] = 0.f;
+            if (tid < G) { s_m[tid] = -INFINITY; s_l[tid] = 0.f; }
+        }
+        cluster.sync();  // every rank's partial is in its shared memory
+        float oo[2] = {0.f, 0.f};
+        if (crank == 0) {
+            float* cw = reinterpret_cast<float*>(ks);  // [G][cs] merge weights
+            if (warp < G) {
+                const int g = warp;
+                const float mk = lane < cs ? cluster.map_shared_rank(&s_m[0], lane)[g] : -INFINITY;
+                const float lk = lane < cs ? cluster.map_shared_rank(&s_l[0], lane)[g] : 0.f;
+                const float M = warp_max(mk);  // rank 0 is active: finite
+                const float w = lane < cs ? exp_ref(__fsub_rn(mk, M)) : 0.f;
+                const float L = warp_sum(lk * w);
+                if (lane < cs) cw[g * cs + lane] = w;
+                if (lane == 0) { s_cm[g] = M; s_cl[g] = L; }
+            }
+            __syncthreads();
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int o = tid + 256 * u;
+                if (o < G * HD) {
+                    const int g = o / HD;
+                    float acc = 0.f;
+                    for (int k = 0; k < cs; ++k) acc = fmaf(cluster.map_shared_rank(&s_o[0][0], k)[o], cw[g * cs + k], acc);
+                    oo[u] = acc;
+                }
+            }
+        }
+        cluster.sync();  // rank 0 has read every peer's shared memory
+        if (crank != 0) return;
+        const int ncl = (nparts + cs - 1) / cs;  // clusters over the sequence
+        const int cl_idx = chunk / cs;
+        if (ncl == 1) {
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int o = tid + 256 * u;
+                if (o < G * HD)
+                    att[(size_t)b * Hl * HD + (size_t)kvh * G * HD + o] = __fdiv_rn(oo[u], s_cl[o / HD]);
+            }
+            return;
+        }
+        // several clusters: publish this cluster's partial as partial cl_idx
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int o = tid + 256 * u;
+            if (o < G * HD) {
+                const int g = o / HD, dd = o - g * HD;
+                float* dst = part + (((size_t)b * Hl + kvh * G + g) * nchunk_max + cl_idx) * (HD + 2);
+                dst[dd] = oo[u];
+                if (dd == 0) { dst[HD] = s_cm[g]; dst[HD + 1] = s_cl[g]; }
+            }
+        }
+        nparts = ncl;
+    }
+    if constexpr (MODE >= 1) {
+        const int nch = nparts;
         // Publish this CTA's partial (barrier, then a device-scope fence that
         // is cumulative over the stores ordered before it) and take a ticket.
         __syncthreads();
@@ -688,6 +775,7 @@ struct at_model {
     float *xa = nullptr, *xb = nullptr, *y = nullptr, *q = nullptr, *att = nullptr, *h = nullptr;
     float *logits = nullptr, *logits_local = nullptr, *att_part = nullptr;
     unsigned* attn_cnt = nullptr;  // [max_batch][Hkvl] tickets of the fused decode attention
+    int attn_cs = 0;               // decode attention cluster size (0: merge through global memory)
     float *kcache = nullptr, *vcache = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
     float* scratch = nullptr;
     unsigned* counters = nullptr;
@@ -787,18 +875,63 @@ struct ProfScope {
 // serialization when pdl is set (the kernel calls pdl_wait before reading
 // what the previous kernel writes).
 template <class... KArgs, class... Args>
-void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, bool pdl, Args... args) {
+void launch_kc(void (*kern)(KArgs...), dim3 grid, dim3 block, dim3 cluster, cudaStream_t s, bool pdl,
+               Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = 0;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (cluster.x * cluster.y * cluster.z > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = cluster.x;
+        attr[na].val.clusterDim.y = cluster.y;
+        attr[na].val.clusterDim.z = cluster.z;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = na;
     AT_CUDA(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...));
+}
+template <class... KArgs, class... Args>
+void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, bool pdl, Args... args) {
+    launch_kc(kern, grid, block, dim3(1, 1, 1), s, pdl, args...);
+}
+
+// Cluster size of the decode attention (clusters of chunk CTAs of one KV head
+// merge through distributed shared memory): 16 where the device can place
+// such clusters (non-portable size), else 8, else 0 (no clusters: MODE 1).
+template <int HD>
+int attn_cluster_size(int hkv, int nchunk, int batch) {
+    auto kern = attn_split_kernel<HD, 2>;
+    for (int cs : {16, 8}) {
+        if (cs == 16 &&
+            cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+            cudaGetLastError();
+            continue;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(hkv, (nchunk + cs - 1) / cs * cs, batch);
+        cfg.blockDim = dim3(256);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = cs;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n >= hkv * batch) return cs;
+        cudaGetLastError();
+    }
+    return 0;
 }
 
 void enqueue_step(at_model* m, int B) {
@@ -858,13 +991,25 @@ void enqueue_step(at_model* m, int B) {
             // one launch (split + merge by the last CTA) when the merge
             // weights of a KV head's query heads fit the K staging buffer
             const bool fused = (m->Hl / m->Hkvl) * m->nchunk_max <= CH * hd;
-            if (fused) {
+            const int cs = m->attn_cs;
+            if (fused && cs > 1) {
+                // chunks merged per cluster through distributed shared memory
+                dim3 gc(m->Hkvl, (m->nchunk_max + cs - 1) / cs * cs, B);
                 if (hd == 128)
-                    launch_k(attn_split_kernel<128, true>, g1, 256, s, m->pdl, qp, (const float*)kc,
+                    launch_kc(attn_split_kernel<128, 2>, gc, 256, dim3(1, cs, 1), s, m->pdl, qp, (const float*)kc,
+                              (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
+                              m->nchunk_max, scale, m->attn_cnt, m->att);
+                else
+                    launch_kc(attn_split_kernel<64, 2>, gc, 256, dim3(1, cs, 1), s, m->pdl, qp, (const float*)kc,
+                              (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
+                              m->nchunk_max, scale, m->attn_cnt, m->att);
+            } else if (fused) {
+                if (hd == 128)
+                    launch_k(attn_split_kernel<128, 1>, g1, 256, s, m->pdl, qp, (const float*)kc,
                              (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
                              m->nchunk_max, scale, m->attn_cnt, m->att);
                 else
-                    launch_k(attn_split_kernel<64, true>, g1, 256, s, m->pdl, qp, (const float*)kc,
+                    launch_k(attn_split_kernel<64, 1>, g1, 256, s, m->pdl, qp, (const float*)kc,
                              (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
                              m->nchunk_max, scale, m->attn_cnt, m->att);
             } else {
@@ -1367,6 +1512,8 @@ int at_model_finalize(at_model* m) {
             alloc_zero((void**)&m->logits_local, (size_t)B * m->Vl * 4);
         }
         m->nchunk_max = (m->ctx_len + CH - 1) / CH;
+        m->attn_cs = (hd == 128) ? attn_cluster_size<128>(m->Hkvl, m->nchunk_max, B)
+                                 : attn_cluster_size<64>(m->Hkvl, m->nchunk_max, B);
         alloc_zero((void**)&m->att_part, (size_t)B * m->Hl * m->nchunk_max * (hd + 2) * 4);
         alloc_zero((void**)&m->attn_cnt, (size_t)B * m->Hkvl * sizeof(unsigned));
         // KV cache (inference/KVCache.java:43-63): [slot][layer][kvHead][ctx][headDim] fp32

@@ -109,9 +109,10 @@ int at_gemv(at_ctx* ctx, const at_qmat* m, const float* x_dev, float* y_dev, int
  * front) and callers that cannot take cudaMalloc's device-wide
  * synchronisation in the middle of a decode loop. at_gemv grows its split-K
  * scratch with cudaMalloc the first time a larger shape needs it; this entry
- * point allocates nothing: the split partials and arrival counters (of
- * splits over more than 8 CTAs; smaller splits combine in thread-block
- * cluster shared memory and need none) live in one static device array of
+ * point allocates nothing: the split partials and arrival counters (at
+ * batch above 2, or of splits over more than 8 CTAs; the other splits
+ * combine in thread-block cluster shared memory and need none) live in one
+ * static device array of
  * 256 KiB (61440 partial floats + 4096 counters),
  * held by every GPU that loads the library until exit. Shapes whose split
  * needs more are rejected with AT_ERR_INVALID_ARG. The first call on a device

@@ -5,6 +5,8 @@ max |logit_gpu - logit_ref| <= 1e-3 x (max - min of the reference logits);
 greedy tokens are identical except where the reference's top-2 gap is below
 that tolerance.
 """
+import dataclasses
+
 import numpy as np
 import pytest
 
@@ -172,3 +174,25 @@ def test_profile_step_counts(cuda):
     m2 = LlamaModel(LlamaConfig.fromShape(shape), synth.generate_numpy(shape, seed=14))
     lg = m2.forwardStep(3, 0).copy()
     assert np.array_equal(m.logitsDevice()[0].cpu().numpy(), lg)
+
+
+def test_long_context_attention_merge(cuda):
+    """Decode attention past one cluster of chunk CTAs (32 positions per CTA;
+    clusters of 16 or 8 CTAs cover 512 or 256 positions): chunk partials merge
+    in distributed shared memory per cluster, cluster partials through global
+    memory. Teacher-forced over 1100 positions; logits within the parity bound
+    at the compared steps (cluster boundaries included)."""
+    shape = dataclasses.replace(synth.TINY, ctx=1100)
+    t = synth.generate_numpy(shape, seed=5)
+    gpu = LlamaModel(LlamaConfig.fromShape(shape), t)
+    orc = ref.LlamaModelRef(oracle_cfg(shape), t)
+    toks = np.random.default_rng(5).integers(0, shape.vocab, shape.ctx)
+    check = set(range(0, shape.ctx, 97)) | {31, 32, 255, 256, 257, 511, 512, 513, 767, 768, 1023, 1024, 1025, 1099}
+    for pos in range(shape.ctx):
+        lr = orc.forward_step(int(toks[pos]), pos)
+        lg = gpu.forwardStep(int(toks[pos]), pos)
+        if pos in check:
+            rng_ = float(lr.max() - lr.min())
+            err = float(np.max(np.abs(lg - lr)))
+            assert err <= REL_TOL * rng_, (pos, err, rng_)
+    gpu.close()

@@ -23,9 +23,9 @@ def static_gemv(m, x, y):
 
 
 @pytest.mark.parametrize("qt", [ref.GGML_Q4_0, ref.GGML_Q8_0])
-# (8192, 64, 8) and (16384, 64, 1) split each block column over more than 8
-# CTAs (32 and 16), so their partials go through the static array; the
-# others combine in cluster shared memory or do not split.
+# The batch-8 cases and (16384, 64, 1) (each block column split over 16 CTAs)
+# put their partials in the static array; the other splits combine in
+# cluster shared memory, and (300, 640, 1) does not split.
 @pytest.mark.parametrize("rows,cols,batch", [(4096, 4096, 1), (2048, 1024, 2), (300, 640, 1), (1024, 512, 8),
                                              (8192, 64, 8), (16384, 64, 1)])
 def test_static_scratch_matches_at_gemv(qt, rows, cols, batch, cuda):
