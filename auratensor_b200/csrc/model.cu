@@ -117,20 +117,33 @@ __device__ __forceinline__ float exp_ref(float v) { return (float)exp((double)v)
 // over positions [p0, p0 + n) = (K q) * scale, chunk max m, l = sum exp(s - m),
 // o = sum exp(s - m) V. K and V of the chunk are staged in shared memory with
 // all of the CTA's 128-bit loads in flight at once.
+// CHK positions per CTA (K and V of the chunk staged in dynamic shared
+// memory, attn_smem_bytes).
 // MODE 0 (prompt path): the chunk partials go to `part` for attn_combine_kernel.
 // MODE 1 (decode step): the last CTA of a (sequence, KV head) to finish its
 // chunk (ticket per pair in `cnt`, reset by that CTA) merges the chunk
 // partials of the G heads into `att` (the log-sum-exp combine of
 // attn_combine_kernel, without a second launch). Needs G * chunks <= CH * HD
 // (the merge weights reuse the K staging buffer).
-// MODE 2 (decode step, launched with clusters of CS CTAs along the chunks):
+// MODE 2 (decode step, CHK = 64, launched with clusters of CS CTAs along the chunks):
 // the CTAs of a cluster keep their partials in shared memory; after a cluster
 // barrier rank 0 merges them through distributed shared memory. When one
 // cluster covers the sequence it writes `att` directly; otherwise the cluster
-// partials (one per CS * CH positions) are merged as in MODE 1. A cluster
+// partials (one per CS * CHK positions) are merged as in MODE 1. A cluster
 // whose first chunk lies past the sequence exits as a whole; idle CTAs of a
 // partly used cluster take part in its barriers with an empty partial.
-template <int HD, int MODE = 0>
+// 16-byte asynchronous copy global -> shared (L2 only).
+__device__ __forceinline__ void cp_async16_smem(void* smem, const void* g) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)), "l"(g)
+                 : "memory");
+}
+
+// Dynamic shared memory of attn_split_kernel: K (rows padded by two float4)
+// and V of a chunk of chk positions.
+constexpr size_t attn_smem_bytes(int hd, int chk) { return (size_t)chk * (hd / 4 + 2 + hd / 4) * 16; }
+constexpr int kAttnClusterChunk = 64;  // positions per CTA of the cluster-merged decode attention
+
+template <int HD, int MODE = 0, int CHK = CH>
 __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict__ q, const float* __restrict__ kc,
                                                          const float* __restrict__ vc,
                                                          const int64_t* __restrict__ pos, float* __restrict__ part,
@@ -143,63 +156,63 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
     // K rows padded by two float4: the 8 lanes of a quarter-warp (4 rows x 2
     // interleaved halves) read 8 distinct 16-byte bank groups.
     constexpr int KP = F4 + 2;
-    __shared__ __align__(16) float4 ks[CH][KP];
-    __shared__ __align__(16) float4 vs[CH][F4];
+    static_assert(CHK % 16 == 0 && CHK <= 64, "a warp's 16 score pairs share one head");
+    // K and V of the chunk in dynamic shared memory: CHK x (KP + F4) float4
+    extern __shared__ __align__(16) float4 kv_smem[];
+    float4 (*ks)[KP] = reinterpret_cast<float4 (*)[KP]>(kv_smem);
+    float4 (*vs)[F4] = reinterpret_cast<float4 (*)[F4]>(kv_smem + CHK * KP);
     __shared__ __align__(16) float4 qs[G_MAX][F4];
-    __shared__ float sc[G_MAX][CH];
+    __shared__ float sc[G_MAX][CHK];
     __shared__ float s_m[G_MAX], s_l[G_MAX];
     __shared__ __align__(16) float s_o[MODE == 2 ? G_MAX : 1][HD];  // MODE 2: this CTA's partial
     __shared__ float s_cm[G_MAX], s_cl[G_MAX];                       // MODE 2: cluster statistics
     __shared__ int s_last;
     const int kvh = blockIdx.x, chunk = blockIdx.y, b = blockIdx.z;
     const int G = Hl / Hkvl;
-    pdl_trigger();
+    // MODE 2 lets the next kernel launch only once its chunk work is done: the
+    // next kernel's CTAs copy their weights before their own wait, and that
+    // flood of copies slows this kernel's shared-memory work on the same SM
+    if constexpr (MODE != 2) pdl_trigger();
     // The position was advanced by an earlier step; the rows of positions
     // before it were appended by earlier steps, so they are loaded before
     // waiting on the QKV kernel, which appends row P - 1 and writes q.
     const int64_t P = pos[b] + 1;
-    const int64_t p0 = (int64_t)chunk * CH;
+    const int64_t p0 = (int64_t)chunk * CHK;
     int cs = 1, crank = 0;
     if constexpr (MODE == 2) {
         cs = (int)cooperative_groups::this_cluster().num_blocks();  // cluster dims (1, cs, 1)
         crank = chunk % cs;
-        if ((int64_t)(chunk - crank) * CH >= P) return;  // the whole cluster is past the sequence
+        if ((int64_t)(chunk - crank) * CHK >= P) return;  // the whole cluster is past the sequence
     } else {
         if (p0 >= P) return;
     }
     const bool active = p0 < P;  // MODE 2 only can be false here (CTA-uniform)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (active) {
-    const int n = (int)((P - p0) < CH ? (P - p0) : CH);
+    const int n = (int)((P - p0) < CHK ? (P - p0) : CHK);
     const int n_past = (p0 + n == P) ? n - 1 : n;
     const float4* kbase = reinterpret_cast<const float4*>(kc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD);
     const float4* vbase = reinterpret_cast<const float4*>(vc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD);
     const float4* qbase = reinterpret_cast<const float4*>(q + (size_t)b * Hl * HD + (size_t)kvh * G * HD);
-    constexpr int PER = (CH * F4 + 255) / 256;
-    float4 kr[PER], vr[PER];
-#pragma unroll
-    for (int k = 0; k < PER; ++k) {
-        const int i = k * 256 + tid;
-        if (i < n_past * F4) { kr[k] = kbase[i]; vr[k] = vbase[i]; }
+    // K and V rows go straight to shared memory (cp.async, all in flight, no
+    // registers); rows before P - 1 are copied before the wait
+    for (int i = tid; i < n_past * F4; i += 256) {
+        cp_async16_smem(&ks[i / F4][i % F4], kbase + i);
+        cp_async16_smem(&vs[i / F4][i % F4], vbase + i);
     }
     pdl_wait();
-#pragma unroll
-    for (int k = 0; k < PER; ++k) {
-        const int i = k * 256 + tid;
-        if (i >= n_past * F4 && i < n * F4) { kr[k] = kbase[i]; vr[k] = vbase[i]; }
+    for (int i = n_past * F4 + tid; i < n * F4; i += 256) {
+        cp_async16_smem(&ks[i / F4][i % F4], kbase + i);
+        cp_async16_smem(&vs[i / F4][i % F4], vbase + i);
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     for (int i = tid; i < G * F4; i += 256) qs[i / F4][i % F4] = qbase[i];
-#pragma unroll
-    for (int k = 0; k < PER; ++k) {
-        const int i = k * 256 + tid;
-        if (i < n * F4) { ks[i / F4][i % F4] = kr[k]; vs[i / F4][i % F4] = vr[k]; }
-    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    // scores: lanes 2p and 2p + 1 take (position p % CH, head p / CH), each
+    // scores: lanes 2p and 2p + 1 take (position p % CHK, head p / CHK), each
     // half of head_dim (interleaved float4), summed with one shuffle
-    static_assert(CH == 32, "a warp's 16 pairs share one head");
-    for (int pr = tid >> 1; pr < CH * G; pr += 128) {
-        const int i = pr & (CH - 1), g = pr / CH, h = tid & 1;
+    for (int pr = tid >> 1; pr < CHK * G; pr += 128) {
+        const int i = pr & (CHK - 1), g = pr / CHK, h = tid & 1;
         float acc = 0.f;
         if (i < n) {
 #pragma unroll
@@ -265,7 +278,7 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
         }
     }
     }  // active
-    int nparts = (int)((P + CH - 1) / CH);  // partials the global merge combines (MODE 1: chunks)
+    int nparts = (int)((P + CHK - 1) / CHK);  // partials the global merge combines (MODE 1: chunks)
     if constexpr (MODE == 2) {
         namespace cg = cooperative_groups;
         cg::cluster_group cluster = cg::this_cluster();
@@ -273,6 +286,7 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
             for (int i = tid; i < G * HD; i += 256) s_o[i / HD][i % HD] = 0.f;
             if (tid < G) { s_m[tid] = -INFINITY; s_l[tid] = 0.f; }
         }
+        pdl_trigger();
         cluster.sync();  // every rank's partial is in its shared memory
         float oo[2] = {0.f, 0.f};
         if (crank == 0) {
@@ -293,8 +307,14 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
                 const int o = tid + 256 * u;
                 if (o < G * HD) {
                     const int g = o / HD;
+                    // all ranks' values in flight at once (cs <= 16)
+                    float v[16];
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) v[k] = k < cs ? cluster.map_shared_rank(&s_o[0][0], k)[o] : 0.f;
                     float acc = 0.f;
-                    for (int k = 0; k < cs; ++k) acc = fmaf(cluster.map_shared_rank(&s_o[0][0], k)[o], cw[g * cs + k], acc);
+#pragma unroll
+                    for (int k = 0; k < 16; ++k)
+                        if (k < cs) acc = fmaf(v[k], cw[g * cs + k], acc);
                     oo[u] = acc;
                 }
             }
@@ -875,12 +895,12 @@ struct ProfScope {
 // serialization when pdl is set (the kernel calls pdl_wait before reading
 // what the previous kernel writes).
 template <class... KArgs, class... Args>
-void launch_kc(void (*kern)(KArgs...), dim3 grid, dim3 block, dim3 cluster, cudaStream_t s, bool pdl,
+void launch_kc(void (*kern)(KArgs...), dim3 grid, dim3 block, dim3 cluster, size_t smem, cudaStream_t s, bool pdl,
                Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     int na = 0;
@@ -902,7 +922,7 @@ void launch_kc(void (*kern)(KArgs...), dim3 grid, dim3 block, dim3 cluster, cuda
 }
 template <class... KArgs, class... Args>
 void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, bool pdl, Args... args) {
-    launch_kc(kern, grid, block, dim3(1, 1, 1), s, pdl, args...);
+    launch_kc(kern, grid, block, dim3(1, 1, 1), 0, s, pdl, args...);
 }
 
 // Cluster size of the decode attention (clusters of chunk CTAs of one KV head
@@ -910,7 +930,12 @@ void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, boo
 // such clusters (non-portable size), else 8, else 0 (no clusters: MODE 1).
 template <int HD>
 int attn_cluster_size(int hkv, int nchunk, int batch) {
-    auto kern = attn_split_kernel<HD, 2>;
+    auto kern = attn_split_kernel<HD, 2, kAttnClusterChunk>;
+    const size_t smem = attn_smem_bytes(HD, kAttnClusterChunk);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
     for (int cs : {16, 8}) {
         if (cs == 16 &&
             cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
@@ -920,6 +945,7 @@ int attn_cluster_size(int hkv, int nchunk, int batch) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(hkv, (nchunk + cs - 1) / cs * cs, batch);
         cfg.blockDim = dim3(256);
+        cfg.dynamicSmemBytes = smem;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 1;
@@ -993,34 +1019,40 @@ void enqueue_step(at_model* m, int B) {
             const bool fused = (m->Hl / m->Hkvl) * m->nchunk_max <= CH * hd;
             const int cs = m->attn_cs;
             if (fused && cs > 1) {
-                // chunks merged per cluster through distributed shared memory
-                dim3 gc(m->Hkvl, (m->nchunk_max + cs - 1) / cs * cs, B);
+                // 64-position chunks merged per cluster through distributed shared memory
+                const int nch64 = (m->ctx_len + kAttnClusterChunk - 1) / kAttnClusterChunk;
+                dim3 gc(m->Hkvl, (nch64 + cs - 1) / cs * cs, B);
+                const size_t sm = attn_smem_bytes(hd, kAttnClusterChunk);
                 if (hd == 128)
-                    launch_kc(attn_split_kernel<128, 2>, gc, 256, dim3(1, cs, 1), s, m->pdl, qp, (const float*)kc,
-                              (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
-                              m->nchunk_max, scale, m->attn_cnt, m->att);
+                    launch_kc(attn_split_kernel<128, 2, kAttnClusterChunk>, gc, 256, dim3(1, cs, 1), sm, s, m->pdl, qp,
+                              (const float*)kc, (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len,
+                              m->slot_stride, m->nchunk_max, scale, m->attn_cnt, m->att);
                 else
-                    launch_kc(attn_split_kernel<64, 2>, gc, 256, dim3(1, cs, 1), s, m->pdl, qp, (const float*)kc,
-                              (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
-                              m->nchunk_max, scale, m->attn_cnt, m->att);
+                    launch_kc(attn_split_kernel<64, 2, kAttnClusterChunk>, gc, 256, dim3(1, cs, 1), sm, s, m->pdl, qp,
+                              (const float*)kc, (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len,
+                              m->slot_stride, m->nchunk_max, scale, m->attn_cnt, m->att);
             } else if (fused) {
                 if (hd == 128)
-                    launch_k(attn_split_kernel<128, 1>, g1, 256, s, m->pdl, qp, (const float*)kc,
+                    launch_kc(attn_split_kernel<128, 1>, g1, 256, dim3(1, 1, 1), attn_smem_bytes(128, CH), s, m->pdl,
+                              qp, (const float*)kc,
                              (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
                              m->nchunk_max, scale, m->attn_cnt, m->att);
                 else
-                    launch_k(attn_split_kernel<64, 1>, g1, 256, s, m->pdl, qp, (const float*)kc,
+                    launch_kc(attn_split_kernel<64, 1>, g1, 256, dim3(1, 1, 1), attn_smem_bytes(64, CH), s, m->pdl,
+                              qp, (const float*)kc,
                              (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
                              m->nchunk_max, scale, m->attn_cnt, m->att);
             } else {
                 unsigned* no_cnt = nullptr;
                 float* no_att = nullptr;
                 if (hd == 128)
-                    launch_k(attn_split_kernel<128>, g1, 256, s, m->pdl, qp, (const float*)kc, (const float*)vc,
+                    launch_kc(attn_split_kernel<128>, g1, 256, dim3(1, 1, 1), attn_smem_bytes(128, CH), s, m->pdl, qp,
+                              (const float*)kc, (const float*)vc,
                              dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max, scale,
                              no_cnt, no_att);
                 else
-                    launch_k(attn_split_kernel<64>, g1, 256, s, m->pdl, qp, (const float*)kc, (const float*)vc,
+                    launch_kc(attn_split_kernel<64>, g1, 256, dim3(1, 1, 1), attn_smem_bytes(64, CH), s, m->pdl, qp,
+                              (const float*)kc, (const float*)vc,
                              dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max, scale,
                              no_cnt, no_att);
                 dim3 g2(m->Hl, B);
@@ -1512,8 +1544,11 @@ int at_model_finalize(at_model* m) {
             alloc_zero((void**)&m->logits_local, (size_t)B * m->Vl * 4);
         }
         m->nchunk_max = (m->ctx_len + CH - 1) / CH;
-        m->attn_cs = (hd == 128) ? attn_cluster_size<128>(m->Hkvl, m->nchunk_max, B)
-                                 : attn_cluster_size<64>(m->Hkvl, m->nchunk_max, B);
+        {
+            const int nch64 = (m->ctx_len + kAttnClusterChunk - 1) / kAttnClusterChunk;
+            m->attn_cs = (hd == 128) ? attn_cluster_size<128>(m->Hkvl, nch64, B)
+                                     : attn_cluster_size<64>(m->Hkvl, nch64, B);
+        }
         alloc_zero((void**)&m->att_part, (size_t)B * m->Hl * m->nchunk_max * (hd + 2) * 4);
         alloc_zero((void**)&m->attn_cnt, (size_t)B * m->Hkvl * sizeof(unsigned));
         // KV cache (inference/KVCache.java:43-63): [slot][layer][kvHead][ctx][headDim] fp32
@@ -1781,11 +1816,11 @@ void run_prompt_batched(at_model* m, const int* tokens, int n) {
             AT_CUDA(cudaGetLastError());
             dim3 g1(m->Hkvl, m->nchunk_max, T), g2(m->Hl, T);
             if (hd == 128) {
-                attn_split_kernel<128><<<g1, 256, 0, s>>>(m->pf_q, kc, vc, m->pf_pos, m->pf_part, m->Hl, m->Hkvl,
+                attn_split_kernel<128><<<g1, 256, attn_smem_bytes(128, CH), s>>>(m->pf_q, kc, vc, m->pf_pos, m->pf_part, m->Hl, m->Hkvl,
                                                           m->ctx_len, 0, m->nchunk_max, scale);
                 attn_combine_kernel<128><<<g2, 128, 0, s>>>(m->pf_part, m->pf_pos, m->pf_att, m->Hl, m->nchunk_max);
             } else {
-                attn_split_kernel<64><<<g1, 256, 0, s>>>(m->pf_q, kc, vc, m->pf_pos, m->pf_part, m->Hl, m->Hkvl,
+                attn_split_kernel<64><<<g1, 256, attn_smem_bytes(64, CH), s>>>(m->pf_q, kc, vc, m->pf_pos, m->pf_part, m->Hl, m->Hkvl,
                                                          m->ctx_len, 0, m->nchunk_max, scale);
                 attn_combine_kernel<64><<<g2, 64, 0, s>>>(m->pf_part, m->pf_pos, m->pf_att, m->Hl, m->nchunk_max);
             }
