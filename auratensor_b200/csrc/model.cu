@@ -127,9 +127,11 @@ __device__ __forceinline__ float exp_ref(float v) { return (float)exp((double)v)
 // (the merge weights reuse the K staging buffer).
 // MODE 2 (decode step, CHK = 64, launched with clusters of CS CTAs along the chunks):
 // the CTAs of a cluster keep their partials in shared memory; after a cluster
-// barrier rank 0 merges them through distributed shared memory. When one
-// cluster covers the sequence it writes `att` directly; otherwise the cluster
-// partials (one per CS * CHK positions) are merged as in MODE 1. A cluster
+// barrier every rank merges a slice of the G * HD outputs, reading one float4
+// of each rank's partial per thread through distributed shared memory. When
+// one cluster covers the sequence the ranks write `att` directly; otherwise
+// the cluster partials (one per CS * CHK positions) are merged as in MODE 1
+// by rank 0 of the last cluster to arrive. A cluster
 // whose first chunk lies past the sequence exits as a whole; idle CTAs of a
 // partly used cluster take part in its barriers with an empty partial.
 // 16-byte asynchronous copy global -> shared (L2 only).
@@ -288,62 +290,58 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
         }
         pdl_trigger();
         cluster.sync();  // every rank's partial is in its shared memory
-        float oo[2] = {0.f, 0.f};
-        if (crank == 0) {
-            float* cw = reinterpret_cast<float*>(ks);  // [G][cs] merge weights
-            if (warp < G) {
-                const int g = warp;
-                const float mk = lane < cs ? cluster.map_shared_rank(&s_m[0], lane)[g] : -INFINITY;
-                const float lk = lane < cs ? cluster.map_shared_rank(&s_l[0], lane)[g] : 0.f;
-                const float M = warp_max(mk);  // rank 0 is active: finite
-                const float w = lane < cs ? exp_ref(__fsub_rn(mk, M)) : 0.f;
-                const float L = warp_sum(lk * w);
-                if (lane < cs) cw[g * cs + lane] = w;
-                if (lane == 0) { s_cm[g] = M; s_cl[g] = L; }
-            }
-            __syncthreads();
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int o = tid + 256 * u;
-                if (o < G * HD) {
-                    const int g = o / HD;
-                    // all ranks' values in flight at once (cs <= 16)
-                    float v[16];
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) v[k] = k < cs ? cluster.map_shared_rank(&s_o[0][0], k)[o] : 0.f;
-                    float acc = 0.f;
-#pragma unroll
-                    for (int k = 0; k < 16; ++k)
-                        if (k < cs) acc = fmaf(v[k], cw[g * cs + k], acc);
-                    oo[u] = acc;
-                }
-            }
+        // Every rank merges a slice of per = G * HD / cs outputs (a whole
+        // number of float4): weights of all heads from the ranks' (m, l), then
+        // one float4 of each rank's o per thread through DSMEM.
+        float* cw = reinterpret_cast<float*>(ks);  // [G][cs] merge weights
+        if (warp < G) {
+            const int g = warp;
+            const float mk = lane < cs ? cluster.map_shared_rank(&s_m[0], lane)[g] : -INFINITY;
+            const float lk = lane < cs ? cluster.map_shared_rank(&s_l[0], lane)[g] : 0.f;
+            const float M = warp_max(mk);  // rank 0 is active: finite
+            const float w = lane < cs ? exp_ref(__fsub_rn(mk, M)) : 0.f;
+            const float L = warp_sum(lk * w);
+            if (lane < cs) cw[g * cs + lane] = w;
+            if (lane == 0) { s_cm[g] = M; s_cl[g] = L; }
         }
-        cluster.sync();  // rank 0 has read every peer's shared memory
-        if (crank != 0) return;
-        const int ncl = (nparts + cs - 1) / cs;  // clusters over the sequence
+        const int per = (G * HD) / cs, nq = per / 4, o_lo = crank * per;
+        float4* pv = reinterpret_cast<float4*>(vs);  // [cs][nq] the ranks' float4 of this slice
+        if (tid < cs * nq) {
+            const int k = tid / nq, j = tid - k * nq;
+            pv[k * nq + j] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(&s_o[0][0], k) + o_lo + 4 * j);
+        }
+        __syncthreads();
+        cluster.sync();  // every rank has read what it needs from its peers
+        const int nclu = (nparts + cs - 1) / cs;  // clusters over the sequence
         const int cl_idx = chunk / cs;
-        if (ncl == 1) {
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int o = tid + 256 * u;
-                if (o < G * HD)
-                    att[(size_t)b * Hl * HD + (size_t)kvh * G * HD + o] = __fdiv_rn(oo[u], s_cl[o / HD]);
+        if (tid < nq) {
+            const int o = o_lo + 4 * tid, g = o / HD, dd = o - g * HD;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int k = 0; k < cs; ++k) {
+                const float4 v = pv[k * nq + tid];
+                const float w = cw[g * cs + k];
+                acc = make_float4(fmaf(v.x, w, acc.x), fmaf(v.y, w, acc.y), fmaf(v.z, w, acc.z), fmaf(v.w, w, acc.w));
             }
-            return;
-        }
-        // several clusters: publish this cluster's partial as partial cl_idx
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int o = tid + 256 * u;
-            if (o < G * HD) {
-                const int g = o / HD, dd = o - g * HD;
+            if (nclu == 1) {
+                const float L = s_cl[g];
+                *reinterpret_cast<float4*>(att + (size_t)b * Hl * HD + (size_t)kvh * G * HD + o) =
+                    make_float4(__fdiv_rn(acc.x, L), __fdiv_rn(acc.y, L), __fdiv_rn(acc.z, L), __fdiv_rn(acc.w, L));
+            } else {
+                // this cluster's partial number cl_idx, merged below across clusters
+                // partial rows are HD + 2 floats: only 4-byte aligned, so scalar stores
                 float* dst = part + (((size_t)b * Hl + kvh * G + g) * nchunk_max + cl_idx) * (HD + 2);
-                dst[dd] = oo[u];
+                dst[dd] = acc.x;
+                dst[dd + 1] = acc.y;
+                dst[dd + 2] = acc.z;
+                dst[dd + 3] = acc.w;
                 if (dd == 0) { dst[HD] = s_cm[g]; dst[HD + 1] = s_cl[g]; }
+                __threadfence();
             }
         }
-        nparts = ncl;
+        if (nclu == 1) return;
+        cluster.sync();  // every slice of the cluster partial is written and fenced
+        if (crank != 0) return;
+        nparts = nclu;
     }
     if constexpr (MODE >= 1) {
         const int nch = nparts;
@@ -1018,7 +1016,8 @@ void enqueue_step(at_model* m, int B) {
             // weights of a KV head's query heads fit the K staging buffer
             const bool fused = (m->Hl / m->Hkvl) * m->nchunk_max <= CH * hd;
             const int cs = m->attn_cs;
-            if (fused && cs > 1) {
+            // each cluster rank merges a whole number of float4 outputs
+            if (fused && cs > 1 && ((m->Hl / m->Hkvl) * hd) % (4 * cs) == 0) {
                 // 64-position chunks merged per cluster through distributed shared memory
                 const int nch64 = (m->ctx_len + kAttnClusterChunk - 1) / kAttnClusterChunk;
                 dim3 gc(m->Hkvl, (nch64 + cs - 1) / cs * cs, B);
