@@ -176,6 +176,11 @@ class GgufFile:
             raise ValueError(f"tensor '{info.name}' extends past end of file")
         return self._buf[start:start + n]
 
+    # The reference's names (format/GgufFile.java:155,319): findTensor returns
+    # null for an unknown name, tensorData the tensor's bytes in the mapping.
+    findTensor = find_tensor
+    tensorData = tensor_data
+
     def close(self):
         try:
             if isinstance(self._mm, mmap.mmap):

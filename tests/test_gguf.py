@@ -46,6 +46,11 @@ def test_roundtrip_tiny_model(tmp_path):
             assert info.num_elements() == int(np.prod(tt["dims"]))
             assert bytes(g.tensor_data(info)) == tt["data"].tobytes()
         assert g.find_tensor("nope") is None
+        # the reference's method names are the same calls
+        assert g.findTensor("nope") is None
+        first = g.tensor_infos[0]
+        assert g.findTensor(first.name) is first
+        assert bytes(g.tensorData(first)) == bytes(g.tensor_data(first))
 
 
 def test_config_defaults():
