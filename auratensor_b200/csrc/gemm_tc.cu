@@ -19,13 +19,14 @@
 // completing on the stage's "full" mbarrier; the weight tile is dequantized
 // by all 8 warps from raw block bytes loaded into registers three steps ahead.
 // One thread issues four tcgen05.mma (K = 16 each) per step and commits them
-// to the stage's "empty" mbarrier; three stages keep the TMA, the dequant and
+// to the stage's "empty" mbarrier; four stages (TC_STAGES) keep the TMA, the dequant and
 // the tensor core working on different steps. The 128 x 128 FP32 accumulator
 // lives in 128 TMEM columns; the epilogue reads it with tcgen05.ld (warp w
 // reads TMEM lanes 32 (w % 4) ..) and stores FP32 rows of Y.
 //
 // Every wait on an mbarrier is bounded; a wait that runs out records an error
-// code, stops issuing, and the CTA still frees its TMEM before returning.
+// code, stops issuing, drains the token-tile copies still in flight, and the
+// CTA still frees its TMEM before returning.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
@@ -288,6 +289,7 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
     tc_fence_after();
     const uint32_t tmem = s_tmem;
     auto fail = [&]() { atomicExch(p.err, 2); s_bad = 1; };
+    int tma_issued = 0;  // token-tile loads issued (warp 0, lane 0)
 
     if (warp == 0) {
         // ---- token tiles by TMA ----
@@ -300,6 +302,7 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
                 }
                 mbar_expect_tx(smem_u32(&s_fb[st]), TC_TILE_BYTES);
                 tma_load_x(smem_u32(b_tile(st)), &xmap, kbase + ks * TC_K, t0, smem_u32(&s_fb[st]));
+                ++tma_issued;
             }
         }
     } else if (warp == 1) {
@@ -353,6 +356,12 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
     if (!ok && tid == 0) atomicExch(p.err, 2);
     __syncthreads();
     ok = ok && (s_bad == 0);
+    // After a failed wait the MMAs may not have consumed every token tile:
+    // drain the loads still in flight (the latest one of each stage, bounded
+    // waits) so that no copy lands in shared memory after the CTA exits.
+    if (!ok && tid == 0)
+        for (int ks = max(0, tma_issued - TC_STAGES); ks < tma_issued; ++ks)
+            mbar_wait(smem_u32(&s_fb[ks % TC_STAGES]), (ks / TC_STAGES) & 1);
     tc_fence_after();
     if (ok && warp >= 2) {
         const int quarter = warp & 3, half = (warp - 2) >> 2;

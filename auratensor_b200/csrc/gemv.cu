@@ -1823,7 +1823,9 @@ void gemv_t_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* float
     int S = 1, per = 0;
     t_config(m, batch, num_sms, &S, &per);
     const size_t n_bc = (size_t)(m->cols / QK);
-    const bool global_split = S > 8 || batch > 2;  // see run_t: the other splits combine in cluster shared memory
+    // see run_t: only a real split (S > 1) touches scratch, and splits of up
+    // to 8 CTAs at batch <= 2 combine in cluster shared memory instead
+    const bool global_split = S > 1 && (S > 8 || batch > 2);
     *floats = global_split ? n_bc * S * batch * 32 : 0;
     *counters = global_split ? n_bc : 0;
 }

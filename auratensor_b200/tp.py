@@ -1,6 +1,8 @@
 """Tensor-parallel bootstrap: one process per GPU, torch.distributed for the
-rendezvous, an NCCL communicator owned by libauratensor_cuda.so for the
-per-layer all-reduces.
+rendezvous, an NCCL communicator owned by libauratensor_cuda.so that
+exchanges the peer-memory handles once at model finalize (the per-layer
+all-reduces and the logits gather are the library's own kernels over NVLink
+peer memory).
 
 Rank 0 creates the 128-byte NCCL unique id through the C ABI and broadcasts
 it with ``torch.distributed``; every rank then creates its ``at_ctx`` with

@@ -13,8 +13,10 @@ flush is needed between steps.
          and the full logits out in host memory each step, then the greedy
          Sampler on the host (the reference's decode loop).
 
-N > 1: one process per GPU (torchrun), Megatron tensor parallelism with NCCL
-all-reduces inside the captured step graph; scaling "strong".
+N > 1: one process per GPU (torchrun), Megatron tensor parallelism; the
+per-layer all-reduces and the logits gather are the library's own kernels over
+NVLink peer memory (NCCL only exchanges the memory handles at load); scaling
+"strong".
 
 --impl reference: the reference's CPU algorithm (load-time dequant to FP32,
 FP32 sgemv; the C restatement under oracle/) on all host cores, each step a
@@ -50,6 +52,7 @@ def parse():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--profile-steps", type=int, default=8)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-parity", action="store_true")
     # smaller cases for profiler captures only (the bench line uses the defaults)
     p.add_argument("--prompt", type=int, default=PROMPT)
     p.add_argument("--layers", type=int, default=None)
@@ -244,6 +247,70 @@ def build_model(shape, seed, ctx, world, keep_host: bool):
     return model, host
 
 
+def parity_check(full_shape, seed, ctx, world, rank):
+    """The bench's decode path against the oracle, in the same run and at the
+    same tensor-parallel degree: a 2-layer model of the bench's dimensions
+    (the same kernels and shard sizes) on every rank, and the C restatement
+    of the reference on rank 0 with the same weights. The oracle runs 8
+    seeded prompt tokens then 16 greedy steps; rank 0 broadcasts that token
+    sequence, every rank steps the device model through it, and rank 0
+    compares the logits of every step: max |delta| / (max - min of the
+    oracle's logits) against the 1e-3 rule, and the greedy tokens (equal, or
+    the oracle's top-2 gap below the rule)."""
+    import dataclasses
+    import torch
+    import torch.distributed as dist
+    from auratensor_b200 import synth
+    from auratensor_b200.inference import LlamaConfig, LlamaModel
+    shape = dataclasses.replace(full_shape, n_layers=2, ctx=64)
+    n_prompt, n_greedy, tol = 8, 16, 1e-3
+    g = torch.Generator(device="cuda").manual_seed(seed + 1000)
+    model = LlamaModel(LlamaConfig.fromShape(shape), None, max_batch=1, ctx=ctx, world=world)
+    orc = None
+    if rank == 0:
+        from oracle.cref import RefDecoder
+        orc = RefDecoder(shape, threads=os.cpu_count() or 1)
+    for name, dims, t in shape.tensor_dims():
+        data = synth.generate_torch_tensor(dims, t, g, "cuda")
+        model.setTensor(name, t, data)
+        if orc is not None:
+            orc.set_tensor(name, t, data.cpu().numpy(), int(np.prod(dims)))
+        del data
+    model.finalize()
+    n = n_prompt + n_greedy
+    seq = torch.zeros(n, dtype=torch.int64, device="cuda")
+    ref_logits = []
+    if rank == 0:
+        toks = [int(v) for v in synth.prompt_ids(shape, seed, n_prompt)]
+        for pos in range(n):
+            lr = orc.forward_step(toks[pos], pos)
+            ref_logits.append(lr)
+            if pos + 1 < n and pos + 1 >= n_prompt:
+                toks.append(int(np.argmax(lr)))
+        seq.copy_(torch.tensor(toks, dtype=torch.int64))
+        orc.close()
+    if world > 1:
+        dist.broadcast(seq, 0)
+    toks = [int(v) for v in seq.cpu().tolist()]
+    worst, equal, rule_ok = 0.0, 0, True
+    for pos in range(n):
+        lg = model.forwardStep(toks[pos], pos)
+        if rank == 0:
+            lr = ref_logits[pos]
+            rng_ = float(lr.max() - lr.min())
+            worst = max(worst, float(np.max(np.abs(lg - lr))) / rng_)
+            if pos >= n_prompt - 1:
+                if int(np.argmax(lg)) == int(np.argmax(lr)):
+                    equal += 1
+                else:
+                    srt = np.sort(lr)
+                    rule_ok = rule_ok and float(srt[-1] - srt[-2]) < tol * rng_
+    model.close()
+    return {"checked": True, "model": f"{shape.name} dims, 2 layers, tp{world}", "steps": n,
+            "max_rel_err": float(f"{worst:.3g}"), "tol": tol, "greedy_steps": n_greedy + 1,
+            "tokens_equal": equal, "passed": bool(worst <= tol and rule_ok)}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -321,6 +388,7 @@ def main():
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         segs, pos = positions(pos, args.steps)
+        timed_pos = [p0 + i for p0, k in segs for i in range(k)]
         e0.record(stream)
         for p0, k in segs:
             model.generate(tok, p0, k, wait=False)
@@ -356,10 +424,21 @@ def main():
             a[1] += n
     value = args.steps / (ms / 1000.0)
     e2e = args.steps / (ms_e2e / 1000.0)
+    parity = None
+    if not args.no_parity:
+        parity = parity_check(shape, args.seed, ctx, world, rank)
     if rank != 0:
         finish(model, ctx, world)
         return
     bytes_per = class_bytes(shape, world, pos)
+    # bytes one GPU must move per decode step (weights of its shards, its KV
+    # heads at the timed positions, activations), over the measured step time
+    step_bytes = 0.0
+    for p in timed_pos:
+        cb = class_bytes(shape, world, p)
+        step_bytes += shape.n_layers * (cb["qkv"] + cb["attn"] + cb["wo"] + cb["ffn_up"] + cb["ffn_down"])
+        step_bytes += cb["lm_head"] + q_bytes(1, shape.dim)
+    step_bytes /= len(timed_pos)
     gemv = {k: v for k, v in tot.items() if k in bytes_per}
     dom = max(gemv, key=lambda k: gemv[k][0])
     avg_ms = gemv[dom][0] / max(1, gemv[dom][1])
@@ -394,7 +473,10 @@ def main():
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "traffic": traffic, "bytes_per_launch": bytes_per[dom],
-                     "avg_launch_us": round(avg_ms * 1000.0, 2)},
+                     "avg_launch_us": round(avg_ms * 1000.0, 2),
+                     "step_bytes": int(step_bytes),
+                     "step_frac": round(step_bytes / (ms / args.steps / 1000.0) / 1e9 / peak, 4)},
+        "parity": parity,
         "kernel_ms_per_step": {k: round(v[0] / args.profile_steps, 4) for k, v in tot.items() if v[1]},
         "eager_step_ms": round(step_ms_eager, 4),
         "gpu_launches": launches_per_step * args.steps,
@@ -410,8 +492,9 @@ def main():
 
 
 def finish(model, ctx, world):
-    """Releases the step graphs (which hold NCCL calls) and the communicator
-    before the process group goes away; every rank takes the same steps."""
+    """Releases the model (its step graphs and the peer-mapped exchange
+    areas) and the context's communicator before the process group goes
+    away; every rank takes the same steps."""
     import torch.distributed as dist
     from auratensor_b200 import _lib
     model.close()

@@ -51,6 +51,10 @@ def lib():
         L.rd_set_tensor.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_void_p, C.c_int64]
         L.rd_forward_step.restype = C.POINTER(C.c_float)
         L.rd_forward_step.argtypes = [C.c_void_p, C.c_int, C.c_int]
+        L.rd_forward_layers.restype = None
+        L.rd_forward_layers.argtypes = [C.c_void_p, C.c_int, C.c_int]
+        L.rd_kv.restype = None
+        L.rd_kv.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         L.rd_times.argtypes = [C.c_void_p] + [C.POINTER(C.c_double)] * 3
         L.rd_destroy.argtypes = [C.c_void_p]
         _lib = L
@@ -77,6 +81,17 @@ class RefDecoder:
     def forward_step(self, token: int, pos: int) -> np.ndarray:
         p = lib().rd_forward_step(self._h, int(token), int(pos))
         return np.ctypeslib.as_array(p, shape=(self.shape.vocab,)).copy()
+
+    def forward_layers(self, token: int, pos: int) -> None:
+        """forward_step without the lm_head: fills the KV cache only."""
+        lib().rd_forward_layers(self._h, int(token), int(pos))
+
+    def kv(self, layer: int, kv_head: int, pos: int):
+        hd = self.shape.dim // self.shape.n_heads
+        k = np.empty(hd, dtype=np.float32)
+        v = np.empty(hd, dtype=np.float32)
+        lib().rd_kv(self._h, layer, kv_head, pos, k.ctypes.data_as(C.c_void_p), v.ctypes.data_as(C.c_void_p))
+        return k, v
 
     def times(self):
         a, b, c = C.c_double(), C.c_double(), C.c_double()

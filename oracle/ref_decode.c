@@ -17,7 +17,8 @@
  * sums per row. The only deviation: the token embedding row is dequantized
  * at lookup instead of dequantizing the whole table at load (a row copy in
  * the reference; it does not change any value).
- * Threads: OpenMP over output rows of each matvec (1 thread = the
+ * Threads: OpenMP over output rows of each matvec and over the query heads
+ * of the attention (1 thread = the
  * reference's single-threaded loop).
  */
 #include <math.h>
@@ -80,20 +81,27 @@ static void dequant(int type, const uint8_t* src, float* dst, int64_t n) {
     }
 }
 
-/* Kernels.sgemv: y[M] = A[M,K] x[K], 16 lane-wise partial sums then a reduce. */
+/* One row of Kernels.sgemv: 16 lane-wise partial sums then a reduce. */
+static float sgemv_row(const float* a, const float* x, int K) {
+    float acc[16] = {0};
+    int k = 0;
+    for (; k + 16 <= K; k += 16)
+        for (int l = 0; l < 16; ++l) acc[l] = fmaf(a[k + l], x[k + l], acc[l]);
+    float s = 0.f;
+    for (int l = 0; l < 16; ++l) s += acc[l];
+    for (; k < K; ++k) s += a[k] * x[k];
+    return s;
+}
+
+/* Kernels.sgemv: y[M] = A[M,K] x[K], rows over the threads. */
 static void sgemv(const float* A, const float* x, float* y, int M, int K) {
 #pragma omp parallel for schedule(static)
-    for (int i = 0; i < M; ++i) {
-        const float* a = A + (size_t)i * K;
-        float acc[16] = {0};
-        int k = 0;
-        for (; k + 16 <= K; k += 16)
-            for (int l = 0; l < 16; ++l) acc[l] = fmaf(a[k + l], x[k + l], acc[l]);
-        float s = 0.f;
-        for (int l = 0; l < 16; ++l) s += acc[l];
-        for (; k < K; ++k) s += a[k] * x[k];
-        y[i] = s;
-    }
+    for (int i = 0; i < M; ++i) y[i] = sgemv_row(A + (size_t)i * K, x, K);
+}
+
+/* The same on the calling thread only (inside a parallel region). */
+static void sgemv_rows(const float* A, const float* x, float* y, int M, int K) {
+    for (int i = 0; i < M; ++i) y[i] = sgemv_row(A + (size_t)i * K, x, K);
 }
 
 static void rmsnorm(float* x, const float* w, int d, float eps) {
@@ -167,7 +175,7 @@ rd_model* rd_create(const rd_cfg* c, int threads) {
     m->x = falloc(d); m->q = falloc((size_t)c->n_heads * hd); m->k = falloc((size_t)c->n_kv * hd);
     m->v = falloc((size_t)c->n_kv * hd); m->att = falloc((size_t)c->n_heads * hd); m->proj = falloc(d);
     m->g = falloc(c->ffn); m->u = falloc(c->ffn); m->ff = falloc(d); m->logits = falloc(c->vocab);
-    m->scores = falloc(c->ctx);
+    m->scores = falloc((size_t)c->n_heads * c->ctx);  /* one row per head */
     return m;
 }
 
@@ -226,16 +234,20 @@ static void layer_step(rd_model* m, int l, int pos) {
     }
     const float scale = (float)(1.0 / sqrt((double)hd));
     const int M = pos + 1;
+    /* Heads are independent (each one's arithmetic is sequential), so they
+     * run on separate threads with a scores row each. */
+#pragma omp parallel for schedule(static)
     for (int h = 0; h < H; ++h) {
         const int kvh = (Hkv == H) ? h : (int)((int64_t)h * Hkv / H);
         const size_t base = ((size_t)l * Hkv + kvh) * ctx * hd;
-        sgemv(m->kc + base, m->q + (size_t)h * hd, m->scores, M, hd);
-        for (int p = 0; p < M; ++p) m->scores[p] *= scale;
-        softmax(m->scores, M);
+        float* sc = m->scores + (size_t)h * ctx;
+        sgemv_rows(m->kc + base, m->q + (size_t)h * hd, sc, M, hd);
+        for (int p = 0; p < M; ++p) sc[p] *= scale;
+        softmax(sc, M);
         float* o = m->att + (size_t)h * hd;
         for (int j = 0; j < hd; ++j) {
             float acc = 0.f;
-            for (int p = 0; p < M; ++p) acc = fmaf(m->vc[base + (size_t)p * hd + j], m->scores[p], acc);
+            for (int p = 0; p < M; ++p) acc = fmaf(m->vc[base + (size_t)p * hd + j], sc[p], acc);
             o[j] = acc;
         }
     }
@@ -250,8 +262,23 @@ static void layer_step(rd_model* m, int l, int pos) {
     for (int i = 0; i < d; ++i) m->x[i] += m->ff[i];
 }
 
+static const float* forward(rd_model* m, int token, int pos, int with_logits);
+
 /* LlamaModel.forwardStep: returns the logits buffer (vocab floats). */
-const float* rd_forward_step(rd_model* m, int token, int pos) {
+const float* rd_forward_step(rd_model* m, int token, int pos) { return forward(m, token, pos, 1); }
+
+/* The same step without the output norm and lm_head (fills the KV cache only;
+ * the logits of such a step are never looked at). */
+void rd_forward_layers(rd_model* m, int token, int pos) { forward(m, token, pos, 0); }
+
+/* K and V of (layer, kv head, position): hd floats each. */
+void rd_kv(const rd_model* m, int layer, int kv_head, int pos, float* k, float* v) {
+    const size_t off = (((size_t)layer * m->c.n_kv + kv_head) * m->c.ctx + pos) * m->hd;
+    memcpy(k, m->kc + off, (size_t)m->hd * 4);
+    memcpy(v, m->vc + off, (size_t)m->hd * 4);
+}
+
+static const float* forward(rd_model* m, int token, int pos, int with_logits) {
     const rd_cfg* c = &m->c;
     const int d = c->dim;
     omp_set_num_threads(m->threads);
@@ -266,8 +293,10 @@ const float* rd_forward_step(rd_model* m, int token, int pos) {
     double t1 = now();
     for (int l = 0; l < c->n_layers; ++l) layer_step(m, l, pos);
     double t2 = now();
-    rmsnorm(m->x, m->out_norm, d, c->eps);
-    sgemv(m->out_w, m->x, m->logits, c->vocab, d);
+    if (with_logits) {
+        rmsnorm(m->x, m->out_norm, d, c->eps);
+        sgemv(m->out_w, m->x, m->logits, c->vocab, d);
+    }
     double t3 = now();
     m->t_embed += t1 - t0;
     m->t_layers += t2 - t1;

@@ -177,11 +177,14 @@ def test_profile_step_counts(cuda):
 
 
 def test_long_context_attention_merge(cuda):
-    """Decode attention past one cluster of chunk CTAs (32 positions per CTA;
-    clusters of 16 or 8 CTAs cover 512 or 256 positions): chunk partials merge
-    in distributed shared memory per cluster, cluster partials through global
-    memory. Teacher-forced over 1100 positions; logits within the parity bound
-    at the compared steps (cluster boundaries included)."""
+    """Decode attention past one cluster of chunk CTAs (64 positions per CTA;
+    clusters of 16 CTAs cover 1024 positions, or 512 where only clusters of 8
+    can be placed): chunk partials merge in distributed shared memory per
+    cluster, cluster partials through global memory. Teacher-forced over 1100
+    positions, so the last ones merge two cluster partials (three with
+    clusters of 8); logits within the parity bound at the compared steps
+    (cluster boundaries included). Head_dim 128 and three or four clusters
+    are covered in test_gpu_shapes.py."""
     shape = dataclasses.replace(synth.TINY, ctx=1100)
     t = synth.generate_numpy(shape, seed=5)
     gpu = LlamaModel(LlamaConfig.fromShape(shape), t)

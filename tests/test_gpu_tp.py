@@ -1,5 +1,6 @@
-"""Tensor parallelism on 2 GPUs (Megatron shards, NCCL all-reduces captured
-in the step graph) against the unsharded oracle.
+"""Tensor parallelism on 2 GPUs (Megatron shards; the per-layer all-reduces
+and the logits gather are the library's own kernels over NVLink peer memory,
+captured in the step graph) against the unsharded oracle.
 
 Two child processes, one per GPU, build the same tiny model from the same
 tensors with ``world=2``; rank 0 compares its logits with the oracle at every

@@ -23,11 +23,13 @@ def static_gemv(m, x, y):
 
 
 @pytest.mark.parametrize("qt", [ref.GGML_Q4_0, ref.GGML_Q8_0])
-# The batch-8 cases and (16384, 64, 1) (each block column split over 16 CTAs)
-# put their partials in the static array; the other splits combine in
-# cluster shared memory, and (300, 640, 1) does not split.
+# The batch-8 cases that split a block column over CTAs and (16384, 64, 1)
+# (each block column split over 16 CTAs) put their partials in the static
+# array; the other splits combine in cluster shared memory, and (300, 640, 1)
+# and (256, 8192, 8) do not split (the latter must not be rejected for
+# partials it never writes).
 @pytest.mark.parametrize("rows,cols,batch", [(4096, 4096, 1), (2048, 1024, 2), (300, 640, 1), (1024, 512, 8),
-                                             (8192, 64, 8), (16384, 64, 1)])
+                                             (8192, 64, 8), (16384, 64, 1), (256, 8192, 8)])
 def test_static_scratch_matches_at_gemv(qt, rows, cols, batch, cuda):
     g = torch.Generator(device=cuda).manual_seed(rows + cols + batch)
     blocks = synth.generate_torch_tensor((rows, cols), qt, g, cuda)
@@ -35,13 +37,16 @@ def test_static_scratch_matches_at_gemv(qt, rows, cols, batch, cuda):
     W = ref.dequant(qt, blocks.cpu().numpy(), rows * cols).reshape(rows, cols).astype(np.float64)
     x = torch.randn((batch, rows), device=cuda)
     want = m.gemv(x).cpu().numpy()  # the existing entry point
-    bound = TOL * (np.abs(x.cpu().numpy()).astype(np.float64) @ np.abs(W)) + 1e-30
+    xd = x.cpu().numpy().astype(np.float64)
+    exact = xd @ W  # the oracle's dequantized weights, in float64
+    bound = TOL * (np.abs(xd) @ np.abs(W)) + 1e-30
     for _ in range(2):
         y = torch.full((batch, cols), float("nan"), device=cuda)
         static_gemv(m, x, y)
         torch.cuda.synchronize()
         got = y.cpu().numpy()
         assert np.all(np.abs(got - want) <= bound)
+        assert np.all(np.abs(got - exact) <= bound)
 
 
 def test_static_scratch_rejects_oversized_split(cuda):
