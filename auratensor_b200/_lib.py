@@ -108,6 +108,8 @@ SIGNATURES = {
     "at_model_forward_batch": [_vp, _vp, _vp, _i, _vp],
     "at_model_logits_device": [_vp, _PP],
     "at_model_argmax": [_vp, _i, _vp],
+    "at_model_step_kernel": [_vp, _vp],
+    "at_model_step_stamps": [_vp, _i, _i64, _vp, _i64, _vp],
     "at_model_generate": [_vp, _i, _i64, _i, _vp],
     "at_model_profile_step": [_vp, _i, _i64, _vp, _vp],
     "at_model_kv_size": [_vp, _i, C.POINTER(C.c_int64)],

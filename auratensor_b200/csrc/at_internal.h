@@ -184,4 +184,84 @@ void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, in
 void launch_sgemv_f32(const float* A, const float* x, float* y, int M, int K, int batch, int a_ld,
                       cudaStream_t s);
 
+// ---------------------------------------------------------------------------
+// Persistent decode step (decode_step.cu): one launch runs a whole batch-1
+// forwardStep (every layer, the lm_head and the argmax) on one CTA per SM,
+// phases separated by grid barriers.
+// ---------------------------------------------------------------------------
+struct DsLayer {  // device table, one entry per layer
+    const uint8_t* qkv;    // orientation-T tiles, inputs d, outputs (Hl + 2 Hkvl) hd
+    const uint8_t* wo;     // orientation-T tiles, inputs Hl hd, outputs d
+    const uint8_t* w1;     // orientation-N tiles [Fl][d]
+    const uint8_t* w3;
+    const uint8_t* w2;     // orientation-N tiles [d][Fl]
+    const float* attn_norm;
+    const float* ffn_norm;
+    float* kc;             // this layer's K cache of slot 0: [Hkvl][ctx][hd]
+    float* vc;
+};
+
+struct DsT {               // an orientation-T matrix in the step
+    int E;                 // inputs (rows)
+    int ngroups;           // 32-row tile groups per block column
+    int ncols;             // block columns (outputs / 32)
+    int nu;                // units (4 row tiles) per block column
+    int S;                 // parts per block column (nu % S == 0); output = sum of the S part sums
+};
+
+struct DsN {               // an orientation-N matrix in the step
+    int rows, nb;          // outputs, 32-element blocks per row
+    int ngroups, nsteps;   // 4-row groups, 32-block steps per group
+};
+
+struct DsParams {
+    const DsLayer* layers;
+    int L;
+    int qtype, hd;
+    int d, Hl, Hkvl, Fl, Vl, ctx;
+    float eps, scale;
+    int64_t tile_t, tile_n; // bytes per T tile / N tile
+    DsT qkv, wo;
+    DsN gu, dn, head;
+    const uint8_t* tok_tiles;
+    QTileMap tok_map;
+    const uint8_t* out_tiles;
+    const float* out_norm;
+    const float* rope_cos;  // [ctx][hd]
+    const float* rope_sin;
+    int* tokens;            // [1]
+    int64_t* pos;           // [1]
+    // activations and exchange buffers
+    float* res0;            // normed residual stream (ping-pong)
+    float* res1;
+    float* ydown;           // down projection output [d]
+    float* qkv_part;        // [qkv.ncols * qkv.S][32]
+    float* wo_part;         // [wo.ncols * wo.S][32]
+    float* h;               // silu(gate) * up [Fl]
+    float* att;             // attention output [Hl * hd]
+    float* apart;           // attention partials [Hkvl][att_max_ctas][G][hd + 2]
+    float* logits;          // [Vl]
+    int att_max_ctas;       // CTAs per KV head at most
+    int nst;                // weight-ring slots per warp (power of two)
+    int slot_bytes;         // bytes per ring slot
+    int gu_pair;            // gate/up units hold the w1 and the w3 tile of one (row group, step)
+    int xs_bytes;           // activation staging bytes
+    unsigned* tickets;      // [Hkvl] attention merge tickets, then one for the argmax
+    unsigned* bar;          // [2]: grid-barrier arrivals, epoch
+    int* err;               // error word (0 = ok)
+    unsigned long long* argkey;
+    int* argmax_out;
+    int greedy;             // advance token / position and append to gen_out
+    int* gen_out;
+    int* gen_count;
+    unsigned long long* stamps;  // optional [gridDim][5 L + 1][4] globaltimer per job
+};
+
+// Shared memory the step kernel needs (dynamic bytes) and its launch.
+size_t decode_step_smem(const DsParams& p);
+void launch_decode_step(const DsParams& p, int num_ctas, cudaStream_t s);
+// Picks the part counts of the T matrices, the ring depth and the staging
+// size for num_ctas CTAs; false when the shapes fall outside the kernel.
+bool decode_step_configure(DsParams* p, int num_ctas);
+
 }  // namespace at

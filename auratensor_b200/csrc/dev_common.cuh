@@ -134,4 +134,17 @@ __device__ __forceinline__ float norm_apply(float x, float inv, float g) {
     return __fmul_rn(__fmul_rn(x, inv), g);
 }
 
+// Order-preserving bits of a float for packed (value, ~index) argmax keys;
+// NaN maps to -inf.
+__device__ __forceinline__ uint32_t ordered_bits(float v) {
+    if (v != v) v = -INFINITY;
+    const uint32_t u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Index of a packed argmax key (the all-ones key marks a NaN at index 0).
+__device__ __forceinline__ int key_index(unsigned long long k) {
+    return (k == ~0ull) ? 0 : (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+}
+
 }  // namespace at

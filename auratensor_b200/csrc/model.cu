@@ -23,6 +23,7 @@
 #include <cooperative_groups.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -651,12 +652,6 @@ __global__ void peer_barrier_kernel(ArPeers peers, int world, int rank, int64_t 
 // (order-preserving bits of the value, ~index) into a 64-bit key with
 // atomicMax, so the result does not depend on CTA order. Keys are zeroed by
 // the embedding kernel at the start of the step.
-__device__ __forceinline__ uint32_t ordered_bits(float v) {
-    if (v != v) v = -INFINITY;
-    const uint32_t u = __float_as_uint(v);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
 __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ logits, int V, int stride,
                                                      unsigned long long* __restrict__ keys) {
     __shared__ unsigned long long sk[8];
@@ -678,10 +673,6 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* __restrict__ l
         for (int w = 1; w < 8; ++w) best = sk[w] > best ? sk[w] : best;
         atomicMax(&keys[b], best);
     }
-}
-
-__device__ __forceinline__ int key_index(unsigned long long k) {
-    return (k == ~0ull) ? 0 : (int)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
 }
 
 // Writes the argmax index of each of the B keys.
@@ -837,6 +828,15 @@ struct at_model {
     std::vector<cudaEvent_t> prof_ev;
     std::vector<int> prof_cls;
     size_t prof_used = 0;
+    // persistent decode step (batch 1, one GPU): one launch per token
+    bool use_ds = false;
+    DsParams ds{};
+    DsLayer* d_ds_layers = nullptr;
+    float *ds_qkv_part = nullptr, *ds_wo_part = nullptr, *ds_apart = nullptr;
+    unsigned *ds_tickets = nullptr, *ds_bar = nullptr;
+    int* ds_err = nullptr;
+    int* h_ds_err = nullptr;              // pinned copy, read after each launch sequence
+    unsigned long long* ds_stamps = nullptr;
     bool finalized = false;
 };
 
@@ -1144,6 +1144,9 @@ void check_peer_allreduce(at_model* m) {
         fail(AT_ERR_NCCL, "tensor-parallel all-reduce: a peer rank did not arrive within the wait limit");
 }
 
+void ds_launch(at_model* m, bool greedy);
+void ds_check(at_model* m);
+
 void run_step(at_model* m, const int* tokens, const int64_t* positions, int B, float* logits_host) {
     AT_REQUIRE(m && m->finalized, AT_ERR_STATE, "model is not finalized");
     AT_REQUIRE(B >= 1 && B <= m->B, AT_ERR_INVALID_ARG, "batch exceeds the model's max_batch");
@@ -1162,8 +1165,13 @@ void run_step(at_model* m, const int* tokens, const int64_t* positions, int B, f
     for (int b = 0; b < B; ++b) { m->h_tokens[b] = tokens[b]; m->h_pos[b] = positions[b]; }
     AT_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tokens, sizeof(int) * B, cudaMemcpyHostToDevice, c->stream));
     AT_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pos, sizeof(int64_t) * B, cudaMemcpyHostToDevice, c->stream));
-    if (!m->graph[B]) m->graph[B] = capture(m, enqueue_step, B);
-    AT_CUDA(cudaGraphLaunch(m->graph[B], c->stream));
+    if (B == 1 && m->use_ds) {
+        ds_launch(m, false);
+        AT_CUDA(cudaMemcpyAsync(m->h_ds_err, m->ds_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    } else {
+        if (!m->graph[B]) m->graph[B] = capture(m, enqueue_step, B);
+        AT_CUDA(cudaGraphLaunch(m->graph[B], c->stream));
+    }
     if (logits_host)
         AT_CUDA(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * (size_t)B * m->V, cudaMemcpyDeviceToHost,
                                 c->stream));
@@ -1171,6 +1179,7 @@ void run_step(at_model* m, const int* tokens, const int64_t* positions, int B, f
         AT_CUDA(cudaMemcpyAsync(m->h_ar_err, m->d_ar_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
     AT_CUDA(cudaStreamSynchronize(c->stream));
     check_peer_allreduce(m);
+    ds_check(m);
     for (int b = 0; b < B; ++b) m->kv_size[b] = std::max<int64_t>(m->kv_size[b], positions[b] + 1);
 }
 
@@ -1212,7 +1221,9 @@ void destroy_model(at_model* m) {
                     m->att_part, m->attn_cnt, m->kcache, m->vcache, m->rope_cos, m->rope_sin, m->scratch, m->counters,
                     m->d_tokens, m->d_pos, m->d_argmax, m->d_gen_out, m->d_gen_count, m->d_argkey,
                     m->d_step, m->ar_base, m->d_ar_err, m->pf_xa, m->pf_xb, m->pf_y, m->pf_qkv, m->pf_q,
-                    m->pf_att, m->pf_g, m->pf_u, m->pf_part, m->pf_tok, m->pf_pos, m->pf_err, m->pf_xbf, m->pf_ws};
+                    m->pf_att, m->pf_g, m->pf_u, m->pf_part, m->pf_tok, m->pf_pos, m->pf_err, m->pf_xbf, m->pf_ws,
+                    m->d_ds_layers, m->ds_qkv_part, m->ds_wo_part, m->ds_apart, m->ds_tickets, m->ds_bar,
+                    m->ds_err, m->ds_stamps};
     for (void* p : bufs)
         if (p) cudaFree(p);
     if (m->h_tokens) cudaFreeHost(m->h_tokens);
@@ -1220,7 +1231,120 @@ void destroy_model(at_model* m) {
     if (m->h_ar_err) cudaFreeHost(m->h_ar_err);
     if (m->h_pf_tok) cudaFreeHost(m->h_pf_tok);
     if (m->h_pf_pos) cudaFreeHost(m->h_pf_pos);
+    if (m->h_ds_err) cudaFreeHost(m->h_ds_err);
     delete m;
+}
+
+// Persistent decode step (opt-in with AT_DECODE_STEP=1 at load): batch 1 on
+// one GPU when every matrix (token embedding and lm_head included) shares one
+// quantized type the kernel supports. Measured slower than the per-kernel
+// step graph on B200 (Llama-3-8B Q4_0: 3.23 against 1.97 ms per token), so
+// the graph stays the default.
+void setup_decode_step(at_model* m) {
+    at_ctx* c = m->ctx;
+    const char* env = std::getenv("AT_DECODE_STEP");
+    if (!env || env[0] != '1') return;
+    if (c->world != 1 || m->layers.empty()) return;
+    const int qt = m->layers[0].qkv.type;
+    for (auto& ly : m->layers)
+        for (const at_qmat* q : {&ly.qkv, &ly.wo, &ly.w1, &ly.w3, &ly.w2})
+            if (q->type != qt || !q->tiles) return;
+    if (m->out.type != qt || !m->out.tiles || m->tok.type != qt || !m->tok.tiles) return;
+    DsParams p{};
+    p.qtype = qt;
+    p.hd = m->hd;
+    p.d = m->d;
+    p.Hl = m->Hl;
+    p.Hkvl = m->Hkvl;
+    p.Fl = m->Fl;
+    p.Vl = m->Vl;
+    p.ctx = m->ctx_len;
+    p.L = m->L;
+    p.eps = m->cfg.rms_norm_eps;
+    p.scale = (float)(1.0 / std::sqrt((double)m->hd));
+    if (!decode_step_configure(&p, c->num_sms)) return;
+    if (const char* ns = std::getenv("AT_DS_NST")) {  // ring depth override (measurement knob)
+        const int v = std::atoi(ns);
+        if (v == 2 || v == 4 || v == 8) {
+            DsParams q = p;
+            q.nst = v;
+            if (decode_step_smem(q) <= 232448 - 20 * 1024) p = q;
+        }
+    }
+    const Layer& l0 = m->layers[0];
+    if (l0.qkv.tile_bytes != p.tile_t || l0.w1.tile_bytes != p.tile_n || l0.qkv.ngroups != p.qkv.ngroups ||
+        l0.wo.ngroups != p.wo.ngroups || l0.w1.nsteps != p.gu.nsteps || l0.w2.nsteps != p.dn.nsteps ||
+        m->out.nsteps != p.head.nsteps || m->out.ngroups != p.head.ngroups)
+        return;
+    std::vector<DsLayer> tab(m->L);
+    const size_t layer_kv = (size_t)m->Hkvl * m->ctx_len * m->hd;
+    for (int L = 0; L < m->L; ++L) {
+        const Layer& ly = m->layers[L];
+        tab[L] = DsLayer{ly.qkv.tiles, ly.wo.tiles, ly.w1.tiles, ly.w3.tiles, ly.w2.tiles, ly.attn_norm, ly.ffn_norm,
+                         m->kcache + L * layer_kv, m->vcache + L * layer_kv};
+    }
+    AT_CUDA(cudaMalloc(&m->d_ds_layers, sizeof(DsLayer) * m->L));
+    AT_CUDA(cudaMemcpy(m->d_ds_layers, tab.data(), sizeof(DsLayer) * m->L, cudaMemcpyHostToDevice));
+    const int G = m->Hl / m->Hkvl;
+    alloc_zero((void**)&m->ds_qkv_part, (size_t)p.qkv.ncols * p.qkv.S * 32 * 4);
+    alloc_zero((void**)&m->ds_wo_part, (size_t)p.wo.ncols * p.wo.S * 32 * 4);
+    alloc_zero((void**)&m->ds_apart, (size_t)m->Hkvl * p.att_max_ctas * G * (m->hd + 2) * 4);
+    alloc_zero((void**)&m->ds_tickets, (size_t)(m->Hkvl + 1) * sizeof(unsigned));
+    alloc_zero((void**)&m->ds_bar, 2 * sizeof(unsigned));
+    alloc_zero((void**)&m->ds_err, sizeof(int));
+    AT_CUDA(cudaMallocHost(&m->h_ds_err, sizeof(int)));
+    *m->h_ds_err = 0;
+    p.layers = m->d_ds_layers;
+    p.tok_tiles = m->tok.tiles;
+    p.tok_map = tile_map(&m->tok);
+    p.out_tiles = m->out.tiles;
+    p.out_norm = m->out_norm;
+    p.rope_cos = m->rope_cos;
+    p.rope_sin = m->rope_sin;
+    p.tokens = m->d_tokens;
+    p.pos = m->d_pos;
+    p.res0 = m->xa;
+    p.res1 = m->xb;
+    p.ydown = m->y;
+    p.qkv_part = m->ds_qkv_part;
+    p.wo_part = m->ds_wo_part;
+    p.h = m->h;
+    p.att = m->att;
+    p.apart = m->ds_apart;
+    p.logits = m->logits;
+    p.tickets = m->ds_tickets;
+    p.bar = m->ds_bar;
+    p.err = m->ds_err;
+    p.argkey = m->d_argkey;
+    p.argmax_out = m->d_argmax;
+    p.gen_out = m->d_gen_out;
+    p.gen_count = m->d_gen_count;
+    p.greedy = 0;
+    p.stamps = nullptr;
+    m->ds = p;
+    m->use_ds = true;
+}
+
+void ds_launch(at_model* m, bool greedy) {
+    DsParams p = m->ds;
+    p.greedy = greedy ? 1 : 0;
+    p.stamps = m->ds_stamps;
+    launch_decode_step(p, m->ctx->num_sms, m->ctx->stream);
+}
+
+// After the stream has synchronized: fails the call when a bounded wait of
+// the step kernel ran out, after clearing its counters for the next launch.
+void ds_check(at_model* m) {
+    if (!m->use_ds || !*m->h_ds_err) return;
+    const int code = *m->h_ds_err;
+    *m->h_ds_err = 0;
+    cudaMemset(m->ds_err, 0, sizeof(int));
+    cudaMemset(m->ds_bar, 0, 2 * sizeof(unsigned));
+    cudaMemset(m->ds_tickets, 0, (size_t)(m->Hkvl + 1) * sizeof(unsigned));
+    cudaMemset(m->d_argkey, 0, sizeof(unsigned long long));
+    cudaDeviceSynchronize();
+    fail(AT_ERR_CUDA, std::string("decode step: a bounded wait ran out (") +
+                          (code == 1 ? "weight copy" : "grid barrier") + ")");
 }
 
 // --- GGUF ------------------------------------------------------------------
@@ -1600,6 +1724,7 @@ int at_model_finalize(at_model* m) {
         alloc_zero((void**)&m->d_gen_count, sizeof(int));
         AT_CUDA(cudaMallocHost(&m->h_tokens, 8 * sizeof(int)));
         AT_CUDA(cudaMallocHost(&m->h_pos, 8 * sizeof(int64_t)));
+        setup_decode_step(m);
         AT_CUDA(cudaDeviceSynchronize());
         m->finalized = true;
     });
@@ -1889,8 +2014,13 @@ int at_model_generate(at_model* m, int first_token, int64_t start_pos, int n_ste
         AT_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tokens, sizeof(int), cudaMemcpyHostToDevice, c->stream));
         AT_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pos, sizeof(int64_t), cudaMemcpyHostToDevice, c->stream));
         AT_CUDA(cudaMemsetAsync(m->d_gen_count, 0, sizeof(int), c->stream));
-        if (!m->graph_gen) m->graph_gen = capture(m, enqueue_generate_step, 1);
-        for (int i = 0; i < n_steps; ++i) AT_CUDA(cudaGraphLaunch(m->graph_gen, c->stream));
+        if (m->use_ds) {
+            for (int i = 0; i < n_steps; ++i) ds_launch(m, true);
+            AT_CUDA(cudaMemcpyAsync(m->h_ds_err, m->ds_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+        } else {
+            if (!m->graph_gen) m->graph_gen = capture(m, enqueue_generate_step, 1);
+            for (int i = 0; i < n_steps; ++i) AT_CUDA(cudaGraphLaunch(m->graph_gen, c->stream));
+        }
         m->kv_size[0] = std::max<int64_t>(m->kv_size[0], start_pos + n_steps);
         if (c->world > 1)
             AT_CUDA(cudaMemcpyAsync(m->h_ar_err, m->d_ar_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
@@ -1899,6 +2029,7 @@ int at_model_generate(at_model* m, int first_token, int64_t start_pos, int n_ste
                                     c->stream));
             AT_CUDA(cudaStreamSynchronize(c->stream));
             check_peer_allreduce(m);
+            ds_check(m);
         }
     });
 }
@@ -1961,6 +2092,44 @@ int at_model_argmax(at_model* m, int batch, int* tokens_host) {
         AT_REQUIRE(batch >= 1 && batch <= m->B, AT_ERR_INVALID_ARG, "batch out of range");
         AT_CUDA(cudaMemcpyAsync(tokens_host, m->d_argmax, sizeof(int) * batch, cudaMemcpyDeviceToHost, m->ctx->stream));
         AT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    });
+}
+
+int at_model_step_kernel(const at_model* m, int* persistent) {
+    return guard([&] {
+        AT_REQUIRE(m && persistent, AT_ERR_INVALID_ARG, "null argument");
+        AT_REQUIRE(m->finalized, AT_ERR_STATE, "model is not finalized");
+        *persistent = m->use_ds ? 1 : 0;
+    });
+}
+
+int at_model_step_stamps(at_model* m, int token, int64_t position, unsigned long long* stamps_host, int64_t n,
+                         int* n_ctas) {
+    return guard([&] {
+        AT_REQUIRE(m && stamps_host && n_ctas, AT_ERR_INVALID_ARG, "null argument");
+        AT_REQUIRE(m->finalized, AT_ERR_STATE, "model is not finalized");
+        AT_REQUIRE(m->use_ds, AT_ERR_STATE, "the model does not use the persistent step kernel");
+        AT_REQUIRE(token >= 0 && token < m->V, AT_ERR_INVALID_ARG, "token id out of range");
+        AT_REQUIRE(position >= 0 && position < m->ctx_len, AT_ERR_STATE, "position exceeds maxContext");
+        at_ctx* c = m->ctx;
+        const int64_t need = (int64_t)c->num_sms * (5 * m->L + 1) * 4;
+        AT_REQUIRE(n >= need, AT_ERR_INVALID_ARG, "stamp buffer needs " + std::to_string(need) + " values");
+        AT_CUDA(cudaSetDevice(c->device));
+        if (!m->ds_stamps) alloc_zero((void**)&m->ds_stamps, (size_t)need * sizeof(unsigned long long));
+        m->h_tokens[0] = token;
+        m->h_pos[0] = position;
+        AT_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tokens, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+        AT_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pos, sizeof(int64_t), cudaMemcpyHostToDevice, c->stream));
+        ds_launch(m, false);
+        AT_CUDA(cudaMemcpyAsync(m->h_ds_err, m->ds_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+        AT_CUDA(cudaMemcpyAsync(stamps_host, m->ds_stamps, (size_t)need * sizeof(unsigned long long),
+                                cudaMemcpyDeviceToHost, c->stream));
+        AT_CUDA(cudaStreamSynchronize(c->stream));
+        cudaFree(m->ds_stamps);  // later steps run without stamps
+        m->ds_stamps = nullptr;
+        ds_check(m);
+        m->kv_size[0] = std::max<int64_t>(m->kv_size[0], position + 1);
+        *n_ctas = c->num_sms;
     });
 }
 

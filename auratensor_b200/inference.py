@@ -230,6 +230,24 @@ class LlamaModel:
         call("at_ctx_stream", self._ctx, C.byref(p))
         return p.value or 0
 
+    def persistentStep(self) -> bool:
+        """True when batch-1 steps run as the one-launch persistent kernel."""
+        v = C.c_int()
+        call("at_model_step_kernel", self._h, C.byref(v))
+        return bool(v.value)
+
+    def stepStamps(self, tokenId: int, position: int) -> np.ndarray:
+        """One persistent-kernel step with per-job %globaltimer stamps:
+        [n_ctas][5 * layers + 1][4] nanoseconds (job start, activations staged,
+        units done, job end)."""
+        jobs = 5 * self.config.blockCount + 1
+        n = 1024 * jobs * 4
+        buf = np.zeros(n, dtype=np.uint64)
+        nc = C.c_int()
+        call("at_model_step_stamps", self._h, int(tokenId), int(position), buf.ctypes.data_as(C.c_void_p), n,
+             C.byref(nc))
+        return buf[: nc.value * jobs * 4].reshape(nc.value, jobs, 4)
+
     def argmax(self, batch: int = 1) -> np.ndarray:
         out = np.empty(batch, dtype=np.int32)
         call("at_model_argmax", self._h, batch, out.ctypes.data_as(C.c_void_p))

@@ -191,6 +191,21 @@ int at_model_logits_device(at_model* m, float** logits_dev);
 /* Greedy token of each of the last step's `batch` rows (Sampler greedy path,
  * inference/Sampler.java:56-67: first index of the maximum). */
 int at_model_argmax(at_model* m, int batch, int* tokens_host);
+/* Which implementation serves batch-1 forwardStep and the greedy loop:
+ * *persistent = 1 for the one-launch persistent step kernel (every layer,
+ * the lm_head and the argmax in one kernel, one CTA per SM; chosen at load
+ * when the environment sets AT_DECODE_STEP=1), 0 for the per-kernel step
+ * graph (the default). Diagnostics; no counterpart in the reference. */
+int at_model_step_kernel(const at_model* m, int* persistent);
+/* One batch-1 step of the persistent step kernel with a %globaltimer stamp
+ * at four points of every job on every CTA (start, activations staged,
+ * units done, end): stamps_host receives [n_ctas][5 * layers + 1][4]
+ * nanosecond values (jobs per layer: QKV, attention, wo, gate/up, down; then
+ * the lm_head); *n_ctas is set. n is the
+ * capacity of stamps_host in values. Diagnostics; no counterpart in the
+ * reference. Fails (AT_ERR_STATE) when the model does not use that kernel. */
+int at_model_step_stamps(at_model* m, int token, int64_t position, unsigned long long* stamps_host, int64_t n,
+                         int* n_ctas);
 /* Greedy decode loop resident on the device (the decode loop of the
  * reference's TokenThroughputBenchmark.decodeLoop, benchmarks/TokenThroughputBenchmark.java:147-158:
  * forwardStep then greedy Sampler.sample, repeated): n_steps steps of slot 0,

@@ -6,6 +6,7 @@ greedy tokens are identical except where the reference's top-2 gap is below
 that tolerance.
 """
 import dataclasses
+import os
 
 import numpy as np
 import pytest
@@ -170,8 +171,14 @@ def test_profile_step_counts(cuda):
     assert r["qkv"][1] == L and r["attn"][1] == L and r["wo"][1] == L
     assert r["ffn_up"][1] == L and r["ffn_down"][1] == L and r["lm_head"][1] == 1
     assert r["comm"][1] == 0 and all(v[0] >= 0 for v in r.values())
-    # the profiled eager step computes the same logits as the graph step
-    m2 = LlamaModel(LlamaConfig.fromShape(shape), synth.generate_numpy(shape, seed=14))
+    # the profiled eager step computes the same logits as the per-kernel step
+    # graph (the persistent step kernel sums in another order)
+    os.environ["AT_DECODE_STEP"] = "0"
+    try:
+        m2 = LlamaModel(LlamaConfig.fromShape(shape), synth.generate_numpy(shape, seed=14))
+    finally:
+        del os.environ["AT_DECODE_STEP"]
+    assert not m2.persistentStep()
     lg = m2.forwardStep(3, 0).copy()
     assert np.array_equal(m.logitsDevice()[0].cpu().numpy(), lg)
 
