@@ -23,7 +23,9 @@ AT_ERR_NCCL = -6
 AT_ERR_OOM = -7
 AT_ERR_TIMEOUT = -8
 
-GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0 = 0, 1, 2, 8
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_Q6_K = 0, 1, 2, 8, 14
+# byte layouts of a model's tensors (include/auratensor.h AT_LAYOUT_*)
+LAYOUT_REFERENCE, LAYOUT_Q4_SPLIT_HALVES, LAYOUT_ATTN_OUT_IN, LAYOUT_LLAMA_CPP = 0, 1, 2, 3
 ORIENT_N, ORIENT_T = 0, 1
 PROF_CLASSES = ["embed", "qkv", "attn", "wo", "ffn_up", "ffn_down", "lm_head", "argmax", "comm"]
 
@@ -60,7 +62,7 @@ class ModelConfig(C.Structure):
     _fields_ = [("context_length", C.c_int64), ("embedding_length", C.c_int64), ("block_count", C.c_int64),
                 ("head_count", C.c_int64), ("head_count_kv", C.c_int64), ("feed_forward_length", C.c_int64),
                 ("vocab_size", C.c_int64), ("rope_freq_base", C.c_float), ("rms_norm_eps", C.c_float),
-                ("max_batch", C.c_int32), ("reserved", C.c_int32)]
+                ("max_batch", C.c_int32), ("layout", C.c_int32)]
 
 
 _vp, _i, _i64, _sz, _f = C.c_void_p, C.c_int, C.c_int64, C.c_size_t, C.c_float
@@ -83,9 +85,11 @@ SIGNATURES = {
     "at_fp16_to_f32": [_vp, _vp, _vp, _i64],
     "at_q4_0_dequant": [_vp, _vp, _vp, _i64],
     "at_q8_0_dequant": [_vp, _vp, _vp, _i64],
+    "at_q6_k_dequant": [_vp, _vp, _vp, _i64],
     "at_q4_0_dot": [_vp, _vp, _vp, _i64, _vp],
     "at_q8_0_dot": [_vp, _vp, _vp, _i64, _vp],
     "at_qmat_create": [_vp, _i, _i, _i64, _i64, _vp, _i, _PP],
+    "at_qmat_create_ex": [_vp, _i, _i, _i, _i64, _i64, _vp, _i, _PP],
     "at_qmat_destroy": [_vp],
     "at_qmat_export": [_vp, _vp, _vp],
     "at_gemv": [_vp, _vp, _vp, _vp, _i],
@@ -101,6 +105,7 @@ SIGNATURES = {
     "at_model_set_tensor": [_vp, C.c_char_p, _i, _vp, _sz, _i],
     "at_model_finalize": [_vp],
     "at_model_load_gguf": [_vp, C.c_char_p, _i, _PP],
+    "at_model_load_gguf_ex": [_vp, C.c_char_p, _i, _i, _PP],
     "at_model_get_config": [_vp, C.POINTER(ModelConfig)],
     "at_model_destroy": [_vp],
     "at_model_forward_step": [_vp, _i, _i64, _vp],

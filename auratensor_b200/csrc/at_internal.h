@@ -94,6 +94,13 @@ namespace at {
 constexpr int QK = 32;
 inline int quant_bytes(int type) { return type == AT_GGML_Q4_0 ? 16 : 32; }
 inline int block_bytes(int type) { return type == AT_GGML_Q4_0 ? 18 : 34; }
+// Bytes of n elements of raw GGUF blocks (Q4_0, Q8_0, Q6_K), -1 for other types.
+inline int64_t raw_bytes(int type, int64_t n) {
+    if (type == AT_GGML_Q4_0) return n / 32 * 18;
+    if (type == AT_GGML_Q8_0) return n / 32 * 34;
+    if (type == AT_GGML_Q6_K) return n / 256 * 210;
+    return -1;
+}
 
 // Byte offsets of the scale and of the quant bytes of block (row, b) (b in
 // units of 32-element blocks) inside the tiles of a matrix.
@@ -128,11 +135,24 @@ void qmat_fill_from_blocks(at_qmat* m, const uint8_t* src_dev, int64_t src_cols,
                            cudaStream_t s);
 // Copies rows [src_r0, +n_rows) x cols [src_c0, +n_cols) of a raw row-major
 // block matrix with src_cols columns into `m` at (dst_r0, dst_c0).
+// nib_split: the source Q4_0 blocks hold llama.cpp's split-halves nibble
+// order (element k low, k + 16 high nibble of byte k); they are stored in the
+// interleaved order (a lossless permutation inside each block).
 void qmat_fill_region(at_qmat* m, const uint8_t* src_dev, int64_t src_cols, int64_t src_r0, int64_t src_c0,
-                      int64_t n_rows, int64_t n_cols, int64_t dst_r0, int64_t dst_c0, cudaStream_t s);
+                      int64_t n_rows, int64_t n_cols, int64_t dst_r0, int64_t dst_c0, cudaStream_t s,
+                      int nib_split = 0);
 // F32 / F16 source into an f32 matrix.
 void qmat_fill_from_float(at_qmat* m, const void* src_dev, int src_type, int64_t src_cols, int64_t r0,
                           int64_t c0, cudaStream_t s);
+
+// Q6_K matrices (q6k.cu): orientation N, whole blocks padded to 224 bytes.
+void q6k_alloc(at_qmat* m);
+void q6k_fill_rows(at_qmat* m, const uint8_t* src_dev, int64_t src_cols, int64_t src_r0, int64_t n_rows,
+                   int64_t dst_r0, cudaStream_t s);
+void q6k_export(const at_qmat* m, uint8_t* dst_dev, cudaStream_t s);
+void launch_q6k_dequant(const uint8_t* src_dev, float* dst_dev, int64_t n, cudaStream_t s);
+void launch_q6k_embed(const at_qmat* tok, const int* tokens, int B, int d, float* xa, float* y,
+                      unsigned long long* argkeys, unsigned* step, cudaStream_t s);
 
 // Prologue/epilogue variants of the fused GEMV kernels.
 enum class Pro { Plain, AddNorm };         // x from global, or x = norm(xin + yin) (F7 residual)
@@ -173,6 +193,8 @@ void launch_gemv_t(const at_qmat* m, int batch, Pro pro, Epi epi, const GemvArgs
 // figure covers every epilogue.
 void gemv_t_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* floats, size_t* counters);
 void gemv_n_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* floats, size_t* counters);
+// Q6_K orientation-N GEMV (q6k.cu): Pro::Plain or Pro::AddNorm, Epi::Plain.
+void launch_gemv_q6k(const at_qmat* m, int batch, Pro pro, const GemvArgs& a, int num_sms, cudaStream_t s);
 // Tensor-core prompt GEMM (gemm_tc.cu): y[t][:] = W x[t][:], bf16 operands,
 // FP32 sums; xbf is a 128-byte aligned device buffer of at least T x in bf16
 // (the activations are converted into it); ws (FP32, may be null) holds the

@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(1024) qdot_kernel(const uint8_t* __restrict__ 
 // ---------------------------------------------------------------------------
 __global__ void repack_kernel(const uint8_t* __restrict__ src, int bb /*18|34*/, int qb /*16|32*/,
                               int64_t src_nb, int64_t r0, int64_t cb0, int64_t n_rows, int64_t n_cb,
-                              int64_t dr0, int64_t dcb0, QTileMap map, uint8_t* __restrict__ tiles) {
+                              int64_t dr0, int64_t dcb0, QTileMap map, uint8_t* __restrict__ tiles, int nib_split) {
     const int64_t total = n_rows * n_cb;
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = t / n_cb, b = t - (t / n_cb) * n_cb;
@@ -92,7 +92,19 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, int bb /*18|34*/,
         tiles[d_off] = s[0];
         tiles[d_off + 1] = s[1];
         uint8_t* q = tiles + q_off;
-        for (int k = 0; k < qb; ++k) q[k] = s[2 + k];
+        if (nib_split) {
+            // llama.cpp order in: element e is the low nibble of byte e (e < 16)
+            // or the high nibble of byte e - 16; interleaved out: byte k holds
+            // elements 2k (low) and 2k + 1 (high)
+            for (int k = 0; k < 16; ++k) {
+                const int e0 = 2 * k, e1 = 2 * k + 1;
+                const uint32_t q0 = (e0 < 16) ? (s[2 + e0] & 0xFu) : (s[2 + e0 - 16] >> 4);
+                const uint32_t q1 = (e1 < 16) ? (s[2 + e1] & 0xFu) : (s[2 + e1 - 16] >> 4);
+                q[k] = (uint8_t)(q0 | (q1 << 4));
+            }
+        } else {
+            for (int k = 0; k < qb; ++k) q[k] = s[2 + k];
+        }
     }
 }
 
@@ -122,6 +134,10 @@ __global__ void float_slice_kernel(const void* __restrict__ src, int src_type, i
 }
 
 void qmat_alloc(at_qmat* m) {
+    if (m->type == AT_GGML_Q6_K) {
+        q6k_alloc(m);
+        return;
+    }
     if (m->type == AT_GGML_F32 || m->type == AT_GGML_F16) {
         m->type = AT_GGML_F32;
         AT_CUDA(cudaMalloc(&m->f32, (size_t)(m->rows * m->cols) * 4));
@@ -155,7 +171,12 @@ void qmat_free(at_qmat* m) {
 }
 
 void qmat_fill_region(at_qmat* m, const uint8_t* src_dev, int64_t src_cols, int64_t src_r0, int64_t src_c0,
-                      int64_t n_rows, int64_t n_cols, int64_t dst_r0, int64_t dst_c0, cudaStream_t s) {
+                      int64_t n_rows, int64_t n_cols, int64_t dst_r0, int64_t dst_c0, cudaStream_t s, int nib_split) {
+    if (m->type == AT_GGML_Q6_K) {
+        AT_REQUIRE(src_c0 == 0 && dst_c0 == 0 && n_cols == m->cols, AT_ERR_INVALID_ARG, "Q6_K rows are copied whole");
+        q6k_fill_rows(m, src_dev, src_cols, src_r0, n_rows, dst_r0, s);
+        return;
+    }
     AT_REQUIRE(src_cols % QK == 0 && src_c0 % QK == 0 && n_cols % QK == 0 && dst_c0 % QK == 0, AT_ERR_INVALID_ARG,
                "block-matrix regions must be aligned to 32 columns");
     AT_REQUIRE(dst_r0 + n_rows <= m->rows && dst_c0 + n_cols <= m->cols, AT_ERR_INVALID_ARG,
@@ -164,7 +185,8 @@ void qmat_fill_region(at_qmat* m, const uint8_t* src_dev, int64_t src_cols, int6
     const int64_t n_cb = n_cols / QK;
     repack_kernel<<<grid_for(n_rows * n_cb), TPB, 0, s>>>(src_dev, block_bytes(m->type), quant_bytes(m->type),
                                                           src_cols / QK, src_r0, src_c0 / QK, n_rows, n_cb, dst_r0,
-                                                          dst_c0 / QK, tile_map(m), m->tiles);
+                                                          dst_c0 / QK, tile_map(m), m->tiles,
+                                                          (nib_split && m->type == AT_GGML_Q4_0) ? 1 : 0);
     AT_CUDA(cudaGetLastError());
 }
 
@@ -420,6 +442,15 @@ int at_q8_0_dequant(at_ctx* ctx, const void* src, float* dst, int64_t n) {
     });
 }
 
+int at_q6_k_dequant(at_ctx* ctx, const void* src, float* dst, int64_t n) {
+    return guard([&] {
+        AT_REQUIRE(ctx, AT_ERR_INVALID_ARG, "null context");
+        AT_REQUIRE(n >= 0 && n % 256 == 0, AT_ERR_INVALID_ARG, "element count must be a multiple of 256");
+        AT_REQUIRE(n == 0 || (src && dst), AT_ERR_INVALID_ARG, "null buffer");
+        if (!n) return;
+        launch_q6k_dequant((const uint8_t*)src, dst, n, ctx->stream);
+    });
+}
 int at_q4_0_dot(at_ctx* ctx, const void* q4, const float* x, int64_t n, float* out) {
     return guard([&] {
         check_blocks(ctx, q4, out, n);
@@ -440,12 +471,17 @@ int at_q8_0_dot(at_ctx* ctx, const void* q8, const float* x, int64_t n, float* o
 
 int at_qmat_create(at_ctx* ctx, int type, int orient, int64_t rows, int64_t cols, const void* blocks,
                    int on_device, at_qmat** out) {
+    return at_qmat_create_ex(ctx, type, orient, 0, rows, cols, blocks, on_device, out);
+}
+int at_qmat_create_ex(at_ctx* ctx, int type, int orient, int layout, int64_t rows, int64_t cols, const void* blocks,
+                      int on_device, at_qmat** out) {
     at_qmat* m = nullptr;
     void* staging = nullptr;
     const int rc = guard([&] {
         AT_REQUIRE(ctx && out && blocks, AT_ERR_INVALID_ARG, "null argument");
         AT_REQUIRE(rows > 0 && cols > 0, AT_ERR_INVALID_ARG, "dims must be positive");
         AT_REQUIRE(orient == AT_ORIENT_N || orient == AT_ORIENT_T, AT_ERR_INVALID_ARG, "bad orientation");
+        AT_REQUIRE((layout & ~AT_LAYOUT_LLAMA_CPP) == 0, AT_ERR_INVALID_ARG, "unknown layout bits");
         AT_CUDA(cudaSetDevice(ctx->device));
         m = new at_qmat();
         m->ctx = ctx;
@@ -458,7 +494,7 @@ int at_qmat_create(at_ctx* ctx, int type, int orient, int64_t rows, int64_t cols
         size_t bytes;
         if (src_type == AT_GGML_F32) bytes = (size_t)(rows * cols) * 4;
         else if (src_type == AT_GGML_F16) bytes = (size_t)(rows * cols) * 2;
-        else bytes = (size_t)(rows * (cols / QK)) * block_bytes(type);
+        else bytes = (size_t)(rows * raw_bytes(type, cols));
         const void* src = blocks;
         if (!on_device) {
             AT_CUDA(cudaMalloc(&staging, bytes));
@@ -466,7 +502,8 @@ int at_qmat_create(at_ctx* ctx, int type, int orient, int64_t rows, int64_t cols
             src = staging;
         }
         if (m->type == AT_GGML_F32) qmat_fill_from_float(m, src, src_type, cols, 0, 0, ctx->stream);
-        else qmat_fill_from_blocks(m, (const uint8_t*)src, cols, 0, 0, ctx->stream);
+        else qmat_fill_region(m, (const uint8_t*)src, cols, 0, 0, rows, cols, 0, 0, ctx->stream,
+                              layout & AT_LAYOUT_Q4_SPLIT_HALVES);
         AT_CUDA(cudaStreamSynchronize(ctx->stream));
         *out = m;
     });
@@ -492,6 +529,10 @@ int at_qmat_export(at_ctx* ctx, const at_qmat* m, void* dst) {
         if (m->type == AT_GGML_F32) {
             AT_CUDA(cudaMemcpyAsync(dst, m->f32, (size_t)(m->rows * m->cols) * 4, cudaMemcpyDeviceToDevice,
                                     ctx->stream));
+            return;
+        }
+        if (m->type == AT_GGML_Q6_K) {
+            q6k_export(m, (uint8_t*)dst, ctx->stream);
             return;
         }
         const int64_t nb = m->cols / QK;

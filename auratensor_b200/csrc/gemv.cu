@@ -1732,6 +1732,11 @@ void gemv_t_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* float
 }
 
 void gemv_n_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* floats, size_t* counters) {
+    if (m->type == AT_GGML_Q6_K) {  // one warp per row: no split
+        *floats = 0;
+        *counters = 0;
+        return;
+    }
     // upper bound over the epilogues (gate/up pairs carry two partials per row)
     if (batch > 2) {
         const NQLayout l = nq_layout(m, batch, num_sms, 2);
@@ -1749,6 +1754,11 @@ void launch_gemv_n(const at_qmat* m, int batch, Pro pro, Epi epi, const GemvArgs
                    cudaStream_t s, bool pdl) {
     AT_REQUIRE(m->cols % QK == 0, AT_ERR_INVALID_ARG, "cols must be a multiple of 32");
     AT_REQUIRE(m->orient == AT_ORIENT_N, AT_ERR_INVALID_ARG, "matrix is not stored for orientation N");
+    if (m->type == AT_GGML_Q6_K) {
+        AT_REQUIRE(epi == Epi::Plain, AT_ERR_UNSUPPORTED, "Q6_K matrices take the plain epilogue only");
+        launch_gemv_q6k(m, batch, pro, a, num_sms, s);
+        return;
+    }
     if (pro == Pro::Plain && epi == Epi::Plain) dispatch_q<Pro::Plain, Epi::Plain, false>(m, batch, a, num_sms, s, pdl);
     else if (pro == Pro::AddNorm && epi == Epi::Plain) dispatch_q<Pro::AddNorm, Epi::Plain, false>(m, batch, a, num_sms, s, pdl);
     else if (pro == Pro::AddNorm && epi == Epi::SiluMul) {

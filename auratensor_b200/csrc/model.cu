@@ -739,6 +739,41 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const float* __restric
 }
 
 // h = silu(g) * u elementwise (in place in g).
+// RoPE and the KV-cache append for B batch rows of a plain QKV output
+// [B][qcols] (attention weights stored [out][in], computed by the
+// orientation-N GEMV): the arithmetic of the fused QKV epilogue
+// (core/Kernels.java:296-309, inference/KVCache.java:79-95), slot b at
+// position pos[b].
+__global__ void __launch_bounds__(256) qkv_rope_rows_kernel(const float* __restrict__ qkv, int qcols,
+                                                            float* __restrict__ q_out, float* __restrict__ kc,
+                                                            float* __restrict__ vc, int64_t slot_stride,
+                                                            const float* __restrict__ rcos,
+                                                            const float* __restrict__ rsin,
+                                                            const int64_t* __restrict__ pos, int hd, int nq, int nkv,
+                                                            int ctx) {
+    const int b = blockIdx.x;
+    const int64_t p = pos[b];
+    const float* row = qkv + (size_t)b * qcols;
+    for (int j = threadIdx.x; j < qcols; j += 256) {
+        const float val = row[j];
+        if (j < nq + nkv) {
+            const int dd = (j < nq ? j : j - nq) % hd;
+            const float partner = row[j ^ 1];
+            const float cs = rcos[p * hd + dd], sn = rsin[p * hd + dd];
+            const float out = ((dd & 1) == 0) ? fmaf(val, cs, __fmul_rn(partner, -sn)) : fmaf(val, cs, __fmul_rn(partner, sn));
+            if (j < nq) {
+                q_out[(size_t)b * nq + j] = out;
+            } else {
+                const int jj = j - nq, kvh = jj / hd;
+                kc[(size_t)b * slot_stride + ((size_t)kvh * ctx + p) * hd + dd] = out;
+            }
+        } else {
+            const int jj = j - nq - nkv, kvh = jj / hd, dd = jj - kvh * hd;
+            vc[(size_t)b * slot_stride + ((size_t)kvh * ctx + p) * hd + dd] = val;
+        }
+    }
+}
+
 __global__ void silu_mul_kernel(float* __restrict__ g, const float* __restrict__ u, int64_t n) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         g[i] = silu_mul(g[i], u[i]);
@@ -776,7 +811,10 @@ struct at_model {
     at_model_config cfg{};
     int d = 0, hd = 0, H = 0, Hkv = 0, F = 0, V = 0, L = 0, ctx_len = 0, B = 1;
     int Hl = 0, Hkvl = 0, Fl = 0, Vl = 0;  // per-rank shares
-    int wtype = -1;                        // type of the first quantized matrix seen
+    int wtype = -1;                        // type of the first quantized matrix seen (Q4_0 / Q8_0)
+    int layout = 0;                        // AT_LAYOUT_* bits of the tensors' bytes
+    bool attn_n = false;                   // attention weights [out][in]: orientation-N GEMVs
+    float* qkvbuf = nullptr;               // attn_n: plain QKV output [max_batch][(Hl + 2 Hkvl) hd]
     std::vector<Layer> layers;
     at_qmat tok, out;
     float* out_norm = nullptr;
@@ -980,7 +1018,9 @@ void enqueue_step(at_model* m, int B) {
     };
     {
         ProfScope p(m, AT_PROF_EMBED);
-        if (m->tok.type == AT_GGML_Q4_0)
+        if (m->tok.type == AT_GGML_Q6_K)
+            launch_q6k_embed(&m->tok, m->d_tokens, B, d, m->xa, m->y, m->d_argkey, m->d_step, s);
+        else if (m->tok.type == AT_GGML_Q4_0)
             embed_kernel<AT_GGML_Q4_0><<<B, 256, 0, s>>>(m->tok.tiles, tile_map(&m->tok), m->d_tokens, d, m->xa,
                                                           m->y, m->d_argkey, m->d_step);
         else
@@ -1005,7 +1045,18 @@ void enqueue_step(at_model* m, int B) {
             a.kv_slot_stride = m->slot_stride;
             a.head_dim = hd; a.n_q_cols = m->Hl * hd; a.n_kv_cols = m->Hkvl * hd; a.ctx_len = m->ctx_len;
             a.scratch = m->scratch; a.counters = m->counters;
-            launch_gemv_t(&ly.qkv, B, Pro::AddNorm, Epi::QkvRope, a, c->num_sms, s, m->pdl);
+            if (m->attn_n) {
+                // [out][in] attention weights: plain QKV rows, then RoPE + KV append
+                const int qcols = (m->Hl + 2 * m->Hkvl) * hd;
+                a.y = m->qkvbuf; a.y_stride = qcols;
+                launch_gemv_n(&ly.qkv, B, Pro::AddNorm, Epi::Plain, a, c->num_sms, s, m->pdl);
+                qkv_rope_rows_kernel<<<B, 256, 0, s>>>(m->qkvbuf, qcols, m->q, kc, vc, m->slot_stride, m->rope_cos,
+                                                       m->rope_sin, m->d_pos, hd, m->Hl * hd, m->Hkvl * hd,
+                                                       m->ctx_len);
+                AT_CUDA(cudaGetLastError());
+            } else {
+                launch_gemv_t(&ly.qkv, B, Pro::AddNorm, Epi::QkvRope, a, c->num_sms, s, m->pdl);
+            }
         }
         {
             ProfScope p(m, AT_PROF_ATTN);
@@ -1067,7 +1118,8 @@ void enqueue_step(at_model* m, int B) {
             GemvArgs o;
             o.x = m->att; o.x_stride = m->Hl * hd; o.y = proj_out(2 * L); o.y_stride = d;
             o.scratch = m->scratch; o.counters = m->counters;
-            launch_gemv_t(&ly.wo, B, Pro::Plain, Epi::Plain, o, c->num_sms, s, m->pdl);
+            if (m->attn_n) launch_gemv_n(&ly.wo, B, Pro::Plain, Epi::Plain, o, c->num_sms, s, m->pdl);
+            else launch_gemv_t(&ly.wo, B, Pro::Plain, Epi::Plain, o, c->num_sms, s, m->pdl);
         }
         allreduce_y(2 * L);
         {
@@ -1223,7 +1275,7 @@ void destroy_model(at_model* m) {
                     m->d_step, m->ar_base, m->d_ar_err, m->pf_xa, m->pf_xb, m->pf_y, m->pf_qkv, m->pf_q,
                     m->pf_att, m->pf_g, m->pf_u, m->pf_part, m->pf_tok, m->pf_pos, m->pf_err, m->pf_xbf, m->pf_ws,
                     m->d_ds_layers, m->ds_qkv_part, m->ds_wo_part, m->ds_apart, m->ds_tickets, m->ds_bar,
-                    m->ds_err, m->ds_stamps};
+                    m->ds_err, m->ds_stamps, m->qkvbuf};
     for (void* p : bufs)
         if (p) cudaFree(p);
     if (m->h_tokens) cudaFreeHost(m->h_tokens);
@@ -1244,7 +1296,7 @@ void setup_decode_step(at_model* m) {
     at_ctx* c = m->ctx;
     const char* env = std::getenv("AT_DECODE_STEP");
     if (!env || env[0] != '1') return;
-    if (c->world != 1 || m->layers.empty()) return;
+    if (c->world != 1 || m->layers.empty() || m->layout != 0) return;
     const int qt = m->layers[0].qkv.type;
     for (auto& ly : m->layers)
         for (const at_qmat* q : {&ly.qkv, &ly.wo, &ly.w1, &ly.w3, &ly.w2})
@@ -1469,6 +1521,9 @@ int at_model_create(at_ctx* ctx, const at_model_config* cfg, at_model** out) {
         m = new at_model();
         m->ctx = ctx;
         m->cfg = *cfg;
+        AT_REQUIRE((cfg->layout & ~AT_LAYOUT_LLAMA_CPP) == 0, AT_ERR_INVALID_ARG, "unknown layout bits");
+        m->layout = cfg->layout;
+        m->attn_n = (cfg->layout & AT_LAYOUT_ATTN_OUT_IN) != 0;
         m->B = cfg->max_batch < 1 ? 1 : cfg->max_batch;
         AT_REQUIRE(m->B <= 8, AT_ERR_INVALID_ARG, "max_batch must be in [1, 8]");
         m->d = (int)cfg->embedding_length;
@@ -1518,17 +1573,21 @@ int at_model_set_tensor(at_model* m, const char* cname, int type, const void* da
         int64_t rows = 0, cols = 0;
         if (is_norm) { rows = 1; cols = d; }
         else if (name == "token_embd.weight" || name == "output.weight") { rows = m->V; cols = d; }
+        // attention bytes are [in][out] in the reference's layout, [out][in] in llama.cpp's
         else if (is_layer && leaf == "attn_q.weight") { rows = d; cols = (int64_t)m->H * hd; }
         else if (is_layer && (leaf == "attn_k.weight" || leaf == "attn_v.weight")) { rows = d; cols = (int64_t)m->Hkv * hd; }
         else if (is_layer && leaf == "attn_output.weight") { rows = (int64_t)m->H * hd; cols = d; }
         else if (is_layer && (leaf == "ffn_gate.weight" || leaf == "ffn_up.weight")) { rows = m->F; cols = d; }
         else if (is_layer && leaf == "ffn_down.weight") { rows = d; cols = m->F; }
         else return;  // tensors the decode path does not read are ignored, as in Weights.load
+        if (m->attn_n && is_layer && leaf.rfind("attn_", 0) == 0 && leaf != "attn_norm.weight") std::swap(rows, cols);
         const int64_t numel = rows * cols;
         size_t expect;
+        const bool emb_or_out = name == "token_embd.weight" || name == "output.weight";
         if (type == AT_GGML_F32) expect = (size_t)numel * 4;
         else if (type == AT_GGML_F16) expect = (size_t)numel * 2;
-        else if (type == AT_GGML_Q4_0 || type == AT_GGML_Q8_0) expect = (size_t)(numel / 32) * block_bytes(type);
+        else if (type == AT_GGML_Q4_0 || type == AT_GGML_Q8_0) expect = (size_t)raw_bytes(type, numel);
+        else if (type == AT_GGML_Q6_K && emb_or_out && cols % 256 == 0) expect = (size_t)raw_bytes(type, numel);
         else fail(AT_ERR_UNSUPPORTED, "tensor '" + name + "' has unsupported type " + std::to_string(type));
         AT_REQUIRE(bytes == expect, AT_ERR_INVALID_ARG,
                    "tensor '" + name + "' has " + std::to_string(bytes) + " bytes, expected " + std::to_string(expect));
@@ -1547,15 +1606,18 @@ int at_model_set_tensor(at_model* m, const char* cname, int type, const void* da
             tmp.type = AT_GGML_F32; tmp.rows = 1; tmp.cols = d; tmp.f32 = *dst; tmp.owns = false;
             qmat_fill_from_float(&tmp, src, type, d, 0, 0, c->stream);
         } else {
-            AT_REQUIRE(type == AT_GGML_Q4_0 || type == AT_GGML_Q8_0, AT_ERR_UNSUPPORTED,
-                       "tensor '" + name + "': the device path keeps weight matrices in Q4_0 or Q8_0");
-            if (m->wtype < 0) m->wtype = type;
+            AT_REQUIRE(type == AT_GGML_Q4_0 || type == AT_GGML_Q8_0 || (type == AT_GGML_Q6_K && emb_or_out),
+                       AT_ERR_UNSUPPORTED,
+                       "tensor '" + name + "': the device path keeps weight matrices in Q4_0 or Q8_0 "
+                       "(Q6_K for token_embd and output)");
+            if (m->wtype < 0 && type != AT_GGML_Q6_K) m->wtype = type;
+            const int nib_split = m->layout & AT_LAYOUT_Q4_SPLIT_HALVES;
             auto place = [&](at_qmat& q, int orient, int64_t qr, int64_t qc, int64_t sr0, int64_t sc0, int64_t nr,
                              int64_t nc, int64_t dr0, int64_t dc0) {
                 make_qmat(q, type, orient, qr, qc);
                 AT_REQUIRE(q.type == type, AT_ERR_UNSUPPORTED,
                            "tensor '" + name + "' differs in type from the tensors fused with it");
-                qmat_fill_region(&q, s8, cols, sr0, sc0, nr, nc, dr0, dc0, c->stream);
+                qmat_fill_region(&q, s8, cols, sr0, sc0, nr, nc, dr0, dc0, c->stream, nib_split);
             };
             const int64_t qcols = (int64_t)(m->Hl + 2 * m->Hkvl) * hd;
             if (name == "token_embd.weight") {
@@ -1566,7 +1628,16 @@ int at_model_set_tensor(at_model* m, const char* cname, int type, const void* da
                 place(m->out, AT_ORIENT_N, m->Vl, d, v0, 0, nv, d, 0, 0);
             } else {
                 Layer& ly = m->layers[layer];
-                if (leaf == "attn_q.weight")
+                const int64_t nq = (int64_t)m->Hl * hd, nkv = (int64_t)m->Hkvl * hd;
+                if (m->attn_n && leaf == "attn_q.weight")  // [out][in]: this rank's heads are rows
+                    place(ly.qkv, AT_ORIENT_N, qcols, d, (int64_t)r * nq, 0, nq, d, 0, 0);
+                else if (m->attn_n && leaf == "attn_k.weight")
+                    place(ly.qkv, AT_ORIENT_N, qcols, d, (int64_t)r * nkv, 0, nkv, d, nq, 0);
+                else if (m->attn_n && leaf == "attn_v.weight")
+                    place(ly.qkv, AT_ORIENT_N, qcols, d, (int64_t)r * nkv, 0, nkv, d, nq + nkv, 0);
+                else if (m->attn_n && leaf == "attn_output.weight")  // its heads are input columns
+                    place(ly.wo, AT_ORIENT_N, d, nq, 0, (int64_t)r * nq, d, nq, 0, 0);
+                else if (leaf == "attn_q.weight")
                     place(ly.qkv, AT_ORIENT_T, d, qcols, 0, (int64_t)r * m->Hl * hd, d, (int64_t)m->Hl * hd, 0, 0);
                 else if (leaf == "attn_k.weight")
                     place(ly.qkv, AT_ORIENT_T, d, qcols, 0, (int64_t)r * m->Hkvl * hd, d, (int64_t)m->Hkvl * hd, 0,
@@ -1646,8 +1717,13 @@ int at_model_finalize(at_model* m) {
         make_qmat(m->out, wt, AT_ORIENT_N, m->Vl, d);
         if (!m->out_norm) alloc_zero((void**)&m->out_norm, (size_t)d * 4);
         for (auto& ly : m->layers) {
-            make_qmat(ly.qkv, wt, AT_ORIENT_T, d, qcols);
-            make_qmat(ly.wo, wt, AT_ORIENT_T, (int64_t)m->Hl * hd, d);
+            if (m->attn_n) {
+                make_qmat(ly.qkv, wt, AT_ORIENT_N, qcols, d);
+                make_qmat(ly.wo, wt, AT_ORIENT_N, d, (int64_t)m->Hl * hd);
+            } else {
+                make_qmat(ly.qkv, wt, AT_ORIENT_T, d, qcols);
+                make_qmat(ly.wo, wt, AT_ORIENT_T, (int64_t)m->Hl * hd, d);
+            }
             make_qmat(ly.w1, wt, AT_ORIENT_N, m->Fl, d);
             make_qmat(ly.w3, ly.w1.type, AT_ORIENT_N, m->Fl, d);
             make_qmat(ly.w2, wt, AT_ORIENT_N, d, m->Fl);
@@ -1700,15 +1776,13 @@ int at_model_finalize(at_model* m) {
         size_t nf = 16, nc = 16;
         for (int b = 1; b <= B; ++b) {
             size_t f1, c1;
-            gemv_t_scratch_need(&m->layers[0].qkv, b, c->num_sms, &f1, &c1);
-            nf = std::max(nf, f1); nc = std::max(nc, c1);
-            gemv_t_scratch_need(&m->layers[0].wo, b, c->num_sms, &f1, &c1);
-            nf = std::max(nf, f1); nc = std::max(nc, c1);
-            for (const at_qmat* q : {&m->layers[0].w1, &m->layers[0].w2, &m->out}) {
-                gemv_n_scratch_need(q, b, c->num_sms, &f1, &c1);
+            for (const at_qmat* q : {&m->layers[0].qkv, &m->layers[0].wo, &m->layers[0].w1, &m->layers[0].w2, &m->out}) {
+                if (q->orient == AT_ORIENT_T) gemv_t_scratch_need(q, b, c->num_sms, &f1, &c1);
+                else gemv_n_scratch_need(q, b, c->num_sms, &f1, &c1);
                 nf = std::max(nf, f1); nc = std::max(nc, c1);
             }
         }
+        if (m->attn_n) alloc_zero((void**)&m->qkvbuf, (size_t)B * qcols * 4);
         alloc_zero((void**)&m->scratch, nf * 4);
         alloc_zero((void**)&m->counters, nc * 4);
         alloc_zero((void**)&m->d_tokens, 8 * sizeof(int));
@@ -1731,6 +1805,10 @@ int at_model_finalize(at_model* m) {
 }
 
 int at_model_load_gguf(at_ctx* ctx, const char* path, int max_batch, at_model** out) {
+    return at_model_load_gguf_ex(ctx, path, max_batch, 0, out);
+}
+
+int at_model_load_gguf_ex(at_ctx* ctx, const char* path, int max_batch, int layout, at_model** out) {
     int fd = -1;
     void* map = MAP_FAILED;
     size_t len = 0;
@@ -1801,6 +1879,7 @@ int at_model_load_gguf(at_ctx* ctx, const char* path, int max_batch, at_model** 
         cfg.rms_norm_eps = (float)n_or(arch + ".attention.layer_norm_rms_epsilon", 1e-5);
         cfg.vocab_size = (int64_t)n_or(arch + ".vocab_size", n_or("tokenizer.ggml.vocab_size", 32000));
         cfg.max_batch = max_batch < 1 ? 1 : max_batch;
+        cfg.layout = layout;
         const int64_t align = (int64_t)n_or("general.alignment", 32);
         AT_REQUIRE(align > 0, AT_ERR_IO, "bad general.alignment");
         const uint64_t data_off = ((v.pos + align - 1) / align) * align;
@@ -1812,6 +1891,7 @@ int at_model_load_gguf(at_ctx* ctx, const char* path, int max_batch, at_model** 
             else if (t.type == AT_GGML_F16) bytes = t.numel * 2;
             else if (t.type == AT_GGML_Q4_0) bytes = (t.numel + 31) / 32 * 18;
             else if (t.type == AT_GGML_Q8_0) bytes = (t.numel + 31) / 32 * 34;
+            else if (t.type == AT_GGML_Q6_K) bytes = (t.numel + 255) / 256 * 210;
             else continue;  // types the decode path cannot use stay zero stand-ins (inference/Weights.java:143-149)
             AT_REQUIRE(data_off + t.off + (uint64_t)bytes <= len, AT_ERR_IO, "tensor '" + t.name + "' past end of file");
             rc2 = at_model_set_tensor(m, t.name.c_str(), t.type, static_cast<const uint8_t*>(map) + data_off + t.off,
@@ -1919,7 +1999,9 @@ void run_prompt_batched(at_model* m, const int* tokens, int n) {
         }
         AT_CUDA(cudaMemcpyAsync(m->pf_tok, m->h_pf_tok, sizeof(int) * T, cudaMemcpyHostToDevice, s));
         AT_CUDA(cudaMemcpyAsync(m->pf_pos, m->h_pf_pos, sizeof(int64_t) * T, cudaMemcpyHostToDevice, s));
-        if (m->tok.type == AT_GGML_Q4_0)
+        if (m->tok.type == AT_GGML_Q6_K)
+            launch_q6k_embed(&m->tok, m->pf_tok, T, d, m->pf_xa, m->pf_y, nullptr, nullptr, s);
+        else if (m->tok.type == AT_GGML_Q4_0)
             embed_kernel<AT_GGML_Q4_0><<<T, 256, 0, s>>>(m->tok.tiles, tile_map(&m->tok), m->pf_tok, d, m->pf_xa,
                                                           m->pf_y, nullptr, nullptr);
         else

@@ -27,7 +27,7 @@ TENSOR_TYPES = {
     7: (24, "Q5_1"), 8: (34, "Q8_0"), 9: (36, "Q8_1"), 10: (84, "Q2_K"), 11: (110, "Q3_K"),
     12: (148, "Q4_K"), 13: (180, "Q5_K"), 14: (210, "Q6_K"), 15: (260, "Q8_K"),
 }
-F32, F16, Q4_0, Q8_0 = 0, 1, 2, 8
+F32, F16, Q4_0, Q8_0, Q6_K = 0, 1, 2, 8, 14
 
 # format/GgufMetadataValueType.java:11-23
 U8, I8, U16, I16, U32, I32, F32V, BOOL, STR, ARR, U64, I64, F64 = range(13)

@@ -63,10 +63,10 @@ class LlamaConfig:
         return cls("llama", s.ctx, s.dim, s.n_layers, s.n_heads, s.n_kv_heads, s.ffn, float(s.rope_theta),
                    float(s.eps), s.vocab)
 
-    def to_c(self, max_batch: int = 1) -> ModelConfig:
+    def to_c(self, max_batch: int = 1, layout: int = 0) -> ModelConfig:
         return ModelConfig(self.contextLength, self.embeddingLength, self.blockCount, self.headCount,
                            self.headCountKv, self.feedForwardLength, self.vocabSize, self.ropeFrequencyBase,
-                           self.rmsNormEpsilon, max_batch, 0)
+                           self.rmsNormEpsilon, max_batch, layout)
 
 
 class KVCache:
@@ -131,13 +131,15 @@ class LlamaModel:
     """
 
     def __init__(self, config: LlamaConfig, tensors: dict | None = None, max_batch: int = 1, ctx=None,
-                 world: int = 1):
+                 world: int = 1, layout: int = 0):
+        """layout: byte layout of the tensors (_lib.LAYOUT_*; 0 is the
+        reference's, _lib.LAYOUT_LLAMA_CPP reads llama.cpp exports)."""
         self.config = config
         self.max_batch = max_batch
         self.world = world
         self._ctx = ctx if ctx is not None else context()
         self._h = C.c_void_p()
-        cfg = config.to_c(max_batch)
+        cfg = config.to_c(max_batch, layout)
         call("at_model_create", self._ctx, C.byref(cfg), C.byref(self._h))
         self._logits = _host_logits(max_batch, config.vocabSize)
         if tensors is not None:
@@ -146,7 +148,7 @@ class LlamaModel:
             self.finalize()
 
     @classmethod
-    def fromGguf(cls, path: str, max_batch: int = 1) -> "LlamaModel":
+    def fromGguf(cls, path: str, max_batch: int = 1, layout: int = 0) -> "LlamaModel":
         with GgufFile.open(path) as g:
             cfg = LlamaConfig.fromGguf(g.metadata)
         self = cls.__new__(cls)
@@ -155,7 +157,7 @@ class LlamaModel:
         self.world = 1
         self._ctx = context()
         self._h = C.c_void_p()
-        call("at_model_load_gguf", self._ctx, path.encode(), max_batch, C.byref(self._h))
+        call("at_model_load_gguf_ex", self._ctx, path.encode(), max_batch, int(layout), C.byref(self._h))
         self._logits = _host_logits(max_batch, cfg.vocabSize)
         return self
 

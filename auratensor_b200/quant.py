@@ -14,7 +14,7 @@ import ctypes as C
 import torch
 
 from . import _lib
-from ._lib import GGML_Q4_0, GGML_Q8_0, ORIENT_N, ORIENT_T, IllegalArgumentException, call
+from ._lib import GGML_Q4_0, GGML_Q6_K, GGML_Q8_0, ORIENT_N, ORIENT_T, IllegalArgumentException, call
 from .core import context, ptr
 
 BLOCK_SIZE = 32
@@ -30,7 +30,13 @@ class QuantBlock:
             return 34
         if ggml_type == GGML_Q4_0:
             return 18
+        if ggml_type == GGML_Q6_K:
+            return 210
         raise IllegalArgumentException(_lib.AT_ERR_INVALID_ARG, f"Not a block-quantized type: {ggml_type}")
+
+    @staticmethod
+    def elementsPerBlock(ggml_type: int) -> int:
+        return 256 if ggml_type == GGML_Q6_K else 32
 
 
 def _check(src: torch.Tensor, n: int, bpb: int):
@@ -72,6 +78,22 @@ class Q8_0(_Codec):
     TYPE, BPB, _DEQ, _DOT = GGML_Q8_0, 34, "at_q8_0_dequant", "at_q8_0_dot"
 
 
+class Q6_K:
+    """quant/Q6_K.java: 210-byte blocks of 256 elements, (d * scale) * (q - 32)."""
+    TYPE, BPB = GGML_Q6_K, 210
+
+    @classmethod
+    def dequantToFloat(cls, src: torch.Tensor, dst: torch.Tensor | None, numElements: int) -> torch.Tensor:
+        if not src.is_cuda or src.dtype != torch.uint8:
+            raise IllegalArgumentException(_lib.AT_ERR_INVALID_ARG, "blocks must be a uint8 CUDA tensor")
+        if numElements % 256 or src.numel() < (numElements // 256) * cls.BPB:
+            raise IllegalArgumentException(_lib.AT_ERR_INVALID_ARG, "bad Q6_K element count or buffer size")
+        if dst is None:
+            dst = torch.empty(numElements, dtype=torch.float32, device=src.device)
+        call("at_q6_k_dequant", context(src.device.index), ptr(src), ptr(dst), int(numElements))
+        return dst
+
+
 class QMatrix:
     """Raw GGUF block matrix re-laid-out on the device for the fused GEMV.
 
@@ -79,7 +101,9 @@ class QMatrix:
     orient T: y[b][c] = sum_r W[r][c] x[b][r] (weights stored [in][out]).
     """
 
-    def __init__(self, ggml_type: int, orient: int, rows: int, cols: int, blocks):
+    def __init__(self, ggml_type: int, orient: int, rows: int, cols: int, blocks, layout: int = 0):
+        """layout: _lib.LAYOUT_Q4_SPLIT_HALVES reads Q4_0 blocks in llama.cpp's
+        nibble order (stored and exported in the reference's order)."""
         self.type, self.orient, self.rows, self.cols = ggml_type, orient, int(rows), int(cols)
         self._h = C.c_void_p()
         if isinstance(blocks, torch.Tensor):
@@ -97,7 +121,8 @@ class QMatrix:
             dev = torch.cuda.current_device()
             src, on_dev = C.c_void_p(keep.ctypes.data), 0
         self.device = dev
-        call("at_qmat_create", context(dev), ggml_type, orient, self.rows, self.cols, src, on_dev, C.byref(self._h))
+        call("at_qmat_create_ex", context(dev), ggml_type, orient, int(layout), self.rows, self.cols, src, on_dev,
+             C.byref(self._h))
         del keep
 
     @property
@@ -129,7 +154,8 @@ class QMatrix:
 
     def export_blocks(self) -> torch.Tensor:
         bpb = QuantBlock.bytesPerBlock(self.type)
-        out = torch.empty(self.rows * (self.cols // 32) * bpb, dtype=torch.uint8, device=f"cuda:{self.device}")
+        per = QuantBlock.elementsPerBlock(self.type)
+        out = torch.empty(self.rows * (self.cols // per) * bpb, dtype=torch.uint8, device=f"cuda:{self.device}")
         call("at_qmat_export", context(self.device), self._h, ptr(out))
         return out
 
@@ -145,4 +171,4 @@ class QMatrix:
             pass
 
 
-__all__ = ["QuantBlock", "Q4_0", "Q8_0", "QMatrix", "ORIENT_N", "ORIENT_T"]
+__all__ = ["QuantBlock", "Q4_0", "Q8_0", "Q6_K", "QMatrix", "ORIENT_N", "ORIENT_T"]

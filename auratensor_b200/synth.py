@@ -7,7 +7,14 @@ Q4_0 quantization (one block of 32 values x): m = the value of largest
 magnitude (first one on ties), d = m / -8, q = clamp(rint(x / d) + 8, 0, 15),
 d stored as IEEE fp16 (round to nearest even), nibbles packed in the
 reference's INTERLEAVED order: byte k = q[2k] | q[2k+1] << 4
-(quant/Q4_0.java:21-22). Q8_0: d = max|x| / 127, q = rint(x / d).
+(quant/Q4_0.java:21-22), or in llama.cpp's split-halves order (byte k =
+q[k] | q[k+16] << 4) for llama.cpp-layout models. Q8_0: d = max|x| / 127,
+q = rint(x / d). Q6_K (token_embd / output of llama.cpp-layout models): per
+256-element block, scale_j = max|x| / 31 of each 16-element sub-block,
+d = max_j scale_j / 16 (fp16; a normal number for these weights, which
+Fp16.toFloat's flush-to-zero needs), int8 sc_j = rint(scale_j / d),
+q = clamp(rint(x / (d sc_j)) + 32, 0, 63), packed as quant/Q6_K.java reads it.
+A llama.cpp-layout model also stores its attention weights [out][in].
 
 ``numpy`` generation serves the tests (the oracle reads the same bytes);
 ``torch`` generation on the GPU serves large models for the benchmark, with
@@ -19,9 +26,12 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from .gguf import F16, F32, Q4_0, Q8_0, GgufWriter, U32, F32V, STR
+from .gguf import F16, F32, Q4_0, Q6_K, Q8_0, GgufWriter, U32, F32V, STR
 
 QK = 32
+QK_K = 256
+LAYOUT_Q4_SPLIT_HALVES, LAYOUT_ATTN_OUT_IN = 1, 2
+LAYOUT_LLAMA_CPP = LAYOUT_Q4_SPLIT_HALVES | LAYOUT_ATTN_OUT_IN
 
 
 @dataclass(frozen=True)
@@ -38,6 +48,8 @@ class ModelShape:
     wtype: int = Q4_0
     tied: bool = False
     eps: float = 1e-5
+    layout: int = 0          # byte layout of the tensors (LAYOUT_*)
+    emb_type: int = -1       # type of token_embd / output (-1: wtype)
 
     @property
     def head_dim(self) -> int:
@@ -47,14 +59,20 @@ class ModelShape:
         """Logical dims (outer to inner) per tensor, in the reference's
         interpretation (inference/Weights.java:84-112)."""
         d, f, hd = self.dim, self.ffn, self.head_dim
-        out = [("token_embd.weight", (self.vocab, d), self.wtype)]
+        et = self.wtype if self.emb_type < 0 else self.emb_type
+        oi = bool(self.layout & LAYOUT_ATTN_OUT_IN)  # attention bytes [out][in] (llama.cpp)
+
+        def att(din, dout):
+            return (dout, din) if oi else (din, dout)
+
+        out = [("token_embd.weight", (self.vocab, d), et)]
         for L in range(self.n_layers):
             p = f"blk.{L}."
             out += [
-                (p + "attn_q.weight", (d, self.n_heads * hd), self.wtype),
-                (p + "attn_k.weight", (d, self.n_kv_heads * hd), self.wtype),
-                (p + "attn_v.weight", (d, self.n_kv_heads * hd), self.wtype),
-                (p + "attn_output.weight", (self.n_heads * hd, d), self.wtype),
+                (p + "attn_q.weight", att(d, self.n_heads * hd), self.wtype),
+                (p + "attn_k.weight", att(d, self.n_kv_heads * hd), self.wtype),
+                (p + "attn_v.weight", att(d, self.n_kv_heads * hd), self.wtype),
+                (p + "attn_output.weight", att(self.n_heads * hd, d), self.wtype),
                 (p + "ffn_gate.weight", (f, d), self.wtype),
                 (p + "ffn_up.weight", (f, d), self.wtype),
                 (p + "ffn_down.weight", (d, f), self.wtype),
@@ -62,14 +80,14 @@ class ModelShape:
                 (p + "ffn_norm.weight", (d,), F32),
             ]
         out.append(("output_norm.weight", (d,), F32))
-        out.append(("output.weight", (self.vocab, d), self.wtype))
+        out.append(("output.weight", (self.vocab, d), et))
         return out
 
     def weight_bytes(self) -> int:
         tot = 0
         for name, dims, t in self.tensor_dims():
             n = int(np.prod(dims))
-            tot += n * 4 if t == F32 else (n // QK) * (18 if t == Q4_0 else 34)
+            tot += n * 4 if t == F32 else ((n // QK_K) * 210 if t == Q6_K else (n // QK) * (18 if t == Q4_0 else 34))
         return tot
 
     def metadata(self):
@@ -95,12 +113,15 @@ LLAMA3_70B = ModelShape("llama-3-70b", 80, 8192, 28672, 64, 8, 128256, 500000.0,
 # Small shapes for parity tests.
 TINY = ModelShape("tiny", 2, 256, 512, 4, 2, 1000, 10000.0, 64, Q4_0)
 TINY_Q8 = ModelShape("tiny-q8", 2, 256, 512, 4, 2, 1000, 1e6, 64, Q8_0)
+# llama.cpp-layout small model: split-halves Q4_0 nibbles, [out][in] attention, Q6_K embedding and output
+TINY_LLAMACPP = ModelShape("tiny-llamacpp", 2, 256, 512, 4, 2, 1000, 10000.0, 64, Q4_0,
+                           layout=LAYOUT_LLAMA_CPP, emb_type=Q6_K)
 
 
 # --------------------------------------------------------------------------
 # numpy quantizers
 # --------------------------------------------------------------------------
-def quantize_q4_0(x: np.ndarray) -> np.ndarray:
+def quantize_q4_0(x: np.ndarray, split: bool = False) -> np.ndarray:
     xb = np.asarray(x, dtype=np.float32).reshape(-1, QK)
     nb = xb.shape[0]
     idx = np.argmax(np.abs(xb), axis=1)
@@ -112,7 +133,42 @@ def quantize_q4_0(x: np.ndarray) -> np.ndarray:
     q = np.clip(q, 0, 15).astype(np.uint8)
     out = np.empty((nb, 18), dtype=np.uint8)
     out[:, 0:2] = d.astype(np.float16).view(np.uint8).reshape(nb, 2)
-    out[:, 2:] = q[:, 0::2] | (q[:, 1::2] << 4)
+    out[:, 2:] = (q[:, :16] | (q[:, 16:] << 4)) if split else (q[:, 0::2] | (q[:, 1::2] << 4))
+    return out.reshape(-1)
+
+
+def _fp16_ftz(d16: np.ndarray) -> np.ndarray:
+    """fp16 -> float32 with subnormals flushed (Fp16.toFloat)."""
+    f = d16.astype(np.float32)
+    return np.where((d16.view(np.uint16) & 0x7C00) == 0, np.float32(0.0), f).astype(np.float32)
+
+
+def quantize_q6_k(x: np.ndarray) -> np.ndarray:
+    xb = np.asarray(x, dtype=np.float32).reshape(-1, QK_K)
+    nb = xb.shape[0]
+    sub = xb.reshape(nb, 16, 16)
+    sreal = np.abs(sub).max(axis=2) / np.float32(31.0)
+    # d = max scale / 16 (int8 scales up to 16) keeps d a normal fp16 for
+    # N(0, 0.02) weights: Fp16.toFloat flushes subnormal scales to zero
+    d16 = (sreal.max(axis=1) / np.float32(16.0)).astype(np.float16)
+    d = _fp16_ftz(d16)
+    safe = np.where(d == 0, np.float32(1.0), d)
+    sc = np.where(d[:, None] == 0, 0, np.clip(np.rint(sreal / safe[:, None]), -128, 127)).astype(np.int8)
+    eff = (d[:, None] * sc.astype(np.float32)).astype(np.float32)
+    effs = np.where(eff == 0, np.float32(1.0), eff)
+    q = np.where(eff[:, :, None] == 0, 32, np.clip(np.rint(sub / effs[:, :, None]) + 32, 0, 63))
+    q = q.astype(np.int32).reshape(nb, 2, 4, 32)  # [half n][group j][l]
+    ql = np.empty((nb, 2, 64), dtype=np.uint8)
+    for jj in range(2):
+        ql[:, :, 32 * jj:32 * jj + 32] = ((q[:, :, jj, :] & 0xF) | ((q[:, :, jj + 2, :] & 0xF) << 4)).astype(np.uint8)
+    qh = np.zeros((nb, 2, 32), dtype=np.int32)
+    for j in range(4):
+        qh |= ((q[:, :, j, :] >> 4) & 3) << (2 * j)
+    out = np.empty((nb, 210), dtype=np.uint8)
+    out[:, :128] = ql.reshape(nb, 128)
+    out[:, 128:192] = qh.astype(np.uint8).reshape(nb, 64)
+    out[:, 192:208] = sc.view(np.uint8)
+    out[:, 208:210] = d16.view(np.uint8).reshape(nb, 2)
     return out.reshape(-1)
 
 
@@ -130,11 +186,13 @@ def quantize_q8_0(x: np.ndarray) -> np.ndarray:
     return out.reshape(-1)
 
 
-def quantize(x: np.ndarray, wtype: int) -> np.ndarray:
+def quantize(x: np.ndarray, wtype: int, layout: int = 0) -> np.ndarray:
     if wtype == Q4_0:
-        return quantize_q4_0(x)
+        return quantize_q4_0(x, split=bool(layout & LAYOUT_Q4_SPLIT_HALVES))
     if wtype == Q8_0:
         return quantize_q8_0(x)
+    if wtype == Q6_K:
+        return quantize_q6_k(x)
     if wtype == F32:
         return np.asarray(x, dtype=np.float32).view(np.uint8).reshape(-1)
     if wtype == F16:
@@ -157,7 +215,7 @@ def generate_numpy(shape: ModelShape, seed: int, std: float = 0.02) -> dict:
             step = 1 << 24
             for s in range(0, n, step):
                 c = min(step, n - s)
-                chunks.append(quantize((rng.standard_normal(c, dtype=np.float32) * np.float32(std)), t))
+                chunks.append(quantize((rng.standard_normal(c, dtype=np.float32) * np.float32(std)), t, shape.layout))
             data = np.concatenate(chunks)
         tensors[name] = {"type": t, "dims": dims, "data": data}
     return tensors
@@ -180,8 +238,38 @@ def write_gguf(shape: ModelShape, tensors: dict, path: str) -> None:
 # --------------------------------------------------------------------------
 # torch (GPU) quantizers: same arithmetic, for multi-GB models
 # --------------------------------------------------------------------------
-def quantize_torch(x, wtype: int):
+def quantize_q6_k_torch(x):
+    """quantize_q6_k on the device (same arithmetic)."""
     import torch
+    xb = x.reshape(-1, QK_K).float()
+    nb = xb.shape[0]
+    sub = xb.reshape(nb, 16, 16)
+    sreal = sub.abs().amax(dim=2) / 31.0
+    d16 = (sreal.amax(dim=1) / 16.0).to(torch.float16)
+    d = torch.where((d16.view(torch.int16) & 0x7C00) == 0, torch.zeros_like(d16, dtype=torch.float32), d16.float())
+    safe = torch.where(d == 0, torch.ones_like(d), d)
+    sc = torch.where((d == 0)[:, None], torch.zeros_like(sreal), torch.round(sreal / safe[:, None]).clamp_(-128, 127))
+    eff = d[:, None] * sc
+    effs = torch.where(eff == 0, torch.ones_like(eff), eff)
+    q = torch.where((eff == 0)[:, :, None], torch.full_like(sub, 32.0),
+                    (torch.round(sub / effs[:, :, None]) + 32).clamp_(0, 63))
+    q = q.to(torch.int32).reshape(nb, 2, 4, 32)
+    out = torch.empty((nb, 210), dtype=torch.uint8, device=x.device)
+    ql = torch.cat([(q[:, :, jj, :] & 0xF) | ((q[:, :, jj + 2, :] & 0xF) << 4) for jj in range(2)], dim=2)
+    qh = torch.zeros((nb, 2, 32), dtype=torch.int32, device=x.device)
+    for j in range(4):
+        qh |= ((q[:, :, j, :] >> 4) & 3) << (2 * j)
+    out[:, :128] = ql.reshape(nb, 128).to(torch.uint8)
+    out[:, 128:192] = qh.reshape(nb, 64).to(torch.uint8)
+    out[:, 192:208] = sc.to(torch.int8).view(torch.uint8)
+    out[:, 208:210] = d16.view(torch.uint8).view(nb, 2)
+    return out.reshape(-1)
+
+
+def quantize_torch(x, wtype: int, layout: int = 0):
+    import torch
+    if wtype == Q6_K:
+        return quantize_q6_k_torch(x)
     xb = x.reshape(-1, QK).float()
     nb = xb.shape[0]
     if wtype == Q4_0:
@@ -193,7 +281,10 @@ def quantize_torch(x, wtype: int):
         q = torch.where((d == 0)[:, None], torch.full_like(q, 8), q).clamp_(0, 15).to(torch.uint8)
         out = torch.empty((nb, 18), dtype=torch.uint8, device=x.device)
         out[:, 0:2] = d.to(torch.float16).view(torch.uint8).view(nb, 2)
-        out[:, 2:] = q[:, 0::2] | (q[:, 1::2] << 4)
+        if layout & LAYOUT_Q4_SPLIT_HALVES:
+            out[:, 2:] = q[:, :16] | (q[:, 16:] << 4)
+        else:
+            out[:, 2:] = q[:, 0::2] | (q[:, 1::2] << 4)
     elif wtype == Q8_0:
         amax = xb.abs().amax(dim=1)
         d = amax / 127.0
@@ -208,17 +299,17 @@ def quantize_torch(x, wtype: int):
     return out.reshape(-1)
 
 
-def generate_torch_tensor(dims, wtype: int, gen, device, std: float = 0.02):
+def generate_torch_tensor(dims, wtype: int, gen, device, std: float = 0.02, layout: int = 0):
     """One quantized tensor generated on the device, chunked to bound memory."""
     import torch
     n = int(np.prod(dims))
     if wtype == F32:
         return torch.ones(n, dtype=torch.float32, device=device).view(torch.uint8)
-    bpb = 18 if wtype == Q4_0 else 34
-    out = torch.empty((n // QK) * bpb, dtype=torch.uint8, device=device)
+    per, bpb = (QK_K, 210) if wtype == Q6_K else (QK, 18 if wtype == Q4_0 else 34)
+    out = torch.empty((n // per) * bpb, dtype=torch.uint8, device=device)
     step = 1 << 26
     for s in range(0, n, step):
         c = min(step, n - s)
         x = torch.randn(c, generator=gen, device=device, dtype=torch.float32) * std
-        out[(s // QK) * bpb:((s + c) // QK) * bpb] = quantize_torch(x, wtype)
+        out[(s // per) * bpb:((s + c) // per) * bpb] = quantize_torch(x, wtype, layout)
     return out

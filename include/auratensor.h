@@ -33,11 +33,26 @@ extern "C" {
 #define AT_ERR_OOM           -7  /* device allocation failed                                            */
 #define AT_ERR_TIMEOUT       -8  /* a bounded wait ran out                                              */
 
-/* GGUF tensor type codes (format/GgufTensorType.java:15-27). */
+/* GGUF tensor type codes (format/GgufTensorType.java:15-27). Q6_K (256
+ * elements per 210-byte block, quant/Q6_K.java) is taken for token_embd and
+ * output only, as real llama.cpp exports store them. */
 #define AT_GGML_F32   0
 #define AT_GGML_F16   1
 #define AT_GGML_Q4_0  2
 #define AT_GGML_Q8_0  8
+#define AT_GGML_Q6_K 14
+
+/* Byte layouts of a model's tensors. 0 is the reference's: Q4_0 nibbles
+ * interleaved (element 2k = low nibble of byte k, quant/Q4_0.java:21-22) and
+ * attention weights read as [in][out] (inference/LlamaModel.java:326-369).
+ * llama.cpp exports use split-halves Q4_0 nibbles (element k = low nibble,
+ * element k + 16 = high nibble of byte k) and [out][in] attention weights
+ * like every other matrix. Split-halves blocks are re-ordered to the
+ * interleaved order at upload (a lossless nibble permutation inside each
+ * block); [out][in] attention weights run through the orientation-N GEMV. */
+#define AT_LAYOUT_Q4_SPLIT_HALVES 1
+#define AT_LAYOUT_ATTN_OUT_IN     2
+#define AT_LAYOUT_LLAMA_CPP       (AT_LAYOUT_Q4_SPLIT_HALVES | AT_LAYOUT_ATTN_OUT_IN)
 
 /* GEMV orientations of a row-major block matrix W[rows][cols] whose
  * quantization blocks run along cols (inference/LlamaModel.java:326-369).
@@ -81,6 +96,9 @@ int at_fp16_to_f32(at_ctx* ctx, const uint16_t* src_dev, float* dst_dev, int64_t
 int at_q4_0_dequant(at_ctx* ctx, const void* src_dev, float* dst_dev, int64_t n);
 /* Q8_0.dequantToFloat (quant/Q8_0.java:32-44). */
 int at_q8_0_dequant(at_ctx* ctx, const void* src_dev, float* dst_dev, int64_t n);
+/* Q6_K.dequantToFloat (quant/Q6_K.java:54-102): x = d * scale[i / 16] * (q - 32),
+ * d fp16 with flush-to-zero, 256 elements per 210-byte block; n % 256 == 0. */
+int at_q6_k_dequant(at_ctx* ctx, const void* src_dev, float* dst_dev, int64_t n);
 /* Q4_0.dot (quant/Q4_0.java:51-90) with dequantToFloat semantics over all 32
  * elements of every block; result written to *out_dev. */
 int at_q4_0_dot(at_ctx* ctx, const void* q4_dev, const float* x_dev, int64_t n, float* out_dev);
@@ -96,6 +114,13 @@ int at_q8_0_dot(at_ctx* ctx, const void* q8_dev, const float* x_dev, int64_t n, 
  * and the transposes of LlamaModel (inference/LlamaModel.java:326-369).  */
 int at_qmat_create(at_ctx* ctx, int ggml_type, int orient, int64_t rows, int64_t cols,
                    const void* blocks, int blocks_on_device, at_qmat** out);
+/* at_qmat_create for blocks in another byte layout: layout
+ * AT_LAYOUT_Q4_SPLIT_HALVES reads Q4_0 blocks in llama.cpp's nibble order
+ * (stored, and exported, in the interleaved order); AT_GGML_Q6_K matrices
+ * take orientation N. No counterpart in the reference (which reads the
+ * interleaved order only and dequantizes Q6_K at load). */
+int at_qmat_create_ex(at_ctx* ctx, int ggml_type, int orient, int layout, int64_t rows, int64_t cols,
+                      const void* blocks, int blocks_on_device, at_qmat** out);
 int at_qmat_destroy(at_qmat* m);
 /* Writes the matrix back as raw GGUF blocks (row-major) to dst_dev. */
 int at_qmat_export(at_ctx* ctx, const at_qmat* m, void* dst_dev);
@@ -156,7 +181,7 @@ typedef struct at_model_config {
     float   rope_freq_base;
     float   rms_norm_eps;
     int32_t max_batch;            /* independent sequences (KV slots), 1..8 */
-    int32_t reserved;
+    int32_t layout;               /* AT_LAYOUT_* bits of the tensors' bytes (0: the reference's) */
 } at_model_config;
 
 /* new LlamaModel(cfg, weights, tok) (inference/LlamaModel.java:79-129) without
@@ -175,6 +200,10 @@ int at_model_finalize(at_model* m);
  * inference/LlamaConfig.java:30-53, inference/Weights.java:83-115): mmap, parse,
  * upload raw blocks once. */
 int at_model_load_gguf(at_ctx* ctx, const char* path, int max_batch, at_model** out);
+/* at_model_load_gguf for files in another byte layout (AT_LAYOUT_*; for
+ * example AT_LAYOUT_LLAMA_CPP for llama.cpp exports). No counterpart in the
+ * reference. */
+int at_model_load_gguf_ex(at_ctx* ctx, const char* path, int max_batch, int layout, at_model** out);
 int at_model_get_config(const at_model* m, at_model_config* out);
 int at_model_destroy(at_model* m);
 /* LlamaModel.forwardStep(tokenId, position) (inference/LlamaModel.java:141-158):

@@ -17,7 +17,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 class RdCfg(C.Structure):
     _fields_ = [("dim", C.c_int), ("ffn", C.c_int), ("n_heads", C.c_int), ("n_kv", C.c_int), ("vocab", C.c_int),
-                ("ctx", C.c_int), ("n_layers", C.c_int), ("rope_base", C.c_float), ("eps", C.c_float)]
+                ("ctx", C.c_int), ("n_layers", C.c_int), ("rope_base", C.c_float), ("eps", C.c_float),
+                ("layout", C.c_int)]
 
 
 def host_tag() -> str:
@@ -68,7 +69,7 @@ class RefDecoder:
         self.shape = shape
         self.n_layers = shape.n_layers if n_layers is None else n_layers
         cfg = RdCfg(shape.dim, shape.ffn, shape.n_heads, shape.n_kv_heads, shape.vocab, shape.ctx, self.n_layers,
-                    float(shape.rope_theta), float(shape.eps))
+                    float(shape.rope_theta), float(shape.eps), int(getattr(shape, "layout", 0)))
         self._h = lib().rd_create(C.byref(cfg), threads)
         self._keep = []
 

@@ -21,8 +21,14 @@ import numpy as np
 from .java_random import JavaRandom
 
 QK = 32                 # quant/QuantBlock.java:27 BLOCK_SIZE
-GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0 = 0, 1, 2, 8   # format/GgufTensorType.java:15-27
-BLOCK_BYTES = {GGML_Q4_0: 18, GGML_Q8_0: 34}             # quant/QuantBlock.java:34-39
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_Q6_K = 0, 1, 2, 8, 14   # format/GgufTensorType.java:15-27
+BLOCK_BYTES = {GGML_Q4_0: 18, GGML_Q8_0: 34, GGML_Q6_K: 210}           # quant/QuantBlock.java:34-39, quant/Q6_K.java:41
+QK_K = 256
+# Byte layouts: 0 = the reference's (interleaved Q4_0 nibbles, attention
+# weights read [in][out]); llama.cpp exports use split-halves nibbles (bit 0)
+# and [out][in] attention weights (bit 1). The reference reads only the first.
+LAYOUT_Q4_SPLIT_HALVES, LAYOUT_ATTN_OUT_IN = 1, 2
+LAYOUT_LLAMA_CPP = LAYOUT_Q4_SPLIT_HALVES | LAYOUT_ATTN_OUT_IN
 
 
 # --------------------------------------------------------------------------
@@ -56,6 +62,43 @@ def q4_0_dequant(blocks, n: int) -> np.ndarray:
     return (q.astype(np.float32) * d[:, None]).reshape(-1)
 
 
+def q4_0_dequant_split(blocks, n: int) -> np.ndarray:
+    """Q4_0 in llama.cpp's nibble order (not the reference's): element k of a
+    block is the low nibble of qs[k], element k + 16 its high nibble."""
+    nb = n // QK
+    raw = np.frombuffer(memoryview(blocks), dtype=np.uint8, count=nb * 18).reshape(nb, 18)
+    d = fp16_bits_to_f32(raw[:, 0].astype(np.uint16) | (raw[:, 1].astype(np.uint16) << 8))
+    qs = raw[:, 2:]
+    q = np.empty((nb, QK), dtype=np.int8)
+    q[:, :16] = (qs & 0x0F).astype(np.int8) - 8
+    q[:, 16:] = (qs >> 4).astype(np.int8) - 8
+    return (q.astype(np.float32) * d[:, None]).reshape(-1)
+
+
+def q6_k_dequant(blocks, n: int) -> np.ndarray:
+    """Q6_K.dequantToFloat (quant/Q6_K.java:54-102), the published llama.cpp
+    dequantize_row_q6_K: per 210-byte block of 256 elements, ql[128] low
+    nibbles, qh[64] high 2-bit pairs, int8 scales[16], fp16 d (flush-to-zero);
+    y[n + l + 32 j] = (d * scale[n/16 + l/16 + 2 j]) * (q - 32) for the two
+    halves n = 0, 128, l = 0..31, j = 0..3, in float."""
+    nb = n // QK_K
+    raw = np.frombuffer(memoryview(blocks), dtype=np.uint8, count=nb * 210).reshape(nb, 210)
+    d = fp16_bits_to_f32(raw[:, 208].astype(np.uint16) | (raw[:, 209].astype(np.uint16) << 8))
+    sc = raw[:, 192:208].view(np.int8).astype(np.float32)
+    y = np.empty((nb, QK_K), dtype=np.float32)
+    l = np.arange(32)
+    for half in range(2):
+        ql = raw[:, 64 * half: 64 * half + 64].astype(np.int32)
+        qh = raw[:, 128 + 32 * half: 128 + 32 * half + 32].astype(np.int32)
+        lo, hi = ql[:, l], ql[:, l + 32]
+        qs = [(lo & 0xF) | (((qh >> 0) & 3) << 4), (hi & 0xF) | (((qh >> 2) & 3) << 4),
+              ((lo >> 4) & 0xF) | (((qh >> 4) & 3) << 4), ((hi >> 4) & 0xF) | (((qh >> 6) & 3) << 4)]
+        for j in range(4):
+            s_ = sc[:, 8 * half + l // 16 + 2 * j]
+            y[:, 128 * half + 32 * j + l] = (d[:, None] * s_) * (qs[j] - 32).astype(np.float32)
+    return y.reshape(-1)
+
+
 def q8_0_dequant(blocks, n: int) -> np.ndarray:
     """Q8_0.dequantToFloat: w[32b+i] = int8(qs[i]) * d."""
     nb = n // QK
@@ -65,16 +108,18 @@ def q8_0_dequant(blocks, n: int) -> np.ndarray:
     return (q * d[:, None]).reshape(-1)
 
 
-def dequant(ggml_type: int, data, n: int) -> np.ndarray:
-    """Load-time conversion of one tensor to FP32 (inference/Weights.java:167-203)."""
+def dequant(ggml_type: int, data, n: int, layout: int = 0) -> np.ndarray:
+    """Load-time conversion of one tensor to FP32 (inference/Weights.java:167-216)."""
     if ggml_type == GGML_F32:
         return np.frombuffer(memoryview(data), dtype=np.float32, count=n).copy()
     if ggml_type == GGML_F16:
         return fp16_bits_to_f32(np.frombuffer(memoryview(data), dtype=np.uint16, count=n))
     if ggml_type == GGML_Q4_0:
-        return q4_0_dequant(data, n)
+        return q4_0_dequant_split(data, n) if layout & LAYOUT_Q4_SPLIT_HALVES else q4_0_dequant(data, n)
     if ggml_type == GGML_Q8_0:
         return q8_0_dequant(data, n)
+    if ggml_type == GGML_Q6_K:
+        return q6_k_dequant(data, n)
     raise ValueError(f"unsupported type {ggml_type}")
 
 
@@ -236,14 +281,21 @@ LAYER_TENSORS = ["attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_output
                  "attn_norm.weight", "ffn_norm.weight"]
 
 
-def load_weight(tensors: dict, name: str, dims) -> np.ndarray:
+ATTN_PROJ = ("attn_q.weight", "attn_k.weight", "attn_v.weight", "attn_output.weight")
+
+
+def load_weight(tensors: dict, name: str, dims, layout: int = 0) -> np.ndarray:
     """Weights.wrapByName (inference/Weights.java:117-203): dequant to FP32,
-    zero stand-in when the tensor is absent."""
+    zero stand-in when the tensor is absent. With [out][in] attention bytes
+    (LAYOUT_ATTN_OUT_IN) the attention matrices are transposed back to the
+    reference's [in][out] reading."""
     n = int(np.prod(dims))
     if name not in tensors:
         return np.zeros(dims, dtype=np.float32)
     t = tensors[name]
-    return dequant(t["type"], t["data"], n).reshape(dims)
+    if (layout & LAYOUT_ATTN_OUT_IN) and name.endswith(ATTN_PROJ):
+        return np.ascontiguousarray(dequant(t["type"], t["data"], n, layout).reshape(dims[::-1]).T)
+    return dequant(t["type"], t["data"], n, layout).reshape(dims)
 
 
 class LlamaModelRef:
@@ -254,17 +306,17 @@ class LlamaModelRef:
     q[k] = sum_e B[e][k] x[e]; wo: y[e] = sum_k B[k][e] a[k].
     """
 
-    def __init__(self, cfg: LlamaConfig, tensors: dict):
+    def __init__(self, cfg: LlamaConfig, tensors: dict, layout: int = 0):
         self.cfg = cfg
         c = cfg
-        self.tok_embd = load_weight(tensors, "token_embd.weight", TENSOR_DIMS["token_embd.weight"](c))
-        self.out_norm = load_weight(tensors, "output_norm.weight", TENSOR_DIMS["output_norm.weight"](c))
-        self.out_w = load_weight(tensors, "output.weight", TENSOR_DIMS["output.weight"](c))
+        self.tok_embd = load_weight(tensors, "token_embd.weight", TENSOR_DIMS["token_embd.weight"](c), layout)
+        self.out_norm = load_weight(tensors, "output_norm.weight", TENSOR_DIMS["output_norm.weight"](c), layout)
+        self.out_w = load_weight(tensors, "output.weight", TENSOR_DIMS["output.weight"](c), layout)
         self.layers = []
         for L in range(c.block_count):
             lw = {}
             for nm in LAYER_TENSORS:
-                lw[nm] = load_weight(tensors, f"blk.{L}.{nm}", TENSOR_DIMS[nm](c))
+                lw[nm] = load_weight(tensors, f"blk.{L}.{nm}", TENSOR_DIMS[nm](c), layout)
             self.layers.append(lw)
         self.kv = KVCache(c.block_count, c.head_count_kv, c.head_dim, c.context_length)
         self.cos, self.sin = rope_tables(c.head_dim, c.rope_freq_base, c.context_length)

@@ -32,6 +32,7 @@
 typedef struct {
     int dim, ffn, n_heads, n_kv, vocab, ctx, n_layers;
     float rope_base, eps;
+    int layout; /* bit 0: llama.cpp split-halves Q4_0 nibbles; bit 1: attention bytes [out][in] */
 } rd_cfg;
 
 typedef struct {
@@ -60,17 +61,51 @@ static float fp16_ftz(uint16_t h) {
     return f;
 }
 
-static void dequant(int type, const uint8_t* src, float* dst, int64_t n) {
+/* Q6_K.dequantToFloat (quant/Q6_K.java:54-102, the published llama.cpp
+ * dequantize_row_q6_K) of one 210-byte block into 256 floats. */
+static void dequant_q6_k_block(const uint8_t* p, float* y) {
+    const float d = fp16_ftz((uint16_t)(p[208] | (p[209] << 8)));
+    for (int n = 0; n < 256; n += 128) {
+        const uint8_t* ql = p + n / 2;
+        const uint8_t* qh = p + 128 + n / 4;
+        const int8_t* sc = (const int8_t*)(p + 192 + n / 16);
+        for (int l = 0; l < 32; ++l) {
+            const int is = l / 16;
+            const int q1 = ((ql[l] & 0x0F) | (((qh[l] >> 0) & 3) << 4)) - 32;
+            const int q2 = ((ql[l + 32] & 0x0F) | (((qh[l] >> 2) & 3) << 4)) - 32;
+            const int q3 = (((ql[l] >> 4) & 0x0F) | (((qh[l] >> 4) & 3) << 4)) - 32;
+            const int q4 = (((ql[l + 32] >> 4) & 0x0F) | (((qh[l] >> 6) & 3) << 4)) - 32;
+            y[n + l] = d * (float)sc[is] * (float)q1;
+            y[n + l + 32] = d * (float)sc[is + 2] * (float)q2;
+            y[n + l + 64] = d * (float)sc[is + 4] * (float)q3;
+            y[n + l + 96] = d * (float)sc[is + 6] * (float)q4;
+        }
+    }
+}
+
+/* split != 0: Q4_0 blocks in llama.cpp's nibble order (element k = low
+ * nibble of byte k, element k + 16 = its high nibble). */
+static void dequant_ex(int type, const uint8_t* src, float* dst, int64_t n, int split) {
     if (type == 0) { memcpy(dst, src, (size_t)n * 4); return; }
     if (type == 1) { for (int64_t i = 0; i < n; ++i) dst[i] = fp16_ftz((uint16_t)(src[2*i] | (src[2*i+1] << 8))); return; }
+    if (type == 14) {
+#pragma omp parallel for schedule(static)
+        for (int64_t b = 0; b < n / 256; ++b) dequant_q6_k_block(src + b * 210, dst + b * 256);
+        return;
+    }
 #pragma omp parallel for schedule(static)
     for (int64_t b = 0; b < n / 32; ++b) {
         if (type == 2) {
             const uint8_t* p = src + b * 18;
             const float d = fp16_ftz((uint16_t)(p[0] | (p[1] << 8)));
             for (int i = 0; i < 32; ++i) {
-                const int pk = p[2 + i / 2];
-                const int q = (i % 2 == 0) ? (pk & 0x0F) : ((pk >> 4) & 0x0F);
+                int q;
+                if (split) {
+                    q = (i < 16) ? (p[2 + i] & 0x0F) : ((p[2 + i - 16] >> 4) & 0x0F);
+                } else {
+                    const int pk = p[2 + i / 2];
+                    q = (i % 2 == 0) ? (pk & 0x0F) : ((pk >> 4) & 0x0F);
+                }
                 dst[b * 32 + i] = (float)(q - 8) * d;
             }
         } else {
@@ -80,6 +115,9 @@ static void dequant(int type, const uint8_t* src, float* dst, int64_t n) {
         }
     }
 }
+
+static int g_split; /* split-halves order of the model being loaded (single-threaded set_tensor) */
+static void dequant(int type, const uint8_t* src, float* dst, int64_t n) { dequant_ex(type, src, dst, n, g_split); }
 
 /* One row of Kernels.sgemv: 16 lane-wise partial sums then a reduce. */
 static float sgemv_row(const float* a, const float* x, int K) {
@@ -184,6 +222,7 @@ int rd_set_tensor(rd_model* m, const char* name, int type, const void* data, int
     const rd_cfg* c = &m->c;
     const int hd = m->hd, d = c->dim;
     omp_set_num_threads(m->threads);
+    g_split = c->layout & 1;
     if (!strcmp(name, "token_embd.weight")) { m->emb_raw = (const uint8_t*)data; m->emb_type = type; return 0; }
     if (!strcmp(name, "output_norm.weight")) { dequant(type, data, m->out_norm, d); return 0; }
     if (!strcmp(name, "output.weight")) { dequant(type, data, m->out_w, numel); return 0; }
@@ -194,17 +233,22 @@ int rd_set_tensor(rd_model* m, const char* name, int type, const void* data, int
     float* tmp = falloc(numel);
     dequant(type, data, tmp, numel);
     int rc = 0;
+    const int out_in = (c->layout & 2) != 0; /* llama.cpp: attention bytes already [out][in] */
     if (!strcmp(leaf, "attn_q.weight") || !strcmp(leaf, "attn_k.weight") || !strcmp(leaf, "attn_v.weight")) {
         /* transposeAttnProj: bytes [emb][out] -> [out][emb] */
         const int out = (int)(numel / d);
         float* dst = leaf[5] == 'q' ? L->qT : (leaf[5] == 'k' ? L->kT : L->vT);
-        for (int e = 0; e < d; ++e)
-            for (int k = 0; k < out; ++k) dst[(size_t)k * d + e] = tmp[(size_t)e * out + k];
+        if (out_in) memcpy(dst, tmp, (size_t)numel * 4);
+        else
+            for (int e = 0; e < d; ++e)
+                for (int k = 0; k < out; ++k) dst[(size_t)k * d + e] = tmp[(size_t)e * out + k];
     } else if (!strcmp(leaf, "attn_output.weight")) {
         /* transposeAttnOut: bytes [H*hd][emb] -> [emb][H*hd] */
         const int tk = c->n_heads * hd;
-        for (int k = 0; k < tk; ++k)
-            for (int e = 0; e < d; ++e) L->oT[(size_t)e * tk + k] = tmp[(size_t)k * d + e];
+        if (out_in) memcpy(L->oT, tmp, (size_t)numel * 4);
+        else
+            for (int k = 0; k < tk; ++k)
+                for (int e = 0; e < d; ++e) L->oT[(size_t)e * tk + k] = tmp[(size_t)k * d + e];
     } else if (!strcmp(leaf, "ffn_gate.weight")) memcpy(L->gate, tmp, (size_t)numel * 4);
     else if (!strcmp(leaf, "ffn_up.weight")) memcpy(L->up, tmp, (size_t)numel * 4);
     else if (!strcmp(leaf, "ffn_down.weight")) memcpy(L->down, tmp, (size_t)numel * 4);
@@ -284,8 +328,10 @@ static const float* forward(rd_model* m, int token, int pos, int with_logits) {
     omp_set_num_threads(m->threads);
     double t0 = now();
     if (m->emb_raw) {
+        g_split = c->layout & 1;
         const int bpb = m->emb_type == 2 ? 18 : (m->emb_type == 8 ? 34 : 0);
-        if (bpb) dequant(m->emb_type, m->emb_raw + (size_t)token * (d / 32) * bpb, m->x, d);
+        if (m->emb_type == 14) dequant(14, m->emb_raw + (size_t)token * (d / 256) * 210, m->x, d);
+        else if (bpb) dequant(m->emb_type, m->emb_raw + (size_t)token * (d / 32) * bpb, m->x, d);
         else dequant(m->emb_type, m->emb_raw + (size_t)token * d * (m->emb_type == 0 ? 4 : 2), m->x, d);
     } else {
         memset(m->x, 0, (size_t)d * 4);

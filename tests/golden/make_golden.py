@@ -165,12 +165,58 @@ def gguf_minimal_header_hex():
     return b.hex()
 
 
+def q6_k_cases():
+    # quant/Q6_KTest.java: dequantMatchesCanonicalInnerLoop (:22-104, Random(7),
+    # d = Float.floatToFloat16(0.04f)), zeroBiasProducesAllZero (:106-131) and
+    # q0MinAndQ63MaxProducedSignExtreme (:133-181). Expected values follow the
+    # test's restatement of the canonical loop: (d * scale) * (q - 32) in float.
+    def block(ql, qh, sc, d16):
+        return bytes(ql) + bytes(qh) + bytes((v & 0xFF) for v in sc) + struct.pack("<H", d16)
+
+    def expect(blk):
+        d16 = blk[208] | (blk[209] << 8)
+        d = float(np.array([d16], dtype=np.uint16).view(np.float16)[0])
+        out = [0.0] * 256
+        for n in (0, 128):
+            for l in range(32):
+                is_ = l // 16
+                lo, hi, qh = blk[n // 2 + l], blk[n // 2 + l + 32], blk[128 + n // 4 + l]
+                s = [np.int8(np.uint8(blk[192 + n // 16 + is_ + 2 * j])) for j in range(4)]
+                q = [((lo & 0xF) | (((qh >> 0) & 3) << 4)) - 32, ((hi & 0xF) | (((qh >> 2) & 3) << 4)) - 32,
+                     (((lo >> 4) & 0xF) | (((qh >> 4) & 3) << 4)) - 32, (((hi >> 4) & 0xF) | (((qh >> 6) & 3) << 4)) - 32]
+                for j in range(4):
+                    out[n + l + 32 * j] = f32(np.float32(np.float32(d) * np.float32(s[j])) * np.float32(q[j]))
+        return out
+
+    r = JavaRandom(7)
+    d16 = int(np.array([np.float16(np.float32(0.04))]).view(np.uint16)[0])
+    sc = [r.next_int(241) - 120 for _ in range(16)]
+    ql = []
+    for _ in range(128):
+        lo = r.next_int(16)
+        hi = r.next_int(16)
+        ql.append(((hi << 4) | lo) & 0xFF)
+    qh = []
+    for _ in range(64):
+        b0, b1, b2, b3 = r.next_int(4), r.next_int(4), r.next_int(4), r.next_int(4)
+        qh.append(b0 | (b1 << 2) | (b2 << 4) | (b3 << 6))
+    canon = block(ql, qh, sc, d16)
+    zero = block([0] * 128, [0xAA] * 64, [1] * 16, 0x3C00)
+    qmax = block([0xFF] * 128, [0xFF] * 64, [1] * 16, 0x3C00)
+    qmin = block([0] * 128, [0] * 64, [1] * 16, 0x3C00)
+    return [{"name": "canonical_random7", "block_hex": canon.hex(), "expect": expect(canon)},
+            {"name": "zero_bias", "block_hex": zero.hex(), "expect": [0.0] * 256},
+            {"name": "q63_max", "block_hex": qmax.hex(), "expect": [31.0] * 256},
+            {"name": "q0_min", "block_hex": qmin.hex(), "expect": [-32.0] * 256}]
+
+
 def main():
     out = {
         "source": "restated from the reference JUnit tests (src/test/java/io/auratensor)",
         "fp16": fp16_cases(),
         "q4_0_dequant": q4_dequant_case(),
         "q4_0_dot_nan": q4_dot_case(),
+        "q6_k_dequant": q6_k_cases(),
         "kernels": kernels_cases(),
         "sampler": sampler_cases(),
         "gguf_minimal_header_hex": gguf_minimal_header_hex(),

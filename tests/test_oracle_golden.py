@@ -139,15 +139,18 @@ def test_missing_output_weight_gives_zero_logits():
     assert np.all(ref.LlamaModelRef(cfg, t).forward_step(1, 0) == 0)
 
 
-def test_c_restatement_matches_numpy_oracle():
-    """The C restatement (CPU baseline) and the numpy oracle agree on a tiny model."""
+@pytest.mark.parametrize("which", ["reference_layout", "llama_cpp_layout"])
+def test_c_restatement_matches_numpy_oracle(which):
+    """The C restatement (CPU baseline) and the numpy oracle agree on a tiny
+    model, in the reference's byte layout and in llama.cpp's (split-halves
+    Q4_0, [out][in] attention, Q6_K embedding and output)."""
     from auratensor_b200 import synth
     from oracle.cref import RefDecoder
-    shape = synth.TINY
+    shape = synth.TINY if which == "reference_layout" else synth.TINY_LLAMACPP
     t = synth.generate_numpy(shape, seed=31)
     cfg = ref.LlamaConfig(shape.ctx, shape.dim, shape.n_layers, shape.n_heads, shape.n_kv_heads, shape.ffn,
                           shape.rope_theta, shape.eps, shape.vocab)
-    a = ref.LlamaModelRef(cfg, t)
+    a = ref.LlamaModelRef(cfg, t, layout=shape.layout)
     b = RefDecoder(shape, threads=2)
     for name, tt in t.items():
         b.set_tensor(name, tt["type"], tt["data"], int(np.prod(tt["dims"])))
@@ -155,3 +158,52 @@ def test_c_restatement_matches_numpy_oracle():
         la = a.forward_step(tok, pos)
         lb = b.forward_step(tok, pos)
         assert np.max(np.abs(la - lb)) <= 1e-5 * float(la.max() - la.min())
+
+
+def test_q6_k_dequant_golden(kats):
+    """The oracle's Q6_K decode against quant/Q6_KTest.java's cases."""
+    for c in kats["q6_k_dequant"]:
+        got = ref.q6_k_dequant(bytes.fromhex(c["block_hex"]), 256)
+        want = np.array(c["expect"], dtype=np.float32)
+        assert np.array_equal(got, want), c["name"]
+
+
+def test_q4_0_split_halves_order():
+    """llama.cpp's nibble order: element k = low nibble of byte k, k + 16 = high nibble."""
+    blk = bytes([0x00, 0x3C]) + bytes(((k + 1) % 16) | ((15 - k) << 4) for k in range(16))  # d = 1.0
+    w = ref.q4_0_dequant_split(blk, 32)
+    assert [int(v) + 8 for v in w[:16]] == [(k + 1) % 16 for k in range(16)]
+    assert [int(v) + 8 for v in w[16:]] == [15 - k for k in range(16)]
+
+
+def test_llama_cpp_layout_is_the_same_model():
+    """A llama.cpp-layout export of the same weights (split-halves nibbles,
+    [out][in] attention) decodes to the reference-layout model's logits."""
+    import dataclasses
+
+    from auratensor_b200 import synth
+    base = dataclasses.replace(synth.TINY, layout=synth.LAYOUT_LLAMA_CPP)
+    t = synth.generate_numpy(base, seed=32)
+    # the reference layout: interleaved nibbles, attention bytes [in][out]
+    t_ref = {}
+    for name, v in t.items():
+        dims, data, tt = v["dims"], v["data"], v["type"]
+        if tt == ref.GGML_Q4_0 and name.endswith(ref.ATTN_PROJ):
+            # [out][in] -> the reference's [in][out] reading, as exact floats
+            w = ref.q4_0_dequant_split(data, int(np.prod(dims))).reshape(dims)
+            data, dims, tt = np.ascontiguousarray(w.T).view(np.uint8).reshape(-1), dims[::-1], ref.GGML_F32
+        elif tt == ref.GGML_Q4_0:
+            # split-halves -> interleaved nibbles: the same quants and scales
+            raw = np.frombuffer(memoryview(data), dtype=np.uint8).reshape(-1, 18)
+            q = np.concatenate([raw[:, 2:] & 0xF, raw[:, 2:] >> 4], axis=1)  # elements 0..31
+            out = raw.copy()
+            out[:, 2:] = q[:, 0::2] | (q[:, 1::2] << 4)
+            data = out.reshape(-1)
+        t_ref[name] = {"type": tt, "dims": dims, "data": data}
+    cfg = ref.LlamaConfig(base.ctx, base.dim, base.n_layers, base.n_heads, base.n_kv_heads, base.ffn,
+                          base.rope_theta, base.eps, base.vocab)
+    a = ref.LlamaModelRef(cfg, t, layout=synth.LAYOUT_LLAMA_CPP)
+    b = ref.LlamaModelRef(cfg, t_ref)
+    for pos, tok in enumerate([3, 99, 500]):
+        la, lb = a.forward_step(tok, pos), b.forward_step(tok, pos)
+        assert np.max(np.abs(la - lb)) <= 1e-5 * float(lb.max() - lb.min())
