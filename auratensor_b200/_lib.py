@@ -65,6 +65,13 @@ class ModelConfig(C.Structure):
                 ("max_batch", C.c_int32), ("layout", C.c_int32)]
 
 
+class SamplerConfigC(C.Structure):
+    """at_sampler_config: Sampler.Config plus a host penalty history."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int32), ("top_p", C.c_float),
+                ("repetition_penalty", C.c_float), ("seed", C.c_int64), ("history", C.c_void_p),
+                ("history_len", C.c_int32), ("reserved", C.c_int32)]
+
+
 _vp, _i, _i64, _sz, _f = C.c_void_p, C.c_int, C.c_int64, C.c_size_t, C.c_float
 _PP = C.POINTER(C.c_void_p)
 
@@ -117,6 +124,14 @@ SIGNATURES = {
     "at_model_step_stamps": [_vp, _i, _i64, _vp, _i64, _vp],
     "at_model_generate": [_vp, _i, _i64, _i, _vp],
     "at_model_profile_step": [_vp, _i, _i64, _vp, _vp],
+    "at_model_sample": [_vp, _i, _vp, _vp],
+    "at_model_generate_sampled": [_vp, _i, _vp, _vp, _i, _vp, _vp],
+    "at_model_forward_prompt_slot": [_vp, _i, _vp, _i],
+    "at_sched_create": [_vp, _PP],
+    "at_sched_destroy": [_vp],
+    "at_sched_submit": [_vp, _vp, _i, _i, _i, _vp, C.POINTER(C.c_int)],
+    "at_sched_step": [_vp, C.POINTER(C.c_int)],
+    "at_sched_result": [_vp, _i, _vp, _i, C.POINTER(C.c_int), C.POINTER(C.c_int)],
     "at_model_kv_size": [_vp, _i, C.POINTER(C.c_int64)],
     "at_model_kv_read": [_vp, _i, _i, _i, _i64, _vp, _vp],
     "at_model_kv_reset": [_vp, _i],

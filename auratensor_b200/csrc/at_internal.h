@@ -279,6 +279,40 @@ struct DsParams {
     unsigned long long* stamps;  // optional [gridDim][5 L + 1][4] globaltimer per job
 };
 
+// Device sampler (sample.cu): Sampler.sample per logits row.
+struct SampleRow {
+    float temperature;
+    int top_k;
+    float top_p;
+    float penalty;             // repetition penalty (1: none)
+    float r;                   // the row's uniform draw in [0, 1) when rng is null
+    unsigned long long* rng;   // device: java.util.Random state advanced per call (unseeded rows), or null
+    const int* hist;           // device: penalty history (may be null)
+    const int* hist_len;       // device: its length (may be null: empty)
+    int* cnt;                  // device: [V] occurrence counts, zero between calls (needed with a penalty)
+};
+void launch_sample(float* logits_dev, int B, int V, int stride, const SampleRow* rows_dev, int* out_dev,
+                   cudaStream_t s);
+// picked -> tokens, pos + 1, seq[b][*step] (seq may be null; *step advances
+// when step is not null), and the penalty history append of the rows whose
+// append flag is set (append null: every row).
+void launch_sample_advance(const int* picked, int B, int* tokens, int64_t* pos, int* seq, int seq_stride, int* step,
+                           int* hist, int hist_stride, int* hist_len, const int* append, cudaStream_t s);
+int sample_k_max();
+
+// Model hooks of the request scheduler (sched.cpp); defined in model.cu.
+int model_max_batch(const at_model* m);
+int64_t model_ctx_len(const at_model* m);
+int model_vocab(const at_model* m);
+bool model_slot_prompt(const at_model* m);  // prompts can run into any KV slot
+// Row `slot`'s sampler settings and penalty history (cfg null: an idle greedy row).
+void sched_set_row(at_model* m, int slot, const at_sampler_config* cfg, const int* history, int n);
+void sched_step(at_model* m, int B, const int* tokens, const int64_t* positions, const int* append, int* picked);
+void sched_prompt(at_model* m, int slot, const int* tokens, int n);
+void sched_reset_slot(at_model* m, int slot);
+// The reference's r: a fresh java.util.Random(seed).nextFloat() (seed 0: an unseeded generator).
+float sampler_r(int64_t seed);
+
 // Shared memory the step kernel needs (dynamic bytes) and its launch.
 size_t decode_step_smem(const DsParams& p);
 void launch_decode_step(const DsParams& p, int num_ctas, cudaStream_t s);

@@ -22,6 +22,7 @@
 
 #include <cooperative_groups.h>
 
+#include <chrono>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -875,6 +876,21 @@ struct at_model {
     int* ds_err = nullptr;
     int* h_ds_err = nullptr;              // pinned copy, read after each launch sequence
     unsigned long long* ds_stamps = nullptr;
+    // device sampling (allocated on first use)
+    SampleRow* d_rows = nullptr;
+    SampleRow* h_rows = nullptr;          // pinned, [max_batch]
+    int* d_hist = nullptr;                // [max_batch][hist_cap] penalty histories
+    int64_t hist_cap = 0;                 // max(maxContext, 8192) ids per row
+    int* d_hist_len = nullptr;            // [max_batch]
+    int* d_pen_cnt = nullptr;             // [max_batch][V] occurrence counts, zero between calls
+    unsigned long long* d_rng = nullptr;  // [max_batch] generator states of unseeded rows
+    int* d_sampled = nullptr;             // [max_batch]
+    int* d_seq = nullptr;                 // [max_batch][ctx] sampled sequences
+    int* d_step_ctr = nullptr;
+    int* d_append = nullptr;              // [max_batch] history-append flags of a scheduler step
+    int* h_i32 = nullptr;                 // pinned staging, [max_batch]
+    unsigned long long* h_rng = nullptr;  // pinned staging, [max_batch]
+    cudaGraphExec_t graph_samp[9] = {};   // step + sample + advance, per batch
     bool finalized = false;
 };
 
@@ -1199,7 +1215,8 @@ void check_peer_allreduce(at_model* m) {
 void ds_launch(at_model* m, bool greedy);
 void ds_check(at_model* m);
 
-void run_step(at_model* m, const int* tokens, const int64_t* positions, int B, float* logits_host) {
+// Checks a step's inputs and enqueues it (copies in, the step); no wait.
+void run_step_enqueue_only(at_model* m, const int* tokens, const int64_t* positions, int B) {
     AT_REQUIRE(m && m->finalized, AT_ERR_STATE, "model is not finalized");
     AT_REQUIRE(B >= 1 && B <= m->B, AT_ERR_INVALID_ARG, "batch exceeds the model's max_batch");
     AT_REQUIRE(tokens && positions, AT_ERR_INVALID_ARG, "null tokens/positions");
@@ -1224,6 +1241,11 @@ void run_step(at_model* m, const int* tokens, const int64_t* positions, int B, f
         if (!m->graph[B]) m->graph[B] = capture(m, enqueue_step, B);
         AT_CUDA(cudaGraphLaunch(m->graph[B], c->stream));
     }
+}
+
+void run_step(at_model* m, const int* tokens, const int64_t* positions, int B, float* logits_host) {
+    run_step_enqueue_only(m, tokens, positions, B);
+    at_ctx* c = m->ctx;
     if (logits_host)
         AT_CUDA(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * (size_t)B * m->V, cudaMemcpyDeviceToHost,
                                 c->stream));
@@ -1260,6 +1282,8 @@ void destroy_model(at_model* m) {
     }
     for (auto& g : m->graph)
         if (g) cudaGraphExecDestroy(g);
+    for (auto& g : m->graph_samp)
+        if (g) cudaGraphExecDestroy(g);
     if (m->graph_gen) cudaGraphExecDestroy(m->graph_gen);
     if (m->graph_prof) cudaGraphExecDestroy(m->graph_prof);
     for (cudaEvent_t e : m->prof_ev) cudaEventDestroy(e);
@@ -1275,7 +1299,8 @@ void destroy_model(at_model* m) {
                     m->d_step, m->ar_base, m->d_ar_err, m->pf_xa, m->pf_xb, m->pf_y, m->pf_qkv, m->pf_q,
                     m->pf_att, m->pf_g, m->pf_u, m->pf_part, m->pf_tok, m->pf_pos, m->pf_err, m->pf_xbf, m->pf_ws,
                     m->d_ds_layers, m->ds_qkv_part, m->ds_wo_part, m->ds_apart, m->ds_tickets, m->ds_bar,
-                    m->ds_err, m->ds_stamps, m->qkvbuf};
+                    m->ds_err, m->ds_stamps, m->qkvbuf, m->d_rows, m->d_hist, m->d_hist_len, m->d_pen_cnt,
+                    m->d_rng, m->d_sampled, m->d_seq, m->d_step_ctr, m->d_append};
     for (void* p : bufs)
         if (p) cudaFree(p);
     if (m->h_tokens) cudaFreeHost(m->h_tokens);
@@ -1284,6 +1309,9 @@ void destroy_model(at_model* m) {
     if (m->h_pf_tok) cudaFreeHost(m->h_pf_tok);
     if (m->h_pf_pos) cudaFreeHost(m->h_pf_pos);
     if (m->h_ds_err) cudaFreeHost(m->h_ds_err);
+    if (m->h_rows) cudaFreeHost(m->h_rows);
+    if (m->h_i32) cudaFreeHost(m->h_i32);
+    if (m->h_rng) cudaFreeHost(m->h_rng);
     delete m;
 }
 
@@ -1946,7 +1974,7 @@ bool prompt_batched_ok(const at_model* m) {
     for (const auto& ly : m->layers)
         for (const at_qmat* q : {&ly.qkv, &ly.wo, &ly.w1, &ly.w3, &ly.w2})
             if (q->type != AT_GGML_Q4_0 && q->type != AT_GGML_Q8_0) return false;
-    return m->tok.type == AT_GGML_Q4_0 || m->tok.type == AT_GGML_Q8_0;
+    return m->tok.type == AT_GGML_Q4_0 || m->tok.type == AT_GGML_Q8_0 || m->tok.type == AT_GGML_Q6_K;
 }
 
 void ensure_prompt_buffers(at_model* m) {
@@ -1980,7 +2008,7 @@ void ensure_prompt_buffers(at_model* m) {
     AT_CUDA(cudaMallocHost(&m->h_pf_pos, PF_T * sizeof(int64_t)));
 }
 
-void run_prompt_batched(at_model* m, const int* tokens, int n) {
+void run_prompt_batched(at_model* m, const int* tokens, int n, int slot) {
     at_ctx* c = m->ctx;
     cudaStream_t s = c->stream;
     AT_CUDA(cudaSetDevice(c->device));
@@ -2010,8 +2038,8 @@ void run_prompt_batched(at_model* m, const int* tokens, int n) {
         AT_CUDA(cudaGetLastError());
         for (int L = 0; L < m->L; ++L) {
             Layer& ly = m->layers[L];
-            float* kc = m->kcache + L * layer_kv;  // slot 0
-            float* vc = m->vcache + L * layer_kv;
+            float* kc = m->kcache + (size_t)slot * m->slot_stride + L * layer_kv;
+            float* vc = m->vcache + (size_t)slot * m->slot_stride + L * layer_kv;
             // attention block: xb = norm(xa + y); q, k, v; RoPE + append; attention; y = wo att
             rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xa, m->pf_y, ly.attn_norm, m->pf_xb, d, eps);
             AT_CUDA(cudaGetLastError());
@@ -2051,21 +2079,25 @@ void run_prompt_batched(at_model* m, const int* tokens, int n) {
     AT_CUDA(cudaMemcpyAsync(&err, m->pf_err, sizeof(int), cudaMemcpyDeviceToHost, s));
     AT_CUDA(cudaStreamSynchronize(s));
     AT_REQUIRE(err == 0, AT_ERR_CUDA, "prompt GEMM: an mbarrier wait ran out");
-    m->kv_size[0] = std::max<int64_t>(m->kv_size[0], n);
+    m->kv_size[slot] = std::max<int64_t>(m->kv_size[slot], n);
+}
+
+void check_prompt(const at_model* m, const int* tokens, int n) {
+    AT_REQUIRE(m && (n == 0 || tokens), AT_ERR_INVALID_ARG, "null argument");
+    // LlamaModel.forwardPrompt (inference/LlamaModel.java:167-170)
+    AT_REQUIRE(n >= 0 && n < m->ctx_len, AT_ERR_INVALID_ARG,
+               "Prompt length " + std::to_string(n) + " exceeds contextLength " + std::to_string(m->ctx_len));
+    AT_REQUIRE(m->finalized, AT_ERR_STATE, "model is not finalized");
+    for (int i = 0; i < n; ++i)
+        AT_REQUIRE(tokens[i] >= 0 && tokens[i] < m->V, AT_ERR_INVALID_ARG,
+                   "token id " + std::to_string(tokens[i]) + " out of range");
 }
 
 int at_model_forward_prompt(at_model* m, const int* tokens, int n) {
     return guard([&] {
-        AT_REQUIRE(m && (n == 0 || tokens), AT_ERR_INVALID_ARG, "null argument");
-        // LlamaModel.forwardPrompt (inference/LlamaModel.java:167-170)
-        AT_REQUIRE(n >= 0 && n < m->ctx_len, AT_ERR_INVALID_ARG,
-                   "Prompt length " + std::to_string(n) + " exceeds contextLength " + std::to_string(m->ctx_len));
-        AT_REQUIRE(m->finalized, AT_ERR_STATE, "model is not finalized");
-        for (int i = 0; i < n; ++i)
-            AT_REQUIRE(tokens[i] >= 0 && tokens[i] < m->V, AT_ERR_INVALID_ARG,
-                       "token id " + std::to_string(tokens[i]) + " out of range");
+        check_prompt(m, tokens, n);
         if (n > 1 && prompt_batched_ok(m)) {
-            run_prompt_batched(m, tokens, n);
+            run_prompt_batched(m, tokens, n, 0);
             return;
         }
         for (int i = 0; i < n; ++i) {
@@ -2115,6 +2147,236 @@ int at_model_generate(at_model* m, int first_token, int64_t start_pos, int n_ste
         }
     });
 }
+
+int at_model_forward_prompt_slot(at_model* m, int slot, const int* tokens, int n) {
+    return guard([&] {
+        check_prompt(m, tokens, n);
+        AT_REQUIRE(slot >= 0 && slot < m->B, AT_ERR_INVALID_ARG, "slot out of range");
+        if (n == 0) return;
+        if (prompt_batched_ok(m) && (n > 1 || slot > 0)) {
+            run_prompt_batched(m, tokens, n, slot);
+            return;
+        }
+        // A decode step writes the KV of every slot below its batch size, so
+        // slots other than 0 need the batched prompt path.
+        AT_REQUIRE(slot == 0, AT_ERR_UNSUPPORTED,
+                   "a prompt into slot " + std::to_string(slot) + " needs the batched prompt path (one GPU, "
+                   "Q4_0/Q8_0 layer matrices, head_dim 64 or 128)");
+        for (int i = 0; i < n; ++i) {
+            const int64_t p = i;
+            run_step(m, tokens + i, &p, 1, nullptr);
+        }
+    });
+}
+
+}  // extern "C"
+
+namespace at {
+
+int64_t history_cap(const at_model* m) { return std::max<int64_t>(m->ctx_len, 8192); }
+
+void ensure_sample_buffers(at_model* m) {
+    if (m->d_rows) return;
+    const size_t B = m->B;
+    alloc_zero((void**)&m->d_rows, B * sizeof(SampleRow));
+    m->hist_cap = history_cap(m);
+    alloc_zero((void**)&m->d_hist, B * m->hist_cap * sizeof(int));
+    alloc_zero((void**)&m->d_hist_len, B * sizeof(int));
+    alloc_zero((void**)&m->d_pen_cnt, B * m->V * sizeof(int));
+    alloc_zero((void**)&m->d_rng, B * sizeof(unsigned long long));
+    alloc_zero((void**)&m->d_sampled, B * sizeof(int));
+    alloc_zero((void**)&m->d_seq, B * m->ctx_len * sizeof(int));
+    alloc_zero((void**)&m->d_step_ctr, sizeof(int));
+    alloc_zero((void**)&m->d_append, B * sizeof(int));
+    AT_CUDA(cudaMallocHost(&m->h_rows, B * sizeof(SampleRow)));
+    AT_CUDA(cudaMallocHost(&m->h_i32, B * sizeof(int)));
+    AT_CUDA(cudaMallocHost(&m->h_rng, B * sizeof(unsigned long long)));
+    for (size_t b = 0; b < B; ++b) m->h_rows[b] = SampleRow{0.f, 1, 1.f, 1.f, 0.f, nullptr, nullptr, nullptr, nullptr};
+}
+
+bool sampler_greedy(const at_sampler_config& c) {
+    return c.temperature == 0.0f || (c.top_k == 1 && c.top_p >= 1.0f);
+}
+
+// Sampler.Config checks: the reference fails on a non-positive topK
+// outside the greedy path (inference/Sampler.java:77-80); the device
+// sampler holds at most sample_k_max() candidates.
+void check_sampler_config(const at_model* m, const at_sampler_config& c, int64_t history_cap) {
+    if (!sampler_greedy(c)) {
+        AT_REQUIRE(c.top_k >= 1, AT_ERR_INVALID_ARG, "topK must be positive");
+        AT_REQUIRE(std::min(c.top_k, m->V) <= sample_k_max(), AT_ERR_UNSUPPORTED,
+                   "topK above " + std::to_string(sample_k_max()) + " is not supported by the device sampler");
+    }
+    AT_REQUIRE(c.history_len >= 0 && (c.history_len == 0 || c.history), AT_ERR_INVALID_ARG, "bad history");
+    AT_REQUIRE(c.history_len <= history_cap, AT_ERR_INVALID_ARG,
+               "history of " + std::to_string(c.history_len) + " tokens exceeds the " + std::to_string(history_cap) +
+                   " the device keeps for the row");
+}
+
+// Row b's sampler settings and penalty history (host ids, n of them) staged
+// for the next sample launch; the caller uploads h_rows.
+void set_sample_row(at_model* m, int b, const at_sampler_config& c, const int* history, int n) {
+    at_ctx* ctx = m->ctx;
+    SampleRow r{};
+    r.temperature = c.temperature;
+    r.top_k = c.top_k;
+    r.top_p = c.top_p;
+    r.penalty = c.repetition_penalty;
+    r.hist = m->d_hist + (size_t)b * m->hist_cap;
+    r.hist_len = m->d_hist_len + b;
+    r.cnt = m->d_pen_cnt + (size_t)b * m->V;
+    if (c.seed != 0) {
+        r.r = sampler_r(c.seed);
+    } else {  // an unseeded generator, advanced on the device per call
+        const uint64_t t = (uint64_t)std::chrono::steady_clock::now().time_since_epoch().count();
+        m->h_rng[b] = ((t + 0x9E3779B97F4A7C15ULL * (uint64_t)(b + 1)) ^ 0x5DEECE66DULL) & ((1ULL << 48) - 1);
+        AT_CUDA(cudaMemcpyAsync(m->d_rng + b, m->h_rng + b, sizeof(unsigned long long), cudaMemcpyHostToDevice,
+                                ctx->stream));
+        r.rng = m->d_rng + b;
+    }
+    m->h_rows[b] = r;
+    m->h_i32[b] = n;
+    if (n > 0)
+        AT_CUDA(cudaMemcpyAsync(m->d_hist + (size_t)b * m->hist_cap, history, sizeof(int) * n, cudaMemcpyHostToDevice,
+                                ctx->stream));
+    AT_CUDA(cudaMemcpyAsync(m->d_hist_len + b, m->h_i32 + b, sizeof(int), cudaMemcpyHostToDevice, ctx->stream));
+}
+
+void upload_sample_rows(at_model* m, int B) {
+    AT_CUDA(cudaMemcpyAsync(m->d_rows, m->h_rows, sizeof(SampleRow) * B, cudaMemcpyHostToDevice, m->ctx->stream));
+}
+
+void enqueue_sampled_step(at_model* m, int B) {
+    cudaStream_t s = m->ctx->stream;
+    enqueue_step(m, B);
+    launch_sample(m->logits, B, m->V, m->V, m->d_rows, m->d_sampled, s);
+    launch_sample_advance(m->d_sampled, B, m->d_tokens, m->d_pos, m->d_seq, m->ctx_len, m->d_step_ctr, m->d_hist,
+                          m->hist_cap, m->d_hist_len, nullptr, s);
+}
+
+}  // namespace at
+
+extern "C" {
+
+int at_model_sample(at_model* m, int batch, const at_sampler_config* cfgs, int* tokens_host) {
+    return guard([&] {
+        AT_REQUIRE(m && cfgs && tokens_host, AT_ERR_INVALID_ARG, "null argument");
+        AT_REQUIRE(m->finalized, AT_ERR_STATE, "model is not finalized");
+        AT_REQUIRE(batch >= 1 && batch <= m->B, AT_ERR_INVALID_ARG, "batch out of range");
+        for (int b = 0; b < batch; ++b) check_sampler_config(m, cfgs[b], history_cap(m));
+        at_ctx* c = m->ctx;
+        AT_CUDA(cudaSetDevice(c->device));
+        AT_CUDA(cudaStreamSynchronize(c->stream));  // the pinned staging buffers are free
+        ensure_sample_buffers(m);
+        for (int b = 0; b < batch; ++b) set_sample_row(m, b, cfgs[b], cfgs[b].history, cfgs[b].history_len);
+        upload_sample_rows(m, batch);
+        launch_sample(m->logits, batch, m->V, m->V, m->d_rows, m->d_sampled, c->stream);
+        AT_CUDA(cudaMemcpyAsync(tokens_host, m->d_sampled, sizeof(int) * batch, cudaMemcpyDeviceToHost, c->stream));
+        AT_CUDA(cudaStreamSynchronize(c->stream));
+    });
+}
+
+int at_model_generate_sampled(at_model* m, int batch, const int* first_tokens, const int64_t* start_pos, int n_steps,
+                              const at_sampler_config* cfgs, int* tokens_out_host) {
+    return guard([&] {
+        AT_REQUIRE(m && first_tokens && start_pos && cfgs, AT_ERR_INVALID_ARG, "null argument");
+        AT_REQUIRE(m->finalized, AT_ERR_STATE, "model is not finalized");
+        AT_REQUIRE(batch >= 1 && batch <= m->B, AT_ERR_INVALID_ARG, "batch out of range");
+        AT_REQUIRE(n_steps >= 0, AT_ERR_INVALID_ARG, "negative step count");
+        for (int b = 0; b < batch; ++b) {
+            AT_REQUIRE(first_tokens[b] >= 0 && first_tokens[b] < m->V, AT_ERR_INVALID_ARG, "token id out of range");
+            AT_REQUIRE(start_pos[b] >= 0, AT_ERR_INVALID_ARG, "negative position");
+            AT_REQUIRE(start_pos[b] + n_steps <= m->ctx_len, AT_ERR_STATE,
+                       "position " + std::to_string(start_pos[b] + n_steps - 1) + " exceeds maxContext " +
+                           std::to_string(m->ctx_len));
+            check_sampler_config(m, cfgs[b], history_cap(m) - n_steps);
+        }
+        if (n_steps == 0) return;
+        at_ctx* c = m->ctx;
+        AT_CUDA(cudaSetDevice(c->device));
+        AT_CUDA(cudaStreamSynchronize(c->stream));
+        ensure_sample_buffers(m);
+        for (int b = 0; b < batch; ++b) {
+            set_sample_row(m, b, cfgs[b], cfgs[b].history, cfgs[b].history_len);
+            m->h_tokens[b] = first_tokens[b];
+            m->h_pos[b] = start_pos[b];
+        }
+        upload_sample_rows(m, batch);
+        AT_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tokens, sizeof(int) * batch, cudaMemcpyHostToDevice, c->stream));
+        AT_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pos, sizeof(int64_t) * batch, cudaMemcpyHostToDevice, c->stream));
+        AT_CUDA(cudaMemsetAsync(m->d_step_ctr, 0, sizeof(int), c->stream));
+        if (!m->graph_samp[batch]) m->graph_samp[batch] = capture(m, enqueue_sampled_step, batch);
+        for (int i = 0; i < n_steps; ++i) AT_CUDA(cudaGraphLaunch(m->graph_samp[batch], c->stream));
+        if (c->world > 1)
+            AT_CUDA(cudaMemcpyAsync(m->h_ar_err, m->d_ar_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+        if (tokens_out_host)
+            AT_CUDA(cudaMemcpy2DAsync(tokens_out_host, sizeof(int) * n_steps, m->d_seq, sizeof(int) * m->ctx_len,
+                                      sizeof(int) * n_steps, batch, cudaMemcpyDeviceToHost, c->stream));
+        AT_CUDA(cudaStreamSynchronize(c->stream));
+        check_peer_allreduce(m);
+        for (int b = 0; b < batch; ++b) m->kv_size[b] = std::max<int64_t>(m->kv_size[b], start_pos[b] + n_steps);
+    });
+}
+
+}  // extern "C"
+
+namespace at {
+
+// Scheduler hooks (sched.cpp).
+int model_max_batch(const at_model* m) { return m->B; }
+int64_t model_ctx_len(const at_model* m) { return m->ctx_len; }
+int model_vocab(const at_model* m) { return m->V; }
+bool model_slot_prompt(const at_model* m) { return prompt_batched_ok(m); }
+
+void sched_set_row(at_model* m, int slot, const at_sampler_config* cfg, const int* history, int n) {
+    AT_REQUIRE(m->finalized, AT_ERR_STATE, "model is not finalized");
+    at_ctx* c = m->ctx;
+    AT_CUDA(cudaSetDevice(c->device));
+    AT_CUDA(cudaStreamSynchronize(c->stream));
+    ensure_sample_buffers(m);
+    if (cfg) {
+        check_sampler_config(m, *cfg, history_cap(m));
+        AT_REQUIRE(n <= history_cap(m), AT_ERR_INVALID_ARG, "history exceeds the device history buffer");
+        set_sample_row(m, slot, *cfg, history, n);
+    } else {  // an idle row: greedy, no penalty
+        m->h_rows[slot] = SampleRow{0.f, 1, 1.f, 1.f, 0.f, nullptr, nullptr, nullptr, nullptr};
+    }
+    AT_CUDA(cudaMemcpyAsync(m->d_rows + slot, m->h_rows + slot, sizeof(SampleRow), cudaMemcpyHostToDevice,
+                            c->stream));
+    AT_CUDA(cudaStreamSynchronize(c->stream));
+}
+
+// One decode step of rows 0..B-1 (tokens at positions), device sampling of
+// every row and the history append of rows with append[b] set; picked
+// receives the B sampled ids.
+void sched_step(at_model* m, int B, const int* tokens, const int64_t* positions, const int* append, int* picked) {
+    AT_REQUIRE(m->d_rows, AT_ERR_STATE, "no sampler rows were set");
+    at_ctx* c = m->ctx;
+    for (int b = 0; b < B; ++b) m->h_i32[b] = append[b] ? 1 : 0;
+    AT_CUDA(cudaMemcpyAsync(m->d_append, m->h_i32, sizeof(int) * B, cudaMemcpyHostToDevice, c->stream));
+    run_step_enqueue_only(m, tokens, positions, B);
+    launch_sample(m->logits, B, m->V, m->V, m->d_rows, m->d_sampled, c->stream);
+    launch_sample_advance(m->d_sampled, B, m->d_tokens, m->d_pos, nullptr, 0, nullptr, m->d_hist, m->hist_cap,
+                          m->d_hist_len, m->d_append, c->stream);
+    AT_CUDA(cudaMemcpyAsync(picked, m->d_sampled, sizeof(int) * B, cudaMemcpyDeviceToHost, c->stream));
+    if (c->world > 1)
+        AT_CUDA(cudaMemcpyAsync(m->h_ar_err, m->d_ar_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    AT_CUDA(cudaStreamSynchronize(c->stream));
+    check_peer_allreduce(m);
+    ds_check(m);
+    for (int b = 0; b < B; ++b) m->kv_size[b] = std::max<int64_t>(m->kv_size[b], positions[b] + 1);
+}
+
+void sched_prompt(at_model* m, int slot, const int* tokens, int n) {
+    check_prompt(m, tokens, n);
+    run_prompt_batched(m, tokens, n, slot);
+}
+
+void sched_reset_slot(at_model* m, int slot) { m->kv_size[slot] = 0; }
+
+}  // namespace at
+
+extern "C" {
 
 int at_model_profile_step(at_model* m, int token, int64_t position, float* class_ms, int* class_launches) {
     return guard([&] {

@@ -32,6 +32,14 @@ bool java_double_less(double x, double y) {
 
 }  // namespace
 
+namespace at {
+float sampler_r(int64_t seed) {
+    int64_t s = seed;
+    if (s == 0) s = (int64_t)std::chrono::steady_clock::now().time_since_epoch().count();
+    return JavaRandom(s).next_float();
+}
+}  // namespace at
+
 extern "C" int at_sample(float* logits, int vocab, const int* history, int n_history, float temperature, int top_k,
                          float top_p, float rep_penalty, int64_t seed, int* out_token) {
     return at::guard([&] {

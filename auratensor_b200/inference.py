@@ -219,6 +219,34 @@ class LlamaModel:
              out.ctypes.data_as(C.c_void_p))
         return out[:nSteps]
 
+    def forwardPromptSlot(self, slot: int, promptTokenIds) -> None:
+        """forwardPrompt into KV slot `slot` (the batched prompt path)."""
+        arr = np.ascontiguousarray(np.asarray(promptTokenIds, dtype=np.int32))
+        call("at_model_forward_prompt_slot", self._h, int(slot), arr.ctypes.data_as(C.c_void_p), int(arr.size))
+
+    def sample(self, configs, histories=None) -> np.ndarray:
+        """Sampler.sample on the device for rows 0..len(configs)-1 of the last
+        step's logits (row b with configs[b] and penalty history histories[b]);
+        the penalty is applied to the device logits in place."""
+        cfgs, keep = _sampler_array(configs, histories)
+        out = np.empty(len(configs), dtype=np.int32)
+        call("at_model_sample", self._h, len(configs), C.cast(cfgs, C.c_void_p), out.ctypes.data_as(C.c_void_p))
+        del keep
+        return out
+
+    def generateSampled(self, firstTokens, startPositions, nSteps: int, configs, histories=None) -> np.ndarray:
+        """Batched sampled decode on the device: [batch][nSteps] tokens, row b in
+        KV slot b with configs[b]; each row's history grows by its samples."""
+        t = np.ascontiguousarray(np.asarray(firstTokens, dtype=np.int32))
+        p = np.ascontiguousarray(np.asarray(startPositions, dtype=np.int64))
+        b = int(t.size)
+        cfgs, keep = _sampler_array(configs, histories)
+        out = np.empty((b, max(1, nSteps)), dtype=np.int32)
+        call("at_model_generate_sampled", self._h, b, t.ctypes.data_as(C.c_void_p), p.ctypes.data_as(C.c_void_p),
+             int(nSteps), C.cast(cfgs, C.c_void_p), out.ctypes.data_as(C.c_void_p))
+        del keep
+        return out[:, :nSteps]
+
     def profileStep(self, tokenId: int, position: int) -> dict:
         """Per-kernel-class device time (ms) and launch counts of one eager step."""
         ms = np.zeros(len(_lib.PROF_CLASSES), dtype=np.float32)
@@ -295,6 +323,21 @@ class SamplerConfig:
     @staticmethod
     def greedy() -> "SamplerConfig":
         return SamplerConfig(1.0, 1, 1.0, 1.0, 0)
+
+
+def _sampler_array(configs, histories):
+    """An at_sampler_config array; the history arrays it points to are returned to be kept alive."""
+    n = len(configs)
+    arr = (_lib.SamplerConfigC * n)()
+    keep = []
+    for b, c in enumerate(configs):
+        h = None if histories is None or histories[b] is None else np.ascontiguousarray(
+            np.asarray(histories[b], dtype=np.int32))
+        keep.append(h)
+        arr[b] = _lib.SamplerConfigC(float(c.temperature), int(c.topK), float(c.topP), float(c.repetitionPenalty),
+                                     int(c.seed), h.ctypes.data if h is not None and h.size else None,
+                                     0 if h is None else int(h.size), 0)
+    return arr, (arr, keep)
 
 
 class Sampler:

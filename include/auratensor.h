@@ -243,6 +243,60 @@ int at_model_step_stamps(at_model* m, int token, int64_t position, unsigned long
  * tokens_out_host receives the n_steps generated tokens; when it is NULL the
  * steps are only enqueued on the context's stream (the call does not wait). */
 int at_model_generate(at_model* m, int first_token, int64_t start_pos, int n_steps, int* tokens_out_host);
+
+/* ---- sampling on the device and batched requests -------------------------
+ * Sampler.Config (inference/Sampler.java:20-30) of one sequence. history is a
+ * host array of previously emitted ids for the repetition penalty. */
+typedef struct at_sampler_config {
+    float temperature;
+    int32_t top_k;
+    float top_p;
+    float repetition_penalty;
+    int64_t seed;                 /* 0: an unseeded generator, as the reference */
+    const int32_t* history;       /* host, may be NULL */
+    int32_t history_len;
+    int32_t reserved;
+} at_sampler_config;
+/* Sampler.sample (inference/Sampler.java:37-121) on the device for each of the
+ * last step's `batch` logits rows, row b with cfgs[b]: the same repetition
+ * penalty (applied to the device logits in place, as the reference mutates
+ * its array), greedy path, stable top-k/top-p and CDF scan with r drawn from
+ * a fresh java.util.Random(seed). top_k above 1024 (outside the greedy path)
+ * is refused with AT_ERR_UNSUPPORTED; use at_sample on host logits then. */
+int at_model_sample(at_model* m, int batch, const at_sampler_config* cfgs, int* tokens_host);
+/* Batched sampled decoding on the device: `batch` sequences (KV slots
+ * 0..batch-1), slot b starting from first_tokens[b] at start_pos[b]; each of
+ * n_steps steps runs the step graph, samples every row with cfgs[b] and feeds
+ * the tokens back without a host round trip (each step's tokens are appended
+ * to the row's penalty history). tokens_out_host: [batch][n_steps]. The
+ * reference samples one sequence per call (inference/Sampler.java:37,
+ * server/InferenceServer.java:112-174). */
+int at_model_generate_sampled(at_model* m, int batch, const int* first_tokens, const int64_t* start_pos, int n_steps,
+                              const at_sampler_config* cfgs, int* tokens_out_host);
+/* LlamaModel.forwardPrompt (inference/LlamaModel.java:166-175) into KV slot
+ * `slot` (the reference has one sequence per model). One GPU. */
+int at_model_forward_prompt_slot(at_model* m, int slot, const int* tokens, int n);
+
+/* Continuous batching over the model's KV slots (one GPU). Requests wait
+ * until a slot is free; at_sched_step admits waiting requests (their prompt
+ * runs into the slot), runs one batched decode step for every active request
+ * with device sampling, and retires requests that reached max_new tokens.
+ * The reference's server runs one request at a time on a shared model
+ * (server/InferenceServer.java:112-174). */
+typedef struct at_sched at_sched;
+int at_sched_create(at_model* m, at_sched** out);
+int at_sched_destroy(at_sched* s);
+/* prompt: n >= 1 ids (host; copied), n + max_new <= the model's context.
+ * Generation stops after max_new tokens or at eos_token (not emitted; < 0:
+ * none), as the server's loop (server/InferenceServer.java:124-134). The
+ * penalty history is the prompt followed by the generated tokens; cfg's own
+ * history fields are ignored. *request_id is set. */
+int at_sched_submit(at_sched* s, const int* prompt, int n, int max_new, int eos_token, const at_sampler_config* cfg,
+                    int* request_id);
+/* One scheduling step; *n_active = requests still running or waiting. */
+int at_sched_step(at_sched* s, int* n_active);
+/* Tokens generated so far for a request (up to cap) and whether it is done. */
+int at_sched_result(at_sched* s, int request_id, int* tokens_host, int cap, int* n_tokens, int* done);
 /* Per-kernel-class device time of one forward step of slot 0, run as a graph
  * with a CUDA event pair around every launch (and no programmatic overlap):
  * class_ms[AT_PROF_CLASSES] milliseconds and class_launches[AT_PROF_CLASSES]

@@ -388,6 +388,13 @@ class SamplerConfig:
     seed: int = 0
 
 
+def _double_compare_key(v: float):
+    """A sort key ordered as java.lang.Double.compare."""
+    if math.isnan(v):
+        return (2, 0.0, 0)
+    return (1, v, 0 if (v == 0.0 and math.copysign(1.0, v) < 0) else 1)
+
+
 def sample(logits: np.ndarray, history, cfg: SamplerConfig) -> int:
     """Sampler.sample: penalty, greedy fast path, stable descending sort,
     top-k, top-p on running/total >= topP, renormalise, CDF scan with
@@ -411,8 +418,10 @@ def sample(logits: np.ndarray, history, cfg: SamplerConfig) -> int:
         return best
     inv_t = f32(f32(1.0) / f32(cfg.temperature))
     adj = (logits * inv_t).astype(np.float32)
-    # stable sort by descending value; equal values keep ascending index order
-    order = sorted(range(vocab), key=lambda i: -float(adj[i]))
+    # Comparator.comparingDouble(..).reversed() under List.sort: stable,
+    # descending in Double.compare's order (NaN above +inf, -0.0 below 0.0);
+    # equal values keep ascending index order
+    order = sorted(range(vocab), key=lambda i: _double_compare_key(float(adj[i])), reverse=True)
     top_k = min(cfg.top_k, vocab)
     max_logit = adj[order[0]]
     probs = np.zeros(top_k, dtype=np.float32)

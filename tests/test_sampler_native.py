@@ -37,3 +37,25 @@ def test_repetition_penalty_mutates_in_place(built_lib):
     logits = np.array([2.0, -2.0, 1.0], dtype=np.float32)
     Sampler.sample(logits, [0, 1], SamplerConfig(1.0, 1, 1.0, 2.0, 3))
     assert logits.tolist() == [1.0, -4.0, 1.0]
+
+
+@pytest.mark.parametrize("seed", [3, 4, 5])
+def test_sampler_special_values_match_oracle(seed, built_lib):
+    """NaN (above +inf in Double.compare), infinities, signed zeros and exact
+    ties, with a negative penalty flipping signs per occurrence."""
+    rng = np.random.default_rng(seed)
+    logits = np.round(rng.standard_normal(3000) * 2).astype(np.float32)
+    idx = rng.choice(3000, size=12, replace=False)
+    logits[idx[:3]] = np.nan
+    logits[idx[3:5]] = np.inf
+    logits[idx[5:7]] = -np.inf
+    logits[idx[7:9]] = 0.0
+    logits[idx[9:12]] = -0.0
+    hist = rng.integers(0, 3000, size=50).tolist() + idx[7:12].tolist() * 2
+    for t, k, p, rp in [(0.7, 40, 0.95, 1.0), (1.0, 1000, 1.0, -1.5), (-0.5, 7, 0.5, 1.1)]:
+        a, b = logits.copy(), logits.copy()
+        got = Sampler.sample(a, hist, SamplerConfig(t, k, p, rp, seed))
+        want = ref.sample(b, hist, ref.SamplerConfig(t, k, p, rp, seed))
+        assert got == want
+        na = np.isnan(a)
+        assert np.array_equal(na, np.isnan(b)) and np.array_equal(a[~na].view(np.uint32), b[~na].view(np.uint32))
