@@ -124,6 +124,7 @@ SIGNATURES = {
     "at_model_step_stamps": [_vp, _i, _i64, _vp, _i64, _vp],
     "at_model_generate": [_vp, _i, _i64, _i, _vp],
     "at_model_profile_step": [_vp, _i, _i64, _vp, _vp],
+    "at_model_profile_batch": [_vp, _i, _vp, _vp, _vp, _vp],
     "at_model_sample": [_vp, _i, _vp, _vp],
     "at_model_generate_sampled": [_vp, _i, _vp, _vp, _i, _vp, _vp],
     "at_model_forward_prompt_slot": [_vp, _i, _vp, _i],

@@ -859,6 +859,7 @@ struct at_model {
     cudaGraphExec_t graph[9] = {};
     cudaGraphExec_t graph_gen = nullptr;  // step + greedy advance (slot 0)
     cudaGraphExec_t graph_prof = nullptr; // step with an event pair around every launch
+    int graph_prof_batch = 0;
     int* d_gen_out = nullptr;             // [ctx] generated tokens
     int* d_gen_count = nullptr;
     // eager profiling: event pairs around each launch
@@ -2378,27 +2379,40 @@ void sched_reset_slot(at_model* m, int slot) { m->kv_size[slot] = 0; }
 
 extern "C" {
 
-int at_model_profile_step(at_model* m, int token, int64_t position, float* class_ms, int* class_launches) {
+int at_model_profile_batch(at_model* m, int batch, const int* tokens, const int64_t* positions, float* class_ms,
+                           int* class_launches) {
     return guard([&] {
-        AT_REQUIRE(m && m->finalized && class_ms && class_launches, AT_ERR_INVALID_ARG, "bad argument");
-        AT_REQUIRE(token >= 0 && token < m->V, AT_ERR_INVALID_ARG, "token id out of range");
-        AT_REQUIRE(position >= 0 && position < m->ctx_len, AT_ERR_STATE, "position exceeds maxContext");
+        AT_REQUIRE(m && m->finalized && class_ms && class_launches && tokens && positions, AT_ERR_INVALID_ARG,
+                   "bad argument");
+        AT_REQUIRE(batch >= 1 && batch <= m->B, AT_ERR_INVALID_ARG, "batch out of range");
+        for (int b = 0; b < batch; ++b) {
+            AT_REQUIRE(tokens[b] >= 0 && tokens[b] < m->V, AT_ERR_INVALID_ARG, "token id out of range");
+            AT_REQUIRE(positions[b] >= 0 && positions[b] < m->ctx_len, AT_ERR_STATE, "position exceeds maxContext");
+        }
         at_ctx* c = m->ctx;
         AT_CUDA(cudaSetDevice(c->device));
-        m->h_tokens[0] = token;
-        m->h_pos[0] = position;
-        AT_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tokens, sizeof(int), cudaMemcpyHostToDevice, c->stream));
-        AT_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pos, sizeof(int64_t), cudaMemcpyHostToDevice, c->stream));
-        // The step is captured once into a graph with an event pair around
-        // every launch and no programmatic overlap, so each pair times one
-        // kernel on the device without host submission gaps.
-        if (!m->graph_prof) {
+        AT_CUDA(cudaStreamSynchronize(c->stream));  // the pinned staging buffers are free
+        for (int b = 0; b < batch; ++b) {
+            m->h_tokens[b] = tokens[b];
+            m->h_pos[b] = positions[b];
+        }
+        AT_CUDA(cudaMemcpyAsync(m->d_tokens, m->h_tokens, sizeof(int) * batch, cudaMemcpyHostToDevice, c->stream));
+        AT_CUDA(cudaMemcpyAsync(m->d_pos, m->h_pos, sizeof(int64_t) * batch, cudaMemcpyHostToDevice, c->stream));
+        // The step is captured into a graph with an event pair around every
+        // launch and no programmatic overlap, so each pair times one kernel on
+        // the device without host submission gaps (recaptured when the batch
+        // changes; the event pairs are shared).
+        if (!m->graph_prof || m->graph_prof_batch != batch) {
+            if (m->graph_prof) {
+                cudaGraphExecDestroy(m->graph_prof);
+                m->graph_prof = nullptr;
+            }
             m->profiling = true;
             m->pdl = false;
             m->prof_used = 0;
             m->prof_cls.clear();
             try {
-                m->graph_prof = capture(m, enqueue_step, 1);
+                m->graph_prof = capture(m, enqueue_step, batch);
             } catch (...) {
                 m->profiling = false;
                 m->pdl = true;
@@ -2406,6 +2420,7 @@ int at_model_profile_step(at_model* m, int token, int64_t position, float* class
             }
             m->profiling = false;
             m->pdl = true;
+            m->graph_prof_batch = batch;
         }
         AT_CUDA(cudaGraphLaunch(m->graph_prof, c->stream));
         if (c->world > 1)
@@ -2419,8 +2434,12 @@ int at_model_profile_step(at_model* m, int token, int64_t position, float* class
             class_ms[m->prof_cls[i]] += ms;
             class_launches[m->prof_cls[i]] += 1;
         }
-        m->kv_size[0] = std::max<int64_t>(m->kv_size[0], position + 1);
+        for (int b = 0; b < batch; ++b) m->kv_size[b] = std::max<int64_t>(m->kv_size[b], positions[b] + 1);
     });
+}
+
+int at_model_profile_step(at_model* m, int token, int64_t position, float* class_ms, int* class_launches) {
+    return at_model_profile_batch(m, 1, &token, &position, class_ms, class_launches);
 }
 
 int at_model_logits_device(at_model* m, float** logits_dev) {

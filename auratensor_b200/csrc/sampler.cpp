@@ -4,6 +4,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstdint>
+#include <cstring>
 #include <numeric>
 #include <vector>
 
@@ -22,12 +23,13 @@ struct JavaRandom {
     float next_float() { return (float)next(24) / (float)(1 << 24); }
 };
 
-// Double.compare(x, y) < 0: NaN is above +inf and -0.0 is below 0.0.
-bool java_double_less(double x, double y) {
-    if (std::isnan(x)) return false;
-    if (std::isnan(y)) return true;
-    if (x != y) return x < y;
-    return std::signbit(x) && !std::signbit(y);
+// Order-preserving bits of a float under Double.compare: NaN above +inf,
+// -0.0 below 0.0, every NaN equal.
+uint32_t double_compare_bits(float v) {
+    if (std::isnan(v)) return 0xFFFFFFFFu;
+    uint32_t u;
+    std::memcpy(&u, &v, 4);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
 }  // namespace
@@ -67,13 +69,19 @@ extern "C" int at_sample(float* logits, int vocab, const int* history, int n_his
         const float inv_t = 1.0f / temperature;
         std::vector<float> adj(vocab);
         for (int i = 0; i < vocab; ++i) adj[i] = logits[i] * inv_t;
-        std::vector<int> idx(vocab);
-        std::iota(idx.begin(), idx.end(), 0);
-        // Comparator.comparingDouble(..).reversed(): b before a when
-        // Double.compare(adj[a], adj[b]) < 0; List.sort is stable.
-        std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return java_double_less(adj[b], adj[a]); });
+        // Comparator.comparingDouble(..).reversed() under List.sort (stable):
+        // descending in Double.compare's order, equal values in index order.
+        // Only the first k places are read, and they are the k largest of the
+        // keys (order bits, then the complemented index), sorted.
         const int k = std::min(top_k, vocab);
         AT_REQUIRE(k >= 1, AT_ERR_INVALID_ARG, "topK must be positive");
+        std::vector<uint64_t> keys(vocab);
+        for (int i = 0; i < vocab; ++i) keys[i] = ((uint64_t)double_compare_bits(adj[i]) << 32) | (0xFFFFFFFFu - (uint32_t)i);
+        auto desc = [](uint64_t a, uint64_t b) { return a > b; };
+        if (k < vocab) std::nth_element(keys.begin(), keys.begin() + (k - 1), keys.end(), desc);
+        std::sort(keys.begin(), keys.begin() + k, desc);
+        std::vector<int> idx(k);
+        for (int i = 0; i < k; ++i) idx[i] = (int)(0xFFFFFFFFu - (uint32_t)(keys[i] & 0xFFFFFFFFu));
         const float max_logit = adj[idx[0]];
         std::vector<float> probs(k);
         float sum_exp = 0.0f;

@@ -255,6 +255,16 @@ class LlamaModel:
              n.ctypes.data_as(C.c_void_p))
         return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(_lib.PROF_CLASSES)}
 
+    def profileBatch(self, tokens, positions) -> dict:
+        """profileStep for one batched step of slots 0..len(tokens)-1."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        p = np.ascontiguousarray(np.asarray(positions, dtype=np.int64))
+        ms = np.zeros(len(_lib.PROF_CLASSES), dtype=np.float32)
+        n = np.zeros(len(_lib.PROF_CLASSES), dtype=np.int32)
+        call("at_model_profile_batch", self._h, int(t.size), t.ctypes.data_as(C.c_void_p),
+             p.ctypes.data_as(C.c_void_p), ms.ctypes.data_as(C.c_void_p), n.ctypes.data_as(C.c_void_p))
+        return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(_lib.PROF_CLASSES)}
+
     def stream(self) -> int:
         p = C.c_void_p()
         call("at_ctx_stream", self._ctx, C.byref(p))

@@ -18,9 +18,23 @@ per-layer all-reduces and the logits gather are the library's own kernels over
 NVLink peer memory (NCCL only exchanges the memory handles at load); scaling
 "strong".
 
+--config selects the other workloads (their own metric names):
+  llama-3-70b              80 layers, dim 8192, Q4_0 (39.5 GB), 1024-token
+                           prompt, greedy decode at context 8192.
+  mistral-7b-q8_0-batch8   Mistral-7B shape, Q8_0, 8 requests with 128-token
+                           seeded prompts, temperature 0.7 / top-k 40 / top-p
+                           0.95 with fixed seeds, batched decode at context
+                           4096; one step = one batched step (8 tokens).
+                           value: at_model_generate_sampled (step graph +
+                           device sampler + token feedback on the device);
+                           e2e: the request scheduler (at_sched_step: tokens
+                           and positions in, sampled ids out, every step).
+
 --impl reference: the reference's CPU algorithm (load-time dequant to FP32,
 FP32 sgemv; the C restatement under oracle/) on all host cores, each step a
-sampled decode token (2 of 32 layers plus the lm_head, extrapolated).
+sampled decode token (2 of the layers plus the lm_head, extrapolated); the
+reference serves one request at a time, so its batch-8 rate is its
+single-sequence rate (plus the host Sampler for the sampled workload).
 """
 from __future__ import annotations
 
@@ -37,10 +51,15 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-METRIC = "Llama-3-8B Q4_0 decode tok/s"
 UNIT = "tok/s"
-PROMPT = 512
 SAMPLE_LAYERS = 2
+# workload name -> (shape name in synth, metric, prompt tokens, batch, sampler (T, topK, topP, penalty) or None)
+CONFIGS = {
+    "llama-3-8b": ("LLAMA3_8B", "Llama-3-8B Q4_0 decode tok/s", 512, 1, None),
+    "llama-3-70b": ("LLAMA3_70B", "Llama-3-70B Q4_0 decode tok/s", 1024, 1, None),
+    "mistral-7b-q8_0-batch8": ("MISTRAL_7B", "Mistral-7B Q8_0 batch-8 sampled decode tok/s", 128, 8,
+                               (0.7, 40, 0.95, 1.0)),
+}
 
 
 def parse():
@@ -53,10 +72,25 @@ def parse():
     p.add_argument("--profile-steps", type=int, default=8)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-parity", action="store_true")
+    p.add_argument("--config", default="llama-3-8b", choices=sorted(CONFIGS))
     # smaller cases for profiler captures only (the bench line uses the defaults)
-    p.add_argument("--prompt", type=int, default=PROMPT)
+    p.add_argument("--prompt", type=int, default=None)
     p.add_argument("--layers", type=int, default=None)
-    return p.parse_args()
+    a = p.parse_args()
+    shape_name, a.metric, prompt, a.batch, a.sampler = CONFIGS[a.config]
+    a.shape_name = shape_name
+    if a.prompt is None:
+        a.prompt = prompt
+    return a
+
+
+def config_shape(args):
+    import dataclasses
+    from auratensor_b200 import synth
+    shape = getattr(synth, args.shape_name)
+    if args.layers is not None:
+        shape = dataclasses.replace(shape, n_layers=args.layers)
+    return shape
 
 
 # ---------------------------------------------------------------------------
@@ -119,19 +153,34 @@ def q_bytes(rows, cols, bpb=18):
     return rows * (cols // 32) * bpb
 
 
-def class_bytes(shape, world, pos):
+def class_bytes(shape, world, pos, batch=1):
+    """Algorithmic bytes of one step per kernel class: the quantized weights
+    once, the activations in and out of every row, and each row's KV cache
+    up to its position (pos: one position or one per row)."""
     d, hd = shape.dim, shape.head_dim
     hl, hkvl, fl = shape.n_heads // world, shape.n_kv_heads // world, shape.ffn // world
     vl = -(-shape.vocab // world)
     qkv_cols = (hl + 2 * hkvl) * hd
+    bpb = 34 if shape.wtype == 8 else 18
+    ps = list(pos) if isinstance(pos, (list, tuple)) else [pos] * batch
     return {
-        "qkv": q_bytes(d, qkv_cols) + d * 4 + qkv_cols * 4,
-        "wo": q_bytes(hl * hd, d) + hl * hd * 4 + d * 4,
-        "ffn_up": 2 * q_bytes(fl, d) + d * 4 + fl * 4,
-        "ffn_down": q_bytes(d, fl) + fl * 4 + d * 4,
-        "lm_head": q_bytes(vl, d) + d * 4 + vl * 4,
-        "attn": 2 * hkvl * (pos + 1) * hd * 4 + 2 * hl * hd * 4,
+        "qkv": q_bytes(d, qkv_cols, bpb) + batch * (d * 4 + qkv_cols * 4),
+        "wo": q_bytes(hl * hd, d, bpb) + batch * (hl * hd * 4 + d * 4),
+        "ffn_up": 2 * q_bytes(fl, d, bpb) + batch * (d * 4 + fl * 4),
+        "ffn_down": q_bytes(d, fl, bpb) + batch * (fl * 4 + d * 4),
+        "lm_head": q_bytes(vl, d, bpb) + batch * (d * 4 + vl * 4),
+        "attn": sum(2 * hkvl * (p + 1) * hd * 4 + 2 * hl * hd * 4 for p in ps),
     }
+
+
+def step_bytes_of(shape, world, positions_per_step, batch):
+    """Mean bytes one GPU must move per step over the timed steps."""
+    tot = 0.0
+    for pos in positions_per_step:
+        cb = class_bytes(shape, world, pos, batch)
+        tot += shape.n_layers * (cb["qkv"] + cb["attn"] + cb["wo"] + cb["ffn_up"] + cb["ffn_down"])
+        tot += cb["lm_head"] + batch * q_bytes(1, shape.dim, 34 if shape.wtype == 8 else 18)
+    return tot / len(positions_per_step)
 
 
 def load_peaks():
@@ -197,28 +246,50 @@ def sample_host_tensors_cpu(shape, seed):
     return out
 
 
+def host_sampler_seconds(vocab, cfg, reps=20):
+    """Seconds per call of the host Sampler (native restatement) on one
+    vocab-sized logits row with the workload's settings."""
+    from auratensor_b200.inference import Sampler, SamplerConfig
+    rng = np.random.default_rng(0)
+    x = (rng.standard_normal(vocab) * 3).astype(np.float32)
+    t, k, p, rp = cfg
+    c = SamplerConfig(t, k, p, rp, 1234)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        Sampler.sample(x.copy(), None, c)
+    return (time.perf_counter() - t0) / reps
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from auratensor_b200 import synth
-    shape = synth.LLAMA3_8B
+    shape = config_shape(args)
     threads = os.cpu_count() or 1
     t0 = time.time()
     tensors = sample_host_tensors_cpu(shape, args.seed)
     gen_s = time.time() - t0
-    rates = cpu_decode_sample(shape, tensors, threads, args.warmup + args.steps, PROMPT)
+    rates = cpu_decode_sample(shape, tensors, threads, args.warmup + args.steps, args.prompt)
     timed = rates[args.warmup:]
-    value = len(timed) / sum(1.0 / r for r in timed)
+    sec_per_tok = sum(1.0 / r for r in timed) / len(timed)
+    sampler_s = 0.0
+    if args.sampler is not None:
+        sampler_s = host_sampler_seconds(shape.vocab, args.sampler)
+    value = 1.0 / (sec_per_tok + sampler_s)
     sample = (f"{SAMPLE_LAYERS} of {shape.n_layers} layers + lm_head per step, decode positions "
-              f"{PROMPT}..{PROMPT + args.warmup + args.steps - 1}, extrapolated to {shape.n_layers} layers")
+              f"{args.prompt}..{args.prompt + args.warmup + args.steps - 1}, extrapolated to {shape.n_layers} layers")
+    if args.sampler is not None:
+        sample += (f"; one request at a time as the reference's server (its batch-{args.batch} rate is its "
+                   f"single-sequence rate), plus the host Sampler ({sampler_s * 1e3:.3f} ms per token)")
     line = {
-        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "metric": args.metric, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(1000.0 / value, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "impl": "reference",
-        "config": {"workload": "llama-3-8b-q4_0-decode", "batch": 1, "prompt_tokens": PROMPT, "context": 2048,
-                   "weights": "Q4_0 dequantized to FP32 at load (reference algorithm)"},
+        "config": {"workload": workload_name(args, shape), "batch": args.batch, "prompt_tokens": args.prompt,
+                   "context": shape.ctx,
+                   "weights": f"{'Q8_0' if shape.wtype == 8 else 'Q4_0'} dequantized to FP32 at load "
+                              "(reference algorithm)"},
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample, "setup_s": round(gen_s, 1)},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -226,14 +297,20 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def workload_name(args, shape):
+    q = "q8_0" if shape.wtype == 8 else "q4_0"
+    base = args.config if q in args.config else f"{args.config}-{q}"
+    return base + ("-sampled-decode" if args.sampler is not None else "-decode")
+
+
 # ---------------------------------------------------------------------------
 # our engine
 # ---------------------------------------------------------------------------
-def build_model(shape, seed, ctx, world, keep_host: bool):
+def build_model(shape, seed, ctx, world, keep_host: bool, max_batch: int = 1):
     import torch
     from auratensor_b200 import synth
     from auratensor_b200.inference import LlamaConfig, LlamaModel
-    model = LlamaModel(LlamaConfig.fromShape(shape), None, max_batch=1, ctx=ctx, world=world)
+    model = LlamaModel(LlamaConfig.fromShape(shape), None, max_batch=max_batch, ctx=ctx, world=world)
     g = torch.Generator(device="cuda").manual_seed(seed)
     host = {}
     for name, dims, t in shape.tensor_dims():
@@ -337,10 +414,11 @@ def main():
         p = C.c_void_p()
         _lib.call("at_ctx_create", local, C.byref(p))
         ctx = p.value
-    shape = synth.LLAMA3_8B
-    if args.layers is not None:
-        import dataclasses
-        shape = dataclasses.replace(shape, n_layers=args.layers)
+    shape = config_shape(args)
+    if args.batch > 1:
+        run_batched(args, shape, ctx, world, rank, local)
+        return
+    PROMPT = args.prompt
     keep_host = (rank == 0 and world == 1 and not args.no_cpu_baseline and args.layers is None)
     t0 = time.time()
     model, host = build_model(shape, args.seed, ctx, world, keep_host)
@@ -359,7 +437,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    prompt = synth.prompt_ids(shape, args.seed, args.prompt).tolist()
+    prompt = synth.prompt_ids(shape, args.seed, PROMPT).tolist()
     t0 = time.time()
     model.forwardPrompt(prompt)
     prefill_s = time.time() - t0
@@ -433,12 +511,7 @@ def main():
     bytes_per = class_bytes(shape, world, pos)
     # bytes one GPU must move per decode step (weights of its shards, its KV
     # heads at the timed positions, activations), over the measured step time
-    step_bytes = 0.0
-    for p in timed_pos:
-        cb = class_bytes(shape, world, p)
-        step_bytes += shape.n_layers * (cb["qkv"] + cb["attn"] + cb["wo"] + cb["ffn_up"] + cb["ffn_down"])
-        step_bytes += cb["lm_head"] + q_bytes(1, shape.dim)
-    step_bytes /= len(timed_pos)
+    step_bytes = step_bytes_of(shape, world, timed_pos, 1)
     gemv = {k: v for k, v in tot.items() if k in bytes_per}
     dom = max(gemv, key=lambda k: gemv[k][0])
     avg_ms = gemv[dom][0] / max(1, gemv[dom][1])
@@ -461,12 +534,13 @@ def main():
                          f"{PROMPT + 64}.., extrapolated to {shape.n_layers} layers; same Q4_0 weights",
                "single_thread_value": round(len(rates1) / sum(1 / r for r in rates1), 4)}
 
+    wbytes = sum(int(np.prod(dims)) // 32 * 18 for _, dims, t in shape.tensor_dims() if t != 0)
     line = {
-        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": args.metric, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "llama-3-8b-q4_0-decode", "batch": 1, "prompt_tokens": PROMPT, "context": ctx_len,
-                   "weights": "Q4_0 (4.6 GB, > L2; no flush needed)", "parallelism": f"tp{world}",
+        "config": {"workload": workload_name(args, shape), "batch": 1, "prompt_tokens": PROMPT, "context": ctx_len,
+                   "weights": f"Q4_0 ({wbytes / 1e9:.1f} GB, > L2; no flush needed)", "parallelism": f"tp{world}",
                    "seed": args.seed},
         "e2e": {"value": round(e2e, 3), "unit": UNIT, "h2d_bytes_per_step": 12,
                 "d2h_bytes_per_step": shape.vocab * 4},
@@ -486,6 +560,195 @@ def main():
         # the untimed prompt (forwardPrompt: tcgen05 GEMMs over 128-token chunks on one GPU), host wall clock
         "prompt": {"tokens": args.prompt, "seconds": round(prefill_s, 4),
                    "tok_s": round(args.prompt / prefill_s, 1) if prefill_s > 0 else None},
+    }
+    print(json.dumps(line), flush=True)
+    finish(model, ctx, world)
+
+
+def batched_parity(full_shape, seed, ctx, batch, sampler):
+    """The batched sampled path against the oracle in the same run: a 2-layer
+    model of the workload's dimensions with `batch` slots. Every row decodes
+    its own 6-token seeded prompt and then 10 sampled tokens, all rows in one
+    batched step each time (the device sampler picks the tokens, each row
+    with its own seed and its prompt-plus-output penalty history). Each row
+    is then replayed through the C restatement of the reference, teacher
+    forced on the device's tokens: the logits must be within 1e-3 of the
+    oracle's range at every step, the device sampler must pick what the host
+    Sampler picks from the device's logits (exact), and the count of steps
+    where the host Sampler on the oracle's logits picks the same id is
+    reported."""
+    import dataclasses
+    import torch
+    from auratensor_b200 import synth
+    from auratensor_b200.inference import LlamaConfig, LlamaModel, Sampler, SamplerConfig
+    from oracle.cref import RefDecoder
+    shape = dataclasses.replace(full_shape, n_layers=2, ctx=64)
+    n_prompt, n_gen, tol = 6, 10, 1e-3
+    g = torch.Generator(device="cuda").manual_seed(seed + 2000)
+    model = LlamaModel(LlamaConfig.fromShape(shape), None, max_batch=batch, ctx=ctx)
+    orc = RefDecoder(shape, threads=os.cpu_count() or 1)
+    for name, dims, t in shape.tensor_dims():
+        data = synth.generate_torch_tensor(dims, t, g, "cuda")
+        model.setTensor(name, t, data)
+        orc.set_tensor(name, t, data.cpu().numpy(), int(np.prod(dims)))
+        del data
+    model.finalize()
+    T, K, P, R = sampler
+    cfgs = [SamplerConfig(T, K, P, R, 1000 + b) for b in range(batch)]
+    prompts = [[int(v) for v in synth.prompt_ids(shape, seed + b, n_prompt)] for b in range(batch)]
+    seqs = [list(p) for p in prompts]
+    dev_logits = [[] for _ in range(batch)]
+    sampler_equal = True
+    for pos in range(n_prompt + n_gen - 1):
+        toks = [seqs[b][pos] for b in range(batch)]
+        lg = model.forwardBatch(toks, [pos] * batch).copy()
+        if pos >= n_prompt - 1:
+            got = model.sample(cfgs, seqs)
+            for b in range(batch):
+                dev_logits[b].append(lg[b].copy())
+                want = Sampler.sample(lg[b].copy(), seqs[b], cfgs[b])
+                sampler_equal = sampler_equal and int(got[b]) == want
+                seqs[b].append(int(got[b]))
+        else:
+            for b in range(batch):
+                dev_logits[b].append(lg[b].copy())
+    worst, agree, total = 0.0, 0, 0
+    for b in range(batch):
+        for pos in range(n_prompt + n_gen - 1):
+            lr = orc.forward_step(seqs[b][pos], pos)
+            lg = dev_logits[b][pos]
+            worst = max(worst, float(np.max(np.abs(lg - lr))) / float(lr.max() - lr.min()))
+            if pos >= n_prompt - 1:
+                total += 1
+                agree += int(Sampler.sample(lr.copy(), seqs[b][:pos + 1], cfgs[b]) == seqs[b][pos + 1])
+    orc.close()
+    model.close()
+    return {"checked": True, "model": f"{shape.name} dims, 2 layers, batch {batch}", "steps": n_prompt + n_gen - 1,
+            "max_rel_err": float(f"{worst:.3g}"), "tol": tol, "sampled_steps": total,
+            "device_sampler_equals_host": sampler_equal, "oracle_logits_same_token": agree,
+            "passed": bool(worst <= tol and sampler_equal)}
+
+
+def run_batched(args, shape, ctx, world, rank, local):
+    """Batched sampled decode: value from at_model_generate_sampled over the
+    batch (device loop), e2e from the request scheduler (at_sched_step)."""
+    import torch
+    from auratensor_b200 import synth
+    from auratensor_b200.inference import SamplerConfig
+    from auratensor_b200.scheduler import BatchScheduler
+    assert world == 1, "the batched sampled workload runs on one GPU"
+    B, n_prompt, ctx_len = args.batch, args.prompt, shape.ctx
+    T, K, P, R = args.sampler
+    cfgs = [SamplerConfig(T, K, P, R, 7 + b) for b in range(B)]
+    total_steps = args.warmup + args.steps
+    assert n_prompt + total_steps <= ctx_len, "steps exceed the context"
+    keep_host = not args.no_cpu_baseline and args.layers is None
+    t0 = time.time()
+    model, host = build_model(shape, args.seed, ctx, world, keep_host, max_batch=B)
+    load_s = time.time() - t0
+    stream = torch.cuda.ExternalStream(model.stream())
+    prompts = [synth.prompt_ids(shape, args.seed + b, n_prompt).tolist() for b in range(B)]
+    torch.cuda.synchronize()
+    t0 = time.time()
+    for b in range(B):
+        model.forwardPromptSlot(b, prompts[b][:-1])
+    prefill_s = time.time() - t0
+    first = [p[-1] for p in prompts]
+    start = [n_prompt - 1] * B
+    hists = [list(p) for p in prompts]
+    warm = model.generateSampled(first, start, args.warmup, cfgs, hists)
+    first2 = [int(warm[b, -1]) for b in range(B)]
+    start2 = [n_prompt - 1 + args.warmup] * B
+    hists2 = [hists[b] + warm[b].tolist() for b in range(B)]
+    gpus = [local]
+    with ClockSampler(gpus) as clk:
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        out = model.generateSampled(first2, start2, args.steps, cfgs, hists2)
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        # e2e: the request scheduler, prompts admitted (untimed), then args.steps timed steps
+        sched = BatchScheduler(model)
+        ids = [sched.submit(prompts[b], total_steps + 1, cfgs[b]) for b in range(B)]
+        for _ in range(args.warmup):
+            sched.step()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        w0 = time.perf_counter()
+        for _ in range(args.steps):
+            sched.step()
+        w1 = time.perf_counter()
+        f1.record(stream)
+        f1.synchronize()
+        ms_e2e = f0.elapsed_time(f1)
+        sched_tokens = [sched.result(r)[0] for r in ids]
+        sched.close()
+    clocks = clk.summary()
+    value = B * args.steps / (ms / 1000.0)
+    e2e = B * args.steps / (ms_e2e / 1000.0)
+    # the scheduler and the device loop are the same computation: their token streams agree
+    agree = sum(int(np.array_equal(sched_tokens[b][: args.warmup + args.steps],
+                                   np.concatenate([warm[b], out[b]]))) for b in range(B))
+    timed_pos = [[n_prompt - 1 + args.warmup + i] * B for i in range(args.steps)]
+    step_bytes = step_bytes_of(shape, world, timed_pos, B)
+    # roofline of the dominant kernel class at batch B (eager, one event pair per launch)
+    tot = {}
+    prof_pos = n_prompt - 1 + total_steps
+    for i in range(args.profile_steps):
+        p = min(prof_pos + i, ctx_len - 1)
+        r = model.profileBatch([1] * B, [p] * B)
+        for k, (msk, n) in r.items():
+            a = tot.setdefault(k, [0.0, 0])
+            a[0] += msk
+            a[1] += n
+    bytes_per = class_bytes(shape, world, prof_pos, B)
+    gemv = {k: v for k, v in tot.items() if k in bytes_per}
+    dom = max(gemv, key=lambda k: gemv[k][0])
+    avg_ms = gemv[dom][0] / max(1, gemv[dom][1])
+    peak, peak_kind = load_peaks()
+    achieved = bytes_per[dom] / (avg_ms / 1000.0) / 1e9
+    parity = None if args.no_parity else batched_parity(shape, args.seed, ctx, B, args.sampler)
+    cpu = None
+    if keep_host:
+        threads = os.cpu_count() or 1
+        rates = cpu_decode_sample(shape, host, threads, 4, n_prompt + 64)
+        sampler_s = host_sampler_seconds(shape.vocab, args.sampler)
+        v = 1.0 / (sum(1 / r for r in rates) / len(rates) + sampler_s)
+        cpu = {"value": round(v, 4), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{SAMPLE_LAYERS} of {shape.n_layers} layers + lm_head, 4 decode tokens at positions "
+                         f"{n_prompt + 64}.., extrapolated to {shape.n_layers} layers, plus the host Sampler "
+                         f"({sampler_s * 1e3:.3f} ms); one request at a time, as the reference's server"}
+    # per step: embed; 5 per layer; lm_head, argmax (2); sample, advance
+    launches_per_step = 1 + 5 * shape.n_layers + 3 + 2
+    line = {
+        "metric": args.metric, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload_name(args, shape), "batch": B, "requests": B, "prompt_tokens": n_prompt,
+                   "context": ctx_len, "sampler": {"temperature": T, "top_k": K, "top_p": P,
+                                                   "repetition_penalty": R, "seeds": [c.seed for c in cfgs]},
+                   "weights": "Q8_0 (7.7 GB, > L2; no flush needed)", "parallelism": "tp1", "seed": args.seed,
+                   "step": f"one batched step = {B} tokens"},
+        "e2e": {"value": round(e2e, 3), "unit": UNIT, "h2d_bytes_per_step": B * (4 + 8 + 4),
+                "d2h_bytes_per_step": B * 4, "api": "at_sched_step (request scheduler)",
+                "host_wall_tok_s": round(B * args.steps / (w1 - w0), 3),
+                "requests_matching_device_loop": agree},
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": None, "bytes_per_launch": bytes_per[dom],
+                     "avg_launch_us": round(avg_ms * 1000.0, 2), "step_bytes": int(step_bytes),
+                     "step_frac": round(step_bytes / (ms / args.steps / 1000.0) / 1e9 / peak, 4)},
+        "parity": parity,
+        "kernel_ms_per_step": {k: round(v[0] / args.profile_steps, 4) for k, v in tot.items() if v[1]},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+        "setup": {"load_s": round(load_s, 1), "prefill_s": round(prefill_s, 2)},
+        "prompt": {"tokens": B * (n_prompt - 1), "seconds": round(prefill_s, 4),
+                   "tok_s": round(B * (n_prompt - 1) / prefill_s, 1) if prefill_s > 0 else None},
     }
     print(json.dumps(line), flush=True)
     finish(model, ctx, world)

@@ -312,6 +312,9 @@ int at_sched_result(at_sched* s, int request_id, int* tokens_host, int cap, int*
 #define AT_PROF_COMM     8  /* NCCL all-reduce / all-gather            */
 #define AT_PROF_CLASSES  9
 int at_model_profile_step(at_model* m, int token, int64_t position, float* class_ms, int* class_launches);
+/* The same for one batched step of slots 0..batch-1. */
+int at_model_profile_batch(at_model* m, int batch, const int* tokens, const int64_t* positions, float* class_ms,
+                           int* class_launches);
 /* KVCache.size / offsetOf / keys() / values() (inference/KVCache.java:70-104):
  * copies head_dim floats of K and V for (slot, layer, kv_head, position). */
 int at_model_kv_size(const at_model* m, int slot, int64_t* size);
