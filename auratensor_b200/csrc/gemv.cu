@@ -677,18 +677,23 @@ __global__ void __launch_bounds__(S_THREADS, 1) gemv_ns_kernel(const NSParams p)
 // ---------------------------------------------------------------------------
 // Orientation N, batch 3..8: split K into 32-block steps
 // ---------------------------------------------------------------------------
-// CTA (p, q) stages the 1024 x values of step q for all batch rows (36 KB at
-// batch 8) and streams the tiles (g, q) of the row groups g of part p
-// through per-warp cp.async rings, a warp owning whole groups; a group's
-// 4 x NM x B sums are combined over the lanes by a butterfly reduce-scatter
-// (lane l ends with value l; matrices one at a time) and stored as the
-// step's partial. A second
-// kernel sums the steps' partials in step order (deterministic) and applies
-// the epilogue. Folded RMSNorm as in the stream kernel: each CTA also stores
-// its step's sums of (xin + yin)^2.
+// CTA (p, q) stages the 1024 x values of step q for all batch rows and
+// streams the tiles (g, q) of the row groups g of part p through per-warp
+// cp.async rings, two tiles per unit: the gate and up tiles of one group
+// (SiLU epilogue) or two consecutive groups. Lane l owns block 32q + l of
+// the unit's 8 rows. x is staged per block as [32 elements][8 batch rows]
+// in the subnormal-scaled form of the stream kernel (plus the block sums of
+// each batch row), so each weight is decoded once (one mask per weight) and
+// applied to the batch by FFMA2 over pairs of batch rows, and every x value
+// read serves 8 rows. A group's 4 x B sums per matrix are combined over the
+// lanes by a butterfly reduce-scatter (lane l ends with value l) and stored
+// as the step's partial. A second kernel sums the steps' partials in step
+// order (deterministic) and applies the epilogue. Folded RMSNorm as in the
+// stream kernel: each CTA also stores its step's sums of (xin + yin)^2.
 constexpr int Q_THREADS = 256;
 constexpr int Q_WARPS = Q_THREADS / 32;
 constexpr int Q_NST = 2;
+constexpr int QX = 268;  // floats per staged block: 32 x 8 values, 8 block sums, 4 padding
 
 struct NQParams {
     const uint8_t* tiles[2];
@@ -719,29 +724,66 @@ __device__ __forceinline__ float lane_transpose_sum(float* v, int lane) {
     return v[0];
 }
 
+// Values per row in a group partial: the batch, 7 padded to 8.
+__host__ __device__ constexpr int nq_stride(int b) { return b == 7 ? 8 : b; }
+
+// The subnormal-scaled fields of elements 4 kc .. 4 kc + 3 of a block (see
+// dot32_dn): Q4_0 from 32-bit word kc / 2 of the block's 16 quant bytes,
+// Q8_0 from word kc of its 32.
+template <int QT>
+__device__ __forceinline__ void q4_fields_dn(uint32_t w, int kc, float* f) {
+    if constexpr (QT == AT_GGML_Q4_0) {
+        if ((kc & 1) == 0) {
+            f[0] = bits_f(w & 0xFu); f[1] = bits_f(w & 0xF0u); f[2] = bits_f(w & 0xF00u); f[3] = bits_f(w & 0xF000u);
+        } else {
+            const uint32_t t = w >> 24;
+            f[0] = bits_f(w & 0xF0000u); f[1] = bits_f(w & 0xF00000u); f[2] = bits_f(t & 0xFu); f[3] = bits_f(t & 0xF0u);
+        }
+    } else {
+        f[0] = bits_f((w ^ 0x80u) & 0xFFu);
+        f[1] = bits_f((w ^ 0x8000u) & 0xFF00u);
+        f[2] = bits_f((w ^ 0x800000u) & 0xFF0000u);
+        f[3] = bits_f((w >> 24) ^ 0x80u);
+    }
+}
+
 template <int QT, int B, Pro PRO, Epi EPI>
 __global__ void __launch_bounds__(Q_THREADS, 1) gemv_nq_kernel(const NQParams p) {
     constexpr int NM = (EPI == Epi::SiluMul) ? 2 : 1;
     using TL = NTile<QT>;
-    constexpr int SLOT = NM * TL::BYTES;
-    constexpr int NV = QTraits<QT>::NV;
+    constexpr int SLOT = 2 * TL::BYTES;  // two tiles per unit
+    constexpr int QB = QTraits<QT>::QB;
+    constexpr int BP = (B + 1) / 2;      // pairs of batch rows
     static_assert(4 * B <= 32, "one 32-value partial per matrix and group");
-    extern __shared__ __align__(16) float xs[];  // [B][32 blocks][XPAD], then the rings
+    extern __shared__ __align__(16) float xs[];  // [32 blocks][QX], then the rings
     pdl_trigger();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int pp = blockIdx.x, q = blockIdx.y;
     const int g0 = (int)((int64_t)pp * p.ngroups / p.P), g1 = (int)((int64_t)(pp + 1) * p.ngroups / p.P);
-    const int nmine = (g1 - g0 - warp + Q_WARPS - 1) / Q_WARPS;  // groups g0 + warp + Q_WARPS * i
-    const uint8_t* ring_ptr = reinterpret_cast<const uint8_t*>(xs) + B * 32 * XPAD * 4 + warp * Q_NST * SLOT;
+    // unit i of this warp: SiLU: group g0 + warp + Q_WARPS i (gate, up); else
+    // groups ga = g0 + 2 (warp + Q_WARPS i) and ga + 1 (when below g1)
+    const int ng = g1 - g0;
+    const int nmine = (NM == 2) ? (ng - warp + Q_WARPS - 1) / Q_WARPS
+                                : ((ng + 1) / 2 - warp + Q_WARPS - 1) / Q_WARPS;
+    const uint8_t* ring_ptr = reinterpret_cast<const uint8_t*>(xs) + 32 * QX * 4 + warp * Q_NST * SLOT;
     const uint32_t ring = (uint32_t)__cvta_generic_to_shared(ring_ptr);
+    auto unit_groups = [&](int i, int* ga, int* gb) {
+        if constexpr (NM == 2) {
+            *ga = *gb = g0 + warp + Q_WARPS * i;
+        } else {
+            *ga = g0 + 2 * (warp + Q_WARPS * i);
+            *gb = *ga + 1 < g1 ? *ga + 1 : -1;
+        }
+    };
     int issued = 0;
     auto issue_next = [&]() {
         const uint32_t slot = ring + (issued & (Q_NST - 1)) * SLOT;
         if (issued < nmine) {
-            const int g = g0 + warp + Q_WARPS * issued;
-            const size_t off = ((size_t)g * p.nsteps + q) * TL::BYTES;
-            copy_unit<TL::CHUNKS>(slot, p.tiles[0] + off, lane);
-            if constexpr (NM == 2) copy_unit<TL::CHUNKS>(slot + TL::BYTES, p.tiles[1] + off, lane);
+            int ga, gb;
+            unit_groups(issued, &ga, &gb);
+            copy_unit<TL::CHUNKS>(slot, p.tiles[0] + ((size_t)ga * p.nsteps + q) * TL::BYTES, lane);
+            if (gb >= 0)
+                copy_unit<TL::CHUNKS>(slot + TL::BYTES, p.tiles[NM - 1] + ((size_t)gb * p.nsteps + q) * TL::BYTES, lane);
         }
         cp_commit();
         ++issued;
@@ -754,10 +796,11 @@ __global__ void __launch_bounds__(Q_THREADS, 1) gemv_nq_kernel(const NQParams p)
     float ss[B];
 #pragma unroll
     for (int b = 0; b < B; ++b) ss[b] = 0.f;
-    for (int idx = tid; idx < B * 32 * 8; idx += Q_THREADS) {
-        const int b = idx / 256, r = idx - b * 256, jl = r >> 3, q4 = r & 7;
+    for (int idx = tid; idx < 8 * 32 * 8; idx += Q_THREADS) {
+        // 8 consecutive lanes hold the 8 float4 of one (batch row, block)
+        const int b = idx >> 8, r = idx & 255, jl = r >> 3, q4 = r & 7;
         float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (jl < nbl) {
+        if (b < B && jl < nbl) {
             const size_t off = (size_t)b * p.a.x_stride + (size_t)(jb + jl) * 32 + q4 * 4;
             if constexpr (PRO == Pro::Plain) {
                 o = *reinterpret_cast<const float4*>(p.a.x + off);
@@ -775,7 +818,17 @@ __global__ void __launch_bounds__(Q_THREADS, 1) gemv_nq_kernel(const NQParams p)
                 o = make_float4(__fmul_rn(t.x, g.x), __fmul_rn(t.y, g.y), __fmul_rn(t.z, g.z), __fmul_rn(t.w, g.w));
             }
         }
-        *reinterpret_cast<float4*>(xs + ((size_t)b * 32 + jl) * XPAD + q4 * 4) = o;
+        float bs = (o.x + o.y) + (o.z + o.w);
+        bs += __shfl_xor_sync(0xffffffffu, bs, 1);
+        bs += __shfl_xor_sync(0xffffffffu, bs, 2);
+        bs += __shfl_xor_sync(0xffffffffu, bs, 4);
+        float* dst = xs + (size_t)jl * QX + q4 * 4 * 8 + b;
+        const int e0 = q4 * 4;
+        dst[0] = __fmul_rn(o.x, exp2_i(kXExp - x_shift_dn<QT>(e0)));
+        dst[8] = __fmul_rn(o.y, exp2_i(kXExp - x_shift_dn<QT>(e0 + 1)));
+        dst[16] = __fmul_rn(o.z, exp2_i(kXExp - x_shift_dn<QT>(e0 + 2)));
+        dst[24] = __fmul_rn(o.w, exp2_i(kXExp - x_shift_dn<QT>(e0 + 3)));
+        if (q4 == 0) xs[(size_t)jl * QX + 256 + b] = __fmul_rn(bs, exp2_i(kXExp - 149));
     }
     if constexpr (PRO == Pro::AddNorm) {
         __shared__ float s_ss[Q_WARPS][B];
@@ -794,40 +847,91 @@ __global__ void __launch_bounds__(Q_THREADS, 1) gemv_nq_kernel(const NQParams p)
     }
     __syncthreads();
 
+    const float* xj = xs + (size_t)lane * QX;  // this lane's block
+    const float offs = (QT == AT_GGML_Q4_0) ? -8.f : -128.f;
     for (int t = 0; t < nmine; ++t) {
         while (issued < t + Q_NST) issue_next();
         cp_wait<Q_NST - 1>();
         __syncwarp();
         const uint8_t* sp = ring_ptr + (t & (Q_NST - 1)) * SLOT;
-        const int g = g0 + warp + Q_WARPS * t;
-        float* dst = p.part + ((size_t)q * p.ngroups + g) * (32 * NM);
+        int ga, gb;
+        unit_groups(t, &ga, &gb);
+        float2 acc[8][BP];
 #pragma unroll
-        for (int m = 0; m < NM; ++m) {  // one matrix at a time keeps 32 partial values live
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+            for (int k = 0; k < BP; ++k) acc[r][k] = f2(0.f, 0.f);
+        float dsc[8];
+        if (lane < nbl) {
+            // row r: tile r / 4, row r % 4 of it
+            const uint8_t* qlane = sp + 256 + lane * QB;
+            const uint8_t* dlane = sp + lane * 2;
+#pragma unroll
+            for (int r = 0; r < 8; ++r)
+                dsc[r] = __fmul_rn(fp16_ftz_fast(*reinterpret_cast<const uint16_t*>(
+                                       dlane + (r >> 2) * TL::BYTES + (r & 3) * 64)),
+                                   kDnUnscale);
+            uint4 qv[8];  // Q4_0: a row's 16 quant bytes; Q8_0: 16 of its 32
+#pragma unroll
+            for (int kc = 0; kc < 8; ++kc) {
+                if (kc == 0 || (QT == AT_GGML_Q8_0 && kc == 4)) {
+#pragma unroll
+                    for (int r = 0; r < 8; ++r)
+                        qv[r] = *reinterpret_cast<const uint4*>(qlane + (r >> 2) * TL::BYTES + (r & 3) * 32 * QB +
+                                                                (kc == 4 ? 16 : 0));
+                }
+                float2 xp[4][BP];
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const float4 x0 = *reinterpret_cast<const float4*>(xj + (4 * kc + kk) * 8);
+                    xp[kk][0] = f2(x0.x, x0.y);
+                    if constexpr (BP > 1) xp[kk][1] = f2(x0.z, x0.w);
+                    if constexpr (BP > 2) {
+                        const float4 x1 = *reinterpret_cast<const float4*>(xj + (4 * kc + kk) * 8 + 4);
+                        xp[kk][2] = f2(x1.x, x1.y);
+                        if constexpr (BP > 3) xp[kk][3] = f2(x1.z, x1.w);
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    const int word = (QT == AT_GGML_Q4_0) ? (kc >> 1) : (kc & 3);
+                    const uint32_t w = word == 0 ? qv[r].x : word == 1 ? qv[r].y : word == 2 ? qv[r].z : qv[r].w;
+                    float f[4];
+                    q4_fields_dn<QT>(w, kc, f);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const float2 w2 = f2(f[kk], f[kk]);
+#pragma unroll
+                        for (int k = 0; k < BP; ++k) acc[r][k] = __ffma2_rn(w2, xp[kk][k], acc[r][k]);
+                    }
+                }
+            }
+        }
+        // block results: d * (sum - offset * block sum of x), per matrix / group tile
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
             float v[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = 0.f;
             if (lane < nbl) {
-                uint4 qv[4][NV];
-                float dsc[4];
-                const uint8_t* tb = sp + m * TL::BYTES;
+                const float4 sxa = *reinterpret_cast<const float4*>(xj + 256);
+                const float4 sxb = *reinterpret_cast<const float4*>(xj + 260);
+                const float sx[8] = {sxa.x, sxa.y, sxa.z, sxa.w, sxb.x, sxb.y, sxb.z, sxb.w};
 #pragma unroll
-                for (int r = 0; r < 4; ++r) {
+                for (int r = 0; r < 4; ++r)
 #pragma unroll
-                    for (int vv = 0; vv < NV; ++vv)
-                        qv[r][vv] = *reinterpret_cast<const uint4*>(tb + 256 + (r * 32 + lane) * TL::QB + 16 * vv);
-                    dsc[r] = fp16_ftz_fast(*reinterpret_cast<const uint16_t*>(tb + (r * 32 + lane) * 2));
-                }
-#pragma unroll
-                for (int b = 0; b < B; ++b) {
-                    const float4* xv = reinterpret_cast<const float4*>(xs + ((size_t)b * 32 + lane) * XPAD);
-                    float4 xr[8];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) xr[k] = xv[k];
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) v[r * B + b] = __fmul_rn(dsc[r], dot32<QT>(qv[r], xr));
-                }
+                    for (int b = 0; b < B; ++b) {
+                        const float2 a2 = acc[4 * m + r][b >> 1];
+                        v[r * nq_stride(B) + b] = __fmul_rn(dsc[4 * m + r], fmaf(offs, sx[b], (b & 1) ? a2.y : a2.x));
+                    }
             }
-            dst[32 * m + lane] = lane_transpose_sum(v, lane);
+            const float tot = lane_transpose_sum(v, lane);
+            if constexpr (NM == 2) {
+                p.part[((size_t)q * p.ngroups + ga) * 64 + 32 * m + lane] = tot;
+            } else {
+                const int g = m ? gb : ga;
+                if (g >= 0) p.part[((size_t)q * p.ngroups + g) * 32 + lane] = tot;
+            }
         }
         __syncwarp();  // every lane is done with this slot before it is refilled
     }
@@ -864,7 +968,7 @@ __global__ void __launch_bounds__(256) gemv_nq_reduce_kernel(const NQParams p) {
         for (int q = 0; q < p.nsteps; ++q) {
             const float* src = p.part + ((size_t)q * p.ngroups + g) * (32 * NM);
 #pragma unroll
-            for (int m = 0; m < NM; ++m) v[m] += src[32 * m + r * B + b];
+            for (int m = 0; m < NM; ++m) v[m] += src[32 * m + r * nq_stride(B) + b];
         }
         const float inv = s_inv[b];
         p.a.y[(size_t)b * p.a.y_stride + row] = n_epilogue<EPI>(__fmul_rn(v[0], inv), __fmul_rn(v[NM - 1], inv));
@@ -1099,6 +1203,69 @@ __device__ __forceinline__ void t_store(const GemvArgs& a, float val, int j, int
             cache[(size_t)b * a.kv_slot_stride + ((size_t)kvh * a.ctx_len + pos) * hd + dd] = out;
         }
     }
+}
+
+// The common end of the T kernels: the RMSNorm scale of a folded AddNorm
+// (per-warp sums of squares in s_red), the normed residual slice, the CTA's
+// partial per (batch row, column) from red[warp][b][col], the combine over the
+// CTAs splitting the rows (cluster shared memory or scratch and counters),
+// and the epilogue store.
+template <int B, Epi EPI>
+__device__ __forceinline__ void t_tail(const TParams& p, float (*red)[B][32], const float* s_red, float* s_inv,
+                                       bool fold, int* s_last, const XoutStash* s_xo, int c, int s) {
+    if (fold && threadIdx.x < B) {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) t += s_red[w * B + threadIdx.x];
+        s_inv[threadIdx.x] = rms_inv(t, p.E, p.a.eps);
+    }
+    __syncthreads();
+    if (fold) write_xout_stashed<B, THREADS>(p.a, p.E, s_inv, blockIdx.x, gridDim.x, s_xo);
+
+    // CTA partial for (block column c, rows [e_lo, e_hi)): thread (b = warp, col = lane)
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float val = 0.f;
+    const int b_me = warp, cl = lane;
+    if (b_me < B) {
+#pragma unroll
+        for (int w = 0; w < 8; ++w) val += red[w][b_me][cl];
+    }
+    if (p.S > 1 && p.cluster) {
+        // The S CTAs of block column c form one cluster (rank = s): rank 0
+        // sums the partials in split order from its peers' shared memory.
+        namespace cg = cooperative_groups;
+        cg::cluster_group cluster = cg::this_cluster();
+        if (b_me < B) red[0][b_me][cl] = val;  // each (b_me, cl) slot is read above only by this thread
+        cluster.sync();
+        if (s == 0 && b_me < B) {
+            val = 0.f;
+            for (int k = 0; k < p.S; ++k) val += cluster.map_shared_rank(&red[0][0][0], k)[b_me * 32 + cl];
+        }
+        cluster.sync();  // peers keep their shared memory until rank 0 has read it
+        if (s != 0) return;
+    } else if (p.S > 1) {
+        if (b_me < B) p.a.scratch[(((size_t)c * p.S + s) * B + b_me) * 32 + cl] = val;
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            const unsigned prev = atomicAdd(&p.a.counters[c], 1u);
+            *s_last = (prev == (unsigned)(p.S - 1));
+        }
+        __syncthreads();
+        if (!*s_last) return;
+        __threadfence();
+        if (b_me < B) {
+            val = 0.f;
+            for (int k = 0; k < p.S; ++k)
+                val += __ldcg(&p.a.scratch[(((size_t)c * p.S + k) * B + b_me) * 32 + cl]);
+        }
+        if (tid == 0) p.a.counters[c] = 0u;
+    }
+    if (b_me >= B) return;
+    if (fold) val = __fmul_rn(val, s_inv[b_me]);
+
+    const int j = c * 32 + cl;
+    t_store<EPI>(p.a, val, j, b_me, EPI == Epi::QkvRope ? rope_coef(p.a, j, b_me) : f2(1.f, 0.f));
 }
 
 template <int QT, int B, Pro PRO, Epi EPI>
@@ -1387,56 +1554,276 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_t_kernel(const TParams p) {
         const int colx = (CPL == 32) ? lane : (8 * quarter + (lane >> 2));
         red[warp][b][colx] = v[0];
     }
-    if (fold && tid < B) {
-        float t = 0.f;
+    t_tail<B, EPI>(p, red, s_red, s_inv, fold, &s_last, &s_xo, c, s);
+}
+
+// ---------------------------------------------------------------------------
+// Orientation T, batch 3..8
+// ---------------------------------------------------------------------------
+// CTA (block column c, rows [e_lo, e_hi)) stages x of its rows as [row][8]
+// (batch rows b < B, times 2^kXExp; padding zero) and its 8 warps stream the
+// column's 32-row tiles round robin through per-warp cp.async rings of whole
+// tiles (576 or 1088 contiguous bytes, TB_NST deep). Lane (rs = lane / 4,
+// quarter = lane % 4) takes rows rs, rs + 8, rs + 16, rs + 24 of a tile and
+// columns 8 quarter .. 8 quarter + 7: each row's 8 weights are decoded once in
+// the subnormal-scaled form (one mask per weight) and applied to all B rows of
+// x by FFMA2 with d * x broadcast into a pair, so the decode is shared by the
+// batch and every staged x value read serves 8 columns. The offset (8 or
+// 128) times the lane's sum of d * x and the per-column power of two are
+// applied once per column; the 8 lanes sharing a quarter combine by a
+// butterfly reduce-scatter, the warps and the row splits as in the batch <= 2
+// kernel (t_tail).
+constexpr int TB_NST = 4;
+
+template <int QT>
+__device__ __forceinline__ void tq_decode_dn(const uint8_t* qp, float2* wv) {
+    if constexpr (QT == AT_GGML_Q4_0) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(qp), t = w >> 24;  // columns 0..7 of the quarter
+        wv[0] = f2(bits_f(w & 0xFu), bits_f(w & 0xF0u));
+        wv[1] = f2(bits_f(w & 0xF00u), bits_f(w & 0xF000u));
+        wv[2] = f2(bits_f(w & 0xF0000u), bits_f(w & 0xF00000u));
+        wv[3] = f2(bits_f(t & 0xFu), bits_f(t & 0xF0u));
+    } else {
+        const uint2 u = *reinterpret_cast<const uint2*>(qp);
+        wv[0] = f2(bits_f((u.x ^ 0x80u) & 0xFFu), bits_f((u.x ^ 0x8000u) & 0xFF00u));
+        wv[1] = f2(bits_f((u.x ^ 0x800000u) & 0xFF0000u), bits_f((u.x >> 24) ^ 0x80u));
+        wv[2] = f2(bits_f((u.y ^ 0x80u) & 0xFFu), bits_f((u.y ^ 0x8000u) & 0xFF00u));
+        wv[3] = f2(bits_f((u.y ^ 0x800000u) & 0xFF0000u), bits_f((u.y >> 24) ^ 0x80u));
+    }
+}
+
+template <int QT, int B, Pro PRO, Epi EPI>
+__global__ void __launch_bounds__(THREADS, 2) gemv_tb_kernel(const TParams p) {
+    constexpr int QB = QTraits<QT>::QB;
+    constexpr int TBYTES = 64 + 32 * QB;
+    constexpr int TCH = TBYTES / 16;
+    constexpr bool fold = PRO == Pro::AddNorm;
+    static_assert(B >= 3 && B <= 8, "batch 3..8");
+    extern __shared__ __align__(16) float xs[];  // [rows of the split, padded to tiles][8], then the rings
+    __shared__ float red[8][B][32];
+    __shared__ float s_red[8 * B];
+    __shared__ float s_inv[B];
+    __shared__ int s_last;
+
+    pdl_trigger();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c = blockIdx.x / p.S, s = blockIdx.x - (blockIdx.x / p.S) * p.S;
+    const int e_lo = s * p.e_per_split;
+    const int e_hi = min(p.E, e_lo + p.e_per_split);
+    const int ne = e_hi - e_lo;
+    const int nt = (ne + 31) >> 5;
+    const int nmine = (nt - warp + 7) >> 3;  // this warp's tiles: warp + 8 i
+    const uint8_t* col = p.tiles + ((size_t)c * p.ngroups + (e_lo >> 5)) * TBYTES;
+    const uint8_t* ring_ptr = reinterpret_cast<const uint8_t*>(xs) + p.ring_off + warp * TB_NST * TBYTES;
+    const uint32_t ring = (uint32_t)__cvta_generic_to_shared(ring_ptr);
+    int issued = 0;
+    auto issue_next = [&]() {
+        if (issued < nmine)
+            copy_unit<TCH>(ring + (issued & (TB_NST - 1)) * TBYTES, col + (size_t)(warp + 8 * issued) * TBYTES, lane);
+        cp_commit();
+        ++issued;
+    };
+    // weights are never written by earlier kernels: the first tiles start before the wait
+    for (int k = 0; k < TB_NST - 1; ++k) issue_next();
+    pdl_wait();
+
+    // The split's rows of x (Plain) or of t * gamma, t = xin + yin (AddNorm:
+    // the RMSNorm is folded, 1/rms multiplies the finished column sums; this
+    // CTA's sums of t^2 over its rows are combined over the splits at the
+    // end), times 2^kXExp; the padding (rows past the split, b >= B) is zero.
+    const float xsc = exp2_i(kXExp);
+    for (int idx = tid; idx < nt * 32 * 8; idx += THREADS) {
+        const int i = idx >> 3, b = idx & 7;
+        if (i >= ne || b >= B) xs[idx] = 0.f;
+    }
+    {
+        const int n4 = ne >> 2;
+        float ss[B];
 #pragma unroll
-        for (int w = 0; w < 8; ++w) t += s_red[w * B + tid];
-        s_inv[tid] = rms_inv(t, p.E, p.a.eps);
+        for (int b = 0; b < B; ++b) ss[b] = 0.f;
+        for (int base = 0; base < B * n4; base += THREADS * 4) {
+            float4 v[4], gv[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int idx = base + k * THREADS + tid;
+                if (idx < B * n4) {
+                    const int bb = idx / n4, e = e_lo + 4 * (idx - bb * n4);
+                    const size_t off = (size_t)bb * p.a.x_stride + e;
+                    if constexpr (PRO == Pro::Plain) {
+                        v[k] = *reinterpret_cast<const float4*>(p.a.x + off);
+                    } else {
+                        float4 t = *reinterpret_cast<const float4*>(p.a.xin + off);
+                        if (p.a.yin) {
+                            const float4 u = *reinterpret_cast<const float4*>(p.a.yin + off);
+                            t.x = __fadd_rn(t.x, u.x); t.y = __fadd_rn(t.y, u.y);
+                            t.z = __fadd_rn(t.z, u.z); t.w = __fadd_rn(t.w, u.w);
+                        }
+                        v[k] = t;
+                        gv[k] = *reinterpret_cast<const float4*>(p.a.gamma + e);
+                    }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int idx = base + k * THREADS + tid;
+                if (idx < B * n4) {
+                    const int bb = idx / n4, i = 4 * (idx - bb * n4);
+                    float4 o = v[k];
+                    if constexpr (fold) {
+                        const float q = fmaf(o.x, o.x, fmaf(o.y, o.y, fmaf(o.z, o.z, __fmul_rn(o.w, o.w))));
+#pragma unroll
+                        for (int b = 0; b < B; ++b)
+                            if (b == bb) ss[b] += q;
+                        const float4 g = gv[k];
+                        o = make_float4(__fmul_rn(o.x, g.x), __fmul_rn(o.y, g.y), __fmul_rn(o.z, g.z),
+                                        __fmul_rn(o.w, g.w));
+                    }
+                    float* dst = xs + (size_t)i * 8 + bb;
+                    dst[0] = __fmul_rn(o.x, xsc);
+                    dst[8] = __fmul_rn(o.y, xsc);
+                    dst[16] = __fmul_rn(o.z, xsc);
+                    dst[24] = __fmul_rn(o.w, xsc);
+                }
+            }
+        }
+        if constexpr (fold) {
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                const float t = warp_sum(ss[b]);
+                if (lane == 0) s_red[warp * B + b] = t;
+            }
+        }
     }
     __syncthreads();
-    if (fold) write_xout_stashed<B, THREADS>(p.a, p.E, s_inv, blockIdx.x, gridDim.x, &s_xo);
 
-    // CTA partial for (block column c, rows [e_lo, e_hi)): thread (b = warp, col = lane)
-    float val = 0.f;
+    const int qtr = lane & 3, rs = lane >> 2;
+    float2 acc[B][4];
+    float dsum[B];  // this lane's sum of d * x * 2^kXExp (offset correction)
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+        dsum[b] = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[b][k] = f2(0.f, 0.f);
+    }
+    for (int t = 0; t < nmine; ++t) {
+        issue_next();  // refills the slot read in step t - 1 with tile t + TB_NST - 1
+        cp_wait<TB_NST - 1>();
+        __syncwarp();  // every lane's pieces of tile t have landed
+        const uint8_t* sp = ring_ptr + (t & (TB_NST - 1)) * TBYTES;
+        const int row0 = (warp + 8 * t) * 32;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int l = rs + 8 * i;
+            const int ir = row0 + l;
+            if (ir < ne) {
+                const float d = fp16_ftz_fast(*reinterpret_cast<const uint16_t*>(sp + 2 * l));
+                float2 wv[4];
+                tq_decode_dn<QT>(sp + 64 + l * QB + qtr * (QB / 4), wv);
+                const float4 xa = *reinterpret_cast<const float4*>(xs + (size_t)ir * 8);
+                const float4 xb = *reinterpret_cast<const float4*>(xs + (size_t)ir * 8 + 4);
+                const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+                for (int b = 0; b < B; ++b) {
+                    const float sv = __fmul_rn(d, xv[b]);
+                    dsum[b] += sv;
+                    const float2 s2 = f2(sv, sv);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) acc[b][k] = __ffma2_rn(wv[k], s2, acc[b][k]);
+                }
+            }
+        }
+        __syncwarp();  // every lane is done with this slot before it is refilled
+    }
+    cp_wait<0>();
+
+    const float offs = (QT == AT_GGML_Q4_0) ? -8.f : -128.f;
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+        const float corr = __fmul_rn(offs, __fmul_rn(dsum[b], exp2_i(-kXExp)));
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            v[2 * k] = fmaf(acc[b][k].x, exp2_i(149 - kXExp - x_shift_dn<QT>(2 * k)), corr);
+            v[2 * k + 1] = fmaf(acc[b][k].y, exp2_i(149 - kXExp - x_shift_dn<QT>(2 * k + 1)), corr);
+        }
+        // reduce-scatter over the lanes of a quarter (lane bits 4, 8, 16): lane
+        // (rs, quarter) ends with column 8 quarter + rs
+        int n = 8;
+#pragma unroll
+        for (int bit = 16; bit >= 4; bit >>= 1) {
+            const bool upper = (lane & bit) != 0;
+            n >>= 1;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                if (t < n) {
+                    const float send = upper ? v[t] : v[t + n];
+                    const float keep = upper ? v[t + n] : v[t];
+                    v[t] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+                }
+            }
+        }
+        red[warp][b][8 * qtr + rs] = v[0];
+    }
+    __syncthreads();
+
+    // CTA partial for (block column c, rows [e_lo, e_hi)): thread (b = warp,
+    // col = lane), plus (lane 0) the CTA's sum of t^2 of batch row b
     const int b_me = warp, cl = lane;
+    float val = 0.f, ssq = 0.f;
     if (b_me < B) {
 #pragma unroll
         for (int w = 0; w < 8; ++w) val += red[w][b_me][cl];
-    }
-    if (p.S > 1 && p.cluster) {
-        // The S CTAs of block column c form one cluster (rank = s): rank 0
-        // sums the partials in split order from its peers' shared memory.
-        namespace cg = cooperative_groups;
-        cg::cluster_group cluster = cg::this_cluster();
-        if (b_me < B) red[0][b_me][cl] = val;  // each (b_me, cl) slot is read above only by this thread
-        cluster.sync();
-        if (s == 0 && b_me < B) {
-            val = 0.f;
-            for (int k = 0; k < p.S; ++k) val += cluster.map_shared_rank(&red[0][0][0], k)[b_me * 32 + cl];
+        if (fold) {
+#pragma unroll
+            for (int w = 0; w < 8; ++w) ssq += s_red[w * B + b_me];
         }
-        cluster.sync();  // peers keep their shared memory until rank 0 has read it
-        if (s != 0) return;
-    } else if (p.S > 1) {
-        if (b_me < B) p.a.scratch[(((size_t)c * p.S + s) * B + b_me) * 32 + cl] = val;
+    }
+    if (p.S > 1) {
+        // splits in scratch [c][S][B][33] (32 column values, then the sum of
+        // squares); the last CTA to arrive sums them in split order
+        float* part = p.a.scratch + (size_t)c * p.S * B * 33;
+        if (b_me < B) {
+            part[((size_t)s * B + b_me) * 33 + cl] = val;
+            if (cl == 0) part[((size_t)s * B + b_me) * 33 + 32] = ssq;
+        }
         __threadfence();
         __syncthreads();
-        if (tid == 0) {
-            const unsigned prev = atomicAdd(&p.a.counters[c], 1u);
-            s_last = (prev == (unsigned)(p.S - 1));
-        }
+        if (tid == 0) s_last = atomicAdd(&p.a.counters[c], 1u) == (unsigned)(p.S - 1);
         __syncthreads();
         if (!s_last) return;
         __threadfence();
         if (b_me < B) {
             val = 0.f;
-            for (int k = 0; k < p.S; ++k)
-                val += __ldcg(&p.a.scratch[(((size_t)c * p.S + k) * B + b_me) * 32 + cl]);
+            ssq = 0.f;
+            for (int k = 0; k < p.S; ++k) {
+                val += __ldcg(&part[((size_t)k * B + b_me) * 33 + cl]);
+                ssq += __ldcg(&part[((size_t)k * B + b_me) * 33 + 32]);
+            }
         }
         if (tid == 0) p.a.counters[c] = 0u;
     }
+    if (fold) {
+        if (b_me < B && cl == 0) s_inv[b_me] = rms_inv(ssq, p.E, p.a.eps);
+        __syncthreads();
+        // the normed residual stream: rows [c E / n_bc, (c + 1) E / n_bc) of every batch row
+        const int n4 = p.E >> 2;
+        const int i0 = (int)((int64_t)c * n4 / p.n_bc), i1 = (int)((int64_t)(c + 1) * n4 / p.n_bc);
+        for (int idx = tid; idx < B * (i1 - i0); idx += THREADS) {
+            const int bb = idx / (i1 - i0), i4 = i0 + idx - bb * (i1 - i0);
+            const size_t off = (size_t)bb * p.a.x_stride + (size_t)i4 * 4;
+            float4 t = *reinterpret_cast<const float4*>(p.a.xin + off);
+            if (p.a.yin) {
+                const float4 u = *reinterpret_cast<const float4*>(p.a.yin + off);
+                t.x = __fadd_rn(t.x, u.x); t.y = __fadd_rn(t.y, u.y); t.z = __fadd_rn(t.z, u.z); t.w = __fadd_rn(t.w, u.w);
+            }
+            const float4 g = *reinterpret_cast<const float4*>(p.a.gamma + (size_t)i4 * 4);
+            const float inv = s_inv[bb];
+            *reinterpret_cast<float4*>(p.a.xout + off) = make_float4(
+                norm_apply(t.x, inv, g.x), norm_apply(t.y, inv, g.y), norm_apply(t.z, inv, g.z), norm_apply(t.w, inv, g.w));
+        }
+        if (b_me < B) val = __fmul_rn(val, s_inv[b_me]);
+    }
     if (b_me >= B) return;
-    if (fold) val = __fmul_rn(val, s_inv[b_me]);
-
     const int j = c * 32 + cl;
     t_store<EPI>(p.a, val, j, b_me, EPI == Epi::QkvRope ? rope_coef(p.a, j, b_me) : f2(1.f, 0.f));
 }
@@ -1583,7 +1970,10 @@ struct NQLayout {
 NQLayout nq_layout(const at_qmat* m, int batch, int num_sms, int nm) {
     NQLayout l;
     const int64_t steps = m->nsteps;
-    l.P = (int)std::max<int64_t>(1, std::min<int64_t>(m->ngroups, (num_sms + steps - 1) / steps));
+    // CTAs per SM from the shared memory (x of one step + two-tile rings)
+    const int smem = 32 * QX * 4 + Q_WARPS * Q_NST * 2 * (4 * 32 * (2 + quant_bytes(m->type)));
+    const int occ = std::max(1, std::min(2, (227 * 1024) / (smem + 4 * 1024)));
+    l.P = (int)std::max<int64_t>(1, std::min<int64_t>(m->ngroups, (occ * num_sms + steps - 1) / steps));
     l.part_floats = (size_t)steps * m->ngroups * 32 * nm;  // one 32-value partial per matrix and group
     l.ssq_floats = (size_t)l.P * steps * batch;
     return l;
@@ -1604,7 +1994,7 @@ void run_nq(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, bo
     p.part = a.scratch;
     p.ssq = a.scratch + l.part_floats;
     p.a = a;
-    const int smem = B * 32 * XPAD * 4 + Q_WARPS * Q_NST * NM * NTile<QT>::BYTES;
+    const int smem = 32 * QX * 4 + Q_WARPS * Q_NST * 2 * NTile<QT>::BYTES;
     const void* fn = reinterpret_cast<const void*>(&gemv_nq_kernel<QT, B, PRO, EPI>);
     ensure_smem(fn, smem);
     cudaLaunchConfig_t cfg = {};
@@ -1673,8 +2063,72 @@ void t_config(const at_qmat* m, int batch, int num_sms, int* S, int* eps_rows) {
     *S = (E + per - 1) / per;
 }
 
+// Row splits of the batch 3..8 T kernel: the S that keeps the most SM slots
+// busy over whole waves (ties: the fewer CTAs), each split at least one tile
+// per warp. CTAs per SM from the shared memory (two at most: 256 threads of
+// up to 128 registers).
+constexpr int kTbMaxSplits = 16;
+bool tb_plan(int qtype, int64_t E, int64_t n_bc, int num_sms, int* S_out, int* rows_out) {
+    const int tbytes = 64 + 32 * quant_bytes(qtype);
+    const int ring_bytes = 8 * TB_NST * tbytes;
+    const int ntiles = (int)((E + 31) / 32);
+    int best_S = 0, best_rows = 0;
+    double best_eff = -1.0;
+    for (int S = 1; S <= kTbMaxSplits; ++S) {
+        const int tiles_per = (ntiles + S - 1) / S;
+        if (S > 1 && tiles_per < 8) break;
+        const int rows = tiles_per * 32;
+        const int smem = rows * 32 + ring_bytes;
+        if (smem > 200 * 1024) continue;
+        const int occ = std::max(1, std::min(2, (227 * 1024) / (smem + 12 * 1024)));
+        const int slots = num_sms * occ;
+        const int Sx = (ntiles + tiles_per - 1) / tiles_per;
+        const int64_t ctas = n_bc * Sx;
+        const int64_t waves = (ctas + slots - 1) / slots;
+        const double eff = (double)ctas / ((double)waves * slots);
+        if (eff > best_eff + 0.02) {
+            best_eff = eff;
+            best_S = Sx;
+            best_rows = rows;
+        }
+    }
+    *S_out = best_S;
+    *rows_out = best_rows;
+    return best_S > 0;
+}
+
+// The batch 3..8 T kernel applies when the rows are 16-byte aligned.
+bool tb_applies(const at_qmat* m, int x_stride) {
+    return m->tile_bytes == 64 + 32 * quant_bytes(m->type) && (m->rows & 3) == 0 && (x_stride & 3) == 0;
+}
+
+template <int QT, int B, Pro PRO, Epi EPI>
+bool run_tb(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, bool pdl) {
+    constexpr int TBYTES = 64 + 32 * QTraits<QT>::QB;
+    if (!tb_applies(m, a.x_stride)) return false;
+    TParams p{};
+    if (!tb_plan(m->type, m->rows, m->cols / QK, num_sms, &p.S, &p.e_per_split)) return false;
+    p.tiles = m->tiles;
+    p.tile_bytes = m->tile_bytes;
+    p.E = (int)m->rows;
+    p.ngroups = (int)m->ngroups;
+    p.n_bc = (int)(m->cols / QK);
+    p.cluster = 0;
+    p.a = a;
+    if (p.S > 1) AT_REQUIRE(a.scratch && a.counters, AT_ERR_STATE, "T GEMV needs split scratch");
+    p.ring_off = p.e_per_split * 32;
+    const int smem = p.ring_off + 8 * TB_NST * TBYTES;
+    const void* fn = reinterpret_cast<const void*>(&gemv_tb_kernel<QT, B, PRO, EPI>);
+    ensure_smem(fn, smem);
+    launch(fn, p.n_bc * p.S, smem, s, pdl, p, THREADS, 1);
+    return true;
+}
+
 template <int QT, int B, Pro PRO, Epi EPI>
 void run_t(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, bool pdl) {
+    if constexpr (B >= 3) {
+        if (run_tb<QT, B, PRO, EPI>(m, a, num_sms, s, pdl)) return;
+    }
     TParams p{};
     p.tiles = m->tiles;
     p.tile_bytes = m->tile_bytes;
@@ -1729,6 +2183,12 @@ void gemv_t_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* float
     const bool global_split = S > 1 && (S > 8 || batch > 2);
     *floats = global_split ? n_bc * S * batch * 32 : 0;
     *counters = global_split ? n_bc : 0;
+    // batch 3..8 with row-aligned x runs the tile-ring kernel, whose split may differ
+    int S2 = 0, per2 = 0;
+    if (batch > 2 && tb_plan(m->type, m->rows, m->cols / QK, num_sms, &S2, &per2) && S2 > 1) {
+        *floats = std::max(*floats, n_bc * S2 * batch * 33);
+        *counters = n_bc;
+    }
 }
 
 void gemv_n_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* floats, size_t* counters) {

@@ -8,6 +8,7 @@ time per call (µs) and the algorithmic bytes (weights + x + y) per second.
     python -m auratensor_b200.sweep                         # Q4_0/Q8_0, batch 1 and 8
     python -m auratensor_b200.sweep --types q4_0 --batch 1
     python -m auratensor_b200.sweep --one 14336 4096 N q4_0 --calls 8   # a few eager calls (for ncu)
+    python -m auratensor_b200.sweep --one 14336 4096 N q8_0 --batch 8  # the same at batch 8
     python -m auratensor_b200.sweep --gemm --types q4_0             # tensor-core prompt GEMM, TFLOP/s
 
 Shapes are (rows, cols) of the stored matrix: orientation N computes
@@ -101,12 +102,12 @@ def time_gemm(qt: int, rows: int, cols: int, orient: int, tokens: int, dev: torc
             "TFLOPs": round(flops / us / 1e6, 1)}
 
 
-def run_one(rows: int, cols: int, orient: int, qt: int, calls: int, dev: torch.device) -> None:
+def run_one(rows: int, cols: int, orient: int, qt: int, calls: int, dev: torch.device, batch: int = 1) -> None:
     """A few eager calls on 4 copies of one matrix (a small case for ncu)."""
     g = torch.Generator(device=dev).manual_seed(0)
     mats = [QMatrix(qt, orient, rows, cols, synth.generate_torch_tensor((rows, cols), qt, g, dev))
             for _ in range(4)]
-    x = torch.randn((1, cols if orient == ORIENT_N else rows), device=dev)
+    x = torch.randn((batch, cols if orient == ORIENT_N else rows), device=dev)
     for i in range(calls):
         mats[i % 4].gemv(x)
     torch.cuda.synchronize()
@@ -132,7 +133,8 @@ def main(argv=None) -> None:
         return
     if args.one:
         rows, cols, o, t = args.one
-        run_one(int(rows), int(cols), ORIENT_N if o.upper() == "N" else ORIENT_T, TYPES[t.lower()], args.calls, dev)
+        run_one(int(rows), int(cols), ORIENT_N if o.upper() == "N" else ORIENT_T, TYPES[t.lower()], args.calls, dev,
+                int(args.batch.split(",")[0]))
         return
     for t in args.types.split(","):
         for rows, cols, orient in SHAPES:
