@@ -62,7 +62,7 @@ class ModelConfig(C.Structure):
     _fields_ = [("context_length", C.c_int64), ("embedding_length", C.c_int64), ("block_count", C.c_int64),
                 ("head_count", C.c_int64), ("head_count_kv", C.c_int64), ("feed_forward_length", C.c_int64),
                 ("vocab_size", C.c_int64), ("rope_freq_base", C.c_float), ("rms_norm_eps", C.c_float),
-                ("max_batch", C.c_int32), ("layout", C.c_int32)]
+                ("max_batch", C.c_int32), ("layout", C.c_int32), ("kv_type", C.c_int32), ("reserved", C.c_int32)]
 
 
 class SamplerConfigC(C.Structure):
@@ -112,7 +112,7 @@ SIGNATURES = {
     "at_model_set_tensor": [_vp, C.c_char_p, _i, _vp, _sz, _i],
     "at_model_finalize": [_vp],
     "at_model_load_gguf": [_vp, C.c_char_p, _i, _PP],
-    "at_model_load_gguf_ex": [_vp, C.c_char_p, _i, _i, _PP],
+    "at_model_load_gguf_ex": [_vp, C.c_char_p, _i, _i, _i, _PP],
     "at_model_get_config": [_vp, C.POINTER(ModelConfig)],
     "at_model_destroy": [_vp],
     "at_model_forward_step": [_vp, _i, _i64, _vp],
@@ -136,6 +136,8 @@ SIGNATURES = {
     "at_model_kv_size": [_vp, _i, C.POINTER(C.c_int64)],
     "at_model_kv_read": [_vp, _i, _i, _i, _i64, _vp, _vp],
     "at_model_kv_reset": [_vp, _i],
+    "at_model_kv_append": [_vp, _i, _i64, _i64, _vp, _vp],
+    "at_model_kv_offset": [_vp, _i64, _i64, _i64, _i64, C.POINTER(C.c_int64)],
     "at_sample": [_vp, _i, _vp, _i, _f, _i, _f, _f, _i64, C.POINTER(C.c_int)],
     "at_tp_unique_id": [_vp],
     "at_ctx_create_tp": [_i, _i, _i, _vp, _PP],

@@ -176,6 +176,10 @@ struct GemvArgs {
     const int64_t* pos = nullptr;      // [B] device
     float* kcache = nullptr;           // [B][L][Hkv][ctx][hd] base of this layer slice
     float* vcache = nullptr;
+    int8_t* kq = nullptr;              // Q8_0 KV cache (kq non-null): quants at the fp32 element
+    int8_t* vq = nullptr;              // index, one fp16 scale per 32 elements
+    uint16_t* ksc = nullptr;
+    uint16_t* vsc = nullptr;
     int64_t kv_slot_stride = 0;        // floats between sequence slots
     int head_dim = 0, n_q_cols = 0, n_kv_cols = 0, ctx_len = 0;
     // T split-K scratch (partials + tile counters)

@@ -1,6 +1,8 @@
 // Device helpers shared by the kernels of libauratensor_cuda.so (sm_100a).
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -130,6 +132,21 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 }
 
 // (x * invRms) * gamma, in that rounding order (core/Kernels.java:145).
+// Q8_0 KV-cache append of one value per lane: the 32 lanes of the (fully
+// active) warp hold the 32 consecutive elements of one block (elem % 32 ==
+// lane). d = max|x| / 127 (fp16, stored once), q = round-half-away(x / d)
+// computed as x * (1 / d) with the fp32 d.
+__device__ __forceinline__ void kv_store_q8(int8_t* q, uint16_t* sc, size_t elem, float v) {
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.f);
+    const float id = d != 0.f ? __fdiv_rn(1.f, d) : 0.f;
+    const float r = roundf(__fmul_rn(v, id));
+    q[elem] = (int8_t)fmaxf(-127.f, fminf(127.f, r));
+    if ((threadIdx.x & 31) == 0) sc[elem >> 5] = __half_as_ushort(__float2half_rn(d));
+}
+
 __device__ __forceinline__ float norm_apply(float x, float inv, float g) {
     return __fmul_rn(__fmul_rn(x, inv), g);
 }

@@ -1199,8 +1199,13 @@ __device__ __forceinline__ void t_store(const GemvArgs& a, float val, int j, int
             const bool is_k = j < nq + nkv;
             const int jj = is_k ? j - nq : j - nq - nkv;
             const int kvh = jj / hd, dd = jj - kvh * hd;
-            float* cache = is_k ? a.kcache : a.vcache;
-            cache[(size_t)b * a.kv_slot_stride + ((size_t)kvh * a.ctx_len + pos) * hd + dd] = out;
+            const size_t e = (size_t)b * a.kv_slot_stride + ((size_t)kvh * a.ctx_len + pos) * hd + dd;
+            if (a.kq) {  // the warp holds one 32-column block (the k / v boundary is block aligned)
+                kv_store_q8(is_k ? a.kq : a.vq, is_k ? a.ksc : a.vsc, e, out);
+            } else {
+                float* cache = is_k ? a.kcache : a.vcache;
+                cache[e] = out;
+            }
         }
     }
 }

@@ -147,14 +147,28 @@ __device__ __forceinline__ void cp_async16_smem(void* smem, const void* g) {
 constexpr size_t attn_smem_bytes(int hd, int chk) { return (size_t)chk * (hd / 4 + 2 + hd / 4) * 16; }
 constexpr int kAttnClusterChunk = 64;  // positions per CTA of the cluster-merged decode attention
 
-template <int HD, int MODE = 0, int CHK = CH>
+// Four K or V elements of a Q8_0 KV cache row chunk (float4 index i of the
+// chunk starting at quant pointer qb, scales sb of the same elements / 32).
+__device__ __forceinline__ float4 kv_dq4(const int8_t* __restrict__ qb, const uint16_t* __restrict__ sb, int i) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(qb + 4 * (size_t)i);
+    const float d = fp16_ftz_fast(sb[i >> 3]);
+    return make_float4(__fmul_rn((float)(int8_t)(w & 0xFFu), d), __fmul_rn((float)(int8_t)((w >> 8) & 0xFFu), d),
+                       __fmul_rn((float)(int8_t)((w >> 16) & 0xFFu), d), __fmul_rn((float)(int8_t)(w >> 24), d));
+}
+
+// KVQ: kc / vc are the int8 quants of a Q8_0 KV cache (same element index)
+// and ksc / vsc its fp16 scales; the chunk's rows are dequantized into the
+// same shared-memory rows the fp32 cache is copied into.
+template <int HD, int MODE = 0, int CHK = CH, bool KVQ = false>
 __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict__ q, const float* __restrict__ kc,
                                                          const float* __restrict__ vc,
                                                          const int64_t* __restrict__ pos, float* __restrict__ part,
                                                          int Hl, int Hkvl, int ctx, int64_t slot_stride,
                                                          int nchunk_max, float scale,
                                                          unsigned* __restrict__ cnt = nullptr,
-                                                         float* __restrict__ att = nullptr) {
+                                                         float* __restrict__ att = nullptr,
+                                                         const uint16_t* __restrict__ ksc = nullptr,
+                                                         const uint16_t* __restrict__ vsc = nullptr) {
     constexpr int G_MAX = 8;
     constexpr int F4 = HD / 4;  // float4 per row
     // K rows padded by two float4: the 8 lanes of a quarter-warp (4 rows x 2
@@ -195,19 +209,37 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float* __restrict
     if (active) {
     const int n = (int)((P - p0) < CHK ? (P - p0) : CHK);
     const int n_past = (p0 + n == P) ? n - 1 : n;
-    const float4* kbase = reinterpret_cast<const float4*>(kc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD);
-    const float4* vbase = reinterpret_cast<const float4*>(vc + (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD);
+    const size_t e0 = (size_t)b * slot_stride + ((size_t)kvh * ctx + p0) * HD;  // first element of the chunk
     const float4* qbase = reinterpret_cast<const float4*>(q + (size_t)b * Hl * HD + (size_t)kvh * G * HD);
-    // K and V rows go straight to shared memory (cp.async, all in flight, no
-    // registers); rows before P - 1 are copied before the wait
-    for (int i = tid; i < n_past * F4; i += 256) {
-        cp_async16_smem(&ks[i / F4][i % F4], kbase + i);
-        cp_async16_smem(&vs[i / F4][i % F4], vbase + i);
-    }
-    pdl_wait();
-    for (int i = n_past * F4 + tid; i < n * F4; i += 256) {
-        cp_async16_smem(&ks[i / F4][i % F4], kbase + i);
-        cp_async16_smem(&vs[i / F4][i % F4], vbase + i);
+    if constexpr (KVQ) {
+        // rows before P - 1 are dequantized before the wait
+        const int8_t* kq = reinterpret_cast<const int8_t*>(kc) + e0;
+        const int8_t* vq = reinterpret_cast<const int8_t*>(vc) + e0;
+        const uint16_t* kss = ksc + (e0 >> 5);
+        const uint16_t* vss = vsc + (e0 >> 5);
+        for (int i = tid; i < n_past * F4; i += 256) {
+            ks[i / F4][i % F4] = kv_dq4(kq, kss, i);
+            vs[i / F4][i % F4] = kv_dq4(vq, vss, i);
+        }
+        pdl_wait();
+        for (int i = n_past * F4 + tid; i < n * F4; i += 256) {
+            ks[i / F4][i % F4] = kv_dq4(kq, kss, i);
+            vs[i / F4][i % F4] = kv_dq4(vq, vss, i);
+        }
+    } else {
+        const float4* kbase = reinterpret_cast<const float4*>(kc + e0);
+        const float4* vbase = reinterpret_cast<const float4*>(vc + e0);
+        // K and V rows go straight to shared memory (cp.async, all in flight, no
+        // registers); rows before P - 1 are copied before the wait
+        for (int i = tid; i < n_past * F4; i += 256) {
+            cp_async16_smem(&ks[i / F4][i % F4], kbase + i);
+            cp_async16_smem(&vs[i / F4][i % F4], vbase + i);
+        }
+        pdl_wait();
+        for (int i = n_past * F4 + tid; i < n * F4; i += 256) {
+            cp_async16_smem(&ks[i / F4][i % F4], kbase + i);
+            cp_async16_smem(&vs[i / F4][i % F4], vbase + i);
+        }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
     for (int i = tid; i < G * F4; i += 256) qs[i / F4][i % F4] = qbase[i];
@@ -711,9 +743,18 @@ __global__ void __launch_bounds__(256) rows_addnorm_kernel(const float* __restri
 // RoPE of q and k (core/Kernels.java:296-309: a' = fma(a, c, b * -s),
 // b' = fma(b, c, a * s)) and the KV-cache append (inference/KVCache.java:79-95)
 // of prompt row t at position p0 + t; q goes to q_out [T][nq].
+// Q8_0 KV cache of one layer (all slots; the slot offset is in the element index).
+struct KvQ {
+    int8_t* kq = nullptr;
+    int8_t* vq = nullptr;
+    uint16_t* ks = nullptr;
+    uint16_t* vs = nullptr;
+};
+
 __global__ void __launch_bounds__(256) rope_append_kernel(const float* __restrict__ qkv, int qcols,
                                                           float* __restrict__ q_out, float* __restrict__ kc,
-                                                          float* __restrict__ vc, const float* __restrict__ rcos,
+                                                          float* __restrict__ vc, KvQ kvq,
+                                                          const float* __restrict__ rcos,
                                                           const float* __restrict__ rsin, int hd, int nq, int nkv,
                                                           int ctx, int64_t p0) {
     const int t = blockIdx.x;
@@ -730,11 +771,15 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const float* __restric
                 q_out[(size_t)t * nq + j] = out;
             } else {
                 const int jj = j - nq, kvh = jj / hd;
-                kc[((size_t)kvh * ctx + pos) * hd + dd] = out;
+                const size_t e = ((size_t)kvh * ctx + pos) * hd + dd;
+                if (kvq.kq) kv_store_q8(kvq.kq, kvq.ks, e, out);  // warp-uniform: 32-aligned column blocks
+                else kc[e] = out;
             }
         } else {
             const int jj = j - nq - nkv, kvh = jj / hd, dd = jj - kvh * hd;
-            vc[((size_t)kvh * ctx + pos) * hd + dd] = val;
+            const size_t e = ((size_t)kvh * ctx + pos) * hd + dd;
+            if (kvq.kq) kv_store_q8(kvq.vq, kvq.vs, e, val);
+            else vc[e] = val;
         }
     }
 }
@@ -745,9 +790,24 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const float* __restric
 // orientation-N GEMV): the arithmetic of the fused QKV epilogue
 // (core/Kernels.java:296-309, inference/KVCache.java:79-95), slot b at
 // position pos[b].
+// KVCache.append of one position: block h (one per KV head), thread dd.
+__global__ void kv_put_kernel(const float* __restrict__ k, const float* __restrict__ v, float* __restrict__ kc,
+                              float* __restrict__ vc, KvQ kvq, int ctx, int hd, int64_t pos) {
+    const int h = blockIdx.x, dd = threadIdx.x;
+    const size_t e = ((size_t)h * ctx + pos) * hd + dd;
+    const float kv = k[h * hd + dd], vv = v[h * hd + dd];
+    if (kvq.kq) {  // hd is a multiple of 32: every warp holds one block
+        kv_store_q8(kvq.kq, kvq.ks, e, kv);
+        kv_store_q8(kvq.vq, kvq.vs, e, vv);
+    } else {
+        kc[e] = kv;
+        vc[e] = vv;
+    }
+}
+
 __global__ void __launch_bounds__(256) qkv_rope_rows_kernel(const float* __restrict__ qkv, int qcols,
                                                             float* __restrict__ q_out, float* __restrict__ kc,
-                                                            float* __restrict__ vc, int64_t slot_stride,
+                                                            float* __restrict__ vc, KvQ kvq, int64_t slot_stride,
                                                             const float* __restrict__ rcos,
                                                             const float* __restrict__ rsin,
                                                             const int64_t* __restrict__ pos, int hd, int nq, int nkv,
@@ -766,11 +826,15 @@ __global__ void __launch_bounds__(256) qkv_rope_rows_kernel(const float* __restr
                 q_out[(size_t)b * nq + j] = out;
             } else {
                 const int jj = j - nq, kvh = jj / hd;
-                kc[(size_t)b * slot_stride + ((size_t)kvh * ctx + p) * hd + dd] = out;
+                const size_t e = (size_t)b * slot_stride + ((size_t)kvh * ctx + p) * hd + dd;
+                if (kvq.kq) kv_store_q8(kvq.kq, kvq.ks, e, out);  // warp-uniform: 32-aligned column blocks
+                else kc[e] = out;
             }
         } else {
             const int jj = j - nq - nkv, kvh = jj / hd, dd = jj - kvh * hd;
-            vc[(size_t)b * slot_stride + ((size_t)kvh * ctx + p) * hd + dd] = val;
+            const size_t e = (size_t)b * slot_stride + ((size_t)kvh * ctx + p) * hd + dd;
+            if (kvq.kq) kv_store_q8(kvq.vq, kvq.vs, e, val);
+            else vc[e] = val;
         }
     }
 }
@@ -807,6 +871,17 @@ struct Layer {
 
 using namespace at;
 
+// Fp16.toFloat with flush-to-zero (core/Fp16.java:19-37), on the host.
+static float fp16_ftz_host(uint16_t h) {
+    const uint32_t sgn = (h >> 15) & 1u, e = (h >> 10) & 0x1Fu, mt = h & 0x3FFu;
+    uint32_t bits = (sgn << 31) | ((e + 112u) << 23) | (mt << 13);
+    if (e == 0u) bits = sgn << 31;
+    if (e == 31u) bits = mt ? 0x7FC00000u : ((sgn << 31) | 0x7F800000u);
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
 struct at_model {
     at_ctx* ctx = nullptr;
     at_model_config cfg{};
@@ -825,6 +900,10 @@ struct at_model {
     unsigned* attn_cnt = nullptr;  // [max_batch][Hkvl] tickets of the fused decode attention
     int attn_cs = 0;               // decode attention cluster size (0: merge through global memory)
     float *kcache = nullptr, *vcache = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
+    bool kv_q8 = false;                   // Q8_0 KV cache: quants + fp16 scales instead of kcache / vcache
+    int8_t *kq8 = nullptr, *vq8 = nullptr;
+    uint16_t *ksc = nullptr, *vsc = nullptr;
+    float* kv_stage = nullptr;            // at_model_kv_append staging: k then v, [Hkvl * hd] each
     float* scratch = nullptr;
     unsigned* counters = nullptr;
     int* d_tokens = nullptr;
@@ -978,6 +1057,24 @@ void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, boo
     launch_kc(kern, grid, block, dim3(1, 1, 1), 0, s, pdl, args...);
 }
 
+// One attention launch over the fp32 or the Q8_0 KV cache of a layer.
+template <int HD, int MODE, int CHK>
+void launch_attn(const KvQ& kvq, const float* kc, const float* vc, dim3 grid, dim3 cluster, size_t smem,
+                 cudaStream_t s, bool pdl, const float* q, const int64_t* pos, float* part, int Hl, int Hkvl, int ctx,
+                 int64_t slot_stride, int nchunk_max, float scale, unsigned* cnt, float* att) {
+    if (kvq.kq)
+        launch_kc(attn_split_kernel<HD, MODE, CHK, true>, grid, 256, cluster, smem, s, pdl, q,
+                  (const float*)kvq.kq, (const float*)kvq.vq, pos, part, Hl, Hkvl, ctx, slot_stride, nchunk_max,
+                  scale, cnt, att, (const uint16_t*)kvq.ks, (const uint16_t*)kvq.vs);
+    else
+        launch_kc(attn_split_kernel<HD, MODE, CHK, false>, grid, 256, cluster, smem, s, pdl, q, kc, vc, pos, part,
+                  Hl, Hkvl, ctx, slot_stride, nchunk_max, scale, cnt, att, (const uint16_t*)nullptr,
+                  (const uint16_t*)nullptr);
+}
+
+// The Q8_0 KV cache of layer L (null pointers for an fp32 cache).
+KvQ kv_layer(const at_model* m, int L);
+
 // Cluster size of the decode attention (clusters of chunk CTAs of one KV head
 // merge through distributed shared memory): 16 where the device can place
 // such clusters (non-portable size), else 8, else 0 (no clusters: MODE 1).
@@ -988,6 +1085,12 @@ int attn_cluster_size(int hkv, int nchunk, int batch) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
         cudaGetLastError();
         return 0;
+    }
+    // the Q8_0-KV variant has the same footprint and launch shape
+    auto kern_q = attn_split_kernel<HD, 2, kAttnClusterChunk, true>;
+    if (cudaFuncSetAttribute(kern_q, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+        cudaFuncSetAttribute(kern_q, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+        cudaGetLastError();
     }
     for (int cs : {16, 8}) {
         if (cs == 16 &&
@@ -1011,6 +1114,12 @@ int attn_cluster_size(int hkv, int nchunk, int batch) {
         cudaGetLastError();
     }
     return 0;
+}
+
+KvQ kv_layer(const at_model* m, int L) {
+    if (!m->kv_q8) return KvQ{};
+    const size_t off = (size_t)L * m->Hkvl * m->ctx_len * m->hd;
+    return KvQ{m->kq8 + off, m->vq8 + off, m->ksc + off / 32, m->vsc + off / 32};
 }
 
 void enqueue_step(at_model* m, int B) {
@@ -1049,8 +1158,9 @@ void enqueue_step(at_model* m, int B) {
     const size_t layer_kv = (size_t)m->Hkvl * m->ctx_len * hd;
     for (int L = 0; L < m->L; ++L) {
         Layer& ly = m->layers[L];
-        float* kc = m->kcache + L * layer_kv;
-        float* vc = m->vcache + L * layer_kv;
+        float* kc = m->kv_q8 ? nullptr : m->kcache + L * layer_kv;
+        float* vc = m->kv_q8 ? nullptr : m->vcache + L * layer_kv;
+        const KvQ kvq = kv_layer(m, L);
         {
             ProfScope p(m, AT_PROF_QKV);
             GemvArgs a;
@@ -1059,6 +1169,7 @@ void enqueue_step(at_model* m, int B) {
             a.y = m->q; a.y_stride = m->Hl * hd;
             a.rope_cos = m->rope_cos; a.rope_sin = m->rope_sin; a.pos = m->d_pos;
             a.kcache = kc; a.vcache = vc;
+            a.kq = kvq.kq; a.vq = kvq.vq; a.ksc = kvq.ks; a.vsc = kvq.vs;
             a.kv_slot_stride = m->slot_stride;
             a.head_dim = hd; a.n_q_cols = m->Hl * hd; a.n_kv_cols = m->Hkvl * hd; a.ctx_len = m->ctx_len;
             a.scratch = m->scratch; a.counters = m->counters;
@@ -1067,9 +1178,9 @@ void enqueue_step(at_model* m, int B) {
                 const int qcols = (m->Hl + 2 * m->Hkvl) * hd;
                 a.y = m->qkvbuf; a.y_stride = qcols;
                 launch_gemv_n(&ly.qkv, B, Pro::AddNorm, Epi::Plain, a, c->num_sms, s, m->pdl);
-                qkv_rope_rows_kernel<<<B, 256, 0, s>>>(m->qkvbuf, qcols, m->q, kc, vc, m->slot_stride, m->rope_cos,
-                                                       m->rope_sin, m->d_pos, hd, m->Hl * hd, m->Hkvl * hd,
-                                                       m->ctx_len);
+                qkv_rope_rows_kernel<<<B, 256, 0, s>>>(m->qkvbuf, qcols, m->q, kc, vc, kvq, m->slot_stride,
+                                                       m->rope_cos, m->rope_sin, m->d_pos, hd, m->Hl * hd,
+                                                       m->Hkvl * hd, m->ctx_len);
                 AT_CUDA(cudaGetLastError());
             } else {
                 launch_gemv_t(&ly.qkv, B, Pro::AddNorm, Epi::QkvRope, a, c->num_sms, s, m->pdl);
@@ -1091,37 +1202,31 @@ void enqueue_step(at_model* m, int B) {
                 dim3 gc(m->Hkvl, (nch64 + cs - 1) / cs * cs, B);
                 const size_t sm = attn_smem_bytes(hd, kAttnClusterChunk);
                 if (hd == 128)
-                    launch_kc(attn_split_kernel<128, 2, kAttnClusterChunk>, gc, 256, dim3(1, cs, 1), sm, s, m->pdl, qp,
-                              (const float*)kc, (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len,
-                              m->slot_stride, m->nchunk_max, scale, m->attn_cnt, m->att);
+                    launch_attn<128, 2, kAttnClusterChunk>(kvq, kc, vc, gc, dim3(1, cs, 1), sm, s, m->pdl, qp, dp,
+                                                           m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
+                                                           m->nchunk_max, scale, m->attn_cnt, m->att);
                 else
-                    launch_kc(attn_split_kernel<64, 2, kAttnClusterChunk>, gc, 256, dim3(1, cs, 1), sm, s, m->pdl, qp,
-                              (const float*)kc, (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len,
-                              m->slot_stride, m->nchunk_max, scale, m->attn_cnt, m->att);
+                    launch_attn<64, 2, kAttnClusterChunk>(kvq, kc, vc, gc, dim3(1, cs, 1), sm, s, m->pdl, qp, dp,
+                                                          m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
+                                                          m->nchunk_max, scale, m->attn_cnt, m->att);
             } else if (fused) {
                 if (hd == 128)
-                    launch_kc(attn_split_kernel<128, 1>, g1, 256, dim3(1, 1, 1), attn_smem_bytes(128, CH), s, m->pdl,
-                              qp, (const float*)kc,
-                             (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
-                             m->nchunk_max, scale, m->attn_cnt, m->att);
+                    launch_attn<128, 1, CH>(kvq, kc, vc, g1, dim3(1, 1, 1), attn_smem_bytes(128, CH), s, m->pdl, qp, dp,
+                                            m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max,
+                                            scale, m->attn_cnt, m->att);
                 else
-                    launch_kc(attn_split_kernel<64, 1>, g1, 256, dim3(1, 1, 1), attn_smem_bytes(64, CH), s, m->pdl,
-                              qp, (const float*)kc,
-                             (const float*)vc, dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride,
-                             m->nchunk_max, scale, m->attn_cnt, m->att);
+                    launch_attn<64, 1, CH>(kvq, kc, vc, g1, dim3(1, 1, 1), attn_smem_bytes(64, CH), s, m->pdl, qp, dp,
+                                           m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max,
+                                           scale, m->attn_cnt, m->att);
             } else {
-                unsigned* no_cnt = nullptr;
-                float* no_att = nullptr;
                 if (hd == 128)
-                    launch_kc(attn_split_kernel<128>, g1, 256, dim3(1, 1, 1), attn_smem_bytes(128, CH), s, m->pdl, qp,
-                              (const float*)kc, (const float*)vc,
-                             dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max, scale,
-                             no_cnt, no_att);
+                    launch_attn<128, 0, CH>(kvq, kc, vc, g1, dim3(1, 1, 1), attn_smem_bytes(128, CH), s, m->pdl, qp, dp,
+                                            m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max,
+                                            scale, nullptr, nullptr);
                 else
-                    launch_kc(attn_split_kernel<64>, g1, 256, dim3(1, 1, 1), attn_smem_bytes(64, CH), s, m->pdl, qp,
-                              (const float*)kc, (const float*)vc,
-                             dp, m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max, scale,
-                             no_cnt, no_att);
+                    launch_attn<64, 0, CH>(kvq, kc, vc, g1, dim3(1, 1, 1), attn_smem_bytes(64, CH), s, m->pdl, qp, dp,
+                                           m->att_part, m->Hl, m->Hkvl, m->ctx_len, m->slot_stride, m->nchunk_max,
+                                           scale, nullptr, nullptr);
                 dim3 g2(m->Hl, B);
                 const float* pp = m->att_part;
                 if (hd == 128)
@@ -1301,7 +1406,7 @@ void destroy_model(at_model* m) {
                     m->pf_att, m->pf_g, m->pf_u, m->pf_part, m->pf_tok, m->pf_pos, m->pf_err, m->pf_xbf, m->pf_ws,
                     m->d_ds_layers, m->ds_qkv_part, m->ds_wo_part, m->ds_apart, m->ds_tickets, m->ds_bar,
                     m->ds_err, m->ds_stamps, m->qkvbuf, m->d_rows, m->d_hist, m->d_hist_len, m->d_pen_cnt,
-                    m->d_rng, m->d_sampled, m->d_seq, m->d_step_ctr, m->d_append};
+                    m->d_rng, m->d_sampled, m->d_seq, m->d_step_ctr, m->d_append, m->kq8, m->vq8, m->ksc, m->vsc, m->kv_stage};
     for (void* p : bufs)
         if (p) cudaFree(p);
     if (m->h_tokens) cudaFreeHost(m->h_tokens);
@@ -1325,7 +1430,7 @@ void setup_decode_step(at_model* m) {
     at_ctx* c = m->ctx;
     const char* env = std::getenv("AT_DECODE_STEP");
     if (!env || env[0] != '1') return;
-    if (c->world != 1 || m->layers.empty() || m->layout != 0) return;
+    if (c->world != 1 || m->layers.empty() || m->layout != 0 || m->kv_q8) return;
     const int qt = m->layers[0].qkv.type;
     for (auto& ly : m->layers)
         for (const at_qmat* q : {&ly.qkv, &ly.wo, &ly.w1, &ly.w3, &ly.w2})
@@ -1553,6 +1658,9 @@ int at_model_create(at_ctx* ctx, const at_model_config* cfg, at_model** out) {
         AT_REQUIRE((cfg->layout & ~AT_LAYOUT_LLAMA_CPP) == 0, AT_ERR_INVALID_ARG, "unknown layout bits");
         m->layout = cfg->layout;
         m->attn_n = (cfg->layout & AT_LAYOUT_ATTN_OUT_IN) != 0;
+        AT_REQUIRE(cfg->kv_type == AT_GGML_F32 || cfg->kv_type == AT_GGML_Q8_0, AT_ERR_UNSUPPORTED,
+                   "KV cache type must be F32 or Q8_0");
+        m->kv_q8 = cfg->kv_type == AT_GGML_Q8_0;
         m->B = cfg->max_batch < 1 ? 1 : cfg->max_batch;
         AT_REQUIRE(m->B <= 8, AT_ERR_INVALID_ARG, "max_batch must be in [1, 8]");
         m->d = (int)cfg->embedding_length;
@@ -1781,8 +1889,15 @@ int at_model_finalize(at_model* m) {
         alloc_zero((void**)&m->attn_cnt, (size_t)B * m->Hkvl * sizeof(unsigned));
         // KV cache (inference/KVCache.java:43-63): [slot][layer][kvHead][ctx][headDim] fp32
         m->slot_stride = (int64_t)m->L * m->Hkvl * m->ctx_len * hd;
-        alloc_zero((void**)&m->kcache, (size_t)B * m->slot_stride * 4);
-        alloc_zero((void**)&m->vcache, (size_t)B * m->slot_stride * 4);
+        if (m->kv_q8) {
+            alloc_zero((void**)&m->kq8, (size_t)B * m->slot_stride);
+            alloc_zero((void**)&m->vq8, (size_t)B * m->slot_stride);
+            alloc_zero((void**)&m->ksc, (size_t)B * m->slot_stride / 32 * 2);
+            alloc_zero((void**)&m->vsc, (size_t)B * m->slot_stride / 32 * 2);
+        } else {
+            alloc_zero((void**)&m->kcache, (size_t)B * m->slot_stride * 4);
+            alloc_zero((void**)&m->vcache, (size_t)B * m->slot_stride * 4);
+        }
         // RoPE tables (inference/RopeCache.java:154-177): freq = (float) pow(base, -2i/hd)
         // in double, angle = pos * freq in float, cos/sin in double then float.
         {
@@ -1834,10 +1949,10 @@ int at_model_finalize(at_model* m) {
 }
 
 int at_model_load_gguf(at_ctx* ctx, const char* path, int max_batch, at_model** out) {
-    return at_model_load_gguf_ex(ctx, path, max_batch, 0, out);
+    return at_model_load_gguf_ex(ctx, path, max_batch, 0, AT_GGML_F32, out);
 }
 
-int at_model_load_gguf_ex(at_ctx* ctx, const char* path, int max_batch, int layout, at_model** out) {
+int at_model_load_gguf_ex(at_ctx* ctx, const char* path, int max_batch, int layout, int kv_type, at_model** out) {
     int fd = -1;
     void* map = MAP_FAILED;
     size_t len = 0;
@@ -1909,6 +2024,7 @@ int at_model_load_gguf_ex(at_ctx* ctx, const char* path, int max_batch, int layo
         cfg.vocab_size = (int64_t)n_or(arch + ".vocab_size", n_or("tokenizer.ggml.vocab_size", 32000));
         cfg.max_batch = max_batch < 1 ? 1 : max_batch;
         cfg.layout = layout;
+        cfg.kv_type = kv_type;
         const int64_t align = (int64_t)n_or("general.alignment", 32);
         AT_REQUIRE(align > 0, AT_ERR_IO, "bad general.alignment");
         const uint64_t data_off = ((v.pos + align - 1) / align) * align;
@@ -2039,24 +2155,29 @@ void run_prompt_batched(at_model* m, const int* tokens, int n, int slot) {
         AT_CUDA(cudaGetLastError());
         for (int L = 0; L < m->L; ++L) {
             Layer& ly = m->layers[L];
-            float* kc = m->kcache + (size_t)slot * m->slot_stride + L * layer_kv;
-            float* vc = m->vcache + (size_t)slot * m->slot_stride + L * layer_kv;
+            const size_t kv_off = (size_t)slot * m->slot_stride + L * layer_kv;
+            float* kc = m->kv_q8 ? nullptr : m->kcache + kv_off;
+            float* vc = m->kv_q8 ? nullptr : m->vcache + kv_off;
+            KvQ kvq;
+            if (m->kv_q8) kvq = KvQ{m->kq8 + kv_off, m->vq8 + kv_off, m->ksc + kv_off / 32, m->vsc + kv_off / 32};
             // attention block: xb = norm(xa + y); q, k, v; RoPE + append; attention; y = wo att
             rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xa, m->pf_y, ly.attn_norm, m->pf_xb, d, eps);
             AT_CUDA(cudaGetLastError());
             launch_gemm_tc(&ly.qkv, m->pf_xb, d, m->pf_qkv, qcols, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
                            c->num_sms, m->pf_err, s);
-            rope_append_kernel<<<T, 256, 0, s>>>(m->pf_qkv, qcols, m->pf_q, kc, vc, m->rope_cos, m->rope_sin, hd, nq,
-                                                 nkv, m->ctx_len, p0);
+            rope_append_kernel<<<T, 256, 0, s>>>(m->pf_qkv, qcols, m->pf_q, kc, vc, kvq, m->rope_cos, m->rope_sin, hd,
+                                                 nq, nkv, m->ctx_len, p0);
             AT_CUDA(cudaGetLastError());
             dim3 g1(m->Hkvl, m->nchunk_max, T), g2(m->Hl, T);
             if (hd == 128) {
-                attn_split_kernel<128><<<g1, 256, attn_smem_bytes(128, CH), s>>>(m->pf_q, kc, vc, m->pf_pos, m->pf_part, m->Hl, m->Hkvl,
-                                                          m->ctx_len, 0, m->nchunk_max, scale);
+                launch_attn<128, 0, CH>(kvq, kc, vc, g1, dim3(1, 1, 1), attn_smem_bytes(128, CH), s, false, m->pf_q,
+                                        m->pf_pos, m->pf_part, m->Hl, m->Hkvl, m->ctx_len, 0, m->nchunk_max, scale,
+                                        nullptr, nullptr);
                 attn_combine_kernel<128><<<g2, 128, 0, s>>>(m->pf_part, m->pf_pos, m->pf_att, m->Hl, m->nchunk_max);
             } else {
-                attn_split_kernel<64><<<g1, 256, attn_smem_bytes(64, CH), s>>>(m->pf_q, kc, vc, m->pf_pos, m->pf_part, m->Hl, m->Hkvl,
-                                                         m->ctx_len, 0, m->nchunk_max, scale);
+                launch_attn<64, 0, CH>(kvq, kc, vc, g1, dim3(1, 1, 1), attn_smem_bytes(64, CH), s, false, m->pf_q,
+                                       m->pf_pos, m->pf_part, m->Hl, m->Hkvl, m->ctx_len, 0, m->nchunk_max, scale,
+                                       nullptr, nullptr);
                 attn_combine_kernel<64><<<g2, 64, 0, s>>>(m->pf_part, m->pf_pos, m->pf_att, m->Hl, m->nchunk_max);
             }
             AT_CUDA(cudaGetLastError());
@@ -2514,9 +2635,68 @@ int at_model_kv_read(at_model* m, int slot, int layer, int kv_head, int64_t posi
         AT_REQUIRE(position >= 0 && position < m->ctx_len, AT_ERR_INVALID_ARG, "position oob");
         const size_t off = (size_t)slot * m->slot_stride +
                            (((size_t)layer * m->Hkvl + kv_head) * m->ctx_len + (size_t)position) * m->hd;
+        if (m->kv_q8) {
+            // quants and scales to the host, read back as q * d (fp16 scale with flush-to-zero)
+            std::vector<int8_t> kq(m->hd), vq(m->hd);
+            std::vector<uint16_t> ks(m->hd / 32), vs(m->hd / 32);
+            AT_CUDA(cudaMemcpyAsync(kq.data(), m->kq8 + off, m->hd, cudaMemcpyDeviceToHost, m->ctx->stream));
+            AT_CUDA(cudaMemcpyAsync(vq.data(), m->vq8 + off, m->hd, cudaMemcpyDeviceToHost, m->ctx->stream));
+            AT_CUDA(cudaMemcpyAsync(ks.data(), m->ksc + off / 32, m->hd / 32 * 2, cudaMemcpyDeviceToHost, m->ctx->stream));
+            AT_CUDA(cudaMemcpyAsync(vs.data(), m->vsc + off / 32, m->hd / 32 * 2, cudaMemcpyDeviceToHost, m->ctx->stream));
+            AT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+            for (int i = 0; i < m->hd; ++i) {
+                k_host[i] = (float)kq[i] * fp16_ftz_host(ks[i / 32]);
+                v_host[i] = (float)vq[i] * fp16_ftz_host(vs[i / 32]);
+            }
+            return;
+        }
         AT_CUDA(cudaMemcpyAsync(k_host, m->kcache + off, m->hd * 4, cudaMemcpyDeviceToHost, m->ctx->stream));
         AT_CUDA(cudaMemcpyAsync(v_host, m->vcache + off, m->hd * 4, cudaMemcpyDeviceToHost, m->ctx->stream));
         AT_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    });
+}
+
+int at_model_kv_append(at_model* m, int slot, int64_t layer, int64_t position, const float* k_host,
+                       const float* v_host) {
+    return guard([&] {
+        AT_REQUIRE(m && m->finalized && k_host && v_host, AT_ERR_INVALID_ARG, "bad argument");
+        AT_REQUIRE(slot >= 0 && slot < m->B, AT_ERR_INVALID_ARG, "slot out of range");
+        // KVCache.append (inference/KVCache.java:79-95)
+        AT_REQUIRE(layer >= 0 && layer < m->L, AT_ERR_INVALID_ARG,
+                   "layer " + std::to_string(layer) + " out of range " + std::to_string(m->L));
+        AT_REQUIRE(position >= 0, AT_ERR_INVALID_ARG, "negative position");
+        AT_REQUIRE(position < m->ctx_len, AT_ERR_STATE,
+                   "position " + std::to_string(position) + " exceeds maxContext " + std::to_string(m->ctx_len));
+        at_ctx* c = m->ctx;
+        AT_CUDA(cudaSetDevice(c->device));
+        const int n = m->Hkvl * m->hd;
+        if (!m->kv_stage) alloc_zero((void**)&m->kv_stage, (size_t)2 * n * 4);
+        AT_CUDA(cudaMemcpyAsync(m->kv_stage, k_host, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream));
+        AT_CUDA(cudaMemcpyAsync(m->kv_stage + n, v_host, (size_t)n * 4, cudaMemcpyHostToDevice, c->stream));
+        const size_t base = (size_t)slot * m->slot_stride + (size_t)layer * m->Hkvl * m->ctx_len * m->hd;
+        KvQ kvq;
+        if (m->kv_q8) kvq = KvQ{m->kq8 + base, m->vq8 + base, m->ksc + base / 32, m->vsc + base / 32};
+        kv_put_kernel<<<m->Hkvl, m->hd, 0, c->stream>>>(m->kv_stage, m->kv_stage + n,
+                                                         m->kv_q8 ? nullptr : m->kcache + base,
+                                                         m->kv_q8 ? nullptr : m->vcache + base, kvq, m->ctx_len,
+                                                         m->hd, position);
+        AT_CUDA(cudaGetLastError());
+        AT_CUDA(cudaStreamSynchronize(c->stream));
+        m->kv_size[slot] = std::max<int64_t>(m->kv_size[slot], position + 1);
+    });
+}
+
+int at_model_kv_offset(const at_model* m, int64_t layer, int64_t kv_head, int64_t position, int64_t dim,
+                       int64_t* byte_offset) {
+    return guard([&] {
+        AT_REQUIRE(m && byte_offset, AT_ERR_INVALID_ARG, "null argument");
+        // KVCache.offsetOf (inference/KVCache.java:70-76), with its checks and messages
+        AT_REQUIRE(layer >= 0 && layer < m->L, AT_ERR_INVALID_ARG, "layer oob");
+        AT_REQUIRE(kv_head >= 0 && kv_head < m->Hkvl, AT_ERR_INVALID_ARG, "kvHead oob");
+        AT_REQUIRE(position >= 0 && position < m->ctx_len, AT_ERR_INVALID_ARG, "position oob");
+        AT_REQUIRE(dim < m->hd, AT_ERR_INVALID_ARG, "dim oob");
+        const int64_t row_bytes = (int64_t)m->ctx_len * m->hd * 4;
+        *byte_offset = (layer * m->Hkvl + kv_head) * row_bytes + position * m->hd * 4 + dim * 4;
     });
 }
 
@@ -2524,8 +2704,16 @@ int at_model_kv_reset(at_model* m, int slot) {
     return guard([&] {
         AT_REQUIRE(m && m->finalized, AT_ERR_INVALID_ARG, "bad argument");
         AT_REQUIRE(slot >= 0 && slot < m->B, AT_ERR_INVALID_ARG, "slot out of range");
-        AT_CUDA(cudaMemsetAsync(m->kcache + (size_t)slot * m->slot_stride, 0, (size_t)m->slot_stride * 4, m->ctx->stream));
-        AT_CUDA(cudaMemsetAsync(m->vcache + (size_t)slot * m->slot_stride, 0, (size_t)m->slot_stride * 4, m->ctx->stream));
+        const size_t off = (size_t)slot * m->slot_stride;
+        if (m->kv_q8) {
+            AT_CUDA(cudaMemsetAsync(m->kq8 + off, 0, (size_t)m->slot_stride, m->ctx->stream));
+            AT_CUDA(cudaMemsetAsync(m->vq8 + off, 0, (size_t)m->slot_stride, m->ctx->stream));
+            AT_CUDA(cudaMemsetAsync(m->ksc + off / 32, 0, (size_t)m->slot_stride / 32 * 2, m->ctx->stream));
+            AT_CUDA(cudaMemsetAsync(m->vsc + off / 32, 0, (size_t)m->slot_stride / 32 * 2, m->ctx->stream));
+        } else {
+            AT_CUDA(cudaMemsetAsync(m->kcache + off, 0, (size_t)m->slot_stride * 4, m->ctx->stream));
+            AT_CUDA(cudaMemsetAsync(m->vcache + off, 0, (size_t)m->slot_stride * 4, m->ctx->stream));
+        }
         AT_CUDA(cudaStreamSynchronize(m->ctx->stream));
         m->kv_size[slot] = 0;
     });

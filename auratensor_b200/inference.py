@@ -63,10 +63,10 @@ class LlamaConfig:
         return cls("llama", s.ctx, s.dim, s.n_layers, s.n_heads, s.n_kv_heads, s.ffn, float(s.rope_theta),
                    float(s.eps), s.vocab)
 
-    def to_c(self, max_batch: int = 1, layout: int = 0) -> ModelConfig:
+    def to_c(self, max_batch: int = 1, layout: int = 0, kv_type: int = 0) -> ModelConfig:
         return ModelConfig(self.contextLength, self.embeddingLength, self.blockCount, self.headCount,
                            self.headCountKv, self.feedForwardLength, self.vocabSize, self.ropeFrequencyBase,
-                           self.rmsNormEpsilon, max_batch, layout)
+                           self.rmsNormEpsilon, max_batch, layout, kv_type, 0)
 
 
 class KVCache:
@@ -98,16 +98,20 @@ class KVCache:
         return self._dims[3] * self._dims[2] * 4
 
     def offsetOf(self, layer, kv_head, position, dim) -> int:
-        L, H, hd, ctx = self._dims
-        if not 0 <= layer < L:
-            raise _lib.IllegalArgumentException(_lib.AT_ERR_INVALID_ARG, "layer oob")
-        if not 0 <= kv_head < H:
-            raise _lib.IllegalArgumentException(_lib.AT_ERR_INVALID_ARG, "kvHead oob")
-        if not 0 <= position < ctx:
-            raise _lib.IllegalArgumentException(_lib.AT_ERR_INVALID_ARG, "position oob")
-        if dim >= hd:
-            raise _lib.IllegalArgumentException(_lib.AT_ERR_INVALID_ARG, "dim oob")
-        return ((layer * H) + kv_head) * self.rowBytes() + position * hd * 4 + dim * 4
+        """KVCache.offsetOf through at_model_kv_offset (same checks and messages)."""
+        v = C.c_int64()
+        call("at_model_kv_offset", self._m._h, int(layer), int(kv_head), int(position), int(dim), C.byref(v))
+        return v.value
+
+    def append(self, layer: int, position: int, kSlice, vSlice) -> None:
+        """KVCache.append: headCountKv x headDim floats of K and of V at `position`."""
+        k = np.ascontiguousarray(np.asarray(kSlice, dtype=np.float32).reshape(-1))
+        v = np.ascontiguousarray(np.asarray(vSlice, dtype=np.float32).reshape(-1))
+        n = self._dims[1] * self._dims[2]
+        if k.size != n or v.size != n:
+            raise _lib.IllegalArgumentException(_lib.AT_ERR_INVALID_ARG, f"K/V slices must hold {n} floats")
+        call("at_model_kv_append", self._m._h, self._slot, int(layer), int(position), k.ctypes.data_as(C.c_void_p),
+             v.ctypes.data_as(C.c_void_p))
 
     def read(self, layer: int, kv_head: int, position: int):
         hd = self._dims[2]
@@ -131,15 +135,16 @@ class LlamaModel:
     """
 
     def __init__(self, config: LlamaConfig, tensors: dict | None = None, max_batch: int = 1, ctx=None,
-                 world: int = 1, layout: int = 0):
+                 world: int = 1, layout: int = 0, kv_type: int = 0):
         """layout: byte layout of the tensors (_lib.LAYOUT_*; 0 is the
-        reference's, _lib.LAYOUT_LLAMA_CPP reads llama.cpp exports)."""
+        reference's, _lib.LAYOUT_LLAMA_CPP reads llama.cpp exports).
+        kv_type: KV cache storage, 0 (F32, the reference's) or 8 (Q8_0)."""
         self.config = config
         self.max_batch = max_batch
         self.world = world
         self._ctx = ctx if ctx is not None else context()
         self._h = C.c_void_p()
-        cfg = config.to_c(max_batch, layout)
+        cfg = config.to_c(max_batch, layout, kv_type)
         call("at_model_create", self._ctx, C.byref(cfg), C.byref(self._h))
         self._logits = _host_logits(max_batch, config.vocabSize)
         if tensors is not None:
@@ -148,7 +153,7 @@ class LlamaModel:
             self.finalize()
 
     @classmethod
-    def fromGguf(cls, path: str, max_batch: int = 1, layout: int = 0) -> "LlamaModel":
+    def fromGguf(cls, path: str, max_batch: int = 1, layout: int = 0, kv_type: int = 0) -> "LlamaModel":
         with GgufFile.open(path) as g:
             cfg = LlamaConfig.fromGguf(g.metadata)
         self = cls.__new__(cls)
@@ -157,7 +162,7 @@ class LlamaModel:
         self.world = 1
         self._ctx = context()
         self._h = C.c_void_p()
-        call("at_model_load_gguf_ex", self._ctx, path.encode(), max_batch, int(layout), C.byref(self._h))
+        call("at_model_load_gguf_ex", self._ctx, path.encode(), max_batch, int(layout), int(kv_type), C.byref(self._h))
         self._logits = _host_logits(max_batch, cfg.vocabSize)
         return self
 

@@ -182,7 +182,17 @@ typedef struct at_model_config {
     float   rms_norm_eps;
     int32_t max_batch;            /* independent sequences (KV slots), 1..8 */
     int32_t layout;               /* AT_LAYOUT_* bits of the tensors' bytes (0: the reference's) */
+    int32_t kv_type;              /* KV cache storage: AT_GGML_F32 (0, the reference's KVCache) or
+                                     AT_GGML_Q8_0 (blocks of 32 along head_dim, see below) */
+    int32_t reserved;
 } at_model_config;
+/* A Q8_0 KV cache (the reference keeps K and V in FP32, KVCache.java:56-61;
+ * its README lists quantized KV as missing) stores each appended K/V head
+ * vector as blocks of 32 elements: d = max|x| / 127 rounded to fp16 once,
+ * q = round-half-away(x * (1 / d)) in int8, read back as q * d (fp16 with
+ * flush-to-zero). Logits then differ from the FP32-KV model by the KV
+ * rounding (stated and tested tolerance: 2e-2 of the logit range); against
+ * the oracle run with the same KV rounding they match within 1e-3. */
 
 /* new LlamaModel(cfg, weights, tok) (inference/LlamaModel.java:79-129) without
  * weights yet; then at_model_set_tensor per GGUF tensor; then at_model_finalize. */
@@ -203,7 +213,7 @@ int at_model_load_gguf(at_ctx* ctx, const char* path, int max_batch, at_model** 
 /* at_model_load_gguf for files in another byte layout (AT_LAYOUT_*; for
  * example AT_LAYOUT_LLAMA_CPP for llama.cpp exports). No counterpart in the
  * reference. */
-int at_model_load_gguf_ex(at_ctx* ctx, const char* path, int max_batch, int layout, at_model** out);
+int at_model_load_gguf_ex(at_ctx* ctx, const char* path, int max_batch, int layout, int kv_type, at_model** out);
 int at_model_get_config(const at_model* m, at_model_config* out);
 int at_model_destroy(at_model* m);
 /* LlamaModel.forwardStep(tokenId, position) (inference/LlamaModel.java:141-158):
@@ -322,6 +332,19 @@ int at_model_kv_read(at_model* m, int slot, int layer, int kv_head, int64_t posi
                      float* k_host, float* v_host);
 /* Rewinds a sequence slot to empty (the reference builds a new KVCache). */
 int at_model_kv_reset(at_model* m, int slot);
+/* KVCache.append(layer, position, kSlice, vSlice) (inference/KVCache.java:79-95)
+ * into KV slot `slot`: k_host / v_host hold head_count_kv (rank-local) x
+ * head_dim floats. Layer out of range: AT_ERR_INVALID_ARG; position at or
+ * past maxContext: AT_ERR_STATE. A Q8_0 cache quantizes on the way in. */
+int at_model_kv_append(at_model* m, int slot, int64_t layer, int64_t position, const float* k_host,
+                       const float* v_host);
+/* KVCache.offsetOf(layer, kvHead, position, dim) (inference/KVCache.java:70-76):
+ * the byte offset of that element in one slot's K (or V) array of the FP32
+ * layout [layer][kvHead][maxContext][headDim], with the reference's checks
+ * (layer, kvHead, position out of range or dim >= headDim: AT_ERR_INVALID_ARG).
+ * For a Q8_0 cache offset / 4 indexes the quants and offset / 128 the scales. */
+int at_model_kv_offset(const at_model* m, int64_t layer, int64_t kv_head, int64_t position, int64_t dim,
+                       int64_t* byte_offset);
 
 /* ---- sampler: Sampler.sample (inference/Sampler.java:37-121), host -------- */
 int at_sample(float* logits, int vocab, const int* history, int n_history, float temperature,

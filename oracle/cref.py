@@ -18,7 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 class RdCfg(C.Structure):
     _fields_ = [("dim", C.c_int), ("ffn", C.c_int), ("n_heads", C.c_int), ("n_kv", C.c_int), ("vocab", C.c_int),
                 ("ctx", C.c_int), ("n_layers", C.c_int), ("rope_base", C.c_float), ("eps", C.c_float),
-                ("layout", C.c_int)]
+                ("layout", C.c_int), ("kv_q8", C.c_int)]
 
 
 def host_tag() -> str:
@@ -65,11 +65,12 @@ def lib():
 class RefDecoder:
     """The reference's decode path in C: load-time dequant, FP32 sgemv."""
 
-    def __init__(self, shape, n_layers: int | None = None, threads: int = 1):
+    def __init__(self, shape, n_layers: int | None = None, threads: int = 1, kv_type: int = 0):
+        """kv_type 8: K/V rounded as the device's Q8_0 KV cache stores them."""
         self.shape = shape
         self.n_layers = shape.n_layers if n_layers is None else n_layers
         cfg = RdCfg(shape.dim, shape.ffn, shape.n_heads, shape.n_kv_heads, shape.vocab, shape.ctx, self.n_layers,
-                    float(shape.rope_theta), float(shape.eps), int(getattr(shape, "layout", 0)))
+                    float(shape.rope_theta), float(shape.eps), int(getattr(shape, "layout", 0)), int(kv_type == 8))
         self._h = lib().rd_create(C.byref(cfg), threads)
         self._keep = []
 

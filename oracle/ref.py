@@ -243,21 +243,43 @@ class LlamaConfig:
         return self.embedding_length // self.head_count
 
 
-class KVCache:
-    """inference/KVCache.java:43-95: fp32 [layer][kvHead][ctx][headDim] K and V."""
+def kv_q8_roundtrip(x: np.ndarray) -> np.ndarray:
+    """The Q8_0 KV-cache rounding of the device path (no reference
+    counterpart: the reference keeps K/V in FP32): per block of 32, d =
+    max|x| / 127 in float32, stored as fp16 (round to nearest even); q =
+    round-half-away-from-zero(x * (1 / d)) clamped to +-127 (q = 0 when d
+    is 0); read back as q * fp16_to_f32_ftz(d)."""
+    x = np.asarray(x, dtype=np.float32).reshape(-1, 32)
+    amax = np.max(np.abs(x), axis=1).astype(np.float32)
+    d = (amax / np.float32(127.0)).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        inv = np.where(d != 0, np.float32(1.0) / np.where(d != 0, d, np.float32(1.0)), np.float32(0.0)).astype(np.float32)
+    y = (x * inv[:, None]).astype(np.float32).astype(np.float64)
+    q = np.clip(np.where(y >= 0, np.floor(y + 0.5), np.ceil(y - 0.5)), -127, 127).astype(np.float32)
+    d16 = d.astype(np.float16).view(np.uint16)
+    dd = fp16_bits_to_f32(d16).astype(np.float32)
+    return (q * dd[:, None]).astype(np.float32).reshape(-1)
 
-    def __init__(self, layers: int, kv_heads: int, head_dim: int, max_ctx: int):
+
+class KVCache:
+    """inference/KVCache.java:43-95: fp32 [layer][kvHead][ctx][headDim] K and V.
+    q8=True stores what the device's Q8_0 KV cache reads back."""
+
+    def __init__(self, layers: int, kv_heads: int, head_dim: int, max_ctx: int, q8: bool = False):
         self.k = np.zeros((layers, kv_heads, max_ctx, head_dim), dtype=np.float32)
         self.v = np.zeros_like(self.k)
         self.max_ctx = max_ctx
         self.size = 0
+        self.q8 = q8
 
     def append(self, layer: int, pos: int, k: np.ndarray, v: np.ndarray) -> None:
         if pos >= self.max_ctx:
             raise RuntimeError(f"position {pos} exceeds maxContext {self.max_ctx}")
         hkv, hd = self.k.shape[1], self.k.shape[3]
-        self.k[layer, :, pos, :] = k.reshape(hkv, hd)
-        self.v[layer, :, pos, :] = v.reshape(hkv, hd)
+        if self.q8:
+            k, v = kv_q8_roundtrip(k), kv_q8_roundtrip(v)
+        self.k[layer, :, pos, :] = np.asarray(k).reshape(hkv, hd)
+        self.v[layer, :, pos, :] = np.asarray(v).reshape(hkv, hd)
         self.size = max(self.size, pos + 1)
 
 
@@ -306,7 +328,7 @@ class LlamaModelRef:
     q[k] = sum_e B[e][k] x[e]; wo: y[e] = sum_k B[k][e] a[k].
     """
 
-    def __init__(self, cfg: LlamaConfig, tensors: dict, layout: int = 0):
+    def __init__(self, cfg: LlamaConfig, tensors: dict, layout: int = 0, kv_type: int = 0):
         self.cfg = cfg
         c = cfg
         self.tok_embd = load_weight(tensors, "token_embd.weight", TENSOR_DIMS["token_embd.weight"](c), layout)
@@ -318,7 +340,7 @@ class LlamaModelRef:
             for nm in LAYER_TENSORS:
                 lw[nm] = load_weight(tensors, f"blk.{L}.{nm}", TENSOR_DIMS[nm](c), layout)
             self.layers.append(lw)
-        self.kv = KVCache(c.block_count, c.head_count_kv, c.head_dim, c.context_length)
+        self.kv = KVCache(c.block_count, c.head_count_kv, c.head_dim, c.context_length, q8=(kv_type == GGML_Q8_0))
         self.cos, self.sin = rope_tables(c.head_dim, c.rope_freq_base, c.context_length)
         self.x = np.zeros(c.embedding_length, dtype=np.float32)
 

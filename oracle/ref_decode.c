@@ -33,6 +33,7 @@ typedef struct {
     int dim, ffn, n_heads, n_kv, vocab, ctx, n_layers;
     float rope_base, eps;
     int layout; /* bit 0: llama.cpp split-halves Q4_0 nibbles; bit 1: attention bytes [out][in] */
+    int kv_q8;  /* 1: K/V rounded as the device's Q8_0 KV cache stores them (no reference counterpart) */
 } rd_cfg;
 
 typedef struct {
@@ -63,6 +64,44 @@ static float fp16_ftz(uint16_t h) {
 
 /* Q6_K.dequantToFloat (quant/Q6_K.java:54-102, the published llama.cpp
  * dequantize_row_q6_K) of one 210-byte block into 256 floats. */
+/* float -> fp16 bits, round to nearest even (IEEE conversion). */
+static uint16_t f32_to_f16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u, ax = x & 0x7FFFFFFFu;
+    if (ax >= 0x7F800000u) return (uint16_t)(sign | (ax > 0x7F800000u ? 0x7E00u : 0x7C00u));
+    if (ax >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u); /* rounds past 65504 */
+    if (ax < 0x38800000u) {                                   /* below 2^-14: subnormal (or zero) */
+        float a;
+        memcpy(&a, &ax, 4);
+        const double q = nearbyint((double)a * 16777216.0);   /* units of 2^-24, ties to even */
+        return (uint16_t)(sign | (uint32_t)q);
+    }
+    uint32_t h = (((ax >> 23) - 112u) << 10) | ((ax & 0x7FFFFFu) >> 13);
+    const uint32_t rem = ax & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h;
+    return (uint16_t)(sign | h);
+}
+
+static float fp16_ftz(uint16_t h);
+
+/* The device's Q8_0 KV rounding of n values (blocks of 32): d = max|x| / 127
+ * stored as fp16, q = roundf(x * (1 / d)) clamped to +-127, x <- q * d. */
+static void kv_q8_round(float* x, int n) {
+    for (int b = 0; b < n; b += 32) {
+        float amax = 0.f;
+        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[b + i]));
+        const float d = amax / 127.f;
+        const float id = d != 0.f ? 1.f / d : 0.f;
+        const float dd = fp16_ftz(f32_to_f16(d));
+        for (int i = 0; i < 32; ++i) {
+            float q = roundf(x[b + i] * id);
+            q = q > 127.f ? 127.f : (q < -127.f ? -127.f : q);
+            x[b + i] = q * dd;
+        }
+    }
+}
+
 static void dequant_q6_k_block(const uint8_t* p, float* y) {
     const float d = fp16_ftz((uint16_t)(p[208] | (p[209] << 8)));
     for (int n = 0; n < 256; n += 128) {
@@ -271,6 +310,10 @@ static void layer_step(rd_model* m, int l, int pos) {
     const float* sr = m->rsin + (size_t)pos * hd;
     rope(m->q, cr, sr, hd, H * hd);
     rope(m->k, cr, sr, hd, Hkv * hd);
+    if (c->kv_q8) {
+        kv_q8_round(m->k, Hkv * hd);
+        kv_q8_round(m->v, Hkv * hd);
+    }
     for (int h = 0; h < Hkv; ++h) {
         const size_t off = (((size_t)l * Hkv + h) * ctx + pos) * hd;
         memcpy(m->kc + off, m->k + (size_t)h * hd, hd * 4);

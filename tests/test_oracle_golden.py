@@ -139,19 +139,21 @@ def test_missing_output_weight_gives_zero_logits():
     assert np.all(ref.LlamaModelRef(cfg, t).forward_step(1, 0) == 0)
 
 
-@pytest.mark.parametrize("which", ["reference_layout", "llama_cpp_layout"])
+@pytest.mark.parametrize("which", ["reference_layout", "llama_cpp_layout", "q8_0_kv"])
 def test_c_restatement_matches_numpy_oracle(which):
     """The C restatement (CPU baseline) and the numpy oracle agree on a tiny
-    model, in the reference's byte layout and in llama.cpp's (split-halves
-    Q4_0, [out][in] attention, Q6_K embedding and output)."""
+    model, in the reference's byte layout, in llama.cpp's (split-halves
+    Q4_0, [out][in] attention, Q6_K embedding and output) and with the Q8_0
+    KV-cache rounding."""
     from auratensor_b200 import synth
     from oracle.cref import RefDecoder
-    shape = synth.TINY if which == "reference_layout" else synth.TINY_LLAMACPP
+    shape = synth.TINY_LLAMACPP if which == "llama_cpp_layout" else synth.TINY
+    kv_type = ref.GGML_Q8_0 if which == "q8_0_kv" else 0
     t = synth.generate_numpy(shape, seed=31)
     cfg = ref.LlamaConfig(shape.ctx, shape.dim, shape.n_layers, shape.n_heads, shape.n_kv_heads, shape.ffn,
                           shape.rope_theta, shape.eps, shape.vocab)
-    a = ref.LlamaModelRef(cfg, t, layout=shape.layout)
-    b = RefDecoder(shape, threads=2)
+    a = ref.LlamaModelRef(cfg, t, layout=shape.layout, kv_type=kv_type)
+    b = RefDecoder(shape, threads=2, kv_type=kv_type)
     for name, tt in t.items():
         b.set_tensor(name, tt["type"], tt["data"], int(np.prod(tt["dims"])))
     for pos, tok in enumerate([3, 99, 500, 7, 7]):
@@ -207,3 +209,21 @@ def test_llama_cpp_layout_is_the_same_model():
     for pos, tok in enumerate([3, 99, 500]):
         la, lb = a.forward_step(tok, pos), b.forward_step(tok, pos)
         assert np.max(np.abs(la - lb)) <= 1e-5 * float(lb.max() - lb.min())
+
+
+def test_kv_q8_rounding():
+    """The Q8_0 KV rounding: zero blocks stay zero, the block maximum is kept
+    to fp16 precision, every value is within half a step d / 2 (plus the
+    fp16 rounding of d), ties round away from zero."""
+    rng = np.random.default_rng(9)
+    x = (rng.standard_normal(32 * 50) * rng.choice([1e-3, 1.0, 40.0], 32 * 50)).astype(np.float32)
+    x[:32] = 0.0
+    y = ref.kv_q8_roundtrip(x)
+    assert np.all(y[:32] == 0)
+    xb, yb = x.reshape(-1, 32), y.reshape(-1, 32)
+    d = np.max(np.abs(xb), axis=1) / 127.0
+    assert np.all(np.abs(xb - yb) <= d[:, None] * (0.5 + 127 * 2.0 ** -11) + 1e-30)
+    # 0.5 * d lands exactly half way: rounds away from zero
+    t = np.zeros(32, dtype=np.float32)
+    t[0], t[1], t[2] = 127.0, 0.5, -0.5
+    assert ref.kv_q8_roundtrip(t)[1:3].tolist() == [1.0, -1.0]
