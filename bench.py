@@ -73,11 +73,16 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-parity", action="store_true")
     p.add_argument("--config", default="llama-3-8b", choices=sorted(CONFIGS))
+    p.add_argument("--kv-type", default="f32", choices=["f32", "q8_0"],
+                   help="KV cache storage (q8_0: the quantized cache, a stated 2e-2 logit tolerance)")
     # smaller cases for profiler captures only (the bench line uses the defaults)
     p.add_argument("--prompt", type=int, default=None)
     p.add_argument("--layers", type=int, default=None)
     a = p.parse_args()
     shape_name, a.metric, prompt, a.batch, a.sampler = CONFIGS[a.config]
+    a.kv = 8 if a.kv_type == "q8_0" else 0
+    if a.kv:
+        a.metric = a.metric.replace(" tok/s", " (Q8_0 KV) tok/s")
     a.shape_name = shape_name
     if a.prompt is None:
         a.prompt = prompt
@@ -153,7 +158,7 @@ def q_bytes(rows, cols, bpb=18):
     return rows * (cols // 32) * bpb
 
 
-def class_bytes(shape, world, pos, batch=1):
+def class_bytes(shape, world, pos, batch=1, kv_type=0):
     """Algorithmic bytes of one step per kernel class: the quantized weights
     once, the activations in and out of every row, and each row's KV cache
     up to its position (pos: one position or one per row)."""
@@ -163,21 +168,22 @@ def class_bytes(shape, world, pos, batch=1):
     qkv_cols = (hl + 2 * hkvl) * hd
     bpb = 34 if shape.wtype == 8 else 18
     ps = list(pos) if isinstance(pos, (list, tuple)) else [pos] * batch
+    kv_elem = 4 if kv_type == 0 else 1 + 2 / 32  # bytes per cached element (Q8_0: quant + shared fp16 scale)
     return {
         "qkv": q_bytes(d, qkv_cols, bpb) + batch * (d * 4 + qkv_cols * 4),
         "wo": q_bytes(hl * hd, d, bpb) + batch * (hl * hd * 4 + d * 4),
         "ffn_up": 2 * q_bytes(fl, d, bpb) + batch * (d * 4 + fl * 4),
         "ffn_down": q_bytes(d, fl, bpb) + batch * (fl * 4 + d * 4),
         "lm_head": q_bytes(vl, d, bpb) + batch * (d * 4 + vl * 4),
-        "attn": sum(2 * hkvl * (p + 1) * hd * 4 + 2 * hl * hd * 4 for p in ps),
+        "attn": sum(2 * hkvl * (p + 1) * hd * kv_elem + 2 * hl * hd * 4 for p in ps),
     }
 
 
-def step_bytes_of(shape, world, positions_per_step, batch):
+def step_bytes_of(shape, world, positions_per_step, batch, kv_type=0):
     """Mean bytes one GPU must move per step over the timed steps."""
     tot = 0.0
     for pos in positions_per_step:
-        cb = class_bytes(shape, world, pos, batch)
+        cb = class_bytes(shape, world, pos, batch, kv_type)
         tot += shape.n_layers * (cb["qkv"] + cb["attn"] + cb["wo"] + cb["ffn_up"] + cb["ffn_down"])
         tot += cb["lm_head"] + batch * q_bytes(1, shape.dim, 34 if shape.wtype == 8 else 18)
     return tot / len(positions_per_step)
@@ -306,11 +312,12 @@ def workload_name(args, shape):
 # ---------------------------------------------------------------------------
 # our engine
 # ---------------------------------------------------------------------------
-def build_model(shape, seed, ctx, world, keep_host: bool, max_batch: int = 1):
+def build_model(shape, seed, ctx, world, keep_host: bool, max_batch: int = 1, kv_type: int = 0):
     import torch
     from auratensor_b200 import synth
     from auratensor_b200.inference import LlamaConfig, LlamaModel
-    model = LlamaModel(LlamaConfig.fromShape(shape), None, max_batch=max_batch, ctx=ctx, world=world)
+    model = LlamaModel(LlamaConfig.fromShape(shape), None, max_batch=max_batch, ctx=ctx, world=world,
+                       kv_type=kv_type)
     g = torch.Generator(device="cuda").manual_seed(seed)
     host = {}
     for name, dims, t in shape.tensor_dims():
@@ -324,7 +331,7 @@ def build_model(shape, seed, ctx, world, keep_host: bool, max_batch: int = 1):
     return model, host
 
 
-def parity_check(full_shape, seed, ctx, world, rank):
+def parity_check(full_shape, seed, ctx, world, rank, kv_type=0):
     """The bench's decode path against the oracle, in the same run and at the
     same tensor-parallel degree: a 2-layer model of the bench's dimensions
     (the same kernels and shard sizes) on every rank, and the C restatement
@@ -342,11 +349,11 @@ def parity_check(full_shape, seed, ctx, world, rank):
     shape = dataclasses.replace(full_shape, n_layers=2, ctx=64)
     n_prompt, n_greedy, tol = 8, 16, 1e-3
     g = torch.Generator(device="cuda").manual_seed(seed + 1000)
-    model = LlamaModel(LlamaConfig.fromShape(shape), None, max_batch=1, ctx=ctx, world=world)
+    model = LlamaModel(LlamaConfig.fromShape(shape), None, max_batch=1, ctx=ctx, world=world, kv_type=kv_type)
     orc = None
     if rank == 0:
         from oracle.cref import RefDecoder
-        orc = RefDecoder(shape, threads=os.cpu_count() or 1)
+        orc = RefDecoder(shape, threads=os.cpu_count() or 1, kv_type=kv_type)
     for name, dims, t in shape.tensor_dims():
         data = synth.generate_torch_tensor(dims, t, g, "cuda")
         model.setTensor(name, t, data)
@@ -421,7 +428,7 @@ def main():
     PROMPT = args.prompt
     keep_host = (rank == 0 and world == 1 and not args.no_cpu_baseline and args.layers is None)
     t0 = time.time()
-    model, host = build_model(shape, args.seed, ctx, world, keep_host)
+    model, host = build_model(shape, args.seed, ctx, world, keep_host, kv_type=args.kv)
     load_s = time.time() - t0
     stream = torch.cuda.ExternalStream(model.stream())
 
@@ -504,20 +511,21 @@ def main():
     e2e = args.steps / (ms_e2e / 1000.0)
     parity = None
     if not args.no_parity:
-        parity = parity_check(shape, args.seed, ctx, world, rank)
+        parity = parity_check(shape, args.seed, ctx, world, rank, args.kv)
     if rank != 0:
         finish(model, ctx, world)
         return
-    bytes_per = class_bytes(shape, world, pos)
+    bytes_per = class_bytes(shape, world, pos, 1, args.kv)
     # bytes one GPU must move per decode step (weights of its shards, its KV
     # heads at the timed positions, activations), over the measured step time
-    step_bytes = step_bytes_of(shape, world, timed_pos, 1)
+    step_bytes = step_bytes_of(shape, world, timed_pos, 1, args.kv)
     gemv = {k: v for k, v in tot.items() if k in bytes_per}
     dom = max(gemv, key=lambda k: gemv[k][0])
     avg_ms = gemv[dom][0] / max(1, gemv[dom][1])
     peak, peak_kind = load_peaks()
     achieved = bytes_per[dom] / (avg_ms / 1000.0) / 1e9
-    traffic = committed_traffic().get(dom)
+    # the committed capture is of the default workload (Llama-3-8B, fp32 KV, one GPU)
+    traffic = committed_traffic().get(dom) if (args.config == "llama-3-8b" and not args.kv and world == 1) else None
     step_ms_eager = sum(v[0] for v in tot.values()) / args.profile_steps
     # embed; per layer QKV, attention (split + merge in one launch), wo, gate/up, down (+ two
     # all-reduces under TP); lm_head, argmax (2), greedy advance (+ logits gather under TP)
@@ -541,7 +549,7 @@ def main():
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": workload_name(args, shape), "batch": 1, "prompt_tokens": PROMPT, "context": ctx_len,
                    "weights": f"Q4_0 ({wbytes / 1e9:.1f} GB, > L2; no flush needed)", "parallelism": f"tp{world}",
-                   "seed": args.seed},
+                   "kv_cache": args.kv_type, "seed": args.seed},
         "e2e": {"value": round(e2e, 3), "unit": UNIT, "h2d_bytes_per_step": 12,
                 "d2h_bytes_per_step": shape.vocab * 4},
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": peak,
@@ -565,7 +573,7 @@ def main():
     finish(model, ctx, world)
 
 
-def batched_parity(full_shape, seed, ctx, batch, sampler):
+def batched_parity(full_shape, seed, ctx, batch, sampler, kv_type=0):
     """The batched sampled path against the oracle in the same run: a 2-layer
     model of the workload's dimensions with `batch` slots. Every row decodes
     its own 6-token seeded prompt and then 10 sampled tokens, all rows in one
@@ -585,8 +593,8 @@ def batched_parity(full_shape, seed, ctx, batch, sampler):
     shape = dataclasses.replace(full_shape, n_layers=2, ctx=64)
     n_prompt, n_gen, tol = 6, 10, 1e-3
     g = torch.Generator(device="cuda").manual_seed(seed + 2000)
-    model = LlamaModel(LlamaConfig.fromShape(shape), None, max_batch=batch, ctx=ctx)
-    orc = RefDecoder(shape, threads=os.cpu_count() or 1)
+    model = LlamaModel(LlamaConfig.fromShape(shape), None, max_batch=batch, ctx=ctx, kv_type=kv_type)
+    orc = RefDecoder(shape, threads=os.cpu_count() or 1, kv_type=kv_type)
     for name, dims, t in shape.tensor_dims():
         data = synth.generate_torch_tensor(dims, t, g, "cuda")
         model.setTensor(name, t, data)
@@ -644,7 +652,7 @@ def run_batched(args, shape, ctx, world, rank, local):
     assert n_prompt + total_steps <= ctx_len, "steps exceed the context"
     keep_host = not args.no_cpu_baseline and args.layers is None
     t0 = time.time()
-    model, host = build_model(shape, args.seed, ctx, world, keep_host, max_batch=B)
+    model, host = build_model(shape, args.seed, ctx, world, keep_host, max_batch=B, kv_type=args.kv)
     load_s = time.time() - t0
     stream = torch.cuda.ExternalStream(model.stream())
     prompts = [synth.prompt_ids(shape, args.seed + b, n_prompt).tolist() for b in range(B)]
@@ -693,7 +701,7 @@ def run_batched(args, shape, ctx, world, rank, local):
     agree = sum(int(np.array_equal(sched_tokens[b][: args.warmup + args.steps],
                                    np.concatenate([warm[b], out[b]]))) for b in range(B))
     timed_pos = [[n_prompt - 1 + args.warmup + i] * B for i in range(args.steps)]
-    step_bytes = step_bytes_of(shape, world, timed_pos, B)
+    step_bytes = step_bytes_of(shape, world, timed_pos, B, args.kv)
     # roofline of the dominant kernel class at batch B (eager, one event pair per launch)
     tot = {}
     prof_pos = n_prompt - 1 + total_steps
@@ -704,13 +712,13 @@ def run_batched(args, shape, ctx, world, rank, local):
             a = tot.setdefault(k, [0.0, 0])
             a[0] += msk
             a[1] += n
-    bytes_per = class_bytes(shape, world, prof_pos, B)
+    bytes_per = class_bytes(shape, world, prof_pos, B, args.kv)
     gemv = {k: v for k, v in tot.items() if k in bytes_per}
     dom = max(gemv, key=lambda k: gemv[k][0])
     avg_ms = gemv[dom][0] / max(1, gemv[dom][1])
     peak, peak_kind = load_peaks()
     achieved = bytes_per[dom] / (avg_ms / 1000.0) / 1e9
-    parity = None if args.no_parity else batched_parity(shape, args.seed, ctx, B, args.sampler)
+    parity = None if args.no_parity else batched_parity(shape, args.seed, ctx, B, args.sampler, args.kv)
     cpu = None
     if keep_host:
         threads = os.cpu_count() or 1
@@ -731,6 +739,7 @@ def run_batched(args, shape, ctx, world, rank, local):
                    "context": ctx_len, "sampler": {"temperature": T, "top_k": K, "top_p": P,
                                                    "repetition_penalty": R, "seeds": [c.seed for c in cfgs]},
                    "weights": "Q8_0 (7.7 GB, > L2; no flush needed)", "parallelism": "tp1", "seed": args.seed,
+                   "kv_cache": args.kv_type,
                    "step": f"one batched step = {B} tokens"},
         "e2e": {"value": round(e2e, 3), "unit": UNIT, "h2d_bytes_per_step": B * (4 + 8 + 4),
                 "d2h_bytes_per_step": B * 4, "api": "at_sched_step (request scheduler)",
