@@ -142,7 +142,7 @@ int at_gemv(at_ctx* ctx, const at_qmat* m, const float* x_dev, float* y_dev, int
  * held by every GPU that loads the library until exit. Shapes whose split
  * needs more are rejected with AT_ERR_INVALID_ARG. The first call on a device
  * looks up the array's device address (cudaGetSymbolAddress, with that device
- * current); make that first call before any stream capture. Every call shares
+ * current). Every call shares
  * the array and zeroes the counters first: calls that overlap on the GPU
  * (other streams or contexts of the same device) race. No counterpart in the
  * reference. m must be stored for AT_ORIENT_T. */
