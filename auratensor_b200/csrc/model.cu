@@ -743,6 +743,172 @@ __global__ void __launch_bounds__(256) rows_addnorm_kernel(const float* __restri
 // RoPE of q and k (core/Kernels.java:296-309: a' = fma(a, c, b * -s),
 // b' = fma(b, c, a * s)) and the KV-cache append (inference/KVCache.java:79-95)
 // of prompt row t at position p0 + t; q goes to q_out [T][nq].
+// Causal attention of a prompt chunk (LlamaModel.attention, inference/
+// LlamaModel.java:255-297, for T consecutive query positions p0 .. p0+T-1).
+// CTA (KV head h, query block) holds R = 32 query rows (QB = 32 / G tokens x
+// the G query heads of h) and streams the keys 0 .. (its last position) in
+// tiles of 64 through shared memory (K and V of the tile; Q8_0 caches are
+// dequantized on the way in): warp w scores rows 4w .. 4w+3 against keys
+// lane and lane + 32 (q rows are broadcast reads, K rows padded to spread the
+// banks), keeps a running max and sum per row (online softmax; keys past a
+// row's own position are masked), writes the tile's probabilities to shared
+// memory and adds P V into its rows' outputs (lane: HD / 32 dimensions).
+// Every K/V row a query block needs is read once per block instead of once
+// per query token. Scores are dot * scale as the reference; the prompt
+// path's tolerance is 2e-2 of the logit range.
+constexpr int PA_R = 32, PA_KT = 64;
+constexpr size_t prompt_attn_smem(int hd) {
+    return (size_t)(PA_R * (hd + 4) + PA_KT * (hd + 4) + PA_KT * hd + PA_R * PA_KT) * 4;
+}
+
+template <int HD, int G, bool KVQ>
+__global__ void __launch_bounds__(256) prompt_attn_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                                                          const float* __restrict__ vc,
+                                                          const uint16_t* __restrict__ ksc,
+                                                          const uint16_t* __restrict__ vsc, float* __restrict__ att,
+                                                          int T, int64_t p0, int Hl, int ctx, float scale) {
+    constexpr int QB = PA_R / G;   // tokens per CTA
+    constexpr int KP = HD + 4;     // padded q / K row (floats)
+    constexpr int F4 = HD / 4;
+    constexpr int DPL = HD / 32;   // output dimensions per lane
+    extern __shared__ __align__(16) float pa_smem[];
+    float* qs = pa_smem;                 // [R][KP]
+    float* ks = qs + PA_R * KP;          // [KT][KP]
+    float* vs = ks + PA_KT * KP;         // [KT][HD]
+    float* ps = vs + PA_KT * HD;         // [R][KT]
+    const int kvh = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nq = Hl * HD;
+    const int t0 = blockIdx.y * QB;
+    const int ntok = min(QB, T - t0);
+    // q rows: row r = ti * G + g is token t0 + ti, query head kvh * G + g
+    for (int i = tid; i < PA_R * F4; i += 256) {
+        const int r = i / F4, f = i - r * F4;
+        const int ti = r / G, g = r - ti * G;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ti < ntok) v = *reinterpret_cast<const float4*>(q + (size_t)(t0 + ti) * nq + (size_t)(kvh * G + g) * HD + 4 * f);
+        *reinterpret_cast<float4*>(qs + r * KP + 4 * f) = v;
+    }
+    int64_t rpos[4];  // position of this warp's rows (-1: no token)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int ti = (4 * warp + j) / G;
+        rpos[j] = ti < ntok ? p0 + t0 + ti : -1;
+    }
+    const int64_t last = p0 + t0 + ntok - 1;
+    const size_t kvbase = (size_t)kvh * ctx * HD;
+    float m[4], l[4], o[4][DPL];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        m[j] = -INFINITY;
+        l[j] = 0.f;
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) o[j][d] = 0.f;
+    }
+    for (int64_t k0 = 0; k0 <= last; k0 += PA_KT) {
+        const int nk = (last + 1 - k0) < PA_KT ? (int)(last + 1 - k0) : PA_KT;
+        __syncthreads();  // the previous tile's K and V are no longer read
+        for (int i = tid; i < PA_KT * F4; i += 256) {
+            const int kr = i / F4, f = i - kr * F4;
+            float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;
+            if (kr < nk) {
+                const size_t e = kvbase + (size_t)(k0 + kr) * HD;
+                if constexpr (KVQ) {
+                    kv4 = kv_dq4(reinterpret_cast<const int8_t*>(kc) + e, ksc + (e >> 5), f);
+                    vv4 = kv_dq4(reinterpret_cast<const int8_t*>(vc) + e, vsc + (e >> 5), f);
+                } else {
+                    kv4 = *reinterpret_cast<const float4*>(kc + e + 4 * f);
+                    vv4 = *reinterpret_cast<const float4*>(vc + e + 4 * f);
+                }
+            }
+            *reinterpret_cast<float4*>(ks + kr * KP + 4 * f) = kv4;
+            *reinterpret_cast<float4*>(vs + kr * HD + 4 * f) = vv4;
+        }
+        __syncthreads();
+        float sc[4][2];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sc[j][0] = sc[j][1] = 0.f;
+#pragma unroll 4
+        for (int f = 0; f < F4; ++f) {
+            const float4 ka = *reinterpret_cast<const float4*>(ks + lane * KP + 4 * f);
+            const float4 kb = *reinterpret_cast<const float4*>(ks + (lane + 32) * KP + 4 * f);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float4 qv = *reinterpret_cast<const float4*>(qs + (4 * warp + j) * KP + 4 * f);
+                sc[j][0] = fmaf(qv.x, ka.x, fmaf(qv.y, ka.y, fmaf(qv.z, ka.z, fmaf(qv.w, ka.w, sc[j][0]))));
+                sc[j][1] = fmaf(qv.x, kb.x, fmaf(qv.y, kb.y, fmaf(qv.z, kb.z, fmaf(qv.w, kb.w, sc[j][1]))));
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const bool ia = lane < nk && k0 + lane <= rpos[j];
+            const bool ib = lane + 32 < nk && k0 + lane + 32 <= rpos[j];
+            const float a = ia ? __fmul_rn(sc[j][0], scale) : -INFINITY;
+            const float bq = ib ? __fmul_rn(sc[j][1], scale) : -INFINITY;
+            const float mn = fmaxf(m[j], warp_max(fmaxf(a, bq)));
+            const float alpha = (mn == -INFINITY) ? 1.f : expf(m[j] - mn);
+            const float pa = ia ? expf(a - mn) : 0.f;
+            const float pb = ib ? expf(bq - mn) : 0.f;
+            l[j] = fmaf(l[j], alpha, warp_sum(pa + pb));
+            m[j] = mn;
+            ps[(4 * warp + j) * PA_KT + lane] = pa;
+            ps[(4 * warp + j) * PA_KT + lane + 32] = pb;
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) o[j][d] *= alpha;
+        }
+        __syncwarp();  // this warp's probabilities are visible to its lanes
+        for (int kk = 0; kk < nk; ++kk) {
+            float vv[DPL];
+            if constexpr (DPL == 4) {
+                const float4 t = *reinterpret_cast<const float4*>(vs + kk * HD + 4 * lane);
+                vv[0] = t.x; vv[1] = t.y; vv[2] = t.z; vv[3] = t.w;
+            } else {
+                const float2 t = *reinterpret_cast<const float2*>(vs + kk * HD + 2 * lane);
+                vv[0] = t.x; vv[1] = t.y;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float pj = ps[(4 * warp + j) * PA_KT + kk];
+#pragma unroll
+                for (int d = 0; d < DPL; ++d) o[j][d] = fmaf(pj, vv[d], o[j][d]);
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int r = 4 * warp + j, ti = r / G, g = r - ti * G;
+        if (ti < ntok) {
+            float* dst = att + (size_t)(t0 + ti) * nq + (size_t)(kvh * G + g) * HD + DPL * lane;
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) dst[d] = __fdiv_rn(o[j][d], l[j]);
+        }
+    }
+}
+
+template <int HD, bool KVQ, int G>
+void launch_prompt_attn_g(int Hkvl, int T, cudaStream_t s, const float* q, const float* kc, const float* vc,
+                          const uint16_t* ksc, const uint16_t* vsc, float* att, int64_t p0, int Hl, int ctx,
+                          float scale) {
+    auto kern = prompt_attn_kernel<HD, G, KVQ>;
+    const size_t smem = prompt_attn_smem(HD);
+    AT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    constexpr int QB = PA_R / G;
+    kern<<<dim3(Hkvl, (T + QB - 1) / QB), 256, smem, s>>>(q, kc, vc, ksc, vsc, att, T, p0, Hl, ctx, scale);
+    AT_CUDA(cudaGetLastError());
+}
+
+template <int HD, bool KVQ>
+void launch_prompt_attn(int G, int Hkvl, int T, cudaStream_t s, const float* q, const float* kc, const float* vc,
+                        const uint16_t* ksc, const uint16_t* vsc, float* att, int64_t p0, int Hl, int ctx,
+                        float scale) {
+    switch (G) {
+#define AT_PA(GG) \
+    case GG: launch_prompt_attn_g<HD, KVQ, GG>(Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale); break;
+        AT_PA(1) AT_PA(2) AT_PA(3) AT_PA(4) AT_PA(5) AT_PA(6) AT_PA(7) AT_PA(8)
+#undef AT_PA
+        default: fail(AT_ERR_UNSUPPORTED, "query heads per KV head must be 1..8");
+    }
+}
+
 // Q8_0 KV cache of one layer (all slots; the slot offset is in the element index).
 struct KvQ {
     int8_t* kq = nullptr;
@@ -2168,17 +2334,25 @@ void run_prompt_batched(at_model* m, const int* tokens, int n, int slot) {
             rope_append_kernel<<<T, 256, 0, s>>>(m->pf_qkv, qcols, m->pf_q, kc, vc, kvq, m->rope_cos, m->rope_sin, hd,
                                                  nq, nkv, m->ctx_len, p0);
             AT_CUDA(cudaGetLastError());
-            dim3 g1(m->Hkvl, m->nchunk_max, T), g2(m->Hl, T);
-            if (hd == 128) {
-                launch_attn<128, 0, CH>(kvq, kc, vc, g1, dim3(1, 1, 1), attn_smem_bytes(128, CH), s, false, m->pf_q,
-                                        m->pf_pos, m->pf_part, m->Hl, m->Hkvl, m->ctx_len, 0, m->nchunk_max, scale,
-                                        nullptr, nullptr);
-                attn_combine_kernel<128><<<g2, 128, 0, s>>>(m->pf_part, m->pf_pos, m->pf_att, m->Hl, m->nchunk_max);
-            } else {
-                launch_attn<64, 0, CH>(kvq, kc, vc, g1, dim3(1, 1, 1), attn_smem_bytes(64, CH), s, false, m->pf_q,
-                                       m->pf_pos, m->pf_part, m->Hl, m->Hkvl, m->ctx_len, 0, m->nchunk_max, scale,
-                                       nullptr, nullptr);
-                attn_combine_kernel<64><<<g2, 64, 0, s>>>(m->pf_part, m->pf_pos, m->pf_att, m->Hl, m->nchunk_max);
+            {
+                const int G = m->Hl / m->Hkvl;
+                const float* kq = m->kv_q8 ? reinterpret_cast<const float*>(kvq.kq) : kc;
+                const float* vq = m->kv_q8 ? reinterpret_cast<const float*>(kvq.vq) : vc;
+                if (hd == 128) {
+                    if (m->kv_q8)
+                        launch_prompt_attn<128, true>(G, m->Hkvl, T, s, m->pf_q, kq, vq, kvq.ks, kvq.vs, m->pf_att, p0,
+                                                      m->Hl, m->ctx_len, scale);
+                    else
+                        launch_prompt_attn<128, false>(G, m->Hkvl, T, s, m->pf_q, kq, vq, nullptr, nullptr, m->pf_att,
+                                                       p0, m->Hl, m->ctx_len, scale);
+                } else {
+                    if (m->kv_q8)
+                        launch_prompt_attn<64, true>(G, m->Hkvl, T, s, m->pf_q, kq, vq, kvq.ks, kvq.vs, m->pf_att, p0,
+                                                     m->Hl, m->ctx_len, scale);
+                    else
+                        launch_prompt_attn<64, false>(G, m->Hkvl, T, s, m->pf_q, kq, vq, nullptr, nullptr, m->pf_att,
+                                                      p0, m->Hl, m->ctx_len, scale);
+                }
             }
             AT_CUDA(cudaGetLastError());
             if (L == m->L - 1) break;  // later layers' inputs only; the KV cache is complete

@@ -189,6 +189,37 @@ def step_bytes_of(shape, world, positions_per_step, batch, kv_type=0):
     return tot / len(positions_per_step)
 
 
+def prompt_flops(shape, n):
+    """FLOPs of the batched prompt path for n tokens: every layer's QKV and
+    attention (2 * 2 * H * hd * (p + 1) per token p), every layer but the
+    last's wo and feed-forward (only the KV cache carries over to decode)."""
+    d, hd, H, Hkv, F, L = shape.dim, shape.head_dim, shape.n_heads, shape.n_kv_heads, shape.ffn, shape.n_layers
+    qcols = (H + 2 * Hkv) * hd
+    linear = 2.0 * n * (L * d * qcols + (L - 1) * (H * hd * d + 3 * d * F))
+    attn = 4.0 * H * hd * L * n * (n + 1) / 2
+    return linear + attn
+
+
+def prompt_line(shape, world, n, dev_s, wall_s, requests=1):
+    """The prompt's device time (CUDA events on the engine's stream) and, on
+    one GPU (the tensor-core path), its FLOP rate against the bf16 peak."""
+    out = {"tokens": n * requests, "seconds": round(dev_s, 4), "wall_seconds": round(wall_s, 4),
+           "tok_s": round(n * requests / dev_s, 1) if dev_s > 0 else None}
+    if world == 1 and dev_s > 0:
+        peak = 1625.1
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peak = float(json.load(f)["bf16_tflops"])
+        except (OSError, KeyError, ValueError):
+            pass
+        tf = prompt_flops(shape, n) * requests / dev_s / 1e12
+        out.update({"path": "tcgen05 bf16 GEMMs, 128-token chunks", "tflops": round(tf, 1),
+                    "peak_tflops": peak, "frac": round(tf / peak, 4)})
+    else:
+        out["path"] = "decode steps (tensor parallel)"
+    return out
+
+
 def load_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -430,7 +461,6 @@ def main():
     t0 = time.time()
     model, host = build_model(shape, args.seed, ctx, world, keep_host, kv_type=args.kv)
     load_s = time.time() - t0
-    stream = torch.cuda.ExternalStream(model.stream())
 
     def barrier():
         if world > 1:
@@ -445,9 +475,16 @@ def main():
         return float(t.item())
 
     prompt = synth.prompt_ids(shape, args.seed, PROMPT).tolist()
+    stream = torch.cuda.ExternalStream(model.stream())
+    torch.cuda.synchronize()
     t0 = time.time()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
     model.forwardPrompt(prompt)
+    p1.record(stream)
+    p1.synchronize()
     prefill_s = time.time() - t0
+    prefill_dev_s = max_over_ranks(p0.elapsed_time(p1)) / 1000.0
     ctx_len = shape.ctx
 
     def positions(start, n):
@@ -566,8 +603,7 @@ def main():
         "cpu_baseline": cpu,
         "setup": {"load_s": round(load_s, 1), "prefill_s": round(prefill_s, 2)},
         # the untimed prompt (forwardPrompt: tcgen05 GEMMs over 128-token chunks on one GPU), host wall clock
-        "prompt": {"tokens": args.prompt, "seconds": round(prefill_s, 4),
-                   "tok_s": round(args.prompt / prefill_s, 1) if prefill_s > 0 else None},
+        "prompt": prompt_line(shape, world, args.prompt, prefill_dev_s, prefill_s),
     }
     print(json.dumps(line), flush=True)
     finish(model, ctx, world)
@@ -658,9 +694,14 @@ def run_batched(args, shape, ctx, world, rank, local):
     prompts = [synth.prompt_ids(shape, args.seed + b, n_prompt).tolist() for b in range(B)]
     torch.cuda.synchronize()
     t0 = time.time()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
     for b in range(B):
         model.forwardPromptSlot(b, prompts[b][:-1])
+    p1.record(stream)
+    p1.synchronize()
     prefill_s = time.time() - t0
+    prefill_dev_s = p0.elapsed_time(p1) / 1000.0
     first = [p[-1] for p in prompts]
     start = [n_prompt - 1] * B
     hists = [list(p) for p in prompts]
@@ -756,8 +797,7 @@ def run_batched(args, shape, ctx, world, rank, local):
         "clocks": clocks,
         "cpu_baseline": cpu,
         "setup": {"load_s": round(load_s, 1), "prefill_s": round(prefill_s, 2)},
-        "prompt": {"tokens": B * (n_prompt - 1), "seconds": round(prefill_s, 4),
-                   "tok_s": round(B * (n_prompt - 1) / prefill_s, 1) if prefill_s > 0 else None},
+        "prompt": prompt_line(shape, world, n_prompt - 1, prefill_dev_s, prefill_s, requests=B),
     }
     print(json.dumps(line), flush=True)
     finish(model, ctx, world)
