@@ -3,14 +3,15 @@
 //
 // The reference processes a prompt one token at a time (forwardPrompt,
 // inference/LlamaModel.java:166-175, each token a forwardStep over FP32
-// weights). Here every projection of a chunk of up to 128 tokens is one GEMM
+// weights). Here every projection of a chunk of up to 256 tokens is one GEMM
 // whose operands are bf16 (the prompt path's tolerance is 2e-2 of the logit
 // range): the weight tile is dequantized from the resident Q4_0 / Q8_0 tiles
 // ((q - 8) * d, or q * d, rounded once to bf16) straight into shared memory,
 // the activations are rounded to bf16 on the way in, and products are summed
 // in FP32 in tensor memory.
 //
-// CTA tile: 128 outputs (MMA M) x 128 tokens (MMA N), K in steps of 64.
+// CTA tile: 128 outputs (MMA M) x 256 tokens (MMA N), K in steps of 64, so a
+// dequantized weight tile feeds 256 tokens.
 // Both operands are K-major in the canonical 128-byte-swizzled layout: row r
 // of a tile is 128 bytes (64 bf16) at (r / 8) * 1024 + (r % 8) * 128, and
 // its 16-byte chunk c is stored at chunk position c ^ (r % 8). The token
@@ -44,14 +45,16 @@ namespace at {
 namespace {
 
 constexpr int TC_M = 128;        // outputs per CTA (MMA M)
-constexpr int TC_N = 128;        // tokens per CTA (MMA N)
+constexpr int TC_N = 256;        // tokens per CTA (MMA N)
 constexpr int TC_K = 64;         // K per pipeline step (one 128-byte swizzle row)
 constexpr int TC_DQ_WARPS = 8;   // warps that dequantize the weight tile (256 threads, one block each)
 constexpr int TC_THREADS_WS = 64 + 32 * TC_DQ_WARPS;  // + a TMA warp and an MMA warp
-constexpr int TC_TILE_BYTES = TC_M * TC_K * 2;  // 16 KB per operand tile (TC_N == TC_M)
+constexpr int TC_TILE_BYTES = TC_M * TC_K * 2;  // 16 KB weight tile
+constexpr int TC_B_BYTES = TC_N * TC_K * 2;     // 32 KB token tile
 constexpr int TC_STAGES = 4;
-constexpr int TC_SMEM = TC_STAGES * 2 * TC_TILE_BYTES + 1024;  // + alignment slack
-constexpr uint32_t TC_TMEM_COLS = 128;
+constexpr int TC_STAGE_BYTES = TC_TILE_BYTES + TC_B_BYTES;
+constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024;  // + alignment slack
+constexpr uint32_t TC_TMEM_COLS = TC_N;                     // FP32 accumulator columns
 constexpr int kTcSpinLimit = 1 << 26;
 constexpr int kTcMaxSplits = 4;
 
@@ -62,6 +65,7 @@ constexpr uint32_t make_idesc_bf16(int m, int n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 static_assert(make_idesc_bf16(128, 128) == 0x08200490u, "tcgen05 instruction descriptor");
+static_assert(make_idesc_bf16(TC_M, TC_N) == 0x08400490u, "tcgen05 instruction descriptor, N = 256");
 
 // Shared-memory matrix descriptor, K-major, 128-byte swizzle: start address
 // >> 4 (bits 0-13), leading byte offset 16 B (encoded 1, unused for this
@@ -151,7 +155,7 @@ struct TcParams {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-// TMA: box {64 k, 128 tokens} at (k0, t0) of the bf16 activations -> swizzled smem tile.
+// TMA: box {64 k, 256 tokens} at (k0, t0) of the bf16 activations -> swizzled smem tile.
 __device__ __forceinline__ void tma_load_x(uint32_t dst, const CUtensorMap* map, int k0, int t0, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
@@ -259,8 +263,8 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int m0 = blockIdx.x * TC_M, t0 = blockIdx.y * TC_N;
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    auto a_tile = [&](int st) { return base + st * 2 * TC_TILE_BYTES; };
-    auto b_tile = [&](int st) { return base + st * 2 * TC_TILE_BYTES + TC_TILE_BYTES; };
+    auto a_tile = [&](int st) { return base + st * TC_STAGE_BYTES; };
+    auto b_tile = [&](int st) { return base + st * TC_STAGE_BYTES + TC_TILE_BYTES; };
     const int nk_all = p.K / TC_K;
     const int ks0 = (int)((int64_t)blockIdx.z * nk_all / p.splits);
     const int nk = (int)((int64_t)(blockIdx.z + 1) * nk_all / p.splits) - ks0;  // steps of this split
@@ -300,7 +304,7 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
                     fail();
                     break;
                 }
-                mbar_expect_tx(smem_u32(&s_fb[st]), TC_TILE_BYTES);
+                mbar_expect_tx(smem_u32(&s_fb[st]), TC_B_BYTES);
                 tma_load_x(smem_u32(b_tile(st)), &xmap, kbase + ks * TC_K, t0, smem_u32(&s_fb[st]));
                 ++tma_issued;
             }
@@ -351,7 +355,7 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
         }
     }
 
-    // ---- epilogue: the accumulator (dequant warps 2-9: lanes 32 (w % 4) .., columns 64 ((w - 2) / 4) ..) ----
+    // ---- epilogue: the accumulator (dequant warps 2-9: lanes 32 (w % 4) .., columns 128 ((w - 2) / 4) ..) ----
     bool ok = mbar_wait(smem_u32(&s_done), 0);
     if (!ok && tid == 0) atomicExch(p.err, 2);
     __syncthreads();
@@ -366,9 +370,9 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
     if (ok && warp >= 2) {
         const int quarter = warp & 3, half = (warp - 2) >> 2;
         const int m = m0 + 32 * quarter + lane;
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-            const int col = 64 * half + 32 * cc;
+#pragma unroll 1
+        for (int cc = 0; cc < TC_N / 64; ++cc) {
+            const int col = (TC_N / 2) * half + 32 * cc;
             float v[32];
             tc_ld32(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)col, v);
             if (m < p.M) {

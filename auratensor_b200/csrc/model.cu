@@ -1083,7 +1083,7 @@ struct at_model {
     int* h_ar_err = nullptr;              // pinned copy, read after each step
     // batched prompt chunks (allocated on the first forwardPrompt that uses them)
     float *pf_xa = nullptr, *pf_xb = nullptr, *pf_y = nullptr, *pf_qkv = nullptr, *pf_q = nullptr;
-    float *pf_att = nullptr, *pf_g = nullptr, *pf_u = nullptr, *pf_part = nullptr;
+    float *pf_att = nullptr, *pf_g = nullptr, *pf_u = nullptr;
     void* pf_xbf = nullptr;               // bf16 activations of the prompt GEMMs
     size_t pf_xbf_bytes = 0;
     float* pf_ws = nullptr;               // split-K partials of the prompt GEMMs
@@ -1569,7 +1569,7 @@ void destroy_model(at_model* m) {
                     m->att_part, m->attn_cnt, m->kcache, m->vcache, m->rope_cos, m->rope_sin, m->scratch, m->counters,
                     m->d_tokens, m->d_pos, m->d_argmax, m->d_gen_out, m->d_gen_count, m->d_argkey,
                     m->d_step, m->ar_base, m->d_ar_err, m->pf_xa, m->pf_xb, m->pf_y, m->pf_qkv, m->pf_q,
-                    m->pf_att, m->pf_g, m->pf_u, m->pf_part, m->pf_tok, m->pf_pos, m->pf_err, m->pf_xbf, m->pf_ws,
+                    m->pf_att, m->pf_g, m->pf_u, m->pf_tok, m->pf_pos, m->pf_err, m->pf_xbf, m->pf_ws,
                     m->d_ds_layers, m->ds_qkv_part, m->ds_wo_part, m->ds_apart, m->ds_tickets, m->ds_bar,
                     m->ds_err, m->ds_stamps, m->qkvbuf, m->d_rows, m->d_hist, m->d_hist_len, m->d_pen_cnt,
                     m->d_rng, m->d_sampled, m->d_seq, m->d_step_ctr, m->d_append, m->kq8, m->vq8, m->ksc, m->vsc, m->kv_stage};
@@ -2244,11 +2244,11 @@ int at_model_forward_step(at_model* m, int token, int64_t position, float* logit
 
 // Prompt chunks of up to PF_T tokens go through every layer together: the
 // projections are tensor-core GEMMs (bf16 operands, FP32 sums; the prompt
-// path's tolerance is 2e-2 of the logit range), attention runs one row per
-// token against the growing KV cache of slot 0. Only the KV cache carries
+// path's tolerance is 2e-2 of the logit range), attention is the causal
+// prompt kernel over the KV cache of the target slot. Only the KV cache carries
 // over to the decode steps, so the last layer's feed-forward and the lm_head
 // are not needed; they are skipped.
-constexpr int PF_T = 128;
+constexpr int PF_T = 256;
 
 bool prompt_batched_ok(const at_model* m) {
     if (m->ctx->world != 1) return false;
@@ -2271,7 +2271,6 @@ void ensure_prompt_buffers(at_model* m) {
     alloc_zero((void**)&m->pf_att, PF_T * nq * 4);
     alloc_zero((void**)&m->pf_g, PF_T * (int64_t)m->Fl * 4);
     alloc_zero((void**)&m->pf_u, PF_T * (int64_t)m->Fl * 4);
-    alloc_zero((void**)&m->pf_part, PF_T * (int64_t)m->Hl * m->nchunk_max * (m->hd + 2) * 4);
     alloc_zero((void**)&m->pf_tok, PF_T * sizeof(int));
     alloc_zero((void**)&m->pf_pos, PF_T * sizeof(int64_t));
     alloc_zero((void**)&m->pf_err, sizeof(int));

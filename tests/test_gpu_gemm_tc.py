@@ -36,7 +36,7 @@ def check(qt, orient, rows, cols, tokens, cuda, seed=0):
 
 @pytest.mark.parametrize("qt", [ref.GGML_Q4_0, ref.GGML_Q8_0])
 @pytest.mark.parametrize("orient", [ORIENT_N, ORIENT_T])
-@pytest.mark.parametrize("tokens", [1, 37, 128, 200])
+@pytest.mark.parametrize("tokens", [1, 37, 128, 200, 256, 300, 512])
 def test_gemm_tc_small(qt, orient, tokens, cuda):
     check(qt, orient, 256, 128, tokens, cuda, seed=tokens)
 
