@@ -1597,6 +1597,24 @@ __device__ __forceinline__ void tq_decode_dn(const uint8_t* qp, float2* wv) {
     }
 }
 
+// tq_decode_dn from the quarter's bytes already in registers (Q4_0: w.x).
+template <int QT>
+__device__ __forceinline__ void tq_decode_dn_w(uint2 w2, float2* wv) {
+    if constexpr (QT == AT_GGML_Q4_0) {
+        const uint32_t w = w2.x, t = w >> 24;
+        wv[0] = f2(bits_f(w & 0xFu), bits_f(w & 0xF0u));
+        wv[1] = f2(bits_f(w & 0xF00u), bits_f(w & 0xF000u));
+        wv[2] = f2(bits_f(w & 0xF0000u), bits_f(w & 0xF00000u));
+        wv[3] = f2(bits_f(t & 0xFu), bits_f(t & 0xF0u));
+    } else {
+        const uint2 u = w2;
+        wv[0] = f2(bits_f((u.x ^ 0x80u) & 0xFFu), bits_f((u.x ^ 0x8000u) & 0xFF00u));
+        wv[1] = f2(bits_f((u.x ^ 0x800000u) & 0xFF0000u), bits_f((u.x >> 24) ^ 0x80u));
+        wv[2] = f2(bits_f((u.y ^ 0x80u) & 0xFFu), bits_f((u.y ^ 0x8000u) & 0xFF00u));
+        wv[3] = f2(bits_f((u.y ^ 0x800000u) & 0xFF0000u), bits_f((u.y >> 24) ^ 0x80u));
+    }
+}
+
 template <int QT, int B, Pro PRO, Epi EPI>
 __global__ void __launch_bounds__(THREADS, 2) gemv_tb_kernel(const TParams p) {
     constexpr int QB = QTraits<QT>::QB;
@@ -1637,22 +1655,24 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_tb_kernel(const TParams p) {
     // CTA's sums of t^2 over its rows are combined over the splits at the
     // end), times 2^kXExp; the padding (rows past the split, b >= B) is zero.
     const float xsc = exp2_i(kXExp);
-    for (int idx = tid; idx < nt * 32 * 8; idx += THREADS) {
-        const int i = idx >> 3, b = idx & 7;
-        if (i >= ne || b >= B) xs[idx] = 0.f;
+    if constexpr (B < 8) {
+        for (int idx = tid; idx < ne * (8 - B); idx += THREADS) xs[(idx / (8 - B)) * 8 + B + idx % (8 - B)] = 0.f;
     }
+    for (int idx = tid; idx < (nt * 32 - ne) * 8; idx += THREADS) xs[(size_t)ne * 8 + idx] = 0.f;
     {
         const int n4 = ne >> 2;
         float ss[B];
 #pragma unroll
         for (int b = 0; b < B; ++b) ss[b] = 0.f;
+        // item idx = (4-row group i4, batch row bb), bb fastest: B consecutive
+        // threads fill the 8-float rows of one group
         for (int base = 0; base < B * n4; base += THREADS * 4) {
             float4 v[4], gv[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const int idx = base + k * THREADS + tid;
                 if (idx < B * n4) {
-                    const int bb = idx / n4, e = e_lo + 4 * (idx - bb * n4);
+                    const int bb = idx % B, e = e_lo + 4 * (idx / B);
                     const size_t off = (size_t)bb * p.a.x_stride + e;
                     if constexpr (PRO == Pro::Plain) {
                         v[k] = *reinterpret_cast<const float4*>(p.a.x + off);
@@ -1672,7 +1692,7 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_tb_kernel(const TParams p) {
             for (int k = 0; k < 4; ++k) {
                 const int idx = base + k * THREADS + tid;
                 if (idx < B * n4) {
-                    const int bb = idx / n4, i = 4 * (idx - bb * n4);
+                    const int bb = idx % B, i = 4 * (idx / B);
                     float4 o = v[k];
                     if constexpr (fold) {
                         const float q = fmaf(o.x, o.x, fmaf(o.y, o.y, fmaf(o.z, o.z, __fmul_rn(o.w, o.w))));
@@ -1702,8 +1722,14 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_tb_kernel(const TParams p) {
     __syncthreads();
 
     const int qtr = lane & 3, rs = lane >> 2;
+    // d * x of a tile's rows, computed once per row (lane l: row l) into this
+    // warp's [32 rows][8] buffer; every quarter-lane of a row reads it
+    // d * x of a tile's rows, computed once per row (lane l: row l) into this
+    // warp's [32 rows][8] buffer; every quarter-lane of a row reads it
+    float* svw = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + p.ring_off + 8 * TB_NST * TBYTES) +
+                 warp * 32 * 8;
     float2 acc[B][4];
-    float dsum[B];  // this lane's sum of d * x * 2^kXExp (offset correction)
+    float dsum[B];  // sum of d * x * 2^kXExp over row `lane` of this warp's tiles (offset correction)
 #pragma unroll
     for (int b = 0; b < B; ++b) {
         dsum[b] = 0.f;
@@ -1716,40 +1742,64 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_tb_kernel(const TParams p) {
         __syncwarp();  // every lane's pieces of tile t have landed
         const uint8_t* sp = ring_ptr + (t & (TB_NST - 1)) * TBYTES;
         const int row0 = (warp + 8 * t) * 32;
+        {
+            const int ir = row0 + lane;
+            float sv[8];
+            if (ir < ne) {
+                const float d = fp16_ftz_fast(*reinterpret_cast<const uint16_t*>(sp + 2 * lane));
+                const float4 xa = *reinterpret_cast<const float4*>(xs + (size_t)ir * 8);
+                const float4 xb = *reinterpret_cast<const float4*>(xs + (size_t)ir * 8 + 4);
+                sv[0] = __fmul_rn(d, xa.x); sv[1] = __fmul_rn(d, xa.y); sv[2] = __fmul_rn(d, xa.z); sv[3] = __fmul_rn(d, xa.w);
+                sv[4] = __fmul_rn(d, xb.x); sv[5] = __fmul_rn(d, xb.y); sv[6] = __fmul_rn(d, xb.z); sv[7] = __fmul_rn(d, xb.w);
+            } else {
+#pragma unroll
+                for (int b = 0; b < 8; ++b) sv[b] = 0.f;
+            }
+#pragma unroll
+            for (int b = 0; b < B; ++b) dsum[b] += sv[b];
+            *reinterpret_cast<float4*>(svw + lane * 8) = make_float4(sv[0], sv[1], sv[2], sv[3]);
+            *reinterpret_cast<float4*>(svw + lane * 8 + 4) = make_float4(sv[4], sv[5], sv[6], sv[7]);
+        }
+        __syncwarp();  // the tile's d * x are visible to the warp
+        // the lane's 4 rows: quant words and d * x loaded together, then the products
+        uint2 qw[4];
+        float4 sa[4], sb[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int l = rs + 8 * i;
-            const int ir = row0 + l;
-            if (ir < ne) {
-                const float d = fp16_ftz_fast(*reinterpret_cast<const uint16_t*>(sp + 2 * l));
-                float2 wv[4];
-                tq_decode_dn<QT>(sp + 64 + l * QB + qtr * (QB / 4), wv);
-                const float4 xa = *reinterpret_cast<const float4*>(xs + (size_t)ir * 8);
-                const float4 xb = *reinterpret_cast<const float4*>(xs + (size_t)ir * 8 + 4);
-                const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+            const uint8_t* qp = sp + 64 + l * QB + qtr * (QB / 4);
+            if constexpr (QT == AT_GGML_Q4_0) qw[i] = make_uint2(*reinterpret_cast<const uint32_t*>(qp), 0u);
+            else qw[i] = *reinterpret_cast<const uint2*>(qp);
+            sa[i] = *reinterpret_cast<const float4*>(svw + l * 8);
+            sb[i] = *reinterpret_cast<const float4*>(svw + l * 8 + 4);
+        }
 #pragma unroll
-                for (int b = 0; b < B; ++b) {
-                    const float sv = __fmul_rn(d, xv[b]);
-                    dsum[b] += sv;
-                    const float2 s2 = f2(sv, sv);
+        for (int i = 0; i < 4; ++i) {
+            // rows past the split have d * x = 0: their products add nothing
+            float2 wv[4];
+            tq_decode_dn_w<QT>(qw[i], wv);
+            const float svr[8] = {sa[i].x, sa[i].y, sa[i].z, sa[i].w, sb[i].x, sb[i].y, sb[i].z, sb[i].w};
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) acc[b][k] = __ffma2_rn(wv[k], s2, acc[b][k]);
-                }
+            for (int b = 0; b < B; ++b) {
+                const float2 s2 = f2(svr[b], svr[b]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) acc[b][k] = __ffma2_rn(wv[k], s2, acc[b][k]);
             }
         }
-        __syncwarp();  // every lane is done with this slot before it is refilled
+        __syncwarp();  // every lane is done with this slot (and the d * x buffer) before they are refilled
     }
     cp_wait<0>();
 
     const float offs = (QT == AT_GGML_Q4_0) ? -8.f : -128.f;
 #pragma unroll
     for (int b = 0; b < B; ++b) {
-        const float corr = __fmul_rn(offs, __fmul_rn(dsum[b], exp2_i(-kXExp)));
+        // the offset times the sum of d * x over every row of this warp's tiles (all lanes)
+        const float corr = __fmul_rn(offs, __fmul_rn(warp_sum(dsum[b]), exp2_i(-kXExp)));
         float v[8];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            v[2 * k] = fmaf(acc[b][k].x, exp2_i(149 - kXExp - x_shift_dn<QT>(2 * k)), corr);
-            v[2 * k + 1] = fmaf(acc[b][k].y, exp2_i(149 - kXExp - x_shift_dn<QT>(2 * k + 1)), corr);
+            v[2 * k] = __fmul_rn(acc[b][k].x, exp2_i(149 - kXExp - x_shift_dn<QT>(2 * k)));
+            v[2 * k + 1] = __fmul_rn(acc[b][k].y, exp2_i(149 - kXExp - x_shift_dn<QT>(2 * k + 1)));
         }
         // reduce-scatter over the lanes of a quarter (lane bits 4, 8, 16): lane
         // (rs, quarter) ends with column 8 quarter + rs
@@ -1767,7 +1817,7 @@ __global__ void __launch_bounds__(THREADS, 2) gemv_tb_kernel(const TParams p) {
                 }
             }
         }
-        red[warp][b][8 * qtr + rs] = v[0];
+        red[warp][b][8 * qtr + rs] = v[0] + corr;
     }
     __syncthreads();
 
@@ -2075,7 +2125,7 @@ void t_config(const at_qmat* m, int batch, int num_sms, int* S, int* eps_rows) {
 constexpr int kTbMaxSplits = 16;
 bool tb_plan(int qtype, int64_t E, int64_t n_bc, int num_sms, int* S_out, int* rows_out) {
     const int tbytes = 64 + 32 * quant_bytes(qtype);
-    const int ring_bytes = 8 * TB_NST * tbytes;
+    const int ring_bytes = 8 * TB_NST * tbytes + 8 * 32 * 8 * 4;  // rings + the warps' d * x buffers
     const int ntiles = (int)((E + 31) / 32);
     int best_S = 0, best_rows = 0;
     double best_eff = -1.0;
@@ -2122,7 +2172,7 @@ bool run_tb(const at_qmat* m, const GemvArgs& a, int num_sms, cudaStream_t s, bo
     p.a = a;
     if (p.S > 1) AT_REQUIRE(a.scratch && a.counters, AT_ERR_STATE, "T GEMV needs split scratch");
     p.ring_off = p.e_per_split * 32;
-    const int smem = p.ring_off + 8 * TB_NST * TBYTES;
+    const int smem = p.ring_off + 8 * TB_NST * TBYTES + 8 * 32 * 8 * 4;  // + the warps' d * x buffers
     const void* fn = reinterpret_cast<const void*>(&gemv_tb_kernel<QT, B, PRO, EPI>);
     ensure_smem(fn, smem);
     launch(fn, p.n_bc * p.S, smem, s, pdl, p, THREADS, 1);
