@@ -2028,7 +2028,9 @@ NQLayout nq_layout(const at_qmat* m, int batch, int num_sms, int nm) {
     // CTAs per SM from the shared memory (x of one step + two-tile rings)
     const int smem = 32 * QX * 4 + Q_WARPS * Q_NST * 2 * (4 * 32 * (2 + quant_bytes(m->type)));
     const int occ = std::max(1, std::min(2, (227 * 1024) / (smem + 4 * 1024)));
-    l.P = (int)std::max<int64_t>(1, std::min<int64_t>(m->ngroups, (occ * num_sms + steps - 1) / steps));
+    // whole waves: P parts x steps CTAs within the SM slots (a second, mostly
+    // empty wave doubled the time of 4096 x 14336)
+    l.P = (int)std::max<int64_t>(1, std::min<int64_t>(m->ngroups, (int64_t)occ * num_sms / steps));
     l.part_floats = (size_t)steps * m->ngroups * 32 * nm;  // one 32-value partial per matrix and group
     l.ssq_floats = (size_t)l.P * steps * batch;
     return l;
