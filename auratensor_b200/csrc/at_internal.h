@@ -201,7 +201,8 @@ void gemv_n_scratch_need(const at_qmat* m, int batch, int num_sms, size_t* float
 void launch_gemv_q6k(const at_qmat* m, int batch, Pro pro, const GemvArgs& a, int num_sms, cudaStream_t s);
 // Tensor-core prompt GEMM (gemm_tc.cu): y[t][:] = W x[t][:], bf16 operands,
 // FP32 sums; xbf is a 128-byte aligned device buffer of at least T x in bf16
-// (the activations are converted into it); ws (FP32, may be null) holds the
+// (the activations are converted into it; with x null it already holds them,
+// rows of `in` elements); ws (FP32, may be null) holds the
 // partials when K is split across CTAs (gemm_tc_splits(m, T) x T x out
 // floats); *err records a bounded wait that ran out (2).
 int gemm_tc_splits(const at_qmat* m, int T, int num_sms);

@@ -12,17 +12,22 @@
 //
 // CTA tile: 128 outputs (MMA M) x 256 tokens (MMA N), K in steps of 64, so a
 // dequantized weight tile feeds 256 tokens.
-// Both operands are K-major in the canonical 128-byte-swizzled layout: row r
-// of a tile is 128 bytes (64 bf16) at (r / 8) * 1024 + (r % 8) * 128, and
-// its 16-byte chunk c is stored at chunk position c ^ (r % 8). The token
+// The token tile and the orientation-N weight tile are K-major in the
+// canonical 128-byte-swizzled layout: row r of a tile is 128 bytes (64 bf16)
+// at (r / 8) * 1024 + (r % 8) * 128, and its 16-byte chunk c is stored at
+// chunk position c ^ (r % 8). An orientation-T block holds 32 consecutive
+// outputs of one input, so that weight tile is M-major (the same swizzle with
+// the roles of outputs and inputs exchanged) and every thread still stores
+// 16-byte chunks. The token
 // tile (bf16 activations) arrives by TMA (cp.async.bulk.tensor with the
 // 128-byte swizzle, rows past the last token zero-filled), one step ahead,
 // completing on the stage's "full" mbarrier; the weight tile is dequantized
-// by all 8 warps from raw block bytes loaded into registers three steps ahead.
+// by one of two groups of 8 warps (alternate steps) from raw block bytes
+// loaded into registers three of the group's steps ahead.
 // One thread issues four tcgen05.mma (K = 16 each) per step and commits them
 // to the stage's "empty" mbarrier; four stages (TC_STAGES) keep the TMA, the dequant and
-// the tensor core working on different steps. The 128 x 128 FP32 accumulator
-// lives in 128 TMEM columns; the epilogue reads it with tcgen05.ld (warp w
+// the tensor core working on different steps. The 128 x 256 FP32 accumulator
+// lives in 256 TMEM columns; the epilogue reads it with tcgen05.ld (warp w
 // reads TMEM lanes 32 (w % 4) ..) and stores FP32 rows of Y.
 //
 // Every wait on an mbarrier is bounded; a wait that runs out records an error
@@ -47,8 +52,9 @@ namespace {
 constexpr int TC_M = 128;        // outputs per CTA (MMA M)
 constexpr int TC_N = 256;        // tokens per CTA (MMA N)
 constexpr int TC_K = 64;         // K per pipeline step (one 128-byte swizzle row)
-constexpr int TC_DQ_WARPS = 8;   // warps that dequantize the weight tile (256 threads, one block each)
-constexpr int TC_THREADS_WS = 64 + 32 * TC_DQ_WARPS;  // + a TMA warp and an MMA warp
+constexpr int TC_DQ_WARPS = 8;   // warps that dequantize one weight tile (256 threads, one block each)
+constexpr int TC_DQ_GROUPS = 2;  // such groups, taking alternate K steps
+constexpr int TC_THREADS_WS = 64 + 32 * TC_DQ_WARPS * TC_DQ_GROUPS;  // + a TMA warp and an MMA warp
 constexpr int TC_TILE_BYTES = TC_M * TC_K * 2;  // 16 KB weight tile
 constexpr int TC_B_BYTES = TC_N * TC_K * 2;     // 32 KB token tile
 constexpr int TC_STAGES = 4;
@@ -76,6 +82,19 @@ __host__ __device__ constexpr uint64_t make_sdesc_sw128(uint32_t smem_addr) {
     return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
 static_assert(make_sdesc_sw128(0) == 0x4000404000010000ull, "tcgen05 shared-memory descriptor");
+
+// The same for an M-major (MN-major) A tile, 128-byte swizzle: a swizzle atom
+// is 8 k-rows of 64 consecutive outputs (128 B each, 1024 B); the leading byte
+// offset is the stride between the two 64-output atoms along M (1024 B,
+// encoded 64, bits 16-29), the stride byte offset the stride between 8-row
+// groups along K (2048 B, encoded 128). Used by orientation T, whose blocks
+// run along the outputs.
+__host__ __device__ constexpr uint64_t make_sdesc_sw128_mn(uint32_t smem_addr) {
+    return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | (64ull << 16) | (128ull << 32) | (1ull << 46) | (2ull << 61);
+}
+static_assert(make_sdesc_sw128_mn(0) == 0x4000408000400000ull, "tcgen05 shared-memory descriptor, MN-major");
+constexpr uint32_t kIdescTransposeA = 1u << 15;  // A is MN-major
+constexpr uint32_t kIdesc = make_idesc_bf16(TC_M, TC_N);
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -191,7 +210,7 @@ __device__ __forceinline__ void load_block(RawBlock& rb, const TcParams& p, int 
     }
     int64_t d_off, q_off;
     p.map.offsets(row, blk, &d_off, &q_off);
-    rb.d = (uint32_t)p.tiles[d_off] | ((uint32_t)p.tiles[d_off + 1] << 8);
+    rb.d = *reinterpret_cast<const uint16_t*>(p.tiles + d_off);  // tiles keep each fp16 scale 2-byte aligned
     rb.q0 = *reinterpret_cast<const uint4*>(p.tiles + q_off);
     if (p.qtype == AT_GGML_Q8_0) rb.q1 = *reinterpret_cast<const uint4*>(p.tiles + q_off + 16);
 }
@@ -239,21 +258,27 @@ __device__ __forceinline__ void store_block(uint8_t* tile, const float* v, int o
                 make_uint4(pack_bf16(v[8 * c], v[8 * c + 1]), pack_bf16(v[8 * c + 2], v[8 * c + 3]),
                            pack_bf16(v[8 * c + 4], v[8 * c + 5]), pack_bf16(v[8 * c + 6], v[8 * c + 7]));
     } else {
-        const int k = tid & 63, cb = tid >> 6;  // 32 outputs (rows 32 cb ..) at column k
-        const int c = k >> 3, e = k & 7;
+        // 32 consecutive outputs (32 cb ..) at input k: half of k-row (k & 7) of
+        // the M-major atom (k >> 3, cb >> 1), chunks 4 (cb & 1) .. + 3
+        const int k = tid & 63, cb = tid >> 6, r = k & 7;
+        uint8_t* row = tile + (k >> 3) * 2048 + (cb >> 1) * 1024 + r * 128;
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-            *reinterpret_cast<__nv_bfloat16*>(tile + sw128_off(32 * cb + i, c) + 2 * e) = __float2bfloat16_rn(v[i]);
+        for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(row + (((4 * (cb & 1) + c) ^ r) << 4)) =
+                make_uint4(pack_bf16(v[8 * c], v[8 * c + 1]), pack_bf16(v[8 * c + 2], v[8 * c + 3]),
+                           pack_bf16(v[8 * c + 4], v[8 * c + 5]), pack_bf16(v[8 * c + 6], v[8 * c + 7]));
     }
 }
 
 constexpr int TC_PF = 3;  // steps of weight bytes in flight per dequant thread (registers)
 
 // Warp roles: warp 0 issues the token tiles' TMA, warp 1 owns TMEM and issues
-// the MMAs, warps 2-9 dequantize the weight tiles (256 threads, one block of
-// 32 weights each per step). Per stage: full_b (TMA bytes), full_a (8 warp
-// arrivals after each warp's stores and proxy fence) and empty (the MMAs'
-// commit); no CTA-wide barrier inside the K loop.
+// the MMAs, warps 2-9 dequantize the weight tiles of even steps and warps
+// 10-17 those of odd steps (256 threads, one block of 32 weights each per
+// step). Per stage: full_b (TMA bytes), full_a (8 warp arrivals after each
+// warp's stores and proxy fence; the group's first warp arrives only after
+// full_b, so full_a alone gates the MMAs) and empty (the MMAs' commit); no
+// CTA-wide barrier inside the K loop.
 __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap,
                                                                    const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -309,53 +334,80 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
                 ++tma_issued;
             }
         }
+        __syncwarp();  // lanes 1-31 park here instead of spinning beside lane 0
     } else if (warp == 1) {
         // ---- MMA issue ----
         if (lane == 0) {
-            constexpr uint32_t idesc = make_idesc_bf16(TC_M, TC_N);
+            const bool mn = p.orient != AT_ORIENT_N;
+            const uint32_t idesc = kIdesc | (mn ? kIdescTransposeA : 0u);
             for (int ks = 0; ks < nk; ++ks) {
                 const int st = ks % TC_STAGES;
                 const uint32_t par = (ks / TC_STAGES) & 1;
-                if (!mbar_wait(smem_u32(&s_fb[st]), par) || !mbar_wait(smem_u32(&s_fa[st]), par)) {
+                if (!mbar_wait(smem_u32(&s_fa[st]), par)) {  // full_a completes after full_b
                     fail();
                     break;
                 }
                 tc_fence_after();
                 const uint32_t a_addr = smem_u32(a_tile(st)), b_addr = smem_u32(b_tile(st));
 #pragma unroll
-                for (int kk = 0; kk < TC_K / 16; ++kk)  // 16 bf16 = 32 bytes per MMA along K
-                    tc_mma(tmem, make_sdesc_sw128(a_addr + 32 * kk), make_sdesc_sw128(b_addr + 32 * kk), idesc,
-                           (ks > 0 || kk > 0) ? 1u : 0u);
+                for (int kk = 0; kk < TC_K / 16; ++kk)  // 16 k per MMA: 32 B of a K-major row, 2 M-major row groups
+                    tc_mma(tmem, mn ? make_sdesc_sw128_mn(a_addr + 4096 * kk) : make_sdesc_sw128(a_addr + 32 * kk),
+                           make_sdesc_sw128(b_addr + 32 * kk), idesc, (ks > 0 || kk > 0) ? 1u : 0u);
                 tc_commit(smem_u32(&s_empty[st]));
             }
             tc_commit(smem_u32(&s_done));  // arrives when every MMA above is complete
         }
+        __syncwarp();
     } else {
         // ---- weight tiles: dequantize into swizzled bf16 ----
-        const int dt = tid - 64;
+        // Group g (warps 2 + 8 g ..) takes steps g, g + 2, ...; with two
+        // warps of each group per scheduler, one group's load and FP
+        // latencies hide behind the other's work. The loop is unrolled by
+        // TC_PF so that slot j always holds the bytes of the same step
+        // sequence: no register copy of a load still in flight (which would
+        // wait for it) between issue and use.
+        constexpr int G = TC_DQ_GROUPS;
+        const int grp = (warp - 2) / TC_DQ_WARPS, dt = (tid - 64) % (32 * TC_DQ_WARPS);
         RawBlock rb[TC_PF];
 #pragma unroll
         for (int i = 0; i < TC_PF; ++i)
-            if (i < nk) load_block(rb[i], p, m0, kbase + i * TC_K, dt);
-        for (int ks = 0; ks < nk; ++ks) {
-            const int st = ks % TC_STAGES;
-            float v[32];
-            decode_block(rb[0], p.qtype, v);
+            if (grp + G * i < nk) load_block(rb[i], p, m0, kbase + (grp + G * i) * TC_K, dt);
+        bool stop = false;
+        for (int kq = grp; kq < nk && !stop; kq += G * TC_PF) {
 #pragma unroll
-            for (int i = 0; i + 1 < TC_PF; ++i) rb[i] = rb[i + 1];
-            if (ks + TC_PF < nk) load_block(rb[TC_PF - 1], p, m0, kbase + (ks + TC_PF) * TC_K, dt);
-            if (ks >= TC_STAGES && !mbar_wait(smem_u32(&s_empty[st]), ((ks - TC_STAGES) / TC_STAGES) & 1)) {
-                if (lane == 0) fail();
-                break;
+            for (int j = 0; j < TC_PF; ++j) {
+                const int ks = kq + G * j;
+                if (ks >= nk) break;
+                const int st = ks % TC_STAGES;
+                float v[32];
+                decode_block(rb[j], p.qtype, v);
+                if (ks + G * TC_PF < nk) load_block(rb[j], p, m0, kbase + (ks + G * TC_PF) * TC_K, dt);
+                if (ks >= TC_STAGES && !mbar_wait(smem_u32(&s_empty[st]), ((ks - TC_STAGES) / TC_STAGES) & 1)) {
+                    if (lane == 0) fail();
+                    stop = true;
+                    break;
+                }
+                store_block(a_tile(st), v, p.orient, dt);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> async proxy
+                __syncwarp();
+                // The group's first warp also waits for the stage's token tile
+                // before it arrives, so that the MMA thread waits on full_a
+                // alone (one barrier round trip per step on its path).
+                int bad = 0;
+                if (lane == 0) {
+                    if (dt < 32) bad = !mbar_wait(smem_u32(&s_fb[st]), (ks / TC_STAGES) & 1);
+                    if (bad) fail();
+                    else asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&s_fa[st])) : "memory");
+                }
+                if (__shfl_sync(0xffffffffu, bad, 0)) {
+                    stop = true;
+                    break;
+                }
             }
-            store_block(a_tile(st), v, p.orient, dt);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> async proxy
-            __syncwarp();
-            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&s_fa[st])) : "memory");
         }
     }
 
-    // ---- epilogue: the accumulator (dequant warps 2-9: lanes 32 (w % 4) .., columns 128 ((w - 2) / 4) ..) ----
+    // ---- epilogue: the accumulator (dequant warps 2-17: lanes 32 (w % 4) .., columns 64 ((w - 2) / 4) ..) ----
     bool ok = mbar_wait(smem_u32(&s_done), 0);
     if (!ok && tid == 0) atomicExch(p.err, 2);
     __syncthreads();
@@ -368,11 +420,12 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
             mbar_wait(smem_u32(&s_fb[ks % TC_STAGES]), (ks / TC_STAGES) & 1);
     tc_fence_after();
     if (ok && warp >= 2) {
-        const int quarter = warp & 3, half = (warp - 2) >> 2;
+        constexpr int parts = TC_DQ_WARPS * TC_DQ_GROUPS / 4;  // warps sharing one TMEM lane quarter
+        const int quarter = warp & 3, part = (warp - 2) >> 2;
         const int m = m0 + 32 * quarter + lane;
 #pragma unroll 1
-        for (int cc = 0; cc < TC_N / 64; ++cc) {
-            const int col = (TC_N / 2) * half + 32 * cc;
+        for (int cc = 0; cc < TC_N / (32 * parts); ++cc) {
+            const int col = (TC_N / parts) * part + 32 * cc;
             float v[32];
             tc_ld32(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)col, v);
             if (m < p.M) {
@@ -451,12 +504,13 @@ void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, in
     const int64_t M = (m->orient == AT_ORIENT_N) ? m->rows : m->cols;
     const int64_t K = (m->orient == AT_ORIENT_N) ? m->cols : m->rows;
     AT_REQUIRE(K % TC_K == 0, AT_ERR_INVALID_ARG, "tensor-core GEMM needs K a multiple of 64");
-    AT_REQUIRE(T >= 1 && x_stride % 4 == 0 && ((uintptr_t)x & 15) == 0, AT_ERR_INVALID_ARG,
+    AT_REQUIRE(T >= 1 && (!x || (x_stride % 4 == 0 && ((uintptr_t)x & 15) == 0)), AT_ERR_INVALID_ARG,
                "tensor-core GEMM: bad activation layout");
     AT_REQUIRE(xbf && ((uintptr_t)xbf & 127) == 0 && xbf_bytes >= (size_t)T * K * 2, AT_ERR_INVALID_ARG,
                "tensor-core GEMM: bf16 staging buffer too small or misaligned");
-    // activations -> bf16 [T][K], described to the TMA unit (128-byte swizzle, zero fill past T)
-    {
+    // activations -> bf16 [T][K] (x null: the caller staged them in xbf), described to the
+    // TMA unit (128-byte swizzle, zero fill past T)
+    if (x) {
         const int64_t n4 = (int64_t)T * K / 4;
         const int grid = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 8);
         to_bf16_kernel<<<grid, 256, 0, s>>>(x, x_stride, static_cast<__nv_bfloat16*>(xbf), (int)K, T);

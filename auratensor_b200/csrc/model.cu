@@ -21,6 +21,7 @@
 #include <unistd.h>
 
 #include <cooperative_groups.h>
+#include <cuda_bf16.h>
 
 #include <chrono>
 #include <cmath>
@@ -717,10 +718,11 @@ __global__ void argmax_index_kernel(const unsigned long long* __restrict__ keys,
 // Batched prompt kernels (one row per prompt token)
 // ---------------------------------------------------------------------------
 // Row-wise x_out = rmsNorm(x_in + y_in) * gamma with the reference's rounding
-// (the F7 residual stream): one CTA per row.
+// (the F7 residual stream): one CTA per row; with xbf, x_out also rounded to
+// bf16 [T][d] for the next tensor-core GEMM.
 __global__ void __launch_bounds__(256) rows_addnorm_kernel(const float* __restrict__ xin, const float* __restrict__ yin,
                                                            const float* __restrict__ gamma, float* __restrict__ xout,
-                                                           int d, float eps) {
+                                                           __nv_bfloat16* __restrict__ xbf, int d, float eps) {
     __shared__ float s_red[8];
     const size_t row = blockIdx.x;
     const float* a = xin + row * d;
@@ -737,12 +739,13 @@ __global__ void __launch_bounds__(256) rows_addnorm_kernel(const float* __restri
 #pragma unroll
     for (int w = 0; w < 8; ++w) tot += s_red[w];
     const float inv = rms_inv(tot, d, eps);
-    for (int i = threadIdx.x; i < d; i += 256) xout[row * d + i] = norm_apply(__fadd_rn(a[i], b[i]), inv, gamma[i]);
+    for (int i = threadIdx.x; i < d; i += 256) {
+        const float o = norm_apply(__fadd_rn(a[i], b[i]), inv, gamma[i]);
+        xout[row * d + i] = o;
+        if (xbf) xbf[row * d + i] = __float2bfloat16_rn(o);
+    }
 }
 
-// RoPE of q and k (core/Kernels.java:296-309: a' = fma(a, c, b * -s),
-// b' = fma(b, c, a * s)) and the KV-cache append (inference/KVCache.java:79-95)
-// of prompt row t at position p0 + t; q goes to q_out [T][nq].
 // Causal attention of a prompt chunk (LlamaModel.attention, inference/
 // LlamaModel.java:255-297, for T consecutive query positions p0 .. p0+T-1).
 // CTA (KV head h, query block) holds R = 32 query rows (QB = 32 / G tokens x
@@ -917,6 +920,9 @@ struct KvQ {
     uint16_t* vs = nullptr;
 };
 
+// RoPE of q and k (core/Kernels.java:296-309: a' = fma(a, c, b * -s),
+// b' = fma(b, c, a * s)) and the KV-cache append (inference/KVCache.java:79-95)
+// of prompt row t at position p0 + t; q goes to q_out [T][nq].
 __global__ void __launch_bounds__(256) rope_append_kernel(const float* __restrict__ qkv, int qcols,
                                                           float* __restrict__ q_out, float* __restrict__ kc,
                                                           float* __restrict__ vc, KvQ kvq,
@@ -950,12 +956,6 @@ __global__ void __launch_bounds__(256) rope_append_kernel(const float* __restric
     }
 }
 
-// h = silu(g) * u elementwise (in place in g).
-// RoPE and the KV-cache append for B batch rows of a plain QKV output
-// [B][qcols] (attention weights stored [out][in], computed by the
-// orientation-N GEMV): the arithmetic of the fused QKV epilogue
-// (core/Kernels.java:296-309, inference/KVCache.java:79-95), slot b at
-// position pos[b].
 // KVCache.append of one position: block h (one per KV head), thread dd.
 __global__ void kv_put_kernel(const float* __restrict__ k, const float* __restrict__ v, float* __restrict__ kc,
                               float* __restrict__ vc, KvQ kvq, int ctx, int hd, int64_t pos) {
@@ -971,6 +971,11 @@ __global__ void kv_put_kernel(const float* __restrict__ k, const float* __restri
     }
 }
 
+// RoPE and the KV-cache append for B batch rows of a plain QKV output
+// [B][qcols] (attention weights stored [out][in], computed by the
+// orientation-N GEMV): the arithmetic of the fused QKV epilogue
+// (core/Kernels.java:296-309, inference/KVCache.java:79-95), slot b at
+// position pos[b].
 __global__ void __launch_bounds__(256) qkv_rope_rows_kernel(const float* __restrict__ qkv, int qcols,
                                                             float* __restrict__ q_out, float* __restrict__ kc,
                                                             float* __restrict__ vc, KvQ kvq, int64_t slot_stride,
@@ -1005,10 +1010,21 @@ __global__ void __launch_bounds__(256) qkv_rope_rows_kernel(const float* __restr
     }
 }
 
-__global__ void silu_mul_kernel(float* __restrict__ g, const float* __restrict__ u, int64_t n) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        g[i] = silu_mul(g[i], u[i]);
+// h = silu(g) * u rounded to bf16: the w2 GEMM's staged input.
+__global__ void silu_mul_bf16_kernel(const float* __restrict__ g, const float* __restrict__ u,
+                                     __nv_bfloat16* __restrict__ h, int64_t n) {
+    const int64_t n4 = n / 4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 a = reinterpret_cast<const float4*>(g)[i], b = reinterpret_cast<const float4*>(u)[i];
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(silu_mul(a.x, b.x), silu_mul(a.y, b.y));
+        const __nv_bfloat162 hi = __floats2bfloat162_rn(silu_mul(a.z, b.z), silu_mul(a.w, b.w));
+        reinterpret_cast<__nv_bfloat162*>(h)[2 * i] = lo;
+        reinterpret_cast<__nv_bfloat162*>(h)[2 * i + 1] = hi;
+    }
+    for (int64_t i = 4 * n4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        h[i] = __float2bfloat16_rn(silu_mul(g[i], u[i]));
 }
+
 
 inline int grid_for(int64_t n, int tpb = 256) {
     int64_t g = (n + tpb - 1) / tpb;
@@ -2300,6 +2316,7 @@ void run_prompt_batched(at_model* m, const int* tokens, int n, int slot) {
     const float eps = m->cfg.rms_norm_eps;
     const float scale = (float)(1.0 / std::sqrt((double)hd));
     const size_t layer_kv = (size_t)m->Hkvl * m->ctx_len * hd;
+    __nv_bfloat16* xbf = static_cast<__nv_bfloat16*>(m->pf_xbf);
     for (int p0 = 0; p0 < n; p0 += PF_T) {
         const int T = std::min(PF_T, n - p0);
         AT_CUDA(cudaStreamSynchronize(s));  // the pinned staging buffers are free again
@@ -2326,9 +2343,9 @@ void run_prompt_batched(at_model* m, const int* tokens, int n, int slot) {
             KvQ kvq;
             if (m->kv_q8) kvq = KvQ{m->kq8 + kv_off, m->vq8 + kv_off, m->ksc + kv_off / 32, m->vsc + kv_off / 32};
             // attention block: xb = norm(xa + y); q, k, v; RoPE + append; attention; y = wo att
-            rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xa, m->pf_y, ly.attn_norm, m->pf_xb, d, eps);
+            rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xa, m->pf_y, ly.attn_norm, m->pf_xb, xbf, d, eps);
             AT_CUDA(cudaGetLastError());
-            launch_gemm_tc(&ly.qkv, m->pf_xb, d, m->pf_qkv, qcols, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
+            launch_gemm_tc(&ly.qkv, nullptr, d, m->pf_qkv, qcols, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
                            c->num_sms, m->pf_err, s);
             rope_append_kernel<<<T, 256, 0, s>>>(m->pf_qkv, qcols, m->pf_q, kc, vc, kvq, m->rope_cos, m->rope_sin, hd,
                                                  nq, nkv, m->ctx_len, p0);
@@ -2358,15 +2375,17 @@ void run_prompt_batched(at_model* m, const int* tokens, int n, int slot) {
             launch_gemm_tc(&ly.wo, m->pf_att, nq, m->pf_y, d, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
                            c->num_sms, m->pf_err, s);
             // feed-forward block: xa = norm(xb + y); h = silu(w1 xa) * (w3 xa); y = w2 h
-            rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xb, m->pf_y, ly.ffn_norm, m->pf_xa, d, eps);
+            // the norm, silu * mul and their bf16 copies feed w1 / w3 / w2 through the staging buffer
+            rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xb, m->pf_y, ly.ffn_norm, m->pf_xa, xbf, d, eps);
             AT_CUDA(cudaGetLastError());
-            launch_gemm_tc(&ly.w1, m->pf_xa, d, m->pf_g, m->Fl, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
+            launch_gemm_tc(&ly.w1, nullptr, d, m->pf_g, m->Fl, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
                            c->num_sms, m->pf_err, s);
-            launch_gemm_tc(&ly.w3, m->pf_xa, d, m->pf_u, m->Fl, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
+            launch_gemm_tc(&ly.w3, nullptr, d, m->pf_u, m->Fl, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
                            c->num_sms, m->pf_err, s);
-            silu_mul_kernel<<<grid_for((int64_t)T * m->Fl), 256, 0, s>>>(m->pf_g, m->pf_u, (int64_t)T * m->Fl);
+            silu_mul_bf16_kernel<<<grid_for((int64_t)T * m->Fl / 4), 256, 0, s>>>(m->pf_g, m->pf_u, xbf,
+                                                                                (int64_t)T * m->Fl);
             AT_CUDA(cudaGetLastError());
-            launch_gemm_tc(&ly.w2, m->pf_g, m->Fl, m->pf_y, d, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
+            launch_gemm_tc(&ly.w2, nullptr, m->Fl, m->pf_y, d, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
                            c->num_sms, m->pf_err, s);
         }
     }
