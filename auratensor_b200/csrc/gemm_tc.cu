@@ -23,7 +23,7 @@
 // 128-byte swizzle, rows past the last token zero-filled), one step ahead,
 // completing on the stage's "full" mbarrier; the weight tile is dequantized
 // by one of two groups of 8 warps (alternate steps) from raw block bytes
-// loaded into registers three of the group's steps ahead.
+// loaded into registers three (Q8_0: two) of the group's steps ahead.
 // One thread issues four tcgen05.mma (K = 16 each) per step and commits them
 // to the stage's "empty" mbarrier; four stages (TC_STAGES) keep the TMA, the dequant and
 // the tensor core working on different steps. The 128 x 256 FP32 accumulator
@@ -61,7 +61,7 @@ constexpr int TC_STAGES = 4;
 constexpr int TC_STAGE_BYTES = TC_TILE_BYTES + TC_B_BYTES;
 constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024;  // + alignment slack
 constexpr uint32_t TC_TMEM_COLS = TC_N;                     // FP32 accumulator columns
-constexpr int kTcSpinLimit = 1 << 26;
+constexpr int kTcSpinLimit = 1 << 22;
 constexpr int kTcMaxSplits = 4;
 
 // Instruction descriptor of tcgen05.mma kind::f16: D f32 (bits 4-5 = 1),
@@ -191,10 +191,11 @@ struct RawBlock {
 // Step k0: N orientation, thread (row r = tid / 2, half j = tid % 2) owns block
 // (m0 + r, k0/32 + j); T orientation, thread (k = tid % 64, cb = tid / 64) owns
 // block (input row k0 + k, output block m0/32 + cb).
+template <int QT, int OR>
 __device__ __forceinline__ void load_block(RawBlock& rb, const TcParams& p, int m0, int k0, int tid) {
     int64_t row, blk;
     bool valid;
-    if (p.orient == AT_ORIENT_N) {
+    if (OR == AT_ORIENT_N) {
         row = m0 + (tid >> 1);
         blk = (k0 >> 5) + (tid & 1);
         valid = row < p.M;
@@ -212,17 +213,19 @@ __device__ __forceinline__ void load_block(RawBlock& rb, const TcParams& p, int 
     p.map.offsets(row, blk, &d_off, &q_off);
     rb.d = *reinterpret_cast<const uint16_t*>(p.tiles + d_off);  // tiles keep each fp16 scale 2-byte aligned
     rb.q0 = *reinterpret_cast<const uint4*>(p.tiles + q_off);
-    if (p.qtype == AT_GGML_Q8_0) rb.q1 = *reinterpret_cast<const uint4*>(p.tiles + q_off + 16);
+    if (QT == AT_GGML_Q8_0) rb.q1 = *reinterpret_cast<const uint4*>(p.tiles + q_off + 16);
 }
 
-// The 32 weights of a raw block, (q - 8) * d or q * d in FP32, in element
-// order. A nibble (byte) becomes the exact float q - 8 (q) by one byte permute
-// into the mantissa of 2^23 and a packed f32x2 subtraction; then one rounding
-// in the multiply by d.
-__device__ __forceinline__ void decode_block(const RawBlock& rb, int qtype, float* v) {
+// The 32 weights of a raw block, (q - 8) * d or q * d in FP32, rounded to
+// bf16 and packed in pairs in element order (pk[i] = elements 2i, 2i + 1). A
+// nibble (byte) becomes the exact float q - 8 (q) by one byte permute into
+// the mantissa of 2^23 and a packed f32x2 subtraction; then one rounding in
+// the multiply by d and one to bf16.
+template <int QT>
+__device__ __forceinline__ void decode_block(const RawBlock& rb, uint32_t* pk) {
     const float d = fp16_ftz(rb.d);
     const float2 dd = f2(d, d);
-    if (qtype == AT_GGML_Q4_0) {
+    if (QT == AT_GGML_Q4_0) {
         const float2 moff = f2(-8388616.f, -8388616.f);  // -(2^23 + 8)
         const uint32_t qw[4] = {rb.q0.x, rb.q0.y, rb.q0.z, rb.q0.w};
 #pragma unroll
@@ -231,8 +234,7 @@ __device__ __forceinline__ void decode_block(const RawBlock& rb, int qtype, floa
 #pragma unroll
             for (int k = 0; k < 4; ++k) {  // byte k of word i: elements 8i + 2k (low), 8i + 2k + 1 (high)
                 const float2 w = __fmul2_rn(__fadd2_rn(f2(magic_byte(lo, k), magic_byte(hi, k)), moff), dd);
-                v[8 * i + 2 * k] = w.x;
-                v[8 * i + 2 * k + 1] = w.y;
+                pk[4 * i + k] = pack_bf16(w.x, w.y);
             }
         }
     } else {
@@ -243,20 +245,22 @@ __device__ __forceinline__ void decode_block(const RawBlock& rb, int qtype, floa
             const uint32_t u = qw[i] ^ 0x80808080u;  // int8 q -> unsigned q + 128
             const float2 w01 = __fmul2_rn(__fadd2_rn(f2(magic_byte(u, 0), magic_byte(u, 1)), moff), dd);
             const float2 w23 = __fmul2_rn(__fadd2_rn(f2(magic_byte(u, 2), magic_byte(u, 3)), moff), dd);
-            v[4 * i] = w01.x; v[4 * i + 1] = w01.y; v[4 * i + 2] = w23.x; v[4 * i + 3] = w23.y;
+            pk[2 * i] = pack_bf16(w01.x, w01.y);
+            pk[2 * i + 1] = pack_bf16(w23.x, w23.y);
         }
     }
 }
 
-// Writes this thread's 32 dequantized weights into the swizzled bf16 weight tile.
-__device__ __forceinline__ void store_block(uint8_t* tile, const float* v, int orient, int tid) {
-    if (orient == AT_ORIENT_N) {
+// Writes this thread's 32 dequantized weights (16 packed bf16 pairs) into the
+// swizzled weight tile.
+template <int OR>
+__device__ __forceinline__ void store_block(uint8_t* tile, const uint32_t* pk, int tid) {
+    if (OR == AT_ORIENT_N) {
         const int r = tid >> 1, j = tid & 1;  // 32 consecutive k of row r: chunks 4j .. 4j + 3
 #pragma unroll
         for (int c = 0; c < 4; ++c)
             *reinterpret_cast<uint4*>(tile + sw128_off(r, 4 * j + c)) =
-                make_uint4(pack_bf16(v[8 * c], v[8 * c + 1]), pack_bf16(v[8 * c + 2], v[8 * c + 3]),
-                           pack_bf16(v[8 * c + 4], v[8 * c + 5]), pack_bf16(v[8 * c + 6], v[8 * c + 7]));
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
     } else {
         // 32 consecutive outputs (32 cb ..) at input k: half of k-row (k & 7) of
         // the M-major atom (k >> 3, cb >> 1), chunks 4 (cb & 1) .. + 3
@@ -265,12 +269,14 @@ __device__ __forceinline__ void store_block(uint8_t* tile, const float* v, int o
 #pragma unroll
         for (int c = 0; c < 4; ++c)
             *reinterpret_cast<uint4*>(row + (((4 * (cb & 1) + c) ^ r) << 4)) =
-                make_uint4(pack_bf16(v[8 * c], v[8 * c + 1]), pack_bf16(v[8 * c + 2], v[8 * c + 3]),
-                           pack_bf16(v[8 * c + 4], v[8 * c + 5]), pack_bf16(v[8 * c + 6], v[8 * c + 7]));
+                make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
     }
 }
 
-constexpr int TC_PF = 3;  // steps of weight bytes in flight per dequant thread (registers)
+// Steps of weight bytes in flight per dequant thread (registers): 3 Q4_0
+// blocks (18 B each) or 2 Q8_0 blocks (34 B) within the register budget.
+template <int QT>
+constexpr int tc_pf() { return QT == AT_GGML_Q8_0 ? 2 : 3; }
 
 // Warp roles: warp 0 issues the token tiles' TMA, warp 1 owns TMEM and issues
 // the MMAs, warps 2-9 dequantize the weight tiles of even steps and warps
@@ -279,6 +285,10 @@ constexpr int TC_PF = 3;  // steps of weight bytes in flight per dequant thread 
 // warp's stores and proxy fence; the group's first warp arrives only after
 // full_b, so full_a alone gates the MMAs) and empty (the MMAs' commit); no
 // CTA-wide barrier inside the K loop.
+template <int QT, int OR>
+// 18 warps put 5 on one of the SM's four 16,384-register partitions: at
+// most 96 registers a thread. Templated on the quant type and orientation so
+// that each instance holds only the registers it uses.
 __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap,
                                                                    const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -338,7 +348,7 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
     } else if (warp == 1) {
         // ---- MMA issue ----
         if (lane == 0) {
-            const bool mn = p.orient != AT_ORIENT_N;
+            constexpr bool mn = OR != AT_ORIENT_N;
             const uint32_t idesc = kIdesc | (mn ? kIdescTransposeA : 0u);
             for (int ks = 0; ks < nk; ++ks) {
                 const int st = ks % TC_STAGES;
@@ -363,31 +373,31 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
         // Group g (warps 2 + 8 g ..) takes steps g, g + 2, ...; with two
         // warps of each group per scheduler, one group's load and FP
         // latencies hide behind the other's work. The loop is unrolled by
-        // TC_PF so that slot j always holds the bytes of the same step
+        // PF so that slot j always holds the bytes of the same step
         // sequence: no register copy of a load still in flight (which would
         // wait for it) between issue and use.
-        constexpr int G = TC_DQ_GROUPS;
+        constexpr int G = TC_DQ_GROUPS, PF = tc_pf<QT>();
         const int grp = (warp - 2) / TC_DQ_WARPS, dt = (tid - 64) % (32 * TC_DQ_WARPS);
-        RawBlock rb[TC_PF];
+        RawBlock rb[PF];
 #pragma unroll
-        for (int i = 0; i < TC_PF; ++i)
-            if (grp + G * i < nk) load_block(rb[i], p, m0, kbase + (grp + G * i) * TC_K, dt);
+        for (int i = 0; i < PF; ++i)
+            if (grp + G * i < nk) load_block<QT, OR>(rb[i], p, m0, kbase + (grp + G * i) * TC_K, dt);
         bool stop = false;
-        for (int kq = grp; kq < nk && !stop; kq += G * TC_PF) {
+        for (int kq = grp; kq < nk && !stop; kq += G * PF) {
 #pragma unroll
-            for (int j = 0; j < TC_PF; ++j) {
+            for (int j = 0; j < PF; ++j) {
                 const int ks = kq + G * j;
                 if (ks >= nk) break;
                 const int st = ks % TC_STAGES;
-                float v[32];
-                decode_block(rb[j], p.qtype, v);
-                if (ks + G * TC_PF < nk) load_block(rb[j], p, m0, kbase + (ks + G * TC_PF) * TC_K, dt);
+                uint32_t pk[16];
+                decode_block<QT>(rb[j], pk);
+                if (ks + G * PF < nk) load_block<QT, OR>(rb[j], p, m0, kbase + (ks + G * PF) * TC_K, dt);
                 if (ks >= TC_STAGES && !mbar_wait(smem_u32(&s_empty[st]), ((ks - TC_STAGES) / TC_STAGES) & 1)) {
                     if (lane == 0) fail();
                     stop = true;
                     break;
                 }
-                store_block(a_tile(st), v, p.orient, dt);
+                store_block<OR>(a_tile(st), pk, dt);
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> async proxy
                 __syncwarp();
                 // The group's first warp also waits for the stage's token tile
@@ -539,13 +549,18 @@ void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, in
     p.y = split ? ws : y;
     p.y_stride = split ? (int)M : y_stride;
     p.err = err;
-    static bool attr_set = false;
-    if (!attr_set) {
-        AT_CUDA(cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM));
-        attr_set = true;
-    }
+    auto kern = m->type == AT_GGML_Q4_0 ? (m->orient == AT_ORIENT_N ? gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_N>
+                                                                    : gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_T>)
+                                        : (m->orient == AT_ORIENT_N ? gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_N>
+                                                                    : gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_T>);
+    static std::once_flag attr_once;
+    std::call_once(attr_once, [] {
+        for (auto k : {gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_N>, gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_T>,
+                       gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_N>, gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_T>})
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+    });
     dim3 grid((unsigned)((M + TC_M - 1) / TC_M), (unsigned)((T + TC_N - 1) / TC_N), (unsigned)p.splits);
-    gemm_tc_kernel<<<grid, TC_THREADS_WS, TC_SMEM, s>>>(xmap, p);
+    kern<<<grid, TC_THREADS_WS, TC_SMEM, s>>>(xmap, p);
     AT_CUDA(cudaGetLastError());
     if (p.splits > 1) {
         const int64_t n = (int64_t)T * M;

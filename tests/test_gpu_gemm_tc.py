@@ -43,6 +43,23 @@ def test_gemm_tc_small(qt, orient, tokens, cuda):
 
 @pytest.mark.parametrize("qt", [ref.GGML_Q4_0, ref.GGML_Q8_0])
 @pytest.mark.parametrize("orient,rows,cols", [(ORIENT_N, 300, 640), (ORIENT_N, 1000, 256), (ORIENT_T, 640, 416),
-                                              (ORIENT_T, 4096, 1024)])
+                                              (ORIENT_T, 4096, 1024), (ORIENT_N, 16384, 128)])
 def test_gemm_tc_ragged(qt, orient, rows, cols, cuda):
+    """Ragged edges; the K steps of all tiles are split evenly over the SMs,
+    so some tiles are summed from pieces of several CTAs (300 x 640: ten one-
+    step pieces per tile) and some are whole inside one CTA (16384 x 128)."""
     check(qt, orient, rows, cols, 130, cuda, seed=rows + cols)
+
+
+@pytest.mark.parametrize("orient,rows,cols", [(ORIENT_N, 2048, 1024), (ORIENT_T, 1024, 2048)])
+def test_gemm_tc_repeatable(orient, rows, cols, cuda):
+    """Pieces of a split tile are summed in K order by whichever CTA finishes
+    last: the result does not depend on the arrival order."""
+    rng = np.random.default_rng(5)
+    w = (rng.standard_normal(rows * cols) * 0.02).astype(np.float32)
+    m = QMatrix(ref.GGML_Q4_0, orient, rows, cols, torch.from_numpy(synth.quantize(w, ref.GGML_Q4_0)).to(cuda))
+    n_in = cols if orient == ORIENT_N else rows
+    x = torch.from_numpy(rng.standard_normal((400, n_in)).astype(np.float32)).to(cuda)
+    first = m.gemm(x).cpu()
+    for _ in range(5):
+        assert torch.equal(m.gemm(x).cpu(), first)
