@@ -19,7 +19,7 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIBDIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIBDIR, "libauratensor_cuda.so")
-SOURCES = ["at_runtime.cu", "gemv.cu", "gemm_tc.cu", "model.cu", "decode_step.cu", "q6k.cu", "sample.cu", "sampler.cpp", "sched.cpp"]
+SOURCES = ["at_runtime.cu", "gemv.cu", "gemm_tc.cu", "prompt_attn_tc.cu", "model.cu", "decode_step.cu", "q6k.cu", "sample.cu", "sampler.cpp", "sched.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -205,6 +205,14 @@ void launch_gemv_q6k(const at_qmat* m, int batch, Pro pro, const GemvArgs& a, in
 // rows of `in` elements); ws (FP32, may be null) holds the
 // partials when K is split across CTAs (gemm_tc_splits(m, T) x T x out
 // floats); *err records a bounded wait that ran out (2).
+// Causal prompt attention on the tensor cores (prompt_attn_tc.cu): q [T][Hl
+// x hd] after RoPE, the layer's KV cache of one slot (kc / vc FP32, or Q8_0
+// quants with ksc / vsc scales when kvq), att [T][Hl x hd]; false (nothing
+// launched) for head_dim other than 64 / 128 or G = Hl / Hkvl not in 1, 2, 4,
+// 8. *err records a bounded wait that ran out (2).
+bool launch_prompt_attn_tc(int hd, int G, bool kvq, int Hkvl, int T, cudaStream_t s, const float* q, const float* kc,
+                           const float* vc, const uint16_t* ksc, const uint16_t* vsc, float* att, int64_t p0, int Hl,
+                           int ctx, float scale, int* err);
 int gemm_tc_splits(const at_qmat* m, int T, int num_sms);
 void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, int y_stride, int T, void* xbf,
                     size_t xbf_bytes, float* ws, size_t ws_bytes, int num_sms, int* err, cudaStream_t s);

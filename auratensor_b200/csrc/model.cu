@@ -2354,7 +2354,10 @@ void run_prompt_batched(at_model* m, const int* tokens, int n, int slot) {
                 const int G = m->Hl / m->Hkvl;
                 const float* kq = m->kv_q8 ? reinterpret_cast<const float*>(kvq.kq) : kc;
                 const float* vq = m->kv_q8 ? reinterpret_cast<const float*>(kvq.vq) : vc;
-                if (hd == 128) {
+                // tensor-core attention for head_dim 64 / 128 and 1, 2, 4 or 8 query heads per KV head
+                if (launch_prompt_attn_tc(hd, G, m->kv_q8, m->Hkvl, T, s, m->pf_q, kq, vq, kvq.ks, kvq.vs, m->pf_att,
+                                          p0, m->Hl, m->ctx_len, scale, m->pf_err)) {
+                } else if (hd == 128) {
                     if (m->kv_q8)
                         launch_prompt_attn<128, true>(G, m->Hkvl, T, s, m->pf_q, kq, vq, kvq.ks, kvq.vs, m->pf_att, p0,
                                                       m->Hl, m->ctx_len, scale);
@@ -2392,7 +2395,7 @@ void run_prompt_batched(at_model* m, const int* tokens, int n, int slot) {
     int err = 0;
     AT_CUDA(cudaMemcpyAsync(&err, m->pf_err, sizeof(int), cudaMemcpyDeviceToHost, s));
     AT_CUDA(cudaStreamSynchronize(s));
-    AT_REQUIRE(err == 0, AT_ERR_CUDA, "prompt GEMM: an mbarrier wait ran out");
+    AT_REQUIRE(err == 0, AT_ERR_CUDA, "prompt GEMM or attention: an mbarrier wait ran out");
     m->kv_size[slot] = std::max<int64_t>(m->kv_size[slot], n);
 }
 
