@@ -453,15 +453,30 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
 }
 
-// y[t][m] = sum over splits z (in order) of ws[z][t][m].
+// y[t][m] = sum over splits z (in order) of ws[z][t][m]; block row t,
+// thread 4 consecutive m (VEC) or one.
+template <bool VEC>
 __global__ void splitk_sum_kernel(const float* __restrict__ ws, int splits, int T, int M, float* __restrict__ y,
                                   int y_stride) {
-    const int64_t n = (int64_t)T * M;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int t = (int)(i / M), m = (int)(i - (int64_t)t * M);
-        float acc = ws[i];
-        for (int z = 1; z < splits; ++z) acc += ws[(size_t)z * n + i];
-        y[(size_t)t * y_stride + m] = acc;
+    const int t = blockIdx.y;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t n = (size_t)T * M, r = (size_t)t * M;
+    if constexpr (VEC) {
+        if (4 * i >= M) return;
+        float4 acc = *reinterpret_cast<const float4*>(ws + r + 4 * i);
+        for (int z = 1; z < splits; ++z) {
+            const float4 v = *reinterpret_cast<const float4*>(ws + z * n + r + 4 * i);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        *reinterpret_cast<float4*>(y + (size_t)t * y_stride + 4 * i) = acc;
+    } else {
+        if (i >= M) return;
+        float acc = ws[r + i];
+        for (int z = 1; z < splits; ++z) acc += ws[z * n + r + i];
+        y[(size_t)t * y_stride + i] = acc;
     }
 }
 
@@ -563,9 +578,12 @@ void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, in
     kern<<<grid, TC_THREADS_WS, TC_SMEM, s>>>(xmap, p);
     AT_CUDA(cudaGetLastError());
     if (p.splits > 1) {
-        const int64_t n = (int64_t)T * M;
-        splitk_sum_kernel<<<(int)std::min<int64_t>((n + 255) / 256, 148 * 8), 256, 0, s>>>(ws, p.splits, T, (int)M, y,
-                                                                                             y_stride);
+        const bool vec = M % 4 == 0 && y_stride % 4 == 0 && ((uintptr_t)y & 15) == 0 && ((uintptr_t)ws & 15) == 0;
+        const int per = vec ? (int)((M / 4 + 127) / 128) : (int)((M + 127) / 128);
+        if (vec)
+            splitk_sum_kernel<true><<<dim3(per, T), 128, 0, s>>>(ws, p.splits, T, (int)M, y, y_stride);
+        else
+            splitk_sum_kernel<false><<<dim3(per, T), 128, 0, s>>>(ws, p.splits, T, (int)M, y, y_stride);
         AT_CUDA(cudaGetLastError());
     }
 }

@@ -135,6 +135,31 @@ __device__ __forceinline__ uint4 pt_row8(const float* __restrict__ c, const uint
     return make_uint4(pt_pack(f[0], f[1]), pt_pack(f[2], f[3]), pt_pack(f[4], f[5]), pt_pack(f[6], f[7]));
 }
 
+// 32 consecutive FP32 columns of this warp's 32 TMEM lanes, written.
+__device__ __forceinline__ void pt_st32(uint32_t taddr, const float* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+          "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+          "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+          "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+          "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+          "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+          "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+          "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+          "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+          "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+          "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// The output accumulator O (FP32) lives in TMEM columns 128 .. 128 + HD and
+// P V of each tile is added into it by the MMA; before that, the softmax
+// warps rescale it by the tile's correction exp(m_old - m_new) (tcgen05.ld /
+// st). The S MMA of a tile is issued after the previous tile's P V, so its
+// completion also means the previous P V is done.
 template <int HD, int G, bool KVQ>
 __global__ void __launch_bounds__(PT_THREADS, 1)
     prompt_attn_tc_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
@@ -146,8 +171,11 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
     constexpr uint32_t ATOM_COL = PT_ROWS * 128;  // bytes of one atom column of a 128-row K-major tile
     constexpr uint32_t idesc_s = pt_idesc(PT_ROWS, PT_KT, false);
     constexpr uint32_t idesc_o = pt_idesc(PT_ROWS, HD, true);
+    constexpr int CH = PT_KT * HD / 8 / PT_THREADS;  // 8-element chunks of K (and of V) per thread per tile
+    constexpr int LB = CH < 8 ? CH : 8;              // chunks whose loads are in flight together
+    static_assert(CH % LB == 0, "load batches");
     extern __shared__ uint8_t pt_raw[];
-    __shared__ __align__(8) uint64_t s_bar[2];  // S complete, O_tile complete
+    __shared__ __align__(8) uint64_t s_bar[2];  // S complete, P V complete
     __shared__ uint32_t s_tmem;
     __shared__ int s_bad;
     uint8_t* qs = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(pt_raw) + 1023) & ~uintptr_t(1023));
@@ -191,30 +219,44 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
     const int row = 32 * (warp & 3) + lane;
     const int64_t qpos = (row / G < ntok) ? p0 + t0 + row / G : -1;
     const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
-    float o[HD];
-#pragma unroll
-    for (int d = 0; d < HD; ++d) o[d] = 0.f;
     float m = -INFINITY, l = 0.f;
 
     for (int kt = 0; kt < ntiles; ++kt) {
         const int64_t k0 = (int64_t)kt * PT_KT;
         const int nk = (last + 1 - k0) < PT_KT ? (int)(last + 1 - k0) : PT_KT;
-        // 1. K (K-major) and V (M-major) of the tile in bf16; rows past nk zero
-        for (int i = tid; i < PT_KT * HD / 8; i += PT_THREADS) {
-            const int kr = i / (HD / 8), c8 = i % (HD / 8);
-            uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
-            if (kr < nk) {
-                const size_t e = kvbase + (size_t)(k0 + kr) * HD + 8 * c8;
-                kv = pt_row8<KVQ>(kc, ksc, e);
-                vv = pt_row8<KVQ>(vc, vsc, e);
+        // 1. the previous P V has read V; K (K-major) and V (M-major) of the
+        //    tile in bf16, rows past nk zero, LB chunks' loads in flight
+        if (kt > 0 && !pt_wait(pt_smem_u32(&s_bar[1]), (kt - 1) & 1)) {
+            atomicExch(err, 2);
+            s_bad = 1;
+        }
+#pragma unroll
+        for (int b = 0; b < CH; b += LB) {
+            uint4 kv[LB], vv[LB];
+#pragma unroll
+            for (int u = 0; u < LB; ++u) {
+                const int i = tid + (b + u) * PT_THREADS;
+                const int kr = i / (HD / 8), c8 = i % (HD / 8);
+                kv[u] = vv[u] = make_uint4(0u, 0u, 0u, 0u);
+                if (kr < nk) {
+                    const size_t e = kvbase + (size_t)(k0 + kr) * HD + 8 * c8;
+                    kv[u] = pt_row8<KVQ>(kc, ksc, e);
+                    vv[u] = pt_row8<KVQ>(vc, vsc, e);
+                }
             }
-            *reinterpret_cast<uint4*>(ks + (c8 >> 3) * ATOM_COL + pt_sw128(kr, c8 & 7)) = kv;
-            *reinterpret_cast<uint4*>(vs + (kr >> 3) * (NA * 1024) + (c8 >> 3) * 1024 + (kr & 7) * 128 +
-                                      (((c8 & 7) ^ (kr & 7)) << 4)) = vv;
+#pragma unroll
+            for (int u = 0; u < LB; ++u) {
+                const int i = tid + (b + u) * PT_THREADS;
+                const int kr = i / (HD / 8), c8 = i % (HD / 8);
+                *reinterpret_cast<uint4*>(ks + (c8 >> 3) * ATOM_COL + pt_sw128(kr, c8 & 7)) = kv[u];
+                *reinterpret_cast<uint4*>(vs + (kr >> 3) * (NA * 1024) + (c8 >> 3) * 1024 + (kr & 7) * 128 +
+                                          (((c8 & 7) ^ (kr & 7)) << 4)) = vv[u];
+            }
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> the MMAs' async proxy
         pt_fence_before();
         __syncthreads();
+        if (s_bad) break;
         // 2. S = Q K^T
         if (tid == 0) {
             pt_fence_after();
@@ -225,8 +267,8 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
                        pt_desc_k(ka + (kk >> 2) * ATOM_COL + 32 * (kk & 3)), idesc_s, kk > 0 ? 1u : 0u);
             pt_commit(pt_smem_u32(&s_bar[0]));
         }
-        // 3. scale, causal mask, online softmax; P (bf16, K-major) to shared memory
-        float alpha = 1.f;
+        // 3. scale, causal mask, online softmax; P (bf16, K-major) to shared
+        //    memory; O rescaled by the correction
         if (warp < 4) {
             if (!pt_wait(pt_smem_u32(&s_bar[0]), kt & 1)) {
                 atomicExch(err, 2);
@@ -236,24 +278,24 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
             float mx = -INFINITY;
 #pragma unroll 1
             for (int c = 0; c < PT_KT / 32; ++c) {
-                float s[32];
-                pt_ld32(trow + 32 * c, s);
+                float sv[32];
+                pt_ld32(trow + 32 * c, sv);
 #pragma unroll
                 for (int i = 0; i < 32; ++i)
-                    if (k0 + 32 * c + i <= qpos) mx = fmaxf(mx, __fmul_rn(s[i], scale));
+                    if (k0 + 32 * c + i <= qpos) mx = fmaxf(mx, __fmul_rn(sv[i], scale));
             }
             const float mn = fmaxf(m, mx);
-            alpha = (mn == -INFINITY) ? 1.f : expf(m - mn);
+            const float alpha = (mn == -INFINITY) ? 1.f : expf(m - mn);
             float sum = 0.f;
 #pragma unroll 1
             for (int c = 0; c < PT_KT / 32; ++c) {
-                float s[32];
-                pt_ld32(trow + 32 * c, s);
+                float sv[32];
+                pt_ld32(trow + 32 * c, sv);
                 uint32_t pk[16];
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
-                    const float a = (k0 + 32 * c + i <= qpos) ? expf(__fmul_rn(s[i], scale) - mn) : 0.f;
-                    const float b = (k0 + 32 * c + i + 1 <= qpos) ? expf(__fmul_rn(s[i + 1], scale) - mn) : 0.f;
+                    const float a = (k0 + 32 * c + i <= qpos) ? expf(__fmul_rn(sv[i], scale) - mn) : 0.f;
+                    const float b = (k0 + 32 * c + i + 1 <= qpos) ? expf(__fmul_rn(sv[i + 1], scale) - mn) : 0.f;
                     sum += a + b;
                     pk[i / 2] = pt_pack(a, b);
                 }
@@ -266,47 +308,56 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
             }
             l = fmaf(l, alpha, sum);
             m = mn;
+            // warp-uniform (tcgen05.ld / st are warp-collective); the previous
+            // P V is complete: it precedes this S
+            if (kt > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+                for (int c = 0; c < HD / 32; ++c) {
+                    float ov[32];
+                    pt_ld32(trow + PT_KT + 32 * c, ov);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+                    pt_st32(trow + PT_KT + 32 * c, ov);
+                }
+            }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         }
         pt_fence_before();
         __syncthreads();
         if (s_bad) break;
-        // 4. O_tile = P V
+        // 4. O (+)= P V
         if (tid == 0) {
             pt_fence_after();
             const uint32_t pa = pt_smem_u32(ps), va = pt_smem_u32(vs);
 #pragma unroll
             for (int kk = 0; kk < PT_KT / 16; ++kk)
                 pt_mma(tmem + PT_KT, pt_desc_k(pa + (kk >> 2) * ATOM_COL + 32 * (kk & 3)),
-                       pt_desc_mn(va + kk * 2 * (NA * 1024), 1024, NA * 1024), idesc_o, kk > 0 ? 1u : 0u);
+                       pt_desc_mn(va + kk * 2 * (NA * 1024), 1024, NA * 1024), idesc_o, (kt > 0 || kk > 0) ? 1u : 0u);
             pt_commit(pt_smem_u32(&s_bar[1]));
         }
-        // 5. o = o * alpha + O_tile
-        if (warp < 4) {
-            if (!pt_wait(pt_smem_u32(&s_bar[1]), kt & 1)) {
-                atomicExch(err, 2);
-                s_bad = 1;
-            }
+    }
+    // 5. the last P V; o / l (the TMEM reads by whole warps, stores by the rows that hold a token)
+    if (!s_bad && warp < 4) {
+        const bool done = __all_sync(0xffffffffu, pt_wait(pt_smem_u32(&s_bar[1]), (ntiles - 1) & 1));
+        if (!done) {
+            if (lane == 0) atomicExch(err, 2);
+        } else {
             pt_fence_after();
-#pragma unroll
+            const int ti = row / G, g = row % G;
+            float* dst = att + (size_t)(t0 + ti) * nq + (size_t)(kvh * G + g) * HD;
+#pragma unroll 1
             for (int c = 0; c < HD / 32; ++c) {
-                float v[32];
-                pt_ld32(trow + PT_KT + 32 * c, v);
+                float ov[32];
+                pt_ld32(trow + PT_KT + 32 * c, ov);
+                if (qpos >= 0) {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) o[32 * c + i] = fmaf(o[32 * c + i], alpha, v[i]);
+                    for (int d = 0; d < 32; d += 4)
+                        *reinterpret_cast<float4*>(dst + 32 * c + d) =
+                            make_float4(__fdiv_rn(ov[d], l), __fdiv_rn(ov[d + 1], l), __fdiv_rn(ov[d + 2], l),
+                                        __fdiv_rn(ov[d + 3], l));
+                }
             }
         }
-        pt_fence_before();
-        __syncthreads();  // K, V, P and both TMEM regions are free for the next tile
-        if (s_bad) break;
-    }
-    if (warp < 4 && !s_bad && qpos >= 0) {
-        const int ti = row / G, g = row % G;
-        float* dst = att + (size_t)(t0 + ti) * nq + (size_t)(kvh * G + g) * HD;
-#pragma unroll
-        for (int d = 0; d < HD; d += 4)
-            *reinterpret_cast<float4*>(dst + d) = make_float4(__fdiv_rn(o[d], l), __fdiv_rn(o[d + 1], l),
-                                                              __fdiv_rn(o[d + 2], l), __fdiv_rn(o[d + 3], l));
     }
     pt_fence_before();
     __syncthreads();
