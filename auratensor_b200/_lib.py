@@ -65,6 +65,17 @@ class ModelConfig(C.Structure):
                 ("max_batch", C.c_int32), ("layout", C.c_int32), ("kv_type", C.c_int32), ("reserved", C.c_int32)]
 
 
+class ShardRegion(C.Structure):
+    """at_shard_region: the part of a weight tensor one tensor-parallel rank keeps."""
+    _fields_ = [("target", C.c_int32), ("orient", C.c_int32), ("rows", C.c_int64), ("cols", C.c_int64),
+                ("local_rows", C.c_int64), ("local_cols", C.c_int64), ("src_row0", C.c_int64),
+                ("src_col0", C.c_int64), ("n_rows", C.c_int64), ("n_cols", C.c_int64), ("dst_row0", C.c_int64),
+                ("dst_col0", C.c_int64)]
+
+
+SHARD_NONE, SHARD_TOKEN_EMBD, SHARD_OUTPUT, SHARD_QKV, SHARD_WO, SHARD_W1, SHARD_W3, SHARD_W2, SHARD_NORM = range(-1, 8)
+
+
 class SamplerConfigC(C.Structure):
     """at_sampler_config: Sampler.Config plus a host penalty history."""
     _fields_ = [("temperature", C.c_float), ("top_k", C.c_int32), ("top_p", C.c_float),
@@ -141,6 +152,7 @@ SIGNATURES = {
     "at_sample": [_vp, _i, _vp, _i, _f, _i, _f, _f, _i64, C.POINTER(C.c_int)],
     "at_tp_unique_id": [_vp],
     "at_ctx_create_tp": [_i, _i, _i, _vp, _PP],
+    "at_tp_shard_region": [_vp, _i, _i, C.c_char_p, _vp],
 }
 
 _lib = None

@@ -1181,6 +1181,73 @@ bool parse_layer(const std::string& name, int* layer, std::string* leaf) {
     return true;
 }
 
+// Model dimensions a tensor-parallel rank's shard cut depends on.
+struct ShardDims {
+    int64_t d, hd, H, Hkv, F, V, Hl, Hkvl, Fl, Vl;
+    int W, r;
+    bool attn_n;  // attention weights [out][in] (llama.cpp) instead of [in][out]
+};
+
+ShardDims shard_dims(const at_model* m, int W, int r) {
+    return ShardDims{m->d, m->hd, m->H, m->Hkv, m->F, m->V, m->Hl, m->Hkvl, m->Fl, m->Vl, W, r, m->attn_n};
+}
+
+// The part of a logical weight tensor that rank r of W keeps and where it
+// lands in the rank's device matrix (Megatron: wq/wk/wv by heads into the
+// fused [q|k|v] matrix, wo by its head rows, w1/w3 by output rows, w2 by
+// input columns, lm_head by vocabulary rows; norms and the embedding whole).
+// The tensor's shape follows Weights.wrapByName (inference/Weights.java:84-112);
+// the upload (at_model_set_tensor) and at_tp_shard_region both use this.
+void shard_region(const ShardDims& s, const std::string& name, at_shard_region* o) {
+    *o = at_shard_region{};
+    o->target = AT_SHARD_NONE;
+    o->orient = AT_ORIENT_N;
+    int layer = -1;
+    std::string leaf;
+    const bool is_layer = parse_layer(name, &layer, &leaf);
+    const int64_t nq = s.Hl * s.hd, nkv = s.Hkvl * s.hd, qcols = nq + 2 * nkv;
+    auto set = [&](int target, int orient, int64_t rows, int64_t cols, int64_t lr, int64_t lc, int64_t sr0,
+                   int64_t sc0, int64_t nr, int64_t nc, int64_t dr0, int64_t dc0) {
+        *o = at_shard_region{target, orient, rows, cols, lr, lc, sr0, sc0, nr, nc, dr0, dc0};
+    };
+    if (name == "output_norm.weight" || (is_layer && (leaf == "attn_norm.weight" || leaf == "ffn_norm.weight"))) {
+        set(AT_SHARD_NORM, AT_ORIENT_N, 1, s.d, 1, s.d, 0, 0, 1, s.d, 0, 0);
+    } else if (name == "token_embd.weight") {
+        set(AT_SHARD_TOKEN_EMBD, AT_ORIENT_N, s.V, s.d, s.V, s.d, 0, 0, s.V, s.d, 0, 0);
+    } else if (name == "output.weight") {
+        const int64_t v0 = (int64_t)s.r * s.Vl;
+        const int64_t nv = std::max<int64_t>(0, std::min<int64_t>(s.Vl, s.V - v0));
+        set(AT_SHARD_OUTPUT, AT_ORIENT_N, s.V, s.d, s.Vl, s.d, v0, 0, nv, s.d, 0, 0);
+    } else if (!is_layer) {
+        return;
+    } else if (s.attn_n) {  // [out][in]: the rank's heads are rows (wq/wk/wv) or input columns (wo)
+        if (leaf == "attn_q.weight")
+            set(AT_SHARD_QKV, AT_ORIENT_N, s.H * s.hd, s.d, qcols, s.d, s.r * nq, 0, nq, s.d, 0, 0);
+        else if (leaf == "attn_k.weight")
+            set(AT_SHARD_QKV, AT_ORIENT_N, s.Hkv * s.hd, s.d, qcols, s.d, s.r * nkv, 0, nkv, s.d, nq, 0);
+        else if (leaf == "attn_v.weight")
+            set(AT_SHARD_QKV, AT_ORIENT_N, s.Hkv * s.hd, s.d, qcols, s.d, s.r * nkv, 0, nkv, s.d, nq + nkv, 0);
+        else if (leaf == "attn_output.weight")
+            set(AT_SHARD_WO, AT_ORIENT_N, s.d, s.H * s.hd, s.d, nq, 0, s.r * nq, s.d, nq, 0, 0);
+    } else {  // the reference's [in][out] attention: the rank's heads are columns (wq/wk/wv) or rows (wo)
+        if (leaf == "attn_q.weight")
+            set(AT_SHARD_QKV, AT_ORIENT_T, s.d, s.H * s.hd, s.d, qcols, 0, s.r * nq, s.d, nq, 0, 0);
+        else if (leaf == "attn_k.weight")
+            set(AT_SHARD_QKV, AT_ORIENT_T, s.d, s.Hkv * s.hd, s.d, qcols, 0, s.r * nkv, s.d, nkv, 0, nq);
+        else if (leaf == "attn_v.weight")
+            set(AT_SHARD_QKV, AT_ORIENT_T, s.d, s.Hkv * s.hd, s.d, qcols, 0, s.r * nkv, s.d, nkv, 0, nq + nkv);
+        else if (leaf == "attn_output.weight")
+            set(AT_SHARD_WO, AT_ORIENT_T, s.H * s.hd, s.d, nq, s.d, s.r * nq, 0, nq, s.d, 0, 0);
+    }
+    if (o->target != AT_SHARD_NONE || !is_layer) return;
+    if (leaf == "ffn_gate.weight")
+        set(AT_SHARD_W1, AT_ORIENT_N, s.F, s.d, s.Fl, s.d, s.r * s.Fl, 0, s.Fl, s.d, 0, 0);
+    else if (leaf == "ffn_up.weight")
+        set(AT_SHARD_W3, AT_ORIENT_N, s.F, s.d, s.Fl, s.d, s.r * s.Fl, 0, s.Fl, s.d, 0, 0);
+    else if (leaf == "ffn_down.weight")
+        set(AT_SHARD_W2, AT_ORIENT_N, s.d, s.F, s.d, s.Fl, 0, s.r * s.Fl, s.d, s.Fl, 0, 0);
+}
+
 // Brackets the launches of one kernel class with events when profiling.
 struct ProfScope {
     at_model* m;
@@ -1872,6 +1939,24 @@ int at_model_create(at_ctx* ctx, const at_model_config* cfg, at_model** out) {
     return rc;
 }
 
+int at_tp_shard_region(const at_model_config* cfg, int world, int rank, const char* tensor_name,
+                       at_shard_region* out) {
+    return guard([&] {
+        AT_REQUIRE(cfg && tensor_name && out, AT_ERR_INVALID_ARG, "null argument");
+        AT_REQUIRE(world >= 1 && world <= 8 && rank >= 0 && rank < world, AT_ERR_INVALID_ARG,
+                   "rank must be in [0, world) and world in [1, 8]");
+        AT_REQUIRE(cfg->head_count > 0 && cfg->head_count_kv > 0 && cfg->embedding_length % cfg->head_count == 0,
+                   AT_ERR_INVALID_ARG, "embedding_length must be a multiple of head_count");
+        const int64_t H = cfg->head_count, Hkv = cfg->head_count_kv, F = cfg->feed_forward_length;
+        const int64_t V = cfg->vocab_size, d = cfg->embedding_length;
+        AT_REQUIRE(Hkv % world == 0, AT_ERR_INVALID_ARG, "KV heads must divide evenly across tensor-parallel ranks");
+        AT_REQUIRE(F % (32 * world) == 0, AT_ERR_INVALID_ARG, "FFN width must split into 32-aligned shards");
+        const ShardDims s{d, d / H, H, Hkv, F, V, H / world, Hkv / world, F / world, (V + world - 1) / world,
+                          world, rank, (cfg->layout & AT_LAYOUT_ATTN_OUT_IN) != 0};
+        shard_region(s, tensor_name, out);
+    });
+}
+
 int at_model_set_tensor(at_model* m, const char* cname, int type, const void* data, size_t bytes, int on_device) {
     void* staging = nullptr;
     const int rc = guard([&] {
@@ -1880,26 +1965,16 @@ int at_model_set_tensor(at_model* m, const char* cname, int type, const void* da
         at_ctx* c = m->ctx;
         AT_CUDA(cudaSetDevice(c->device));
         const std::string name(cname);
-        const int W = c->world, r = c->rank;
-        const int d = m->d, hd = m->hd;
+        const int d = m->d;
         int layer = -1;
         std::string leaf;
         const bool is_layer = parse_layer(name, &layer, &leaf);
         if (is_layer) AT_REQUIRE(layer >= 0 && layer < m->L, AT_ERR_INVALID_ARG, "layer index out of range: " + name);
-        const bool is_norm = (name == "output_norm.weight") || (is_layer && (leaf == "attn_norm.weight" ||
-                                                                              leaf == "ffn_norm.weight"));
-        // element count of the logical tensor (inference/Weights.java:84-112)
-        int64_t rows = 0, cols = 0;
-        if (is_norm) { rows = 1; cols = d; }
-        else if (name == "token_embd.weight" || name == "output.weight") { rows = m->V; cols = d; }
-        // attention bytes are [in][out] in the reference's layout, [out][in] in llama.cpp's
-        else if (is_layer && leaf == "attn_q.weight") { rows = d; cols = (int64_t)m->H * hd; }
-        else if (is_layer && (leaf == "attn_k.weight" || leaf == "attn_v.weight")) { rows = d; cols = (int64_t)m->Hkv * hd; }
-        else if (is_layer && leaf == "attn_output.weight") { rows = (int64_t)m->H * hd; cols = d; }
-        else if (is_layer && (leaf == "ffn_gate.weight" || leaf == "ffn_up.weight")) { rows = m->F; cols = d; }
-        else if (is_layer && leaf == "ffn_down.weight") { rows = d; cols = m->F; }
-        else return;  // tensors the decode path does not read are ignored, as in Weights.load
-        if (m->attn_n && is_layer && leaf.rfind("attn_", 0) == 0 && leaf != "attn_norm.weight") std::swap(rows, cols);
+        at_shard_region rg;
+        shard_region(shard_dims(m, c->world, c->rank), name, &rg);
+        const bool is_norm = rg.target == AT_SHARD_NORM;
+        if (rg.target == AT_SHARD_NONE) return;  // tensors the decode path does not read are ignored, as in Weights.load
+        const int64_t rows = rg.rows, cols = rg.cols;
         const int64_t numel = rows * cols;
         size_t expect;
         const bool emb_or_out = name == "token_embd.weight" || name == "output.weight";
@@ -1938,42 +2013,19 @@ int at_model_set_tensor(at_model* m, const char* cname, int type, const void* da
                            "tensor '" + name + "' differs in type from the tensors fused with it");
                 qmat_fill_region(&q, s8, cols, sr0, sc0, nr, nc, dr0, dc0, c->stream, nib_split);
             };
-            const int64_t qcols = (int64_t)(m->Hl + 2 * m->Hkvl) * hd;
-            if (name == "token_embd.weight") {
-                place(m->tok, AT_ORIENT_N, m->V, d, 0, 0, m->V, d, 0, 0);
-            } else if (name == "output.weight") {
-                const int64_t v0 = (int64_t)r * m->Vl;
-                const int64_t nv = std::max<int64_t>(0, std::min<int64_t>(m->Vl, m->V - v0));
-                place(m->out, AT_ORIENT_N, m->Vl, d, v0, 0, nv, d, 0, 0);
-            } else {
-                Layer& ly = m->layers[layer];
-                const int64_t nq = (int64_t)m->Hl * hd, nkv = (int64_t)m->Hkvl * hd;
-                if (m->attn_n && leaf == "attn_q.weight")  // [out][in]: this rank's heads are rows
-                    place(ly.qkv, AT_ORIENT_N, qcols, d, (int64_t)r * nq, 0, nq, d, 0, 0);
-                else if (m->attn_n && leaf == "attn_k.weight")
-                    place(ly.qkv, AT_ORIENT_N, qcols, d, (int64_t)r * nkv, 0, nkv, d, nq, 0);
-                else if (m->attn_n && leaf == "attn_v.weight")
-                    place(ly.qkv, AT_ORIENT_N, qcols, d, (int64_t)r * nkv, 0, nkv, d, nq + nkv, 0);
-                else if (m->attn_n && leaf == "attn_output.weight")  // its heads are input columns
-                    place(ly.wo, AT_ORIENT_N, d, nq, 0, (int64_t)r * nq, d, nq, 0, 0);
-                else if (leaf == "attn_q.weight")
-                    place(ly.qkv, AT_ORIENT_T, d, qcols, 0, (int64_t)r * m->Hl * hd, d, (int64_t)m->Hl * hd, 0, 0);
-                else if (leaf == "attn_k.weight")
-                    place(ly.qkv, AT_ORIENT_T, d, qcols, 0, (int64_t)r * m->Hkvl * hd, d, (int64_t)m->Hkvl * hd, 0,
-                          (int64_t)m->Hl * hd);
-                else if (leaf == "attn_v.weight")
-                    place(ly.qkv, AT_ORIENT_T, d, qcols, 0, (int64_t)r * m->Hkvl * hd, d, (int64_t)m->Hkvl * hd, 0,
-                          (int64_t)(m->Hl + m->Hkvl) * hd);
-                else if (leaf == "attn_output.weight")
-                    place(ly.wo, AT_ORIENT_T, (int64_t)m->Hl * hd, d, (int64_t)r * m->Hl * hd, 0, (int64_t)m->Hl * hd, d,
-                          0, 0);
-                else if (leaf == "ffn_gate.weight")
-                    place(ly.w1, AT_ORIENT_N, m->Fl, d, (int64_t)r * m->Fl, 0, m->Fl, d, 0, 0);
-                else if (leaf == "ffn_up.weight")
-                    place(ly.w3, AT_ORIENT_N, m->Fl, d, (int64_t)r * m->Fl, 0, m->Fl, d, 0, 0);
-                else if (leaf == "ffn_down.weight")
-                    place(ly.w2, AT_ORIENT_N, d, m->Fl, 0, (int64_t)r * m->Fl, d, m->Fl, 0, 0);
+            at_qmat* dst = nullptr;
+            switch (rg.target) {
+                case AT_SHARD_TOKEN_EMBD: dst = &m->tok; break;
+                case AT_SHARD_OUTPUT: dst = &m->out; break;
+                case AT_SHARD_QKV: dst = &m->layers[layer].qkv; break;
+                case AT_SHARD_WO: dst = &m->layers[layer].wo; break;
+                case AT_SHARD_W1: dst = &m->layers[layer].w1; break;
+                case AT_SHARD_W3: dst = &m->layers[layer].w3; break;
+                case AT_SHARD_W2: dst = &m->layers[layer].w2; break;
+                default: fail(AT_ERR_INVALID_ARG, "tensor '" + name + "' has no device matrix");
             }
+            place(*dst, rg.orient, rg.local_rows, rg.local_cols, rg.src_row0, rg.src_col0, rg.n_rows, rg.n_cols,
+                  rg.dst_row0, rg.dst_col0);
         }
         AT_CUDA(cudaStreamSynchronize(c->stream));
         m->seen[name] = true;

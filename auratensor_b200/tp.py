@@ -17,7 +17,7 @@ import ctypes as C
 import torch
 import torch.distributed as dist
 
-from ._lib import call
+from ._lib import ModelConfig, ShardRegion, call
 
 
 def shard_plan(n_heads: int, n_kv_heads: int, ffn: int, vocab: int, world: int) -> dict:
@@ -42,6 +42,14 @@ def shard_plan(n_heads: int, n_kv_heads: int, ffn: int, vocab: int, world: int) 
             for r in range(world)
         },
     }
+
+
+def shard_region(cfg: ModelConfig, world: int, rank: int, tensor_name: str) -> ShardRegion:
+    """The part of a GGUF tensor rank ``rank`` keeps, as the library's upload
+    cuts it (``at_tp_shard_region``: host-only, no GPU needed)."""
+    out = ShardRegion()
+    call("at_tp_shard_region", C.byref(cfg), world, rank, tensor_name.encode(), C.byref(out))
+    return out
 
 
 def unique_id() -> bytes:

@@ -357,6 +357,37 @@ int at_tp_unique_id(uint8_t out_id[128]);
  * all-reduce after each attention block and each MLP block. */
 int at_ctx_create_tp(int device, int rank, int world, const uint8_t id[128], at_ctx** out);
 
+/* The shard of one GGUF weight tensor that rank `rank` of `world` keeps, as
+ * at_model_set_tensor cuts it (host-only query, no device work). The tensor's
+ * shape follows Weights.wrapByName (inference/Weights.java:84-112); the cut is
+ * Megatron's: wq/wk/wv by heads into the rank's fused [q|k|v] matrix, wo by
+ * its head rows (input), w1/w3 by output rows, w2 by input columns, lm_head
+ * by vocabulary rows (the last rank's share may be short or empty); norms and
+ * the token embedding stay whole. With cfg->layout & AT_LAYOUT_ATTN_OUT_IN
+ * the attention tensors are [out][in] and the same heads are rows/columns
+ * swapped. Tensors the decode path does not read give target AT_SHARD_NONE.
+ * Fails like at_model_create when the heads or the FFN do not divide. */
+#define AT_SHARD_NONE        -1
+#define AT_SHARD_TOKEN_EMBD   0
+#define AT_SHARD_OUTPUT       1
+#define AT_SHARD_QKV          2
+#define AT_SHARD_WO           3
+#define AT_SHARD_W1           4
+#define AT_SHARD_W3           5
+#define AT_SHARD_W2           6
+#define AT_SHARD_NORM         7
+typedef struct at_shard_region {
+    int32_t target;                 /* AT_SHARD_*: the rank's device matrix the bytes go to */
+    int32_t orient;                 /* AT_ORIENT_N / AT_ORIENT_T of that matrix */
+    int64_t rows, cols;             /* the whole tensor as its bytes are laid out: [rows][cols] */
+    int64_t local_rows, local_cols; /* the rank's device matrix */
+    int64_t src_row0, src_col0;     /* first row / column of the tensor this rank keeps */
+    int64_t n_rows, n_cols;         /* extent of that part (0 rows: nothing) */
+    int64_t dst_row0, dst_col0;     /* where the part starts in the device matrix */
+} at_shard_region;
+int at_tp_shard_region(const at_model_config* cfg, int world, int rank, const char* tensor_name,
+                       at_shard_region* out);
+
 #ifdef __cplusplus
 }
 #endif
