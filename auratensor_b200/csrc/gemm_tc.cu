@@ -10,8 +10,10 @@
 // the activations are rounded to bf16 on the way in, and products are summed
 // in FP32 in tensor memory.
 //
-// CTA tile: 128 outputs (MMA M) x 256 tokens (MMA N), K in steps of 64, so a
-// dequantized weight tile feeds 256 tokens.
+// CTA tile: 128 outputs (MMA M) x 256 or 512 tokens (NB token tiles of MMA
+// N = 256, one TMEM accumulator each), K in steps of 64, so a dequantized
+// weight tile feeds up to 512 tokens: the dequant warps, not the tensor pipe,
+// bound the 256-token form.
 // The token tile and the orientation-N weight tile are K-major in the
 // canonical 128-byte-swizzled layout: row r of a tile is 128 bytes (64 bf16)
 // at (r / 8) * 1024 + (r % 8) * 128, and its 16-byte chunk c is stored at
@@ -24,11 +26,14 @@
 // completing on the stage's "full" mbarrier; the weight tile is dequantized
 // by one of two groups of 8 warps (alternate steps) from raw block bytes
 // loaded into registers three (Q8_0: two) of the group's steps ahead.
-// One thread issues four tcgen05.mma (K = 16 each) per step and commits them
-// to the stage's "empty" mbarrier; four stages (TC_STAGES) keep the TMA, the dequant and
-// the tensor core working on different steps. The 128 x 256 FP32 accumulator
-// lives in 256 TMEM columns; the epilogue reads it with tcgen05.ld (warp w
-// reads TMEM lanes 32 (w % 4) ..) and stores FP32 rows of Y.
+// One thread issues four tcgen05.mma (K = 16 each) per token tile and step
+// and commits them to the stages' "empty" mbarriers. The weight tiles and the
+// token tiles have rings of their own: four weight stages, and four 32 KB
+// (NB = 1) or two 64 KB (NB = 2) token stages, so the TMA, the dequant and
+// the tensor core work on different steps within 192 KB of shared memory.
+// The 128 x 256 NB FP32 accumulator lives in 256 NB TMEM columns; the
+// epilogue reads it with tcgen05.ld (warp w reads TMEM lanes 32 (w % 4) ..)
+// and stores FP32 rows of Y.
 //
 // Every wait on an mbarrier is bounded; a wait that runs out records an error
 // code, stops issuing, drains the token-tile copies still in flight, and the
@@ -57,10 +62,13 @@ constexpr int TC_DQ_GROUPS = 2;  // such groups, taking alternate K steps
 constexpr int TC_THREADS_WS = 64 + 32 * TC_DQ_WARPS * TC_DQ_GROUPS;  // + a TMA warp and an MMA warp
 constexpr int TC_TILE_BYTES = TC_M * TC_K * 2;  // 16 KB weight tile
 constexpr int TC_B_BYTES = TC_N * TC_K * 2;     // 32 KB token tile
-constexpr int TC_STAGES = 4;
-constexpr int TC_STAGE_BYTES = TC_TILE_BYTES + TC_B_BYTES;
-constexpr int TC_SMEM = TC_STAGES * TC_STAGE_BYTES + 1024;  // + alignment slack
-constexpr uint32_t TC_TMEM_COLS = TC_N;                     // FP32 accumulator columns
+constexpr int TC_A_STAGES = 4;                  // weight-tile ring
+// token-tile ring of NB tiles per stage, and the dynamic shared memory
+template <int NB>
+constexpr int tc_b_stages() { return NB == 1 ? 4 : 2; }
+template <int NB>
+constexpr int tc_smem() { return TC_A_STAGES * TC_TILE_BYTES + tc_b_stages<NB>() * NB * TC_B_BYTES + 1024; }
+static_assert(tc_smem<1>() <= 227 * 1024 && tc_smem<2>() <= 227 * 1024, "shared memory per CTA");
 constexpr int kTcSpinLimit = 1 << 22;
 constexpr int kTcMaxSplits = 4;
 
@@ -281,25 +289,30 @@ constexpr int tc_pf() { return QT == AT_GGML_Q8_0 ? 2 : 3; }
 // Warp roles: warp 0 issues the token tiles' TMA, warp 1 owns TMEM and issues
 // the MMAs, warps 2-9 dequantize the weight tiles of even steps and warps
 // 10-17 those of odd steps (256 threads, one block of 32 weights each per
-// step). Per stage: full_b (TMA bytes), full_a (8 warp arrivals after each
-// warp's stores and proxy fence; the group's first warp arrives only after
-// full_b, so full_a alone gates the MMAs) and empty (the MMAs' commit); no
+// step). Per weight stage: full_a (8 warp arrivals after each warp's stores
+// and proxy fence; the group's first warp arrives only after the step's
+// full_b, so full_a alone gates the MMAs) and empty_a; per token stage:
+// full_b (TMA bytes) and empty_b; both empties are the MMAs' commits. No
 // CTA-wide barrier inside the K loop.
-template <int QT, int OR>
+template <int QT, int OR, int NB>
 // 18 warps put 5 on one of the SM's four 16,384-register partitions: at
 // most 96 registers a thread. Templated on the quant type and orientation so
 // that each instance holds only the registers it uses.
 __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap,
                                                                    const TcParams p) {
+    constexpr int AS = TC_A_STAGES, BS = tc_b_stages<NB>();
+    constexpr uint32_t TMEM_COLS = TC_N * NB;  // FP32 accumulator columns
     extern __shared__ uint8_t smem_raw[];
-    __shared__ __align__(8) uint64_t s_fa[TC_STAGES], s_fb[TC_STAGES], s_empty[TC_STAGES], s_done;
+    __shared__ __align__(8) uint64_t s_fa[AS], s_ea[AS], s_fb[BS], s_eb[BS], s_done;
     __shared__ uint32_t s_tmem;
     __shared__ int s_bad;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int m0 = blockIdx.x * TC_M, t0 = blockIdx.y * TC_N;
+    const int m0 = blockIdx.x * TC_M, t0 = blockIdx.y * TC_N * NB;
+    // token tiles of this CTA that hold tokens (the last CTA row may have one)
+    const int nbv = (NB == 2 && t0 + TC_N < p.T) ? 2 : 1;
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    auto a_tile = [&](int st) { return base + st * TC_STAGE_BYTES; };
-    auto b_tile = [&](int st) { return base + st * TC_STAGE_BYTES + TC_TILE_BYTES; };
+    auto a_tile = [&](int st) { return base + st * TC_TILE_BYTES; };
+    auto b_tile = [&](int st) { return base + AS * TC_TILE_BYTES + st * NB * TC_B_BYTES; };
     const int nk_all = p.K / TC_K;
     const int ks0 = (int)((int64_t)blockIdx.z * nk_all / p.splits);
     const int nk = (int)((int64_t)(blockIdx.z + 1) * nk_all / p.splits) - ks0;  // steps of this split
@@ -308,15 +321,18 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
 
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                     "r"(TC_TMEM_COLS)
+                     "r"(TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        for (int st = 0; st < TC_STAGES; ++st) {
+        for (int st = 0; st < AS; ++st) {
             mbar_init(smem_u32(&s_fa[st]), TC_DQ_WARPS);
+            mbar_init(smem_u32(&s_ea[st]), 1);
+        }
+        for (int st = 0; st < BS; ++st) {
             mbar_init(smem_u32(&s_fb[st]), 1);
-            mbar_init(smem_u32(&s_empty[st]), 1);
+            mbar_init(smem_u32(&s_eb[st]), 1);
         }
         mbar_init(smem_u32(&s_done), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -334,13 +350,15 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
         // ---- token tiles by TMA ----
         if (lane == 0) {
             for (int ks = 0; ks < nk; ++ks) {
-                const int st = ks % TC_STAGES;
-                if (ks >= TC_STAGES && !mbar_wait(smem_u32(&s_empty[st]), ((ks - TC_STAGES) / TC_STAGES) & 1)) {
+                const int st = ks % BS;
+                if (ks >= BS && !mbar_wait(smem_u32(&s_eb[st]), ((ks - BS) / BS) & 1)) {
                     fail();
                     break;
                 }
-                mbar_expect_tx(smem_u32(&s_fb[st]), TC_B_BYTES);
-                tma_load_x(smem_u32(b_tile(st)), &xmap, kbase + ks * TC_K, t0, smem_u32(&s_fb[st]));
+                mbar_expect_tx(smem_u32(&s_fb[st]), TC_B_BYTES * nbv);
+                for (int nb = 0; nb < nbv; ++nb)
+                    tma_load_x(smem_u32(b_tile(st) + nb * TC_B_BYTES), &xmap, kbase + ks * TC_K, t0 + nb * TC_N,
+                               smem_u32(&s_fb[st]));
                 ++tma_issued;
             }
         }
@@ -351,19 +369,23 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
             constexpr bool mn = OR != AT_ORIENT_N;
             const uint32_t idesc = kIdesc | (mn ? kIdescTransposeA : 0u);
             for (int ks = 0; ks < nk; ++ks) {
-                const int st = ks % TC_STAGES;
-                const uint32_t par = (ks / TC_STAGES) & 1;
-                if (!mbar_wait(smem_u32(&s_fa[st]), par)) {  // full_a completes after full_b
+                const int sa = ks % AS, sb = ks % BS;
+                if (!mbar_wait(smem_u32(&s_fa[sa]), (ks / AS) & 1)) {  // full_a completes after full_b
                     fail();
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a_addr = smem_u32(a_tile(st)), b_addr = smem_u32(b_tile(st));
+                const uint32_t a_addr = smem_u32(a_tile(sa)), b_addr = smem_u32(b_tile(sb));
 #pragma unroll
-                for (int kk = 0; kk < TC_K / 16; ++kk)  // 16 k per MMA: 32 B of a K-major row, 2 M-major row groups
-                    tc_mma(tmem, mn ? make_sdesc_sw128_mn(a_addr + 4096 * kk) : make_sdesc_sw128(a_addr + 32 * kk),
-                           make_sdesc_sw128(b_addr + 32 * kk), idesc, (ks > 0 || kk > 0) ? 1u : 0u);
-                tc_commit(smem_u32(&s_empty[st]));
+                for (int kk = 0; kk < TC_K / 16; ++kk) {  // 16 k per MMA: 32 B of a K-major row, 2 M-major row groups
+                    const uint64_t ad =
+                        mn ? make_sdesc_sw128_mn(a_addr + 4096 * kk) : make_sdesc_sw128(a_addr + 32 * kk);
+                    for (int nb = 0; nb < nbv; ++nb)  // accumulator nb: tokens t0 + 256 nb ..
+                        tc_mma(tmem + (uint32_t)(nb * TC_N), ad, make_sdesc_sw128(b_addr + nb * TC_B_BYTES + 32 * kk),
+                               idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+                }
+                tc_commit(smem_u32(&s_ea[sa]));
+                tc_commit(smem_u32(&s_eb[sb]));
             }
             tc_commit(smem_u32(&s_done));  // arrives when every MMA above is complete
         }
@@ -388,11 +410,11 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
             for (int j = 0; j < PF; ++j) {
                 const int ks = kq + G * j;
                 if (ks >= nk) break;
-                const int st = ks % TC_STAGES;
+                const int st = ks % AS;
                 uint32_t pk[16];
                 decode_block<QT>(rb[j], pk);
                 if (ks + G * PF < nk) load_block<QT, OR>(rb[j], p, m0, kbase + (ks + G * PF) * TC_K, dt);
-                if (ks >= TC_STAGES && !mbar_wait(smem_u32(&s_empty[st]), ((ks - TC_STAGES) / TC_STAGES) & 1)) {
+                if (ks >= AS && !mbar_wait(smem_u32(&s_ea[st]), ((ks - AS) / AS) & 1)) {
                     if (lane == 0) fail();
                     stop = true;
                     break;
@@ -405,7 +427,7 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
                 // alone (one barrier round trip per step on its path).
                 int bad = 0;
                 if (lane == 0) {
-                    if (dt < 32) bad = !mbar_wait(smem_u32(&s_fb[st]), (ks / TC_STAGES) & 1);
+                    if (dt < 32) bad = !mbar_wait(smem_u32(&s_fb[ks % BS]), (ks / BS) & 1);
                     if (bad) fail();
                     else asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&s_fa[st])) : "memory");
                 }
@@ -426,16 +448,17 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
     // drain the loads still in flight (the latest one of each stage, bounded
     // waits) so that no copy lands in shared memory after the CTA exits.
     if (!ok && tid == 0)
-        for (int ks = max(0, tma_issued - TC_STAGES); ks < tma_issued; ++ks)
-            mbar_wait(smem_u32(&s_fb[ks % TC_STAGES]), (ks / TC_STAGES) & 1);
+        for (int ks = max(0, tma_issued - BS); ks < tma_issued; ++ks)
+            mbar_wait(smem_u32(&s_fb[ks % BS]), (ks / BS) & 1);
     tc_fence_after();
     if (ok && warp >= 2) {
         constexpr int parts = TC_DQ_WARPS * TC_DQ_GROUPS / 4;  // warps sharing one TMEM lane quarter
         const int quarter = warp & 3, part = (warp - 2) >> 2;
         const int m = m0 + 32 * quarter + lane;
 #pragma unroll 1
-        for (int cc = 0; cc < TC_N / (32 * parts); ++cc) {
-            const int col = (TC_N / parts) * part + 32 * cc;
+        for (int cc = 0; cc < TC_N * NB / (32 * parts); ++cc) {
+            const int col = (TC_N * NB / parts) * part + 32 * cc;
+            if (t0 + col >= p.T) break;  // the part's later columns hold no tokens either
             float v[32];
             tc_ld32(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)col, v);
             if (m < p.M) {
@@ -450,7 +473,7 @@ __global__ void __launch_bounds__(TC_THREADS_WS, 1) gemm_tc_kernel(const __grid_
     tc_fence_before();
     __syncthreads();
     if (warp == 1)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
 }
 
 // y[t][m] = sum over splits z (in order) of ws[z][t][m]; block row t,
@@ -512,10 +535,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace
 
+// Token tiles per CTA: two (512 tokens, every dequantized weight tile feeds
+// twice the tokens) once a chunk has more than 256 tokens.
+int gemm_tc_nb(int T) { return T > TC_N ? 2 : 1; }
+
 int gemm_tc_splits(const at_qmat* m, int T, int num_sms) {
     const int64_t M = (m->orient == AT_ORIENT_N) ? m->rows : m->cols;
     const int64_t K = (m->orient == AT_ORIENT_N) ? m->cols : m->rows;
-    const int64_t tiles = ((M + TC_M - 1) / TC_M) * ((T + TC_N - 1) / TC_N);
+    const int64_t tn = (int64_t)TC_N * gemm_tc_nb(T);
+    const int64_t tiles = ((M + TC_M - 1) / TC_M) * ((T + tn - 1) / tn);
     // enough CTAs for most SMs, each split keeping at least 8 K-steps
     int64_t sp = std::max<int64_t>(1, (num_sms + tiles / 2) / tiles);
     sp = std::min<int64_t>(sp, std::max<int64_t>(1, (K / TC_K) / 8));
@@ -564,18 +592,24 @@ void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, in
     p.y = split ? ws : y;
     p.y_stride = split ? (int)M : y_stride;
     p.err = err;
-    auto kern = m->type == AT_GGML_Q4_0 ? (m->orient == AT_ORIENT_N ? gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_N>
-                                                                    : gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_T>)
-                                        : (m->orient == AT_ORIENT_N ? gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_N>
-                                                                    : gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_T>);
+    const int nb = gemm_tc_nb(T);
+    const bool q4 = m->type == AT_GGML_Q4_0, on = m->orient == AT_ORIENT_N;
+    auto kern = nb == 1 ? (q4 ? (on ? gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_N, 1> : gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_T, 1>)
+                              : (on ? gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_N, 1> : gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_T, 1>))
+                        : (q4 ? (on ? gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_N, 2> : gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_T, 2>)
+                              : (on ? gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_N, 2> : gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_T, 2>));
     static std::once_flag attr_once;
     std::call_once(attr_once, [] {
-        for (auto k : {gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_N>, gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_T>,
-                       gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_N>, gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_T>})
-            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+        for (auto k : {gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_N, 1>, gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_T, 1>,
+                       gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_N, 1>, gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_T, 1>})
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem<1>());
+        for (auto k : {gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_N, 2>, gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_T, 2>,
+                       gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_N, 2>, gemm_tc_kernel<AT_GGML_Q8_0, AT_ORIENT_T, 2>})
+            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem<2>());
     });
-    dim3 grid((unsigned)((M + TC_M - 1) / TC_M), (unsigned)((T + TC_N - 1) / TC_N), (unsigned)p.splits);
-    kern<<<grid, TC_THREADS_WS, TC_SMEM, s>>>(xmap, p);
+    const int tn = TC_N * nb;
+    dim3 grid((unsigned)((M + TC_M - 1) / TC_M), (unsigned)((T + tn - 1) / tn), (unsigned)p.splits);
+    kern<<<grid, TC_THREADS_WS, nb == 1 ? tc_smem<1>() : tc_smem<2>(), s>>>(xmap, p);
     AT_CUDA(cudaGetLastError());
     if (p.splits > 1) {
         const bool vec = M % 4 == 0 && y_stride % 4 == 0 && ((uintptr_t)y & 15) == 0 && ((uintptr_t)ws & 15) == 0;

@@ -2315,8 +2315,9 @@ int at_model_forward_step(at_model* m, int token, int64_t position, float* logit
 // path's tolerance is 2e-2 of the logit range), attention is the causal
 // prompt kernel over the KV cache of the target slot. Only the KV cache carries
 // over to the decode steps, so the last layer's feed-forward and the lm_head
-// are not needed; they are skipped.
-constexpr int PF_T = 256;
+// are not needed; they are skipped. A chunk of 512 tokens is one CTA row of
+// the GEMMs (two 256-token tiles per dequantized weight tile).
+constexpr int PF_T = 512;
 
 bool prompt_batched_ok(const at_model* m) {
     if (m->ctx->world != 1) return false;

@@ -12,10 +12,11 @@
 //      columns 0..127;
 //   3. warps 0-3 (TMEM lane quarters; thread = query row) read S, apply the
 //      scale (dot * scale, as the reference), the causal mask and the online
-//      softmax (running max and sum), and write P in bf16 (K-major A operand);
-//   4. one thread issues O_tile = P V (N = HD) into TMEM columns 128..;
-//   5. warps 0-3 fold O_tile into the row's FP32 output registers, rescaled
-//      by the softmax correction.
+//      softmax (running max and sum), write P in bf16 (K-major A operand)
+//      and rescale the output accumulator O (TMEM columns 128..) by the
+//      tile's correction;
+//   4. one thread issues O += P V (N = HD) into those TMEM columns;
+//   5. after the last tile, warps 0-3 read O and store o / l.
 // Operands are bf16 with FP32 sums (the prompt path's tolerance is 2e-2 of
 // the logit range). Every wait on an mbarrier is bounded: a wait that runs
 // out records an error code and the CTA frees its TMEM and returns.

@@ -235,7 +235,7 @@ def prompt_line(shape, world, n, dev_s, wall_s, requests=1):
         except (OSError, KeyError, ValueError):
             pass
         tf = prompt_flops(shape, n) * requests / dev_s / 1e12
-        out.update({"path": "tcgen05 bf16 GEMMs, 256-token chunks", "tflops": round(tf, 1),
+        out.update({"path": "tcgen05 bf16 GEMMs and attention, 512-token chunks", "tflops": round(tf, 1),
                     "peak_tflops": peak, "frac": round(tf / peak, 4)})
     else:
         out["path"] = "decode steps (tensor parallel)"
@@ -616,7 +616,7 @@ def main():
         "clocks": clocks,
         "cpu_baseline": cpu,
         "setup": {"load_s": round(load_s, 1), "prefill_s": round(prefill_s, 2)},
-        # the prompt outside the decode timing (forwardPrompt: tcgen05 GEMMs over 256-token chunks on one
+        # the prompt outside the decode timing (forwardPrompt: tcgen05 GEMMs over 512-token chunks on one
         # GPU), median of 3 runs after one warm-up, CUDA events
         "prompt": prompt_line(shape, world, args.prompt, prefill_dev_s, prefill_s),
     }

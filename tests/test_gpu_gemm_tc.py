@@ -36,19 +36,24 @@ def check(qt, orient, rows, cols, tokens, cuda, seed=0):
 
 @pytest.mark.parametrize("qt", [ref.GGML_Q4_0, ref.GGML_Q8_0])
 @pytest.mark.parametrize("orient", [ORIENT_N, ORIENT_T])
-@pytest.mark.parametrize("tokens", [1, 37, 128, 200, 256, 300, 512])
+@pytest.mark.parametrize("tokens", [1, 37, 128, 200, 256, 257, 300, 512, 513, 700, 1100])
 def test_gemm_tc_small(qt, orient, tokens, cuda):
+    """Above 256 tokens a CTA takes two 256-token tiles per weight tile (two
+    TMEM accumulators); a last CTA row may hold one tile (513, 700) or two
+    (1100: 512 + 512 + 76)."""
     check(qt, orient, 256, 128, tokens, cuda, seed=tokens)
 
 
 @pytest.mark.parametrize("qt", [ref.GGML_Q4_0, ref.GGML_Q8_0])
 @pytest.mark.parametrize("orient,rows,cols", [(ORIENT_N, 300, 640), (ORIENT_N, 1000, 256), (ORIENT_T, 640, 416),
                                               (ORIENT_T, 4096, 1024), (ORIENT_N, 16384, 128)])
-def test_gemm_tc_ragged(qt, orient, rows, cols, cuda):
+@pytest.mark.parametrize("tokens", [130, 450])
+def test_gemm_tc_ragged(qt, orient, rows, cols, tokens, cuda):
     """Ragged edges; the K steps of all tiles are split evenly over the SMs,
     so some tiles are summed from pieces of several CTAs (300 x 640: ten one-
-    step pieces per tile) and some are whole inside one CTA (16384 x 128)."""
-    check(qt, orient, rows, cols, 130, cuda, seed=rows + cols)
+    step pieces per tile) and some are whole inside one CTA (16384 x 128);
+    450 tokens run the two-tile CTAs."""
+    check(qt, orient, rows, cols, tokens, cuda, seed=rows + cols)
 
 
 @pytest.mark.parametrize("orient,rows,cols", [(ORIENT_N, 2048, 1024), (ORIENT_T, 1024, 2048)])
