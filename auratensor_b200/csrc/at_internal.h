@@ -1,6 +1,7 @@
 // Internal declarations shared by the translation units of libauratensor_cuda.so.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <cstdio>
@@ -204,18 +205,27 @@ void launch_gemv_q6k(const at_qmat* m, int batch, Pro pro, const GemvArgs& a, in
 // (the activations are converted into it; with x null it already holds them,
 // rows of `in` elements); ws (FP32, may be null) holds the
 // partials when K is split across CTAs (gemm_tc_splits(m, T) x T x out
-// floats); *err records a bounded wait that ran out (2).
+// floats); *err records a bounded wait that ran out (2). With opt.defer,
+// split partials stay in ws ([split][T][out], rows of `out` floats) for the
+// consumer to sum in split order, and the split count is returned there (1:
+// y holds the result).
 // Causal prompt attention on the tensor cores (prompt_attn_tc.cu): q [T][Hl
 // x hd] after RoPE, the layer's KV cache of one slot (kc / vc FP32, or Q8_0
 // quants with ksc / vsc scales when kvq), att [T][Hl x hd]; false (nothing
 // launched) for head_dim other than 64 / 128 or G = Hl / Hkvl not in 1, 2, 4,
 // 8. *err records a bounded wait that ran out (2).
+// With att_bf non-null the output is written there in bf16 (the wo GEMM's
+// staged operand, rounded as its conversion would) instead of att.
 bool launch_prompt_attn_tc(int hd, int G, bool kvq, int Hkvl, int T, cudaStream_t s, const float* q, const float* kc,
                            const float* vc, const uint16_t* ksc, const uint16_t* vsc, float* att, int64_t p0, int Hl,
-                           int ctx, float scale, int* err);
+                           int ctx, float scale, int* err, __nv_bfloat16* att_bf = nullptr);
+struct GemmTcOut {
+    int* defer = nullptr;  // split count out; partials left in ws
+};
 int gemm_tc_splits(const at_qmat* m, int T, int num_sms);
 void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, int y_stride, int T, void* xbf,
-                    size_t xbf_bytes, float* ws, size_t ws_bytes, int num_sms, int* err, cudaStream_t s);
+                    size_t xbf_bytes, float* ws, size_t ws_bytes, int num_sms, int* err, cudaStream_t s,
+                    const GemmTcOut& opt = GemmTcOut{});
 void launch_sgemv_f32(const float* A, const float* x, float* y, int M, int K, int batch, int a_ld,
                       cudaStream_t s);
 

@@ -551,7 +551,8 @@ int gemm_tc_splits(const at_qmat* m, int T, int num_sms) {
 }
 
 void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, int y_stride, int T, void* xbf,
-                    size_t xbf_bytes, float* ws, size_t ws_bytes, int num_sms, int* err, cudaStream_t s) {
+                    size_t xbf_bytes, float* ws, size_t ws_bytes, int num_sms, int* err, cudaStream_t s,
+                    const GemmTcOut& opt) {
     AT_REQUIRE(m->type == AT_GGML_Q4_0 || m->type == AT_GGML_Q8_0, AT_ERR_UNSUPPORTED,
                "tensor-core GEMM supports Q4_0 and Q8_0");
     const int64_t M = (m->orient == AT_ORIENT_N) ? m->rows : m->cols;
@@ -592,6 +593,7 @@ void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, in
     p.y = split ? ws : y;
     p.y_stride = split ? (int)M : y_stride;
     p.err = err;
+    if (opt.defer) *opt.defer = p.splits;
     const int nb = gemm_tc_nb(T);
     const bool q4 = m->type == AT_GGML_Q4_0, on = m->orient == AT_ORIENT_N;
     auto kern = nb == 1 ? (q4 ? (on ? gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_N, 1> : gemm_tc_kernel<AT_GGML_Q4_0, AT_ORIENT_T, 1>)
@@ -611,7 +613,7 @@ void launch_gemm_tc(const at_qmat* m, const float* x, int x_stride, float* y, in
     dim3 grid((unsigned)((M + TC_M - 1) / TC_M), (unsigned)((T + tn - 1) / tn), (unsigned)p.splits);
     kern<<<grid, TC_THREADS_WS, nb == 1 ? tc_smem<1>() : tc_smem<2>(), s>>>(xmap, p);
     AT_CUDA(cudaGetLastError());
-    if (p.splits > 1) {
+    if (p.splits > 1 && !opt.defer) {
         const bool vec = M % 4 == 0 && y_stride % 4 == 0 && ((uintptr_t)y & 15) == 0 && ((uintptr_t)ws & 15) == 0;
         const int per = vec ? (int)((M / 4 + 127) / 128) : (int)((M + 127) / 128);
         if (vec)

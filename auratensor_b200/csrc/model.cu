@@ -720,17 +720,52 @@ __global__ void argmax_index_kernel(const unsigned long long* __restrict__ keys,
 // Row-wise x_out = rmsNorm(x_in + y_in) * gamma with the reference's rounding
 // (the F7 residual stream): one CTA per row; with xbf, x_out also rounded to
 // bf16 [T][d] for the next tensor-core GEMM.
+// Element i of y summed over `splits` (<= 4) K-split GEMM partials `stride`
+// floats apart, in split order (the order of splitk_sum_kernel); the
+// partials' loads are predicated, not a loop, so they are all in flight.
+constexpr int kMaxPromptSplits = 4;
+__device__ __forceinline__ float4 split_sum4(const float* __restrict__ y, int splits, size_t stride, size_t i) {
+    float4 acc = *reinterpret_cast<const float4*>(y + i);
+    float4 p[kMaxPromptSplits - 1];
+#pragma unroll
+    for (int z = 1; z < kMaxPromptSplits; ++z)
+        if (z < splits) p[z - 1] = *reinterpret_cast<const float4*>(y + (size_t)z * stride + i);
+#pragma unroll
+    for (int z = 1; z < kMaxPromptSplits; ++z)
+        if (z < splits) {
+            acc.x += p[z - 1].x;
+            acc.y += p[z - 1].y;
+            acc.z += p[z - 1].z;
+            acc.w += p[z - 1].w;
+        }
+    return acc;
+}
+
+// One prompt row (CTA of 256 threads): t = x + y (y summed over its K-split
+// partials), RMSNorm of t into xout (FP32, the reference's rounding) and
+// xbf (bf16, the next GEMM's operand). t is staged in shared memory once
+// (d <= 8192, a multiple of 4).
+constexpr int kRowsMaxDim = 8192;
 __global__ void __launch_bounds__(256) rows_addnorm_kernel(const float* __restrict__ xin, const float* __restrict__ yin,
                                                            const float* __restrict__ gamma, float* __restrict__ xout,
-                                                           __nv_bfloat16* __restrict__ xbf, int d, float eps) {
+                                                           __nv_bfloat16* __restrict__ xbf, int d, float eps,
+                                                           int ysplits = 1, size_t ysplit_stride = 0) {
+    __shared__ float4 s_t[kRowsMaxDim / 4];
     __shared__ float s_red[8];
     const size_t row = blockIdx.x;
-    const float* a = xin + row * d;
-    const float* b = yin + row * d;
+    const int n4 = d >> 2;
+    const float4* a = reinterpret_cast<const float4*>(xin + row * d);
     float acc = 0.f;
-    for (int i = threadIdx.x; i < d; i += 256) {
-        const float t = __fadd_rn(a[i], b[i]);
-        acc = fmaf(t, t, acc);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n4; i += 256) {
+        const float4 y = split_sum4(yin, ysplits, ysplit_stride, row * d + 4 * (size_t)i);
+        const float4 x = a[i];
+        const float4 t = make_float4(__fadd_rn(x.x, y.x), __fadd_rn(x.y, y.y), __fadd_rn(x.z, y.z), __fadd_rn(x.w, y.w));
+        s_t[i] = t;
+        acc = fmaf(t.x, t.x, acc);
+        acc = fmaf(t.y, t.y, acc);
+        acc = fmaf(t.z, t.z, acc);
+        acc = fmaf(t.w, t.w, acc);
     }
     acc = warp_sum(acc);
     if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = acc;
@@ -739,10 +774,19 @@ __global__ void __launch_bounds__(256) rows_addnorm_kernel(const float* __restri
 #pragma unroll
     for (int w = 0; w < 8; ++w) tot += s_red[w];
     const float inv = rms_inv(tot, d, eps);
-    for (int i = threadIdx.x; i < d; i += 256) {
-        const float o = norm_apply(__fadd_rn(a[i], b[i]), inv, gamma[i]);
-        xout[row * d + i] = o;
-        if (xbf) xbf[row * d + i] = __float2bfloat16_rn(o);
+    const float4* g4 = reinterpret_cast<const float4*>(gamma);
+    for (int i = threadIdx.x; i < n4; i += 256) {
+        const float4 t = s_t[i], g = g4[i];
+        const float4 o = make_float4(norm_apply(t.x, inv, g.x), norm_apply(t.y, inv, g.y), norm_apply(t.z, inv, g.z),
+                                     norm_apply(t.w, inv, g.w));
+        reinterpret_cast<float4*>(xout + row * d)[i] = o;
+        if (xbf) {
+            const __nv_bfloat162 lo = __floats2bfloat162_rn(o.x, o.y), hi = __floats2bfloat162_rn(o.z, o.w);
+            uint2 u;
+            u.x = *reinterpret_cast<const uint32_t*>(&lo);
+            u.y = *reinterpret_cast<const uint32_t*>(&hi);
+            reinterpret_cast<uint2*>(xbf + row * d)[i] = u;
+        }
     }
 }
 
@@ -923,20 +967,31 @@ struct KvQ {
 // RoPE of q and k (core/Kernels.java:296-309: a' = fma(a, c, b * -s),
 // b' = fma(b, c, a * s)) and the KV-cache append (inference/KVCache.java:79-95)
 // of prompt row t at position p0 + t; q goes to q_out [T][nq].
+// One prompt token (CTA of 256 threads): the QKV GEMM's row (summed over
+// its K-split partials, staged in shared memory; qcols <= 10240) gets RoPE
+// on q and k; q goes to q_out, k and v are appended to the KV cache.
+constexpr int kRopeMaxCols = 10240;
 __global__ void __launch_bounds__(256) rope_append_kernel(const float* __restrict__ qkv, int qcols,
                                                           float* __restrict__ q_out, float* __restrict__ kc,
                                                           float* __restrict__ vc, KvQ kvq,
                                                           const float* __restrict__ rcos,
                                                           const float* __restrict__ rsin, int hd, int nq, int nkv,
-                                                          int ctx, int64_t p0) {
+                                                          int ctx, int64_t p0, int splits = 1,
+                                                          size_t split_stride = 0) {
+    __shared__ float4 s_row4[kRopeMaxCols / 4];
+    const float* s_row = reinterpret_cast<const float*>(s_row4);
     const int t = blockIdx.x;
     const int64_t pos = p0 + t;
-    const float* row = qkv + (size_t)t * qcols;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < qcols / 4; i += 256)
+        s_row4[i] = split_sum4(qkv, splits, split_stride, (size_t)t * qcols + 4 * (size_t)i);
+    __syncthreads();
+#pragma unroll 4
     for (int j = threadIdx.x; j < qcols; j += 256) {
-        const float val = row[j];
+        const float val = s_row[j];
         if (j < nq + nkv) {
             const int dd = (j < nq ? j : j - nq) % hd;
-            const float partner = row[j ^ 1];
+            const float partner = s_row[j ^ 1];
             const float cs = rcos[pos * hd + dd], sn = rsin[pos * hd + dd];
             const float out = ((dd & 1) == 0) ? fmaf(val, cs, __fmul_rn(partner, -sn)) : fmaf(val, cs, __fmul_rn(partner, sn));
             if (j < nq) {
@@ -2323,6 +2378,8 @@ bool prompt_batched_ok(const at_model* m) {
     if (m->ctx->world != 1) return false;
     if (m->hd != 64 && m->hd != 128) return false;
     if (m->d % 64 || (m->Hl * m->hd) % 64 || m->Fl % 64) return false;
+    // one row of the norm and of the QKV output fits the row kernels' shared memory
+    if (m->d > kRowsMaxDim || (m->Hl + 2 * m->Hkvl) * m->hd > kRopeMaxCols) return false;
     for (const auto& ly : m->layers)
         for (const at_qmat* q : {&ly.qkv, &ly.wo, &ly.w1, &ly.w3, &ly.w2})
             if (q->type != AT_GGML_Q4_0 && q->type != AT_GGML_Q8_0) return false;
@@ -2388,6 +2445,11 @@ void run_prompt_batched(at_model* m, const int* tokens, int n, int slot) {
             embed_kernel<AT_GGML_Q8_0><<<T, 256, 0, s>>>(m->tok.tiles, tile_map(&m->tok), m->pf_tok, d, m->pf_xa,
                                                           m->pf_y, nullptr, nullptr);
         AT_CUDA(cudaGetLastError());
+        // The residual update y of the attention norm: the embedding's zeros,
+        // then the down projection's output or its K-split partials in pf_ws
+        // (summed by the consumer in split order)
+        const float* ysrc = m->pf_y;
+        int ysp = 1;
         for (int L = 0; L < m->L; ++L) {
             Layer& ly = m->layers[L];
             const size_t kv_off = (size_t)slot * m->slot_stride + L * layer_kv;
@@ -2396,20 +2458,28 @@ void run_prompt_batched(at_model* m, const int* tokens, int n, int slot) {
             KvQ kvq;
             if (m->kv_q8) kvq = KvQ{m->kq8 + kv_off, m->vq8 + kv_off, m->ksc + kv_off / 32, m->vsc + kv_off / 32};
             // attention block: xb = norm(xa + y); q, k, v; RoPE + append; attention; y = wo att
-            rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xa, m->pf_y, ly.attn_norm, m->pf_xb, xbf, d, eps);
+            rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xa, ysrc, ly.attn_norm, m->pf_xb, xbf, d, eps, ysp,
+                                                  (size_t)T * d);
             AT_CUDA(cudaGetLastError());
+            int sp = 1;
+            GemmTcOut defer;
+            defer.defer = &sp;
             launch_gemm_tc(&ly.qkv, nullptr, d, m->pf_qkv, qcols, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
-                           c->num_sms, m->pf_err, s);
-            rope_append_kernel<<<T, 256, 0, s>>>(m->pf_qkv, qcols, m->pf_q, kc, vc, kvq, m->rope_cos, m->rope_sin, hd,
-                                                 nq, nkv, m->ctx_len, p0);
+                           c->num_sms, m->pf_err, s, defer);
+            AT_REQUIRE(sp <= kMaxPromptSplits, AT_ERR_STATE, "prompt GEMM split count above the consumers' limit");
+            rope_append_kernel<<<T, 256, 0, s>>>(sp > 1 ? m->pf_ws : m->pf_qkv, qcols, m->pf_q, kc, vc, kvq, m->rope_cos,
+                                                 m->rope_sin, hd, nq, nkv, m->ctx_len, p0, sp, (size_t)T * qcols);
             AT_CUDA(cudaGetLastError());
+            bool att_bf = false;  // the attention output already sits in the bf16 staging buffer
             {
                 const int G = m->Hl / m->Hkvl;
                 const float* kq = m->kv_q8 ? reinterpret_cast<const float*>(kvq.kq) : kc;
                 const float* vq = m->kv_q8 ? reinterpret_cast<const float*>(kvq.vq) : vc;
                 // tensor-core attention for head_dim 64 / 128 and 1, 2, 4 or 8 query heads per KV head
+                // (the last layer's attention output is not needed: write nothing)
                 if (launch_prompt_attn_tc(hd, G, m->kv_q8, m->Hkvl, T, s, m->pf_q, kq, vq, kvq.ks, kvq.vs, m->pf_att,
-                                          p0, m->Hl, m->ctx_len, scale, m->pf_err)) {
+                                          p0, m->Hl, m->ctx_len, scale, m->pf_err, xbf)) {
+                    att_bf = true;
                 } else if (hd == 128) {
                     if (m->kv_q8)
                         launch_prompt_attn<128, true>(G, m->Hkvl, T, s, m->pf_q, kq, vq, kvq.ks, kvq.vs, m->pf_att, p0,
@@ -2428,11 +2498,12 @@ void run_prompt_batched(at_model* m, const int* tokens, int n, int slot) {
             }
             AT_CUDA(cudaGetLastError());
             if (L == m->L - 1) break;  // later layers' inputs only; the KV cache is complete
-            launch_gemm_tc(&ly.wo, m->pf_att, nq, m->pf_y, d, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
-                           c->num_sms, m->pf_err, s);
+            launch_gemm_tc(&ly.wo, att_bf ? nullptr : m->pf_att, nq, m->pf_y, d, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws,
+                           m->pf_ws_bytes, c->num_sms, m->pf_err, s, defer);
             // feed-forward block: xa = norm(xb + y); h = silu(w1 xa) * (w3 xa); y = w2 h
             // the norm, silu * mul and their bf16 copies feed w1 / w3 / w2 through the staging buffer
-            rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xb, m->pf_y, ly.ffn_norm, m->pf_xa, xbf, d, eps);
+            rows_addnorm_kernel<<<T, 256, 0, s>>>(m->pf_xb, sp > 1 ? m->pf_ws : m->pf_y, ly.ffn_norm, m->pf_xa, xbf, d,
+                                                  eps, sp, (size_t)T * d);
             AT_CUDA(cudaGetLastError());
             launch_gemm_tc(&ly.w1, nullptr, d, m->pf_g, m->Fl, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
                            c->num_sms, m->pf_err, s);
@@ -2442,7 +2513,9 @@ void run_prompt_batched(at_model* m, const int* tokens, int n, int slot) {
                                                                                 (int64_t)T * m->Fl);
             AT_CUDA(cudaGetLastError());
             launch_gemm_tc(&ly.w2, nullptr, m->Fl, m->pf_y, d, T, m->pf_xbf, m->pf_xbf_bytes, m->pf_ws, m->pf_ws_bytes,
-                           c->num_sms, m->pf_err, s);
+                           c->num_sms, m->pf_err, s, defer);
+            ysrc = sp > 1 ? m->pf_ws : m->pf_y;
+            ysp = sp;
         }
     }
     int err = 0;

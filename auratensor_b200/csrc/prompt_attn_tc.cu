@@ -5,9 +5,11 @@
 // CTA (KV head h, query block): 128 query rows = 128 / G tokens x the G query
 // heads of h, so every K/V row the block needs is read once for all G heads.
 // The keys 0 .. (the block's last position) are walked in tiles of 128:
-//   1. all threads convert the tile's K and V rows (FP32 or Q8_0 cache) to
-//      bf16 in shared memory: K K-major (the B operand of Q K^T), V M-major
-//      (the B operand of P V, dimensions contiguous: no transpose);
+//   1. the tile's K and V rows (FP32 or Q8_0 cache) are converted to bf16 in
+//      one of two shared-memory tile buffers: K K-major (the B operand of
+//      Q K^T), V M-major (the B operand of P V, dimensions contiguous: no
+//      transpose); all threads load the first tile, then warps 4-7 load
+//      tile k + 1 while warps 0-3 run the softmax of tile k;
 //   2. one thread issues S = Q K^T (M 128, N 128 keys, K = HD) into TMEM
 //      columns 0..127;
 //   3. warps 0-3 (TMEM lane quarters; thread = query row) read S, apply the
@@ -136,6 +138,44 @@ __device__ __forceinline__ uint4 pt_row8(const float* __restrict__ c, const uint
     return make_uint4(pt_pack(f[0], f[1]), pt_pack(f[2], f[3]), pt_pack(f[4], f[5]), pt_pack(f[6], f[7]));
 }
 
+// K (K-major, 128-row atom columns) and V (M-major) of the key tile at k0
+// (nk valid rows, the rest zero) into one tile buffer, by NT threads (index
+// lt), LB chunks' loads in flight per thread.
+template <int HD, bool KVQ, int NT>
+__device__ __forceinline__ void pt_load_kv(uint8_t* ks, uint8_t* vs, const float* __restrict__ kc,
+                                           const float* __restrict__ vc, const uint16_t* __restrict__ ksc,
+                                           const uint16_t* __restrict__ vsc, size_t kvbase, int64_t k0, int nk,
+                                           int lt) {
+    constexpr int NA = HD / 64;
+    constexpr uint32_t ATOM_COL = 128 * 128;        // bytes of one atom column of a 128-row K-major tile
+    constexpr int CH = 128 * HD / 8 / NT;           // 8-element chunks of K (and of V) per thread
+    constexpr int LB = CH < 8 ? CH : 8;             // chunks whose loads are in flight together
+    static_assert(CH % LB == 0, "load batches");
+#pragma unroll
+    for (int b = 0; b < CH; b += LB) {
+        uint4 kv[LB], vv[LB];
+#pragma unroll
+        for (int u = 0; u < LB; ++u) {
+            const int i = lt + (b + u) * NT;
+            const int kr = i / (HD / 8), c8 = i % (HD / 8);
+            kv[u] = vv[u] = make_uint4(0u, 0u, 0u, 0u);
+            if (kr < nk) {
+                const size_t e = kvbase + (size_t)(k0 + kr) * HD + 8 * c8;
+                kv[u] = pt_row8<KVQ>(kc, ksc, e);
+                vv[u] = pt_row8<KVQ>(vc, vsc, e);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < LB; ++u) {
+            const int i = lt + (b + u) * NT;
+            const int kr = i / (HD / 8), c8 = i % (HD / 8);
+            *reinterpret_cast<uint4*>(ks + (c8 >> 3) * ATOM_COL + pt_sw128(kr, c8 & 7)) = kv[u];
+            *reinterpret_cast<uint4*>(vs + (kr >> 3) * (NA * 1024) + (c8 >> 3) * 1024 + (kr & 7) * 128 +
+                                      (((c8 & 7) ^ (kr & 7)) << 4)) = vv[u];
+        }
+    }
+}
+
 // 32 consecutive FP32 columns of this warp's 32 TMEM lanes, written.
 __device__ __forceinline__ void pt_st32(uint32_t taddr, const float* v) {
     asm volatile(
@@ -165,24 +205,24 @@ template <int HD, int G, bool KVQ>
 __global__ void __launch_bounds__(PT_THREADS, 1)
     prompt_attn_tc_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                           const uint16_t* __restrict__ ksc, const uint16_t* __restrict__ vsc, float* __restrict__ att,
-                          int T, int64_t p0, int Hl, int ctx, float scale, int* err) {
+                          int T, int64_t p0, int Hl, int ctx, float scale, int* err,
+                          __nv_bfloat16* __restrict__ att_bf) {
     constexpr int QB = PT_ROWS / G;  // tokens per CTA
     constexpr int NA = HD / 64;      // 128-byte atom columns of a Q / K row
     constexpr uint32_t QK_BYTES = PT_ROWS * HD * 2, V_BYTES = PT_KT * HD * 2;
     constexpr uint32_t ATOM_COL = PT_ROWS * 128;  // bytes of one atom column of a 128-row K-major tile
     constexpr uint32_t idesc_s = pt_idesc(PT_ROWS, PT_KT, false);
     constexpr uint32_t idesc_o = pt_idesc(PT_ROWS, HD, true);
-    constexpr int CH = PT_KT * HD / 8 / PT_THREADS;  // 8-element chunks of K (and of V) per thread per tile
-    constexpr int LB = CH < 8 ? CH : 8;              // chunks whose loads are in flight together
-    static_assert(CH % LB == 0, "load batches");
+    static_assert(PT_KT == PT_ROWS, "K tiles share the 128-row atom layout of Q");
     extern __shared__ uint8_t pt_raw[];
     __shared__ __align__(8) uint64_t s_bar[2];  // S complete, P V complete
     __shared__ uint32_t s_tmem;
     __shared__ int s_bad;
     uint8_t* qs = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(pt_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* ks = qs + QK_BYTES;
-    uint8_t* vs = ks + QK_BYTES;
-    uint8_t* ps = vs + V_BYTES;
+    uint8_t* ps = qs + QK_BYTES;
+    // two K / V tile buffers: tile k uses buffer k & 1
+    auto ks = [&](int buf) { return ps + PT_ROWS * PT_KT * 2 + buf * (QK_BYTES + V_BYTES); };
+    auto vs = [&](int buf) { return ks(buf) + QK_BYTES; };
     const int kvh = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nq = Hl * HD;
     const int t0 = blockIdx.y * QB;
@@ -211,6 +251,10 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
         if (ti < ntok) v = pt_row8<false>(q, nullptr, (size_t)(t0 + ti) * nq + (size_t)(kvh * G + g) * HD + 8 * c8);
         *reinterpret_cast<uint4*>(qs + (c8 >> 3) * ATOM_COL + pt_sw128(r, c8 & 7)) = v;
     }
+    // the first key tile, by all threads
+    pt_load_kv<HD, KVQ, PT_THREADS>(ks(0), vs(0), kc, vc, ksc, vsc, kvbase, 0, (last + 1) < PT_KT ? (int)(last + 1) : PT_KT,
+                                    tid);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> the MMAs' async proxy
     pt_fence_before();
     __syncthreads();
     pt_fence_after();
@@ -224,44 +268,11 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
 
     for (int kt = 0; kt < ntiles; ++kt) {
         const int64_t k0 = (int64_t)kt * PT_KT;
-        const int nk = (last + 1 - k0) < PT_KT ? (int)(last + 1 - k0) : PT_KT;
-        // 1. the previous P V has read V; K (K-major) and V (M-major) of the
-        //    tile in bf16, rows past nk zero, LB chunks' loads in flight
-        if (kt > 0 && !pt_wait(pt_smem_u32(&s_bar[1]), (kt - 1) & 1)) {
-            atomicExch(err, 2);
-            s_bad = 1;
-        }
-#pragma unroll
-        for (int b = 0; b < CH; b += LB) {
-            uint4 kv[LB], vv[LB];
-#pragma unroll
-            for (int u = 0; u < LB; ++u) {
-                const int i = tid + (b + u) * PT_THREADS;
-                const int kr = i / (HD / 8), c8 = i % (HD / 8);
-                kv[u] = vv[u] = make_uint4(0u, 0u, 0u, 0u);
-                if (kr < nk) {
-                    const size_t e = kvbase + (size_t)(k0 + kr) * HD + 8 * c8;
-                    kv[u] = pt_row8<KVQ>(kc, ksc, e);
-                    vv[u] = pt_row8<KVQ>(vc, vsc, e);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < LB; ++u) {
-                const int i = tid + (b + u) * PT_THREADS;
-                const int kr = i / (HD / 8), c8 = i % (HD / 8);
-                *reinterpret_cast<uint4*>(ks + (c8 >> 3) * ATOM_COL + pt_sw128(kr, c8 & 7)) = kv[u];
-                *reinterpret_cast<uint4*>(vs + (kr >> 3) * (NA * 1024) + (c8 >> 3) * 1024 + (kr & 7) * 128 +
-                                          (((c8 & 7) ^ (kr & 7)) << 4)) = vv[u];
-            }
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> the MMAs' async proxy
-        pt_fence_before();
-        __syncthreads();
-        if (s_bad) break;
+        const int buf = kt & 1;
         // 2. S = Q K^T
         if (tid == 0) {
             pt_fence_after();
-            const uint32_t qa = pt_smem_u32(qs), ka = pt_smem_u32(ks);
+            const uint32_t qa = pt_smem_u32(qs), ka = pt_smem_u32(ks(buf));
 #pragma unroll
             for (int kk = 0; kk < HD / 16; ++kk)
                 pt_mma(tmem, pt_desc_k(qa + (kk >> 2) * ATOM_COL + 32 * (kk & 3)),
@@ -322,6 +333,18 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
                 }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        } else if (kt + 1 < ntiles) {
+            // 1'. warps 4-7: the next tile into the other buffer, once the
+            //     previous tile's P V (the last reader of that buffer) is done
+            if (kt > 0 && !pt_wait(pt_smem_u32(&s_bar[1]), (kt - 1) & 1)) {
+                atomicExch(err, 2);
+                s_bad = 1;
+            } else {
+                const int64_t k1 = k0 + PT_KT;
+                pt_load_kv<HD, KVQ, PT_THREADS - 128>(ks(buf ^ 1), vs(buf ^ 1), kc, vc, ksc, vsc, kvbase, k1,
+                                                      (last + 1 - k1) < PT_KT ? (int)(last + 1 - k1) : PT_KT, tid - 128);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            }
         }
         pt_fence_before();
         __syncthreads();
@@ -329,7 +352,7 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
         // 4. O (+)= P V
         if (tid == 0) {
             pt_fence_after();
-            const uint32_t pa = pt_smem_u32(ps), va = pt_smem_u32(vs);
+            const uint32_t pa = pt_smem_u32(ps), va = pt_smem_u32(vs(buf));
 #pragma unroll
             for (int kk = 0; kk < PT_KT / 16; ++kk)
                 pt_mma(tmem + PT_KT, pt_desc_k(pa + (kk >> 2) * ATOM_COL + 32 * (kk & 3)),
@@ -345,17 +368,29 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
         } else {
             pt_fence_after();
             const int ti = row / G, g = row % G;
-            float* dst = att + (size_t)(t0 + ti) * nq + (size_t)(kvh * G + g) * HD;
+            const size_t off = (size_t)(t0 + ti) * nq + (size_t)(kvh * G + g) * HD;
 #pragma unroll 1
             for (int c = 0; c < HD / 32; ++c) {
                 float ov[32];
                 pt_ld32(trow + PT_KT + 32 * c, ov);
                 if (qpos >= 0) {
+                    if (att_bf) {  // the wo GEMM's bf16 operand (round to nearest even, as its conversion)
 #pragma unroll
-                    for (int d = 0; d < 32; d += 4)
-                        *reinterpret_cast<float4*>(dst + 32 * c + d) =
-                            make_float4(__fdiv_rn(ov[d], l), __fdiv_rn(ov[d + 1], l), __fdiv_rn(ov[d + 2], l),
-                                        __fdiv_rn(ov[d + 3], l));
+                        for (int d = 0; d < 32; d += 8) {
+                            uint4 u;
+                            u.x = pt_pack(__fdiv_rn(ov[d], l), __fdiv_rn(ov[d + 1], l));
+                            u.y = pt_pack(__fdiv_rn(ov[d + 2], l), __fdiv_rn(ov[d + 3], l));
+                            u.z = pt_pack(__fdiv_rn(ov[d + 4], l), __fdiv_rn(ov[d + 5], l));
+                            u.w = pt_pack(__fdiv_rn(ov[d + 6], l), __fdiv_rn(ov[d + 7], l));
+                            *reinterpret_cast<uint4*>(att_bf + off + 32 * c + d) = u;
+                        }
+                    } else {
+#pragma unroll
+                        for (int d = 0; d < 32; d += 4)
+                            *reinterpret_cast<float4*>(att + off + 32 * c + d) =
+                                make_float4(__fdiv_rn(ov[d], l), __fdiv_rn(ov[d + 1], l), __fdiv_rn(ov[d + 2], l),
+                                            __fdiv_rn(ov[d + 3], l));
+                    }
                 }
             }
         }
@@ -366,11 +401,16 @@ __global__ void __launch_bounds__(PT_THREADS, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PT_TMEM_COLS) : "memory");
 }
 
-constexpr size_t pt_smem(int hd) { return (size_t)(2 * PT_ROWS * hd * 2 + PT_KT * hd * 2 + PT_ROWS * PT_KT * 2) + 1024; }
+// q, P and two K / V tile buffers (bf16) + alignment slack
+constexpr size_t pt_smem(int hd) {
+    return (size_t)(PT_ROWS * hd * 2 + PT_ROWS * PT_KT * 2 + 2 * (PT_KT * hd * 2 + PT_KT * hd * 2)) + 1024;
+}
+static_assert(pt_smem(128) <= 227 * 1024, "shared memory per CTA");
 
 template <int HD, int G, bool KVQ>
 void pt_launch(int Hkvl, int T, cudaStream_t s, const float* q, const float* kc, const float* vc, const uint16_t* ksc,
-               const uint16_t* vsc, float* att, int64_t p0, int Hl, int ctx, float scale, int* err) {
+               const uint16_t* vsc, float* att, int64_t p0, int Hl, int ctx, float scale, int* err,
+               __nv_bfloat16* att_bf) {
     auto kern = prompt_attn_tc_kernel<HD, G, KVQ>;
     static bool attr = false;  // per instance
     if (!attr) {
@@ -379,19 +419,19 @@ void pt_launch(int Hkvl, int T, cudaStream_t s, const float* q, const float* kc,
     }
     constexpr int QB = PT_ROWS / G;
     kern<<<dim3(Hkvl, (T + QB - 1) / QB), PT_THREADS, pt_smem(HD), s>>>(q, kc, vc, ksc, vsc, att, T, p0, Hl, ctx,
-                                                                       scale, err);
+                                                                       scale, err, att_bf);
     AT_CUDA(cudaGetLastError());
 }
 
 template <int HD, bool KVQ>
 bool pt_dispatch_g(int G, int Hkvl, int T, cudaStream_t s, const float* q, const float* kc, const float* vc,
                    const uint16_t* ksc, const uint16_t* vsc, float* att, int64_t p0, int Hl, int ctx, float scale,
-                   int* err) {
+                   int* err, __nv_bfloat16* att_bf) {
     switch (G) {
-        case 1: pt_launch<HD, 1, KVQ>(Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err); return true;
-        case 2: pt_launch<HD, 2, KVQ>(Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err); return true;
-        case 4: pt_launch<HD, 4, KVQ>(Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err); return true;
-        case 8: pt_launch<HD, 8, KVQ>(Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err); return true;
+        case 1: pt_launch<HD, 1, KVQ>(Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err, att_bf); return true;
+        case 2: pt_launch<HD, 2, KVQ>(Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err, att_bf); return true;
+        case 4: pt_launch<HD, 4, KVQ>(Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err, att_bf); return true;
+        case 8: pt_launch<HD, 8, KVQ>(Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err, att_bf); return true;
         default: return false;
     }
 }
@@ -400,13 +440,13 @@ bool pt_dispatch_g(int G, int Hkvl, int T, cudaStream_t s, const float* q, const
 
 bool launch_prompt_attn_tc(int hd, int G, bool kvq, int Hkvl, int T, cudaStream_t s, const float* q, const float* kc,
                            const float* vc, const uint16_t* ksc, const uint16_t* vsc, float* att, int64_t p0, int Hl,
-                           int ctx, float scale, int* err) {
+                           int ctx, float scale, int* err, __nv_bfloat16* att_bf) {
     if (hd == 128)
-        return kvq ? pt_dispatch_g<128, true>(G, Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err)
-                   : pt_dispatch_g<128, false>(G, Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err);
+        return kvq ? pt_dispatch_g<128, true>(G, Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err, att_bf)
+                   : pt_dispatch_g<128, false>(G, Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err, att_bf);
     if (hd == 64)
-        return kvq ? pt_dispatch_g<64, true>(G, Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err)
-                   : pt_dispatch_g<64, false>(G, Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err);
+        return kvq ? pt_dispatch_g<64, true>(G, Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err, att_bf)
+                   : pt_dispatch_g<64, false>(G, Hkvl, T, s, q, kc, vc, ksc, vsc, att, p0, Hl, ctx, scale, err, att_bf);
     return false;
 }
 
