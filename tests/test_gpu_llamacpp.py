@@ -128,9 +128,10 @@ def test_llama_cpp_batched_decode(cuda):
 
 
 def test_llama_cpp_prompt_path(cuda):
-    shape = dataclasses.replace(synth.TINY_LLAMACPP, ctx=512)
+    # 600 tokens: a 512-token chunk of the batched prompt path and a short one
+    shape = dataclasses.replace(synth.TINY_LLAMACPP, ctx=640)
     t = synth.generate_numpy(shape, seed=53)
-    n = 200
+    n = 600
     prompt = synth.prompt_ids(shape, 53, n + 3).tolist()
     gpu = LlamaModel(LlamaConfig.fromShape(shape), t, layout=LCPP)
     orc = ref.LlamaModelRef(oracle_cfg(shape), t, layout=LCPP)

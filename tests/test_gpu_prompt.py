@@ -2,9 +2,10 @@
 oracle's token-by-token forwardStep.
 
 The prompt path's rule: KV-cache contents and the following decode logits
-within 2e-2 of the oracle's range (per layer and head for the cache). Prompts
-of 7, 130 and 300 tokens cover one chunk, a chunk boundary and three chunks
-of 128 tokens.
+within 2e-2 of the oracle's range (per layer and head for the cache). The
+prompt path runs chunks of 512 tokens (the GEMMs' two 256-token tiles);
+prompts of 7, 130 and 300 tokens are one chunk (one or two token tiles),
+600 tokens a chunk boundary, 1100 tokens two whole chunks and a short one.
 """
 import dataclasses
 
@@ -24,9 +25,9 @@ def oracle_cfg(s):
 
 
 @pytest.mark.parametrize("base", [synth.TINY, synth.TINY_Q8], ids=["q4_0", "q8_0"])
-@pytest.mark.parametrize("n", [7, 130, 300])
+@pytest.mark.parametrize("n", [7, 130, 300, 600, 1100])
 def test_batched_prompt_matches_oracle(base, n, cuda):
-    shape = dataclasses.replace(base, ctx=512)
+    shape = dataclasses.replace(base, ctx=1200)
     t = synth.generate_numpy(shape, seed=31)
     prompt = synth.prompt_ids(shape, 31, n + 4).tolist()
     gpu = LlamaModel(LlamaConfig.fromShape(shape), t)

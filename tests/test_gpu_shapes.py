@@ -12,7 +12,7 @@ inference/LlamaModel.java:141-297).
   four clusters of chunk CTAs at the end.
 - Llama-3-70B shape (dim 8192, FFN 28672, 64/8 heads: GQA group 8), 1 layer.
 - The batched prompt path (tensor-core GEMMs, bf16 operands) at head_dim 128
-  over 320 tokens (three 128-token chunks).
+  over 600 tokens (a 512-token chunk and an 88-token one).
 
 Rules (the FP32 GEMV path): logits within 1e-3 x (max - min of the oracle's
 logits) at every compared step; greedy tokens equal except where the
@@ -128,8 +128,8 @@ def test_llama3_70b_shape_gqa8(cuda):
 
 
 def test_hd128_batched_prompt(cuda):
-    shape = dataclasses.replace(synth.LLAMA3_8B, n_layers=2, ctx=512)
-    n = 320
+    shape = dataclasses.replace(synth.LLAMA3_8B, n_layers=2, ctx=640)
+    n = 600
     gpu, orc = build_pair(shape, 83)
     prompt = np.random.default_rng(84).integers(0, shape.vocab, n + 4).tolist()
     gpu.forwardPrompt(prompt[:n])
