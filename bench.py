@@ -56,6 +56,7 @@ UNIT = "tok/s"
 SAMPLE_LAYERS = 2
 # workload name -> (shape name in synth, metric, prompt tokens, batch, sampler (T, topK, topP, penalty) or None)
 CONFIGS = {
+    "llama-3.2-1b": ("LLAMA32_1B", "Llama-3.2-1B Q4_0 decode tok/s", 8, 1, None),
     "llama-3-8b": ("LLAMA3_8B", "Llama-3-8B Q4_0 decode tok/s", 512, 1, None),
     "llama-3-70b": ("LLAMA3_70B", "Llama-3-70B Q4_0 decode tok/s", 1024, 1, None),
     "mistral-7b-q8_0-batch8": ("MISTRAL_7B", "Mistral-7B Q8_0 batch-8 sampled decode tok/s", 128, 8,

@@ -11,6 +11,8 @@ inference/LlamaModel.java:141-297).
 - Mistral-7B shape in Q8_0 (vocab 32000, theta 1e6), 1 layer, context 4096:
   four clusters of chunk CTAs at the end.
 - Llama-3-70B shape (dim 8192, FFN 28672, 64/8 heads: GQA group 8), 1 layer.
+- The Llama-3.2-1B configuration whole (16 layers, head_dim 64, tied
+  embeddings, context 128): 8 prompt tokens and 32 greedy decode steps.
 - The batched prompt path (tensor-core GEMMs, bf16 operands) at head_dim 128
   over 600 tokens (a 512-token chunk and an 88-token one).
 
@@ -114,6 +116,50 @@ def test_mistral_7b_shape_q8_0_four_clusters(cuda):
     check = {0, 1023, 1024, 2047, 2048, 3071, 3072, 3073, 4000}
     gpu, orc, worst = run_teacher_forced(shape, 81, check, n_greedy=6)
     check_kv(gpu, orc, shape, (0, 1024, 3072, 4095), REL_TOL)
+    gpu.close()
+    orc.close()
+
+
+def test_llama32_1b_config_workload(cuda):
+    """The 1B configuration as specified: all 16 layers, dim 2048, head_dim
+    64, tied embeddings (output.weight is the token_embd bytes), context 128;
+    8 seeded prompt tokens through forwardStep (the reference's forwardPrompt
+    is one forwardStep per token), then 32 greedy decode steps fed the
+    oracle's argmax. Every step's logits within 1e-3 of the range; greedy
+    tokens equal except where the oracle's top-2 gap is below that."""
+    shape = synth.LLAMA32_1B
+    assert shape.tied and shape.ctx == 128 and shape.head_dim == 64 and shape.n_layers == 16
+    g = torch.Generator(device="cuda").manual_seed(85)
+    gpu = LlamaModel(LlamaConfig.fromShape(shape), None)
+    orc = RefDecoder(shape, threads=os.cpu_count() or 1)
+    emb = None
+    for name, dims, t in shape.tensor_dims():
+        data = emb if name == "output.weight" else synth.generate_torch_tensor(dims, t, g, "cuda")
+        if name == "token_embd.weight":
+            emb = data
+        gpu.setTensor(name, t, data)
+        orc.set_tensor(name, t, data.cpu().numpy(), int(np.prod(dims)))
+    gpu.finalize()
+    prompt = synth.prompt_ids(shape, 85, 8).tolist()
+    n_prompt, n_decode = 8, 32
+    tok, worst, agree = prompt[0], 0.0, 0
+    for pos in range(n_prompt + n_decode - 1):
+        if pos < n_prompt:
+            tok = prompt[pos]
+        lr = orc.forward_step(tok, pos)
+        lg = gpu.forwardStep(tok, pos).copy()
+        worst = max(worst, check_logits(lg, lr, REL_TOL, pos))
+        if pos >= n_prompt - 1:  # this step's argmax is a generated token
+            ref_tok = int(np.argmax(lr))
+            if int(np.argmax(lg)) == ref_tok:
+                agree += 1
+            else:
+                srt = np.sort(lr)
+                assert float(srt[-1] - srt[-2]) < REL_TOL * float(lr.max() - lr.min()), ("greedy", pos)
+            tok = ref_tok
+    assert gpu.kvCache().size() == n_prompt + n_decode - 1
+    assert agree >= n_decode - 2  # near-ties aside, the same 32 tokens
+    check_kv(gpu, orc, shape, (0, 7, n_prompt + n_decode - 2), REL_TOL)
     gpu.close()
     orc.close()
 
