@@ -3,7 +3,7 @@
 //
 // The reference processes a prompt one token at a time (forwardPrompt,
 // inference/LlamaModel.java:166-175, each token a forwardStep over FP32
-// weights). Here every projection of a chunk of up to 256 tokens is one GEMM
+// weights). Here every projection of a chunk of up to 512 tokens is one GEMM
 // whose operands are bf16 (the prompt path's tolerance is 2e-2 of the logit
 // range): the weight tile is dequantized from the resident Q4_0 / Q8_0 tiles
 // ((q - 8) * d, or q * d, rounded once to bf16) straight into shared memory,
