@@ -7,6 +7,9 @@
 #include <cstring>
 #include <numeric>
 #include <vector>
+#if defined(__SSE2__)
+#include <immintrin.h>
+#endif
 
 #include "at_internal.h"
 
@@ -30,6 +33,57 @@ uint32_t double_compare_bits(float v) {
     uint32_t u;
     std::memcpy(&u, &v, 4);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Sampler.java's greedy loop (inference/Sampler.java:56-67): scanning left
+// to right, an element replaces the running maximum only if it is greater.
+// So a NaN wins only at index 0 (nothing is greater than it, and it is
+// greater than nothing), later NaNs are skipped, and equal values (-0.0 and
+// 0.0 included) keep the first index. Computed as the maximum over 16
+// independent lanes seeded with element 0 (no compare chain carried from one
+// element to the next) and then the first index holding that maximum: the
+// same index as the scan. With SSE, lane update max(x, m) is MAXPS(x, m),
+// which yields m when x is NaN or equal, exactly the scan's rule.
+int greedy_index(const float* x, int n) {
+    const float x0 = x[0];
+    if (std::isnan(x0)) return 0;
+    constexpr int W = 16;
+    float m[W];
+    int i = 0;
+#if defined(__SSE2__)
+    __m128 a0 = _mm_set1_ps(x0), a1 = a0, a2 = a0, a3 = a0;
+    for (; i + W <= n; i += W) {
+        a0 = _mm_max_ps(_mm_loadu_ps(x + i), a0);
+        a1 = _mm_max_ps(_mm_loadu_ps(x + i + 4), a1);
+        a2 = _mm_max_ps(_mm_loadu_ps(x + i + 8), a2);
+        a3 = _mm_max_ps(_mm_loadu_ps(x + i + 12), a3);
+    }
+    _mm_storeu_ps(m, a0);
+    _mm_storeu_ps(m + 4, a1);
+    _mm_storeu_ps(m + 8, a2);
+    _mm_storeu_ps(m + 12, a3);
+#else
+    for (int j = 0; j < W; ++j) m[j] = x0;
+    for (; i + W <= n; i += W)
+        for (int j = 0; j < W; ++j) m[j] = x[i + j] > m[j] ? x[i + j] : m[j];
+#endif
+    for (; i < n; ++i) m[0] = x[i] > m[0] ? x[i] : m[0];
+    float top = m[0];
+    for (int j = 1; j < W; ++j) top = m[j] > top ? m[j] : top;
+    int k = 0;
+#if defined(__SSE2__)
+    const __m128 t = _mm_set1_ps(top);
+    for (; k + W <= n; k += W) {
+        const int hit = _mm_movemask_ps(_mm_cmpeq_ps(_mm_loadu_ps(x + k), t)) |
+                        (_mm_movemask_ps(_mm_cmpeq_ps(_mm_loadu_ps(x + k + 4), t)) << 4) |
+                        (_mm_movemask_ps(_mm_cmpeq_ps(_mm_loadu_ps(x + k + 8), t)) << 8) |
+                        (_mm_movemask_ps(_mm_cmpeq_ps(_mm_loadu_ps(x + k + 12), t)) << 12);
+        if (hit) return k + __builtin_ctz((unsigned)hit);
+    }
+#endif
+    for (; k < n; ++k)
+        if (x[k] == top) return k;
+    return 0;  // not reached: top is one of the elements
 }
 
 }  // namespace
@@ -58,11 +112,7 @@ extern "C" int at_sample(float* logits, int vocab, const int* history, int n_his
         }
         // 2) greedy fast path (Sampler.java:56-67)
         if (temperature == 0.0f || (top_k == 1 && top_p >= 1.0f)) {
-            int best = 0;
-            float bs = logits[0];
-            for (int i = 1; i < vocab; ++i)
-                if (logits[i] > bs) { bs = logits[i]; best = i; }
-            *out_token = best;
+            *out_token = greedy_index(logits, vocab);
             return;
         }
         // 3) temperature, stable descending sort, top-k, top-p (Sampler.java:71-110)

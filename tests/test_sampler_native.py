@@ -59,3 +59,44 @@ def test_sampler_special_values_match_oracle(seed, built_lib):
         assert got == want
         na = np.isnan(a)
         assert np.array_equal(na, np.isnan(b)) and np.array_equal(a[~na].view(np.uint32), b[~na].view(np.uint32))
+
+
+def _scan_greedy(x):
+    """Sampler.java's greedy loop as written: replace the best only when greater."""
+    best, bs = 0, x[0]
+    for i in range(1, len(x)):
+        if x[i] > bs:
+            bs, best = x[i], i
+    return best
+
+
+@pytest.mark.parametrize("n", [1, 2, 15, 16, 17, 31, 33, 64, 1000, 128256])
+def test_greedy_index_matches_the_scan(n, built_lib):
+    """The native greedy path (lane-wise maxima, then the first index holding
+    the maximum) picks the scan's index: NaN first wins, later NaNs are
+    skipped, ties and -0.0 / 0.0 keep the first index, also across the
+    16-lane blocks and in the tail."""
+    rng = np.random.default_rng(n)
+    greedy = SamplerConfig.greedy()
+    cases = [rng.standard_normal(n).astype(np.float32),
+             rng.integers(-3, 3, n).astype(np.float32),          # many ties
+             np.full(n, -np.inf, dtype=np.float32),
+             np.zeros(n, dtype=np.float32)]
+    x = rng.standard_normal(n).astype(np.float32)
+    x[rng.integers(0, n, max(1, n // 7))] = np.nan               # NaNs after index 0
+    cases.append(x)
+    x = np.zeros(n, dtype=np.float32)
+    x[::2] = -0.0                                                 # -0.0 and 0.0 are equal
+    cases.append(x)
+    x = rng.standard_normal(n).astype(np.float32)
+    x[0] = np.nan                                                 # NaN at index 0 wins
+    cases.append(x)
+    x = rng.standard_normal(n).astype(np.float32)
+    x[-1] = np.inf                                                # maximum in the tail
+    cases.append(x)
+    x = rng.standard_normal(n).astype(np.float32)
+    x[rng.integers(0, n, 3)] = 50.0                               # a repeated maximum
+    cases.append(x)
+    for x in cases:
+        want = _scan_greedy(x.tolist())
+        assert Sampler.sample(x.copy(), None, greedy) == want
